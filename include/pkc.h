@@ -1,0 +1,161 @@
+/*
+ * pkc.h — C ABI of the B200 FastConformer encoder library (libpkc.so).
+ *
+ * This is the seam parakeet.cpp's host code calls instead of building ggml
+ * graphs for the encoder hot path. Every entry point is plain C: opaque
+ * handles, raw pointers and sizes, integer status codes, no exceptions and no
+ * torch or CUDA types in the signatures (CUDA streams travel as void*).
+ *
+ * Reference interfaces replaced (paths inside parakeet.cpp):
+ *   pkc_model_open        ModelLoader::load + realize_weights + Backend init
+ *                         (src/model_loader.cpp:99-166, :47-98; src/backend.cpp:61-113)
+ *   pkc_mel_batch         GpuMel::compute per clip + build_mel_batch
+ *                         (src/mel_gpu.cpp:34-162; src/model.cpp:119-144)
+ *   pkc_encode_batch      Encoder::forward_batch (src/encoder.hpp:43-46, src/encoder.cpp:97-167)
+ *   pkc_encode_pcm_batch  steps 1-2 of Model::transcribe_16k_batch (src/model.cpp:164-181)
+ *   pkc_last_error        parakeet_capi_last_error (include/parakeet_capi.h:136)
+ *
+ * Threading: one call per pkc_model at a time (the reference serialises every
+ * graph on one global mutex, src/ggml_graph.cpp:84). Different models may be
+ * used from different threads.
+ *
+ * Ownership: the caller owns every buffer passed in; the model owns its device
+ * weights and workspaces. Nothing returned needs freeing except the model.
+ */
+#ifndef PKC_H
+#define PKC_H
+
+#include <stddef.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define PKC_ABI_VERSION 1
+
+typedef struct pkc_model pkc_model;
+
+typedef enum pkc_status {
+  PKC_OK = 0,
+  PKC_ERR_ARG = 1,          /* invalid argument (NULL pointer, bad size, ...) */
+  PKC_ERR_IO = 2,           /* file could not be opened or read */
+  PKC_ERR_FORMAT = 3,       /* malformed GGUF or missing tensor / key */
+  PKC_ERR_UNSUPPORTED = 4,  /* configuration outside what the kernels implement */
+  PKC_ERR_CUDA = 5,         /* CUDA runtime error (launch, copy, allocation) */
+  PKC_ERR_OOM = 6,          /* device or host allocation failed */
+  PKC_ERR_KERNEL = 7,       /* a kernel reported an error through its error word */
+  PKC_ERR_INTERNAL = 8
+} pkc_status;
+
+/* Output layouts of the encoder entry points. */
+typedef enum pkc_layout {
+  /* per item channels-first [d_model, valid_Tout[b]] (enc[c*T + t]), items
+     concatenated; this is what Encoder::forward_batch returns per item */
+  PKC_LAYOUT_CHANNELS_FIRST = 0,
+  /* per item time-major [valid_Tout[b], d_model] (enc[t*d + c]), items
+     concatenated; what the transducer decoders consume (src/model.cpp:148-162) */
+  PKC_LAYOUT_TIME_MAJOR = 1
+} pkc_layout;
+
+typedef struct pkc_model_info {
+  int d_model, n_layers, n_heads, ff_dim, conv_kernel;
+  int n_mels, n_fft, win_length, hop_length, sample_rate;
+  int subsampling_factor, subsampling_conv_channels;
+  int xscaling;
+  int weight_type;  /* GGUF type id of the encoder linear weights (0 f32, 1 f16, 8 q8_0, 12 q4_k, 30 bf16) */
+  int compute_bf16; /* 1: bf16 tensor-core operands, 0: f16 */
+  int n_devices;
+  int vocab_size, blank_id;
+  char arch[32];
+} pkc_model_info;
+
+/* ABI version of this header/implementation (PKC_ABI_VERSION). */
+int pkc_abi_version(void);
+
+/* Human-readable description of the last error on `m`, or of the last failed
+   pkc_model_open on this thread when m is NULL. Never NULL. */
+const char* pkc_last_error(const pkc_model* m);
+
+/* Load a parakeet GGUF and upload the encoder weights to each listed CUDA
+   device (devices == NULL or n_devices == 0: device 0). Weights are re-packed
+   once at load into the kernels' layouts. */
+pkc_status pkc_model_open(const char* gguf_path, const int* devices, int n_devices,
+                          pkc_model** out);
+
+/* Release the model and all device memory it holds. Safe on NULL. */
+void pkc_model_close(pkc_model* m);
+
+pkc_status pkc_model_info_get(const pkc_model* m, pkc_model_info* out);
+
+/* Number of mel frames the front end produces for a clip of n samples
+   (1 + n / hop, the reference's n_frames for n_fft == 2*pad). */
+int pkc_mel_frames(const pkc_model* m, int n_samples);
+
+/* Number of encoder output frames for a clip whose mel has T frames (the
+   reference's Subsampling::valid_out_len with the offline T-1 convention). */
+int pkc_encoder_frames(const pkc_model* m, int mel_frames);
+
+/* Batched log-mel front end (16 kHz mono f32 PCM, one pointer per clip).
+   feats_out: [B][n_mels][T_max] f32, zero padded (the reference's MelBatch),
+   where T_max = max_b mel_frames(n_samples[b]); T_out[b] receives each clip's
+   frame count. feats_cap is the capacity of feats_out in floats. */
+pkc_status pkc_mel_batch(pkc_model* m, const float* const* pcm, const int* n_samples, int B,
+                         float* feats_out, size_t feats_cap, int* T_out);
+
+/* Batched encoder on a host MelBatch ([B][n_mels][T_max] f32, valid_T[b] true
+   mel frames). Writes every item's encoder output into `out` (layout as
+   requested, items concatenated), valid_Tout[b] its frame count. out_cap is
+   the capacity of out in floats; d_model_out may be NULL. */
+pkc_status pkc_encode_batch(pkc_model* m, const float* mel, int B, int n_mels, int T_max,
+                            const int* valid_T, int layout, float* out, size_t out_cap,
+                            int* valid_Tout, int* d_model_out);
+
+/* PCM -> encoder output in one call (mel front end + encoder), host buffers.
+   With several devices the clips are sharded across them by length. */
+pkc_status pkc_encode_pcm_batch(pkc_model* m, const float* const* pcm, const int* n_samples,
+                                int B, int layout, float* out, size_t out_cap, int* valid_Tout);
+
+/* Floats needed by pkc_encode_pcm_batch's `out` for these clip lengths. */
+size_t pkc_encode_out_floats(const pkc_model* m, const int* n_samples, int B);
+
+/* Device-resident variant on one device of the model: d_pcm holds the clips
+   concatenated (f32, already in that device's memory), d_out receives the
+   outputs (time-major, items concatenated). `stream` is a cudaStream_t or
+   NULL for the model's own stream. Asynchronous with respect to the host
+   unless sync != 0. */
+pkc_status pkc_encode_pcm_device(pkc_model* m, int device_slot, const float* d_pcm,
+                                 const int* n_samples, int B, float* d_out, void* stream,
+                                 int sync);
+
+/* Per-kernel-class timing (CUDA events around every launch on the model's
+   stream). enable != 0 turns it on and clears the accumulators. */
+pkc_status pkc_profile_enable(pkc_model* m, int enable);
+/* Copy up to cap entries of {name, launches, total_ms, flops, bytes}. Returns
+   the number of kernel classes recorded. */
+typedef struct pkc_kernel_stat {
+  char name[32];
+  long long launches;
+  double total_ms;
+  double flops;  /* algorithmic FLOPs summed over launches */
+  double bytes;  /* algorithmic HBM bytes summed over launches */
+} pkc_kernel_stat;
+int pkc_profile_read(pkc_model* m, pkc_kernel_stat* out, int cap);
+
+/* Assign B clips to n_dev devices (longest-processing-time greedy on the
+   cost T'(c1 + c2 T') of each clip's encoder length). assign[b] receives the
+   device slot of clip b. Pure host arithmetic. */
+pkc_status pkc_shard_plan(const int* n_samples, int B, int n_dev, int hop, int* assign);
+
+/* ---- kernel-level entry points (used by the parity tests; device pointers) */
+
+/* D[M,N] = A[M,K] * B[N,K]^T with a fused epilogue on the tcgen05 GEMM.
+   dtype 0 = f16, 1 = bf16 operands; epi/act as in the kernel header. */
+pkc_status pkc_gemm(const void* A, int lda, const void* Bw, int ldb, int M, int N, int K,
+                    int dtype, int epi, int act, float alpha, const float* bias, void* out,
+                    int ldo, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* PKC_H */

@@ -1,0 +1,296 @@
+// Dense contraction for every projection of the encoder: D = A * B^T with
+// A [M, K] activations and B [N, K] weights, both K-major f16 or bf16 in HBM,
+// accumulated in f32 in tensor memory by tcgen05.mma (kind::f16), operands
+// staged by TMA (128-byte swizzle) through a 4-deep mbarrier pipeline.
+//
+// Warp roles (128 threads, one CTA per 128x256 output tile):
+//   warp 0 lane 0  TMA producer
+//   warp 1 lane 0  MMA issuer (single thread, as tcgen05 requires)
+//   warps 0..3     epilogue: each warp drains its 32 TMEM lanes (= 32 rows)
+//
+// Fused epilogues (the reference runs each as a separate ggml node):
+//   STORE_H   : out_h   = act(acc + bias)                    (act: none/SiLU/ReLU)
+//   RESID_F32 : out_f32 = out_f32 + alpha * (acc + bias)     (half-step FFN, residual adds)
+//   STORE_F32 : out_f32 = alpha * (acc + bias)               (subsampling output linear, xscale)
+//   GLU_H     : out_h[c] = (a + ba) * sigmoid(g + bg)        (conv module pointwise_conv1 + GLU)
+//   POWER_F32 : out_f32[c] = a^2 + g^2                       (mel DFT: re^2 + im^2)
+// For GLU_H / POWER_F32 the weight rows are pre-arranged so that within each
+// 256-column tile, columns [0,128) hold the "a" half and [128,256) the paired
+// "g" half; the tile writes 128 output columns starting at n0/2.
+#include "common.cuh"
+#include "gemm.h"
+
+namespace pkc {
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 64;  // 64 x 2 bytes = one 128-byte swizzle row
+constexpr int STAGES = 4;
+constexpr int THREADS = 128;
+constexpr int A_STAGE_BYTES = BM * BK * 2;
+constexpr int B_STAGE_BYTES = BN * BK * 2;
+constexpr int SMEM_BYTES = STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + 256 + 1024;
+constexpr uint32_t TMEM_COLS = 256;
+
+template <typename H, int EPI>
+__global__ void __launch_bounds__(THREADS, 1)
+    k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+              GemmArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem =
+      reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_STAGE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * B_STAGE_BYTES);
+  // bars[0..S) full, bars[S..2S) empty, bars[2S] accumulator ready
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int n0 = blockIdx.x * BN;
+  const int m0 = blockIdx.y * BM;
+  const int KB = args.K / BK;
+
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+    for (int s = 0; s < 2 * STAGES + 1; ++s) mbar_init(smem_u32(&bars[s]), 1);
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 0) {
+    tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t accb = smem_u32(&bars[2 * STAGES]);
+
+  if (warp == 0 && lane == 0) {
+    // ---- TMA producer
+    for (int kb = 0; kb < KB; ++kb) {
+      const int s = kb % STAGES;
+      const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
+      if (!mbar_wait(smem_u32(&bars[STAGES + s]), ph ^ 1u, args.err, DEV_ERR_TIMEOUT_EMPTY)) break;
+      const uint32_t fb = smem_u32(&bars[s]);
+      mbar_arrive_expect_tx(fb, A_STAGE_BYTES + B_STAGE_BYTES);
+      tma_load_2d(smem_u32(sA + s * A_STAGE_BYTES), &tmA, fb, kb * BK, m0);
+      tma_load_2d(smem_u32(sB + s * B_STAGE_BYTES), &tmB, fb, kb * BK, n0);
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ---- MMA issuer
+    constexpr uint32_t idesc = idesc_f16(BM, BN, is_bf16<H>::value ? 1 : 0);
+    bool ok = true;
+    for (int kb = 0; kb < KB; ++kb) {
+      const int s = kb % STAGES;
+      const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
+      if (!mbar_wait(smem_u32(&bars[s]), ph, args.err, DEV_ERR_TIMEOUT_FULL)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const uint64_t da = smem_desc_sw128(smem_u32(sA + s * A_STAGE_BYTES));
+      const uint64_t db = smem_desc_sw128(smem_u32(sB + s * B_STAGE_BYTES));
+#pragma unroll
+      for (int k = 0; k < BK / 16; ++k) {
+        // advance 16 elements (32 bytes) along K inside the swizzle atom
+        umma_f16(tmem, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc,
+                 (kb > 0 || k > 0) ? 1u : 0u);
+      }
+      umma_commit(smem_u32(&bars[STAGES + s]));
+    }
+    if (ok) umma_commit(accb);
+  }
+  __syncwarp();
+
+  // ---- epilogue: warp w owns TMEM lanes [32w, 32w+32) = tile rows
+  // every lane waits, then the warp reconverges before the .sync.aligned loads
+  const bool have_acc =
+      __all_sync(0xffffffffu, mbar_wait(accb, 0, args.err, DEV_ERR_TIMEOUT_ACCUM) ? 1 : 0) != 0;
+  tc_fence_after();
+  const int row = m0 + warp * 32 + lane;
+  const bool row_ok = have_acc && row < args.M;
+  const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+  uint32_t r[32];
+
+  if constexpr (EPI == EPI_GLU_H || EPI == EPI_POWER_F32) {
+    uint32_t g[32];
+#pragma unroll 1
+    for (int j = 0; j < BN / 64; ++j) {
+      tmem_ld32(trow + 32 * j, r);
+      tmem_ld32(trow + BN / 2 + 32 * j, g);
+      tmem_ld_wait();
+      if (!row_ok) continue;
+      const int oc = n0 / 2 + 32 * j;
+      if constexpr (EPI == EPI_GLU_H) {
+        const float* ba = args.bias ? args.bias + n0 + 32 * j : nullptr;
+        const float* bg = args.bias ? args.bias + n0 + BN / 2 + 32 * j : nullptr;
+        H* out = reinterpret_cast<H*>(args.out) + (size_t)row * args.ldo + oc;
+        uint32_t w[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          float a0 = __uint_as_float(r[2 * i]), a1 = __uint_as_float(r[2 * i + 1]);
+          float g0 = __uint_as_float(g[2 * i]), g1 = __uint_as_float(g[2 * i + 1]);
+          if (ba) {
+            a0 += ba[2 * i]; a1 += ba[2 * i + 1];
+            g0 += bg[2 * i]; g1 += bg[2 * i + 1];
+          }
+          w[i] = pack2<H>(a0 * sigmoidf_(g0), a1 * sigmoidf_(g1));
+        }
+        uint4* o4 = reinterpret_cast<uint4*>(out);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) o4[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+      } else {
+        float* out = reinterpret_cast<float*>(args.out) + (size_t)row * args.ldo + oc;
+        float4* o4 = reinterpret_cast<float4*>(out);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          float v[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float a = __uint_as_float(r[4 * q + e]);
+            const float b = __uint_as_float(g[4 * q + e]);
+            v[e] = a * a + b * b;
+          }
+          o4[q] = make_float4(v[0], v[1], v[2], v[3]);
+        }
+      }
+    }
+  } else {
+#pragma unroll 1
+    for (int j = 0; j < BN / 32; ++j) {
+      tmem_ld32(trow + 32 * j, r);
+      tmem_ld_wait();
+      if (!row_ok) continue;
+      const int n = n0 + 32 * j;
+      float v[32];
+#pragma unroll
+      for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+      if (args.bias) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) v[i] += args.bias[n + i];
+      }
+      if constexpr (EPI == EPI_STORE_H) {
+        if (args.act == ACT_SILU) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = siluf_(v[i]);
+        } else if (args.act == ACT_RELU) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = fmaxf(v[i], 0.0f);
+        }
+        H* out = reinterpret_cast<H*>(args.out) + (size_t)row * args.ldo + n;
+        uint4* o4 = reinterpret_cast<uint4*>(out);
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+          o4[q] = make_uint4(pack2<H>(v[8 * q], v[8 * q + 1]), pack2<H>(v[8 * q + 2], v[8 * q + 3]),
+                             pack2<H>(v[8 * q + 4], v[8 * q + 5]), pack2<H>(v[8 * q + 6], v[8 * q + 7]));
+      } else if constexpr (EPI == EPI_RESID_F32) {
+        float4* o4 = reinterpret_cast<float4*>(reinterpret_cast<float*>(args.out) +
+                                               (size_t)row * args.ldo + n);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          float4 o = o4[q];
+          o.x += args.alpha * v[4 * q];
+          o.y += args.alpha * v[4 * q + 1];
+          o.z += args.alpha * v[4 * q + 2];
+          o.w += args.alpha * v[4 * q + 3];
+          o4[q] = o;
+        }
+      } else {  // EPI_STORE_F32
+        float4* o4 = reinterpret_cast<float4*>(reinterpret_cast<float*>(args.out) +
+                                               (size_t)row * args.ldo + n);
+#pragma unroll
+        for (int q = 0; q < 8; ++q)
+          o4[q] = make_float4(args.alpha * v[4 * q], args.alpha * v[4 * q + 1],
+                              args.alpha * v[4 * q + 2], args.alpha * v[4 * q + 3]);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) tmem_dealloc(tmem, TMEM_COLS);
+}
+
+}  // namespace
+
+// ------------------------------------------------------------------ host side
+
+static PFN_encodeTiled_t g_encode = nullptr;
+
+static bool get_encode_fn() {
+  if (g_encode) return true;
+  cudaDriverEntryPointQueryResult q;
+  void* fn = nullptr;
+  if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+      q != cudaDriverEntryPointSuccess || !fn)
+    return false;
+  g_encode = reinterpret_cast<PFN_encodeTiled_t>(fn);
+  return true;
+}
+
+bool make_tmap_kmajor(CUtensorMap* map, const void* base, int rows, int K, int ld_elems,
+                      int box_rows, bool bf16) {
+  if (!get_encode_fn()) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)ld_elems * 2};
+  cuuint32_t box[2] = {(cuuint32_t)BK, (cuuint32_t)box_rows};
+  cuuint32_t es[2] = {1, 1};
+  CUresult r = g_encode(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                        2, const_cast<void*>(base), dims, strides, box, es,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <typename H, int EPI>
+static cudaError_t launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
+                            cudaStream_t st) {
+  auto kern = k_gemm_tc<H, EPI>;
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    if (e != cudaSuccess) return e;
+    attr_set[dev & 63] = true;
+  }
+  dim3 grid(a.N / BN, (a.M + BM - 1) / BM);
+  kern<<<grid, THREADS, SMEM_BYTES, st>>>(ta, tb, a);
+  return cudaGetLastError();
+}
+
+int gemm_tile_n() { return BN; }
+int gemm_tile_k() { return BK; }
+int gemm_tile_m() { return BM; }
+
+cudaError_t gemm_launch(const void* A, int lda, const void* B, int ldb, bool bf16,
+                        const GemmArgs& args, cudaStream_t st) {
+  if (args.M <= 0) return cudaSuccess;
+  if (args.N % BN != 0 || args.K % BK != 0 || args.K <= 0 || (lda % 8) != 0 || (ldb % 8) != 0 ||
+      (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15) ||
+      (args.ldo % 8) != 0 || args.M > 65535 * BM)
+    return cudaErrorInvalidValue;
+  CUtensorMap ta, tb;
+  if (!make_tmap_kmajor(&ta, A, args.M, args.K, lda, BM, bf16)) return cudaErrorInvalidValue;
+  if (!make_tmap_kmajor(&tb, B, args.N, args.K, ldb, BN, bf16)) return cudaErrorInvalidValue;
+  switch (args.epi) {
+#define PKC_GEMM_CASE(E)                                                                   \
+  case E:                                                                                  \
+    return bf16 ? launch_t<__nv_bfloat16, E>(ta, tb, args, st) : launch_t<__half, E>(ta, tb, args, st);
+    PKC_GEMM_CASE(EPI_STORE_H)
+    PKC_GEMM_CASE(EPI_RESID_F32)
+    PKC_GEMM_CASE(EPI_STORE_F32)
+    PKC_GEMM_CASE(EPI_GLU_H)
+    PKC_GEMM_CASE(EPI_POWER_F32)
+#undef PKC_GEMM_CASE
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace pkc

@@ -1,0 +1,48 @@
+// Host interface of the tcgen05 GEMM (see gemm.cu).
+#pragma once
+#include <cuda.h>
+#include <cuda_runtime.h>
+
+namespace pkc {
+
+enum EpiKind : int {
+  EPI_STORE_H = 0,
+  EPI_RESID_F32 = 1,
+  EPI_STORE_F32 = 2,
+  EPI_GLU_H = 3,
+  EPI_POWER_F32 = 4,
+};
+enum ActKind : int { ACT_NONE = 0, ACT_SILU = 1, ACT_RELU = 2 };
+
+struct GemmArgs {
+  int M, N, K;
+  int epi;            // EpiKind
+  int act;            // ActKind, EPI_STORE_H only
+  float alpha;        // RESID_F32 / STORE_F32 scale
+  const float* bias;  // [N] (GEMM column order) or nullptr
+  void* out;          // output base (h or f32 per epilogue)
+  int ldo;            // output row stride in elements
+  int* err;           // device error word
+};
+
+typedef CUresult (*PFN_encodeTiled_t)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                                      const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                                      const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                                      CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+// Encode a 2-D K-major tensor map (inner dim K, outer dim rows) with 128-byte
+// swizzle and a [64 x box_rows] box.
+bool make_tmap_kmajor(CUtensorMap* map, const void* base, int rows, int K, int ld_elems,
+                      int box_rows, bool bf16);
+
+// D[M,N] = A[M,K] * B[N,K]^T with the epilogue in args. A and B hold f16
+// (bf16 == false) or bf16 elements with row strides lda / ldb (elements).
+// Requires N % 256 == 0, K % 64 == 0, 16-byte aligned bases and strides.
+cudaError_t gemm_launch(const void* A, int lda, const void* B, int ldb, bool bf16,
+                        const GemmArgs& args, cudaStream_t st);
+
+int gemm_tile_m();
+int gemm_tile_n();
+int gemm_tile_k();
+
+}  // namespace pkc

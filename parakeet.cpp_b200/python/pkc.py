@@ -1,0 +1,227 @@
+"""ctypes binding of libpkc.so (include/pkc.h).
+
+This is the Python face of the C ABI used by the tests, bench.py and
+__graft_entry__.py. It mirrors the reference's operator interface for the
+encoder path: Encoder::forward_batch (src/encoder.hpp:43), GpuMel::compute +
+build_mel_batch (src/mel_gpu.hpp:20, src/model.cpp:119) and the C-API error
+convention (status code + last_error string, include/parakeet_capi.h:136).
+
+There is no fallback: if libpkc.so is missing or a call fails, an exception is
+raised.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import POINTER, c_char, c_char_p, c_double, c_float, c_int, c_longlong, c_size_t, c_void_p
+
+import numpy as np
+
+PKG_DIR = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+LIB_PATH = os.path.join(PKG_DIR, "libpkc.so")
+
+PKC_OK = 0
+STATUS_NAMES = {
+    0: "PKC_OK", 1: "PKC_ERR_ARG", 2: "PKC_ERR_IO", 3: "PKC_ERR_FORMAT",
+    4: "PKC_ERR_UNSUPPORTED", 5: "PKC_ERR_CUDA", 6: "PKC_ERR_OOM", 7: "PKC_ERR_KERNEL",
+    8: "PKC_ERR_INTERNAL",
+}
+LAYOUT_CHANNELS_FIRST = 0
+LAYOUT_TIME_MAJOR = 1
+
+EPI_STORE_H, EPI_RESID_F32, EPI_STORE_F32, EPI_GLU_H, EPI_POWER_F32 = range(5)
+ACT_NONE, ACT_SILU, ACT_RELU = range(3)
+
+
+class PkcError(RuntimeError):
+    def __init__(self, status: int, msg: str):
+        super().__init__(f"{STATUS_NAMES.get(status, status)}: {msg}")
+        self.status = status
+
+
+class ModelInfo(ctypes.Structure):
+    _fields_ = [
+        ("d_model", c_int), ("n_layers", c_int), ("n_heads", c_int), ("ff_dim", c_int),
+        ("conv_kernel", c_int), ("n_mels", c_int), ("n_fft", c_int), ("win_length", c_int),
+        ("hop_length", c_int), ("sample_rate", c_int), ("subsampling_factor", c_int),
+        ("subsampling_conv_channels", c_int), ("xscaling", c_int), ("weight_type", c_int),
+        ("compute_bf16", c_int), ("n_devices", c_int), ("vocab_size", c_int),
+        ("blank_id", c_int), ("arch", c_char * 32),
+    ]
+
+
+class KernelStat(ctypes.Structure):
+    _fields_ = [("name", c_char * 32), ("launches", c_longlong), ("total_ms", c_double),
+                ("flops", c_double), ("bytes", c_double)]
+
+
+_lib = None
+
+
+def lib():
+    """Load libpkc.so once; raise if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise FileNotFoundError(f"{LIB_PATH} not built; run __graft_entry__.build()")
+        L = ctypes.CDLL(LIB_PATH)
+        _declare(L)
+        _lib = L
+    return _lib
+
+
+def _declare(L):
+    def fn(name, res, *args):
+        f = getattr(L, name)
+        f.restype = res
+        f.argtypes = list(args)
+    fn("pkc_abi_version", c_int)
+    fn("pkc_last_error", c_char_p, c_void_p)
+    fn("pkc_gemm", c_int, c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int,
+       c_int, c_float, c_void_p, c_void_p, c_int, c_void_p)
+    optional = [
+        ("pkc_model_open", c_int, c_char_p, POINTER(c_int), c_int, POINTER(c_void_p)),
+        ("pkc_model_close", None, c_void_p),
+        ("pkc_model_info_get", c_int, c_void_p, POINTER(ModelInfo)),
+        ("pkc_mel_frames", c_int, c_void_p, c_int),
+        ("pkc_encoder_frames", c_int, c_void_p, c_int),
+        ("pkc_mel_batch", c_int, c_void_p, POINTER(c_void_p), POINTER(c_int), c_int, c_void_p,
+         c_size_t, POINTER(c_int)),
+        ("pkc_encode_batch", c_int, c_void_p, c_void_p, c_int, c_int, c_int, POINTER(c_int), c_int,
+         c_void_p, c_size_t, POINTER(c_int), POINTER(c_int)),
+        ("pkc_encode_pcm_batch", c_int, c_void_p, POINTER(c_void_p), POINTER(c_int), c_int, c_int,
+         c_void_p, c_size_t, POINTER(c_int)),
+        ("pkc_encode_out_floats", c_size_t, c_void_p, POINTER(c_int), c_int),
+        ("pkc_encode_pcm_device", c_int, c_void_p, c_int, c_void_p, POINTER(c_int), c_int,
+         c_void_p, c_void_p, c_int),
+        ("pkc_profile_enable", c_int, c_void_p, c_int),
+        ("pkc_profile_read", c_int, c_void_p, POINTER(KernelStat), c_int),
+        ("pkc_shard_plan", c_int, POINTER(c_int), c_int, c_int, c_int, POINTER(c_int)),
+    ]
+    for name, res, *args in optional:
+        if hasattr(L, name):
+            fn(name, res, *args)
+
+
+def _check(status: int, model=None):
+    if status != PKC_OK:
+        msg = lib().pkc_last_error(model)
+        raise PkcError(status, msg.decode() if msg else "")
+
+
+def _ints(xs):
+    arr = (c_int * len(xs))(*[int(x) for x in xs])
+    return arr
+
+
+def gemm(A, B, M, N, K, *, bf16, epi, act=ACT_NONE, alpha=1.0, bias=None, out, ldo,
+         lda=None, ldb=None, stream=0):
+    """D = A[M,K] * B[N,K]^T with a fused epilogue (device pointers as ints)."""
+    _check(lib().pkc_gemm(c_void_p(A), lda or K, c_void_p(B), ldb or K, M, N, K, 1 if bf16 else 0,
+                          epi, act, alpha, c_void_p(bias) if bias else None, c_void_p(out), ldo,
+                          c_void_p(stream) if stream else None))
+
+
+def shard_plan(n_samples, n_dev, hop=160):
+    out = (c_int * len(n_samples))()
+    _check(lib().pkc_shard_plan(_ints(n_samples), len(n_samples), n_dev, hop, out))
+    return list(out)
+
+
+class Model:
+    """An open GGUF model on one or more CUDA devices (pkc_model)."""
+
+    def __init__(self, gguf_path: str, devices=(0,)):
+        L = lib()
+        h = c_void_p()
+        devs = _ints(devices)
+        st = L.pkc_model_open(gguf_path.encode(), devs, len(devices), ctypes.byref(h))
+        _check(st, None)
+        self._h = h
+        info = ModelInfo()
+        _check(L.pkc_model_info_get(h, ctypes.byref(info)), h)
+        self.info = info
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().pkc_model_close(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def handle(self):
+        return self._h
+
+    def mel_frames(self, n):
+        return lib().pkc_mel_frames(self._h, int(n))
+
+    def encoder_frames(self, mel_frames):
+        return lib().pkc_encoder_frames(self._h, int(mel_frames))
+
+    def mel_batch(self, pcms):
+        """GpuMel::compute per clip stacked as MelBatch: ([B, n_mels, T_max], T[B])."""
+        B = len(pcms)
+        pcms = [np.ascontiguousarray(p, dtype=np.float32) for p in pcms]
+        ptrs = (c_void_p * B)(*[p.ctypes.data for p in pcms])
+        ns = _ints([len(p) for p in pcms])
+        T = [self.mel_frames(len(p)) for p in pcms]
+        Tmax = max(T) if T else 0
+        out = np.zeros((B, self.info.n_mels, Tmax), dtype=np.float32)
+        T_out = (c_int * B)()
+        _check(lib().pkc_mel_batch(self._h, ptrs, ns, B, out.ctypes.data, out.size, T_out), self._h)
+        return out, list(T_out)
+
+    def encode_batch(self, mel, valid_T, layout=LAYOUT_CHANNELS_FIRST):
+        """Encoder::forward_batch: list of per-item outputs ([d, T_b] or [T_b, d])."""
+        mel = np.ascontiguousarray(mel, dtype=np.float32)
+        B, F, Tmax = mel.shape
+        vout = [self.encoder_frames(int(t)) for t in valid_T]
+        d = self.info.d_model
+        out = np.zeros(sum(vout) * d, dtype=np.float32)
+        vt = (c_int * B)()
+        dm = c_int()
+        _check(lib().pkc_encode_batch(self._h, mel.ctypes.data, B, F, Tmax, _ints(valid_T), layout,
+                                      out.ctypes.data, out.size, vt, ctypes.byref(dm)), self._h)
+        return _split(out, list(vt), d, layout)
+
+    def encode_pcm_batch(self, pcms, layout=LAYOUT_CHANNELS_FIRST):
+        B = len(pcms)
+        pcms = [np.ascontiguousarray(p, dtype=np.float32) for p in pcms]
+        ptrs = (c_void_p * B)(*[p.ctypes.data for p in pcms])
+        ns = _ints([len(p) for p in pcms])
+        n = lib().pkc_encode_out_floats(self._h, ns, B)
+        out = np.zeros(n, dtype=np.float32)
+        vt = (c_int * B)()
+        _check(lib().pkc_encode_pcm_batch(self._h, ptrs, ns, B, layout, out.ctypes.data, out.size,
+                                          vt), self._h)
+        return _split(out, list(vt), self.info.d_model, layout)
+
+    def encode_pcm_device(self, d_pcm, n_samples, d_out, stream=0, slot=0, sync=False):
+        _check(lib().pkc_encode_pcm_device(self._h, slot, c_void_p(d_pcm), _ints(n_samples),
+                                           len(n_samples), c_void_p(d_out),
+                                           c_void_p(stream) if stream else None, 1 if sync else 0),
+               self._h)
+
+    def profile_enable(self, on=True):
+        _check(lib().pkc_profile_enable(self._h, 1 if on else 0), self._h)
+
+    def profile_read(self):
+        cap = 64
+        arr = (KernelStat * cap)()
+        n = lib().pkc_profile_read(self._h, arr, cap)
+        return [dict(name=a.name.decode(), launches=a.launches, total_ms=a.total_ms,
+                     flops=a.flops, bytes=a.bytes) for a in arr[:n]]
+
+
+def _split(flat, vt, d, layout):
+    outs, off = [], 0
+    for t in vt:
+        blk = flat[off:off + t * d]
+        outs.append(blk.reshape(d, t) if layout == LAYOUT_CHANNELS_FIRST else blk.reshape(t, d))
+        off += t * d
+    return outs
