@@ -1,0 +1,438 @@
+"""ORACLE — CPU restatement of parakeet.cpp's encoder hot path.
+
+TEST INFRASTRUCTURE ONLY. Only tests/, __graft_entry__.smoke() and bench.py's
+CPU-baseline legs may import this module, and only as the checker (or as the
+timed CPU baseline); the product path (libpkc.so) never calls it.
+
+What it restates (paths inside parakeet.cpp, the reference):
+  * MelFrontend::compute + MelKernel::frame_logmel   src/mel.cpp:63-176
+  * GpuMel::compute (DFT-as-matmul front end)        src/mel_gpu.cpp:15-162
+  * rel_pos_encoding                                 src/pos_enc.cpp:10-34
+  * Subsampling::build_graph_batched, valid_out_len  src/subsampling.cpp:25-240
+  * RelPosAttention::build_graph_batched             src/relpos_attention.cpp:162-306
+  * build_conv_module (batched)                      src/conformer.cpp:38-164
+  * ConformerLayer::build_graph_batched              src/conformer.cpp:285-353
+  * Encoder::forward_batch                           src/encoder.cpp:97-167
+The batched graph is restated literally: every item is zero-padded to the
+batch's T_max and every mask the reference builds (per-stage subsampling time
+masks, output-frame mask, attention key mask and padded-query zeroing, conv
+pre-depthwise mask) is applied, so padding effects are modelled, not assumed.
+
+Arithmetic is float64 throughout (the reference computes in f32 with ggml);
+the op semantics follow ggml: ggml_norm = (x-mean)/sqrt(var+eps) with the
+population variance; soft_max_ext(a, mask, scale) = softmax(a*scale + mask);
+silu(x) = x*sigmoid(x); GLU = first half * sigmoid(second half); BatchNorm
+folded into f32 scale/shift on the host exactly as conformer.cpp:134-154 does.
+
+Pinning: ggml itself (the library that executes these graphs) is absent from
+the reference checkout, so the graph arithmetic cannot be run here. The oracle
+is pinned against (a) the reference's own CPU mel front end and positional
+encoding compiled from its sources (oracle/_ref, see Makefile.ref), (b) the
+reference's known-answer test (tests/test_fft.cpp: a cosine at bin 8 peaks at
+bin 8) and its GpuMel-vs-MelFrontend tolerance (tests/test_mel_gpu.cpp: < 0.05),
+(c) a literal pad/reshape/view restatement of rel_shift, and (d) the
+reference's batched == standalone padding-invariance property
+(tests/test_encoder_batch.cpp). The encoder graph beyond those anchors is
+"parity unpinned" against ggml's own kernels.
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import numpy as np
+
+LN_EPS = 1e-5
+BN_EPS = 1e-5
+NORM_EPS = 1e-5       # per-feature mel normalisation (src/mel.cpp:13)
+INF_VAL = 10000.0     # sinusoid base (src/pos_enc.cpp:8)
+
+
+def cdiv_trunc(a: int, b: int) -> int:
+    """C integer division (truncates toward zero), as the reference's int math."""
+    q = abs(a) // abs(b)
+    return q if (a >= 0) == (b >= 0) else -q
+
+
+def valid_out_len(T: int, in_valid: int = -1) -> int:
+    """Subsampling::valid_out_len (src/subsampling.cpp:25-46), offline path."""
+    valid = in_valid if in_valid >= 0 else T - 1
+    for _ in range(3):
+        valid = cdiv_trunc(valid + 2 - 3, 2) + 1
+    return valid
+
+
+def conv_out_len(n: int) -> int:
+    """Spatial output of a k=3, s=2, p=1 convolution."""
+    return (n + 2 - 3) // 2 + 1
+
+
+# =========================================================== weights
+
+class Weights:
+    """GGUF tensors as float32 arrays in torch/numpy shape (dequantised with
+    gguf-py: exactly the values ggml's mul_mat sees for f16/q8_0/q4_k weights);
+    every op promotes them to float64."""
+
+    def __init__(self, gguf_path: str):
+        import gguf
+        r = gguf.GGUFReader(gguf_path)
+        self.kv = {}
+        for f in r.fields.values():
+            try:
+                self.kv[f.name] = f.contents()
+            except Exception:
+                pass
+        self.t = {}
+        self.types = {}
+        for t in r.tensors:
+            ne = [int(x) for x in t.shape]
+            shape = tuple(reversed(ne))
+            qt = t.tensor_type
+            self.types[t.name] = int(qt)
+            if qt in (gguf.GGMLQuantizationType.F32, gguf.GGMLQuantizationType.F16):
+                arr = np.asarray(t.data).astype(np.float32).reshape(shape)
+            else:
+                arr = gguf.quants.dequantize(np.asarray(t.data), qt).astype(np.float32).reshape(shape)
+            self.t[t.name] = arr
+        kv = self.kv
+        self.d = int(kv["parakeet.encoder.d_model"])
+        self.L = int(kv["parakeet.encoder.n_layers"])
+        self.H = int(kv["parakeet.encoder.n_heads"])
+        self.K = int(kv["parakeet.encoder.conv_kernel"])
+        self.C = int(kv["parakeet.encoder.subsampling_conv_channels"])
+        self.xscaling = bool(kv.get("parakeet.encoder.xscaling", True))
+        self.n_mels = int(kv["parakeet.preprocessor.n_mels"])
+        self.n_fft = int(kv["parakeet.preprocessor.n_fft"])
+        self.hop = int(kv["parakeet.preprocessor.hop_length"])
+        self.preemph = float(kv.get("parakeet.preprocessor.preemph", 0.0))
+        self.mag_power = float(kv.get("parakeet.preprocessor.mag_power", 2.0))
+        self.log_guard = float(kv.get("parakeet.preprocessor.log_zero_guard", 0.0))
+        self.per_feature = kv.get("parakeet.preprocessor.normalize", "per_feature") == "per_feature"
+
+    def get(self, name):
+        return self.t.get(name)
+
+    def window(self) -> np.ndarray:
+        """Hann window centre-padded to n_fft (src/mel.cpp:29-44), f32."""
+        w = np.zeros(self.n_fft, dtype=np.float32)
+        src = self.t.get("preprocessor.featurizer.window")
+        if src is not None:
+            src = src.astype(np.float32).reshape(-1)
+            left = (self.n_fft - len(src)) // 2
+            w[left:left + len(src)] = src
+        return w
+
+    def fb(self) -> np.ndarray:
+        nb = self.n_fft // 2 + 1
+        return self.t["preprocessor.featurizer.fb"].astype(np.float32).reshape(self.n_mels, nb)
+
+
+# =========================================================== mel front end
+
+def _preemph_pad(samples: np.ndarray, n_fft: int, hop: int, preemph: float):
+    S = len(samples)
+    s = samples.astype(np.float64)
+    x = s.copy()
+    if preemph > 0 and S > 0:
+        x[1:] = s[1:] - float(np.float32(preemph)) * s[:-1]
+    pad = n_fft // 2
+    padded = np.zeros(S + 2 * pad, dtype=np.float64)
+    padded[pad:pad + S] = x
+    T = 1 + (S + 2 * pad - n_fft) // hop if S + 2 * pad >= n_fft else 0
+    idx = np.arange(T)[:, None] * hop + np.arange(n_fft)[None, :]
+    return padded[idx], T, (S // hop if S > 0 else 0)
+
+
+def _normalize(feats: np.ndarray, seq_len: int) -> np.ndarray:
+    """Per-feature normalisation (src/mel.cpp:150-174), double precision."""
+    F, T = feats.shape
+    valid = min(seq_len, T)
+    out = np.zeros_like(feats)
+    for m in range(F):
+        row = feats[m].astype(np.float64)
+        mean = row[:valid].sum() / valid if valid > 0 else 0.0
+        var = ((row[:valid] - mean) ** 2).sum() / (valid - 1) if valid > 1 else 0.0
+        sd = math.sqrt(var) + NORM_EPS
+        out[m, :valid] = ((row[:valid] - mean) / sd).astype(np.float32)
+    return out
+
+
+def mel_frontend(w: Weights, samples: np.ndarray) -> np.ndarray:
+    """MelFrontend::compute: FFT front end, feats [n_mels, T] f32."""
+    if len(samples) == 0:
+        return np.zeros((w.n_mels, 0), dtype=np.float32)
+    frames, T, seq_len = _preemph_pad(samples, w.n_fft, w.hop, w.preemph)
+    win = w.window().astype(np.float64)
+    fr = (frames * win[None, :]).astype(np.float32)
+    spec = np.fft.rfft(fr.astype(np.float64), axis=1)
+    re = spec.real.astype(np.float32).astype(np.float64)
+    im = spec.imag.astype(np.float32).astype(np.float64)
+    mag = np.sqrt(re * re + im * im)
+    power = mag if w.mag_power == 1.0 else mag ** w.mag_power
+    mel = power @ w.fb().astype(np.float64).T                     # [T, F]
+    feats = np.log(mel + float(np.float32(w.log_guard))).astype(np.float32).T
+    return _normalize(feats, seq_len) if w.per_feature else feats
+
+
+def mel_gpu_graph(w: Weights, samples: np.ndarray) -> np.ndarray:
+    """GpuMel::compute: DFT as f32 matmuls, power, filterbank, log (f32)."""
+    if len(samples) == 0:
+        return np.zeros((w.n_mels, 0), dtype=np.float32)
+    frames, T, seq_len = _preemph_pad(samples, w.n_fft, w.hop, w.preemph)
+    win = w.window().astype(np.float64)
+    xw = (frames * win[None, :]).astype(np.float32).astype(np.float64)
+    N = w.n_fft
+    nb = N // 2 + 1
+    ang = 2.0 * np.pi * np.outer(np.arange(nb), np.arange(N)) / N
+    cosb = np.cos(ang).astype(np.float32).astype(np.float64)
+    sinb = (-np.sin(ang)).astype(np.float32).astype(np.float64)
+    re = (xw @ cosb.T).astype(np.float32)
+    im = (xw @ sinb.T).astype(np.float32)
+    power = (re * re + im * im).astype(np.float32).astype(np.float64)
+    mel = (power @ w.fb().astype(np.float64).T).astype(np.float32)
+    lm = np.log(mel + np.float32(w.log_guard)).astype(np.float32).T
+    return _normalize(lm, seq_len) if w.per_feature else lm
+
+
+def mel_batch(w: Weights, pcms, gpu_graph: bool = True):
+    """build_mel_batch (src/model.cpp:119-144): [B, F, T_max] zero padded + T[b]."""
+    feats = [(mel_gpu_graph if gpu_graph else mel_frontend)(w, p) for p in pcms]
+    Ts = [f.shape[1] for f in feats]
+    Tmax = max(Ts) if Ts else 0
+    out = np.zeros((len(pcms), w.n_mels, Tmax), dtype=np.float32)
+    for b, f in enumerate(feats):
+        out[b, :, :f.shape[1]] = f
+    return out, Ts
+
+
+# =========================================================== positional encoding
+
+def rel_pos_encoding(T: int, d: int) -> np.ndarray:
+    """rel_pos_encoding (src/pos_enc.cpp:10-34): [2T-1, d] f32, positions
+    T-1 ... -(T-1), sin on even dims, cos on odd dims."""
+    half = d // 2
+    factor = -(math.log(INF_VAL) / d)
+    div = np.exp(np.arange(half, dtype=np.float64) * 2 * factor)
+    pos = (T - 1) - np.arange(2 * T - 1, dtype=np.float64)
+    arg = pos[:, None] * div[None, :]
+    pe = np.zeros((2 * T - 1, d), dtype=np.float32)
+    pe[:, 0::2] = np.sin(arg)
+    pe[:, 1::2] = np.cos(arg)
+    return pe
+
+
+# =========================================================== subsampling
+
+def _conv3x3_s2(x: np.ndarray, wk: np.ndarray) -> np.ndarray:
+    """x [..., H, W] zero-padded by 1; wk [..., 3, 3] broadcast against x's
+    leading dims; returns sum_{kh,kw} wk*x at stride 2 -> [..., H', W']."""
+    H, W = x.shape[-2:]
+    Ho, Wo = conv_out_len(H), conv_out_len(W)
+    xp = np.zeros(x.shape[:-2] + (H + 2, W + 2), dtype=np.float64)
+    xp[..., 1:H + 1, 1:W + 1] = x
+    out = 0
+    for kh in range(3):
+        for kw in range(3):
+            sl = xp[..., kh:kh + 2 * Ho - 1:2, kw:kw + 2 * Wo - 1:2]
+            out = out + wk[..., kh, kw][..., None, None] * sl
+    return out
+
+
+def subsampling_batched(w: Weights, mel: np.ndarray, valid_in: list[int]):
+    """Subsampling::build_graph_batched (src/subsampling.cpp:48-240).
+    mel [B, F, T] -> (x [B, Tp, d], out_valid [B])."""
+    B, F, T = mel.shape
+    C = w.C
+    x = mel.astype(np.float64).transpose(0, 2, 1)             # [B, T, F] (H=T, W=F)
+    vt0 = [v if v >= 0 else T - 1 for v in valid_in]
+    vt1 = [cdiv_trunc(v - 1, 2) + 1 for v in vt0]
+    vt2 = [cdiv_trunc(v - 1, 2) + 1 for v in vt1]
+
+    def mask_time(t, vt):                                    # t [B, C?, H, W]
+        H = t.shape[-2]
+        m = (np.arange(H)[None, :] < np.array(vt)[:, None]).astype(np.float64)
+        return t * m.reshape((t.shape[0],) + (1,) * (t.ndim - 3) + (H, 1))
+
+    g = lambda n: w.get("encoder.pre_encode." + n)
+    x = mask_time(x, vt0)                                      # [B, T, F]
+    w0 = g("conv.0.weight")[:, 0]                              # [C, 3, 3]
+    y = _conv3x3_s2(x[:, None], w0[None])                      # [B, C, T1, F1]
+    y = np.maximum(y + g("conv.0.bias")[None, :, None, None], 0.0)
+    for dw_i, pw_i, vt in ((2, 3, vt1), (5, 6, vt2)):
+        y = mask_time(y, vt)
+        y = _conv3x3_s2(y, g(f"conv.{dw_i}.weight")[:, 0][None]) + g(f"conv.{dw_i}.bias")[None, :, None, None]
+        pw = g(f"conv.{pw_i}.weight")[:, :, 0, 0]               # [C_out, C_in]
+        y = np.einsum("oc,bchw->bohw", pw, y) + g(f"conv.{pw_i}.bias")[None, :, None, None]
+        y = np.maximum(y, 0.0)
+    _, _, Tp, Fp = y.shape
+    flat = y.transpose(0, 2, 1, 3).reshape(B, Tp, C * Fp)      # idx c*F' + f
+    out_valid = [min(valid_out_len(T, v), Tp) for v in valid_in]
+    m = (np.arange(Tp)[None, :] < np.array(out_valid)[:, None]).astype(np.float64)
+    flat = flat * m[:, :, None]
+    out = flat @ g("out.weight").T + g("out.bias")
+    return out, out_valid
+
+
+# =========================================================== conformer layer
+
+def layer_norm(x, g, b):
+    mean = x.mean(axis=-1, keepdims=True)
+    var = ((x - mean) ** 2).mean(axis=-1, keepdims=True)
+    return (x - mean) / np.sqrt(var + LN_EPS) * g + b
+
+
+def silu(x):
+    return x / (1.0 + np.exp(-x))
+
+
+def sigmoid(x):
+    return 1.0 / (1.0 + np.exp(-x))
+
+
+def linear(x, W, b=None):
+    y = x @ W.T
+    return y + b if b is not None else y
+
+
+def rel_shift_index(bd_raw: np.ndarray) -> np.ndarray:
+    """bd[..., i, j] = bd_raw[..., i, j - i + T - 1] (bd_raw [..., T, 2T-1])."""
+    T = bd_raw.shape[-2]
+    i = np.arange(T)[:, None]
+    j = np.arange(T)[None, :]
+    return np.take_along_axis(bd_raw, np.broadcast_to(j - i + T - 1, bd_raw.shape[:-2] + (T, T)), axis=-1)
+
+
+def rel_shift_literal(bd_raw: np.ndarray) -> np.ndarray:
+    """The reference's rel_shift op sequence (src/relpos_attention.cpp:230-238)
+    replayed on a C-ordered buffer, for one [T_q, 2T-1] slab. ggml ne0 is the
+    fastest axis, so a ggml tensor [ne0, ne1] is a numpy array [ne1, ne0]."""
+    T = bd_raw.shape[0]
+    P = 2 * T - 1
+    padded = np.concatenate([np.zeros((T, 1)), bd_raw], axis=1)       # pad_ext lp0=1 -> [2T, T]
+    flat = padded.reshape(-1)                                          # contiguous
+    as_T_2T = flat.reshape(2 * T, T)                                   # reshape_4d(T, 2T)
+    view = as_T_2T[1:]                                                 # view: 2T-1 rows, offset nb[1]
+    cont = np.ascontiguousarray(view).reshape(-1)                      # cont
+    as_P_T = cont.reshape(T, P)                                        # reshape_4d(2T-1, T)
+    return np.ascontiguousarray(as_P_T[:, :T])                         # view [T, T] offset 0 + cont
+
+
+def relpos_attention(w: Weights, li: int, x: np.ndarray, pe: np.ndarray, valid: int,
+                     literal_shift: bool = False) -> np.ndarray:
+    """RelPosAttention::build_graph_batched for one item (src/relpos_attention.cpp:162-306).
+    x [T, d] (the normalised attention input), pe [2T-1, d]."""
+    T, d = x.shape
+    H = w.H
+    dk = d // H
+    pre = f"encoder.layers.{li}.self_attn."
+    g = lambda n: w.get(pre + n)
+    q = linear(x, g("linear_q.weight"), g("linear_q.bias")).reshape(T, H, dk).transpose(1, 0, 2)
+    k = linear(x, g("linear_k.weight"), g("linear_k.bias")).reshape(T, H, dk).transpose(1, 0, 2)
+    v = linear(x, g("linear_v.weight"), g("linear_v.bias")).reshape(T, H, dk).transpose(1, 0, 2)
+    p = linear(pe.astype(np.float64), g("linear_pos.weight")).reshape(2 * T - 1, H, dk).transpose(1, 0, 2)
+    qu = q + g("pos_bias_u")[:, None, :]
+    qv = q + g("pos_bias_v")[:, None, :]
+    ac = qu @ k.transpose(0, 2, 1)                              # [H, Tq, Tk]
+    bd_raw = qv @ p.transpose(0, 2, 1)                          # [H, Tq, 2T-1]
+    if literal_shift:
+        bd = np.stack([rel_shift_literal(bd_raw[h]) for h in range(H)])
+    else:
+        bd = rel_shift_index(bd_raw)
+    scale = 1.0 / math.sqrt(dk)
+    mask = np.where(np.arange(T) < valid, 0.0, -np.inf)[None, None, :]
+    s = (ac + bd) * scale + mask
+    s = s - s.max(axis=-1, keepdims=True)
+    e = np.exp(s)
+    attn = e / e.sum(axis=-1, keepdims=True)
+    ctx = (attn @ v).transpose(1, 0, 2).reshape(T, d)
+    ctx[valid:] = 0.0
+    return linear(ctx, g("linear_out.weight"), g("linear_out.bias"))
+
+
+def bn_fold(w: Weights, pre: str):
+    """Host BatchNorm fold in f32 (src/conformer.cpp:134-154)."""
+    gmm = w.get(pre + "conv.batch_norm.weight").astype(np.float32)
+    bb = w.get(pre + "conv.batch_norm.bias").astype(np.float32)
+    m = w.get(pre + "conv.batch_norm.running_mean").astype(np.float32)
+    var = w.get(pre + "conv.batch_norm.running_var").astype(np.float32)
+    sc = (gmm / np.sqrt(var + np.float32(BN_EPS))).astype(np.float32)
+    sh = (bb - m * sc).astype(np.float32)
+    return sc.astype(np.float64), sh.astype(np.float64)
+
+
+def conv_module(w: Weights, li: int, c: np.ndarray, valid: int) -> np.ndarray:
+    """build_conv_module for one item (src/conformer.cpp:38-164), batch_norm variant."""
+    T, d = c.shape
+    pre = f"encoder.layers.{li}."
+    g = lambda n: w.get(pre + n)
+    y = linear(c, g("conv.pointwise_conv1.weight")[:, :, 0], g("conv.pointwise_conv1.bias"))
+    glu = y[:, :d] * sigmoid(y[:, d:])
+    glu[valid:] = 0.0
+    K = w.K
+    pad = (K - 1) // 2
+    dww = g("conv.depthwise_conv.weight")[:, 0, :]             # [d, K]
+    gp = np.zeros((T + 2 * pad, d))
+    gp[pad:pad + T] = glu
+    dw = np.zeros((T, d))
+    for k in range(K):
+        dw += gp[k:k + T] * dww[:, k][None, :]
+    if g("conv.depthwise_conv.bias") is not None:
+        dw += g("conv.depthwise_conv.bias")
+    sc, sh = bn_fold(w, pre)
+    nrm = silu(dw * sc + sh)
+    return linear(nrm, g("conv.pointwise_conv2.weight")[:, :, 0], g("conv.pointwise_conv2.bias"))
+
+
+def conformer_layer(w: Weights, li: int, x: np.ndarray, pe: np.ndarray, valid: int) -> np.ndarray:
+    """ConformerLayer::build_graph_batched for one item (src/conformer.cpp:285-353)."""
+    pre = f"encoder.layers.{li}."
+    g = lambda n: w.get(pre + n)
+    ln = lambda t, nm: layer_norm(t, g(nm + ".weight"), g(nm + ".bias"))
+
+    def ff(t, nm):
+        h = silu(linear(t, g(nm + ".linear1.weight"), g(nm + ".linear1.bias")))
+        return linear(h, g(nm + ".linear2.weight"), g(nm + ".linear2.bias"))
+
+    r = x + 0.5 * ff(ln(x, "norm_feed_forward1"), "feed_forward1")
+    r = r + relpos_attention(w, li, ln(r, "norm_self_att"), pe, valid)
+    r = r + conv_module(w, li, ln(r, "norm_conv"), valid)
+    r = r + 0.5 * ff(ln(r, "norm_feed_forward2"), "feed_forward2")
+    return ln(r, "norm_out")
+
+
+@dataclass
+class EncodeResult:
+    outs: list            # per item [valid_b, d] (time-major) float64
+    valid: list
+    Tp: int
+    sub_out: np.ndarray   # subsampling output [B, Tp, d]
+
+
+def encoder_forward_batch(w: Weights, mel: np.ndarray, valid_T: list[int], n_layers: int | None = None,
+                          capture: dict | None = None) -> EncodeResult:
+    """Encoder::forward_batch (src/encoder.cpp:97-167). mel [B, F, T_max]."""
+    B = mel.shape[0]
+    vin = [v - 1 for v in valid_T]
+    x, vout = subsampling_batched(w, mel, vin)
+    sub_out = x.copy()
+    if w.xscaling:
+        x = x * math.sqrt(w.d)
+    Tp = x.shape[1]
+    pe = rel_pos_encoding(Tp, w.d)
+    L = w.L if n_layers is None else n_layers
+    outs = []
+    for b in range(B):
+        xb = x[b]
+        for li in range(L):
+            xb = conformer_layer(w, li, xb, pe, vout[b])
+            if capture is not None:
+                capture.setdefault(li, []).append(xb[:vout[b]].copy())
+        outs.append(xb[:vout[b]])
+    return EncodeResult(outs, vout, Tp, sub_out)
+
+
+def encode_pcm_batch(w: Weights, pcms, n_layers: int | None = None, gpu_graph_mel: bool = True):
+    """Model::transcribe_16k_batch steps 1-2 (src/model.cpp:164-181)."""
+    mel, Ts = mel_batch(w, pcms, gpu_graph=gpu_graph_mel)
+    return encoder_forward_batch(w, mel, Ts, n_layers=n_layers)

@@ -1,0 +1,320 @@
+// The model-level C ABI (include/pkc.h): open/close, mel front end, encoder,
+// multi-GPU sharding and profiling. No exception crosses this boundary.
+#include <algorithm>
+#include <cstring>
+#include <memory>
+#include <mutex>
+#include <numeric>
+#include <thread>
+
+#include "../../include/pkc.h"
+#include "encoder.hpp"
+#include "gguf.hpp"
+#include "model.hpp"
+#include "status.hpp"
+
+struct pkc_model {
+  pkc::Config cfg;
+  std::vector<std::unique_ptr<pkc::DeviceRunner>> runners;
+  std::mutex mu;
+  std::string last_error;
+};
+
+namespace pkc {
+const char* model_error(const pkc_model* m) { return m->last_error.c_str(); }
+}  // namespace pkc
+
+namespace {
+
+pkc_status fail(pkc_model* m, pkc_status st, const std::string& msg) {
+  m->last_error = msg;
+  return st;
+}
+
+// Encoder frames (T') of a clip, and the sharding cost T'(1 + T'/8192):
+// linear work per frame plus the attention's quadratic term.
+double clip_cost(int v) { return (double)v * (1.0 + (double)v / 8192.0); }
+
+void lpt_assign(const std::vector<double>& cost, int n_dev, std::vector<int>& assign) {
+  const int B = (int)cost.size();
+  std::vector<int> order(B);
+  std::iota(order.begin(), order.end(), 0);
+  std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return cost[a] > cost[b]; });
+  std::vector<double> load(n_dev, 0.0);
+  assign.assign(B, 0);
+  for (int b : order) {
+    int best = 0;
+    for (int k = 1; k < n_dev; ++k)
+      if (load[k] < load[best]) best = k;
+    assign[b] = best;
+    load[best] += cost[b];
+  }
+}
+
+}  // namespace
+
+extern "C" {
+
+pkc_status pkc_model_open(const char* gguf_path, const int* devices, int n_devices, pkc_model** out) {
+  if (!out) return pkc::set_thread_error(PKC_ERR_ARG, "pkc_model_open: out is NULL");
+  *out = nullptr;
+  if (!gguf_path) return pkc::set_thread_error(PKC_ERR_ARG, "pkc_model_open: path is NULL");
+  try {
+    auto g = std::make_unique<pkc::GgufFile>();
+    std::string err;
+    if (!g->open(gguf_path, err))
+      return pkc::set_thread_error(err.rfind("cannot open", 0) == 0 ? PKC_ERR_IO : PKC_ERR_FORMAT, err);
+    auto m = std::make_unique<pkc_model>();
+    err = pkc::read_config(*g, m->cfg);
+    if (!err.empty()) return pkc::set_thread_error(PKC_ERR_UNSUPPORTED, err);
+    std::vector<int> devs;
+    if (!devices || n_devices <= 0) devs.push_back(0);
+    else devs.assign(devices, devices + n_devices);
+    int count = 0;
+    if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0)
+      return pkc::set_thread_error(PKC_ERR_CUDA, "no CUDA device available");
+    for (int dv : devs) {
+      if (dv < 0 || dv >= count)
+        return pkc::set_thread_error(PKC_ERR_ARG, "device index " + std::to_string(dv) + " out of range");
+      auto r = std::make_unique<pkc::DeviceRunner>(m->cfg, dv);
+      err = r->init(*g);
+      if (!err.empty()) {
+        const bool oom = err.find("cudaMalloc") != std::string::npos;
+        return pkc::set_thread_error(oom ? PKC_ERR_OOM : (err.find("tensor") != std::string::npos ? PKC_ERR_FORMAT : PKC_ERR_CUDA), err);
+      }
+      m->runners.push_back(std::move(r));
+    }
+    *out = m.release();
+    return PKC_OK;
+  } catch (const std::bad_alloc&) {
+    return pkc::set_thread_error(PKC_ERR_OOM, "host allocation failed");
+  } catch (const std::exception& e) {
+    return pkc::set_thread_error(PKC_ERR_INTERNAL, e.what());
+  }
+}
+
+void pkc_model_close(pkc_model* m) {
+  if (!m) return;
+  try {
+    delete m;
+  } catch (...) {
+  }
+}
+
+pkc_status pkc_model_info_get(const pkc_model* m, pkc_model_info* o) {
+  if (!m || !o) return pkc::set_thread_error(PKC_ERR_ARG, "pkc_model_info_get: NULL argument");
+  const pkc::Config& c = m->cfg;
+  std::memset(o, 0, sizeof(*o));
+  o->d_model = c.d_model; o->n_layers = c.n_layers; o->n_heads = c.n_heads; o->ff_dim = c.ff_dim;
+  o->conv_kernel = c.conv_kernel; o->n_mels = c.n_mels; o->n_fft = c.n_fft;
+  o->win_length = c.win_length; o->hop_length = c.hop_length; o->sample_rate = c.sample_rate;
+  o->subsampling_factor = c.subsampling_factor; o->subsampling_conv_channels = c.sub_channels;
+  o->xscaling = c.xscaling ? 1 : 0; o->weight_type = (int)c.weight_type;
+  o->compute_bf16 = c.bf16 ? 1 : 0; o->n_devices = (int)m->runners.size();
+  o->vocab_size = c.vocab_size; o->blank_id = c.blank_id;
+  std::strncpy(o->arch, c.arch.c_str(), sizeof(o->arch) - 1);
+  return PKC_OK;
+}
+
+int pkc_mel_frames(const pkc_model* m, int n_samples) {
+  if (!m || n_samples < 0) return 0;
+  return pkc::mel_frames_for(m->cfg, n_samples);
+}
+
+int pkc_encoder_frames(const pkc_model* m, int mel_frames) {
+  if (!m || mel_frames <= 0) return 0;
+  return pkc::encoder_frames_for(mel_frames);
+}
+
+size_t pkc_encode_out_floats(const pkc_model* m, const int* n_samples, int B) {
+  if (!m || !n_samples || B <= 0) return 0;
+  size_t n = 0;
+  for (int b = 0; b < B; ++b)
+    n += (size_t)pkc::encoder_frames_for(pkc::mel_frames_for(m->cfg, n_samples[b])) * m->cfg.d_model;
+  return n;
+}
+
+pkc_status pkc_shard_plan(const int* n_samples, int B, int n_dev, int hop, int* assign) {
+  if (!n_samples || !assign || B < 0 || n_dev <= 0 || hop <= 0)
+    return pkc::set_thread_error(PKC_ERR_ARG, "pkc_shard_plan: bad arguments");
+  std::vector<double> cost(B);
+  for (int b = 0; b < B; ++b) {
+    if (n_samples[b] <= 0) return pkc::set_thread_error(PKC_ERR_ARG, "pkc_shard_plan: empty clip");
+    cost[b] = clip_cost(pkc::encoder_frames_for(1 + n_samples[b] / hop));
+  }
+  std::vector<int> a;
+  lpt_assign(cost, n_dev, a);
+  std::copy(a.begin(), a.end(), assign);
+  return PKC_OK;
+}
+
+pkc_status pkc_mel_batch(pkc_model* m, const float* const* pcm, const int* n_samples, int B,
+                         float* feats_out, size_t feats_cap, int* T_out) {
+  if (!m) return pkc::set_thread_error(PKC_ERR_ARG, "pkc_mel_batch: model is NULL");
+  std::lock_guard<std::mutex> lk(m->mu);
+  if (!pcm || !n_samples || B <= 0 || !feats_out || !T_out) return fail(m, PKC_ERR_ARG, "pkc_mel_batch: bad arguments");
+  try {
+    std::vector<const float*> p(pcm, pcm + B);
+    std::vector<int> n(n_samples, n_samples + B);
+    int Tmax = 0;
+    for (int b = 0; b < B; ++b) {
+      if (n[b] <= 0 || !p[b]) return fail(m, PKC_ERR_ARG, "pkc_mel_batch: empty clip " + std::to_string(b));
+      T_out[b] = pkc::mel_frames_for(m->cfg, n[b]);
+      Tmax = std::max(Tmax, T_out[b]);
+    }
+    if ((size_t)B * m->cfg.n_mels * Tmax > feats_cap) return fail(m, PKC_ERR_ARG, "pkc_mel_batch: feats_out too small");
+    std::string err;
+    const pkc_status s = m->runners[0]->mel_host(p, n, Tmax, feats_out, err);
+    return s == PKC_OK ? s : fail(m, s, err);
+  } catch (const std::exception& e) {
+    return fail(m, PKC_ERR_INTERNAL, e.what());
+  }
+}
+
+pkc_status pkc_encode_batch(pkc_model* m, const float* mel, int B, int n_mels, int T_max,
+                            const int* valid_T, int layout, float* out, size_t out_cap,
+                            int* valid_Tout, int* d_model_out) {
+  if (!m) return pkc::set_thread_error(PKC_ERR_ARG, "pkc_encode_batch: model is NULL");
+  std::lock_guard<std::mutex> lk(m->mu);
+  if (!mel || B <= 0 || T_max <= 0 || !valid_T || !out || !valid_Tout)
+    return fail(m, PKC_ERR_ARG, "pkc_encode_batch: bad arguments");
+  if (n_mels != m->cfg.n_mels) return fail(m, PKC_ERR_ARG, "pkc_encode_batch: n_mels does not match the model");
+  if (layout != PKC_LAYOUT_CHANNELS_FIRST && layout != PKC_LAYOUT_TIME_MAJOR)
+    return fail(m, PKC_ERR_ARG, "pkc_encode_batch: unknown layout");
+  try {
+    size_t need = 0;
+    for (int b = 0; b < B; ++b) {
+      if (valid_T[b] < 1 || valid_T[b] > T_max) return fail(m, PKC_ERR_ARG, "pkc_encode_batch: valid_T out of range");
+      valid_Tout[b] = pkc::encoder_frames_for(valid_T[b]);
+      need += (size_t)valid_Tout[b] * m->cfg.d_model;
+    }
+    if (need > out_cap) return fail(m, PKC_ERR_ARG, "pkc_encode_batch: out too small");
+    if (d_model_out) *d_model_out = m->cfg.d_model;
+    std::string err;
+    const pkc_status s = m->runners[0]->encode_mel_host(mel, B, n_mels, T_max, valid_T, layout, out, err);
+    return s == PKC_OK ? s : fail(m, s, err);
+  } catch (const std::exception& e) {
+    return fail(m, PKC_ERR_INTERNAL, e.what());
+  }
+}
+
+pkc_status pkc_encode_pcm_batch(pkc_model* m, const float* const* pcm, const int* n_samples, int B,
+                                int layout, float* out, size_t out_cap, int* valid_Tout) {
+  if (!m) return pkc::set_thread_error(PKC_ERR_ARG, "pkc_encode_pcm_batch: model is NULL");
+  std::lock_guard<std::mutex> lk(m->mu);
+  if (!pcm || !n_samples || B <= 0 || !out || !valid_Tout)
+    return fail(m, PKC_ERR_ARG, "pkc_encode_pcm_batch: bad arguments");
+  if (layout != PKC_LAYOUT_CHANNELS_FIRST && layout != PKC_LAYOUT_TIME_MAJOR)
+    return fail(m, PKC_ERR_ARG, "pkc_encode_pcm_batch: unknown layout");
+  try {
+    const int d = m->cfg.d_model;
+    std::vector<size_t> off(B + 1, 0);
+    for (int b = 0; b < B; ++b) {
+      if (n_samples[b] <= 0 || !pcm[b]) return fail(m, PKC_ERR_ARG, "pkc_encode_pcm_batch: empty clip " + std::to_string(b));
+      valid_Tout[b] = pkc::encoder_frames_for(pkc::mel_frames_for(m->cfg, n_samples[b]));
+      off[b + 1] = off[b] + (size_t)valid_Tout[b] * d;
+    }
+    if (off[B] > out_cap) return fail(m, PKC_ERR_ARG, "pkc_encode_pcm_batch: out too small");
+    const int nd = (int)m->runners.size();
+    if (nd == 1) {
+      std::string err;
+      std::vector<const float*> p(pcm, pcm + B);
+      std::vector<int> n(n_samples, n_samples + B);
+      const pkc_status s = m->runners[0]->encode_pcm_host(p, n, layout, out, err);
+      return s == PKC_OK ? s : fail(m, s, err);
+    }
+    // shard whole utterances across devices (no collective: each device runs
+    // its own clips end to end), then scatter the outputs back in order
+    std::vector<double> cost(B);
+    for (int b = 0; b < B; ++b) cost[b] = clip_cost(valid_Tout[b]);
+    std::vector<int> assign;
+    lpt_assign(cost, nd, assign);
+    std::vector<std::vector<int>> items(nd);
+    for (int b = 0; b < B; ++b) items[assign[b]].push_back(b);
+    std::vector<std::vector<float>> bufs(nd);
+    std::vector<pkc_status> st(nd, PKC_OK);
+    std::vector<std::string> errs(nd);
+    std::vector<std::thread> th;
+    for (int k = 0; k < nd; ++k) {
+      if (items[k].empty()) continue;
+      th.emplace_back([&, k] {
+        try {
+          std::vector<const float*> p;
+          std::vector<int> n;
+          size_t tot = 0;
+          for (int b : items[k]) { p.push_back(pcm[b]); n.push_back(n_samples[b]); tot += off[b + 1] - off[b]; }
+          bufs[k].resize(tot);
+          st[k] = m->runners[k]->encode_pcm_host(p, n, layout, bufs[k].data(), errs[k]);
+        } catch (const std::exception& e) {
+          st[k] = PKC_ERR_INTERNAL;
+          errs[k] = e.what();
+        }
+      });
+    }
+    for (auto& t : th) t.join();
+    for (int k = 0; k < nd; ++k)
+      if (st[k] != PKC_OK) return fail(m, st[k], "device " + std::to_string(m->runners[k]->device()) + ": " + errs[k]);
+    for (int k = 0; k < nd; ++k) {
+      size_t pos = 0;
+      for (int b : items[k]) {
+        const size_t n = off[b + 1] - off[b];
+        std::memcpy(out + off[b], bufs[k].data() + pos, n * 4);
+        pos += n;
+      }
+    }
+    return PKC_OK;
+  } catch (const std::exception& e) {
+    return fail(m, PKC_ERR_INTERNAL, e.what());
+  }
+}
+
+pkc_status pkc_encode_pcm_device(pkc_model* m, int device_slot, const float* d_pcm,
+                                 const int* n_samples, int B, float* d_out, void* stream, int sync) {
+  if (!m) return pkc::set_thread_error(PKC_ERR_ARG, "pkc_encode_pcm_device: model is NULL");
+  std::lock_guard<std::mutex> lk(m->mu);
+  if (!d_pcm || !n_samples || B <= 0 || !d_out) return fail(m, PKC_ERR_ARG, "pkc_encode_pcm_device: bad arguments");
+  if (device_slot < 0 || device_slot >= (int)m->runners.size())
+    return fail(m, PKC_ERR_ARG, "pkc_encode_pcm_device: bad device slot");
+  try {
+    std::vector<int> n(n_samples, n_samples + B);
+    for (int b = 0; b < B; ++b)
+      if (n[b] <= 0) return fail(m, PKC_ERR_ARG, "pkc_encode_pcm_device: empty clip");
+    std::string err;
+    const pkc_status s = m->runners[device_slot]->encode_pcm_device(
+        d_pcm, n, d_out, reinterpret_cast<cudaStream_t>(stream), sync != 0, err);
+    return s == PKC_OK ? s : fail(m, s, err);
+  } catch (const std::exception& e) {
+    return fail(m, PKC_ERR_INTERNAL, e.what());
+  }
+}
+
+pkc_status pkc_profile_enable(pkc_model* m, int enable) {
+  if (!m) return pkc::set_thread_error(PKC_ERR_ARG, "pkc_profile_enable: model is NULL");
+  std::lock_guard<std::mutex> lk(m->mu);
+  for (auto& r : m->runners) r->profile_enable(enable != 0);
+  return PKC_OK;
+}
+
+int pkc_profile_read(pkc_model* m, pkc_kernel_stat* out, int cap) {
+  if (!m || !out || cap <= 0) return 0;
+  std::lock_guard<std::mutex> lk(m->mu);
+  std::vector<pkc::KernelStatAcc> all;
+  for (auto& r : m->runners)
+    for (const auto& k : r->profile_read()) {
+      auto it = std::find_if(all.begin(), all.end(), [&](const pkc::KernelStatAcc& a) { return a.name == k.name; });
+      if (it == all.end()) all.push_back(k);
+      else { it->launches += k.launches; it->ms += k.ms; it->flops += k.flops; it->bytes += k.bytes; }
+    }
+  const int n = std::min<int>(cap, (int)all.size());
+  for (int i = 0; i < n; ++i) {
+    std::memset(&out[i], 0, sizeof(out[i]));
+    std::strncpy(out[i].name, all[i].name.c_str(), sizeof(out[i].name) - 1);
+    out[i].launches = all[i].launches;
+    out[i].total_ms = all[i].ms;
+    out[i].flops = all[i].flops;
+    out[i].bytes = all[i].bytes;
+  }
+  return n;
+}
+
+}  // extern "C"

@@ -1,0 +1,510 @@
+// Per-device encoder runtime: batch planning, workspace, and the launch
+// sequence that replaces the reference's single fused ggml graph
+// (Encoder::forward_batch, src/encoder.cpp:97-167; ConformerLayer::
+// build_graph_batched, src/conformer.cpp:285-353).
+//
+// One conformer layer is 15 launches on one stream:
+//   LN(ff1) [fused with the previous layer's LN(out)] -> GEMM+SiLU -> GEMM+0.5*res
+//   LN(att) -> QKV GEMM -> pos GEMM -> rel-pos flash attention -> out GEMM+res
+//   LN(conv) -> pw1 GEMM+GLU -> depthwise+BN+SiLU -> pw2 GEMM+res
+//   LN(ff2) -> GEMM+SiLU -> GEMM+0.5*res -> LN(out)
+#include "encoder.hpp"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+
+#include "kernels/gemm.h"
+#include "kernels/kernels.h"
+
+namespace pkc {
+
+int mel_frames_for(const Config& c, int S) {
+  const int pad = c.n_fft / 2;
+  const int padded = S + 2 * pad;
+  return padded >= c.n_fft ? 1 + (padded - c.n_fft) / c.hop_length : 0;
+}
+
+// Subsampling::valid_out_len with the offline T-1 entry (src/subsampling.cpp:25-46);
+// C++ integer division truncates toward zero exactly like the reference's.
+static int stage_len(int v) { return (v + 2 - 3) / 2 + 1; }
+int encoder_frames_for(int T) { return stage_len(stage_len(stage_len(T - 1))); }
+
+void make_plan(const Config& c, const std::vector<int>& n_samples, const std::vector<int>& mel_T,
+               Plan& p) {
+  const bool pcm = !n_samples.empty();
+  p = Plan();
+  p.B = (int)(pcm ? n_samples.size() : mel_T.size());
+  const int B = p.B;
+  p.S.assign(B, 0); p.pcm_off.assign(B + 1, 0);
+  p.Tm.assign(B, 0); p.mel_off.assign(B + 1, 0); p.mval.assign(B, 0);
+  p.v1.assign(B, 0); p.v1_off.assign(B + 1, 0);
+  p.v2.assign(B, 0); p.v2_off.assign(B + 1, 0);
+  p.v.assign(B, 0); p.v_off.assign(B + 1, 0);
+  for (int b = 0; b < B; ++b) {
+    p.S[b] = pcm ? n_samples[b] : 0;
+    p.Tm[b] = pcm ? mel_frames_for(c, n_samples[b]) : mel_T[b];
+    p.mval[b] = p.Tm[b] - 1;
+    p.v1[b] = stage_len(p.mval[b]);
+    p.v2[b] = stage_len(p.v1[b]);
+    p.v[b] = stage_len(p.v2[b]);
+    p.pcm_off[b + 1] = p.pcm_off[b] + p.S[b];
+    p.mel_off[b + 1] = p.mel_off[b] + p.Tm[b];
+    p.v1_off[b + 1] = p.v1_off[b] + p.v1[b];
+    p.v2_off[b + 1] = p.v2_off[b] + p.v2[b];
+    p.v_off[b + 1] = p.v_off[b] + p.v[b];
+    p.max_Tm = std::max(p.max_Tm, p.Tm[b]);
+    p.max_v1 = std::max(p.max_v1, p.v1[b]);
+    p.max_v2 = std::max(p.max_v2, p.v2[b]);
+    p.max_v = std::max(p.max_v, p.v[b]);
+  }
+  p.total_samples = p.pcm_off[B];
+  p.total_frames = p.mel_off[B];
+  p.M1 = p.v1_off[B];
+  p.M2 = p.v2_off[B];
+  p.M = p.v_off[B];
+  p.centre = p.max_v;
+  const int qt = attn_query_tile();
+  for (int b = 0; b < B; ++b)
+    for (int q0 = 0; q0 < p.v[b]; q0 += qt) {
+      p.attn_tiles.push_back(b);
+      p.attn_tiles.push_back(q0);
+    }
+}
+
+namespace {
+size_t al(size_t x) { return (x + 255) / 256 * 256; }
+}  // namespace
+
+DeviceRunner::~DeviceRunner() {
+  cudaSetDevice(device_);
+  if (stream_) cudaStreamSynchronize(stream_);
+  for (cudaEvent_t e : ev_pool_) cudaEventDestroy(e);
+  if (ws_) cudaFree(ws_);
+  if (err_word_) cudaFree(err_word_);
+  if (h_tables_) cudaFreeHost(h_tables_);
+  free_weights(w_);
+  if (stream_) cudaStreamDestroy(stream_);
+}
+
+std::string DeviceRunner::init(const GgufFile& g) {
+  if (cudaSetDevice(device_) != cudaSuccess) return "cannot select CUDA device " + std::to_string(device_);
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, device_) != cudaSuccess) return "cudaGetDeviceProperties failed";
+  if (prop.major != 10) return std::string("device ") + prop.name + " is not sm_100 (B200); the kernels are sm_100a only";
+  if (cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking) != cudaSuccess) return "stream creation failed";
+  if (cudaMalloc(&err_word_, sizeof(int)) != cudaSuccess) return "cudaMalloc failed";
+  cudaMemset(err_word_, 0, sizeof(int));
+  power_ld_ = cfg_.n_fft / 2 + 8;
+  return upload_weights(g, cfg_, w_);
+}
+
+bool DeviceRunner::ensure_ws(size_t bytes) {
+  if (bytes <= ws_bytes_) return true;
+  last_key_.clear();
+  cudaStreamSynchronize(stream_);
+  if (ws_) cudaFree(ws_);
+  ws_ = nullptr;
+  ws_bytes_ = 0;
+  const size_t want = bytes + bytes / 8;
+  if (cudaMalloc(&ws_, want) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  ws_bytes_ = want;
+  return true;
+}
+
+// ------------------------------------------------------------------ profiling
+void DeviceRunner::profile_enable(bool on) {
+  cudaSetDevice(device_);
+  cudaStreamSynchronize(stream_);
+  prof_on_ = on;
+  prof_recs_.clear();
+  prof_classes_.clear();
+  ev_next_ = 0;
+}
+
+void DeviceRunner::prof_begin(cudaStream_t st) {
+  if (!prof_on_) return;
+  if (ev_next_ + 2 > ev_pool_.size()) {
+    for (int i = 0; i < 256; ++i) {
+      cudaEvent_t e;
+      cudaEventCreate(&e);
+      ev_pool_.push_back(e);
+    }
+  }
+  prof_open_ = ev_pool_[ev_next_++];
+  cudaEventRecord(prof_open_, st);
+}
+
+void DeviceRunner::prof_end(cudaStream_t st, const char* name, double flops, double bytes) {
+  if (!prof_on_) return;
+  cudaEvent_t e = ev_pool_[ev_next_++];
+  cudaEventRecord(e, st);
+  int cls = -1;
+  for (size_t i = 0; i < prof_classes_.size(); ++i)
+    if (prof_classes_[i].name == name) cls = (int)i;
+  if (cls < 0) {
+    prof_classes_.push_back(KernelStatAcc{name});
+    cls = (int)prof_classes_.size() - 1;
+  }
+  prof_recs_.push_back(ProfRec{cls, prof_open_, e, flops, bytes});
+}
+
+std::vector<KernelStatAcc> DeviceRunner::profile_read() {
+  cudaSetDevice(device_);
+  cudaStreamSynchronize(stream_);
+  for (const ProfRec& r : prof_recs_) {
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, r.a, r.b);
+    KernelStatAcc& k = prof_classes_[r.cls];
+    k.launches += 1;
+    k.ms += ms;
+    k.flops += r.flops;
+    k.bytes += r.bytes;
+  }
+  prof_recs_.clear();
+  ev_next_ = 0;
+  return prof_classes_;
+}
+
+// ------------------------------------------------------------------ launches
+pkc_status DeviceRunner::gemm(const void* A, int lda, const void* B, int ldb, bool bf16, int M,
+                              int N, int K, int epi, int act, float alpha, const float* bias,
+                              void* out, int ldo, cudaStream_t st, const char* name,
+                              std::string& err) {
+  GemmArgs a{};
+  a.M = M; a.N = N; a.K = K; a.epi = epi; a.act = act; a.alpha = alpha; a.bias = bias;
+  a.out = out; a.ldo = ldo; a.err = err_word_;
+  prof_begin(st);
+  const cudaError_t e = gemm_launch(A, lda, B, ldb, bf16, a, st);
+  const int osz = (epi == EPI_RESID_F32 || epi == EPI_STORE_F32 || epi == EPI_POWER_F32) ? 4 : 2;
+  const int ncols = (epi == EPI_GLU_H || epi == EPI_POWER_F32) ? N / 2 : N;
+  prof_end(st, name, 2.0 * M * N * K,
+           2.0 * ((double)M * K + (double)N * K) + (double)M * ncols * osz * (epi == EPI_RESID_F32 ? 2 : 1));
+  if (e != cudaSuccess) {
+    err = std::string("GEMM ") + name + " launch failed: " + cudaGetErrorString(e);
+    return PKC_ERR_CUDA;
+  }
+  return PKC_OK;
+}
+
+#define PKC_CK(expr, what)                                                             \
+  do {                                                                                 \
+    cudaError_t e_ = (expr);                                                           \
+    if (e_ != cudaSuccess) {                                                           \
+      err = std::string(what) + ": " + cudaGetErrorString(e_);                         \
+      return PKC_ERR_CUDA;                                                             \
+    }                                                                                  \
+  } while (0)
+#define PKC_ST(expr)                 \
+  do {                               \
+    pkc_status s_ = (expr);          \
+    if (s_ != PKC_OK) return s_;     \
+  } while (0)
+
+pkc_status DeviceRunner::prepare(const Plan& p, cudaStream_t st, std::string& err) {
+  const Config& c = cfg_;
+  const int d = c.d_model, F = c.n_mels, C = c.sub_channels;
+  const size_t hs = 2;
+  const int B = p.B;
+  // Same geometry as the previous batch on this stream: tables and carve are
+  // still valid (lets a device-resident caller launch step after step without
+  // a host synchronisation in between).
+  std::vector<int> key;
+  key.reserve(2 * (size_t)B + 2);
+  key.push_back(B);
+  for (int b = 0; b < B; ++b) { key.push_back(p.S[b]); key.push_back(p.Tm[b]); }
+  if (!last_key_.empty() && key == last_key_) return PKC_OK;
+  last_key_.clear();
+  const int ntiles = (int)p.attn_tiles.size() / 2;
+  const size_t n_tab = (size_t)(B + 1) * 5 + (size_t)B * 6 + (size_t)ntiles * 2 + 8;
+  const int np = std::max(1, 2 * p.centre - 1);
+  size_t sz = 0;
+  auto take = [&](size_t bytes) { const size_t o = sz; sz += al(bytes); return o; };
+  const size_t o_tab = take(n_tab * 4);
+  const size_t o_pcm = take((size_t)p.total_samples * 4);
+  const size_t o_dft = take((size_t)p.total_frames * 3 * c.n_fft * 2);
+  const size_t o_pow = take((size_t)p.total_frames * power_ld_ * 4);
+  const size_t o_log = take((size_t)p.total_frames * F * 4);
+  const size_t o_mb = take((size_t)B * F * p.max_Tm * 4);
+  const size_t o_s1 = take((size_t)p.M1 * c.F1 * C * 2);
+  const size_t o_s2a = take((size_t)p.M2 * c.F2 * C * 2);
+  const size_t o_s2b = take((size_t)p.M2 * c.F2 * C * 2);
+  const size_t o_s3a = take((size_t)p.M * c.F3 * C * 2);
+  const size_t o_s3b = take((size_t)p.M * c.F3 * C * 2);
+  const size_t o_x = take((size_t)p.M * d * 4);
+  const size_t o_h = take((size_t)p.M * d * hs);
+  const size_t o_ff = take((size_t)p.M * c.ff_dim * hs);
+  const size_t o_qkv = take((size_t)p.M * 3 * d * hs);
+  const size_t o_ctx = take((size_t)p.M * d * hs);
+  const size_t o_pe = take((size_t)np * d * hs);
+  const size_t o_pt = take((size_t)np * d * hs);
+  const size_t o_out = take((size_t)p.M * d * 4);
+  if (!ensure_ws(sz)) {
+    err = "workspace allocation of " + std::to_string(sz) + " bytes failed";
+    return PKC_ERR_OOM;
+  }
+  uint8_t* base = static_cast<uint8_t*>(ws_);
+  b_.tables = reinterpret_cast<int*>(base + o_tab);
+  b_.pcm = reinterpret_cast<float*>(base + o_pcm);
+  b_.dft_a = base + o_dft;
+  b_.power = reinterpret_cast<float*>(base + o_pow);
+  b_.logmel = reinterpret_cast<float*>(base + o_log);
+  b_.melbatch = reinterpret_cast<float*>(base + o_mb);
+  b_.s1 = base + o_s1; b_.s2a = base + o_s2a; b_.s2b = base + o_s2b;
+  b_.s3a = base + o_s3a; b_.s3b = base + o_s3b;
+  b_.x = reinterpret_cast<float*>(base + o_x);
+  b_.hbuf = base + o_h; b_.ffh = base + o_ff; b_.qkv = base + o_qkv; b_.ctx = base + o_ctx;
+  b_.pe = base + o_pe; b_.ptab = base + o_pt;
+  b_.out = reinterpret_cast<float*>(base + o_out);
+
+  // item tables -> pinned staging -> device (one copy)
+  if (h_tables_cap_ < n_tab) {
+    cudaStreamSynchronize(st);
+    if (h_tables_) cudaFreeHost(h_tables_);
+    h_tables_ = nullptr;
+    h_tables_cap_ = 0;
+    PKC_CK(cudaMallocHost(&h_tables_, n_tab * 2 * 4), "pinned table allocation");
+    h_tables_cap_ = n_tab * 2;
+  } else {
+    cudaStreamSynchronize(st);  // the previous table upload has finished reading
+  }
+  int* h = h_tables_;
+  int* dv = b_.tables;
+  size_t pos = 0;
+  auto put = [&](const std::vector<int>& v, int*& dst) {
+    std::memcpy(h + pos, v.data(), v.size() * 4);
+    dst = dv + pos;
+    pos += v.size();
+  };
+  put(p.pcm_off, t_pcm_off); put(p.S, t_S); put(p.mel_off, t_mel_off); put(p.Tm, t_Tm);
+  put(p.mval, t_mval); put(p.v1_off, t_v1_off); put(p.v1, t_v1); put(p.v2_off, t_v2_off);
+  put(p.v2, t_v2); put(p.v_off, t_v_off); put(p.v, t_v); put(p.attn_tiles, t_tiles);
+  PKC_CK(cudaMemcpyAsync(dv, h, pos * 4, cudaMemcpyHostToDevice, st), "table upload");
+  last_key_ = std::move(key);
+  return PKC_OK;
+}
+
+pkc_status DeviceRunner::run_frontend(const Plan& p, cudaStream_t st, std::string& err) {
+  const Config& c = cfg_;
+  ItemTables t{p.B, t_pcm_off, t_S, t_mel_off, t_Tm, t_mval, t_v1_off, t_v1, t_v2_off, t_v2, t_v_off, t_v};
+  MelArgs ma{b_.pcm, w_.window, c.n_fft, c.hop_length, c.preemph, p.total_frames,
+             reinterpret_cast<__half*>(b_.dft_a), b_.power, power_ld_};
+  prof_begin(st);
+  PKC_CK(mel_frames_launch(ma, t, st), "mel_frames");
+  prof_end(st, "mel_frames", 0.0, (double)p.total_samples * 4 * 3.2 + (double)p.total_frames * 3 * c.n_fft * 2);
+  PKC_ST(gemm(b_.dft_a, 3 * c.n_fft, w_.dft_basis, 3 * c.n_fft, false, p.total_frames, c.n_fft,
+              3 * c.n_fft, EPI_POWER_F32, ACT_NONE, 1.f, nullptr, b_.power, power_ld_, st, "gemm_dft", err));
+  FbArgs fa{b_.power, power_ld_, w_.fb_start, w_.fb_len, w_.fb_off, w_.fb_w, c.n_mels,
+            c.log_zero_guard, p.total_frames, b_.logmel};
+  prof_begin(st);
+  PKC_CK(mel_fb_log_launch(fa, st), "mel_fb_log");
+  prof_end(st, "mel_fb_log", 0.0, (double)p.total_frames * (power_ld_ + c.n_mels) * 4);
+  prof_begin(st);
+  PKC_CK(mel_norm_launch(b_.logmel, c.n_mels, t, st), "mel_norm");
+  prof_end(st, "mel_norm", 0.0, (double)p.total_frames * c.n_mels * 4 * 3);
+  return PKC_OK;
+}
+
+pkc_status DeviceRunner::run_encoder(const Plan& p, cudaStream_t st, std::string& err) {
+  const Config& c = cfg_;
+  const int d = c.d_model, FF = c.ff_dim, C = c.sub_channels, H = c.n_heads, K = c.conv_kernel;
+  const bool bf = c.bf16;
+  const int M = p.M;
+  const double hs = 2.0;
+  ItemTables t{p.B, t_pcm_off, t_S, t_mel_off, t_Tm, t_mval, t_v1_off, t_v1, t_v2_off, t_v2, t_v_off, t_v};
+
+  // ---- subsampling (src/subsampling.cpp:48-240)
+  prof_begin(st);
+  PKC_CK(sub_conv0_launch(b_.logmel, c.n_mels, w_.c0_w, w_.c0_b, C,
+                          reinterpret_cast<__nv_bfloat16*>(b_.s1), c.F1, t, p.max_v1, st), "conv0");
+  prof_end(st, "sub_conv0", 2.0 * p.M1 * c.F1 * C * 9, (double)p.total_frames * c.n_mels * 4 + (double)p.M1 * c.F1 * C * 2);
+  prof_begin(st);
+  PKC_CK(sub_dw_launch(reinterpret_cast<const __nv_bfloat16*>(b_.s1), c.F1, t_v1_off, t_v1, w_.dw1_w,
+                       w_.dw1_b, C, reinterpret_cast<__nv_bfloat16*>(b_.s2a), c.F2, t_v2_off, t_v2, p.B,
+                       p.max_v2, st), "dw1");
+  prof_end(st, "sub_dw", 2.0 * p.M2 * c.F2 * C * 9, ((double)p.M1 * c.F1 + (double)p.M2 * c.F2) * C * 2);
+  PKC_ST(gemm(b_.s2a, C, w_.pw1_w, C, true, p.M2 * c.F2, C, C, EPI_STORE_H, ACT_RELU, 1.f, w_.pw1_b,
+              b_.s2b, C, st, "gemm_sub_pw", err));
+  prof_begin(st);
+  PKC_CK(sub_dw_launch(reinterpret_cast<const __nv_bfloat16*>(b_.s2b), c.F2, t_v2_off, t_v2, w_.dw2_w,
+                       w_.dw2_b, C, reinterpret_cast<__nv_bfloat16*>(b_.s3a), c.F3, t_v_off, t_v, p.B,
+                       p.max_v, st), "dw2");
+  prof_end(st, "sub_dw", 2.0 * M * c.F3 * C * 9, ((double)p.M2 * c.F2 + (double)M * c.F3) * C * 2);
+  PKC_ST(gemm(b_.s3a, C, w_.pw2_w, C, true, M * c.F3, C, C, EPI_STORE_H, ACT_RELU, 1.f, w_.pw2_b,
+              b_.s3b, C, st, "gemm_sub_pw", err));
+  const float xs = c.xscaling ? std::sqrt((float)d) : 1.f;
+  PKC_ST(gemm(b_.s3b, c.F3 * C, w_.out_w, c.F3 * C, true, M, d, c.F3 * C, EPI_STORE_F32, ACT_NONE, xs,
+              w_.out_b, b_.x, d, st, "gemm_sub_out", err));
+
+  // ---- relative positional table (src/pos_enc.cpp:10-34), shared by the batch
+  const int np = 2 * p.centre - 1;
+  prof_begin(st);
+  PKC_CK(pos_table_launch(b_.pe, p.centre, d, bf, st), "pos_table");
+  prof_end(st, "pos_table", 0.0, (double)np * d * hs);
+
+  const int ntiles = (int)p.attn_tiles.size() / 2;
+  double attn_flops = 0.0;
+  for (int b = 0; b < p.B; ++b) {
+    const double T = p.v[b];
+    attn_flops += 2.0 * T * T * d * 2 + 2.0 * T * (2 * T - 1) * d;
+  }
+  for (int li = 0; li < c.n_layers; ++li) {
+    const LayerWeights& L = w_.layers[li];
+    // FFN1: r = x + 0.5 * FFN(LN(x))
+    if (li == 0) {
+      prof_begin(st);
+      PKC_CK(layernorm_launch(b_.x, M, d, L.ln_ff1_g, L.ln_ff1_b, b_.hbuf, bf, nullptr, nullptr, false, st), "ln");
+      prof_end(st, "layernorm", 0.0, (double)M * d * (4 + hs));
+    }
+    PKC_ST(gemm(b_.hbuf, d, L.ff1_w1, d, bf, M, FF, d, EPI_STORE_H, ACT_SILU, 1.f, L.ff1_b1, b_.ffh, FF, st, "gemm_ffn", err));
+    PKC_ST(gemm(b_.ffh, FF, L.ff1_w2, FF, bf, M, d, FF, EPI_RESID_F32, ACT_NONE, 0.5f, L.ff1_b2, b_.x, d, st, "gemm_ffn", err));
+    // MHSA
+    prof_begin(st);
+    PKC_CK(layernorm_launch(b_.x, M, d, L.ln_att_g, L.ln_att_b, b_.hbuf, bf, nullptr, nullptr, false, st), "ln");
+    prof_end(st, "layernorm", 0.0, (double)M * d * (4 + hs));
+    PKC_ST(gemm(b_.hbuf, d, L.qkv_w, d, bf, M, 3 * d, d, EPI_STORE_H, ACT_NONE, 1.f, L.qkv_b, b_.qkv, 3 * d, st, "gemm_qkv", err));
+    PKC_ST(gemm(b_.pe, d, L.pos_w, d, bf, np, d, d, EPI_STORE_H, ACT_NONE, 1.f, nullptr, b_.ptab, d, st, "gemm_pos", err));
+    AttnArgs aa{b_.qkv, b_.ptab, np, p.centre, L.pos_u, L.pos_v, t_tiles, ntiles, t_v_off, t_v, b_.ctx, d, H};
+    prof_begin(st);
+    PKC_CK(attention_launch(aa, bf, st), "attention");
+    prof_end(st, "attention", attn_flops, (double)M * (3 * d + d) * hs + (double)np * d * hs);
+    PKC_ST(gemm(b_.ctx, d, L.out_w, d, bf, M, d, d, EPI_RESID_F32, ACT_NONE, 1.f, L.out_b, b_.x, d, st, "gemm_out", err));
+    // conv module
+    prof_begin(st);
+    PKC_CK(layernorm_launch(b_.x, M, d, L.ln_conv_g, L.ln_conv_b, b_.hbuf, bf, nullptr, nullptr, false, st), "ln");
+    prof_end(st, "layernorm", 0.0, (double)M * d * (4 + hs));
+    PKC_ST(gemm(b_.hbuf, d, L.pw1_w, d, bf, M, 2 * d, d, EPI_GLU_H, ACT_NONE, 1.f, L.pw1_b, b_.ctx, d, st, "gemm_pw1_glu", err));
+    prof_begin(st);
+    PKC_CK(dwconv_bn_silu_launch(b_.ctx, b_.hbuf, d, K, L.dw_w, L.dw_b, L.bn_scale, L.bn_shift, t_v_off,
+                                 t_v, p.B, p.max_v, bf, st), "dwconv");
+    prof_end(st, "dwconv", 2.0 * M * d * K, (double)M * d * hs * 2);
+    PKC_ST(gemm(b_.hbuf, d, L.pw2_w, d, bf, M, d, d, EPI_RESID_F32, ACT_NONE, 1.f, L.pw2_b, b_.x, d, st, "gemm_pw2", err));
+    // FFN2
+    prof_begin(st);
+    PKC_CK(layernorm_launch(b_.x, M, d, L.ln_ff2_g, L.ln_ff2_b, b_.hbuf, bf, nullptr, nullptr, false, st), "ln");
+    prof_end(st, "layernorm", 0.0, (double)M * d * (4 + hs));
+    PKC_ST(gemm(b_.hbuf, d, L.ff2_w1, d, bf, M, FF, d, EPI_STORE_H, ACT_SILU, 1.f, L.ff2_b1, b_.ffh, FF, st, "gemm_ffn", err));
+    PKC_ST(gemm(b_.ffh, FF, L.ff2_w2, FF, bf, M, d, FF, EPI_RESID_F32, ACT_NONE, 0.5f, L.ff2_b2, b_.x, d, st, "gemm_ffn", err));
+    // norm_out (+ next layer's norm_feed_forward1 in the same pass)
+    const bool last = li + 1 == c.n_layers;
+    const LayerWeights* N = last ? nullptr : &w_.layers[li + 1];
+    prof_begin(st);
+    PKC_CK(layernorm_launch(b_.x, M, d, L.ln_out_g, L.ln_out_b, last ? nullptr : b_.hbuf, bf,
+                            last ? nullptr : N->ln_ff1_g, last ? nullptr : N->ln_ff1_b, true, st), "ln");
+    prof_end(st, "layernorm", 0.0, (double)M * d * (8 + (last ? 0 : hs)));
+  }
+  return PKC_OK;
+}
+
+pkc_status DeviceRunner::finish(cudaStream_t st, std::string& err) {
+  int h_err = 0;
+  PKC_CK(cudaMemcpyAsync(&h_err, err_word_, sizeof(int), cudaMemcpyDeviceToHost, st), "error word read");
+  PKC_CK(cudaStreamSynchronize(st), "stream synchronize");
+  if (h_err != 0) {
+    cudaMemsetAsync(err_word_, 0, sizeof(int), st);
+    cudaStreamSynchronize(st);
+    err = "kernel reported error " + std::to_string(h_err) + " (bounded wait timed out)";
+    return PKC_ERR_KERNEL;
+  }
+  return PKC_OK;
+}
+
+pkc_status DeviceRunner::encode_pcm_host(const std::vector<const float*>& pcm,
+                                         const std::vector<int>& n, int layout, float* host_out,
+                                         std::string& err) {
+  cudaSetDevice(device_);
+  Plan p;
+  make_plan(cfg_, n, {}, p);
+  cudaStream_t st = stream_;
+  PKC_ST(prepare(p, st, err));
+  for (int b = 0; b < p.B; ++b)
+    if (n[b] > 0)
+      PKC_CK(cudaMemcpyAsync(b_.pcm + p.pcm_off[b], pcm[b], (size_t)n[b] * 4, cudaMemcpyHostToDevice, st), "pcm upload");
+  PKC_ST(run_frontend(p, st, err));
+  PKC_ST(run_encoder(p, st, err));
+  const int d = cfg_.d_model;
+  const float* src = b_.x;
+  if (layout == PKC_LAYOUT_CHANNELS_FIRST) {
+    prof_begin(st);
+    PKC_CK(to_channels_first_launch(b_.x, b_.out, d, t_v_off, t_v, p.B, p.max_v, st), "transpose");
+    prof_end(st, "to_channels_first", 0.0, (double)p.M * d * 8);
+    src = b_.out;
+  }
+  PKC_CK(cudaMemcpyAsync(host_out, src, (size_t)p.M * d * 4, cudaMemcpyDeviceToHost, st), "output download");
+  return finish(st, err);
+}
+
+pkc_status DeviceRunner::encode_pcm_device(const float* d_pcm, const std::vector<int>& n, float* d_out,
+                                           cudaStream_t st_in, bool sync, std::string& err) {
+  cudaSetDevice(device_);
+  Plan p;
+  make_plan(cfg_, n, {}, p);
+  cudaStream_t st = st_in ? st_in : stream_;
+  PKC_ST(prepare(p, st, err));
+  float* saved_pcm = b_.pcm;
+  float* saved_x = b_.x;
+  b_.pcm = const_cast<float*>(d_pcm);
+  b_.x = d_out;
+  pkc_status s = run_frontend(p, st, err);
+  if (s == PKC_OK) s = run_encoder(p, st, err);
+  b_.pcm = saved_pcm;
+  b_.x = saved_x;
+  if (s != PKC_OK) return s;
+  if (sync) return finish(st, err);
+  return PKC_OK;
+}
+
+pkc_status DeviceRunner::encode_mel_host(const float* mel, int B, int n_mels, int T_max,
+                                         const int* valid_T, int layout, float* host_out,
+                                         std::string& err) {
+  cudaSetDevice(device_);
+  std::vector<int> mt(valid_T, valid_T + B);
+  Plan p;
+  make_plan(cfg_, {}, mt, p);
+  cudaStream_t st = stream_;
+  PKC_ST(prepare(p, st, err));
+  // the planner sized melbatch for max valid_T; the caller's rows are T_max long
+  float* staging = nullptr;
+  const size_t bytes = (size_t)B * n_mels * T_max * 4;
+  float* dst = b_.melbatch;
+  if (T_max != p.max_Tm) {
+    PKC_CK(cudaMallocAsync(&staging, bytes, st), "mel staging allocation");
+    dst = staging;
+  }
+  PKC_CK(cudaMemcpyAsync(dst, mel, bytes, cudaMemcpyHostToDevice, st), "mel upload");
+  ItemTables t{p.B, t_pcm_off, t_S, t_mel_off, t_Tm, t_mval, t_v1_off, t_v1, t_v2_off, t_v2, t_v_off, t_v};
+  PKC_CK(batch_to_packed_launch(dst, n_mels, T_max, b_.logmel, t, p.max_Tm, st), "mel repack");
+  if (staging) cudaFreeAsync(staging, st);
+  PKC_ST(run_encoder(p, st, err));
+  const int d = cfg_.d_model;
+  const float* src = b_.x;
+  if (layout == PKC_LAYOUT_CHANNELS_FIRST) {
+    PKC_CK(to_channels_first_launch(b_.x, b_.out, d, t_v_off, t_v, p.B, p.max_v, st), "transpose");
+    src = b_.out;
+  }
+  PKC_CK(cudaMemcpyAsync(host_out, src, (size_t)p.M * d * 4, cudaMemcpyDeviceToHost, st), "output download");
+  return finish(st, err);
+}
+
+pkc_status DeviceRunner::mel_host(const std::vector<const float*>& pcm, const std::vector<int>& n,
+                                  int T_max, float* host_out, std::string& err) {
+  cudaSetDevice(device_);
+  Plan p;
+  make_plan(cfg_, n, {}, p);
+  cudaStream_t st = stream_;
+  PKC_ST(prepare(p, st, err));
+  for (int b = 0; b < p.B; ++b)
+    if (n[b] > 0)
+      PKC_CK(cudaMemcpyAsync(b_.pcm + p.pcm_off[b], pcm[b], (size_t)n[b] * 4, cudaMemcpyHostToDevice, st), "pcm upload");
+  PKC_ST(run_frontend(p, st, err));
+  ItemTables t{p.B, t_pcm_off, t_S, t_mel_off, t_Tm, t_mval, t_v1_off, t_v1, t_v2_off, t_v2, t_v_off, t_v};
+  PKC_CK(mel_to_batch_launch(b_.logmel, cfg_.n_mels, T_max, b_.melbatch, t, st), "mel batch");
+  PKC_CK(cudaMemcpyAsync(host_out, b_.melbatch, (size_t)p.B * cfg_.n_mels * T_max * 4,
+                         cudaMemcpyDeviceToHost, st), "mel download");
+  return finish(st, err);
+}
+
+}  // namespace pkc

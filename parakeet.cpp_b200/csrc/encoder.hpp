@@ -1,0 +1,110 @@
+// Batch planner and per-device encoder runtime.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "../../include/pkc.h"
+#include "model.hpp"
+
+namespace pkc {
+
+// Geometry of one batch on one device: every utterance keeps only its valid
+// frames at every stage (the reference pads to T_max and masks).
+struct Plan {
+  int B = 0;
+  std::vector<int> S, pcm_off;        // samples
+  std::vector<int> Tm, mel_off;       // mel frames per utterance
+  std::vector<int> mval;              // mel frames the encoder reads (Tm - 1)
+  std::vector<int> v1, v1_off, v2, v2_off, v, v_off;
+  long long total_samples = 0;
+  int total_frames = 0, M1 = 0, M2 = 0, M = 0;
+  int max_Tm = 0, max_v1 = 0, max_v2 = 0, max_v = 0;
+  int centre = 0;                     // positional table centre = max v
+  std::vector<int> attn_tiles;        // (item, q0) pairs
+};
+
+// n_samples given: PCM path. mel_T given instead (n_samples empty): mel path
+// where mel_T[b] = valid mel frames from the caller.
+void make_plan(const Config& c, const std::vector<int>& n_samples, const std::vector<int>& mel_T,
+               Plan& p);
+int mel_frames_for(const Config& c, int n_samples);
+int encoder_frames_for(int mel_frames);
+
+struct KernelStatAcc {
+  std::string name;
+  long long launches = 0;
+  double ms = 0, flops = 0, bytes = 0;
+};
+
+class DeviceRunner {
+ public:
+  DeviceRunner(const Config& c, int device) : cfg_(c), device_(device) {}
+  ~DeviceRunner();
+  std::string init(const GgufFile& g);
+  int device() const { return device_; }
+  cudaStream_t stream() const { return stream_; }
+
+  // Runs the front end (if pcm) and the encoder. Inputs either in host memory
+  // (copied in) or already on the device. Output: time-major [M, d] f32 in
+  // x_out (device, may be the workspace) - see encode_* helpers.
+  pkc_status encode_pcm_host(const std::vector<const float*>& pcm, const std::vector<int>& n,
+                             int layout, float* host_out, std::string& err);
+  pkc_status encode_pcm_device(const float* d_pcm, const std::vector<int>& n, float* d_out,
+                               cudaStream_t st, bool sync, std::string& err);
+  pkc_status encode_mel_host(const float* mel, int B, int n_mels, int T_max, const int* valid_T,
+                             int layout, float* host_out, std::string& err);
+  pkc_status mel_host(const std::vector<const float*>& pcm, const std::vector<int>& n, int T_max,
+                      float* host_out, std::string& err);
+
+  void profile_enable(bool on);
+  std::vector<KernelStatAcc> profile_read();
+
+ private:
+  pkc_status prepare(const Plan& p, cudaStream_t st, std::string& err);
+  pkc_status run_frontend(const Plan& p, cudaStream_t st, std::string& err);
+  pkc_status run_encoder(const Plan& p, cudaStream_t st, std::string& err);
+  pkc_status finish(cudaStream_t st, std::string& err);
+  bool ensure_ws(size_t bytes);
+  void prof_begin(cudaStream_t st);
+  void prof_end(cudaStream_t st, const char* name, double flops, double bytes);
+  pkc_status gemm(const void* A, int lda, const void* B, int ldb, bool bf16, int M, int N, int K,
+                  int epi, int act, float alpha, const float* bias, void* out, int ldo,
+                  cudaStream_t st, const char* name, std::string& err);
+
+  Config cfg_;
+  int device_;
+  cudaStream_t stream_ = nullptr;
+  DeviceWeights w_;
+  void* ws_ = nullptr;
+  size_t ws_bytes_ = 0;
+  int* err_word_ = nullptr;
+  int* h_tables_ = nullptr;  // pinned staging for the item tables
+  size_t h_tables_cap_ = 0;
+  // carved workspace pointers for the current plan
+  struct Ptrs {
+    float* pcm = nullptr; void* dft_a = nullptr; float* power = nullptr; float* logmel = nullptr;
+    float* melbatch = nullptr; void* s1 = nullptr; void* s2a = nullptr; void* s2b = nullptr;
+    void* s3a = nullptr; void* s3b = nullptr; float* x = nullptr; void* hbuf = nullptr;
+    void* ffh = nullptr; void* qkv = nullptr; void* pe = nullptr; void* ptab = nullptr;
+    void* ctx = nullptr; float* out = nullptr; int* tables = nullptr;
+  } b_;
+  // device table pointers for the current plan
+  int *t_pcm_off, *t_S, *t_mel_off, *t_Tm, *t_mval, *t_v1_off, *t_v1, *t_v2_off, *t_v2, *t_v_off,
+      *t_v, *t_tiles;
+  int power_ld_ = 0;
+  // plan cache: the device tables and workspace carve of the last batch
+  std::vector<int> last_key_;
+  // profiling
+  bool prof_on_ = false;
+  struct ProfRec { int cls; cudaEvent_t a, b; double flops, bytes; };
+  std::vector<ProfRec> prof_recs_;
+  std::vector<cudaEvent_t> ev_pool_;
+  size_t ev_next_ = 0;
+  std::vector<KernelStatAcc> prof_classes_;
+  cudaEvent_t prof_open_ = nullptr;
+};
+
+}  // namespace pkc

@@ -1,0 +1,115 @@
+// Host interface of the non-GEMM kernels (mel front end, subsampling convs,
+// LayerNorm, positional table, attention, conv module, output layout).
+//
+// Data layout in HBM (all packed per utterance, no T_max padding):
+//   pcm      f32 [sum S_b]                 utterances concatenated
+//   dft_a    f16 [sum Tm_b, 3*n_fft]       [Xhi | Xhi | Xlo] windowed frames
+//   power    f32 [sum Tm_b, power_ld]      |X|^2 for bins 0..n_fft/2
+//   logmel   f32 [sum Tm_b, F]             time-major log-mel, normalised in place
+//   s1       bf16 [sum v1_b, F1, C]        subsampling stage outputs, channel fastest
+//   x        f32 [M, d]                    residual stream, M = sum v_b
+//   h-type activations (f16 or bf16) [M, *] for every GEMM operand
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+
+namespace pkc {
+
+// Per-batch item tables (device pointers). Offsets are prefix sums (size B+1).
+struct ItemTables {
+  int B;
+  const int* pcm_off;  // samples
+  const int* n_samples;
+  const int* mel_off;  // mel frames (Tm_b each)
+  const int* mel_T;    // Tm_b
+  const int* mel_valid;  // frames the encoder reads (Tm_b - 1)
+  const int* v1_off; const int* v1;
+  const int* v2_off; const int* v2;
+  const int* v_off; const int* v;
+};
+
+struct MelArgs {
+  const float* pcm;
+  const float* window;  // [n_fft], centre-padded
+  int n_fft, hop;
+  float preemph;
+  int total_frames;
+  __half* dft_a;        // [total_frames, 3*n_fft]
+  float* power;         // [total_frames, power_ld]
+  int power_ld;
+};
+cudaError_t mel_frames_launch(const MelArgs& a, const ItemTables& t, cudaStream_t st);
+
+struct FbArgs {
+  const float* power; int power_ld;
+  const int* fb_start; const int* fb_len; const int* fb_off; const float* fb_w;
+  int n_mels;
+  float log_guard;
+  int total_frames;
+  float* logmel;        // [total_frames, n_mels]
+};
+cudaError_t mel_fb_log_launch(const FbArgs& a, cudaStream_t st);
+
+// Per-feature normalisation in place over each item's first mel_valid frames;
+// frames >= mel_valid are zeroed (src/mel_gpu.cpp:137-161).
+cudaError_t mel_norm_launch(float* logmel, int n_mels, const ItemTables& t, cudaStream_t st);
+
+// packed [sum Tm_b, F] -> [B][F][T_max] zero padded (the reference MelBatch)
+cudaError_t mel_to_batch_launch(const float* logmel, int n_mels, int T_max, float* out,
+                                const ItemTables& t, cudaStream_t st);
+// [B][F][T_max] -> packed [sum Tm_b, F] (Tm_b = mel_T[b])
+cudaError_t batch_to_packed_launch(const float* in, int n_mels, int T_max, float* logmel,
+                                   const ItemTables& t, int max_T, cudaStream_t st);
+
+// Subsampling stage 0: Conv2d(1 -> C, 3x3, stride 2, pad 1) + bias + ReLU.
+cudaError_t sub_conv0_launch(const float* logmel, int F, const float* w /*[C][9]*/, const float* b,
+                             int C, __nv_bfloat16* out, int F1, const ItemTables& t, int max_v1,
+                             cudaStream_t st);
+// Depthwise Conv2d(C, 3x3, stride 2, pad 1, groups C) + bias.
+// stage 1: in = (v1, F_in) -> out = (v2, F_out); stage 2: (v2 -> v)
+cudaError_t sub_dw_launch(const __nv_bfloat16* in, int F_in, const int* in_off, const int* in_valid,
+                          const float* w /*[9][C]*/, const float* b, int C, __nv_bfloat16* out,
+                          int F_out, const int* out_off, const int* out_valid, int B, int max_out,
+                          cudaStream_t st);
+
+// LayerNorm over d (ggml_norm, eps 1e-5) * gamma + beta.
+// out_h (may be null): normalised result in the compute type.
+// If g2 != nullptr: y = LN(x; g, b) is written back to x (f32) and
+// out_h = LN(y; g2, b2) (norm_out of one layer fused with the next layer's
+// norm_feed_forward1).
+cudaError_t layernorm_launch(float* x, int M, int d, const float* g, const float* b, void* out_h,
+                             bool bf16, const float* g2, const float* b2, bool write_x,
+                             cudaStream_t st);
+
+// Sinusoid table over relative positions centre-1 ... -(centre-1): [2*centre-1, d].
+cudaError_t pos_table_launch(void* out, int centre, int d, bool bf16, cudaStream_t st);
+
+struct AttnArgs {
+  const void* qkv;      // [M, 3d]
+  const void* ptab;     // [ptab_rows, d]
+  int ptab_rows, centre;
+  const float* bias_u;  // [H*dk]
+  const float* bias_v;
+  const int* tiles;     // [n_tiles][2] (item, q0)
+  int n_tiles;
+  const int* item_off;
+  const int* item_len;
+  void* ctx;            // [M, d]
+  int d, n_heads;
+};
+cudaError_t attention_launch(const AttnArgs& a, bool bf16, cudaStream_t st);
+int attn_query_tile();
+
+// Conv module middle: depthwise Conv1d(K, pad (K-1)/2) over each item's frames
+// (zeros outside) + bias -> BatchNorm (folded scale/shift) -> SiLU.
+cudaError_t dwconv_bn_silu_launch(const void* in, void* out, int d, int K, const float* w /*[K][d]*/,
+                                  const float* bias, const float* scale, const float* shift,
+                                  const int* item_off, const int* item_len, int B, int max_len,
+                                  bool bf16, cudaStream_t st);
+
+// packed time-major [M, d] -> per item channels-first [d, v_b], items concatenated
+cudaError_t to_channels_first_launch(const float* x, float* out, int d, const int* item_off,
+                                     const int* item_len, int B, int max_len, cudaStream_t st);
+
+}  // namespace pkc

@@ -1,0 +1,214 @@
+// Per-layer memory-bound kernels of the conformer block:
+//   k_layernorm     ggml_norm(x, 1e-5) * gamma + beta (src/conformer.cpp:300-307),
+//                   optionally two in a row (norm_out of layer i, then
+//                   norm_feed_forward1 of layer i+1) in one pass over the row
+//   k_pos_table     rel_pos_encoding sinusoids (src/pos_enc.cpp:10-34), f64 math
+//   k_dwconv        conv module depthwise Conv1d(K, pad (K-1)/2) + bias ->
+//                   BatchNorm (host-folded scale/shift, src/conformer.cpp:134-154)
+//                   -> SiLU, with zeros outside each utterance's frames (the
+//                   reference's pre-depthwise time mask, :63-79)
+//   k_to_chfirst    packed time-major -> per-utterance channels-first output
+#include "common.cuh"
+#include "kernels.h"
+
+namespace pkc {
+
+namespace {
+
+// One warp per row; each lane holds d/32 values (NV float4 chunks).
+template <int NV, typename H>
+__global__ void __launch_bounds__(256)
+    k_layernorm(float* __restrict__ x, int M, const float* __restrict__ g, const float* __restrict__ b,
+                H* __restrict__ out_h, const float* __restrict__ g2, const float* __restrict__ b2,
+                int write_x) {
+  constexpr int D = NV * 128;
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= M) return;
+  float* xr = x + (size_t)row * D;
+  float v[NV * 4];
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    const float4 q = *reinterpret_cast<const float4*>(xr + (i * 32 + lane) * 4);
+    v[4 * i] = q.x; v[4 * i + 1] = q.y; v[4 * i + 2] = q.z; v[4 * i + 3] = q.w;
+  }
+  auto norm = [&](const float* gg, const float* bb) {
+    float s = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV * 4; ++i) s += v[i];
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+    const float mean = s / (float)D;
+    float s2 = 0.f;
+#pragma unroll
+    for (int i = 0; i < NV * 4; ++i) {
+      v[i] -= mean;
+      s2 += v[i] * v[i];
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+    const float scale = 1.0f / sqrtf(s2 / (float)D + 1e-5f);
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      const int c = (i * 32 + lane) * 4;
+#pragma unroll
+      for (int e = 0; e < 4; ++e) v[4 * i + e] = v[4 * i + e] * scale * gg[c + e] + bb[c + e];
+    }
+  };
+  norm(g, b);
+  if (write_x) {
+#pragma unroll
+    for (int i = 0; i < NV; ++i)
+      *reinterpret_cast<float4*>(xr + (i * 32 + lane) * 4) =
+          make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+  }
+  if (g2) norm(g2, b2);
+  if (out_h) {
+    H* o = out_h + (size_t)row * D;
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      uint2 w;
+      w.x = pack2<H>(v[4 * i], v[4 * i + 1]);
+      w.y = pack2<H>(v[4 * i + 2], v[4 * i + 3]);
+      *reinterpret_cast<uint2*>(o + (i * 32 + lane) * 4) = w;
+    }
+  }
+}
+
+template <typename H>
+__global__ void k_pos_table(H* out, int centre, int d) {
+  const int half = d / 2;
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const int rows = 2 * centre - 1;
+  if (idx >= (long long)rows * half) return;
+  const int r = (int)(idx / half);
+  const int i = (int)(idx % half);
+  const double factor = -(log(10000.0) / (double)d);
+  const double div = exp((double)(2 * i) * factor);
+  const double arg = (double)(centre - 1 - r) * div;
+  out[(size_t)r * d + 2 * i] = to_h<H>((float)sin(arg));
+  out[(size_t)r * d + 2 * i + 1] = to_h<H>((float)cos(arg));
+}
+
+// One thread = one frame x 8 channels. grid (.., B)
+template <typename H>
+__global__ void __launch_bounds__(256)
+    k_dwconv_bn_silu(const H* __restrict__ in, H* __restrict__ out, int d, int K,
+                     const float* __restrict__ w, const float* __restrict__ bias,
+                     const float* __restrict__ scale, const float* __restrict__ shift,
+                     const int* __restrict__ item_off, const int* __restrict__ item_len) {
+  const int b = blockIdx.y;
+  const int cg = d / 8;
+  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  const int T = item_len[b];
+  if (idx >= (long long)T * cg) return;
+  const int c0 = (int)(idx % cg) * 8;
+  const int t = (int)(idx / cg);
+  const int pad = (K - 1) / 2;
+  const H* x = in + (size_t)item_off[b] * d;
+  float acc[8];
+#pragma unroll
+  for (int c = 0; c < 8; ++c) acc[c] = 0.f;
+  for (int k = 0; k < K; ++k) {
+    const int ti = t + k - pad;
+    if (ti < 0 || ti >= T) continue;
+    const uint4 raw = *reinterpret_cast<const uint4*>(x + (size_t)ti * d + c0);
+    const H* hv = reinterpret_cast<const H*>(&raw);
+    const float* wk = w + (size_t)k * d + c0;
+#pragma unroll
+    for (int c = 0; c < 8; ++c) acc[c] = fmaf(wk[c], from_h(hv[c]), acc[c]);
+  }
+  float r[8];
+#pragma unroll
+  for (int c = 0; c < 8; ++c) {
+    float y = acc[c] + (bias ? bias[c0 + c] : 0.f);
+    y = y * scale[c0 + c] + shift[c0 + c];
+    r[c] = siluf_(y);
+  }
+  uint4 o;
+  o.x = pack2<H>(r[0], r[1]);
+  o.y = pack2<H>(r[2], r[3]);
+  o.z = pack2<H>(r[4], r[5]);
+  o.w = pack2<H>(r[6], r[7]);
+  *reinterpret_cast<uint4*>(out + ((size_t)item_off[b] + t) * d + c0) = o;
+}
+
+// 32x32 tiled transpose per item: out[off*d + c*T + t] = x[(off + t)*d + c]
+__global__ void k_to_chfirst(const float* __restrict__ x, float* __restrict__ out, int d,
+                             const int* __restrict__ item_off, const int* __restrict__ item_len) {
+  __shared__ float tile[32][33];
+  const int b = blockIdx.z;
+  const int T = item_len[b];
+  const int t0 = blockIdx.x * 32, c0 = blockIdx.y * 32;
+  if (t0 >= T) return;
+  const size_t off = (size_t)item_off[b];
+  for (int r = threadIdx.y; r < 32; r += 8) {
+    const int t = t0 + r, c = c0 + threadIdx.x;
+    tile[r][threadIdx.x] = (t < T) ? x[(off + t) * d + c] : 0.f;
+  }
+  __syncthreads();
+  for (int r = threadIdx.y; r < 32; r += 8) {
+    const int c = c0 + r, t = t0 + threadIdx.x;
+    if (t < T) out[off * d + (size_t)c * T + t] = tile[threadIdx.x][r];
+  }
+}
+
+}  // namespace
+
+cudaError_t layernorm_launch(float* x, int M, int d, const float* g, const float* b, void* out_h,
+                             bool bf16, const float* g2, const float* b2, bool write_x,
+                             cudaStream_t st) {
+  if (M <= 0) return cudaSuccess;
+  const dim3 grid((M + 7) / 8);
+  const int wx = write_x ? 1 : 0;
+#define PKC_LN(NV)                                                                                   \
+  if (bf16)                                                                                          \
+    k_layernorm<NV, __nv_bfloat16><<<grid, 256, 0, st>>>(x, M, g, b, (__nv_bfloat16*)out_h, g2, b2, wx); \
+  else                                                                                               \
+    k_layernorm<NV, __half><<<grid, 256, 0, st>>>(x, M, g, b, (__half*)out_h, g2, b2, wx);
+  switch (d) {
+    case 256: PKC_LN(2) break;
+    case 512: PKC_LN(4) break;
+    case 768: PKC_LN(6) break;
+    case 1024: PKC_LN(8) break;
+    default: return cudaErrorInvalidValue;
+  }
+#undef PKC_LN
+  return cudaGetLastError();
+}
+
+cudaError_t pos_table_launch(void* out, int centre, int d, bool bf16, cudaStream_t st) {
+  const long long n = (long long)(2 * centre - 1) * (d / 2);
+  if (n <= 0) return cudaSuccess;
+  const unsigned grid = (unsigned)((n + 255) / 256);
+  if (bf16) k_pos_table<__nv_bfloat16><<<grid, 256, 0, st>>>((__nv_bfloat16*)out, centre, d);
+  else k_pos_table<__half><<<grid, 256, 0, st>>>((__half*)out, centre, d);
+  return cudaGetLastError();
+}
+
+cudaError_t dwconv_bn_silu_launch(const void* in, void* out, int d, int K, const float* w,
+                                  const float* bias, const float* scale, const float* shift,
+                                  const int* item_off, const int* item_len, int B, int max_len,
+                                  bool bf16, cudaStream_t st) {
+  if (B <= 0 || max_len <= 0) return cudaSuccess;
+  if (d % 8) return cudaErrorInvalidValue;
+  const long long n = (long long)max_len * (d / 8);
+  const dim3 grid((unsigned)((n + 255) / 256), B);
+  if (bf16)
+    k_dwconv_bn_silu<__nv_bfloat16><<<grid, 256, 0, st>>>((const __nv_bfloat16*)in, (__nv_bfloat16*)out, d,
+                                                          K, w, bias, scale, shift, item_off, item_len);
+  else
+    k_dwconv_bn_silu<__half><<<grid, 256, 0, st>>>((const __half*)in, (__half*)out, d, K, w, bias, scale,
+                                                   shift, item_off, item_len);
+  return cudaGetLastError();
+}
+
+cudaError_t to_channels_first_launch(const float* x, float* out, int d, const int* item_off,
+                                     const int* item_len, int B, int max_len, cudaStream_t st) {
+  if (B <= 0 || max_len <= 0) return cudaSuccess;
+  if (d % 32) return cudaErrorInvalidValue;
+  k_to_chfirst<<<dim3((max_len + 31) / 32, d / 32, B), dim3(32, 8), 0, st>>>(x, out, d, item_off, item_len);
+  return cudaGetLastError();
+}
+
+}  // namespace pkc

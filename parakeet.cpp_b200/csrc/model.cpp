@@ -1,0 +1,413 @@
+// GGUF -> device weights. Every tensor is converted once at load into the
+// layout its kernel reads (reference counterpart: ModelLoader::realize_weights,
+// src/model_loader.cpp:47-98, which uploads ggml tensors unchanged).
+//
+// Re-packing done here:
+//   * linear weights -> the layer compute type (f16, or bf16 for bf16 GGUFs);
+//     f32 / q8_0 / q4_k weights are dequantised on the host and rounded once
+//   * q, k, v projections concatenated into one [3d, d] weight (one GEMM)
+//   * pointwise_conv1 rows paired for the GLU epilogue: within each 256-row
+//     tile, rows [0,128) are value channels 128t.. and rows [128,256) the
+//     gate channels of the same 128 channels (F.glu: value = first half)
+//   * BatchNorm folded to f32 scale/shift exactly as src/conformer.cpp:134-154
+//   * depthwise weights transposed to tap-major [K][d] for coalesced reads
+//   * subsampling pointwise convs and output linear in bf16 (their activations
+//     are bf16: random-init magnitudes there fall below f16's normal range);
+//     the output linear's columns permuted from c*F' + f (the reference's
+//     channel-major flatten, src/subsampling.cpp:194-202) to f*C + c
+//   * the mel DFT basis split into f16 hi/lo parts, [Bhi | Blo | Bhi], with
+//     cos/-sin rows of each 128-bin group paired for the POWER epilogue
+#include "model.hpp"
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <functional>
+#include <thread>
+
+#include "half.hpp"
+
+namespace pkc {
+
+namespace {
+
+int conv_len(int n) { return (n + 2 - 3) / 2 + 1; }
+
+struct Staging {
+  std::vector<uint8_t> buf;
+  size_t add(const void* src, size_t n) {
+    const size_t off = (buf.size() + 255) / 256 * 256;
+    buf.resize(off + n);
+    if (src) std::memcpy(buf.data() + off, src, n);
+    return off;
+  }
+};
+
+// Offsets are carried in the pointer fields until the arena exists.
+template <typename T>
+T* as_off(size_t off) { return reinterpret_cast<T*>(off + 1); }  // +1: 0 means "absent"
+template <typename T>
+void reloc(T*& p, uint8_t* base) {
+  if (p) p = reinterpret_cast<T*>(base + (reinterpret_cast<uintptr_t>(p) - 1));
+}
+
+void parallel_rows(int64_t n, const std::function<void(int64_t, int64_t)>& fn) {
+  const int nt = (int)std::min<int64_t>(std::max(1u, std::thread::hardware_concurrency()),
+                                        std::max<int64_t>(1, n / 64));
+  if (nt <= 1) { fn(0, n); return; }
+  std::vector<std::thread> th;
+  for (int i = 0; i < nt; ++i) {
+    const int64_t a = n * i / nt, b = n * (i + 1) / nt;
+    th.emplace_back([&fn, a, b] { fn(a, b); });
+  }
+  for (auto& t : th) t.join();
+}
+
+// Read tensor `name` as a row-major f32 [N][K] matrix.
+bool read_f32(const GgufFile& g, const std::string& name, int64_t N, int64_t K,
+              std::vector<float>& out, std::string& err) {
+  const GgufTensor* t = g.tensor(name);
+  if (!t) { err = "missing tensor " + name; return false; }
+  if (t->nelem() != N * K) {
+    err = "tensor " + name + " has " + std::to_string(t->nelem()) + " elements, expected " +
+          std::to_string(N * K);
+    return false;
+  }
+  const bool plain = t->type == GT_F32 || t->type == GT_F16 || t->type == GT_BF16;
+  if (!plain && t->ne[0] != K) { err = "quantised tensor " + name + " is not K-major"; return false; }
+  const size_t rb = ggml_row_bytes(t->type, K);
+  if (!rb) { err = "tensor " + name + ": unsupported GGML type " + std::to_string(t->type); return false; }
+  out.resize((size_t)(N * K));
+  bool ok = true;
+  parallel_rows(N, [&](int64_t a, int64_t b) {
+    for (int64_t r = a; r < b; ++r)
+      if (!ggml_to_f32(t->type, t->data + rb * r, K, out.data() + r * K)) ok = false;
+  });
+  if (!ok) err = "tensor " + name + ": conversion failed";
+  return ok;
+}
+
+bool read_vec(const GgufFile& g, const std::string& name, int64_t n, std::vector<float>& out,
+              std::string& err) {
+  return read_f32(g, name, 1, n, out, err);
+}
+
+// Convert f32 rows to 16-bit (f16 or bf16) words.
+std::vector<uint16_t> to_h(const std::vector<float>& v, bool bf16) {
+  std::vector<uint16_t> h(v.size());
+  parallel_rows((int64_t)v.size(), [&](int64_t a, int64_t b) {
+    for (int64_t i = a; i < b; ++i) h[i] = bf16 ? f32_to_bf16(v[i]) : f32_to_f16(v[i]);
+  });
+  return h;
+}
+
+// Linear weight [N][K] in the target 16-bit type; bytes copied verbatim when
+// the GGUF already stores that type.
+bool read_h(const GgufFile& g, const std::string& name, int64_t N, int64_t K, bool bf16,
+            std::vector<uint16_t>& out, std::string& err) {
+  const GgufTensor* t = g.tensor(name);
+  if (t && t->nelem() == N * K && ((t->type == GT_F16 && !bf16) || (t->type == GT_BF16 && bf16))) {
+    out.resize((size_t)(N * K));
+    std::memcpy(out.data(), t->data, out.size() * 2);
+    return true;
+  }
+  std::vector<float> f;
+  if (!read_f32(g, name, N, K, f, err)) return false;
+  out = to_h(f, bf16);
+  return true;
+}
+
+}  // namespace
+
+std::string read_config(const GgufFile& g, Config& c) {
+  c.arch = g.str("parakeet.arch");
+  c.feat_in = (int)g.u32("parakeet.encoder.feat_in");
+  c.d_model = (int)g.u32("parakeet.encoder.d_model");
+  c.n_layers = (int)g.u32("parakeet.encoder.n_layers");
+  c.n_heads = (int)g.u32("parakeet.encoder.n_heads");
+  c.ff_dim = (int)g.u32("parakeet.encoder.ff_dim");
+  c.conv_kernel = (int)g.u32("parakeet.encoder.conv_kernel");
+  c.conv_norm_type = g.str("parakeet.encoder.conv_norm_type", "batch_norm");
+  c.subsampling_factor = (int)g.u32("parakeet.encoder.subsampling_factor");
+  c.sub_channels = (int)g.u32("parakeet.encoder.subsampling_conv_channels");
+  c.xscaling = g.boolean("parakeet.encoder.xscaling", true);
+  c.att_context_style = g.str("parakeet.encoder.att_context_style", "regular");
+  c.causal_downsampling = g.boolean("parakeet.encoder.causal_downsampling", false);
+  c.conv_causal = g.boolean("parakeet.encoder.conv_causal", false);
+  c.sample_rate = (int)g.u32("parakeet.preprocessor.sample_rate", 16000);
+  c.n_mels = (int)g.u32("parakeet.preprocessor.n_mels");
+  c.n_fft = (int)g.u32("parakeet.preprocessor.n_fft");
+  c.win_length = (int)g.u32("parakeet.preprocessor.win_length");
+  c.hop_length = (int)g.u32("parakeet.preprocessor.hop_length");
+  c.preemph = g.f32("parakeet.preprocessor.preemph", 0.f);
+  c.mag_power = g.f32("parakeet.preprocessor.mag_power", 2.f);
+  c.normalize = g.str("parakeet.preprocessor.normalize", "per_feature");
+  c.log_zero_guard = g.f32("parakeet.preprocessor.log_zero_guard", 0.f);
+  c.vocab_size = (int)g.u32("parakeet.vocab_size");
+  c.blank_id = (int)g.u32("parakeet.blank_id");
+  if (c.d_model <= 0 || c.vocab_size <= 0) return "GGUF lacks parakeet.encoder.d_model / vocab_size";
+  if (c.n_layers <= 0 || c.n_heads <= 0 || c.d_model % c.n_heads) return "bad encoder geometry";
+  const int dk = c.d_model / c.n_heads;
+  if (dk != 64 && dk != 128) return "head size " + std::to_string(dk) + " not supported (64 or 128)";
+  if (c.d_model % 256 || c.d_model > 1024) return "d_model must be a multiple of 256, at most 1024";
+  if (c.ff_dim % 256) return "ff_dim must be a multiple of 256";
+  if (c.sub_channels != 256) return "subsampling_conv_channels must be 256";
+  if (c.subsampling_factor != 8) return "only dw_striding 8x subsampling is implemented";
+  if (c.conv_norm_type != "batch_norm") return "conv_norm_type " + c.conv_norm_type + " (streaming) not supported";
+  if (c.att_context_style != "regular" || c.causal_downsampling || c.conv_causal)
+    return "cache-aware streaming models are out of scope";
+  if (c.conv_kernel % 2 == 0) return "depthwise kernel must be odd";
+  if (c.n_fft != 512) return "n_fft must be 512";
+  if (c.hop_length <= 0 || c.win_length <= 0 || c.win_length > c.n_fft) return "bad STFT geometry";
+  if (c.mag_power != 2.f) return "mag_power must be 2";
+  if (c.normalize != "per_feature") return "normalize must be per_feature";
+  if (c.n_mels <= 0 || c.n_mels > 512) return "bad n_mels";
+  c.F1 = conv_len(c.n_mels);
+  c.F2 = conv_len(c.F1);
+  c.F3 = conv_len(c.F2);
+  if ((c.F3 * c.sub_channels) % 64) return "subsampling flatten width must be a multiple of 64";
+  const GgufTensor* probe = g.tensor("encoder.layers.0.feed_forward1.linear1.weight");
+  if (!probe) return "missing encoder.layers.0.feed_forward1.linear1.weight";
+  c.weight_type = probe->type;
+  c.bf16 = probe->type == GT_BF16;
+  return "";
+}
+
+std::string upload_weights(const GgufFile& g, const Config& c, DeviceWeights& w) {
+  std::string err;
+  Staging st;
+  const int d = c.d_model, FF = c.ff_dim, C = c.sub_channels, K = c.conv_kernel, H = c.n_heads;
+  const bool bf = c.bf16;
+  std::vector<float> f, f2, f3, f4;
+  std::vector<uint16_t> h;
+
+  auto put_f = [&](const std::vector<float>& v) { return as_off<float>(st.add(v.data(), v.size() * 4)); };
+  auto put_h = [&](const std::vector<uint16_t>& v) { return as_off<void>(st.add(v.data(), v.size() * 2)); };
+  auto opt_vec = [&](const std::string& name, int64_t n) -> float* {
+    if (!g.tensor(name)) return nullptr;
+    std::vector<float> v;
+    if (!read_vec(g, name, n, v, err)) return nullptr;
+    return put_f(v);
+  };
+
+  // ---------------- mel front end
+  {
+    const int N = c.n_fft, nb = N / 2 + 1;
+    std::vector<float> win(N, 0.f);
+    if (g.tensor("preprocessor.featurizer.window")) {
+      const GgufTensor* t = g.tensor("preprocessor.featurizer.window");
+      if (!read_vec(g, "preprocessor.featurizer.window", t->nelem(), f, err)) return err;
+      const int wl = (int)f.size(), left = (N - wl) / 2;
+      for (int i = 0; i < wl; ++i)
+        if (left + i >= 0 && left + i < N) win[left + i] = f[i];
+    }
+    w.window = put_f(win);
+    // DFT basis rows (GEMM columns): tile t of 256 = cos rows of bins 128t..128t+127,
+    // then the -sin rows of the same bins; each row [hi | lo | hi] in f16.
+    std::vector<uint16_t> basis((size_t)N * 3 * N);
+    for (int n = 0; n < N; ++n) {
+      const int tile = n / 256, r = n % 256;
+      const int bin = tile * 128 + (r % 128);
+      const bool is_sin = r >= 128;
+      for (int k = 0; k < N; ++k) {
+        const double ang = 2.0 * M_PI * (double)bin * (double)k / (double)N;
+        const float v = is_sin ? (float)(-std::sin(ang)) : (float)std::cos(ang);
+        const uint16_t hi = f32_to_f16(v);
+        const uint16_t lo = f32_to_f16(v - f16_to_f32(hi));
+        basis[(size_t)n * 3 * N + k] = hi;
+        basis[(size_t)n * 3 * N + N + k] = lo;
+        basis[(size_t)n * 3 * N + 2 * N + k] = hi;
+      }
+    }
+    w.dft_basis = put_h(basis);
+    if (!read_f32(g, "preprocessor.featurizer.fb", c.n_mels, nb, f, err)) return err;
+    std::vector<int> fs(c.n_mels), fl(c.n_mels), fo(c.n_mels);
+    std::vector<float> fw;
+    for (int m = 0; m < c.n_mels; ++m) {
+      int a = 0, b = nb;
+      while (a < nb && f[(size_t)m * nb + a] == 0.f) ++a;
+      while (b > a && f[(size_t)m * nb + b - 1] == 0.f) --b;
+      fs[m] = a;
+      fl[m] = b - a;
+      fo[m] = (int)fw.size();
+      for (int k = a; k < b; ++k) fw.push_back(f[(size_t)m * nb + k]);
+    }
+    if (fw.empty()) fw.push_back(0.f);
+    w.fb_start = as_off<int>(st.add(fs.data(), fs.size() * 4));
+    w.fb_len = as_off<int>(st.add(fl.data(), fl.size() * 4));
+    w.fb_off = as_off<int>(st.add(fo.data(), fo.size() * 4));
+    w.fb_w = put_f(fw);
+  }
+
+  // ---------------- subsampling
+  {
+    const std::string p = "encoder.pre_encode.";
+    if (!read_f32(g, p + "conv.0.weight", C, 9, f, err)) return err;
+    w.c0_w = put_f(f);
+    if (!read_vec(g, p + "conv.0.bias", C, f, err)) return err;
+    w.c0_b = put_f(f);
+    for (int s = 0; s < 2; ++s) {
+      const int dwi = s == 0 ? 2 : 5, pwi = dwi + 1;
+      if (!read_f32(g, p + "conv." + std::to_string(dwi) + ".weight", C, 9, f, err)) return err;
+      std::vector<float> tap(9 * C);
+      for (int ch = 0; ch < C; ++ch)
+        for (int k = 0; k < 9; ++k) tap[(size_t)k * C + ch] = f[(size_t)ch * 9 + k];
+      float* dww = put_f(tap);
+      if (!read_vec(g, p + "conv." + std::to_string(dwi) + ".bias", C, f, err)) return err;
+      float* dwb = put_f(f);
+      if (!read_f32(g, p + "conv." + std::to_string(pwi) + ".weight", C, C, f, err)) return err;
+      void* pww = put_h(to_h(f, true));
+      if (!read_vec(g, p + "conv." + std::to_string(pwi) + ".bias", C, f, err)) return err;
+      float* pwb = put_f(f);
+      if (s == 0) { w.dw1_w = dww; w.dw1_b = dwb; w.pw1_w = pww; w.pw1_b = pwb; }
+      else { w.dw2_w = dww; w.dw2_b = dwb; w.pw2_w = pww; w.pw2_b = pwb; }
+    }
+    const int F3 = c.F3, KW = C * F3;
+    if (!read_f32(g, p + "out.weight", d, KW, f, err)) return err;
+    std::vector<float> perm((size_t)d * KW);
+    for (int o = 0; o < d; ++o)
+      for (int ch = 0; ch < C; ++ch)
+        for (int ff = 0; ff < F3; ++ff)
+          perm[(size_t)o * KW + ff * C + ch] = f[(size_t)o * KW + ch * F3 + ff];
+    w.out_w = put_h(to_h(perm, true));
+    if (!read_vec(g, p + "out.bias", d, f, err)) return err;
+    w.out_b = put_f(f);
+  }
+
+  // ---------------- conformer layers
+  w.layers.assign(c.n_layers, LayerWeights{});
+  for (int li = 0; li < c.n_layers; ++li) {
+    LayerWeights& L = w.layers[li];
+    const std::string p = "encoder.layers." + std::to_string(li) + ".";
+    auto vec = [&](const std::string& n, int64_t len) -> float* {
+      std::vector<float> v;
+      if (!read_vec(g, p + n, len, v, err)) return nullptr;
+      return put_f(v);
+    };
+    struct { const char* nm; float** gg; float** bb; } lns[] = {
+        {"norm_feed_forward1", &L.ln_ff1_g, &L.ln_ff1_b}, {"norm_self_att", &L.ln_att_g, &L.ln_att_b},
+        {"norm_conv", &L.ln_conv_g, &L.ln_conv_b}, {"norm_feed_forward2", &L.ln_ff2_g, &L.ln_ff2_b},
+        {"norm_out", &L.ln_out_g, &L.ln_out_b}};
+    for (auto& ln : lns) {
+      *ln.gg = vec(std::string(ln.nm) + ".weight", d);
+      *ln.bb = vec(std::string(ln.nm) + ".bias", d);
+      if (!*ln.gg || !*ln.bb) return err;
+    }
+    struct { const char* nm; void** w1; void** w2; float** b1; float** b2; } ffs[] = {
+        {"feed_forward1", &L.ff1_w1, &L.ff1_w2, &L.ff1_b1, &L.ff1_b2},
+        {"feed_forward2", &L.ff2_w1, &L.ff2_w2, &L.ff2_b1, &L.ff2_b2}};
+    for (auto& ff : ffs) {
+      const std::string n = p + ff.nm;
+      if (!read_h(g, n + ".linear1.weight", FF, d, bf, h, err)) return err;
+      *ff.w1 = put_h(h);
+      if (!read_h(g, n + ".linear2.weight", d, FF, bf, h, err)) return err;
+      *ff.w2 = put_h(h);
+      *ff.b1 = opt_vec(n + ".linear1.bias", FF);
+      *ff.b2 = opt_vec(n + ".linear2.bias", d);
+      if (!err.empty()) return err;
+    }
+    const std::string a = p + "self_attn.";
+    {
+      std::vector<uint16_t> qkv((size_t)3 * d * d);
+      const char* nms[3] = {"linear_q", "linear_k", "linear_v"};
+      std::vector<float> bq((size_t)3 * d, 0.f);
+      bool any_b = false;
+      for (int i = 0; i < 3; ++i) {
+        if (!read_h(g, a + nms[i] + ".weight", d, d, bf, h, err)) return err;
+        std::memcpy(qkv.data() + (size_t)i * d * d, h.data(), (size_t)d * d * 2);
+        if (g.tensor(a + nms[i] + ".bias")) {
+          if (!read_vec(g, a + nms[i] + ".bias", d, f, err)) return err;
+          std::memcpy(bq.data() + (size_t)i * d, f.data(), (size_t)d * 4);
+          any_b = true;
+        }
+      }
+      L.qkv_w = put_h(qkv);
+      L.qkv_b = any_b ? put_f(bq) : nullptr;
+    }
+    if (!read_h(g, a + "linear_pos.weight", d, d, bf, h, err)) return err;
+    L.pos_w = put_h(h);
+    if (!read_h(g, a + "linear_out.weight", d, d, bf, h, err)) return err;
+    L.out_w = put_h(h);
+    L.out_b = opt_vec(a + "linear_out.bias", d);
+    if (!err.empty()) return err;
+    L.pos_u = vec("self_attn.pos_bias_u", d);
+    L.pos_v = vec("self_attn.pos_bias_v", d);
+    if (!L.pos_u || !L.pos_v) return err;
+    (void)H;
+    // conv module
+    {
+      if (!read_f32(g, p + "conv.pointwise_conv1.weight", 2 * d, d, f, err)) return err;
+      std::vector<float> paired((size_t)2 * d * d);
+      std::vector<float> pb((size_t)2 * d, 0.f);
+      const bool has_b = g.tensor(p + "conv.pointwise_conv1.bias") != nullptr;
+      if (has_b && !read_vec(g, p + "conv.pointwise_conv1.bias", 2 * d, f2, err)) return err;
+      for (int n = 0; n < 2 * d; ++n) {
+        const int tile = n / 256, r = n % 256;
+        const int src = r < 128 ? tile * 128 + r : d + tile * 128 + (r - 128);
+        std::memcpy(paired.data() + (size_t)n * d, f.data() + (size_t)src * d, (size_t)d * 4);
+        if (has_b) pb[n] = f2[src];
+      }
+      L.pw1_w = put_h(to_h(paired, bf));
+      L.pw1_b = has_b ? put_f(pb) : nullptr;
+      if (!read_f32(g, p + "conv.depthwise_conv.weight", d, K, f, err)) return err;
+      std::vector<float> tap((size_t)K * d);
+      for (int ch = 0; ch < d; ++ch)
+        for (int k = 0; k < K; ++k) tap[(size_t)k * d + ch] = f[(size_t)ch * K + k];
+      L.dw_w = put_f(tap);
+      L.dw_b = opt_vec(p + "conv.depthwise_conv.bias", d);
+      if (!err.empty()) return err;
+      if (!read_vec(g, p + "conv.batch_norm.weight", d, f, err) ||
+          !read_vec(g, p + "conv.batch_norm.bias", d, f2, err) ||
+          !read_vec(g, p + "conv.batch_norm.running_mean", d, f3, err) ||
+          !read_vec(g, p + "conv.batch_norm.running_var", d, f4, err))
+        return err;
+      std::vector<float> sc(d), sh(d);
+      for (int ch = 0; ch < d; ++ch) {
+        sc[ch] = f[ch] / std::sqrt(f4[ch] + 1e-5f);
+        sh[ch] = f2[ch] - f3[ch] * sc[ch];
+      }
+      L.bn_scale = put_f(sc);
+      L.bn_shift = put_f(sh);
+      if (!read_f32(g, p + "conv.pointwise_conv2.weight", d, d, f, err)) return err;
+      L.pw2_w = put_h(to_h(f, bf));
+      L.pw2_b = opt_vec(p + "conv.pointwise_conv2.bias", d);
+      if (!err.empty()) return err;
+    }
+  }
+
+  // ---------------- upload
+  void* dev = nullptr;
+  if (cudaMalloc(&dev, st.buf.size()) != cudaSuccess)
+    return "cudaMalloc of " + std::to_string(st.buf.size()) + " weight bytes failed";
+  if (cudaMemcpy(dev, st.buf.data(), st.buf.size(), cudaMemcpyHostToDevice) != cudaSuccess) {
+    cudaFree(dev);
+    return "weight upload failed";
+  }
+  w.arena = dev;
+  w.arena_bytes = st.buf.size();
+  uint8_t* base = static_cast<uint8_t*>(dev);
+  reloc(w.window, base); reloc(w.dft_basis, base);
+  reloc(w.fb_start, base); reloc(w.fb_len, base); reloc(w.fb_off, base); reloc(w.fb_w, base);
+  reloc(w.c0_w, base); reloc(w.c0_b, base);
+  reloc(w.dw1_w, base); reloc(w.dw1_b, base); reloc(w.dw2_w, base); reloc(w.dw2_b, base);
+  reloc(w.pw1_w, base); reloc(w.pw2_w, base); reloc(w.pw1_b, base); reloc(w.pw2_b, base);
+  reloc(w.out_w, base); reloc(w.out_b, base);
+  for (LayerWeights& L : w.layers) {
+    float** fp[] = {&L.ln_ff1_g, &L.ln_ff1_b, &L.ln_att_g, &L.ln_att_b, &L.ln_conv_g, &L.ln_conv_b,
+                    &L.ln_ff2_g, &L.ln_ff2_b, &L.ln_out_g, &L.ln_out_b, &L.ff1_b1, &L.ff1_b2,
+                    &L.ff2_b1, &L.ff2_b2, &L.qkv_b, &L.out_b, &L.pos_u, &L.pos_v, &L.pw1_b,
+                    &L.dw_w, &L.dw_b, &L.bn_scale, &L.bn_shift, &L.pw2_b};
+    for (float** q : fp) reloc(*q, base);
+    void** vp[] = {&L.ff1_w1, &L.ff1_w2, &L.ff2_w1, &L.ff2_w2, &L.qkv_w, &L.pos_w, &L.out_w,
+                   &L.pw1_w, &L.pw2_w};
+    for (void** q : vp) reloc(*q, base);
+  }
+  return "";
+}
+
+void free_weights(DeviceWeights& w) {
+  if (w.arena) cudaFree(w.arena);
+  w.arena = nullptr;
+}
+
+}  // namespace pkc

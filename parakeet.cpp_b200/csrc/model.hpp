@@ -1,0 +1,84 @@
+// Model configuration (the reference's ParakeetConfig, src/model_loader.hpp:27-52)
+// and the per-device weight arena with every tensor re-packed once at load
+// into the layout its kernel reads.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "gguf.hpp"
+
+namespace pkc {
+
+struct Config {
+  std::string arch;
+  int feat_in = 0, d_model = 0, n_layers = 0, n_heads = 0, ff_dim = 0, conv_kernel = 0;
+  std::string conv_norm_type = "batch_norm";
+  int subsampling_factor = 0, sub_channels = 0;
+  bool xscaling = true;
+  std::string att_context_style = "regular";
+  bool causal_downsampling = false, conv_causal = false;
+  int sample_rate = 16000, n_mels = 0, n_fft = 0, win_length = 0, hop_length = 0;
+  float preemph = 0.f, mag_power = 2.f, log_zero_guard = 0.f;
+  std::string normalize = "per_feature";
+  int vocab_size = 0, blank_id = 0;
+  // derived
+  int F1 = 0, F2 = 0, F3 = 0;
+  uint32_t weight_type = 0;  // GGUF type of the encoder linear weights
+  bool bf16 = false;         // tensor-core operand type of the conformer layers
+};
+
+// Read and validate the configuration. Returns an empty string on success,
+// else the reason the model cannot run on this library.
+std::string read_config(const GgufFile& g, Config& c);
+
+struct LayerWeights {
+  float *ln_ff1_g, *ln_ff1_b, *ln_att_g, *ln_att_b, *ln_conv_g, *ln_conv_b;
+  float *ln_ff2_g, *ln_ff2_b, *ln_out_g, *ln_out_b;
+  void *ff1_w1, *ff1_w2, *ff2_w1, *ff2_w2;           // [FF, d], [d, FF]
+  float *ff1_b1, *ff1_b2, *ff2_b1, *ff2_b2;          // optional
+  void* qkv_w;                                       // [3d, d]
+  float* qkv_b;                                      // [3d] optional
+  void* pos_w;                                       // [d, d]
+  void* out_w;                                       // [d, d]
+  float* out_b;
+  float *pos_u, *pos_v;                              // [H * dk]
+  void* pw1_w;                                       // [2d, d] GLU-paired rows
+  float* pw1_b;                                      // [2d] paired, optional
+  float* dw_w;                                       // [K][d]
+  float* dw_b;                                       // optional
+  float *bn_scale, *bn_shift;                        // [d]
+  void* pw2_w;                                       // [d, d]
+  float* pw2_b;
+};
+
+struct DeviceWeights {
+  int device = 0;
+  void* arena = nullptr;
+  size_t arena_bytes = 0;
+  // mel front end
+  float* window = nullptr;        // [n_fft] centre-padded
+  void* dft_basis = nullptr;      // f16 [n_fft, 3*n_fft]
+  int* fb_start = nullptr;
+  int* fb_len = nullptr;
+  int* fb_off = nullptr;
+  float* fb_w = nullptr;
+  // subsampling
+  float *c0_w, *c0_b;             // [C][9], [C]
+  float *dw1_w, *dw1_b, *dw2_w, *dw2_b;  // [9][C], [C]
+  void *pw1_w, *pw2_w;            // bf16 [C, C]
+  float *pw1_b, *pw2_b;
+  void* out_w;                    // bf16 [d, F3*C] (columns f*C + c)
+  float* out_b;
+  std::vector<LayerWeights> layers;
+};
+
+// Upload every encoder weight of `g` to the current CUDA device.
+// Returns an empty string on success, else an error message.
+std::string upload_weights(const GgufFile& g, const Config& c, DeviceWeights& w);
+void free_weights(DeviceWeights& w);
+
+}  // namespace pkc

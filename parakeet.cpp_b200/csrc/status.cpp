@@ -15,7 +15,3 @@ const char* thread_error() { return g_thread_error.c_str(); }
 
 }  // namespace pkc
 
-// Until the model runtime is linked in, a model handle carries no message.
-namespace pkc {
-__attribute__((weak)) const char* model_error(const pkc_model*) { return ""; }
-}  // namespace pkc

@@ -1,0 +1,144 @@
+"""GPU parity: libpkc.so (through the C ABI) against the CPU oracle, which
+restates parakeet.cpp's batched encoder graph in float64.
+
+Tolerances (stated per the north star): encoder outputs within 2e-2 relative
+error (max |gpu - oracle| / max |oracle| over each utterance's output) for the
+f16 / bf16 compute path; the log-mel front end within 2e-3 absolute on
+normalised features (the reference's own GPU-vs-CPU mel test allows 0.05).
+Quantised weights (q8_0 / q4_k) are dequantised once to the compute type, so
+they carry one extra rounding of the weight and use the same bound.
+"""
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+
+SR = 16000
+
+
+def rel_err(got, ref):
+    return float(np.abs(got - ref).max() / max(np.abs(ref).max(), 1e-30))
+
+
+@pytest.fixture(scope="session")
+def models(tmp_path_factory):
+    import synth
+    d = str(tmp_path_factory.mktemp("models"))
+    small = dict(n_layers=3, d_model=256, n_heads=4, ff_dim=1024, vocab=64, pred_hidden=64,
+                 joint_hidden=64)
+    cfgs = {
+        "f16": synth.small_cfg("c2_0.6b_f16", n_mels=80, **small),
+        "f32_bias": synth.small_cfg("c1_110m", **small),
+        "bf16": synth.small_cfg("c5_0.6b_bf16_long", n_mels=128, **small),
+        "q8_0": synth.small_cfg("c3_0.6b_q8", n_mels=80, **small),
+        "q4_k": synth.small_cfg("c4_1.1b_q4k", n_mels=128, **small),
+        "dk128": synth.small_cfg("c2_0.6b_f16", n_layers=2, d_model=512, n_heads=4, ff_dim=1024,
+                                 vocab=64, pred_hidden=64, joint_hidden=64),
+    }
+    return {k: synth.ensure_gguf(c, d) for k, c in cfgs.items()}
+
+
+@pytest.fixture(scope="session")
+def opened(models):
+    import pkc
+    cache = {}
+
+    def get(kind):
+        if kind not in cache:
+            cache[kind] = pkc.Model(models[kind])
+        return cache[kind]
+    yield get
+    for m in cache.values():
+        m.close()
+
+
+@pytest.fixture(scope="session")
+def oracles(models):
+    import oracle
+    cache = {}
+
+    def get(kind):
+        if kind not in cache:
+            cache[kind] = oracle.Weights(models[kind])
+        return cache[kind]
+    return get
+
+
+def clips(lengths, seed=0):
+    import synth
+    return [synth.synth_audio(n, seed * 1000 + i) for i, n in enumerate(lengths)]
+
+
+def test_mel_front_end_matches_oracle(opened, oracles):
+    import oracle
+    m, w = opened("f16"), oracles("f16")
+    pcm = clips([SR * 2 + 77, SR, 5000, 161, 1600])
+    got, T = m.mel_batch(pcm)
+    ref, Tr = oracle.mel_batch(w, pcm, gpu_graph=True)
+    assert T == Tr
+    assert np.abs(got - ref).max() < 2e-3, np.abs(got - ref).max()
+    ref_fft, _ = oracle.mel_batch(w, pcm, gpu_graph=False)
+    assert np.abs(got - ref_fft).max() < 2e-3
+
+
+@pytest.mark.parametrize("kind", ["f16", "f32_bias", "bf16", "q8_0", "q4_k", "dk128"])
+def test_encoder_matches_oracle(opened, oracles, kind):
+    import oracle
+    m, w = opened(kind), oracles(kind)
+    pcm = clips([SR * 3 + 500, SR * 1 + 1234, SR * 2], seed=1)
+    outs = m.encode_pcm_batch(pcm)
+    ref = oracle.encode_pcm_batch(w, pcm)
+    assert [o.shape[1] for o in outs] == ref.valid
+    for got, r in zip(outs, ref.outs):
+        e = rel_err(got, r.T)
+        assert e < 2e-2, (kind, e)
+
+
+def test_batched_equals_standalone(opened):
+    m = opened("f16")
+    pcm = clips([SR * 4 + 17, SR * 2 + 999, 3000], seed=2)
+    together = m.encode_pcm_batch(pcm)
+    for i, p in enumerate(pcm):
+        alone = m.encode_pcm_batch([p])[0]
+        np.testing.assert_array_equal(together[i], alone)
+
+
+def test_mel_entry_matches_pcm_entry(opened):
+    import pkc
+    m = opened("f16")
+    pcm = clips([SR * 2 + 5, SR + 160 * 7], seed=3)
+    mel, T = m.mel_batch(pcm)
+    a = m.encode_batch(mel, T)
+    b = m.encode_pcm_batch(pcm)
+    for x, y in zip(a, b):
+        np.testing.assert_array_equal(x, y)
+    tm = m.encode_pcm_batch(pcm, layout=pkc.LAYOUT_TIME_MAJOR)
+    for x, y in zip(tm, b):
+        np.testing.assert_array_equal(x.T, y)
+
+
+def test_tiny_and_boundary_clips(opened, oracles):
+    """Edge lengths: one hop, just under one hop (0 valid mel frames: the
+    reference's integer recurrence still yields one output frame), and lengths
+    that make every stage's frame count odd/even."""
+    import oracle
+    m, w = opened("f16"), oracles("f16")
+    lengths = [100, 160, 161, 1280, 1281, 1440, 2560 + 160]
+    pcm = clips(lengths, seed=4)
+    outs = m.encode_pcm_batch(pcm)
+    ref = oracle.encode_pcm_batch(w, pcm)
+    for got, r in zip(outs, ref.outs):
+        assert got.shape == r.T.shape
+        assert rel_err(got, r.T) < 2e-2
+
+
+def test_bad_arguments(opened):
+    import pkc
+    m = opened("f16")
+    with pytest.raises(pkc.PkcError) as e:
+        m.encode_pcm_batch([np.zeros(0, dtype=np.float32)])
+    assert e.value.status == 1
+    mel = np.zeros((1, 81, 50), dtype=np.float32)
+    with pytest.raises(pkc.PkcError) as e:
+        m.encode_batch(mel, [50])
+    assert e.value.status == 1
