@@ -1,0 +1,402 @@
+"""Batch RTFx of the FastConformer encoder hot path on B200.
+
+One step = one batch of synthetic utterances through the hot path (log-mel
+front end, dw-striding subsampling, all conformer layers) of the workload's
+model. `value` is audio-seconds per second with the PCM already in HBM (the
+device-resident C-ABI entry); `e2e` is the same metric through the public
+host-buffer C-ABI call (pinned PCM in, encoder output back to host memory,
+copies inside the timed region).
+
+Multi-GPU: one process per GPU (torchrun); every rank encodes its own batch of
+the workload (utterances sharded by whole clips, no collective on the data
+path) -> "scaling": "weak". Timing is CUDA events on the launching stream,
+max over ranks.
+
+`--impl reference` times the reference's CPU path on the host cores instead:
+parakeet.cpp's ggml encoder cannot be built here (its ggml dependency is absent
+from the checkout), so the encoder runs as the CPU restatement in oracle/
+(numpy, float64, all BLAS threads) and the mel front end as parakeet.cpp's own
+MelFrontend compiled from its sources (oracle/_ref) when present.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+for p in (os.path.join(REPO, "parakeet.cpp_b200", "python"), os.path.join(REPO, "oracle")):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+METRIC = "batch RTFx (audio-s/s) at 1/2/4/8 B200; per-kernel % of HBM/tensor peak"
+UNIT = "audio-s/s"
+DEFAULT_CONFIG = "c2_0.6b_f16"
+SR = 16000
+L2_FLUSH_BYTES = 256 << 20
+
+
+def env_int(k, d):
+    try:
+        return int(os.environ.get(k, d))
+    except ValueError:
+        return d
+
+
+def load_peaks():
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            pk = json.load(f)
+        return pk, "measured"
+    except Exception:
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def profile_traffic(config):
+    """Per-launch DRAM traffic of the dominant kernel from the committed ncu
+    summary (a line `traffic_bytes_per_launch[<config>]: <int>`), else None."""
+    path = os.path.join(REPO, "profiles", "gemm_tcgen05_ncu.md")
+    try:
+        with open(path) as f:
+            for line in f:
+                key = f"traffic_bytes_per_launch[{config}]:"
+                if line.strip().startswith(key):
+                    return float(line.split(":", 1)[1].strip())
+    except OSError:
+        pass
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = f"/tmp/pkc_clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        try:
+            self.f = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.gpu), "-lms", "200"], stdout=self.f,
+                                         stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *a):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.f.close()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        try:
+            with open(self.path) as f:
+                for line in f:
+                    parts = [x.strip() for x in line.split(",")]
+                    if len(parts) < 9:
+                        continue
+                    try:
+                        sm.append(float(parts[1]))
+                        mx = float(parts[2])
+                    except ValueError:
+                        continue
+                    for n, v in zip(names, parts[5:9]):
+                        if v.lower() == "active":
+                            reasons.add(n)
+        except OSError:
+            pass
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def workload(config, rank, batch=None):
+    import synth
+    b, lo, hi = synth.BATCHES[config]
+    b = batch or b
+    pcm = synth.synth_batch(config, seed=1000 + rank, batch=b)
+    return pcm, {"batch": b, "len_s": [lo, hi]}
+
+
+# ----------------------------------------------------------------------- ours
+
+def run_ours(args, rank, world, local_rank):
+    import numpy as np
+    import torch
+    import torch.distributed as dist
+    import pkc
+    import synth
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    cfg = synth.CONFIGS[args.config]
+    if rank == 0 or world == 1:
+        path = synth.ensure_gguf(cfg)
+    if world > 1:
+        dist.barrier()
+    path = synth.ensure_gguf(cfg)
+
+    pcm, winfo = workload(args.config, rank, args.batch)
+    n = [len(p) for p in pcm]
+    audio_s = sum(n) / SR
+
+    model = pkc.Model(path, devices=(local_rank,))
+    d = model.info.d_model
+    out_floats = lib_out_floats = int(sum(model.encoder_frames(model.mel_frames(x)) for x in n) * d)
+    flat = np.concatenate(pcm).astype(np.float32)
+    d_pcm = torch.from_numpy(flat).to(dev)
+    d_out = torch.empty(out_floats, dtype=torch.float32, device=dev)
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        model.encode_pcm_device(d_pcm.data_ptr(), n, d_out.data_ptr(), stream=stream.cuda_stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    model.encode_pcm_device(d_pcm.data_ptr(), n, d_out.data_ptr(), stream=stream.cuda_stream, sync=True)
+
+    # ---- timed region: K steps, L2 flushed between steps (outside the step events)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local_rank) as clk:
+        for i in range(args.steps):
+            flush.zero_()
+            starts[i].record(stream)
+            step()
+            ends[i].record(stream)
+        torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
+    # the device path reports kernel errors through its error word on sync
+    model.encode_pcm_device(d_pcm.data_ptr(), n, d_out.data_ptr(), stream=stream.cuda_stream, sync=True)
+
+    # ---- per-kernel classes (a separate profiled pass of the same steps)
+    model.profile_enable(True)
+    for _ in range(max(1, min(args.steps, 5))):
+        step()
+    torch.cuda.synchronize(dev)
+    stats = model.profile_read()
+    model.profile_enable(False)
+    prof_steps = max(1, min(args.steps, 5))
+
+    # ---- e2e: public host-buffer API, pinned PCM in, output to host
+    pinned = [torch.from_numpy(p).pin_memory() for p in pcm]
+    host_pcm = [t.numpy() for t in pinned]
+    host_out_bytes = out_floats * 4
+    for _ in range(max(1, args.warmup)):
+        model.encode_pcm_batch(host_pcm, layout=pkc.LAYOUT_TIME_MAJOR)
+    lib_stream = torch.cuda.ExternalStream(model.stream(), device=dev)
+    e_start = torch.cuda.Event(enable_timing=True)
+    e_end = torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    e_start.record(lib_stream)
+    for _ in range(args.steps):
+        model.encode_pcm_batch(host_pcm, layout=pkc.LAYOUT_TIME_MAJOR)
+    e_end.record(lib_stream)
+    torch.cuda.synchronize(dev)
+    e2e_wall = time.perf_counter() - t0
+    e2e_ms = e_start.elapsed_time(e_end)
+
+    vals = torch.tensor([ms, e2e_ms, audio_s, e2e_wall * 1e3], dtype=torch.float64, device=dev)
+    if world > 1:
+        mx = vals.clone()
+        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+        tot = vals.clone()
+        dist.all_reduce(tot, op=dist.ReduceOp.SUM)
+        ms_max, e2e_max, wall_max = mx[0].item(), mx[1].item(), mx[3].item()
+        audio_total = tot[2].item()
+    else:
+        ms_max, e2e_max, wall_max, audio_total = ms, e2e_ms, e2e_wall * 1e3, audio_s
+    model.close()
+    if rank != 0:
+        return None
+
+    value = audio_total * args.steps / (ms_max / 1e3)
+    peaks, peak_src = load_peaks()
+    gemm = [s for s in stats if s["name"].startswith("gemm_")]
+    g_ms = sum(s["total_ms"] for s in gemm)
+    g_fl = sum(s["flops"] for s in gemm)
+    g_n = sum(s["launches"] for s in gemm)
+    achieved = g_fl / (g_ms / 1e3) / 1e12 if g_ms > 0 else 0.0
+    peak = peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))
+    traffic = profile_traffic(args.config)
+    launches_per_step = sum(s["launches"] for s in stats) / prof_steps
+    kernels = []
+    tot_ms = sum(s["total_ms"] for s in stats) or 1.0
+    for s in sorted(stats, key=lambda s: -s["total_ms"]):
+        k = {"name": s["name"], "launches_per_step": s["launches"] / prof_steps,
+             "ms_per_step": round(s["total_ms"] / prof_steps, 4), "share": round(s["total_ms"] / tot_ms, 4)}
+        if s["flops"] > 0 and s["name"].startswith(("gemm", "attention")):
+            k["tflops"] = round(s["flops"] / (s["total_ms"] / 1e3) / 1e12, 1)
+            k["frac_tensor_peak"] = round(k["tflops"] / peak, 3)
+        elif s["bytes"] > 0:
+            k["gbs"] = round(s["bytes"] / (s["total_ms"] / 1e3) / 1e9, 1)
+            k["frac_hbm_peak"] = round(k["gbs"] / peaks["hbm_gbs"], 3)
+        kernels.append(k)
+    line = {
+        "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16" if not "bf16" in args.config else "bf16",
+        "data": "synthetic (seeded sines + noise; random-init weights, BASELINE.json init)",
+        "config": {"workload": f"{args.config}: {synth.CONFIGS[args.config].n_layers}-layer d{d} FastConformer encoder "
+                               f"({synth.CONFIGS[args.config].dtype} weights), PCM -> encoder output, "
+                               f"batch {winfo['batch']} clips of U({winfo['len_s'][0]},{winfo['len_s'][1]}) s per GPU",
+                   "audio_s_per_step_per_gpu": round(audio_s, 2), "parallelism": f"utterance-sharded dp{world}",
+                   "l2": "256 MiB written between timed steps (L2 flush); per-step working set > 1 GB"},
+        "e2e": {"value": round(audio_total * args.steps / (e2e_max / 1e3), 1), "unit": UNIT,
+                "h2d_bytes_per_step": int(sum(n) * 4), "d2h_bytes_per_step": int(host_out_bytes),
+                "api": "pkc_encode_pcm_batch (host buffers, pinned PCM)",
+                "wall_value": round(audio_total * args.steps / (wall_max / 1e3), 1)},
+        "gpu_launches": int(round(launches_per_step * args.steps)),
+        "roofline": {"bound": "tensor", "kernel": "k_gemm_tc (tcgen05 GEMM, all encoder projections)",
+                     "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+                     "frac": round(achieved / peak, 3) if peak else None, "traffic": traffic,
+                     "launches_per_step": g_n / prof_steps,
+                     "peak_source": f"{peak_src} bf16_tflops_sustained (dense f16/bf16 tensor peak)"},
+        "kernels": kernels,
+        "clocks": clk.summary(),
+    }
+    if not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline(args, path, pcm)
+    return line
+
+
+# ----------------------------------------------------------------------- CPU
+
+def cpu_sample(pcm_all, budget_s=2.0):
+    """A bounded slice of the workload: the shortest clip of the batch, cut to
+    at most budget_s seconds."""
+    c = min(pcm_all, key=len)
+    return [c[: int(budget_s * SR)]]
+
+
+def cpu_encode(w, clip):
+    import numpy as np
+    import oracle
+    import ref
+    if ref.available():
+        feats = ref.mel(clip, n_mels=w.n_mels, n_fft=w.n_fft, hop=w.hop, win_length=len(w.t["preprocessor.featurizer.window"]),
+                        preemph=w.preemph, mag_power=w.mag_power, log_guard=w.log_guard,
+                        per_feature=w.per_feature, window=w.t["preprocessor.featurizer.window"].astype(np.float32),
+                        fb=w.fb())
+    else:
+        feats = oracle.mel_frontend(w, clip)
+    return oracle.encoder_forward_batch(w, feats[None], [feats.shape[1]])
+
+
+def cpu_baseline(args, path, pcm):
+    import oracle
+    w = oracle.Weights(path)
+    sample = cpu_sample(pcm)
+    audio = sum(len(c) for c in sample) / SR
+    cpu_encode(w, sample[0])  # warm
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        cpu_encode(w, sample[0])
+        reps += 1
+        if time.perf_counter() - t0 > 10.0 or reps >= 3:
+            break
+    dt = (time.perf_counter() - t0) / reps
+    return {"value": round(audio / dt, 3), "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+            "sample": f"1 clip of {audio:.2f} s (shortest of the batch) through the full model; "
+                      f"encoder = numpy float64 restatement, mel = parakeet.cpp MelFrontend (oracle/_ref)"}
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return None
+    import oracle
+    import synth
+    cfg = synth.CONFIGS[args.config]
+    path = synth.ensure_gguf(cfg)
+    pcm, winfo = workload(args.config, 0, args.batch)
+    w = oracle.Weights(path)
+    sample = cpu_sample(pcm)
+    audio = sum(len(c) for c in sample) / SR
+    for _ in range(args.warmup):
+        cpu_encode(w, sample[0])
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        cpu_encode(w, sample[0])
+    dt = time.perf_counter() - t0
+    v = audio * args.steps / dt
+    cores = os.cpu_count()
+    return {"metric": METRIC, "value": round(v, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 1), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f64", "impl": "reference",
+            "data": "synthetic", "config": {"workload": f"{args.config} (bounded CPU sample)",
+                                             "sample": f"1 clip of {audio:.2f} s per step"},
+            "cpu_baseline": {"value": round(v, 3), "unit": UNIT, "cores": cores, "kind": "port",
+                             "sample": f"1 clip of {audio:.2f} s per step; parakeet.cpp's ggml encoder is not "
+                                       "buildable here (ggml absent), so the encoder is the numpy float64 "
+                                       "restatement and the mel front end parakeet.cpp's own MelFrontend"},
+            "e2e": {"value": round(v, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default=DEFAULT_CONFIG)
+    ap.add_argument("--batch", type=int, default=None)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
+    world = env_int("WORLD_SIZE", 1)
+    rank = env_int("RANK", 0)
+    local_rank = env_int("LOCAL_RANK", 0)
+    if args.impl == "reference":
+        line = run_reference(args, rank, world)
+        if line:
+            print(json.dumps(line), flush=True)
+        return
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local_rank)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=torch.device("cuda", local_rank))
+    try:
+        line = run_ours(args, rank, world, local_rank)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+    if line:
+        print(json.dumps(line), flush=True)
+
+
+if __name__ == "__main__":
+    main()

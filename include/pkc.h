@@ -127,6 +127,11 @@ pkc_status pkc_encode_pcm_device(pkc_model* m, int device_slot, const float* d_p
                                  const int* n_samples, int B, float* d_out, void* stream,
                                  int sync);
 
+/* The CUDA stream (a cudaStream_t, as void*) that the host-buffer entry points
+   of device slot `device_slot` run on; lets a caller bracket a call with its
+   own events. NULL for a bad slot. */
+void* pkc_model_stream(const pkc_model* m, int device_slot);
+
 /* Per-kernel-class timing (CUDA events around every launch on the model's
    stream). enable != 0 turns it on and clears the accumulators. */
 pkc_status pkc_profile_enable(pkc_model* m, int enable);

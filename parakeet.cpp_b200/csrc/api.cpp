@@ -288,6 +288,11 @@ pkc_status pkc_encode_pcm_device(pkc_model* m, int device_slot, const float* d_p
   }
 }
 
+void* pkc_model_stream(const pkc_model* m, int device_slot) {
+  if (!m || device_slot < 0 || device_slot >= (int)m->runners.size()) return nullptr;
+  return reinterpret_cast<void*>(m->runners[device_slot]->stream());
+}
+
 pkc_status pkc_profile_enable(pkc_model* m, int enable) {
   if (!m) return pkc::set_thread_error(PKC_ERR_ARG, "pkc_profile_enable: model is NULL");
   std::lock_guard<std::mutex> lk(m->mu);

@@ -95,6 +95,7 @@ def _declare(L):
         ("pkc_encode_pcm_device", c_int, c_void_p, c_int, c_void_p, POINTER(c_int), c_int,
          c_void_p, c_void_p, c_int),
         ("pkc_profile_enable", c_int, c_void_p, c_int),
+        ("pkc_model_stream", c_void_p, c_void_p, c_int),
         ("pkc_profile_read", c_int, c_void_p, POINTER(KernelStat), c_int),
         ("pkc_shard_plan", c_int, POINTER(c_int), c_int, c_int, c_int, POINTER(c_int)),
     ]
@@ -206,6 +207,10 @@ class Model:
                                            len(n_samples), c_void_p(d_out),
                                            c_void_p(stream) if stream else None, 1 if sync else 0),
                self._h)
+
+    def stream(self, slot=0):
+        """cudaStream_t (as int) that the host-buffer entry points use."""
+        return lib().pkc_model_stream(self._h, slot) or 0
 
     def profile_enable(self, on=True):
         _check(lib().pkc_profile_enable(self._h, 1 if on else 0), self._h)
