@@ -165,7 +165,10 @@ def run_ours(args, rank, world, local_rank):
     d_pcm = torch.from_numpy(flat).to(dev)
     d_out = torch.empty(out_floats, dtype=torch.float32, device=dev)
     flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
-    stream = torch.cuda.current_stream(dev)
+    # one stream for everything timed: the library launches on it, the events
+    # are recorded on it, and the L2 flush runs on it between steps
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
 
     def step():
         model.encode_pcm_device(d_pcm.data_ptr(), n, d_out.data_ptr(), stream=stream.cuda_stream)
@@ -365,7 +368,7 @@ def run_reference(args, rank, world):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--config", default=DEFAULT_CONFIG)

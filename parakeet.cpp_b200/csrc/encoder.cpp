@@ -12,6 +12,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 
 #include "kernels/gemm.h"
@@ -79,6 +80,7 @@ size_t al(size_t x) { return (x + 255) / 256 * 256; }
 DeviceRunner::~DeviceRunner() {
   cudaSetDevice(device_);
   if (stream_) cudaStreamSynchronize(stream_);
+  drop_graphs();
   for (cudaEvent_t e : ev_pool_) cudaEventDestroy(e);
   if (ws_) cudaFree(ws_);
   if (err_word_) cudaFree(err_word_);
@@ -96,6 +98,8 @@ std::string DeviceRunner::init(const GgufFile& g) {
   if (cudaMalloc(&err_word_, sizeof(int)) != cudaSuccess) return "cudaMalloc failed";
   cudaMemset(err_word_, 0, sizeof(int));
   power_ld_ = cfg_.n_fft / 2 + 8;
+  const char* ng = getenv("PKC_NO_GRAPH");
+  use_graphs_ = !(ng && ng[0] == '1');
   return upload_weights(g, cfg_, w_);
 }
 
@@ -103,6 +107,7 @@ bool DeviceRunner::ensure_ws(size_t bytes) {
   if (bytes <= ws_bytes_) return true;
   last_key_.clear();
   cudaStreamSynchronize(stream_);
+  drop_graphs();
   if (ws_) cudaFree(ws_);
   ws_ = nullptr;
   ws_bytes_ = 0;
@@ -120,6 +125,7 @@ void DeviceRunner::profile_enable(bool on) {
   cudaSetDevice(device_);
   cudaStreamSynchronize(stream_);
   prof_on_ = on;
+  drop_graphs();
   prof_recs_.clear();
   prof_classes_.clear();
   ev_next_ = 0;
@@ -127,6 +133,15 @@ void DeviceRunner::profile_enable(bool on) {
 
 void DeviceRunner::prof_begin(cudaStream_t st) {
   if (!prof_on_) return;
+  if (capture_events_) {
+    cudaEvent_t e = nullptr;
+    if (cudaEventCreate(&e) != cudaSuccess) { prof_error_ = true; return; }
+    capture_events_->push_back(e);
+    prof_open_ = e;
+    // external: becomes an event-record node that replays re-record
+    if (cudaEventRecordWithFlags(prof_open_, st, cudaEventRecordExternal) != cudaSuccess) prof_error_ = true;
+    return;
+  }
   if (ev_next_ + 2 > ev_pool_.size()) {
     for (int i = 0; i < 256; ++i) {
       cudaEvent_t e;
@@ -140,8 +155,16 @@ void DeviceRunner::prof_begin(cudaStream_t st) {
 
 void DeviceRunner::prof_end(cudaStream_t st, const char* name, double flops, double bytes) {
   if (!prof_on_) return;
-  cudaEvent_t e = ev_pool_[ev_next_++];
-  cudaEventRecord(e, st);
+  cudaEvent_t e = nullptr;
+  if (capture_events_) {
+    if (cudaEventCreate(&e) != cudaSuccess) { prof_error_ = true; return; }
+    capture_events_->push_back(e);
+  } else {
+    e = ev_pool_[ev_next_++];
+  }
+  const cudaError_t re = capture_events_ ? cudaEventRecordWithFlags(e, st, cudaEventRecordExternal)
+                                         : cudaEventRecord(e, st);
+  if (re != cudaSuccess) prof_error_ = true;
   int cls = -1;
   for (size_t i = 0; i < prof_classes_.size(); ++i)
     if (prof_classes_[i].name == name) cls = (int)i;
@@ -166,7 +189,10 @@ std::vector<KernelStatAcc> DeviceRunner::profile_read() {
   }
   prof_recs_.clear();
   ev_next_ = 0;
-  return prof_classes_;
+  cudaGetLastError();
+  std::vector<KernelStatAcc> out = prof_classes_;
+  if (prof_error_) out.push_back(KernelStatAcc{"profile_event_error"});
+  return out;
 }
 
 // ------------------------------------------------------------------ launches
@@ -319,7 +345,7 @@ pkc_status DeviceRunner::run_encoder(const Plan& p, cudaStream_t st, std::string
   // ---- subsampling (src/subsampling.cpp:48-240)
   prof_begin(st);
   PKC_CK(sub_conv0_launch(b_.logmel, c.n_mels, w_.c0_w, w_.c0_b, C,
-                          reinterpret_cast<__nv_bfloat16*>(b_.s1), c.F1, t, p.max_v1, st), "conv0");
+                          reinterpret_cast<__nv_bfloat16*>(b_.s1), c.F1, t, p.M1, st), "conv0");
   prof_end(st, "sub_conv0", 2.0 * p.M1 * c.F1 * C * 9, (double)p.total_frames * c.n_mels * 4 + (double)p.M1 * c.F1 * C * 2);
   prof_begin(st);
   PKC_CK(sub_dw_launch(reinterpret_cast<const __nv_bfloat16*>(b_.s1), c.F1, t_v1_off, t_v1, w_.dw1_w,
@@ -412,6 +438,90 @@ pkc_status DeviceRunner::finish(cudaStream_t st, std::string& err) {
   return PKC_OK;
 }
 
+void DeviceRunner::drop_graphs() {
+  for (GraphEntry& g : graphs_) {
+    if (g.exec) cudaGraphExecDestroy(g.exec);
+    for (cudaEvent_t e : g.events) cudaEventDestroy(e);
+  }
+  graphs_.clear();
+}
+
+pkc_status DeviceRunner::run_eager(const Plan& p, cudaStream_t st, bool transpose, std::string& err) {
+  cudaGetLastError();  // launch checks below must not see an unrelated earlier error
+  PKC_ST(run_frontend(p, st, err));
+  PKC_ST(run_encoder(p, st, err));
+  if (transpose) {
+    prof_begin(st);
+    PKC_CK(to_channels_first_launch(b_.x, b_.out, cfg_.d_model, t_v_off, t_v, p.B, p.max_v, st), "transpose");
+    prof_end(st, "to_channels_first", 0.0, (double)p.M * cfg_.d_model * 8);
+  }
+  return PKC_OK;
+}
+
+pkc_status DeviceRunner::run_graphed(const Plan& p, cudaStream_t st, bool transpose, std::string& err) {
+  if (!use_graphs_) return run_eager(p, st, transpose, err);
+  GraphEntry* hit = nullptr;
+  for (GraphEntry& g : graphs_)
+    if (g.key == last_key_ && g.pcm == b_.pcm && g.x == b_.x && g.transpose == transpose && g.prof == prof_on_)
+      hit = &g;
+  if (!hit) {
+    GraphEntry ge;
+    ge.key = last_key_;
+    ge.pcm = b_.pcm;
+    ge.x = b_.x;
+    ge.transpose = transpose;
+    ge.prof = prof_on_;
+    std::vector<ProfRec> saved;
+    saved.swap(prof_recs_);
+    capture_events_ = &ge.events;
+    PKC_CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal), "graph capture begin");
+    pkc_status s = run_eager(p, st, transpose, err);
+    cudaGraph_t graph = nullptr;
+    const cudaError_t ce = cudaStreamEndCapture(st, &graph);
+    capture_events_ = nullptr;
+    ge.recs.swap(prof_recs_);
+    prof_recs_.swap(saved);
+    if (s != PKC_OK || ce != cudaSuccess) {
+      if (graph) cudaGraphDestroy(graph);
+      for (cudaEvent_t e : ge.events) cudaEventDestroy(e);
+      cudaGetLastError();
+      if (s == PKC_OK) err = std::string("graph capture: ") + cudaGetErrorString(ce);
+      return s != PKC_OK ? s : PKC_ERR_CUDA;
+    }
+    const cudaError_t ie = cudaGraphInstantiate(&ge.exec, graph, 0);
+    cudaGraphDestroy(graph);
+    if (ie != cudaSuccess) {
+      for (cudaEvent_t e : ge.events) cudaEventDestroy(e);
+      err = std::string("graph instantiate: ") + cudaGetErrorString(ie);
+      return PKC_ERR_CUDA;
+    }
+    if (graphs_.size() >= 4) {
+      cudaStreamSynchronize(st);
+      GraphEntry& old = graphs_.front();
+      cudaGraphExecDestroy(old.exec);
+      for (cudaEvent_t e : old.events) cudaEventDestroy(e);
+      graphs_.erase(graphs_.begin());
+    }
+    graphs_.push_back(std::move(ge));
+    hit = &graphs_.back();
+  }
+  PKC_CK(cudaGraphLaunch(hit->exec, st), "graph launch");
+  if (hit->prof) {
+    // the graph's event nodes are re-recorded on every replay: read them now
+    PKC_CK(cudaStreamSynchronize(st), "profile synchronize");
+    for (const ProfRec& r : hit->recs) {
+      float ms = 0.f;
+      PKC_CK(cudaEventElapsedTime(&ms, r.a, r.b), "profile event read");
+      KernelStatAcc& k = prof_classes_[r.cls];
+      k.launches += 1;
+      k.ms += ms;
+      k.flops += r.flops;
+      k.bytes += r.bytes;
+    }
+  }
+  return PKC_OK;
+}
+
 pkc_status DeviceRunner::encode_pcm_host(const std::vector<const float*>& pcm,
                                          const std::vector<int>& n, int layout, float* host_out,
                                          std::string& err) {
@@ -423,16 +533,10 @@ pkc_status DeviceRunner::encode_pcm_host(const std::vector<const float*>& pcm,
   for (int b = 0; b < p.B; ++b)
     if (n[b] > 0)
       PKC_CK(cudaMemcpyAsync(b_.pcm + p.pcm_off[b], pcm[b], (size_t)n[b] * 4, cudaMemcpyHostToDevice, st), "pcm upload");
-  PKC_ST(run_frontend(p, st, err));
-  PKC_ST(run_encoder(p, st, err));
+  const bool cf = layout == PKC_LAYOUT_CHANNELS_FIRST;
+  PKC_ST(run_graphed(p, st, cf, err));
   const int d = cfg_.d_model;
-  const float* src = b_.x;
-  if (layout == PKC_LAYOUT_CHANNELS_FIRST) {
-    prof_begin(st);
-    PKC_CK(to_channels_first_launch(b_.x, b_.out, d, t_v_off, t_v, p.B, p.max_v, st), "transpose");
-    prof_end(st, "to_channels_first", 0.0, (double)p.M * d * 8);
-    src = b_.out;
-  }
+  const float* src = cf ? b_.out : b_.x;
   PKC_CK(cudaMemcpyAsync(host_out, src, (size_t)p.M * d * 4, cudaMemcpyDeviceToHost, st), "output download");
   return finish(st, err);
 }
@@ -448,8 +552,7 @@ pkc_status DeviceRunner::encode_pcm_device(const float* d_pcm, const std::vector
   float* saved_x = b_.x;
   b_.pcm = const_cast<float*>(d_pcm);
   b_.x = d_out;
-  pkc_status s = run_frontend(p, st, err);
-  if (s == PKC_OK) s = run_encoder(p, st, err);
+  pkc_status s = run_graphed(p, st, false, err);
   b_.pcm = saved_pcm;
   b_.x = saved_x;
   if (s != PKC_OK) return s;

@@ -100,11 +100,29 @@ class DeviceRunner {
   // profiling
   bool prof_on_ = false;
   struct ProfRec { int cls; cudaEvent_t a, b; double flops, bytes; };
+  // CUDA graphs of the whole launch sequence, one per (plan, in/out pointers):
+  // replaying skips ~380 host launches and tensor-map encodes per batch
+  struct GraphEntry {
+    std::vector<int> key;
+    const void* pcm = nullptr;
+    const void* x = nullptr;
+    bool transpose = false, prof = false;
+    cudaGraphExec_t exec = nullptr;
+    std::vector<ProfRec> recs;
+    std::vector<cudaEvent_t> events;
+  };
+  std::vector<GraphEntry> graphs_;
+  std::vector<cudaEvent_t>* capture_events_ = nullptr;
+  bool use_graphs_ = true;
+  pkc_status run_graphed(const Plan& p, cudaStream_t st, bool transpose, std::string& err);
+  pkc_status run_eager(const Plan& p, cudaStream_t st, bool transpose, std::string& err);
+  void drop_graphs();
   std::vector<ProfRec> prof_recs_;
   std::vector<cudaEvent_t> ev_pool_;
   size_t ev_next_ = 0;
   std::vector<KernelStatAcc> prof_classes_;
   cudaEvent_t prof_open_ = nullptr;
+  bool prof_error_ = false;  // an event call failed while profiling (reported by profile_read)
 };
 
 }  // namespace pkc

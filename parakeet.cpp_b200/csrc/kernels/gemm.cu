@@ -3,20 +3,13 @@
 // accumulated in f32 in tensor memory by tcgen05.mma (kind::f16), operands
 // staged by TMA (128-byte swizzle) through a 4-deep mbarrier pipeline.
 //
-// Warp roles (128 threads, one CTA per 128x256 output tile):
-//   warp 0 lane 0  TMA producer
+// Persistent CTAs (one per SM), 6 warps:
+//   warp 0 lane 0  TMA producer (runs ahead across tiles through a 4-stage ring)
 //   warp 1 lane 0  MMA issuer (single thread, as tcgen05 requires)
-//   warps 0..3     epilogue: each warp drains its 32 TMEM lanes (= 32 rows)
+//   warps 2..5     epilogue: warp w drains TMEM lanes [32(w%4), 32(w%4)+32)
+// Two 256-column f32 accumulators in TMEM (all 512 columns): the epilogue of
+// tile i runs while the MMAs of tile i+1 fill the other accumulator.
 //
-// Fused epilogues (the reference runs each as a separate ggml node):
-//   STORE_H   : out_h   = act(acc + bias)                    (act: none/SiLU/ReLU)
-//   RESID_F32 : out_f32 = out_f32 + alpha * (acc + bias)     (half-step FFN, residual adds)
-//   STORE_F32 : out_f32 = alpha * (acc + bias)               (subsampling output linear, xscale)
-//   GLU_H     : out_h[c] = (a + ba) * sigmoid(g + bg)        (conv module pointwise_conv1 + GLU)
-//   POWER_F32 : out_f32[c] = a^2 + g^2                       (mel DFT: re^2 + im^2)
-// For GLU_H / POWER_F32 the weight rows are pre-arranged so that within each
-// 256-column tile, columns [0,128) hold the "a" half and [128,256) the paired
-// "g" half; the tile writes 128 output columns starting at n0/2.
 #include "common.cuh"
 #include "gemm.h"
 
@@ -28,95 +21,20 @@ constexpr int BM = 128;
 constexpr int BN = 256;
 constexpr int BK = 64;  // 64 x 2 bytes = one 128-byte swizzle row
 constexpr int STAGES = 4;
-constexpr int THREADS = 128;
+constexpr int EPI_WARPS = 4;
+constexpr int THREADS = 64 + 32 * EPI_WARPS;
 constexpr int A_STAGE_BYTES = BM * BK * 2;
 constexpr int B_STAGE_BYTES = BN * BK * 2;
 constexpr int SMEM_BYTES = STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + 256 + 1024;
-constexpr uint32_t TMEM_COLS = 256;
+constexpr uint32_t TMEM_COLS = 512;  // two 128 x 256 f32 accumulators
 
+// Drain one 128 x 256 accumulator (this thread: one row, trow = its TMEM row
+// address) through the fused epilogue. Every lane executes the TMEM loads
+// (.sync.aligned); only rows inside M store.
 template <typename H, int EPI>
-__global__ void __launch_bounds__(THREADS, 1)
-    k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
-              GemmArgs args) {
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem =
-      reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sA = smem;
-  uint8_t* sB = smem + STAGES * A_STAGE_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * B_STAGE_BYTES);
-  // bars[0..S) full, bars[S..2S) empty, bars[2S] accumulator ready
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 1);
-
-  const int warp = threadIdx.x >> 5;
-  const int lane = threadIdx.x & 31;
-  const int n0 = blockIdx.x * BN;
-  const int m0 = blockIdx.y * BM;
-  const int KB = args.K / BK;
-
-  if (threadIdx.x == 0) {
-    prefetch_tmap(&tmA);
-    prefetch_tmap(&tmB);
-    for (int s = 0; s < 2 * STAGES + 1; ++s) mbar_init(smem_u32(&bars[s]), 1);
-    fence_barrier_init();
-    fence_proxy_async_smem();
-  }
-  if (warp == 0) {
-    tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = *tmem_slot;
-  const uint32_t accb = smem_u32(&bars[2 * STAGES]);
-
-  if (warp == 0 && lane == 0) {
-    // ---- TMA producer
-    for (int kb = 0; kb < KB; ++kb) {
-      const int s = kb % STAGES;
-      const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
-      if (!mbar_wait(smem_u32(&bars[STAGES + s]), ph ^ 1u, args.err, DEV_ERR_TIMEOUT_EMPTY)) break;
-      const uint32_t fb = smem_u32(&bars[s]);
-      mbar_arrive_expect_tx(fb, A_STAGE_BYTES + B_STAGE_BYTES);
-      tma_load_2d(smem_u32(sA + s * A_STAGE_BYTES), &tmA, fb, kb * BK, m0);
-      tma_load_2d(smem_u32(sB + s * B_STAGE_BYTES), &tmB, fb, kb * BK, n0);
-    }
-  } else if (warp == 1 && lane == 0) {
-    // ---- MMA issuer
-    constexpr uint32_t idesc = idesc_f16(BM, BN, is_bf16<H>::value ? 1 : 0);
-    bool ok = true;
-    for (int kb = 0; kb < KB; ++kb) {
-      const int s = kb % STAGES;
-      const uint32_t ph = (uint32_t)(kb / STAGES) & 1u;
-      if (!mbar_wait(smem_u32(&bars[s]), ph, args.err, DEV_ERR_TIMEOUT_FULL)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const uint64_t da = smem_desc_sw128(smem_u32(sA + s * A_STAGE_BYTES));
-      const uint64_t db = smem_desc_sw128(smem_u32(sB + s * B_STAGE_BYTES));
-#pragma unroll
-      for (int k = 0; k < BK / 16; ++k) {
-        // advance 16 elements (32 bytes) along K inside the swizzle atom
-        umma_f16(tmem, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc,
-                 (kb > 0 || k > 0) ? 1u : 0u);
-      }
-      umma_commit(smem_u32(&bars[STAGES + s]));
-    }
-    if (ok) umma_commit(accb);
-  }
-  __syncwarp();
-
-  // ---- epilogue: warp w owns TMEM lanes [32w, 32w+32) = tile rows
-  // every lane waits, then the warp reconverges before the .sync.aligned loads
-  const bool have_acc =
-      __all_sync(0xffffffffu, mbar_wait(accb, 0, args.err, DEV_ERR_TIMEOUT_ACCUM) ? 1 : 0) != 0;
-  tc_fence_after();
-  const int row = m0 + warp * 32 + lane;
-  const bool row_ok = have_acc && row < args.M;
-  const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+__device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t trow, int row,
+                                              bool row_ok, int n0) {
   uint32_t r[32];
-
   if constexpr (EPI == EPI_GLU_H || EPI == EPI_POWER_F32) {
     uint32_t g[32];
 #pragma unroll 1
@@ -145,8 +63,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
         for (int q = 0; q < 4; ++q) o4[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
       } else {
-        float* out = reinterpret_cast<float*>(args.out) + (size_t)row * args.ldo + oc;
-        float4* o4 = reinterpret_cast<float4*>(out);
+        float4* o4 = reinterpret_cast<float4*>(reinterpret_cast<float*>(args.out) + (size_t)row * args.ldo + oc);
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
           float v[4];
@@ -182,15 +99,13 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
           for (int i = 0; i < 32; ++i) v[i] = fmaxf(v[i], 0.0f);
         }
-        H* out = reinterpret_cast<H*>(args.out) + (size_t)row * args.ldo + n;
-        uint4* o4 = reinterpret_cast<uint4*>(out);
+        uint4* o4 = reinterpret_cast<uint4*>(reinterpret_cast<H*>(args.out) + (size_t)row * args.ldo + n);
 #pragma unroll
         for (int q = 0; q < 4; ++q)
           o4[q] = make_uint4(pack2<H>(v[8 * q], v[8 * q + 1]), pack2<H>(v[8 * q + 2], v[8 * q + 3]),
                              pack2<H>(v[8 * q + 4], v[8 * q + 5]), pack2<H>(v[8 * q + 6], v[8 * q + 7]));
       } else if constexpr (EPI == EPI_RESID_F32) {
-        float4* o4 = reinterpret_cast<float4*>(reinterpret_cast<float*>(args.out) +
-                                               (size_t)row * args.ldo + n);
+        float4* o4 = reinterpret_cast<float4*>(reinterpret_cast<float*>(args.out) + (size_t)row * args.ldo + n);
 #pragma unroll
         for (int q = 0; q < 8; ++q) {
           float4 o = o4[q];
@@ -201,13 +116,132 @@ __global__ void __launch_bounds__(THREADS, 1)
           o4[q] = o;
         }
       } else {  // EPI_STORE_F32
-        float4* o4 = reinterpret_cast<float4*>(reinterpret_cast<float*>(args.out) +
-                                               (size_t)row * args.ldo + n);
+        float4* o4 = reinterpret_cast<float4*>(reinterpret_cast<float*>(args.out) + (size_t)row * args.ldo + n);
 #pragma unroll
         for (int q = 0; q < 8; ++q)
-          o4[q] = make_float4(args.alpha * v[4 * q], args.alpha * v[4 * q + 1],
-                              args.alpha * v[4 * q + 2], args.alpha * v[4 * q + 3]);
+          o4[q] = make_float4(args.alpha * v[4 * q], args.alpha * v[4 * q + 1], args.alpha * v[4 * q + 2],
+                              args.alpha * v[4 * q + 3]);
       }
+    }
+  }
+}
+
+template <typename H, int EPI>
+__global__ void __launch_bounds__(THREADS, 1)
+    k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+              GemmArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem =
+      reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES * A_STAGE_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * B_STAGE_BYTES);
+  // bars: [0,S) full, [S,2S) empty, 2S+{0,1} accumulator full, 2S+{2,3} accumulator empty
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int KB = args.K / BK;
+  const int tiles_m = (args.M + BM - 1) / BM;
+  const int n_tiles = tiles_m * (args.N / BN);
+
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+    for (int s = 0; s < 2 * STAGES; ++s) mbar_init(smem_u32(&bars[s]), 1);
+    mbar_init(smem_u32(&bars[2 * STAGES + 0]), 1);
+    mbar_init(smem_u32(&bars[2 * STAGES + 1]), 1);
+    mbar_init(smem_u32(&bars[2 * STAGES + 2]), EPI_WARPS);
+    mbar_init(smem_u32(&bars[2 * STAGES + 3]), EPI_WARPS);
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 0) {
+    tmem_alloc(smem_u32(tmem_slot), TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---- TMA producer
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
+        const int m0 = (tile % tiles_m) * BM;
+        const int n0 = (tile / tiles_m) * BN;
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1u;
+          if (!mbar_wait(smem_u32(&bars[STAGES + s]), ph ^ 1u, args.err, DEV_ERR_TIMEOUT_EMPTY)) {
+            ok = false;
+            break;
+          }
+          const uint32_t fb = smem_u32(&bars[s]);
+          mbar_arrive_expect_tx(fb, A_STAGE_BYTES + B_STAGE_BYTES);
+          tma_load_2d(smem_u32(sA + s * A_STAGE_BYTES), &tmA, fb, kb * BK, m0);
+          tma_load_2d(smem_u32(sB + s * B_STAGE_BYTES), &tmB, fb, kb * BK, n0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      // ---- MMA issuer
+      constexpr uint32_t idesc = idesc_f16(BM, BN, is_bf16<H>::value ? 1 : 0);
+      uint32_t it = 0;
+      int local = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x, ++local) {
+        const int buf = local & 1;
+        const uint32_t use = (uint32_t)(local >> 1);
+        if (!mbar_wait(smem_u32(&bars[2 * STAGES + 2 + buf]), (use & 1u) ^ 1u, args.err,
+                       DEV_ERR_TIMEOUT_ACCUM))
+          break;
+        tc_fence_after();
+        const uint32_t acc = tmem + (uint32_t)(buf * BN);
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1u;
+          if (!mbar_wait(smem_u32(&bars[s]), ph, args.err, DEV_ERR_TIMEOUT_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = smem_desc_sw128(smem_u32(sA + s * A_STAGE_BYTES));
+          const uint64_t db = smem_desc_sw128(smem_u32(sB + s * B_STAGE_BYTES));
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            umma_f16(acc, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc,
+                     (kb > 0 || k > 0) ? 1u : 0u);
+          umma_commit(smem_u32(&bars[STAGES + s]));  // frees the smem stage
+        }
+        if (ok) umma_commit(smem_u32(&bars[2 * STAGES + buf]));  // accumulator ready
+      }
+    }
+  } else {
+    // ---- epilogue warps 2..5
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    int local = 0;
+    for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++local) {
+      const int buf = local & 1;
+      const uint32_t use = (uint32_t)(local >> 1);
+      const bool have =
+          __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars[2 * STAGES + buf]), use & 1u, args.err,
+                                            DEV_ERR_TIMEOUT_ACCUM) ? 1 : 0) != 0;
+      if (!have) break;
+      tc_fence_after();
+      const int m0 = (tile % tiles_m) * BM;
+      const int n0 = (tile / tiles_m) * BN;
+      const int row = m0 + q * 32 + lane;
+      const bool row_ok = row < args.M;
+      const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
+      epilogue_tile<H, EPI>(args, trow, row, row_ok, n0);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&bars[2 * STAGES + 2 + buf]));
     }
   }
 
@@ -259,7 +293,10 @@ static cudaError_t launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const 
     if (e != cudaSuccess) return e;
     attr_set[dev & 63] = true;
   }
-  dim3 grid(a.N / BN, (a.M + BM - 1) / BM);
+  static int n_sm[64] = {};
+  if (!n_sm[dev & 63]) cudaDeviceGetAttribute(&n_sm[dev & 63], cudaDevAttrMultiProcessorCount, dev);
+  const int n_tiles = (a.N / BN) * ((a.M + BM - 1) / BM);
+  const int grid = n_tiles < n_sm[dev & 63] ? n_tiles : n_sm[dev & 63];
   kern<<<grid, THREADS, SMEM_BYTES, st>>>(ta, tb, a);
   return cudaGetLastError();
 }
@@ -273,7 +310,7 @@ cudaError_t gemm_launch(const void* A, int lda, const void* B, int ldb, bool bf1
   if (args.M <= 0) return cudaSuccess;
   if (args.N % BN != 0 || args.K % BK != 0 || args.K <= 0 || (lda % 8) != 0 || (ldb % 8) != 0 ||
       (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15) ||
-      (args.ldo % 8) != 0 || args.M > 65535 * BM)
+      (args.ldo % 8) != 0)
     return cudaErrorInvalidValue;
   CUtensorMap ta, tb;
   if (!make_tmap_kmajor(&ta, A, args.M, args.K, lda, BM, bf16)) return cudaErrorInvalidValue;

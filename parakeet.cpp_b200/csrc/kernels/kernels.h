@@ -64,7 +64,7 @@ cudaError_t batch_to_packed_launch(const float* in, int n_mels, int T_max, float
 
 // Subsampling stage 0: Conv2d(1 -> C, 3x3, stride 2, pad 1) + bias + ReLU.
 cudaError_t sub_conv0_launch(const float* logmel, int F, const float* w /*[C][9]*/, const float* b,
-                             int C, __nv_bfloat16* out, int F1, const ItemTables& t, int max_v1,
+                             int C, __nv_bfloat16* out, int F1, const ItemTables& t, int total_v1,
                              cudaStream_t st);
 // Depthwise Conv2d(C, 3x3, stride 2, pad 1, groups C) + bias.
 // stage 1: in = (v1, F_in) -> out = (v2, F_out); stage 2: (v2 -> v)

@@ -90,47 +90,65 @@ __global__ void k_pos_table(H* out, int centre, int d) {
   out[(size_t)r * d + 2 * i + 1] = to_h<H>((float)cos(arg));
 }
 
-// One thread = one frame x 8 channels. grid (.., B)
-template <typename H>
-__global__ void __launch_bounds__(256)
-    k_dwconv_bn_silu(const H* __restrict__ in, H* __restrict__ out, int d, int K,
+// One CTA = DW_FRAMES consecutive frames of one utterance x all d channels;
+// one thread = 8 channels (16-byte loads), its K taps held in registers and
+// reused across the CTA's frames. grid (ceil(max_len / DW_FRAMES), B)
+constexpr int DW_FRAMES = 16;
+
+template <typename H, int K>
+__global__ void __launch_bounds__(128)
+    k_dwconv_bn_silu(const H* __restrict__ in, H* __restrict__ out, int d,
                      const float* __restrict__ w, const float* __restrict__ bias,
                      const float* __restrict__ scale, const float* __restrict__ shift,
                      const int* __restrict__ item_off, const int* __restrict__ item_len) {
   const int b = blockIdx.y;
-  const int cg = d / 8;
-  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   const int T = item_len[b];
-  if (idx >= (long long)T * cg) return;
-  const int c0 = (int)(idx % cg) * 8;
-  const int t = (int)(idx / cg);
-  const int pad = (K - 1) / 2;
+  const int t0 = blockIdx.x * DW_FRAMES;
+  if (t0 >= T) return;
+  constexpr int pad = (K - 1) / 2;
   const H* x = in + (size_t)item_off[b] * d;
-  float acc[8];
+  H* y = out + (size_t)item_off[b] * d;
+  for (int c0 = threadIdx.x * 8; c0 < d; c0 += blockDim.x * 8) {
+    float wk[K][8];
 #pragma unroll
-  for (int c = 0; c < 8; ++c) acc[c] = 0.f;
-  for (int k = 0; k < K; ++k) {
-    const int ti = t + k - pad;
-    if (ti < 0 || ti >= T) continue;
-    const uint4 raw = *reinterpret_cast<const uint4*>(x + (size_t)ti * d + c0);
-    const H* hv = reinterpret_cast<const H*>(&raw);
-    const float* wk = w + (size_t)k * d + c0;
+    for (int k = 0; k < K; ++k) {
+      const float4 a = *reinterpret_cast<const float4*>(w + (size_t)k * d + c0);
+      const float4 c = *reinterpret_cast<const float4*>(w + (size_t)k * d + c0 + 4);
+      wk[k][0] = a.x; wk[k][1] = a.y; wk[k][2] = a.z; wk[k][3] = a.w;
+      wk[k][4] = c.x; wk[k][5] = c.y; wk[k][6] = c.z; wk[k][7] = c.w;
+    }
+    float bi[8], sc[8], sh[8];
 #pragma unroll
-    for (int c = 0; c < 8; ++c) acc[c] = fmaf(wk[c], from_h(hv[c]), acc[c]);
+    for (int c = 0; c < 8; ++c) {
+      bi[c] = bias ? bias[c0 + c] : 0.f;
+      sc[c] = scale[c0 + c];
+      sh[c] = shift[c0 + c];
+    }
+    const int t1 = min(t0 + DW_FRAMES, T);
+    for (int t = t0; t < t1; ++t) {
+      float acc[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) acc[c] = 0.f;
+#pragma unroll
+      for (int k = 0; k < K; ++k) {
+        const int ti = t + k - pad;
+        if (ti < 0 || ti >= T) continue;
+        const uint4 raw = *reinterpret_cast<const uint4*>(x + (size_t)ti * d + c0);
+        const H* hv = reinterpret_cast<const H*>(&raw);
+#pragma unroll
+        for (int c = 0; c < 8; ++c) acc[c] = fmaf(wk[k][c], from_h(hv[c]), acc[c]);
+      }
+      float r[8];
+#pragma unroll
+      for (int c = 0; c < 8; ++c) r[c] = siluf_((acc[c] + bi[c]) * sc[c] + sh[c]);
+      uint4 o;
+      o.x = pack2<H>(r[0], r[1]);
+      o.y = pack2<H>(r[2], r[3]);
+      o.z = pack2<H>(r[4], r[5]);
+      o.w = pack2<H>(r[6], r[7]);
+      *reinterpret_cast<uint4*>(y + (size_t)t * d + c0) = o;
+    }
   }
-  float r[8];
-#pragma unroll
-  for (int c = 0; c < 8; ++c) {
-    float y = acc[c] + (bias ? bias[c0 + c] : 0.f);
-    y = y * scale[c0 + c] + shift[c0 + c];
-    r[c] = siluf_(y);
-  }
-  uint4 o;
-  o.x = pack2<H>(r[0], r[1]);
-  o.y = pack2<H>(r[2], r[3]);
-  o.z = pack2<H>(r[4], r[5]);
-  o.w = pack2<H>(r[6], r[7]);
-  *reinterpret_cast<uint4*>(out + ((size_t)item_off[b] + t) * d + c0) = o;
 }
 
 // 32x32 tiled transpose per item: out[off*d + c*T + t] = x[(off + t)*d + c]
@@ -192,14 +210,23 @@ cudaError_t dwconv_bn_silu_launch(const void* in, void* out, int d, int K, const
                                   bool bf16, cudaStream_t st) {
   if (B <= 0 || max_len <= 0) return cudaSuccess;
   if (d % 8) return cudaErrorInvalidValue;
-  const long long n = (long long)max_len * (d / 8);
-  const dim3 grid((unsigned)((n + 255) / 256), B);
-  if (bf16)
-    k_dwconv_bn_silu<__nv_bfloat16><<<grid, 256, 0, st>>>((const __nv_bfloat16*)in, (__nv_bfloat16*)out, d,
-                                                          K, w, bias, scale, shift, item_off, item_len);
-  else
-    k_dwconv_bn_silu<__half><<<grid, 256, 0, st>>>((const __half*)in, (__half*)out, d, K, w, bias, scale,
-                                                   shift, item_off, item_len);
+  const dim3 grid((max_len + DW_FRAMES - 1) / DW_FRAMES, B);
+  const int threads = d / 8 < 128 ? d / 8 : 128;
+#define PKC_DW(KK)                                                                                 \
+  if (bf16)                                                                                        \
+    k_dwconv_bn_silu<__nv_bfloat16, KK><<<grid, threads, 0, st>>>(                                  \
+        (const __nv_bfloat16*)in, (__nv_bfloat16*)out, d, w, bias, scale, shift, item_off, item_len); \
+  else                                                                                             \
+    k_dwconv_bn_silu<__half, KK><<<grid, threads, 0, st>>>((const __half*)in, (__half*)out, d, w, bias, \
+                                                          scale, shift, item_off, item_len);
+  switch (K) {
+    case 9: PKC_DW(9) break;
+    case 7: PKC_DW(7) break;
+    case 5: PKC_DW(5) break;
+    case 3: PKC_DW(3) break;
+    default: return cudaErrorInvalidValue;
+  }
+#undef PKC_DW
   return cudaGetLastError();
 }
 

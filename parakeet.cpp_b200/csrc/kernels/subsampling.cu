@@ -19,47 +19,46 @@ namespace pkc {
 namespace {
 
 // conv.0: 1 -> C channels, 3x3, stride 2, pad 1, + bias, ReLU.
-// One thread = one output (t, f) and 8 channels. grid (.., B)
+// One CTA = one output frame of one utterance, one thread per channel: the
+// thread keeps its 9 taps in registers, the three input mel rows sit in shared
+// memory, and each step over f writes C consecutive bf16 (coalesced).
+// grid.x = sum of v1 over the batch (row -> utterance by binary search).
 __global__ void __launch_bounds__(256)
     k_conv0(const float* __restrict__ logmel, int F, const float* __restrict__ w,
             const float* __restrict__ bias, int C, __nv_bfloat16* __restrict__ out, int F1,
             ItemTables t) {
-  const int b = blockIdx.y;
-  const int cg = C / 8;
-  const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  const int v1 = t.v1[b];
-  if (idx >= (long long)v1 * F1 * cg) return;
-  const int c0 = (int)(idx % cg) * 8;
-  const long long pos = idx / cg;
-  const int f = (int)(pos % F1);
-  const int tt = (int)(pos / F1);
+  extern __shared__ float rows[];  // [3][F + 2], zero padded on both sides
+  const int row = blockIdx.x;
+  int lo = 0, hi = t.B - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (t.v1_off[mid] <= row) lo = mid; else hi = mid - 1;
+  }
+  const int b = lo;
+  const int tt = row - t.v1_off[b];
   const int valid = t.mel_valid[b];  // masked mel frames past this are zero
   const float* x = logmel + (size_t)t.mel_off[b] * F;
-  float in[9];
-#pragma unroll
-  for (int kh = 0; kh < 3; ++kh) {
+  for (int i = threadIdx.x; i < 3 * (F + 2); i += blockDim.x) {
+    const int kh = i / (F + 2), fi = i % (F + 2) - 1;
     const int ti = 2 * tt - 1 + kh;
+    rows[i] = (fi >= 0 && fi < F && ti >= 0 && ti < valid) ? x[(size_t)ti * F + fi] : 0.f;
+  }
+  __syncthreads();
+  __nv_bfloat16* o = out + (size_t)row * F1 * C;
+  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    float wk[9];
 #pragma unroll
-    for (int kw = 0; kw < 3; ++kw) {
-      const int fi = 2 * f - 1 + kw;
-      in[kh * 3 + kw] = (ti >= 0 && ti < valid && fi >= 0 && fi < F) ? x[(size_t)ti * F + fi] : 0.f;
+    for (int k = 0; k < 9; ++k) wk[k] = w[c * 9 + k];
+    const float bc = bias[c];
+    for (int f = 0; f < F1; ++f) {
+      float s = bc;
+#pragma unroll
+      for (int kh = 0; kh < 3; ++kh)
+#pragma unroll
+        for (int kw = 0; kw < 3; ++kw) s = fmaf(wk[kh * 3 + kw], rows[kh * (F + 2) + 2 * f + kw], s);
+      o[(size_t)f * C + c] = __float2bfloat16_rn(fmaxf(s, 0.f));
     }
   }
-  float acc[8];
-#pragma unroll
-  for (int c = 0; c < 8; ++c) {
-    float s = bias[c0 + c];
-    const float* wc = w + (c0 + c) * 9;
-#pragma unroll
-    for (int k = 0; k < 9; ++k) s = fmaf(wc[k], in[k], s);
-    acc[c] = fmaxf(s, 0.f);
-  }
-  uint4 o;
-  o.x = pack2<__nv_bfloat16>(acc[0], acc[1]);
-  o.y = pack2<__nv_bfloat16>(acc[2], acc[3]);
-  o.z = pack2<__nv_bfloat16>(acc[4], acc[5]);
-  o.w = pack2<__nv_bfloat16>(acc[6], acc[7]);
-  *reinterpret_cast<uint4*>(out + (((size_t)t.v1_off[b] + tt) * F1 + f) * C + c0) = o;
 }
 
 // depthwise 3x3 stride 2 pad 1 + bias (no activation: ReLU follows the pointwise conv)
@@ -108,12 +107,11 @@ __global__ void __launch_bounds__(256)
 }  // namespace
 
 cudaError_t sub_conv0_launch(const float* logmel, int F, const float* w, const float* b, int C,
-                             __nv_bfloat16* out, int F1, const ItemTables& t, int max_v1,
+                             __nv_bfloat16* out, int F1, const ItemTables& t, int total_v1,
                              cudaStream_t st) {
-  if (t.B <= 0 || max_v1 <= 0) return cudaSuccess;
-  if (C % 8) return cudaErrorInvalidValue;
-  const long long n = (long long)max_v1 * F1 * (C / 8);
-  k_conv0<<<dim3((unsigned)((n + 255) / 256), t.B), 256, 0, st>>>(logmel, F, w, b, C, out, F1, t);
+  if (t.B <= 0 || total_v1 <= 0) return cudaSuccess;
+  const size_t smem = (size_t)3 * (F + 2) * sizeof(float);
+  k_conv0<<<total_v1, 256, smem, st>>>(logmel, F, w, b, C, out, F1, t);
   return cudaGetLastError();
 }
 

@@ -156,7 +156,8 @@ std::string read_config(const GgufFile& g, Config& c) {
   if (c.conv_norm_type != "batch_norm") return "conv_norm_type " + c.conv_norm_type + " (streaming) not supported";
   if (c.att_context_style != "regular" || c.causal_downsampling || c.conv_causal)
     return "cache-aware streaming models are out of scope";
-  if (c.conv_kernel % 2 == 0) return "depthwise kernel must be odd";
+  if (c.conv_kernel % 2 == 0 || c.conv_kernel < 3 || c.conv_kernel > 9)
+    return "depthwise kernel must be odd, 3..9";
   if (c.n_fft != 512) return "n_fft must be 512";
   if (c.hop_length <= 0 || c.win_length <= 0 || c.win_length > c.n_fft) return "bad STFT geometry";
   if (c.mag_power != 2.f) return "mag_power must be 2";

@@ -20,7 +20,8 @@ def _setup(M, N, K, dtype, seed=0):
 
 
 @pytest.mark.parametrize("bf16", [False, True])
-@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (300, 512, 1024), (1000, 1024, 4096), (7, 256, 128)])
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (300, 512, 1024), (1000, 1024, 4096), (7, 256, 128),
+                                   (20000, 1024, 256), (4099, 3072, 1024)])
 def test_store_h_bias(cuda, bf16, M, N, K):
     import torch
     import pkc
