@@ -159,6 +159,14 @@ pkc_status pkc_gemm(const void* A, int lda, const void* Bw, int ldb, int M, int 
                     int dtype, int epi, int act, float alpha, const float* bias, void* out,
                     int ldo, void* stream);
 
+/* Relative-position attention of one layer for B utterances packed along
+   rows (item b owns rows [off_b, off_b + len[b])). qkv [M, 3d] and ptab
+   [2*centre-1, d] in the compute type (dtype 0 f16, 1 bf16), bias_u/v [d] f32,
+   ctx [M, d] out. centre >= max len. Device pointers; lens on the host. */
+pkc_status pkc_relpos_attention(const void* qkv, const void* ptab, int centre,
+                                const float* bias_u, const float* bias_v, const int* lens, int B,
+                                int d, int n_heads, int dtype, void* ctx, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -9,6 +9,8 @@
 
 #include "../../include/pkc.h"
 #include "kernels/gemm.h"
+#include "kernels/kernels.h"
+#include <vector>
 #include "status.hpp"
 
 namespace {
@@ -61,3 +63,40 @@ extern "C" pkc_status pkc_gemm(const void* A, int lda, const void* Bw, int ldb, 
 }
 
 extern "C" int pkc_abi_version(void) { return PKC_ABI_VERSION; }
+
+extern "C" pkc_status pkc_relpos_attention(const void* qkv, const void* ptab, int centre,
+                                           const float* bias_u, const float* bias_v, const int* lens,
+                                           int B, int d, int n_heads, int dtype, void* ctx,
+                                           void* stream) {
+  if (!qkv || !ptab || !bias_u || !bias_v || !lens || B <= 0 || !ctx || n_heads <= 0 ||
+      (dtype != 0 && dtype != 1))
+    return pkc::set_thread_error(PKC_ERR_ARG, "pkc_relpos_attention: bad arguments");
+  std::vector<int> off(B + 1, 0), len(lens, lens + B), tiles;
+  for (int b = 0; b < B; ++b) {
+    if (len[b] <= 0 || len[b] > centre)
+      return pkc::set_thread_error(PKC_ERR_ARG, "pkc_relpos_attention: lens must be in [1, centre]");
+    off[b + 1] = off[b] + len[b];
+    for (int q0 = 0; q0 < len[b]; q0 += pkc::attn_query_tile()) {
+      tiles.push_back(b);
+      tiles.push_back(q0);
+    }
+  }
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  std::vector<int> host;
+  host.insert(host.end(), off.begin(), off.end());
+  host.insert(host.end(), len.begin(), len.end());
+  host.insert(host.end(), tiles.begin(), tiles.end());
+  int* dtab = nullptr;
+  if (cudaMalloc(&dtab, host.size() * sizeof(int)) != cudaSuccess)
+    return pkc::set_thread_error(PKC_ERR_OOM, "pkc_relpos_attention: table allocation failed");
+  cudaMemcpyAsync(dtab, host.data(), host.size() * sizeof(int), cudaMemcpyHostToDevice, st);
+  pkc::AttnArgs a{qkv, ptab, 2 * centre - 1, centre, bias_u, bias_v, dtab + 2 * B + 1,
+                  (int)tiles.size() / 2, dtab, dtab + B + 1, ctx, d, n_heads};
+  cudaError_t e = pkc::attention_launch(a, dtype == 1, st);
+  cudaError_t e2 = cudaStreamSynchronize(st);
+  cudaFree(dtab);
+  if (e != cudaSuccess || e2 != cudaSuccess)
+    return pkc::set_thread_error(PKC_ERR_CUDA, std::string("pkc_relpos_attention: ") +
+                                                   cudaGetErrorString(e != cudaSuccess ? e : e2));
+  return PKC_OK;
+}

@@ -28,7 +28,6 @@ namespace {
 constexpr int QT = 64;   // query rows per CTA
 constexpr int KT = 32;   // keys per iteration
 constexpr int PW = QT + KT - 1;  // positional rows needed per CTA iteration (95)
-constexpr int PWR = 96;          // rounded
 constexpr int WPWR = 48;         // positional rows per warp: 16 + KT - 1 = 47, rounded to n8
 constexpr int NTHREADS = 128;
 
@@ -67,19 +66,28 @@ __device__ __forceinline__ void mma16816<__nv_bfloat16>(float (&d)[4], const uin
       : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
 }
 
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
+  // zero-fills the 16 bytes when !valid (src-size 0)
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(valid ? 16 : 0)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+constexpr int PRING = 128;  // positional rows resident: window (QT+KT-1) + next KT
+
 template <typename H, int DK>
 struct AttnSmem {
   static constexpr int LD = DK + 8;  // padded row (halves): conflict-free ldmatrix
-  H qu[QT * LD];
-  H qv[QT * LD];
-  H k[KT * LD];
-  H v[KT * LD];
-  H p[PWR * LD];
+  H k[2][KT * LD];
+  H v[2][KT * LD];
+  H p[PRING * LD];                  // ring over absolute positional rows (row mod PRING)
   float bd[4][16][WPWR + 4];
 };
 
 template <typename H, int DK>
-__global__ void __launch_bounds__(NTHREADS)
+__global__ void __launch_bounds__(NTHREADS, 2)
     k_relpos_attn(const H* __restrict__ qkv, const H* __restrict__ ptab, int ptab_rows, int centre,
                   const float* __restrict__ bias_u, const float* __restrict__ bias_v,
                   const int* __restrict__ tiles,     // [n_tiles][2]: item, q0
@@ -89,6 +97,7 @@ __global__ void __launch_bounds__(NTHREADS)
   extern __shared__ __align__(16) uint8_t smem_raw[];
   using S = AttnSmem<H, DK>;
   constexpr int LD = S::LD;
+  constexpr int CH = DK / 8;  // 16-byte chunks per row
   S& sm = *reinterpret_cast<S*>(smem_raw);
 
   const int tile = blockIdx.x;
@@ -100,31 +109,59 @@ __global__ void __launch_bounds__(NTHREADS)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g = lane >> 2, t4 = lane & 3;
   const int ld3 = 3 * d;
+  const int iw = q0 + warp * 16;             // first query row of this warp
+  const int rb0 = centre - 1 - (q0 + QT - 1);  // first positional row of key tile 0's window
 
-  // ---- Q tile -> (q + u), (q + v), rounded to H
-  {
-    constexpr int CH = DK / 8;
-    for (int i = threadIdx.x; i < QT * CH; i += NTHREADS) {
+  auto load_kv = [&](int stage, int j0) {
+    for (int i = threadIdx.x; i < KT * CH; i += NTHREADS) {
       const int r = i / CH, c = i % CH;
-      const int qi = q0 + r;
-      float qf[8];
-      if (qi < T) {
-        uint4 raw = *reinterpret_cast<const uint4*>(qkv + (size_t)(off + qi) * ld3 + head * DK + c * 8);
-        const H* hv = reinterpret_cast<const H*>(&raw);
+      const int kj = j0 + r;
+      const bool ok = kj < T;
+      const H* base = qkv + (size_t)(off + (ok ? kj : 0)) * ld3 + head * DK + c * 8;
+      cp_async16(smem_u32(&sm.k[stage][r * LD + c * 8]), base + d, ok);
+      cp_async16(smem_u32(&sm.v[stage][r * LD + c * 8]), base + 2 * d, ok);
+    }
+  };
+  auto load_p = [&](int pr0, int nrows) {  // absolute positional rows [pr0, pr0 + nrows)
+    for (int i = threadIdx.x; i < nrows * CH; i += NTHREADS) {
+      const int r = i / CH, c = i % CH;
+      const int pr = pr0 + r;
+      const bool ok = pr >= 0 && pr < ptab_rows;
+      const int slot = ((pr % PRING) + PRING) % PRING;
+      cp_async16(smem_u32(&sm.p[slot * LD + c * 8]), ptab + (size_t)(ok ? pr : 0) * d + head * DK + c * 8, ok);
+    }
+  };
+
+  // ---- prologue: first positional window + first K/V tile in flight
+  load_p(rb0, PW);
+  load_kv(0, 0);
+  cp_async_commit();
+
+  // ---- Q fragments (q + u, q + v) straight from global into registers
+  uint32_t qu[DK / 16][4], qv[DK / 16][4];
+  {
+    const int r0 = iw + g, r1 = iw + g + 8;
+    const H* src0 = qkv + (size_t)(off + (r0 < T ? r0 : 0)) * ld3 + head * DK;
+    const H* src1 = qkv + (size_t)(off + (r1 < T ? r1 : 0)) * ld3 + head * DK;
 #pragma unroll
-        for (int e = 0; e < 8; ++e) qf[e] = from_h(hv[e]);
-      } else {
+    for (int kk = 0; kk < DK / 16; ++kk) {
 #pragma unroll
-        for (int e = 0; e < 8; ++e) qf[e] = 0.f;
+      for (int hh = 0; hh < 4; ++hh) {
+        // a0: (g, 2t), a1: (g+8, 2t), a2: (g, 2t+8), a3: (g+8, 2t+8)
+        const int col = kk * 16 + 2 * t4 + ((hh >> 1) ? 8 : 0);
+        const bool hi_row = hh & 1;
+        const H* src = hi_row ? src1 : src0;
+        const bool ok = (hi_row ? r1 : r0) < T;
+        float x0 = 0.f, x1 = 0.f;
+        if (ok) {
+          x0 = from_h(src[col]);
+          x1 = from_h(src[col + 1]);
+        }
+        const float* bu = bias_u + head * DK + col;
+        const float* bv = bias_v + head * DK + col;
+        qu[kk][hh] = pack2<H>(x0 + bu[0], x1 + bu[1]);
+        qv[kk][hh] = pack2<H>(x0 + bv[0], x1 + bv[1]);
       }
-      H ou[8], ov[8];
-#pragma unroll
-      for (int e = 0; e < 8; ++e) {
-        ou[e] = to_h<H>(qf[e] + bias_u[head * DK + c * 8 + e]);
-        ov[e] = to_h<H>(qf[e] + bias_v[head * DK + c * 8 + e]);
-      }
-      *reinterpret_cast<uint4*>(&sm.qu[r * LD + c * 8]) = *reinterpret_cast<uint4*>(ou);
-      *reinterpret_cast<uint4*>(&sm.qv[r * LD + c * 8]) = *reinterpret_cast<uint4*>(ov);
     }
   }
 
@@ -133,63 +170,38 @@ __global__ void __launch_bounds__(NTHREADS)
   for (int i = 0; i < DK / 8; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
   float mrow[2] = {-INFINITY, -INFINITY};
   float lrow[2] = {0.f, 0.f};
+  const uint32_t p_base = smem_u32(sm.p);
 
-  const int iw = q0 + warp * 16;  // first query row of this warp
-  const uint32_t qu_base = smem_u32(sm.qu), qv_base = smem_u32(sm.qv);
-  const uint32_t k_base = smem_u32(sm.k), v_base = smem_u32(sm.v), p_base = smem_u32(sm.p);
-
-  for (int j0 = 0; j0 < T; j0 += KT) {
-    __syncthreads();  // previous iteration's readers are done with k/v/p/bd
-    {
-      constexpr int CH = DK / 8;
-      for (int i = threadIdx.x; i < KT * CH; i += NTHREADS) {
-        const int r = i / CH, c = i % CH;
-        const int kj = j0 + r;
-        uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
-        if (kj < T) {
-          const H* base = qkv + (size_t)(off + kj) * ld3 + head * DK + c * 8;
-          kv = *reinterpret_cast<const uint4*>(base + d);
-          vv = *reinterpret_cast<const uint4*>(base + 2 * d);
-        }
-        *reinterpret_cast<uint4*>(&sm.k[r * LD + c * 8]) = kv;
-        *reinterpret_cast<uint4*>(&sm.v[r * LD + c * 8]) = vv;
-      }
-      // positional window: block rows rb .. rb+PWR-1 with rb = centre-1-(q0+QT-1)+j0
-      const int rb = centre - 1 - (q0 + QT - 1) + j0;
-      for (int i = threadIdx.x; i < PWR * CH; i += NTHREADS) {
-        const int r = i / CH, c = i % CH;
-        const int pr = rb + r;
-        uint4 pv = make_uint4(0, 0, 0, 0);
-        if (r < PW && pr >= 0 && pr < ptab_rows)
-          pv = *reinterpret_cast<const uint4*>(ptab + (size_t)pr * d + head * DK + c * 8);
-        *reinterpret_cast<uint4*>(&sm.p[r * LD + c * 8]) = pv;
-      }
+  int stage = 0;
+  for (int j0 = 0; j0 < T; j0 += KT, stage ^= 1) {
+    // prefetch the next key tile and the positional rows it adds to the window
+    if (j0 + KT < T) {
+      load_kv(stage ^ 1, j0 + KT);
+      load_p(rb0 + j0 + PW, KT);
     }
+    cp_async_commit();
+    cp_async_wait<1>();
     __syncthreads();
 
-    // ---- skewed positional scores: BD[16][48] = Qv(16 x DK) * Pwin(48 x DK)^T
-    // warp window rows start at cw = (QT-16) - 16*warp (see header comment)
-    const int cw = (QT - 16) - 16 * warp;
+    const uint32_t k_base = smem_u32(sm.k[stage]), v_base = smem_u32(sm.v[stage]);
+    // ---- skewed positional scores: BD[16][48] = Qv * Pwin^T. The warp's window
+    // starts at absolute row rw = rb0 + j0 + (QT-16) - 16*warp.
+    const int rw = rb0 + j0 + (QT - 16) - 16 * warp;
     {
       float bdacc[WPWR / 8][4];
 #pragma unroll
       for (int n = 0; n < WPWR / 8; ++n) bdacc[n][0] = bdacc[n][1] = bdacc[n][2] = bdacc[n][3] = 0.f;
 #pragma unroll
-      for (int kk = 0; kk < DK / 16; ++kk) {
-        uint32_t a[4];
-        {
-          const int row = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-          const int col = kk * 16 + (lane >> 4) * 8;
-          ldsm_x4(qv_base + (uint32_t)((row * LD + col) * 2), a[0], a[1], a[2], a[3]);
-        }
+      for (int n = 0; n < WPWR / 16; ++n) {
+        const int prow = rw + n * 16 + (lane & 7) + (lane >> 4) * 8;
+        const int slot = ((prow % PRING) + PRING) % PRING;
 #pragma unroll
-        for (int n = 0; n < WPWR / 16; ++n) {
+        for (int kk = 0; kk < DK / 16; ++kk) {
           uint32_t b0, b1, b2, b3;
-          const int prow = cw + n * 16 + (lane & 7) + (lane >> 4) * 8;
           const int col = kk * 16 + ((lane >> 3) & 1) * 8;
-          ldsm_x4(p_base + (uint32_t)((prow * LD + col) * 2), b0, b1, b2, b3);
-          mma16816<H>(bdacc[2 * n], a, b0, b1);
-          mma16816<H>(bdacc[2 * n + 1], a, b2, b3);
+          ldsm_x4(p_base + (uint32_t)((slot * LD + col) * 2), b0, b1, b2, b3);
+          mma16816<H>(bdacc[2 * n], qv[kk], b0, b1);
+          mma16816<H>(bdacc[2 * n + 1], qv[kk], b2, b3);
         }
       }
 #pragma unroll
@@ -202,31 +214,24 @@ __global__ void __launch_bounds__(NTHREADS)
     }
     __syncwarp();
 
-    // ---- content scores: S[16][32] = Qu * K^T, plus the shifted positional term
+    // ---- content scores S[16][KT] = Qu * K^T plus the shifted positional term
     float s[KT / 8][4];
 #pragma unroll
     for (int n = 0; n < KT / 8; ++n) s[n][0] = s[n][1] = s[n][2] = s[n][3] = 0.f;
 #pragma unroll
-    for (int kk = 0; kk < DK / 16; ++kk) {
-      uint32_t a[4];
-      {
-        const int row = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-        const int col = kk * 16 + (lane >> 4) * 8;
-        ldsm_x4(qu_base + (uint32_t)((row * LD + col) * 2), a[0], a[1], a[2], a[3]);
-      }
+    for (int n = 0; n < KT / 16; ++n) {
+      const int krow = n * 16 + (lane & 7) + (lane >> 4) * 8;
 #pragma unroll
-      for (int n = 0; n < KT / 16; ++n) {
+      for (int kk = 0; kk < DK / 16; ++kk) {
         uint32_t b0, b1, b2, b3;
-        const int krow = n * 16 + (lane & 7) + (lane >> 4) * 8;
         const int col = kk * 16 + ((lane >> 3) & 1) * 8;
         ldsm_x4(k_base + (uint32_t)((krow * LD + col) * 2), b0, b1, b2, b3);
-        mma16816<H>(s[2 * n], a, b0, b1);
-        mma16816<H>(s[2 * n + 1], a, b2, b3);
+        mma16816<H>(s[2 * n], qu[kk], b0, b1);
+        mma16816<H>(s[2 * n + 1], qu[kk], b2, b3);
       }
     }
-    // positional term: local row ri (0..15), local key cj (0..31):
-    // P row r = centre-1-(iw+ri)+(j0+cj); warp window starts at
-    // r_w = centre-1-(iw+15)+j0, so column = r - r_w = 15 - ri + cj.
+    // local row ri, local key cj: positional row centre-1-(iw+ri)+(j0+cj), i.e.
+    // window column 15 - ri + cj
     float mnew[2];
 #pragma unroll
     for (int hr = 0; hr < 2; ++hr) {
@@ -247,7 +252,6 @@ __global__ void __launch_bounds__(NTHREADS)
       mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
       mnew[hr] = mx;
     }
-    // online softmax (base-2 exponent; scale_log2 = log2(e)/sqrt(dk))
     float alpha[2];
 #pragma unroll
     for (int hr = 0; hr < 2; ++hr) {
@@ -290,7 +294,9 @@ __global__ void __launch_bounds__(NTHREADS)
         mma16816<H>(o[2 * n + 1], a, b2, b3);
       }
     }
+    __syncthreads();  // all warps done with this stage before it is refilled
   }
+  cp_async_wait<0>();
 
   // ---- normalise and store this warp's 16 rows
 #pragma unroll

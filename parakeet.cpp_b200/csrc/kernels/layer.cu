@@ -51,8 +51,12 @@ __global__ void __launch_bounds__(256)
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
       const int c = (i * 32 + lane) * 4;
-#pragma unroll
-      for (int e = 0; e < 4; ++e) v[4 * i + e] = v[4 * i + e] * scale * gg[c + e] + bb[c + e];
+      const float4 g4 = *reinterpret_cast<const float4*>(gg + c);
+      const float4 b4 = *reinterpret_cast<const float4*>(bb + c);
+      v[4 * i] = v[4 * i] * scale * g4.x + b4.x;
+      v[4 * i + 1] = v[4 * i + 1] * scale * g4.y + b4.y;
+      v[4 * i + 2] = v[4 * i + 2] * scale * g4.z + b4.z;
+      v[4 * i + 3] = v[4 * i + 3] * scale * g4.w + b4.w;
     }
   };
   norm(g, b);
@@ -91,9 +95,10 @@ __global__ void k_pos_table(H* out, int centre, int d) {
 }
 
 // One CTA = DW_FRAMES consecutive frames of one utterance x all d channels;
-// one thread = 8 channels (16-byte loads), its K taps held in registers and
-// reused across the CTA's frames. grid (ceil(max_len / DW_FRAMES), B)
-constexpr int DW_FRAMES = 16;
+// one thread = 8 channels (16-byte loads): the DW_FRAMES + K - 1 input rows it
+// needs are loaded once into registers (zeros outside the utterance), the K
+// taps are held in registers. grid (ceil(max_len / DW_FRAMES), B)
+constexpr int DW_FRAMES = 4;
 
 template <typename H, int K>
 __global__ void __launch_bounds__(128)
@@ -106,47 +111,53 @@ __global__ void __launch_bounds__(128)
   const int t0 = blockIdx.x * DW_FRAMES;
   if (t0 >= T) return;
   constexpr int pad = (K - 1) / 2;
+  constexpr int NR = DW_FRAMES + K - 1;
   const H* x = in + (size_t)item_off[b] * d;
   H* y = out + (size_t)item_off[b] * d;
   for (int c0 = threadIdx.x * 8; c0 < d; c0 += blockDim.x * 8) {
-    float wk[K][8];
+    uint4 rows[NR];
+#pragma unroll
+    for (int r = 0; r < NR; ++r) {
+      const int ti = t0 - pad + r;
+      rows[r] = (ti >= 0 && ti < T) ? *reinterpret_cast<const uint4*>(x + (size_t)ti * d + c0)
+                                    : make_uint4(0, 0, 0, 0);
+    }
+    float acc[DW_FRAMES][8];
+#pragma unroll
+    for (int f = 0; f < DW_FRAMES; ++f)
+#pragma unroll
+      for (int c = 0; c < 8; ++c) acc[f][c] = 0.f;
 #pragma unroll
     for (int k = 0; k < K; ++k) {
-      const float4 a = *reinterpret_cast<const float4*>(w + (size_t)k * d + c0);
-      const float4 c = *reinterpret_cast<const float4*>(w + (size_t)k * d + c0 + 4);
-      wk[k][0] = a.x; wk[k][1] = a.y; wk[k][2] = a.z; wk[k][3] = a.w;
-      wk[k][4] = c.x; wk[k][5] = c.y; wk[k][6] = c.z; wk[k][7] = c.w;
-    }
-    float bi[8], sc[8], sh[8];
+      const float4 wa = *reinterpret_cast<const float4*>(w + (size_t)k * d + c0);
+      const float4 wb = *reinterpret_cast<const float4*>(w + (size_t)k * d + c0 + 4);
+      const float wk[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
 #pragma unroll
-    for (int c = 0; c < 8; ++c) {
-      bi[c] = bias ? bias[c0 + c] : 0.f;
-      sc[c] = scale[c0 + c];
-      sh[c] = shift[c0 + c];
-    }
-    const int t1 = min(t0 + DW_FRAMES, T);
-    for (int t = t0; t < t1; ++t) {
-      float acc[8];
+      for (int f = 0; f < DW_FRAMES; ++f) {
+        const H* hv = reinterpret_cast<const H*>(&rows[f + k]);
 #pragma unroll
-      for (int c = 0; c < 8; ++c) acc[c] = 0.f;
-#pragma unroll
-      for (int k = 0; k < K; ++k) {
-        const int ti = t + k - pad;
-        if (ti < 0 || ti >= T) continue;
-        const uint4 raw = *reinterpret_cast<const uint4*>(x + (size_t)ti * d + c0);
-        const H* hv = reinterpret_cast<const H*>(&raw);
-#pragma unroll
-        for (int c = 0; c < 8; ++c) acc[c] = fmaf(wk[k][c], from_h(hv[c]), acc[c]);
+        for (int c = 0; c < 8; ++c) acc[f][c] = fmaf(wk[c], from_h(hv[c]), acc[f][c]);
       }
+    }
+    const float4 s0 = *reinterpret_cast<const float4*>(scale + c0), s1 = *reinterpret_cast<const float4*>(scale + c0 + 4);
+    const float4 h0 = *reinterpret_cast<const float4*>(shift + c0), h1 = *reinterpret_cast<const float4*>(shift + c0 + 4);
+    const float sc[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+    const float sh[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+    float bi[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) bi[c] = bias ? bias[c0 + c] : 0.f;
+#pragma unroll
+    for (int f = 0; f < DW_FRAMES; ++f) {
+      if (t0 + f >= T) break;
       float r[8];
 #pragma unroll
-      for (int c = 0; c < 8; ++c) r[c] = siluf_((acc[c] + bi[c]) * sc[c] + sh[c]);
+      for (int c = 0; c < 8; ++c) r[c] = siluf_((acc[f][c] + bi[c]) * sc[c] + sh[c]);
       uint4 o;
       o.x = pack2<H>(r[0], r[1]);
       o.y = pack2<H>(r[2], r[3]);
       o.z = pack2<H>(r[4], r[5]);
       o.w = pack2<H>(r[6], r[7]);
-      *reinterpret_cast<uint4*>(y + (size_t)t * d + c0) = o;
+      *reinterpret_cast<uint4*>(y + (size_t)(t0 + f) * d + c0) = o;
     }
   }
 }

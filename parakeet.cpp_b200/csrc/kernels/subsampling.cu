@@ -78,23 +78,28 @@ __global__ void __launch_bounds__(256)
   const int tt = (int)(pos / F_out);
   const int vi = in_valid[b];
   const __nv_bfloat16* x = in + (size_t)in_off[b] * F_in * C;
-  float acc[8];
-#pragma unroll
-  for (int c = 0; c < 8; ++c) acc[c] = bias[c0 + c];
+  uint4 raw[9];
 #pragma unroll
   for (int kh = 0; kh < 3; ++kh) {
     const int ti = 2 * tt - 1 + kh;
-    if (ti < 0 || ti >= vi) continue;
 #pragma unroll
     for (int kw = 0; kw < 3; ++kw) {
       const int fi = 2 * f - 1 + kw;
-      if (fi < 0 || fi >= F_in) continue;
-      const uint4 raw = *reinterpret_cast<const uint4*>(x + ((size_t)ti * F_in + fi) * C + c0);
-      const __nv_bfloat16* hv = reinterpret_cast<const __nv_bfloat16*>(&raw);
-      const float* wk = w + (kh * 3 + kw) * C + c0;
-#pragma unroll
-      for (int c = 0; c < 8; ++c) acc[c] = fmaf(wk[c], __bfloat162float(hv[c]), acc[c]);
+      raw[kh * 3 + kw] = (ti >= 0 && ti < vi && fi >= 0 && fi < F_in)
+                             ? *reinterpret_cast<const uint4*>(x + ((size_t)ti * F_in + fi) * C + c0)
+                             : make_uint4(0, 0, 0, 0);
     }
+  }
+  const float4 b0 = *reinterpret_cast<const float4*>(bias + c0), b1 = *reinterpret_cast<const float4*>(bias + c0 + 4);
+  float acc[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
+#pragma unroll
+  for (int k = 0; k < 9; ++k) {
+    const float4 wa = *reinterpret_cast<const float4*>(w + k * C + c0);
+    const float4 wb = *reinterpret_cast<const float4*>(w + k * C + c0 + 4);
+    const float wk[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+    const __nv_bfloat16* hv = reinterpret_cast<const __nv_bfloat16*>(&raw[k]);
+#pragma unroll
+    for (int c = 0; c < 8; ++c) acc[c] = fmaf(wk[c], __bfloat162float(hv[c]), acc[c]);
   }
   uint4 o;
   o.x = pack2<__nv_bfloat16>(acc[0], acc[1]);

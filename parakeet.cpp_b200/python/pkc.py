@@ -98,6 +98,8 @@ def _declare(L):
         ("pkc_model_stream", c_void_p, c_void_p, c_int),
         ("pkc_profile_read", c_int, c_void_p, POINTER(KernelStat), c_int),
         ("pkc_shard_plan", c_int, POINTER(c_int), c_int, c_int, c_int, POINTER(c_int)),
+        ("pkc_relpos_attention", c_int, c_void_p, c_void_p, c_int, c_void_p, c_void_p, POINTER(c_int),
+         c_int, c_int, c_int, c_int, c_void_p, c_void_p),
     ]
     for name, res, *args in optional:
         if hasattr(L, name):
@@ -121,6 +123,13 @@ def gemm(A, B, M, N, K, *, bf16, epi, act=ACT_NONE, alpha=1.0, bias=None, out, l
     _check(lib().pkc_gemm(c_void_p(A), lda or K, c_void_p(B), ldb or K, M, N, K, 1 if bf16 else 0,
                           epi, act, alpha, c_void_p(bias) if bias else None, c_void_p(out), ldo,
                           c_void_p(stream) if stream else None))
+
+
+def relpos_attention(qkv, ptab, centre, bias_u, bias_v, lens, d, n_heads, *, bf16, ctx, stream=0):
+    """Rel-pos attention kernel on packed rows (device pointers as ints)."""
+    _check(lib().pkc_relpos_attention(c_void_p(qkv), c_void_p(ptab), centre, c_void_p(bias_u),
+                                      c_void_p(bias_v), _ints(lens), len(lens), d, n_heads,
+                                      1 if bf16 else 0, c_void_p(ctx), c_void_p(stream) if stream else None))
 
 
 def shard_plan(n_samples, n_dev, hop=160):
