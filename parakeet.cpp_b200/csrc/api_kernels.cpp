@@ -90,7 +90,7 @@ extern "C" pkc_status pkc_relpos_attention(const void* qkv, const void* ptab, in
   if (cudaMalloc(&dtab, host.size() * sizeof(int)) != cudaSuccess)
     return pkc::set_thread_error(PKC_ERR_OOM, "pkc_relpos_attention: table allocation failed");
   cudaMemcpyAsync(dtab, host.data(), host.size() * sizeof(int), cudaMemcpyHostToDevice, st);
-  pkc::AttnArgs a{qkv, ptab, 2 * centre - 1, centre, bias_u, bias_v, dtab + 2 * B + 1,
+  pkc::AttnArgs a{qkv, ptab, 2 * centre - 1, centre, d, bias_u, bias_v, dtab + 2 * B + 1,
                   (int)tiles.size() / 2, dtab, dtab + B + 1, ctx, d, n_heads};
   cudaError_t e = pkc::attention_launch(a, dtype == 1, st);
   cudaError_t e2 = cudaStreamSynchronize(st);

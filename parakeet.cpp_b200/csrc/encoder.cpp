@@ -266,7 +266,7 @@ pkc_status DeviceRunner::prepare(const Plan& p, cudaStream_t st, std::string& er
   const size_t o_qkv = take((size_t)p.M * 3 * d * hs);
   const size_t o_ctx = take((size_t)p.M * d * hs);
   const size_t o_pe = take((size_t)np * d * hs);
-  const size_t o_pt = take((size_t)np * d * hs);
+  const size_t o_pt = take((size_t)np * d * c.n_layers * hs);
   const size_t o_out = take((size_t)p.M * d * 4);
   if (!ensure_ws(sz)) {
     err = "workspace allocation of " + std::to_string(sz) + " bytes failed";
@@ -371,6 +371,12 @@ pkc_status DeviceRunner::run_encoder(const Plan& p, cudaStream_t st, std::string
   PKC_CK(pos_table_launch(b_.pe, p.centre, d, bf, st), "pos_table");
   prof_end(st, "pos_table", 0.0, (double)np * d * hs);
 
+  // every layer's linear_pos (no bias) in one GEMM: ptab [np, L*d], layer l at column l*d
+  const int Ld = c.n_layers * d;
+  PKC_ST(gemm(b_.pe, d, w_.pos_all_w, d, bf, np, Ld, d, EPI_STORE_H, ACT_NONE, 1.f, nullptr, b_.ptab, Ld,
+              st, "gemm_pos", err));
+
+
   const int ntiles = (int)p.attn_tiles.size() / 2;
   double attn_flops = 0.0;
   for (int b = 0; b < p.B; ++b) {
@@ -392,8 +398,8 @@ pkc_status DeviceRunner::run_encoder(const Plan& p, cudaStream_t st, std::string
     PKC_CK(layernorm_launch(b_.x, M, d, L.ln_att_g, L.ln_att_b, b_.hbuf, bf, nullptr, nullptr, false, st), "ln");
     prof_end(st, "layernorm", 0.0, (double)M * d * (4 + hs));
     PKC_ST(gemm(b_.hbuf, d, L.qkv_w, d, bf, M, 3 * d, d, EPI_STORE_H, ACT_NONE, 1.f, L.qkv_b, b_.qkv, 3 * d, st, "gemm_qkv", err));
-    PKC_ST(gemm(b_.pe, d, L.pos_w, d, bf, np, d, d, EPI_STORE_H, ACT_NONE, 1.f, nullptr, b_.ptab, d, st, "gemm_pos", err));
-    AttnArgs aa{b_.qkv, b_.ptab, np, p.centre, L.pos_u, L.pos_v, t_tiles, ntiles, t_v_off, t_v, b_.ctx, d, H};
+    AttnArgs aa{b_.qkv, static_cast<const uint8_t*>(b_.ptab) + (size_t)li * d * 2, np, p.centre, Ld,
+                L.pos_u, L.pos_v, t_tiles, ntiles, t_v_off, t_v, b_.ctx, d, H};
     prof_begin(st);
     PKC_CK(attention_launch(aa, bf, st), "attention");
     prof_end(st, "attention", attn_flops, (double)M * (3 * d + d) * hs + (double)np * d * hs);

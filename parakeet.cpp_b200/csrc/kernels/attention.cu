@@ -88,7 +88,7 @@ struct AttnSmem {
 
 template <typename H, int DK>
 __global__ void __launch_bounds__(NTHREADS, 2)
-    k_relpos_attn(const H* __restrict__ qkv, const H* __restrict__ ptab, int ptab_rows, int centre,
+    k_relpos_attn(const H* __restrict__ qkv, const H* __restrict__ ptab, int ptab_rows, int ptab_ld, int centre,
                   const float* __restrict__ bias_u, const float* __restrict__ bias_v,
                   const int* __restrict__ tiles,     // [n_tiles][2]: item, q0
                   const int* __restrict__ item_off,  // [B] first packed row of each item
@@ -128,7 +128,7 @@ __global__ void __launch_bounds__(NTHREADS, 2)
       const int pr = pr0 + r;
       const bool ok = pr >= 0 && pr < ptab_rows;
       const int slot = ((pr % PRING) + PRING) % PRING;
-      cp_async16(smem_u32(&sm.p[slot * LD + c * 8]), ptab + (size_t)(ok ? pr : 0) * d + head * DK + c * 8, ok);
+      cp_async16(smem_u32(&sm.p[slot * LD + c * 8]), ptab + (size_t)(ok ? pr : 0) * ptab_ld + head * DK + c * 8, ok);
     }
   };
 
@@ -322,7 +322,7 @@ cudaError_t launch_attn(const AttnArgs& a, cudaStream_t st) {
   dim3 grid(a.n_tiles, a.n_heads);
   const float scale_log2 = 1.4426950408889634f / sqrtf((float)DK);
   kern<<<grid, NTHREADS, smem, st>>>(reinterpret_cast<const H*>(a.qkv), reinterpret_cast<const H*>(a.ptab),
-                                     a.ptab_rows, a.centre, a.bias_u, a.bias_v, a.tiles, a.item_off,
+                                     a.ptab_rows, a.ptab_ld > 0 ? a.ptab_ld : a.d, a.centre, a.bias_u, a.bias_v, a.tiles, a.item_off,
                                      a.item_len, reinterpret_cast<H*>(a.ctx), a.d, scale_log2);
   return cudaGetLastError();
 }

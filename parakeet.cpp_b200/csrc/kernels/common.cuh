@@ -186,8 +186,11 @@ struct is_bf16 { static constexpr bool value = false; };
 template <>
 struct is_bf16<__nv_bfloat16> { static constexpr bool value = true; };
 
-__device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + __expf(-x)); }
-__device__ __forceinline__ float siluf_(float x) { return x / (1.0f + __expf(-x)); }
+// Fast-reciprocal forms (a full IEEE divide per element throttled the GEMM
+// epilogues). For x << 0, __expf(-x) overflows to +inf and the reciprocal
+// gives 0, the correct limit of both functions.
+__device__ __forceinline__ float sigmoidf_(float x) { return __fdividef(1.0f, 1.0f + __expf(-x)); }
+__device__ __forceinline__ float siluf_(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
 template <typename H>
 __device__ __forceinline__ H to_h(float x);

@@ -87,8 +87,9 @@ cudaError_t pos_table_launch(void* out, int centre, int d, bool bf16, cudaStream
 
 struct AttnArgs {
   const void* qkv;      // [M, 3d]
-  const void* ptab;     // [ptab_rows, d]
+  const void* ptab;     // [ptab_rows, ptab_ld] (this layer's d columns)
   int ptab_rows, centre;
+  int ptab_ld;          // row stride of ptab in elements (>= d)
   const float* bias_u;  // [H*dk]
   const float* bias_v;
   const int* tiles;     // [n_tiles][2] (item, q0)

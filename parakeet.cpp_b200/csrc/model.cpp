@@ -277,6 +277,8 @@ std::string upload_weights(const GgufFile& g, const Config& c, DeviceWeights& w)
 
   // ---------------- conformer layers
   w.layers.assign(c.n_layers, LayerWeights{});
+  std::vector<uint16_t> pos_all;
+  pos_all.reserve((size_t)c.n_layers * d * d);
   for (int li = 0; li < c.n_layers; ++li) {
     LayerWeights& L = w.layers[li];
     const std::string p = "encoder.layers." + std::to_string(li) + ".";
@@ -326,7 +328,8 @@ std::string upload_weights(const GgufFile& g, const Config& c, DeviceWeights& w)
       L.qkv_b = any_b ? put_f(bq) : nullptr;
     }
     if (!read_h(g, a + "linear_pos.weight", d, d, bf, h, err)) return err;
-    L.pos_w = put_h(h);
+    pos_all.insert(pos_all.end(), h.begin(), h.end());
+    L.pos_w = nullptr;
     if (!read_h(g, a + "linear_out.weight", d, d, bf, h, err)) return err;
     L.out_w = put_h(h);
     L.out_b = opt_vec(a + "linear_out.bias", d);
@@ -376,6 +379,10 @@ std::string upload_weights(const GgufFile& g, const Config& c, DeviceWeights& w)
     }
   }
 
+  w.pos_all_w = put_h(pos_all);
+  pos_all.clear();
+  pos_all.shrink_to_fit();
+
   // ---------------- upload
   void* dev = nullptr;
   if (cudaMalloc(&dev, st.buf.size()) != cudaSuccess)
@@ -392,7 +399,7 @@ std::string upload_weights(const GgufFile& g, const Config& c, DeviceWeights& w)
   reloc(w.c0_w, base); reloc(w.c0_b, base);
   reloc(w.dw1_w, base); reloc(w.dw1_b, base); reloc(w.dw2_w, base); reloc(w.dw2_b, base);
   reloc(w.pw1_w, base); reloc(w.pw2_w, base); reloc(w.pw1_b, base); reloc(w.pw2_b, base);
-  reloc(w.out_w, base); reloc(w.out_b, base);
+  reloc(w.out_w, base); reloc(w.out_b, base); reloc(w.pos_all_w, base);
   for (LayerWeights& L : w.layers) {
     float** fp[] = {&L.ln_ff1_g, &L.ln_ff1_b, &L.ln_att_g, &L.ln_att_b, &L.ln_conv_g, &L.ln_conv_b,
                     &L.ln_ff2_g, &L.ln_ff2_b, &L.ln_out_g, &L.ln_out_b, &L.ff1_b1, &L.ff1_b2,

@@ -73,6 +73,7 @@ struct DeviceWeights {
   float *pw1_b, *pw2_b;
   void* out_w;                    // bf16 [d, F3*C] (columns f*C + c)
   float* out_b;
+  void* pos_all_w = nullptr;      // [L*d, d]: every layer's linear_pos, one GEMM per batch
   std::vector<LayerWeights> layers;
 };
 
