@@ -136,6 +136,21 @@ def workload(config, rank, batch=None):
     return pcm, {"batch": b, "len_s": [lo, hi]}
 
 
+def combine_ranks(ms, e2e_ms, audio_s, wall_ms, world, device):
+    """Whole-job timing: the slowest rank's times (MAX) and every rank's audio
+    (SUM); on one rank the values pass through."""
+    if world <= 1:
+        return ms, e2e_ms, audio_s, wall_ms
+    import torch
+    import torch.distributed as dist
+    vals = torch.tensor([ms, e2e_ms, audio_s, wall_ms], dtype=torch.float64, device=device)
+    mx = vals.clone()
+    dist.all_reduce(mx, op=dist.ReduceOp.MAX)
+    tot = vals.clone()
+    dist.all_reduce(tot, op=dist.ReduceOp.SUM)
+    return mx[0].item(), mx[1].item(), tot[2].item(), mx[3].item()
+
+
 # ----------------------------------------------------------------------- ours
 
 def run_ours(args, rank, world, local_rank):
@@ -228,16 +243,7 @@ def run_ours(args, rank, world, local_rank):
     e2e_wall = time.perf_counter() - t0
     e2e_ms = e_start.elapsed_time(e_end)
 
-    vals = torch.tensor([ms, e2e_ms, audio_s, e2e_wall * 1e3], dtype=torch.float64, device=dev)
-    if world > 1:
-        mx = vals.clone()
-        dist.all_reduce(mx, op=dist.ReduceOp.MAX)
-        tot = vals.clone()
-        dist.all_reduce(tot, op=dist.ReduceOp.SUM)
-        ms_max, e2e_max, wall_max = mx[0].item(), mx[1].item(), mx[3].item()
-        audio_total = tot[2].item()
-    else:
-        ms_max, e2e_max, wall_max, audio_total = ms, e2e_ms, e2e_wall * 1e3, audio_s
+    ms_max, e2e_max, audio_total, wall_max = combine_ranks(ms, e2e_ms, audio_s, e2e_wall * 1e3, world, dev)
     model.close()
     if rank != 0:
         return None

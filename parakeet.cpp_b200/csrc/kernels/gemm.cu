@@ -77,6 +77,44 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t tro
         }
       }
     }
+  } else if constexpr (EPI == EPI_RESID_F32) {
+    // residual rows are prefetched one chunk ahead so their global latency
+    // overlaps the TMEM load and the previous chunk's arithmetic
+    float* xrow = reinterpret_cast<float*>(args.out) + (size_t)(row_ok ? row : 0) * args.ldo + n0;
+    float4 cur[8], nxt[8];
+    if (row_ok) {
+#pragma unroll
+      for (int q = 0; q < 8; ++q) cur[q] = reinterpret_cast<const float4*>(xrow)[q];
+    }
+#pragma unroll 1
+    for (int j = 0; j < BN / 32; ++j) {
+      tmem_ld32(trow + 32 * j, r);
+      if (row_ok && j + 1 < BN / 32) {
+#pragma unroll
+        for (int q = 0; q < 8; ++q) nxt[q] = reinterpret_cast<const float4*>(xrow + 32 * (j + 1))[q];
+      }
+      tmem_ld_wait();
+      if (row_ok) {
+        const int n = n0 + 32 * j;
+        float4* o4 = reinterpret_cast<float4*>(xrow + 32 * j);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+          float b0 = 0.f, b1 = 0.f, b2 = 0.f, b3 = 0.f;
+          if (args.bias) {
+            const float4 bb = reinterpret_cast<const float4*>(args.bias + n)[q];
+            b0 = bb.x; b1 = bb.y; b2 = bb.z; b3 = bb.w;
+          }
+          float4 o = cur[q];
+          o.x += args.alpha * (__uint_as_float(r[4 * q]) + b0);
+          o.y += args.alpha * (__uint_as_float(r[4 * q + 1]) + b1);
+          o.z += args.alpha * (__uint_as_float(r[4 * q + 2]) + b2);
+          o.w += args.alpha * (__uint_as_float(r[4 * q + 3]) + b3);
+          o4[q] = o;
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < 8; ++q) cur[q] = nxt[q];
+    }
   } else {
 #pragma unroll 1
     for (int j = 0; j < BN / 32; ++j) {
@@ -104,17 +142,6 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t tro
         for (int q = 0; q < 4; ++q)
           o4[q] = make_uint4(pack2<H>(v[8 * q], v[8 * q + 1]), pack2<H>(v[8 * q + 2], v[8 * q + 3]),
                              pack2<H>(v[8 * q + 4], v[8 * q + 5]), pack2<H>(v[8 * q + 6], v[8 * q + 7]));
-      } else if constexpr (EPI == EPI_RESID_F32) {
-        float4* o4 = reinterpret_cast<float4*>(reinterpret_cast<float*>(args.out) + (size_t)row * args.ldo + n);
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          float4 o = o4[q];
-          o.x += args.alpha * v[4 * q];
-          o.y += args.alpha * v[4 * q + 1];
-          o.z += args.alpha * v[4 * q + 2];
-          o.w += args.alpha * v[4 * q + 3];
-          o4[q] = o;
-        }
       } else {  // EPI_STORE_F32
         float4* o4 = reinterpret_cast<float4*>(reinterpret_cast<float*>(args.out) + (size_t)row * args.ldo + n);
 #pragma unroll

@@ -83,30 +83,31 @@ __global__ void k_mel_fb_log(FbArgs a) {
   a.logmel[(size_t)row * a.n_mels + m] = logf(acc + a.log_guard);
 }
 
-// block (32 mel bins) x (8 frame lanes); grid (ceil(F/32), B)
-__global__ void __launch_bounds__(256) k_mel_norm(float* logmel, int F, ItemTables t) {
+// block (32 mel bins) x (32 frame lanes); grid (ceil(F/32), B)
+constexpr int NORM_LANES = 32;
+__global__ void __launch_bounds__(1024) k_mel_norm(float* logmel, int F, ItemTables t) {
   const int b = blockIdx.y;
   const int m = blockIdx.x * 32 + threadIdx.x;
   const int T = t.mel_T[b];
   const int valid = min(t.mel_valid[b], T);
   float* base = logmel + (size_t)t.mel_off[b] * F;
-  __shared__ double red[8][33];
+  __shared__ double red[NORM_LANES][33];
   __shared__ double stat[2][32];
   double acc = 0.0;
   if (m < F)
-    for (int f = threadIdx.y; f < valid; f += 8) acc += (double)base[(size_t)f * F + m];
+    for (int f = threadIdx.y; f < valid; f += NORM_LANES) acc += (double)base[(size_t)f * F + m];
   red[threadIdx.y][threadIdx.x] = acc;
   __syncthreads();
   if (threadIdx.y == 0) {
     double s = 0.0;
-    for (int k = 0; k < 8; ++k) s += red[k][threadIdx.x];
+    for (int k = 0; k < NORM_LANES; ++k) s += red[k][threadIdx.x];
     stat[0][threadIdx.x] = valid > 0 ? s / (double)valid : 0.0;
   }
   __syncthreads();
   const double mean = stat[0][threadIdx.x];
   acc = 0.0;
   if (m < F)
-    for (int f = threadIdx.y; f < valid; f += 8) {
+    for (int f = threadIdx.y; f < valid; f += NORM_LANES) {
       const double dlt = (double)base[(size_t)f * F + m] - mean;
       acc += dlt * dlt;
     }
@@ -114,14 +115,14 @@ __global__ void __launch_bounds__(256) k_mel_norm(float* logmel, int F, ItemTabl
   __syncthreads();
   if (threadIdx.y == 0) {
     double s = 0.0;
-    for (int k = 0; k < 8; ++k) s += red[k][threadIdx.x];
+    for (int k = 0; k < NORM_LANES; ++k) s += red[k][threadIdx.x];
     const double var = valid > 1 ? s / (double)(valid - 1) : 0.0;
     stat[1][threadIdx.x] = sqrt(var) + 1e-5;
   }
   __syncthreads();
   const double sd = stat[1][threadIdx.x];
   if (m < F)
-    for (int f = threadIdx.y; f < T; f += 8) {
+    for (int f = threadIdx.y; f < T; f += NORM_LANES) {
       float* p = base + (size_t)f * F + m;
       *p = f < valid ? (float)(((double)*p - mean) / sd) : 0.0f;
     }
@@ -161,7 +162,7 @@ cudaError_t mel_fb_log_launch(const FbArgs& a, cudaStream_t st) {
 
 cudaError_t mel_norm_launch(float* logmel, int n_mels, const ItemTables& t, cudaStream_t st) {
   if (t.B <= 0) return cudaSuccess;
-  k_mel_norm<<<dim3((n_mels + 31) / 32, t.B), dim3(32, 8), 0, st>>>(logmel, n_mels, t);
+  k_mel_norm<<<dim3((n_mels + 31) / 32, t.B), dim3(32, NORM_LANES), 0, st>>>(logmel, n_mels, t);
   return cudaGetLastError();
 }
 
