@@ -167,6 +167,20 @@ pkc_status pkc_relpos_attention(const void* qkv, const void* ptab, int centre,
                                 const float* bias_u, const float* bias_v, const int* lens, int B,
                                 int d, int n_heads, int dtype, void* ctx, void* stream);
 
+/* The same attention as pkc_relpos_attention, for callers that may not
+   allocate device memory: hosts whose own allocator owns all of HBM (a serving
+   runtime that reserves memory up front, or one whose accounting must see
+   every byte), where a cudaMalloc is refused or stalls the whole device. No
+   counterpart in the reference. Its small tables live in one fixed 80 KiB
+   device array that the library holds on each GPU until exit. Limits: at most
+   1024 utterances and the query tiles of about 10000 x 64 frames per call;
+   larger calls fail with PKC_ERR_ARG. The first call on a device looks up the
+   array's address. Calls that overlap on the GPU race on the shared array. */
+pkc_status pkc_relpos_attention_noalloc(const void* qkv, const void* ptab, int centre,
+                                        const float* bias_u, const float* bias_v, const int* lens,
+                                        int B, int d, int n_heads, int dtype, void* ctx,
+                                        void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -100,6 +100,8 @@ def _declare(L):
         ("pkc_shard_plan", c_int, POINTER(c_int), c_int, c_int, c_int, POINTER(c_int)),
         ("pkc_relpos_attention", c_int, c_void_p, c_void_p, c_int, c_void_p, c_void_p, POINTER(c_int),
          c_int, c_int, c_int, c_int, c_void_p, c_void_p),
+        ("pkc_relpos_attention_noalloc", c_int, c_void_p, c_void_p, c_int, c_void_p, c_void_p,
+         POINTER(c_int), c_int, c_int, c_int, c_int, c_void_p, c_void_p),
     ]
     for name, res, *args in optional:
         if hasattr(L, name):
@@ -130,6 +132,16 @@ def relpos_attention(qkv, ptab, centre, bias_u, bias_v, lens, d, n_heads, *, bf1
     _check(lib().pkc_relpos_attention(c_void_p(qkv), c_void_p(ptab), centre, c_void_p(bias_u),
                                       c_void_p(bias_v), _ints(lens), len(lens), d, n_heads,
                                       1 if bf16 else 0, c_void_p(ctx), c_void_p(stream) if stream else None))
+
+
+def relpos_attention_noalloc(qkv, ptab, centre, bias_u, bias_v, lens, d, n_heads, *, bf16, ctx,
+                             stream=0):
+    """The attention entry point that allocates no device memory (fixed
+    tables inside the library); same arguments as relpos_attention."""
+    _check(lib().pkc_relpos_attention_noalloc(c_void_p(qkv), c_void_p(ptab), centre, c_void_p(bias_u),
+                                              c_void_p(bias_v), _ints(lens), len(lens), d, n_heads,
+                                              1 if bf16 else 0, c_void_p(ctx),
+                                              c_void_p(stream) if stream else None))
 
 
 def shard_plan(n_samples, n_dev, hop=160):
