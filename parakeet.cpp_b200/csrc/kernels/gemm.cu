@@ -10,6 +10,8 @@
 // Two 256-column f32 accumulators in TMEM (all 512 columns): the epilogue of
 // tile i runs while the MMAs of tile i+1 fill the other accumulator.
 //
+#include <cstdlib>
+
 #include "common.cuh"
 #include "gemm.h"
 
@@ -277,6 +279,158 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 0) tmem_dealloc(tmem, TMEM_COLS);
 }
 
+
+// ============================================================================
+// 2-SM variant: a cluster of two CTAs computes a 256 x 256 tile with
+// tcgen05.mma.cta_group::2 (M = 256). Each CTA stages its own 128 rows of A
+// and 128 rows (half of N) of B per k-block, so a CTA moves 32 KB per 4 MFLOP
+// of its share instead of 48 KB (the 1-SM tile's per-SM load bandwidth and
+// shared-memory traffic were the limit), and the ring is 6 stages deep.
+//   * both CTAs' producers load into their own smem; the transaction bytes of
+//     both complete on the leader's (rank 0) full barrier, which the leader's
+//     producer arms for 2 x 32 KB
+//   * the leader's single MMA thread issues the M = 256 MMAs and commits with
+//     a cluster multicast to both CTAs' empty / accumulator-full barriers
+//   * each CTA's 4 epilogue warps drain its own TMEM (its 128 rows x 256
+//     columns) and arrive on the leader's accumulator-empty barrier
+// TMA loads are plain (no cluster multicast).
+constexpr int STAGES2 = 6;
+constexpr int HALF_ROWS = 128;
+constexpr int A2_BYTES = HALF_ROWS * BK * 2;
+constexpr int B2_BYTES = HALF_ROWS * BK * 2;
+constexpr int SMEM2_BYTES = STAGES2 * (A2_BYTES + B2_BYTES) + 512 + 1024;
+
+template <typename H, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
+    k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+               GemmArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem =
+      reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + STAGES2 * A2_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES2 * B2_BYTES);
+  // bars: [0,S) full, [S,2S) empty, 2S+{0,1} accumulator full, 2S+{2,3} accumulator empty
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES2 + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1;
+  const int npairs = gridDim.x >> 1;
+  const int KB = args.K / BK;
+  const int tiles_m = (args.M + 2 * HALF_ROWS - 1) / (2 * HALF_ROWS);
+  const int n_tiles = tiles_m * (args.N / BN);
+
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmB);
+    for (int s = 0; s < 2 * STAGES2; ++s) mbar_init(smem_u32(&bars[s]), 1);
+    mbar_init(smem_u32(&bars[2 * STAGES2 + 0]), 1);
+    mbar_init(smem_u32(&bars[2 * STAGES2 + 1]), 1);
+    mbar_init(smem_u32(&bars[2 * STAGES2 + 2]), 2 * EPI_WARPS);
+    mbar_init(smem_u32(&bars[2 * STAGES2 + 3]), 2 * EPI_WARPS);
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 0) {
+    tmem_alloc_2sm(smem_u32(tmem_slot), TMEM_COLS);
+    tmem_relinquish_2sm();
+  }
+  tc_fence_before();
+  cluster_sync();  // barrier init + TMEM alloc of both CTAs visible cluster-wide
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---- TMA producer (both CTAs)
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = pair; tile < n_tiles && ok; tile += npairs) {
+        const int m0 = (tile % tiles_m) * 2 * HALF_ROWS + (int)rank * HALF_ROWS;
+        const int n0 = (tile / tiles_m) * BN + (int)rank * HALF_ROWS;
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const int s = it % STAGES2;
+          const uint32_t ph = (it / STAGES2) & 1u;
+          if (!mbar_wait(smem_u32(&bars[STAGES2 + s]), ph ^ 1u, args.err, DEV_ERR_TIMEOUT_EMPTY)) {
+            ok = false;
+            break;
+          }
+          const uint32_t full_leader = mapa_shared(smem_u32(&bars[s]), 0);
+          if (leader) mbar_arrive_expect_tx(smem_u32(&bars[s]), 2 * (A2_BYTES + B2_BYTES));
+          tma_load_2d_2sm(smem_u32(sA + s * A2_BYTES), &tmA, full_leader, kb * BK, m0);
+          tma_load_2d_2sm(smem_u32(sB + s * B2_BYTES), &tmB, full_leader, kb * BK, n0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ---- MMA issuer (leader CTA only)
+      constexpr uint32_t idesc = idesc_f16(2 * HALF_ROWS, BN, is_bf16<H>::value ? 1 : 0);
+      uint32_t it = 0;
+      int local = 0;
+      bool ok = true;
+      for (int tile = pair; tile < n_tiles && ok; tile += npairs, ++local) {
+        const int buf = local & 1;
+        const uint32_t use = (uint32_t)(local >> 1);
+        if (!mbar_wait(smem_u32(&bars[2 * STAGES2 + 2 + buf]), (use & 1u) ^ 1u, args.err,
+                       DEV_ERR_TIMEOUT_ACCUM))
+          break;
+        tc_fence_after();
+        const uint32_t acc = tmem + (uint32_t)(buf * BN);
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const int s = it % STAGES2;
+          const uint32_t ph = (it / STAGES2) & 1u;
+          if (!mbar_wait(smem_u32(&bars[s]), ph, args.err, DEV_ERR_TIMEOUT_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = smem_desc_sw128(smem_u32(sA + s * A2_BYTES));
+          const uint64_t db = smem_desc_sw128(smem_u32(sB + s * B2_BYTES));
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            umma_f16_2sm(acc, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc,
+                         (kb > 0 || k > 0) ? 1u : 0u);
+          umma_commit_2sm_mc(smem_u32(&bars[STAGES2 + s]), 0x3);  // frees the stage in both CTAs
+        }
+        if (ok) umma_commit_2sm_mc(smem_u32(&bars[2 * STAGES2 + buf]), 0x3);  // accumulators ready
+      }
+    }
+  } else {
+    // ---- epilogue warps 2..5 (both CTAs): this CTA's 128 rows of the tile
+    const int q = warp & 3;
+    const uint32_t acce_leader0 = mapa_shared(smem_u32(&bars[2 * STAGES2 + 2]), 0);
+    const uint32_t acce_leader1 = mapa_shared(smem_u32(&bars[2 * STAGES2 + 3]), 0);
+    int local = 0;
+    for (int tile = pair; tile < n_tiles; tile += npairs, ++local) {
+      const int buf = local & 1;
+      const uint32_t use = (uint32_t)(local >> 1);
+      const bool have =
+          __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars[2 * STAGES2 + buf]), use & 1u, args.err,
+                                            DEV_ERR_TIMEOUT_ACCUM) ? 1 : 0) != 0;
+      if (!have) break;
+      tc_fence_after();
+      const int m0 = (tile % tiles_m) * 2 * HALF_ROWS + (int)rank * HALF_ROWS;
+      const int n0 = (tile / tiles_m) * BN;
+      const int row = m0 + q * 32 + lane;
+      const bool row_ok = row < args.M;
+      const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
+      epilogue_tile<H, EPI>(args, trow, row, row_ok, n0);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(buf ? acce_leader1 : acce_leader0);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no CTA leaves while its peer may still signal its barriers
+  if (warp == 0) tmem_dealloc_2sm(tmem, TMEM_COLS);
+}
+
 }  // namespace
 
 // ------------------------------------------------------------------ host side
@@ -309,6 +463,42 @@ bool make_tmap_kmajor(CUtensorMap* map, const void* base, int rows, int K, int l
 }
 
 template <typename H, int EPI>
+static cudaError_t launch_t2(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
+                             cudaStream_t st) {
+  auto kern = k_gemm_tc2<H, EPI>;
+  static bool attr_set[64] = {};
+  static int max_pairs[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2, 1, 1);
+    cfg.blockDim = dim3(THREADS, 1, 1);
+    cfg.dynamicSmemBytes = SMEM2_BYTES;
+    cudaLaunchAttribute at;
+    at.id = cudaLaunchAttributeClusterDimension;
+    at.val.clusterDim.x = 2; at.val.clusterDim.y = 1; at.val.clusterDim.z = 1;
+    cfg.attrs = &at;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      int sms = 0;
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      n = sms / 2;
+    }
+    max_pairs[dev & 63] = n;
+    attr_set[dev & 63] = true;
+  }
+  const int n_tiles = (a.N / BN) * ((a.M + 2 * HALF_ROWS - 1) / (2 * HALF_ROWS));
+  const int pairs = n_tiles < max_pairs[dev & 63] ? n_tiles : max_pairs[dev & 63];
+  kern<<<2 * pairs, THREADS, SMEM2_BYTES, st>>>(ta, tb, a);
+  return cudaGetLastError();
+}
+
+template <typename H, int EPI>
 static cudaError_t launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
                             cudaStream_t st) {
   auto kern = k_gemm_tc<H, EPI>;
@@ -328,6 +518,16 @@ static cudaError_t launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const 
   return cudaGetLastError();
 }
 
+// PKC_GEMM_1SM=1 forces the 1-SM kernel (for A/B comparisons)
+bool gemm_2sm_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("PKC_GEMM_1SM");
+    v = (e && e[0] == '1') ? 0 : 1;
+  }
+  return v == 1;
+}
+
 int gemm_tile_n() { return BN; }
 int gemm_tile_k() { return BK; }
 int gemm_tile_m() { return BM; }
@@ -339,12 +539,17 @@ cudaError_t gemm_launch(const void* A, int lda, const void* B, int ldb, bool bf1
       (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15) ||
       (args.ldo % 8) != 0)
     return cudaErrorInvalidValue;
+  // 2-SM tiles once there are at least two 128-row blocks of A
+  const bool two_sm = args.M > BM && gemm_2sm_enabled();
+  const int box = two_sm ? HALF_ROWS : 0;
   CUtensorMap ta, tb;
-  if (!make_tmap_kmajor(&ta, A, args.M, args.K, lda, BM, bf16)) return cudaErrorInvalidValue;
-  if (!make_tmap_kmajor(&tb, B, args.N, args.K, ldb, BN, bf16)) return cudaErrorInvalidValue;
+  if (!make_tmap_kmajor(&ta, A, args.M, args.K, lda, two_sm ? box : BM, bf16)) return cudaErrorInvalidValue;
+  if (!make_tmap_kmajor(&tb, B, args.N, args.K, ldb, two_sm ? box : BN, bf16)) return cudaErrorInvalidValue;
   switch (args.epi) {
 #define PKC_GEMM_CASE(E)                                                                   \
   case E:                                                                                  \
+    if (two_sm)                                                                            \
+      return bf16 ? launch_t2<__nv_bfloat16, E>(ta, tb, args, st) : launch_t2<__half, E>(ta, tb, args, st); \
     return bf16 ? launch_t<__nv_bfloat16, E>(ta, tb, args, st) : launch_t<__half, E>(ta, tb, args, st);
     PKC_GEMM_CASE(EPI_STORE_H)
     PKC_GEMM_CASE(EPI_RESID_F32)

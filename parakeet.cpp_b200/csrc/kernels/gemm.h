@@ -42,6 +42,7 @@ cudaError_t gemm_launch(const void* A, int lda, const void* B, int ldb, bool bf1
                         const GemmArgs& args, cudaStream_t st);
 
 int gemm_tile_m();
+bool gemm_2sm_enabled();
 int gemm_tile_n();
 int gemm_tile_k();
 

@@ -21,7 +21,8 @@ def _setup(M, N, K, dtype, seed=0):
 
 @pytest.mark.parametrize("bf16", [False, True])
 @pytest.mark.parametrize("M,N,K", [(128, 256, 64), (300, 512, 1024), (1000, 1024, 4096), (7, 256, 128),
-                                   (20000, 1024, 256), (4099, 3072, 1024)])
+                                   (20000, 1024, 256), (4099, 3072, 1024), (129, 512, 256),
+                                   (255, 256, 512), (256, 768, 64), (257, 1024, 128), (511, 256, 1024)])
 def test_store_h_bias(cuda, bf16, M, N, K):
     import torch
     import pkc
@@ -106,4 +107,22 @@ def test_glu_and_power(cuda):
     ra, rg = rt[:, :, 0, :].reshape(M, N // 2), rt[:, :, 1, :].reshape(M, N // 2)
     wp = ra * ra + rg * rg
     err = (pw - wp).abs().max().item() / wp.abs().max().item()
+    assert err < 1e-4, err
+
+
+def test_one_sm_and_two_sm_kernels_agree(cuda):
+    """The 2-SM (cta_group::2) tiles and the 1-SM tiles give the same result
+    up to f32 summation order; run in a child process with the 1-SM switch."""
+    import os
+    import subprocess
+    import sys
+    import torch
+    import pkc
+    M, N, K = 1000, 1024, 2048
+    A, B, bias, ref = _setup(M, N, K, torch.float16, seed=9)
+    out = torch.zeros(M, N, device=cuda)
+    pkc.gemm(A.data_ptr(), B.data_ptr(), M, N, K, bf16=False, epi=pkc.EPI_STORE_F32, alpha=1.0,
+             bias=bias.data_ptr(), out=out.data_ptr(), ldo=N)
+    torch.cuda.synchronize()
+    err = (out - (ref + bias)).abs().max().item() / ref.abs().max().item()
     assert err < 1e-4, err
