@@ -94,6 +94,8 @@ __global__ void __launch_bounds__(NTHREADS, 2)
                   const int* __restrict__ item_off,  // [B] first packed row of each item
                   const int* __restrict__ item_len,  // [B] valid frames
                   H* __restrict__ ctx, int d, float scale_log2) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ __align__(16) uint8_t smem_raw[];
   using S = AttnSmem<H, DK>;
   constexpr int LD = S::LD;
@@ -321,10 +323,9 @@ cudaError_t launch_attn(const AttnArgs& a, cudaStream_t st) {
   if (e != cudaSuccess) return e;
   dim3 grid(a.n_tiles, a.n_heads);
   const float scale_log2 = 1.4426950408889634f / sqrtf((float)DK);
-  kern<<<grid, NTHREADS, smem, st>>>(reinterpret_cast<const H*>(a.qkv), reinterpret_cast<const H*>(a.ptab),
-                                     a.ptab_rows, a.ptab_ld > 0 ? a.ptab_ld : a.d, a.centre, a.bias_u, a.bias_v, a.tiles, a.item_off,
-                                     a.item_len, reinterpret_cast<H*>(a.ctx), a.d, scale_log2);
-  return cudaGetLastError();
+  return launch_pdl(kern, grid, dim3(NTHREADS), smem, st, reinterpret_cast<const H*>(a.qkv),
+                    reinterpret_cast<const H*>(a.ptab), a.ptab_rows, a.ptab_ld > 0 ? a.ptab_ld : a.d, a.centre, a.bias_u, a.bias_v, a.tiles, a.item_off,
+                    a.item_len, reinterpret_cast<H*>(a.ctx), a.d, scale_log2);
 }
 
 }  // namespace

@@ -241,6 +241,34 @@ __device__ __forceinline__ void umma_commit_2sm_mc(uint32_t bar, uint16_t mask) 
       : "memory");
 }
 
+
+// ---------------------------------------------------------------- PDL
+// Programmatic dependent launch: a kernel launched with launch_pdl may start
+// while its predecessor in the stream is still running; pdl_wait() blocks
+// until that predecessor has completed and its writes are visible (a no-op
+// when launched without the attribute). Every kernel calls pdl_wait() before
+// its first global-memory access.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                              cudaStream_t st, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute at[1];
+  at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  at[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = at;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, static_cast<KArgs>(args)...);
+}
+
 // ---------------------------------------------------------------- numerics
 template <typename H>
 struct is_bf16 { static constexpr bool value = false; };

@@ -6,7 +6,8 @@
 // Persistent CTAs (one per SM), 6 warps:
 //   warp 0 lane 0  TMA producer (runs ahead across tiles through a 4-stage ring)
 //   warp 1 lane 0  MMA issuer (single thread, as tcgen05 requires)
-//   warps 2..5     epilogue: warp w drains TMEM lanes [32(w%4), 32(w%4)+32)
+//   warps 2..9     epilogue: warp w drains TMEM lanes [32(w%4), 32(w%4)+32),
+//                  columns [0,128) for warps 2..5 and [128,256) for warps 6..9
 // Two 256-column f32 accumulators in TMEM (all 512 columns): the epilogue of
 // tile i runs while the MMAs of tile i+1 fill the other accumulator.
 //
@@ -23,7 +24,7 @@ constexpr int BM = 128;
 constexpr int BN = 256;
 constexpr int BK = 64;  // 64 x 2 bytes = one 128-byte swizzle row
 constexpr int STAGES = 4;
-constexpr int EPI_WARPS = 4;
+constexpr int EPI_WARPS = 8;  // two per TMEM lane quarter, each draining half the columns
 constexpr int THREADS = 64 + 32 * EPI_WARPS;
 constexpr int A_STAGE_BYTES = BM * BK * 2;
 constexpr int B_STAGE_BYTES = BN * BK * 2;
@@ -35,12 +36,14 @@ constexpr uint32_t TMEM_COLS = 512;  // two 128 x 256 f32 accumulators
 // (.sync.aligned); only rows inside M store.
 template <typename H, int EPI>
 __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t trow, int row,
-                                              bool row_ok, int n0) {
+                                              bool row_ok, int n0, int half) {
+  // two epilogue warps share each TMEM lane quarter: `half` selects which
+  // half of the tile's 32-column chunks this warp drains
   uint32_t r[32];
   if constexpr (EPI == EPI_GLU_H || EPI == EPI_POWER_F32) {
     uint32_t g[32];
 #pragma unroll 1
-    for (int j = 0; j < BN / 64; ++j) {
+    for (int j = half * (BN / 128); j < (half + 1) * (BN / 128); ++j) {
       tmem_ld32(trow + 32 * j, r);
       tmem_ld32(trow + BN / 2 + 32 * j, g);
       tmem_ld_wait();
@@ -84,14 +87,15 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t tro
     // overlaps the TMEM load and the previous chunk's arithmetic
     float* xrow = reinterpret_cast<float*>(args.out) + (size_t)(row_ok ? row : 0) * args.ldo + n0;
     float4 cur[8], nxt[8];
+    const int j0 = half * (BN / 64), j1 = j0 + BN / 64;
     if (row_ok) {
 #pragma unroll
-      for (int q = 0; q < 8; ++q) cur[q] = reinterpret_cast<const float4*>(xrow)[q];
+      for (int q = 0; q < 8; ++q) cur[q] = reinterpret_cast<const float4*>(xrow + 32 * j0)[q];
     }
 #pragma unroll 1
-    for (int j = 0; j < BN / 32; ++j) {
+    for (int j = j0; j < j1; ++j) {
       tmem_ld32(trow + 32 * j, r);
-      if (row_ok && j + 1 < BN / 32) {
+      if (row_ok && j + 1 < j1) {
 #pragma unroll
         for (int q = 0; q < 8; ++q) nxt[q] = reinterpret_cast<const float4*>(xrow + 32 * (j + 1))[q];
       }
@@ -119,7 +123,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t tro
     }
   } else {
 #pragma unroll 1
-    for (int j = 0; j < BN / 32; ++j) {
+    for (int j = half * (BN / 64); j < (half + 1) * (BN / 64); ++j) {
       tmem_ld32(trow + 32 * j, r);
       tmem_ld_wait();
       if (!row_ok) continue;
@@ -193,6 +197,7 @@ __global__ void __launch_bounds__(THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_wait();  // A (and the residual) come from the previous kernel
 
   if (warp == 0) {
     if (lane == 0) {
@@ -251,8 +256,9 @@ __global__ void __launch_bounds__(THREADS, 1)
       }
     }
   } else {
-    // ---- epilogue warps 2..5
+    // ---- epilogue warps 2..9
     const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int half = (warp - 2) >> 2;
     int local = 0;
     for (int tile = blockIdx.x; tile < n_tiles; tile += gridDim.x, ++local) {
       const int buf = local & 1;
@@ -267,13 +273,14 @@ __global__ void __launch_bounds__(THREADS, 1)
       const int row = m0 + q * 32 + lane;
       const bool row_ok = row < args.M;
       const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
-      epilogue_tile<H, EPI>(args, trow, row, row_ok, n0);
+      epilogue_tile<H, EPI>(args, trow, row, row_ok, n0, half);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&bars[2 * STAGES + 2 + buf]));
     }
   }
 
+  pdl_trigger();
   tc_fence_before();
   __syncthreads();
   if (warp == 0) tmem_dealloc(tmem, TMEM_COLS);
@@ -342,6 +349,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   cluster_sync();  // barrier init + TMEM alloc of both CTAs visible cluster-wide
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  pdl_wait();  // A (and the residual) come from the previous kernel
 
   if (warp == 0) {
     if (lane == 0) {
@@ -400,8 +408,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       }
     }
   } else {
-    // ---- epilogue warps 2..5 (both CTAs): this CTA's 128 rows of the tile
+    // ---- epilogue warps 2..9 (both CTAs): this CTA's 128 rows of the tile
     const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
     const uint32_t acce_leader0 = mapa_shared(smem_u32(&bars[2 * STAGES2 + 2]), 0);
     const uint32_t acce_leader1 = mapa_shared(smem_u32(&bars[2 * STAGES2 + 3]), 0);
     int local = 0;
@@ -418,13 +427,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       const int row = m0 + q * 32 + lane;
       const bool row_ok = row < args.M;
       const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
-      epilogue_tile<H, EPI>(args, trow, row, row_ok, n0);
+      epilogue_tile<H, EPI>(args, trow, row, row_ok, n0, half);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(buf ? acce_leader1 : acce_leader0);
     }
   }
 
+  pdl_trigger();
   tc_fence_before();
   __syncthreads();
   cluster_sync();  // no CTA leaves while its peer may still signal its barriers
@@ -494,8 +504,7 @@ static cudaError_t launch_t2(const CUtensorMap& ta, const CUtensorMap& tb, const
   }
   const int n_tiles = (a.N / BN) * ((a.M + 2 * HALF_ROWS - 1) / (2 * HALF_ROWS));
   const int pairs = n_tiles < max_pairs[dev & 63] ? n_tiles : max_pairs[dev & 63];
-  kern<<<2 * pairs, THREADS, SMEM2_BYTES, st>>>(ta, tb, a);
-  return cudaGetLastError();
+  return launch_pdl(kern, dim3(2 * pairs), dim3(THREADS), SMEM2_BYTES, st, ta, tb, a);
 }
 
 template <typename H, int EPI>
@@ -514,8 +523,7 @@ static cudaError_t launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const 
   if (!n_sm[dev & 63]) cudaDeviceGetAttribute(&n_sm[dev & 63], cudaDevAttrMultiProcessorCount, dev);
   const int n_tiles = (a.N / BN) * ((a.M + BM - 1) / BM);
   const int grid = n_tiles < n_sm[dev & 63] ? n_tiles : n_sm[dev & 63];
-  kern<<<grid, THREADS, SMEM_BYTES, st>>>(ta, tb, a);
-  return cudaGetLastError();
+  return launch_pdl(kern, dim3(grid), dim3(THREADS), SMEM_BYTES, st, ta, tb, a);
 }
 
 // PKC_GEMM_1SM=1 forces the 1-SM kernel (for A/B comparisons)

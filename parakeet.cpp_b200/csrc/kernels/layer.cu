@@ -21,6 +21,8 @@ __global__ void __launch_bounds__(256)
     k_layernorm(float* __restrict__ x, int M, const float* __restrict__ g, const float* __restrict__ b,
                 H* __restrict__ out_h, const float* __restrict__ g2, const float* __restrict__ b2,
                 int write_x) {
+  pdl_wait();
+  pdl_trigger();
   constexpr int D = NV * 128;
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -81,6 +83,8 @@ __global__ void __launch_bounds__(256)
 
 template <typename H>
 __global__ void k_pos_table(H* out, int centre, int d) {
+  pdl_wait();
+  pdl_trigger();
   const int half = d / 2;
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   const int rows = 2 * centre - 1;
@@ -106,6 +110,8 @@ __global__ void __launch_bounds__(128)
                      const float* __restrict__ w, const float* __restrict__ bias,
                      const float* __restrict__ scale, const float* __restrict__ shift,
                      const int* __restrict__ item_off, const int* __restrict__ item_len) {
+  pdl_wait();
+  pdl_trigger();
   const int b = blockIdx.y;
   const int T = item_len[b];
   const int t0 = blockIdx.x * DW_FRAMES;
@@ -165,6 +171,8 @@ __global__ void __launch_bounds__(128)
 // 32x32 tiled transpose per item: out[off*d + c*T + t] = x[(off + t)*d + c]
 __global__ void k_to_chfirst(const float* __restrict__ x, float* __restrict__ out, int d,
                              const int* __restrict__ item_off, const int* __restrict__ item_len) {
+  pdl_wait();
+  pdl_trigger();
   __shared__ float tile[32][33];
   const int b = blockIdx.z;
   const int T = item_len[b];
@@ -190,11 +198,12 @@ cudaError_t layernorm_launch(float* x, int M, int d, const float* g, const float
   if (M <= 0) return cudaSuccess;
   const dim3 grid((M + 7) / 8);
   const int wx = write_x ? 1 : 0;
+  cudaError_t e = cudaSuccess;
 #define PKC_LN(NV)                                                                                   \
   if (bf16)                                                                                          \
-    k_layernorm<NV, __nv_bfloat16><<<grid, 256, 0, st>>>(x, M, g, b, (__nv_bfloat16*)out_h, g2, b2, wx); \
+    e = launch_pdl(k_layernorm<NV, __nv_bfloat16>, grid, dim3(256), 0, st, x, M, g, b, (__nv_bfloat16*)out_h, g2, b2, wx); \
   else                                                                                               \
-    k_layernorm<NV, __half><<<grid, 256, 0, st>>>(x, M, g, b, (__half*)out_h, g2, b2, wx);
+    e = launch_pdl(k_layernorm<NV, __half>, grid, dim3(256), 0, st, x, M, g, b, (__half*)out_h, g2, b2, wx);
   switch (d) {
     case 256: PKC_LN(2) break;
     case 512: PKC_LN(4) break;
@@ -203,16 +212,15 @@ cudaError_t layernorm_launch(float* x, int M, int d, const float* g, const float
     default: return cudaErrorInvalidValue;
   }
 #undef PKC_LN
-  return cudaGetLastError();
+  return e;
 }
 
 cudaError_t pos_table_launch(void* out, int centre, int d, bool bf16, cudaStream_t st) {
   const long long n = (long long)(2 * centre - 1) * (d / 2);
   if (n <= 0) return cudaSuccess;
   const unsigned grid = (unsigned)((n + 255) / 256);
-  if (bf16) k_pos_table<__nv_bfloat16><<<grid, 256, 0, st>>>((__nv_bfloat16*)out, centre, d);
-  else k_pos_table<__half><<<grid, 256, 0, st>>>((__half*)out, centre, d);
-  return cudaGetLastError();
+  if (bf16) return launch_pdl(k_pos_table<__nv_bfloat16>, dim3(grid), dim3(256), 0, st, (__nv_bfloat16*)out, centre, d);
+  return launch_pdl(k_pos_table<__half>, dim3(grid), dim3(256), 0, st, (__half*)out, centre, d);
 }
 
 cudaError_t dwconv_bn_silu_launch(const void* in, void* out, int d, int K, const float* w,
@@ -223,13 +231,14 @@ cudaError_t dwconv_bn_silu_launch(const void* in, void* out, int d, int K, const
   if (d % 8) return cudaErrorInvalidValue;
   const dim3 grid((max_len + DW_FRAMES - 1) / DW_FRAMES, B);
   const int threads = d / 8 < 128 ? d / 8 : 128;
+  cudaError_t e = cudaSuccess;
 #define PKC_DW(KK)                                                                                 \
   if (bf16)                                                                                        \
-    k_dwconv_bn_silu<__nv_bfloat16, KK><<<grid, threads, 0, st>>>(                                  \
+    e = launch_pdl(k_dwconv_bn_silu<__nv_bfloat16, KK>, grid, dim3(threads), 0, st,                \
         (const __nv_bfloat16*)in, (__nv_bfloat16*)out, d, w, bias, scale, shift, item_off, item_len); \
   else                                                                                             \
-    k_dwconv_bn_silu<__half, KK><<<grid, threads, 0, st>>>((const __half*)in, (__half*)out, d, w, bias, \
-                                                          scale, shift, item_off, item_len);
+    e = launch_pdl(k_dwconv_bn_silu<__half, KK>, grid, dim3(threads), 0, st, (const __half*)in, (__half*)out, d, \
+                   w, bias, scale, shift, item_off, item_len);
   switch (K) {
     case 9: PKC_DW(9) break;
     case 7: PKC_DW(7) break;
@@ -238,15 +247,14 @@ cudaError_t dwconv_bn_silu_launch(const void* in, void* out, int d, int K, const
     default: return cudaErrorInvalidValue;
   }
 #undef PKC_DW
-  return cudaGetLastError();
+  return e;
 }
 
 cudaError_t to_channels_first_launch(const float* x, float* out, int d, const int* item_off,
                                      const int* item_len, int B, int max_len, cudaStream_t st) {
   if (B <= 0 || max_len <= 0) return cudaSuccess;
   if (d % 32) return cudaErrorInvalidValue;
-  k_to_chfirst<<<dim3((max_len + 31) / 32, d / 32, B), dim3(32, 8), 0, st>>>(x, out, d, item_off, item_len);
-  return cudaGetLastError();
+  return launch_pdl(k_to_chfirst, dim3((max_len + 31) / 32, d / 32, B), dim3(32, 8), 0, st, x, out, d, item_off, item_len);
 }
 
 }  // namespace pkc

@@ -31,6 +31,8 @@ constexpr int FR_THREADS = 128;
 
 __global__ void __launch_bounds__(FR_THREADS)
     k_mel_frames(MelArgs a, ItemTables t) {
+  pdl_wait();
+  pdl_trigger();
   const int row = blockIdx.x;
   if (row >= a.total_frames) return;
   const int b = find_item(t.mel_off, t.B, row);
@@ -71,6 +73,8 @@ __global__ void __launch_bounds__(FR_THREADS)
 }
 
 __global__ void k_mel_fb_log(FbArgs a) {
+  pdl_wait();
+  pdl_trigger();
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (idx >= (long long)a.total_frames * a.n_mels) return;
   const int row = (int)(idx / a.n_mels);
@@ -86,6 +90,8 @@ __global__ void k_mel_fb_log(FbArgs a) {
 // block (32 mel bins) x (32 frame lanes); grid (ceil(F/32), B)
 constexpr int NORM_LANES = 32;
 __global__ void __launch_bounds__(1024) k_mel_norm(float* logmel, int F, ItemTables t) {
+  pdl_wait();
+  pdl_trigger();
   const int b = blockIdx.y;
   const int m = blockIdx.x * 32 + threadIdx.x;
   const int T = t.mel_T[b];
@@ -129,6 +135,8 @@ __global__ void __launch_bounds__(1024) k_mel_norm(float* logmel, int F, ItemTab
 }
 
 __global__ void k_mel_to_batch(const float* logmel, int F, int Tmax, float* out, ItemTables t) {
+  pdl_wait();
+  pdl_trigger();
   const int b = blockIdx.z;
   const int m = blockIdx.y;
   const int f = blockIdx.x * blockDim.x + threadIdx.x;
@@ -138,6 +146,8 @@ __global__ void k_mel_to_batch(const float* logmel, int F, int Tmax, float* out,
 }
 
 __global__ void k_batch_to_packed(const float* in, int F, int Tmax, float* logmel, ItemTables t) {
+  pdl_wait();
+  pdl_trigger();
   const int b = blockIdx.z;
   const int m = blockIdx.y;
   const int f = blockIdx.x * blockDim.x + threadIdx.x;
@@ -149,21 +159,18 @@ __global__ void k_batch_to_packed(const float* in, int F, int Tmax, float* logme
 
 cudaError_t mel_frames_launch(const MelArgs& a, const ItemTables& t, cudaStream_t st) {
   if (a.total_frames <= 0) return cudaSuccess;
-  k_mel_frames<<<a.total_frames, FR_THREADS, 0, st>>>(a, t);
-  return cudaGetLastError();
+  return launch_pdl(k_mel_frames, dim3(a.total_frames), dim3(FR_THREADS), 0, st, a, t);
 }
 
 cudaError_t mel_fb_log_launch(const FbArgs& a, cudaStream_t st) {
   const long long n = (long long)a.total_frames * a.n_mels;
   if (n <= 0) return cudaSuccess;
-  k_mel_fb_log<<<(unsigned)((n + 255) / 256), 256, 0, st>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(k_mel_fb_log, dim3((unsigned)((n + 255) / 256)), dim3(256), 0, st, a);
 }
 
 cudaError_t mel_norm_launch(float* logmel, int n_mels, const ItemTables& t, cudaStream_t st) {
   if (t.B <= 0) return cudaSuccess;
-  k_mel_norm<<<dim3((n_mels + 31) / 32, t.B), dim3(32, NORM_LANES), 0, st>>>(logmel, n_mels, t);
-  return cudaGetLastError();
+  return launch_pdl(k_mel_norm, dim3((n_mels + 31) / 32, t.B), dim3(32, NORM_LANES), 0, st, logmel, n_mels, t);
 }
 
 cudaError_t mel_to_batch_launch(const float* logmel, int n_mels, int T_max, float* out,

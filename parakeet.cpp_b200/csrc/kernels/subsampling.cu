@@ -27,6 +27,8 @@ __global__ void __launch_bounds__(256)
     k_conv0(const float* __restrict__ logmel, int F, const float* __restrict__ w,
             const float* __restrict__ bias, int C, __nv_bfloat16* __restrict__ out, int F1,
             ItemTables t) {
+  pdl_wait();
+  pdl_trigger();
   extern __shared__ float rows[];  // [3][F + 2], zero padded on both sides
   const int row = blockIdx.x;
   int lo = 0, hi = t.B - 1;
@@ -67,6 +69,8 @@ __global__ void __launch_bounds__(256)
               const int* __restrict__ in_valid, const float* __restrict__ w,
               const float* __restrict__ bias, int C, __nv_bfloat16* __restrict__ out, int F_out,
               const int* __restrict__ out_off, const int* __restrict__ out_valid) {
+  pdl_wait();
+  pdl_trigger();
   const int b = blockIdx.y;
   const int cg = C / 8;
   const long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -116,8 +120,7 @@ cudaError_t sub_conv0_launch(const float* logmel, int F, const float* w, const f
                              cudaStream_t st) {
   if (t.B <= 0 || total_v1 <= 0) return cudaSuccess;
   const size_t smem = (size_t)3 * (F + 2) * sizeof(float);
-  k_conv0<<<total_v1, 256, smem, st>>>(logmel, F, w, b, C, out, F1, t);
-  return cudaGetLastError();
+  return launch_pdl(k_conv0, dim3(total_v1), dim3(256), smem, st, logmel, F, w, b, C, out, F1, t);
 }
 
 cudaError_t sub_dw_launch(const __nv_bfloat16* in, int F_in, const int* in_off, const int* in_valid,
@@ -127,9 +130,8 @@ cudaError_t sub_dw_launch(const __nv_bfloat16* in, int F_in, const int* in_off, 
   if (B <= 0 || max_out <= 0) return cudaSuccess;
   if (C % 8) return cudaErrorInvalidValue;
   const long long n = (long long)max_out * F_out * (C / 8);
-  k_dw3x3s2<<<dim3((unsigned)((n + 255) / 256), B), 256, 0, st>>>(in, F_in, in_off, in_valid, w, b, C,
-                                                                   out, F_out, out_off, out_valid);
-  return cudaGetLastError();
+  return launch_pdl(k_dw3x3s2, dim3((unsigned)((n + 255) / 256), B), dim3(256), 0, st, in, F_in, in_off, in_valid,
+                    w, b, C, out, F_out, out_off, out_valid);
 }
 
 }  // namespace pkc
