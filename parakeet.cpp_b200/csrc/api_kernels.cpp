@@ -86,17 +86,23 @@ extern "C" pkc_status pkc_relpos_attention(const void* qkv, const void* ptab, in
   host.insert(host.end(), off.begin(), off.end());
   host.insert(host.end(), len.begin(), len.end());
   host.insert(host.end(), tiles.begin(), tiles.end());
+  host.push_back(0);  // device error word
   int* dtab = nullptr;
   if (cudaMalloc(&dtab, host.size() * sizeof(int)) != cudaSuccess)
     return pkc::set_thread_error(PKC_ERR_OOM, "pkc_relpos_attention: table allocation failed");
   cudaMemcpyAsync(dtab, host.data(), host.size() * sizeof(int), cudaMemcpyHostToDevice, st);
+  int* derr = dtab + host.size() - 1;
   pkc::AttnArgs a{qkv, ptab, 2 * centre - 1, centre, d, bias_u, bias_v, dtab + 2 * B + 1,
-                  (int)tiles.size() / 2, dtab, dtab + B + 1, ctx, d, n_heads};
+                  (int)tiles.size() / 2, dtab, dtab + B + 1, ctx, d, n_heads, off[B], derr};
   cudaError_t e = pkc::attention_launch(a, dtype == 1, st);
   cudaError_t e2 = cudaStreamSynchronize(st);
+  int h_err = 0;
+  if (e == cudaSuccess && e2 == cudaSuccess) e2 = cudaMemcpy(&h_err, derr, sizeof(int), cudaMemcpyDeviceToHost);
   cudaFree(dtab);
   if (e != cudaSuccess || e2 != cudaSuccess)
     return pkc::set_thread_error(PKC_ERR_CUDA, std::string("pkc_relpos_attention: ") +
                                                    cudaGetErrorString(e != cudaSuccess ? e : e2));
+  if (h_err != 0)
+    return pkc::set_thread_error(PKC_ERR_KERNEL, "pkc_relpos_attention: kernel error word " + std::to_string(h_err));
   return PKC_OK;
 }

@@ -65,8 +65,13 @@ void make_plan(const Config& c, const std::vector<int>& n_samples, const std::ve
   p.M2 = p.v2_off[B];
   p.M = p.v_off[B];
   p.centre = p.max_v;
+  // attention query tiles, longest utterances first: a tile's cost grows with
+  // its utterance's length, so the block scheduler gets the long ones early
   const int qt = attn_query_tile();
-  for (int b = 0; b < B; ++b)
+  std::vector<int> order(B);
+  for (int b = 0; b < B; ++b) order[b] = b;
+  std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return p.v[a] > p.v[b]; });
+  for (int b : order)
     for (int q0 = 0; q0 < p.v[b]; q0 += qt) {
       p.attn_tiles.push_back(b);
       p.attn_tiles.push_back(q0);
@@ -399,7 +404,7 @@ pkc_status DeviceRunner::run_encoder(const Plan& p, cudaStream_t st, std::string
     prof_end(st, "layernorm", 0.0, (double)M * d * (4 + hs));
     PKC_ST(gemm(b_.hbuf, d, L.qkv_w, d, bf, M, 3 * d, d, EPI_STORE_H, ACT_NONE, 1.f, L.qkv_b, b_.qkv, 3 * d, st, "gemm_qkv", err));
     AttnArgs aa{b_.qkv, static_cast<const uint8_t*>(b_.ptab) + (size_t)li * d * 2, np, p.centre, Ld,
-                L.pos_u, L.pos_v, t_tiles, ntiles, t_v_off, t_v, b_.ctx, d, H};
+                L.pos_u, L.pos_v, t_tiles, ntiles, t_v_off, t_v, b_.ctx, d, H, M, err_word_};
     prof_begin(st);
     PKC_CK(attention_launch(aa, bf, st), "attention");
     prof_end(st, "attention", attn_flops, (double)M * (3 * d + d) * hs + (double)np * d * hs);

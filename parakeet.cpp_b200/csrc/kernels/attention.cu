@@ -18,6 +18,8 @@
 // Layout: qkv [M, 3d] (q | k | v, head h at columns h*dk), ptab [NP, d] (the
 // linear_pos output over relative positions centre-1 ... -(centre-1)),
 // ctx [M, d]; all f16 or bf16. One CTA = (one 64-row query tile, one head).
+#include <cstdlib>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -330,15 +332,32 @@ cudaError_t launch_attn(const AttnArgs& a, cudaStream_t st) {
 
 }  // namespace
 
-int attn_query_tile() { return QT; }
+int attn_mma_query_tile() { return QT; }
 
-cudaError_t attention_launch(const AttnArgs& a, bool bf16, cudaStream_t st) {
+cudaError_t attention_mma_launch(const AttnArgs& a, bool bf16, cudaStream_t st) {
   if (a.n_tiles <= 0) return cudaSuccess;
   const int dk = a.d / a.n_heads;
   if (a.d % a.n_heads != 0) return cudaErrorInvalidValue;
   if (dk == 128) return bf16 ? launch_attn<__nv_bfloat16, 128>(a, st) : launch_attn<__half, 128>(a, st);
   if (dk == 64) return bf16 ? launch_attn<__nv_bfloat16, 64>(a, st) : launch_attn<__half, 64>(a, st);
   return cudaErrorInvalidValue;
+}
+
+// The tcgen05 kernel (attention_tc.cu) is the product path; PKC_ATTN_MMA_SYNC=1
+// selects this warp-level mma.sync kernel instead, for A/B comparisons.
+bool attn_use_mma_sync() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("PKC_ATTN_MMA_SYNC");
+    v = (e && e[0] == '1') ? 1 : 0;
+  }
+  return v == 1;
+}
+
+int attn_query_tile() { return attn_use_mma_sync() ? attn_mma_query_tile() : attn_tc_query_tile(); }
+
+cudaError_t attention_launch(const AttnArgs& a, bool bf16, cudaStream_t st) {
+  return attn_use_mma_sync() ? attention_mma_launch(a, bf16, st) : attention_tc_launch(a, bf16, st);
 }
 
 }  // namespace pkc

@@ -89,17 +89,18 @@ extern "C" pkc_status pkc_relpos_attention_noalloc(const void* qkv, const void* 
   const int qt = attn_query_tile();
   long long n_tiles = 0;
   for (int b = 0; b < B; ++b) n_tiles += (lens[b] + qt - 1) / qt;
-  if ((long long)host.size() + 2 * n_tiles > kNoAllocTableInts)
+  if ((long long)host.size() + 2 * n_tiles + 1 > kNoAllocTableInts)
     return set_thread_error(PKC_ERR_ARG,
                             "pkc_relpos_attention_noalloc: " + std::to_string(n_tiles) +
                                 " query tiles exceed the fixed table (" +
-                                std::to_string((kNoAllocTableInts - (int)host.size()) / 2) + " max)");
+                                std::to_string((kNoAllocTableInts - 1 - (int)host.size()) / 2) + " max)");
   const size_t tiles_at = host.size();
   for (int b = 0; b < B; ++b)
     for (int q0 = 0; q0 < lens[b]; q0 += qt) {
       host.push_back(b);
       host.push_back(q0);
     }
+  host.push_back(0);  // device error word
   int dev = 0;
   cudaGetDevice(&dev);
   std::string err;
@@ -109,12 +110,16 @@ extern "C" pkc_status pkc_relpos_attention_noalloc(const void* qkv, const void* 
   cudaError_t e = cudaMemcpyAsync(tab, host.data(), host.size() * sizeof(int), cudaMemcpyHostToDevice, st);
   if (e == cudaSuccess) {
     AttnArgs a{qkv, ptab, 2 * centre - 1, centre, d, bias_u, bias_v, tab + tiles_at, (int)n_tiles,
-               tab, tab + B + 1, ctx, d, n_heads};
+               tab, tab + B + 1, ctx, d, n_heads, host[B], tab + host.size() - 1};
     e = attention_launch(a, dtype == 1, st);
   }
   // the host table vector must outlive the copy
   if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  int h_err = 0;
+  if (e == cudaSuccess) e = cudaMemcpy(&h_err, tab + host.size() - 1, sizeof(int), cudaMemcpyDeviceToHost);
   if (e != cudaSuccess)
     return set_thread_error(PKC_ERR_CUDA, std::string("pkc_relpos_attention_noalloc: ") + cudaGetErrorString(e));
+  if (h_err != 0)
+    return set_thread_error(PKC_ERR_KERNEL, "pkc_relpos_attention_noalloc: kernel error word " + std::to_string(h_err));
   return PKC_OK;
 }

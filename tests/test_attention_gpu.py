@@ -62,3 +62,39 @@ def test_relpos_attention_matches_torch(cuda, bf16, dk, lens):
     ref = reference(qkv, ptab, centre, bu, bv, lens, H)
     err = (ctx.float() - ref).abs().max().item() / ref.abs().max().item()
     assert err < (2e-2 if bf16 else 5e-3), err
+
+
+@pytest.mark.parametrize("bf16", [False, True])
+@pytest.mark.parametrize("dk,lens", [(128, [129, 65, 1, 191, 128, 64]), (64, [257, 63, 130])])
+def test_relpos_attention_tile_edges(cuda, bf16, dk, lens):
+    """Lengths one past / one short of the 128-row query tile and the 64-key tile."""
+    test_relpos_attention_matches_torch(cuda, bf16, dk, lens)
+
+
+@pytest.mark.parametrize("bf16", [False, True])
+def test_relpos_attention_late_maximum(cuda, bf16):
+    """Keys late in the utterance carry much larger scores than the first key
+    tiles, so the running maximum of every row moves after P V has started
+    accumulating: the rescale of the partial output must be exact."""
+    import torch
+    import pkc
+    H, dk = 8, 128
+    d = H * dk
+    lens = [700, 300]
+    dt = torch.bfloat16 if bf16 else torch.float16
+    g = torch.Generator().manual_seed(77)
+    M = sum(lens)
+    centre = max(lens)
+    qkv = torch.randn(M, 3 * d, generator=g) * 0.8
+    # keys 0..383 small, keys 384.. of the first utterance three times larger
+    qkv[384:700, d:2 * d] *= 3.0
+    qkv = qkv.to(dt).to(cuda)
+    ptab = (torch.randn(2 * centre - 1, d, generator=g) * 0.3).to(dt).to(cuda)
+    bu = (torch.randn(d, generator=g) * 0.05).to(cuda)
+    bv = (torch.randn(d, generator=g) * 0.05).to(cuda)
+    ctx = torch.zeros(M, d, dtype=dt, device=cuda)
+    pkc.relpos_attention(qkv.data_ptr(), ptab.data_ptr(), centre, bu.data_ptr(), bv.data_ptr(), lens,
+                         d, H, bf16=bf16, ctx=ctx.data_ptr())
+    ref = reference(qkv, ptab, centre, bu, bv, lens, H)
+    err = (ctx.float() - ref).abs().max().item() / ref.abs().max().item()
+    assert err < (2e-2 if bf16 else 5e-3), err
