@@ -175,113 +175,121 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int rb = p.centre - 1 - (q0 + QM - 1);  // first positional row of chunk 0
 
   if (warp == 0) {
-    if (lane == 0) {
-      // ---------------------------------------------------------------- TMA producer
-      const int colq = head * DK, colk = p.d + head * DK, colv = 2 * p.d + head * DK;
-      mbar_arrive_expect_tx(bar(B_QFULL), L::Q_BYTES);
+    // ------------------------------------------------------------------ TMA producer
+    // The whole warp runs the loop (waits are warp-wide); one elected lane
+    // arms the barriers and issues the copies.
+    const uint32_t leader = elect_one();
+    auto wwait = [&](int b, uint32_t parity) -> bool {
+      return __all_sync(0xffffffffu, mbar_wait(bar(b), parity, p.err, DEV_ERR_TIMEOUT_ATTN)) != 0;
+    };
+    const int colq = head * DK, colk = p.d + head * DK, colv = 2 * p.d + head * DK;
+    mbar_arrive_expect_tx_if(leader, bar(B_QFULL), L::Q_BYTES);
+#pragma unroll
+    for (int kb = 0; kb < L::KB; ++kb)
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+        tma_load_2d_if(leader, sbase + L::OFF_QU + kb * QM * 128 + h * 64 * 128, &tm_qkv, bar(B_QFULL),
+                       colq + kb * 64, off + q0 + 64 * h);
+    int n = 0;
+    for (; n < n_loads; ++n) {
+      const int s = n % RING;
+      if (!wwait(B_REMPTY + s, ((uint32_t)(n / RING) & 1u) ^ 1u)) break;
+      const LoadSeq ls = load_at(n, nT);
+      const CUtensorMap* map = ls.kind == 1 ? &tm_pos : &tm_qkv;
+      const int col = ls.kind == 0 ? colk : ls.kind == 1 ? head * DK : colv;
+      const int row = ls.kind == 1 ? rb + KN * ls.idx : off + KN * ls.idx;
+      mbar_arrive_expect_tx_if(leader, bar(B_RFULL + s), L::T_BYTES);
 #pragma unroll
       for (int kb = 0; kb < L::KB; ++kb)
-#pragma unroll
-        for (int h = 0; h < 2; ++h)
-          tma_load_2d(sbase + L::OFF_QU + kb * QM * 128 + h * 64 * 128, &tm_qkv, bar(B_QFULL), colq + kb * 64,
-                      off + q0 + 64 * h);
-      int n = 0;
-      for (; n < n_loads; ++n) {
-        const int s = n % RING;
-        if (!mbar_wait(bar(B_REMPTY + s), ((uint32_t)(n / RING) & 1u) ^ 1u, p.err, DEV_ERR_TIMEOUT_ATTN)) break;
-        const LoadSeq ls = load_at(n, nT);
-        const CUtensorMap* map = ls.kind == 1 ? &tm_pos : &tm_qkv;
-        const int col = ls.kind == 0 ? colk : ls.kind == 1 ? head * DK : colv;
-        const int row = ls.kind == 1 ? rb + KN * ls.idx : off + KN * ls.idx;
-        mbar_arrive_expect_tx(bar(B_RFULL + s), L::T_BYTES);
-#pragma unroll
-        for (int kb = 0; kb < L::KB; ++kb)
-          tma_load_2d(sbase + L::OFF_RING + s * L::T_BYTES + kb * KN * 128, map, bar(B_RFULL + s), col + kb * 64, row);
-      }
-      if (n < n_loads) {
-        // a consumer gave up: let every copy already issued land before the
-        // CTA may exit (the last load of each stage; earlier ones on the same
-        // stage were consumed, or a later one could not have been issued)
-        mbar_wait(bar(B_QFULL), 0, nullptr, 0);
-        for (int m = n - RING; m < n; ++m)
-          if (m >= 0) mbar_wait(bar(B_RFULL + m % RING), (uint32_t)(m / RING) & 1u, nullptr, 0);
-      }
+        tma_load_2d_if(leader, sbase + L::OFF_RING + s * L::T_BYTES + kb * KN * 128, map, bar(B_RFULL + s),
+                       col + kb * 64, row);
+    }
+    if (n < n_loads) {
+      // a consumer gave up: let every copy already issued land before the
+      // CTA may exit (the last load of each stage; earlier ones on the same
+      // stage were consumed, or a later one could not have been issued)
+      mbar_wait(bar(B_QFULL), 0, nullptr, 0);
+      for (int m = n - RING; m < n; ++m)
+        if (m >= 0) mbar_wait(bar(B_RFULL + m % RING), (uint32_t)(m / RING) & 1u, nullptr, 0);
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      // ---------------------------------------------------------------- MMA issuer
-      constexpr int fmt = is_bf16<H>::value ? 1 : 0;
-      constexpr uint32_t id_s = idesc_f16(QM, KN, fmt);
-      constexpr uint32_t id_pv = idesc_f16(QM, DK, fmt) | (1u << 16);  // B (V) MN-major
-      bool ok = mbar_wait(bar(B_QREADY), 0, p.err, DEV_ERR_TIMEOUT_ATTN);
+    // ------------------------------------------------------------------ MMA issuer
+    // Whole warp, one elected lane issuing (commits track that lane's MMAs).
+    const uint32_t leader = elect_one();
+    auto wwait = [&](int b, uint32_t parity) -> bool {
+      return __all_sync(0xffffffffu, mbar_wait(bar(b), parity, p.err, DEV_ERR_TIMEOUT_ATTN)) != 0;
+    };
+    constexpr int fmt = is_bf16<H>::value ? 1 : 0;
+    constexpr uint32_t id_s = idesc_f16(QM, KN, fmt);
+    constexpr uint32_t id_pv = idesc_f16(QM, DK, fmt) | (1u << 16);  // B (V) MN-major
+    bool ok = wwait(B_QREADY, 0);
+    tc_fence_after();
+    const uint64_t dqu = smem_desc_sw128(sbase + L::OFF_QU);
+    // K-step kk (16 elements of dk): k-block kk/4, 32 bytes per step inside it
+    auto a_off = [](int kk) { return (uint64_t)(((kk >> 2) * QM * 128 + (kk & 3) * 32) >> 4); };
+    auto b_off = [](int kk) { return (uint64_t)(((kk >> 2) * KN * 128 + (kk & 3) * 32) >> 4); };
+    auto ring_wait = [&](int n) -> bool {
+      if (!wwait(B_RFULL + n % RING, (uint32_t)(n / RING) & 1u)) return false;
       tc_fence_after();
-      const uint64_t dqu = smem_desc_sw128(sbase + L::OFF_QU);
-      // K-step kk (16 elements of dk): k-block kk/4, 32 bytes per step inside it
-      auto a_off = [](int kk) { return (uint64_t)(((kk >> 2) * QM * 128 + (kk & 3) * 32) >> 4); };
-      auto b_off = [](int kk) { return (uint64_t)(((kk >> 2) * KN * 128 + (kk & 3) * 32) >> 4); };
-      auto ring_wait = [&](int n) -> bool {
-        if (!mbar_wait(bar(B_RFULL + n % RING), (uint32_t)(n / RING) & 1u, p.err, DEV_ERR_TIMEOUT_ATTN)) return false;
+      return true;
+    };
+    auto ring_addr = [&](int n) { return sbase + L::OFF_RING + (n % RING) * L::T_BYTES; };
+    auto s_mma = [&](int u) -> bool {  // S = Qu K(u)^T
+      const int n = pos_k(u);
+      if (!ring_wait(n)) return false;
+      const uint64_t db = smem_desc_sw128(ring_addr(n));
+#pragma unroll
+      for (int kk = 0; kk < DK / 16; ++kk)
+        umma_f16_if(leader, tmem + TM_S, dqu + a_off(kk), db + b_off(kk), id_s, kk > 0 ? 1u : 0u);
+      umma_commit_if(leader, bar(B_REMPTY + n % RING));
+      return true;
+    };
+    auto c_mma = [&](int c) -> bool {  // chunk c = Qv (tensor memory) P(c)^T
+      const int n = pos_c(c);
+      if (!ring_wait(n)) return false;
+      const uint64_t db = smem_desc_sw128(ring_addr(n));
+      const uint32_t dcol = TM_BD + 64u * (uint32_t)(c % 3);
+#pragma unroll
+      for (int kk = 0; kk < DK / 16; ++kk)
+        umma_f16_ts_if(leader, tmem + dcol, tmem + TM_QV + 8u * kk, db + b_off(kk), id_s, kk > 0 ? 1u : 0u);
+      umma_commit_if(leader, bar(B_REMPTY + n % RING));
+      return true;
+    };
+    auto pv = [&](int u) -> bool {  // O += P(u) (tensor memory) V(u)
+      if (!wwait(B_PFULL + (u & 1), ((uint32_t)u >> 1) & 1u)) return false;
+      const int n = pos_v(u, nT);
+      if (!ring_wait(n)) return false;
+      const uint64_t dv = smem_desc_sw128_mn(ring_addr(n), KN * 128, 1024);
+      const uint32_t pa = tmem + TM_P + 32u * (uint32_t)(u & 1);
+#pragma unroll
+      for (int kk = 0; kk < KN / 16; ++kk)
+        umma_f16_ts_if(leader, tmem + TM_O, pa + 8u * kk, dv + (uint64_t)((kk * 16 * 128) >> 4), id_pv,
+                       (u > 0 || kk > 0) ? 1u : 0u);
+      umma_commit_if(leader, bar(B_REMPTY + n % RING));
+      umma_commit_if(leader, bar(B_PVDONE + (u & 1)));
+      return true;
+    };
+    ok = ok && c_mma(0) && c_mma(1) && s_mma(0) && c_mma(2);
+    if (ok) umma_commit_if(leader, bar(B_SFULL));
+    // S(u+1) and chunk u+3 go to the tensor pipe as soon as the softmax has
+    // read tile u, ahead of P(u-1) V(u-1): the softmax waits on S, while
+    // P V only has to finish before the P buffer comes round again
+    for (int u = 0; u < nT && ok; ++u) {
+      if (u + 1 < nT) {
+        // S and chunk u are free once the softmax has read tile u
+        ok = wwait(B_STFREE, (uint32_t)u & 1u);
+        if (!ok) break;
         tc_fence_after();
-        return true;
-      };
-      auto ring_addr = [&](int n) { return sbase + L::OFF_RING + (n % RING) * L::T_BYTES; };
-      auto s_mma = [&](int u) -> bool {  // S = Qu K(u)^T
-        const int n = pos_k(u);
-        if (!ring_wait(n)) return false;
-        const uint64_t db = smem_desc_sw128(ring_addr(n));
-#pragma unroll
-        for (int kk = 0; kk < DK / 16; ++kk)
-          umma_f16(tmem + TM_S, dqu + a_off(kk), db + b_off(kk), id_s, kk > 0 ? 1u : 0u);
-        umma_commit(bar(B_REMPTY + n % RING));
-        return true;
-      };
-      auto c_mma = [&](int c) -> bool {  // chunk c = Qv (tensor memory) P(c)^T
-        const int n = pos_c(c);
-        if (!ring_wait(n)) return false;
-        const uint64_t db = smem_desc_sw128(ring_addr(n));
-        const uint32_t dcol = TM_BD + 64u * (uint32_t)(c % 3);
-#pragma unroll
-        for (int kk = 0; kk < DK / 16; ++kk)
-          umma_f16_ts(tmem + dcol, tmem + TM_QV + 8u * kk, db + b_off(kk), id_s, kk > 0 ? 1u : 0u);
-        umma_commit(bar(B_REMPTY + n % RING));
-        return true;
-      };
-      auto pv = [&](int u) -> bool {  // O += P(u) (tensor memory) V(u)
-        if (!mbar_wait(bar(B_PFULL + (u & 1)), ((uint32_t)u >> 1) & 1u, p.err, DEV_ERR_TIMEOUT_ATTN)) return false;
-        const int n = pos_v(u, nT);
-        if (!ring_wait(n)) return false;
-        const uint64_t dv = smem_desc_sw128_mn(ring_addr(n), KN * 128, 1024);
-        const uint32_t pa = tmem + TM_P + 32u * (uint32_t)(u & 1);
-#pragma unroll
-        for (int kk = 0; kk < KN / 16; ++kk)
-          umma_f16_ts(tmem + TM_O, pa + 8u * kk, dv + (uint64_t)((kk * 16 * 128) >> 4), id_pv,
-                      (u > 0 || kk > 0) ? 1u : 0u);
-        umma_commit(bar(B_REMPTY + n % RING));
-        umma_commit(bar(B_PVDONE + (u & 1)));
-        return true;
-      };
-      ok = ok && c_mma(0) && c_mma(1) && s_mma(0) && c_mma(2);
-      if (ok) umma_commit(bar(B_SFULL));
-      // S(u+1) and chunk u+3 go to the tensor pipe as soon as the softmax has
-      // read tile u, ahead of P(u-1) V(u-1): the softmax waits on S, while
-      // P V only has to finish before the P buffer comes round again
-      for (int u = 0; u < nT && ok; ++u) {
-        if (u + 1 < nT) {
-          // S and chunk u are free once the softmax has read tile u
-          ok = mbar_wait(bar(B_STFREE), (uint32_t)u & 1u, p.err, DEV_ERR_TIMEOUT_ATTN);
-          if (!ok) break;
-          tc_fence_after();
-          ok = s_mma(u + 1) && c_mma(u + 3);
-          if (!ok) break;
-          umma_commit(bar(B_SFULL));
-        }
-        if (u >= 1) ok = pv(u - 1);
+        ok = s_mma(u + 1) && c_mma(u + 3);
+        if (!ok) break;
+        umma_commit_if(leader, bar(B_SFULL));
       }
-      if (ok) pv(nT - 1);
-      // every issued MMA has completed before TMEM can be released
-      umma_commit(bar(B_FINAL));
-      mbar_wait(bar(B_FINAL), 0, p.err, DEV_ERR_TIMEOUT_ATTN);
+      if (u >= 1) ok = pv(u - 1);
     }
+    if (ok) pv(nT - 1);
+    // every issued MMA has completed before TMEM can be released
+    umma_commit_if(leader, bar(B_FINAL));
+    wwait(B_FINAL, 0);
   } else {
     // ---------------------------------------------------------------- softmax warps
     const int q = warp & 3;              // TMEM lane quarter
