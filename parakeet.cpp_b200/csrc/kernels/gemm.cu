@@ -28,133 +28,128 @@ constexpr int EPI_WARPS = 8;  // two per TMEM lane quarter, each draining half t
 constexpr int THREADS = 64 + 32 * EPI_WARPS;
 constexpr int A_STAGE_BYTES = BM * BK * 2;
 constexpr int B_STAGE_BYTES = BN * BK * 2;
-constexpr int SMEM_BYTES = STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + 256 + 1024;
+constexpr int SMEM_BYTES = STAGES * (A_STAGE_BYTES + B_STAGE_BYTES) + 8 * 4096 + 256 + 1024;
 constexpr uint32_t TMEM_COLS = 512;  // two 128 x 256 f32 accumulators
 
-// Drain one 128 x 256 accumulator (this thread: one row, trow = its TMEM row
-// address) through the fused epilogue. Every lane executes the TMEM loads
-// (.sync.aligned); only rows inside M store.
+constexpr int EPI_STAGE_BYTES = 32 * 32 * 4;  // per epilogue warp: 32 rows x 32 f32 columns
+
+// Drain this warp's share of one accumulator tile (TMEM lanes row0..row0+31,
+// half `half` of the 32-column chunks) through the fused epilogue.
+// tcgen05.ld hands each thread one row, but a global access per thread-row
+// touches 32 rows (32 cache lines) per instruction. So every chunk is staged
+// through a per-warp 32 x 32 f32 tile in shared memory -- 16-byte chunk c of
+// row r at (c ^ (r & 7)), conflict-free both ways -- and leaves with lanes
+// laid along the rows: each instruction then covers 4 rows x 128 bytes.
+// Every lane executes the TMEM loads (.sync.aligned); only rows < M store.
 template <typename H, int EPI>
-__device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t trow, int row,
-                                              bool row_ok, int n0, int half) {
-  // two epilogue warps share each TMEM lane quarter: `half` selects which
-  // half of the tile's 32-column chunks this warp drains
-  uint32_t r[32];
-  if constexpr (EPI == EPI_GLU_H || EPI == EPI_POWER_F32) {
-    uint32_t g[32];
+__device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t trow, int row0, int n0,
+                                              int half, uint8_t* stage) {
+  constexpr bool PAIRED = EPI == EPI_GLU_H || EPI == EPI_POWER_F32;
+  const int lane = threadIdx.x & 31;
+  const int rr = lane >> 3, cc = lane & 7;  // coalesced layout: rows 4k + rr, 16-byte chunk cc
+  const uint32_t sst = smem_u32(stage);
+  // output chunk j: columns [32j, 32j + 32) of the output tile (PAIRED: value
+  // columns 32j and gate columns BN/2 + 32j of the accumulator)
+  const int j0 = PAIRED ? half * (BN / 128) : half * (BN / 64);
+  const int j1 = PAIRED ? j0 + BN / 128 : j0 + BN / 64;
+  const int oc0 = PAIRED ? n0 / 2 : n0;  // output column of chunk 0
+  float4 cur[8], nxt[8];
+  auto row_ok = [&](int k) { return row0 + 4 * k + rr < args.M; };
+  auto resid = [&](int j, int k) {
+    return reinterpret_cast<float4*>(reinterpret_cast<float*>(args.out) + (size_t)(row0 + 4 * k + rr) * args.ldo +
+                                     oc0 + 32 * j + 4 * cc);
+  };
+  if constexpr (EPI == EPI_RESID_F32) {
+#pragma unroll
+    for (int k = 0; k < 8; ++k)
+      if (row_ok(k)) cur[k] = *resid(j0, k);
+  }
 #pragma unroll 1
-    for (int j = half * (BN / 128); j < (half + 1) * (BN / 128); ++j) {
+  for (int j = j0; j < j1; ++j) {
+    uint32_t r[32];
+    if constexpr (PAIRED) {
+      uint32_t g[32];
       tmem_ld32(trow + 32 * j, r);
       tmem_ld32(trow + BN / 2 + 32 * j, g);
       tmem_ld_wait();
-      if (!row_ok) continue;
-      const int oc = n0 / 2 + 32 * j;
-      if constexpr (EPI == EPI_GLU_H) {
-        const float* ba = args.bias ? args.bias + n0 + 32 * j : nullptr;
-        const float* bg = args.bias ? args.bias + n0 + BN / 2 + 32 * j : nullptr;
-        H* out = reinterpret_cast<H*>(args.out) + (size_t)row * args.ldo + oc;
-        uint32_t w[16];
+      const float* ba = args.bias ? args.bias + n0 + 32 * j : nullptr;
+      const float* bg = args.bias ? args.bias + n0 + BN / 2 + 32 * j : nullptr;
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          float a0 = __uint_as_float(r[2 * i]), a1 = __uint_as_float(r[2 * i + 1]);
-          float g0 = __uint_as_float(g[2 * i]), g1 = __uint_as_float(g[2 * i + 1]);
+      for (int i = 0; i < 32; ++i) {
+        float a = __uint_as_float(r[i]), gg = __uint_as_float(g[i]);
+        if constexpr (EPI == EPI_GLU_H) {
           if (ba) {
-            a0 += ba[2 * i]; a1 += ba[2 * i + 1];
-            g0 += bg[2 * i]; g1 += bg[2 * i + 1];
+            a += ba[i];
+            gg += bg[i];
           }
-          w[i] = pack2<H>(a0 * sigmoidf_(g0), a1 * sigmoidf_(g1));
+          r[i] = __float_as_uint(a * sigmoidf_(gg));
+        } else {
+          r[i] = __float_as_uint(a * a + gg * gg);
         }
-        uint4* o4 = reinterpret_cast<uint4*>(out);
+      }
+    } else {
+      tmem_ld32(trow + 32 * j, r);
+      if constexpr (EPI == EPI_RESID_F32) {
+        // residual of the next chunk in flight during this one
+        if (j + 1 < j1) {
 #pragma unroll
-        for (int q = 0; q < 4; ++q) o4[q] = make_uint4(w[4 * q], w[4 * q + 1], w[4 * q + 2], w[4 * q + 3]);
+          for (int k = 0; k < 8; ++k)
+            if (row_ok(k)) nxt[k] = *resid(j + 1, k);
+        }
+      }
+      tmem_ld_wait();
+    }
+    // row layout -> staging tile
+#pragma unroll
+    for (int c = 0; c < 8; ++c)
+      *reinterpret_cast<uint4*>(stage + lane * 128 + ((c ^ (lane & 7)) << 4)) =
+          make_uint4(r[4 * c], r[4 * c + 1], r[4 * c + 2], r[4 * c + 3]);
+    __syncwarp();
+    // staging tile -> rows (lanes along the row)
+    const int oc = oc0 + 32 * j + 4 * cc;
+    float4 b4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    if constexpr (!PAIRED) {
+      if (args.bias) b4 = *reinterpret_cast<const float4*>(args.bias + oc);
+    }
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const int rl = 4 * k + rr;
+      float4 w;
+      asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
+                   : "=f"(w.x), "=f"(w.y), "=f"(w.z), "=f"(w.w)
+                   : "r"(sst + rl * 128 + ((cc ^ (rl & 7)) << 4)));
+      if (!row_ok(k)) continue;
+      const size_t ro = (size_t)(row0 + rl) * args.ldo + oc;
+      if constexpr (EPI == EPI_RESID_F32) {
+        float4 o = cur[k];
+        o.x += args.alpha * (w.x + b4.x);
+        o.y += args.alpha * (w.y + b4.y);
+        o.z += args.alpha * (w.z + b4.z);
+        o.w += args.alpha * (w.w + b4.w);
+        *reinterpret_cast<float4*>(reinterpret_cast<float*>(args.out) + ro) = o;
+      } else if constexpr (EPI == EPI_STORE_F32) {
+        *reinterpret_cast<float4*>(reinterpret_cast<float*>(args.out) + ro) =
+            make_float4(args.alpha * (w.x + b4.x), args.alpha * (w.y + b4.y), args.alpha * (w.z + b4.z),
+                        args.alpha * (w.w + b4.w));
+      } else if constexpr (EPI == EPI_POWER_F32) {
+        *reinterpret_cast<float4*>(reinterpret_cast<float*>(args.out) + ro) = w;
       } else {
-        float4* o4 = reinterpret_cast<float4*>(reinterpret_cast<float*>(args.out) + (size_t)row * args.ldo + oc);
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          float v[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const float a = __uint_as_float(r[4 * q + e]);
-            const float b = __uint_as_float(g[4 * q + e]);
-            v[e] = a * a + b * b;
+        float x0 = w.x, x1 = w.y, x2 = w.z, x3 = w.w;
+        if constexpr (EPI == EPI_STORE_H) {
+          x0 += b4.x; x1 += b4.y; x2 += b4.z; x3 += b4.w;
+          if (args.act == ACT_SILU) {
+            x0 = siluf_(x0); x1 = siluf_(x1); x2 = siluf_(x2); x3 = siluf_(x3);
+          } else if (args.act == ACT_RELU) {
+            x0 = fmaxf(x0, 0.f); x1 = fmaxf(x1, 0.f); x2 = fmaxf(x2, 0.f); x3 = fmaxf(x3, 0.f);
           }
-          o4[q] = make_float4(v[0], v[1], v[2], v[3]);
         }
+        *reinterpret_cast<uint2*>(reinterpret_cast<H*>(args.out) + ro) = make_uint2(pack2<H>(x0, x1), pack2<H>(x2, x3));
       }
     }
-  } else if constexpr (EPI == EPI_RESID_F32) {
-    // residual rows are prefetched one chunk ahead so their global latency
-    // overlaps the TMEM load and the previous chunk's arithmetic
-    float* xrow = reinterpret_cast<float*>(args.out) + (size_t)(row_ok ? row : 0) * args.ldo + n0;
-    float4 cur[8], nxt[8];
-    const int j0 = half * (BN / 64), j1 = j0 + BN / 64;
-    if (row_ok) {
+    __syncwarp();  // the staging tile is reused by the next chunk
+    if constexpr (EPI == EPI_RESID_F32) {
 #pragma unroll
-      for (int q = 0; q < 8; ++q) cur[q] = reinterpret_cast<const float4*>(xrow + 32 * j0)[q];
-    }
-#pragma unroll 1
-    for (int j = j0; j < j1; ++j) {
-      tmem_ld32(trow + 32 * j, r);
-      if (row_ok && j + 1 < j1) {
-#pragma unroll
-        for (int q = 0; q < 8; ++q) nxt[q] = reinterpret_cast<const float4*>(xrow + 32 * (j + 1))[q];
-      }
-      tmem_ld_wait();
-      if (row_ok) {
-        const int n = n0 + 32 * j;
-        float4* o4 = reinterpret_cast<float4*>(xrow + 32 * j);
-#pragma unroll
-        for (int q = 0; q < 8; ++q) {
-          float b0 = 0.f, b1 = 0.f, b2 = 0.f, b3 = 0.f;
-          if (args.bias) {
-            const float4 bb = reinterpret_cast<const float4*>(args.bias + n)[q];
-            b0 = bb.x; b1 = bb.y; b2 = bb.z; b3 = bb.w;
-          }
-          float4 o = cur[q];
-          o.x += args.alpha * (__uint_as_float(r[4 * q]) + b0);
-          o.y += args.alpha * (__uint_as_float(r[4 * q + 1]) + b1);
-          o.z += args.alpha * (__uint_as_float(r[4 * q + 2]) + b2);
-          o.w += args.alpha * (__uint_as_float(r[4 * q + 3]) + b3);
-          o4[q] = o;
-        }
-      }
-#pragma unroll
-      for (int q = 0; q < 8; ++q) cur[q] = nxt[q];
-    }
-  } else {
-#pragma unroll 1
-    for (int j = half * (BN / 64); j < (half + 1) * (BN / 64); ++j) {
-      tmem_ld32(trow + 32 * j, r);
-      tmem_ld_wait();
-      if (!row_ok) continue;
-      const int n = n0 + 32 * j;
-      float v[32];
-#pragma unroll
-      for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
-      if (args.bias) {
-#pragma unroll
-        for (int i = 0; i < 32; ++i) v[i] += args.bias[n + i];
-      }
-      if constexpr (EPI == EPI_STORE_H) {
-        if (args.act == ACT_SILU) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = siluf_(v[i]);
-        } else if (args.act == ACT_RELU) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) v[i] = fmaxf(v[i], 0.0f);
-        }
-        uint4* o4 = reinterpret_cast<uint4*>(reinterpret_cast<H*>(args.out) + (size_t)row * args.ldo + n);
-#pragma unroll
-        for (int q = 0; q < 4; ++q)
-          o4[q] = make_uint4(pack2<H>(v[8 * q], v[8 * q + 1]), pack2<H>(v[8 * q + 2], v[8 * q + 3]),
-                             pack2<H>(v[8 * q + 4], v[8 * q + 5]), pack2<H>(v[8 * q + 6], v[8 * q + 7]));
-      } else {  // EPI_STORE_F32
-        float4* o4 = reinterpret_cast<float4*>(reinterpret_cast<float*>(args.out) + (size_t)row * args.ldo + n);
-#pragma unroll
-        for (int q = 0; q < 8; ++q)
-          o4[q] = make_float4(args.alpha * v[4 * q], args.alpha * v[4 * q + 1], args.alpha * v[4 * q + 2],
-                              args.alpha * v[4 * q + 3]);
-      }
+      for (int k = 0; k < 8; ++k) cur[k] = nxt[k];
     }
   }
 }
@@ -168,7 +163,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * A_STAGE_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES * B_STAGE_BYTES);
+  uint8_t* sE = sB + STAGES * B_STAGE_BYTES;  // epilogue staging, EPI_STAGE_BYTES per epilogue warp
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sE + EPI_WARPS * EPI_STAGE_BYTES);
   // bars: [0,S) full, [S,2S) empty, 2S+{0,1} accumulator full, 2S+{2,3} accumulator empty
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
 
@@ -270,10 +266,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       tc_fence_after();
       const int m0 = (tile % tiles_m) * BM;
       const int n0 = (tile / tiles_m) * BN;
-      const int row = m0 + q * 32 + lane;
-      const bool row_ok = row < args.M;
       const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
-      epilogue_tile<H, EPI>(args, trow, row, row_ok, n0, half);
+      epilogue_tile<H, EPI>(args, trow, m0 + q * 32, n0, half, sE + (warp - 2) * EPI_STAGE_BYTES);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(smem_u32(&bars[2 * STAGES + 2 + buf]));
@@ -305,7 +299,7 @@ constexpr int STAGES2 = 6;
 constexpr int HALF_ROWS = 128;
 constexpr int A2_BYTES = HALF_ROWS * BK * 2;
 constexpr int B2_BYTES = HALF_ROWS * BK * 2;
-constexpr int SMEM2_BYTES = STAGES2 * (A2_BYTES + B2_BYTES) + 512 + 1024;
+constexpr int SMEM2_BYTES = STAGES2 * (A2_BYTES + B2_BYTES) + 8 * 4096 + 512 + 1024;
 
 template <typename H, int EPI>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
@@ -316,7 +310,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES2 * A2_BYTES;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sB + STAGES2 * B2_BYTES);
+  uint8_t* sE = sB + STAGES2 * B2_BYTES;  // epilogue staging, EPI_STAGE_BYTES per epilogue warp
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sE + EPI_WARPS * EPI_STAGE_BYTES);
   // bars: [0,S) full, [S,2S) empty, 2S+{0,1} accumulator full, 2S+{2,3} accumulator empty
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES2 + 4);
 
@@ -424,10 +419,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       tc_fence_after();
       const int m0 = (tile % tiles_m) * 2 * HALF_ROWS + (int)rank * HALF_ROWS;
       const int n0 = (tile / tiles_m) * BN;
-      const int row = m0 + q * 32 + lane;
-      const bool row_ok = row < args.M;
       const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
-      epilogue_tile<H, EPI>(args, trow, row, row_ok, n0, half);
+      epilogue_tile<H, EPI>(args, trow, m0 + q * 32, n0, half, sE + (warp - 2) * EPI_STAGE_BYTES);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(buf ? acce_leader1 : acce_leader0);
@@ -545,6 +538,7 @@ cudaError_t gemm_launch(const void* A, int lda, const void* B, int ldb, bool bf1
   if (args.M <= 0) return cudaSuccess;
   if (args.N % BN != 0 || args.K % BK != 0 || args.K <= 0 || (lda % 8) != 0 || (ldb % 8) != 0 ||
       (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15) ||
+      (reinterpret_cast<uintptr_t>(args.bias) & 15) || (reinterpret_cast<uintptr_t>(args.out) & 15) ||
       (args.ldo % 8) != 0)
     return cudaErrorInvalidValue;
   // 2-SM tiles once there are at least two 128-row blocks of A
