@@ -29,10 +29,18 @@ __global__ void __launch_bounds__(256)
   if (row >= M) return;
   float* xr = x + (size_t)row * D;
   float v[NV * 4];
+  // gamma / beta are issued together with the row so their latency overlaps
+  // the row load instead of following the reductions
+  float4 g4[NV], b4[NV];
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
     const float4 q = *reinterpret_cast<const float4*>(xr + (i * 32 + lane) * 4);
     v[4 * i] = q.x; v[4 * i + 1] = q.y; v[4 * i + 2] = q.z; v[4 * i + 3] = q.w;
+  }
+#pragma unroll
+  for (int i = 0; i < NV; ++i) {
+    g4[i] = __ldg(reinterpret_cast<const float4*>(g + (i * 32 + lane) * 4));
+    b4[i] = __ldg(reinterpret_cast<const float4*>(b + (i * 32 + lane) * 4));
   }
   auto norm = [&](const float* gg, const float* bb) {
     float s = 0.f;
@@ -52,23 +60,27 @@ __global__ void __launch_bounds__(256)
     const float scale = 1.0f / sqrtf(s2 / (float)D + 1e-5f);
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
-      const int c = (i * 32 + lane) * 4;
-      const float4 g4 = *reinterpret_cast<const float4*>(gg + c);
-      const float4 b4 = *reinterpret_cast<const float4*>(bb + c);
-      v[4 * i] = v[4 * i] * scale * g4.x + b4.x;
-      v[4 * i + 1] = v[4 * i + 1] * scale * g4.y + b4.y;
-      v[4 * i + 2] = v[4 * i + 2] * scale * g4.z + b4.z;
-      v[4 * i + 3] = v[4 * i + 3] * scale * g4.w + b4.w;
+      v[4 * i] = v[4 * i] * scale * g4[i].x + b4[i].x;
+      v[4 * i + 1] = v[4 * i + 1] * scale * g4[i].y + b4[i].y;
+      v[4 * i + 2] = v[4 * i + 2] * scale * g4[i].z + b4[i].z;
+      v[4 * i + 3] = v[4 * i + 3] * scale * g4[i].w + b4[i].w;
+    }
+    if (gg) {  // the second norm's gamma / beta (loaded after the first norm used g4 / b4)
+#pragma unroll
+      for (int i = 0; i < NV; ++i) {
+        g4[i] = __ldg(reinterpret_cast<const float4*>(gg + (i * 32 + lane) * 4));
+        b4[i] = __ldg(reinterpret_cast<const float4*>(bb + (i * 32 + lane) * 4));
+      }
     }
   };
-  norm(g, b);
+  norm(g2, b2);
   if (write_x) {
 #pragma unroll
     for (int i = 0; i < NV; ++i)
       *reinterpret_cast<float4*>(xr + (i * 32 + lane) * 4) =
           make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
   }
-  if (g2) norm(g2, b2);
+  if (g2) norm(nullptr, nullptr);
   if (out_h) {
     H* o = out_h + (size_t)row * D;
 #pragma unroll
@@ -98,14 +110,19 @@ __global__ void k_pos_table(H* out, int centre, int d) {
   out[(size_t)r * d + 2 * i + 1] = to_h<H>((float)cos(arg));
 }
 
-// One CTA = DW_FRAMES consecutive frames of one utterance x all d channels;
-// one thread = 8 channels (16-byte loads): the DW_FRAMES + K - 1 input rows it
-// needs are loaded once into registers (zeros outside the utterance), the K
-// taps are held in registers. grid (ceil(max_len / DW_FRAMES), B)
-constexpr int DW_FRAMES = 4;
+// One CTA = DW_FRAMES consecutive frames of one utterance x DW_CH channels;
+// one thread = 8 channels (16-byte accesses). Each thread issues the loads of
+// all DW_FRAMES + K - 1 input rows it needs at once (zeros outside the
+// utterance) -- many 16-byte requests in flight per thread, read
+// amplification (DW_FRAMES + K - 1) / DW_FRAMES -- keeps the K taps in
+// registers, and writes DW_FRAMES rows. grid (ceil(max_len / DW_FRAMES), B,
+// ceil(d / DW_CH)).
+constexpr int DW_FRAMES = 16;
+constexpr int DW_THREADS = 64;
+constexpr int DW_CH = DW_THREADS * 8;
 
 template <typename H, int K>
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(DW_THREADS)
     k_dwconv_bn_silu(const H* __restrict__ in, H* __restrict__ out, int d,
                      const float* __restrict__ w, const float* __restrict__ bias,
                      const float* __restrict__ scale, const float* __restrict__ shift,
@@ -115,56 +132,59 @@ __global__ void __launch_bounds__(128)
   const int b = blockIdx.y;
   const int T = item_len[b];
   const int t0 = blockIdx.x * DW_FRAMES;
-  if (t0 >= T) return;
+  const int c0 = blockIdx.z * DW_CH + threadIdx.x * 8;
+  if (t0 >= T || c0 >= d) return;
   constexpr int pad = (K - 1) / 2;
   constexpr int NR = DW_FRAMES + K - 1;
-  const H* x = in + (size_t)item_off[b] * d;
-  H* y = out + (size_t)item_off[b] * d;
-  for (int c0 = threadIdx.x * 8; c0 < d; c0 += blockDim.x * 8) {
-    uint4 rows[NR];
+  const H* x = in + (size_t)item_off[b] * d + c0;
+  H* y = out + (size_t)item_off[b] * d + c0;
+  uint4 rows[NR];
 #pragma unroll
-    for (int r = 0; r < NR; ++r) {
-      const int ti = t0 - pad + r;
-      rows[r] = (ti >= 0 && ti < T) ? *reinterpret_cast<const uint4*>(x + (size_t)ti * d + c0)
-                                    : make_uint4(0, 0, 0, 0);
-    }
-    float acc[DW_FRAMES][8];
+  for (int r = 0; r < NR; ++r) {
+    const int ti = t0 - pad + r;
+    rows[r] = (ti >= 0 && ti < T) ? __ldg(reinterpret_cast<const uint4*>(x + (size_t)ti * d)) : make_uint4(0, 0, 0, 0);
+  }
+  float wk[K][8];
 #pragma unroll
-    for (int f = 0; f < DW_FRAMES; ++f)
+  for (int k = 0; k < K; ++k) {
+    const float4 wa = __ldg(reinterpret_cast<const float4*>(w + (size_t)k * d + c0));
+    const float4 wb = __ldg(reinterpret_cast<const float4*>(w + (size_t)k * d + c0 + 4));
+    wk[k][0] = wa.x; wk[k][1] = wa.y; wk[k][2] = wa.z; wk[k][3] = wa.w;
+    wk[k][4] = wb.x; wk[k][5] = wb.y; wk[k][6] = wb.z; wk[k][7] = wb.w;
+  }
+  const float4 s0 = __ldg(reinterpret_cast<const float4*>(scale + c0)), s1 = __ldg(reinterpret_cast<const float4*>(scale + c0 + 4));
+  const float4 h0 = __ldg(reinterpret_cast<const float4*>(shift + c0)), h1 = __ldg(reinterpret_cast<const float4*>(shift + c0 + 4));
+  float sc[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+  float sh[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+  if (bias) {
+    // (acc + bias) * scale + shift = acc * scale + (bias * scale + shift)
+    const float4 b0 = __ldg(reinterpret_cast<const float4*>(bias + c0)), b1 = __ldg(reinterpret_cast<const float4*>(bias + c0 + 4));
+    const float bi[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
 #pragma unroll
-      for (int c = 0; c < 8; ++c) acc[f][c] = 0.f;
+    for (int c = 0; c < 8; ++c) sh[c] = fmaf(bi[c], sc[c], sh[c]);
+  }
+  const int nf = min(DW_FRAMES, T - t0);
+#pragma unroll
+  for (int f = 0; f < DW_FRAMES; ++f) {
+    if (f >= nf) break;
+    float acc[8];
+#pragma unroll
+    for (int c = 0; c < 8; ++c) acc[c] = 0.f;
 #pragma unroll
     for (int k = 0; k < K; ++k) {
-      const float4 wa = *reinterpret_cast<const float4*>(w + (size_t)k * d + c0);
-      const float4 wb = *reinterpret_cast<const float4*>(w + (size_t)k * d + c0 + 4);
-      const float wk[8] = {wa.x, wa.y, wa.z, wa.w, wb.x, wb.y, wb.z, wb.w};
+      const H* hv = reinterpret_cast<const H*>(&rows[f + k]);
 #pragma unroll
-      for (int f = 0; f < DW_FRAMES; ++f) {
-        const H* hv = reinterpret_cast<const H*>(&rows[f + k]);
-#pragma unroll
-        for (int c = 0; c < 8; ++c) acc[f][c] = fmaf(wk[c], from_h(hv[c]), acc[f][c]);
-      }
+      for (int c = 0; c < 8; ++c) acc[c] = fmaf(wk[k][c], from_h(hv[c]), acc[c]);
     }
-    const float4 s0 = *reinterpret_cast<const float4*>(scale + c0), s1 = *reinterpret_cast<const float4*>(scale + c0 + 4);
-    const float4 h0 = *reinterpret_cast<const float4*>(shift + c0), h1 = *reinterpret_cast<const float4*>(shift + c0 + 4);
-    const float sc[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-    const float sh[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
-    float bi[8];
+    float r[8];
 #pragma unroll
-    for (int c = 0; c < 8; ++c) bi[c] = bias ? bias[c0 + c] : 0.f;
-#pragma unroll
-    for (int f = 0; f < DW_FRAMES; ++f) {
-      if (t0 + f >= T) break;
-      float r[8];
-#pragma unroll
-      for (int c = 0; c < 8; ++c) r[c] = siluf_((acc[f][c] + bi[c]) * sc[c] + sh[c]);
-      uint4 o;
-      o.x = pack2<H>(r[0], r[1]);
-      o.y = pack2<H>(r[2], r[3]);
-      o.z = pack2<H>(r[4], r[5]);
-      o.w = pack2<H>(r[6], r[7]);
-      *reinterpret_cast<uint4*>(y + (size_t)(t0 + f) * d + c0) = o;
-    }
+    for (int c = 0; c < 8; ++c) r[c] = siluf_(fmaf(acc[c], sc[c], sh[c]));
+    uint4 o;
+    o.x = pack2<H>(r[0], r[1]);
+    o.y = pack2<H>(r[2], r[3]);
+    o.z = pack2<H>(r[4], r[5]);
+    o.w = pack2<H>(r[6], r[7]);
+    *reinterpret_cast<uint4*>(y + (size_t)(t0 + f) * d) = o;
   }
 }
 
@@ -229,8 +249,8 @@ cudaError_t dwconv_bn_silu_launch(const void* in, void* out, int d, int K, const
                                   bool bf16, cudaStream_t st) {
   if (B <= 0 || max_len <= 0) return cudaSuccess;
   if (d % 8) return cudaErrorInvalidValue;
-  const dim3 grid((max_len + DW_FRAMES - 1) / DW_FRAMES, B);
-  const int threads = d / 8 < 128 ? d / 8 : 128;
+  const dim3 grid((max_len + DW_FRAMES - 1) / DW_FRAMES, B, (d + DW_CH - 1) / DW_CH);
+  const int threads = DW_THREADS;
   cudaError_t e = cudaSuccess;
 #define PKC_DW(KK)                                                                                 \
   if (bf16)                                                                                        \
