@@ -105,6 +105,10 @@ std::string DeviceRunner::init(const GgufFile& g) {
   power_ld_ = cfg_.n_fft / 2 + 8;
   const char* ng = getenv("PKC_NO_GRAPH");
   use_graphs_ = !(ng && ng[0] == '1');
+  // PKC_SUB_UNFUSED=1: conv.0 and the first depthwise as two kernels with the
+  // conv.0 map in memory (A/B comparisons); the default is the fused kernel
+  const char* su = getenv("PKC_SUB_UNFUSED");
+  sub_unfused_ = (su && su[0] == '1') || (cfg_.F1 != 64 && cfg_.F1 != 40);
   return upload_weights(g, cfg_, w_);
 }
 
@@ -260,7 +264,7 @@ pkc_status DeviceRunner::prepare(const Plan& p, cudaStream_t st, std::string& er
   const size_t o_pow = take((size_t)p.total_frames * power_ld_ * 4);
   const size_t o_log = take((size_t)p.total_frames * F * 4);
   const size_t o_mb = take((size_t)B * F * p.max_Tm * 4);
-  const size_t o_s1 = take((size_t)p.M1 * c.F1 * C * 2);
+  const size_t o_s1 = take(sub_unfused_ ? (size_t)p.M1 * c.F1 * C * 2 : 0);
   const size_t o_s2a = take((size_t)p.M2 * c.F2 * C * 2);
   const size_t o_s2b = take((size_t)p.M2 * c.F2 * C * 2);
   const size_t o_s3a = take((size_t)p.M * c.F3 * C * 2);
@@ -348,15 +352,25 @@ pkc_status DeviceRunner::run_encoder(const Plan& p, cudaStream_t st, std::string
   ItemTables t{p.B, t_pcm_off, t_S, t_mel_off, t_Tm, t_mval, t_v1_off, t_v1, t_v2_off, t_v2, t_v_off, t_v};
 
   // ---- subsampling (src/subsampling.cpp:48-240)
-  prof_begin(st);
-  PKC_CK(sub_conv0_launch(b_.logmel, c.n_mels, w_.c0_w, w_.c0_b, C,
-                          reinterpret_cast<__nv_bfloat16*>(b_.s1), c.F1, t, p.M1, st), "conv0");
-  prof_end(st, "sub_conv0", 2.0 * p.M1 * c.F1 * C * 9, (double)p.total_frames * c.n_mels * 4 + (double)p.M1 * c.F1 * C * 2);
-  prof_begin(st);
-  PKC_CK(sub_dw_launch(reinterpret_cast<const __nv_bfloat16*>(b_.s1), c.F1, t_v1_off, t_v1, w_.dw1_w,
-                       w_.dw1_b, C, reinterpret_cast<__nv_bfloat16*>(b_.s2a), c.F2, t_v2_off, t_v2, p.B,
-                       p.max_v2, st), "dw1");
-  prof_end(st, "sub_dw", 2.0 * p.M2 * c.F2 * C * 9, ((double)p.M1 * c.F1 + (double)p.M2 * c.F2) * C * 2);
+  if (sub_unfused_) {
+    prof_begin(st);
+    PKC_CK(sub_conv0_launch(b_.logmel, c.n_mels, w_.c0_w, w_.c0_b, C,
+                            reinterpret_cast<__nv_bfloat16*>(b_.s1), c.F1, t, p.M1, st), "conv0");
+    prof_end(st, "sub_conv0", 2.0 * p.M1 * c.F1 * C * 9, (double)p.total_frames * c.n_mels * 4 + (double)p.M1 * c.F1 * C * 2);
+    prof_begin(st);
+    PKC_CK(sub_dw_launch(reinterpret_cast<const __nv_bfloat16*>(b_.s1), c.F1, t_v1_off, t_v1, w_.dw1_w,
+                         w_.dw1_b, C, reinterpret_cast<__nv_bfloat16*>(b_.s2a), c.F2, t_v2_off, t_v2, p.B,
+                         p.max_v2, st), "dw1");
+    prof_end(st, "sub_dw", 2.0 * p.M2 * c.F2 * C * 9, ((double)p.M1 * c.F1 + (double)p.M2 * c.F2) * C * 2);
+  } else {
+    // conv.0 + ReLU + first depthwise in one kernel; algorithmic bytes: mel
+    // read once, stage-2 frames written once
+    prof_begin(st);
+    PKC_CK(sub_stage1_launch(b_.logmel, c.n_mels, w_.c0_w, w_.c0_b, w_.dw1_w, w_.dw1_b, C,
+                             reinterpret_cast<__nv_bfloat16*>(b_.s2a), c.F1, t, p.max_v2, st), "stage1");
+    prof_end(st, "sub_stage1", 2.0 * p.M1 * c.F1 * C * 9 + 2.0 * p.M2 * c.F2 * C * 9,
+             (double)p.total_frames * c.n_mels * 4 + (double)p.M2 * c.F2 * C * 2);
+  }
   PKC_ST(gemm(b_.s2a, C, w_.pw1_w, C, true, p.M2 * c.F2, C, C, EPI_STORE_H, ACT_RELU, 1.f, w_.pw1_b,
               b_.s2b, C, st, "gemm_sub_pw", err));
   prof_begin(st);

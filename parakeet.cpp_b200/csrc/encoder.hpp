@@ -81,6 +81,7 @@ class DeviceRunner {
   void* ws_ = nullptr;
   size_t ws_bytes_ = 0;
   int* err_word_ = nullptr;
+  bool sub_unfused_ = false;
   int* h_tables_ = nullptr;  // pinned staging for the item tables
   size_t h_tables_cap_ = 0;
   // carved workspace pointers for the current plan

@@ -66,6 +66,11 @@ cudaError_t batch_to_packed_launch(const float* in, int n_mels, int T_max, float
 cudaError_t sub_conv0_launch(const float* logmel, int F, const float* w /*[C][9]*/, const float* b,
                              int C, __nv_bfloat16* out, int F1, const ItemTables& t, int total_v1,
                              cudaStream_t st);
+// Stage 1 fused (conv.0 + ReLU, then the first depthwise + bias): mel ->
+// stage-2 frames [sum v2, F2, C] bf16, no conv.0 map in memory. F1 = 64 or 40.
+cudaError_t sub_stage1_launch(const float* logmel, int F, const float* w0, const float* b0, const float* w1,
+                              const float* b1, int C, __nv_bfloat16* out, int F1, const ItemTables& t,
+                              int max_v2, cudaStream_t st);
 // Depthwise Conv2d(C, 3x3, stride 2, pad 1, groups C) + bias.
 // stage 1: in = (v1, F_in) -> out = (v2, F_out); stage 2: (v2 -> v)
 cudaError_t sub_dw_launch(const __nv_bfloat16* in, int F_in, const int* in_off, const int* in_valid,

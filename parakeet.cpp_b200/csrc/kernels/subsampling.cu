@@ -113,7 +113,200 @@ __global__ void __launch_bounds__(256)
   *reinterpret_cast<uint4*>(out + (((size_t)out_off[b] + tt) * F_out + f) * C + c0) = o;
 }
 
+// ---------------------------------------------------------------------------
+// Stage 1 fused: conv.0 (1 -> C, 3x3, s2, p1) + bias + ReLU, then the first
+// depthwise 3x3 s2 p1 + bias, without the C-channel conv.0 map (v1 x F1 x C,
+// the largest tensor of the encoder) ever reaching memory.
+//
+// One CTA = S1_T2 consecutive stage-2 frames of one utterance x S1_CG
+// channels. It needs conv.0 rows t1 = 2 t2_0 - 1 ... 2 (t2_0 + S1_T2) - 1
+// (S1_ROWS of them) and mel rows 4 t2_0 - 3 ... (S1_MROWS):
+//  1. the mel rows go to shared memory (zeros outside the utterance's valid
+//     frames and outside [0, F));
+//  2. conv.0 runs on the tensor cores as [positions x 16] x [16 x channels]
+//     (the 9 taps, zero-padded to K = 16; f16 operands, f32 accumulation,
+//     mma.sync m16n8k16 -- K = 9 is far too small for a tcgen05 tile), and
+//     bias + ReLU go into a bf16 tile in shared memory: rows outside
+//     [0, v1) are zero, which is the reference's stage-2 input mask;
+//  3. the depthwise conv reads that tile and writes stage-2 frames (bf16).
+// The bf16 tile matches the rounding of the unfused path, where the conv.0
+// map is stored in bf16.
+constexpr int S1_T2 = 4;
+constexpr int S1_CG = 64;
+constexpr int S1_ROWS = 2 * S1_T2 + 1;
+constexpr int S1_MROWS = 4 * S1_T2 + 3;
+constexpr int S1_THREADS = 256;
+
+__device__ __forceinline__ void mma16816_f16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+template <int F1>
+__global__ void __launch_bounds__(S1_THREADS)
+    k_sub_stage1(const float* __restrict__ logmel, int F, const float* __restrict__ w0,
+                 const float* __restrict__ b0, const float* __restrict__ w1, const float* __restrict__ b1,
+                 int C, __nv_bfloat16* __restrict__ out, ItemTables t) {
+  constexpr int F2 = (F1 - 1) / 2 + 1;
+  constexpr int NP = S1_ROWS * F1;          // conv.0 positions in the tile
+  constexpr int MT = (NP + 15) / 16;        // 16-position MMA tiles
+  constexpr int NT = S1_CG / 8;             // 8-channel MMA tiles
+  pdl_wait();
+  pdl_trigger();
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  const int b = blockIdx.y;
+  const int t2_0 = blockIdx.x * S1_T2;
+  const int v2b = t.v2[b];
+  if (t2_0 >= v2b) return;
+  const int cg0 = blockIdx.z * S1_CG;
+  const int v1b = t.v1[b], mvalid = t.mel_valid[b];
+  const float* mel = logmel + (size_t)t.mel_off[b] * F;
+  const int t1_0 = 2 * t2_0 - 1;
+  const int tm_0 = 2 * t1_0 - 1;
+  const int FP = F + 2;                      // padded mel row
+  float* melt = reinterpret_cast<float*>(smem_raw);                              // [S1_MROWS][FP]
+  uint8_t* s1 = smem_raw + (((size_t)S1_MROWS * FP * 4 + 127) / 128) * 128;      // [S1_ROWS*F1][S1_CG] bf16
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+
+  // 1. mel rows
+  for (int i = tid; i < S1_MROWS * FP; i += S1_THREADS) {
+    const int r = i / FP, col = i % FP - 1;
+    const int tm = tm_0 + r;
+    melt[i] = (col >= 0 && col < F && tm >= 0 && tm < mvalid) ? mel[(size_t)tm * F + col] : 0.f;
+  }
+  __syncthreads();
+
+  // 2. conv.0 on the tensor cores
+  {
+    const int g = lane >> 2, t4 = lane & 3;
+    uint32_t bf[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      const float* wc = w0 + (size_t)(cg0 + nt * 8 + g) * 9;
+      const int k0 = 2 * t4, k2 = 2 * t4 + 8;
+      bf[nt][0] = pack2<__half>(wc[k0], wc[k0 + 1]);  // k0 + 1 <= 7
+      bf[nt][1] = pack2<__half>(k2 < 9 ? wc[k2] : 0.f, 0.f);
+    }
+    float bias[NT][2];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      bias[nt][0] = b0[cg0 + nt * 8 + 2 * t4];
+      bias[nt][1] = b0[cg0 + nt * 8 + 2 * t4 + 1];
+    }
+    auto tap = [&](int p, int k) -> float {
+      if (p >= NP || k >= 9) return 0.f;
+      const int r1 = p / F1, f1 = p % F1;
+      return melt[(2 * r1 + k / 3) * FP + 2 * f1 + k % 3];
+    };
+    for (int mt = warp; mt < MT; mt += S1_THREADS / 32) {
+      const int p0 = mt * 16 + g, p1 = p0 + 8;
+      uint32_t a[4];
+      a[0] = pack2<__half>(tap(p0, 2 * t4), tap(p0, 2 * t4 + 1));
+      a[1] = pack2<__half>(tap(p1, 2 * t4), tap(p1, 2 * t4 + 1));
+      a[2] = pack2<__half>(tap(p0, 2 * t4 + 8), tap(p0, 2 * t4 + 9));
+      a[3] = pack2<__half>(tap(p1, 2 * t4 + 8), tap(p1, 2 * t4 + 9));
+      // rows of this tile's positions outside [0, v1) are zero (stage-2 input mask)
+      const bool live0 = p0 < NP && t1_0 + p0 / F1 >= 0 && t1_0 + p0 / F1 < v1b;
+      const bool live1 = p1 < NP && t1_0 + p1 / F1 >= 0 && t1_0 + p1 / F1 < v1b;
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        mma16816_f16(acc, a, bf[nt][0], bf[nt][1]);
+        // (position, 8-channel chunk nt) at chunk slot nt ^ (f1 & 7) of the position's 128-byte row
+        if (p0 < NP) {
+          const uint32_t v = live0 ? pack2<__nv_bfloat16>(fmaxf(acc[0] + bias[nt][0], 0.f), fmaxf(acc[1] + bias[nt][1], 0.f)) : 0u;
+          *reinterpret_cast<uint32_t*>(s1 + (size_t)p0 * (S1_CG * 2) + ((nt ^ ((p0 % F1) & 7)) << 4) + 4 * t4) = v;
+        }
+        if (p1 < NP) {
+          const uint32_t v = live1 ? pack2<__nv_bfloat16>(fmaxf(acc[2] + bias[nt][0], 0.f), fmaxf(acc[3] + bias[nt][1], 0.f)) : 0u;
+          *reinterpret_cast<uint32_t*>(s1 + (size_t)p1 * (S1_CG * 2) + ((nt ^ ((p1 % F1) & 7)) << 4) + 4 * t4) = v;
+        }
+      }
+    }
+  }
+  __syncthreads();
+
+  // 3. depthwise 3x3 s2 p1 + bias: thread = 8 channels (chunk ch) of positions
+  //    (frame tt, f2) = pos, pos + 32, ...
+  const int ch = tid & 7;
+  const int c = cg0 + ch * 8;
+  float wk[9][8], bi[8];
+#pragma unroll
+  for (int k = 0; k < 9; ++k) {
+    const float4 wa = __ldg(reinterpret_cast<const float4*>(w1 + (size_t)k * C + c));
+    const float4 wb = __ldg(reinterpret_cast<const float4*>(w1 + (size_t)k * C + c + 4));
+    wk[k][0] = wa.x; wk[k][1] = wa.y; wk[k][2] = wa.z; wk[k][3] = wa.w;
+    wk[k][4] = wb.x; wk[k][5] = wb.y; wk[k][6] = wb.z; wk[k][7] = wb.w;
+  }
+  {
+    const float4 ba = __ldg(reinterpret_cast<const float4*>(b1 + c));
+    const float4 bb = __ldg(reinterpret_cast<const float4*>(b1 + c + 4));
+    bi[0] = ba.x; bi[1] = ba.y; bi[2] = ba.z; bi[3] = ba.w; bi[4] = bb.x; bi[5] = bb.y; bi[6] = bb.z; bi[7] = bb.w;
+  }
+  __nv_bfloat16* ob = out + (size_t)t.v2_off[b] * F2 * C;
+  for (int pos = tid >> 3; pos < S1_T2 * F2; pos += S1_THREADS / 8) {
+    const int tt = pos / F2, f2 = pos % F2;
+    if (t2_0 + tt >= v2b) break;
+    float acc[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = bi[e];
+#pragma unroll
+    for (int kh = 0; kh < 3; ++kh) {
+#pragma unroll
+      for (int kw = 0; kw < 3; ++kw) {
+        const int f1 = 2 * f2 - 1 + kw;
+        if (f1 < 0 || f1 >= F1) continue;
+        const int p = (2 * tt + kh) * F1 + f1;
+        const uint4 raw = *reinterpret_cast<const uint4*>(s1 + (size_t)p * (S1_CG * 2) + ((ch ^ (f1 & 7)) << 4));
+        const __nv_bfloat16* hv = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] = fmaf(wk[kh * 3 + kw][e], __bfloat162float(hv[e]), acc[e]);
+      }
+    }
+    uint4 o;
+    o.x = pack2<__nv_bfloat16>(acc[0], acc[1]);
+    o.y = pack2<__nv_bfloat16>(acc[2], acc[3]);
+    o.z = pack2<__nv_bfloat16>(acc[4], acc[5]);
+    o.w = pack2<__nv_bfloat16>(acc[6], acc[7]);
+    *reinterpret_cast<uint4*>(ob + ((size_t)(t2_0 + tt) * F2 + f2) * C + c) = o;
+  }
+}
+
 }  // namespace
+
+size_t sub_stage1_smem(int F, int F1) {
+  return (((size_t)S1_MROWS * (F + 2) * 4 + 127) / 128) * 128 + (size_t)S1_ROWS * F1 * S1_CG * 2;
+}
+
+cudaError_t sub_stage1_launch(const float* logmel, int F, const float* w0, const float* b0, const float* w1,
+                              const float* b1, int C, __nv_bfloat16* out, int F1, const ItemTables& t,
+                              int max_v2, cudaStream_t st) {
+  if (t.B <= 0 || max_v2 <= 0) return cudaSuccess;
+  if (C % S1_CG != 0) return cudaErrorInvalidValue;
+  const size_t smem = sub_stage1_smem(F, F1);
+  const dim3 grid((max_v2 + S1_T2 - 1) / S1_T2, t.B, C / S1_CG);
+  int dev = 0;
+  cudaGetDevice(&dev);
+#define PKC_S1(FF)                                                                                   \
+  {                                                                                                  \
+    static size_t attr[64] = {};                                                                     \
+    if (attr[dev & 63] < smem) {                                                                     \
+      const cudaError_t e = cudaFuncSetAttribute(k_sub_stage1<FF>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
+      if (e != cudaSuccess) return e;                                                                \
+      attr[dev & 63] = smem;                                                                         \
+    }                                                                                                \
+    return launch_pdl(k_sub_stage1<FF>, grid, dim3(S1_THREADS), smem, st, logmel, F, w0, b0, w1, b1, C, out, t); \
+  }
+  switch (F1) {
+    case 64: PKC_S1(64)
+    case 40: PKC_S1(40)
+    default: return cudaErrorInvalidValue;
+  }
+#undef PKC_S1
+}
 
 cudaError_t sub_conv0_launch(const float* logmel, int F, const float* w, const float* b, int C,
                              __nv_bfloat16* out, int F1, const ItemTables& t, int total_v1,
