@@ -208,12 +208,19 @@ std::vector<KernelStatAcc> DeviceRunner::profile_read() {
 pkc_status DeviceRunner::gemm(const void* A, int lda, const void* B, int ldb, bool bf16, int M,
                               int N, int K, int epi, int act, float alpha, const float* bias,
                               void* out, int ldo, cudaStream_t st, const char* name,
-                              std::string& err) {
+                              std::string& err, const QWeight* qw) {
   GemmArgs a{};
   a.M = M; a.N = N; a.K = K; a.epi = epi; a.act = act; a.alpha = alpha; a.bias = bias;
   a.out = out; a.ldo = ldo; a.err = err_word_;
   prof_begin(st);
-  const cudaError_t e = gemm_launch(A, lda, B, ldb, bf16, a, st);
+  cudaError_t e;
+  if (qw && qw->type) {
+    // block-quantised weight, dequantised inside the GEMM
+    const QuantB qb{qw->type, qw->q, qw->s0, qw->s1};
+    e = gemm_launch_q(A, lda, qb, bf16, a, st);
+  } else {
+    e = gemm_launch(A, lda, B, ldb, bf16, a, st);
+  }
   const int osz = (epi == EPI_RESID_F32 || epi == EPI_STORE_F32 || epi == EPI_POWER_F32) ? 4 : 2;
   const int ncols = (epi == EPI_GLU_H || epi == EPI_POWER_F32) ? N / 2 : N;
   prof_end(st, name, 2.0 * M * N * K,
@@ -393,7 +400,7 @@ pkc_status DeviceRunner::run_encoder(const Plan& p, cudaStream_t st, std::string
   // every layer's linear_pos (no bias) in one GEMM: ptab [np, L*d], layer l at column l*d
   const int Ld = c.n_layers * d;
   PKC_ST(gemm(b_.pe, d, w_.pos_all_w, d, bf, np, Ld, d, EPI_STORE_H, ACT_NONE, 1.f, nullptr, b_.ptab, Ld,
-              st, "gemm_pos", err));
+              st, "gemm_pos", err, &w_.pos_all_q));
 
 
   const int ntiles = (int)p.attn_tiles.size() / 2;
@@ -410,19 +417,19 @@ pkc_status DeviceRunner::run_encoder(const Plan& p, cudaStream_t st, std::string
       PKC_CK(layernorm_launch(b_.x, M, d, L.ln_ff1_g, L.ln_ff1_b, b_.hbuf, bf, nullptr, nullptr, false, st), "ln");
       prof_end(st, "layernorm", 0.0, (double)M * d * (4 + hs));
     }
-    PKC_ST(gemm(b_.hbuf, d, L.ff1_w1, d, bf, M, FF, d, EPI_STORE_H, ACT_SILU, 1.f, L.ff1_b1, b_.ffh, FF, st, "gemm_ffn", err));
-    PKC_ST(gemm(b_.ffh, FF, L.ff1_w2, FF, bf, M, d, FF, EPI_RESID_F32, ACT_NONE, 0.5f, L.ff1_b2, b_.x, d, st, "gemm_ffn", err));
+    PKC_ST(gemm(b_.hbuf, d, L.ff1_w1, d, bf, M, FF, d, EPI_STORE_H, ACT_SILU, 1.f, L.ff1_b1, b_.ffh, FF, st, "gemm_ffn", err, &L.ff1_q1));
+    PKC_ST(gemm(b_.ffh, FF, L.ff1_w2, FF, bf, M, d, FF, EPI_RESID_F32, ACT_NONE, 0.5f, L.ff1_b2, b_.x, d, st, "gemm_ffn", err, &L.ff1_q2));
     // MHSA
     prof_begin(st);
     PKC_CK(layernorm_launch(b_.x, M, d, L.ln_att_g, L.ln_att_b, b_.hbuf, bf, nullptr, nullptr, false, st), "ln");
     prof_end(st, "layernorm", 0.0, (double)M * d * (4 + hs));
-    PKC_ST(gemm(b_.hbuf, d, L.qkv_w, d, bf, M, 3 * d, d, EPI_STORE_H, ACT_NONE, 1.f, L.qkv_b, b_.qkv, 3 * d, st, "gemm_qkv", err));
+    PKC_ST(gemm(b_.hbuf, d, L.qkv_w, d, bf, M, 3 * d, d, EPI_STORE_H, ACT_NONE, 1.f, L.qkv_b, b_.qkv, 3 * d, st, "gemm_qkv", err, &L.qkv_q));
     AttnArgs aa{b_.qkv, static_cast<const uint8_t*>(b_.ptab) + (size_t)li * d * 2, np, p.centre, Ld,
                 L.pos_u, L.pos_v, t_tiles, ntiles, t_v_off, t_v, b_.ctx, d, H, M, err_word_};
     prof_begin(st);
     PKC_CK(attention_launch(aa, bf, st), "attention");
     prof_end(st, "attention", attn_flops, (double)M * (3 * d + d) * hs + (double)np * d * hs);
-    PKC_ST(gemm(b_.ctx, d, L.out_w, d, bf, M, d, d, EPI_RESID_F32, ACT_NONE, 1.f, L.out_b, b_.x, d, st, "gemm_out", err));
+    PKC_ST(gemm(b_.ctx, d, L.out_w, d, bf, M, d, d, EPI_RESID_F32, ACT_NONE, 1.f, L.out_b, b_.x, d, st, "gemm_out", err, &L.out_q));
     // conv module
     prof_begin(st);
     PKC_CK(layernorm_launch(b_.x, M, d, L.ln_conv_g, L.ln_conv_b, b_.hbuf, bf, nullptr, nullptr, false, st), "ln");
@@ -437,8 +444,8 @@ pkc_status DeviceRunner::run_encoder(const Plan& p, cudaStream_t st, std::string
     prof_begin(st);
     PKC_CK(layernorm_launch(b_.x, M, d, L.ln_ff2_g, L.ln_ff2_b, b_.hbuf, bf, nullptr, nullptr, false, st), "ln");
     prof_end(st, "layernorm", 0.0, (double)M * d * (4 + hs));
-    PKC_ST(gemm(b_.hbuf, d, L.ff2_w1, d, bf, M, FF, d, EPI_STORE_H, ACT_SILU, 1.f, L.ff2_b1, b_.ffh, FF, st, "gemm_ffn", err));
-    PKC_ST(gemm(b_.ffh, FF, L.ff2_w2, FF, bf, M, d, FF, EPI_RESID_F32, ACT_NONE, 0.5f, L.ff2_b2, b_.x, d, st, "gemm_ffn", err));
+    PKC_ST(gemm(b_.hbuf, d, L.ff2_w1, d, bf, M, FF, d, EPI_STORE_H, ACT_SILU, 1.f, L.ff2_b1, b_.ffh, FF, st, "gemm_ffn", err, &L.ff2_q1));
+    PKC_ST(gemm(b_.ffh, FF, L.ff2_w2, FF, bf, M, d, FF, EPI_RESID_F32, ACT_NONE, 0.5f, L.ff2_b2, b_.x, d, st, "gemm_ffn", err, &L.ff2_q2));
     // norm_out (+ next layer's norm_feed_forward1 in the same pass)
     const bool last = li + 1 == c.n_layers;
     const LayerWeights* N = last ? nullptr : &w_.layers[li + 1];

@@ -72,7 +72,7 @@ class DeviceRunner {
   void prof_end(cudaStream_t st, const char* name, double flops, double bytes);
   pkc_status gemm(const void* A, int lda, const void* B, int ldb, bool bf16, int M, int N, int K,
                   int epi, int act, float alpha, const float* bias, void* out, int ldo,
-                  cudaStream_t st, const char* name, std::string& err);
+                  cudaStream_t st, const char* name, std::string& err, const QWeight* qw = nullptr);
 
   Config cfg_;
   int device_;

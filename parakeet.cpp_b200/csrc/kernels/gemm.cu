@@ -423,7 +423,276 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       epilogue_tile<H, EPI>(args, trow, m0 + q * 32, n0, half, sE + (warp - 2) * EPI_STAGE_BYTES);
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(buf ? acce_leader1 : acce_leader0);
+      if (lane == 0) mbar_arrive_remote_cta(buf ? acce_leader1 : acce_leader0);
+    }
+  }
+
+  pdl_trigger();
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no CTA leaves while its peer may still signal its barriers
+  if (warp == 0) tmem_dealloc_2sm(tmem, TMEM_COLS);
+}
+
+// ============================================================================
+// 2-SM variant with B dequantised inside the kernel (Q8_0 / Q4_K weights).
+// Each CTA's producer loads its 128 rows of A (TMA, completing on the pair
+// leader's stage barrier, as in k_gemm_tc2) and its 128 rows of the quantised
+// B block (TMA into a raw staging ring, completing on a local barrier). Four
+// converter warps turn the raw block into the 16-bit, 128-byte-swizzled tile
+// the MMA reads -- one B row per converter thread -- then arrive on the
+// leader's stage barrier, whose phase therefore completes when A has landed
+// in both CTAs and both CTAs' B halves are converted. The dequantisation is
+// the load-time one bit for bit: Q8_0 d*q, Q4_K (d*sc)*q - dmin*m, in f32,
+// rounded once to f16 / bf16.
+// Two rings: QSTAGES stages of {A tile, raw quantised B} loaded by TMA (deep
+// enough to cover the load latency), and QBSTAGES stages of converted B (the
+// converters run up to that many k-blocks ahead of the MMA).
+constexpr int QSTAGES = 5;
+constexpr int QBSTAGES = 3;
+constexpr int CVT_WARPS = 4;
+constexpr int QTHREADS = 64 + 32 * EPI_WARPS + 32 * CVT_WARPS;  // 448
+
+template <int QT>
+struct QLayout {
+  static constexpr int RAW_Q = QT == QT_Q8_0 ? HALF_ROWS * 64 : HALF_ROWS * 32;  // one k-block of q
+  static constexpr int RAW_S = QT == QT_Q8_0 ? 2 * HALF_ROWS * 4 : 2 * 2 * HALF_ROWS * 4;
+  static constexpr int RAW = RAW_Q + RAW_S;  // 9216 / 6144: multiples of 1024
+  static constexpr int SMEM = QSTAGES * (A2_BYTES + RAW) + QBSTAGES * B2_BYTES + EPI_WARPS * EPI_STAGE_BYTES + 768 + 1024;
+};
+
+// Dequantise row r of the CTA's raw B block (one k-block of 64 values) into
+// the swizzled 16-bit tile: 16-byte chunk c of row r at (c ^ (r & 7)).
+template <typename H, int QT>
+__device__ __forceinline__ void dequant_row(const uint8_t* raw, uint8_t* dst, int r) {
+  using QL = QLayout<QT>;
+  const float* s0 = reinterpret_cast<const float*>(raw + QL::RAW_Q);
+  uint32_t w[32];
+  if constexpr (QT == QT_Q8_0 && !is_bf16<H>::value) {
+    // row r: 64 int8 as four 16-byte chunks, 64-byte TMA swizzle: chunk c at
+    // c ^ ((r >> 1) & 3). f16 without conversion instructions: the half with
+    // bits 0x64 | (b ^ 0x80) is 1024 + b + 128 exactly, minus 1152 is b
+    // exactly, and one f16 multiply by the scale (an f16 value) rounds b * d
+    // once -- the same value as the f32 product rounded to f16.
+    const __half2 off = __float2half2_rn(1152.f);
+    const __half2 dd0 = __float2half2_rn(s0[r]), dd1 = __float2half2_rn(s0[HALF_ROWS + r]);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const uint4 v = *reinterpret_cast<const uint4*>(raw + r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
+      const uint32_t ws[4] = {v.x, v.y, v.z, v.w};
+      const __half2 dd = c < 2 ? dd0 : dd1;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint32_t lo = __byte_perm(ws[i], 0x64646464u, 0x4140) ^ 0x00800080u;
+        const uint32_t hi = __byte_perm(ws[i], 0x64646464u, 0x4342) ^ 0x00800080u;
+        const __half2 a = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&lo), off), dd);
+        const __half2 b = __hmul2(__hsub2(*reinterpret_cast<const __half2*>(&hi), off), dd);
+        w[8 * c + 2 * i] = *reinterpret_cast<const uint32_t*>(&a);
+        w[8 * c + 2 * i + 1] = *reinterpret_cast<const uint32_t*>(&b);
+      }
+    }
+  } else if constexpr (QT == QT_Q8_0) {
+    const float d0 = s0[r], d1 = s0[HALF_ROWS + r];
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      const uint4 v = *reinterpret_cast<const uint4*>(raw + r * 64 + ((c ^ ((r >> 1) & 3)) << 4));
+      const int8_t* q = reinterpret_cast<const int8_t*>(&v);
+      const float d = c < 2 ? d0 : d1;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) w[8 * c + i] = pack2<H>(d * (float)q[2 * i], d * (float)q[2 * i + 1]);
+    }
+  } else {
+    // row r: 32 bytes of nibbles (byte j = values 2j, 2j+1), 32-byte TMA
+    // swizzle: chunk c at c ^ ((r >> 2) & 1); sub-block b = values [32b, 32b+32)
+    const float* s1 = s0 + 2 * HALF_ROWS;
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+      const uint4 v = *reinterpret_cast<const uint4*>(raw + r * 32 + ((c ^ ((r >> 2) & 1)) << 4));
+      const uint8_t* q = reinterpret_cast<const uint8_t*>(&v);
+      const float ds = s0[c * HALF_ROWS + r], dm = s1[c * HALF_ROWS + r];
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        // nibble -> f32 without a conversion instruction: the float with
+        // bits 0x4B000000 | q is 2^23 + q, minus 2^23 is q exactly
+        const float qlo = __uint_as_float(0x4B000000u | (q[i] & 15u)) - 8388608.f;
+        const float qhi = __uint_as_float(0x4B000000u | (uint32_t)(q[i] >> 4)) - 8388608.f;
+        const float lo = __fsub_rn(__fmul_rn(ds, qlo), dm);
+        const float hi = __fsub_rn(__fmul_rn(ds, qhi), dm);
+        w[16 * c + i] = pack2<H>(lo, hi);
+      }
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < 8; ++c)
+    *reinterpret_cast<uint4*>(dst + r * 128 + ((c ^ (r & 7)) << 4)) = make_uint4(w[4 * c], w[4 * c + 1], w[4 * c + 2], w[4 * c + 3]);
+}
+
+template <typename H, int EPI, int QT>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
+    k_gemm_tc2q(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmQ,
+                const __grid_constant__ CUtensorMap tmS0, const __grid_constant__ CUtensorMap tmS1,
+                GemmArgs args) {
+  using QL = QLayout<QT>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem =
+      reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sA = smem;
+  uint8_t* sB = smem + QSTAGES * A2_BYTES;          // converted B ring (QBSTAGES)
+  uint8_t* sR = sB + QBSTAGES * B2_BYTES;           // raw quantised B ring (QSTAGES)
+  uint8_t* sE = sR + QSTAGES * QL::RAW;  // epilogue staging, EPI_STAGE_BYTES per epilogue warp
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sE + EPI_WARPS * EPI_STAGE_BYTES);
+  // bars: [0,S) full (leader: A bytes of both CTAs + both CTAs' converters),
+  //       [S,2S) stage empty (MMA commit + this CTA's converters),
+  //       [2S,3S) raw full (local TMA), 3S+{0,1} accumulator full,
+  //       3S+{2,3} accumulator empty, 3S+4+[0,SB) converted-B slot empty (MMA commit)
+  constexpr int S = QSTAGES;
+  constexpr int SB = QBSTAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 3 * S + 4 + SB);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1;
+  const int npairs = gridDim.x >> 1;
+  const int KB = args.K / BK;
+  const int tiles_m = (args.M + 2 * HALF_ROWS - 1) / (2 * HALF_ROWS);
+  const int n_tiles = tiles_m * (args.N / BN);
+
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&tmA);
+    prefetch_tmap(&tmQ);
+    prefetch_tmap(&tmS0);
+    if (QT == QT_Q4_K) prefetch_tmap(&tmS1);
+    for (int i = 0; i < S; ++i) {
+      mbar_init(smem_u32(&bars[i]), 1 + 2 * CVT_WARPS);
+      mbar_init(smem_u32(&bars[S + i]), 1 + CVT_WARPS);
+      mbar_init(smem_u32(&bars[2 * S + i]), 1);
+    }
+    mbar_init(smem_u32(&bars[3 * S + 0]), 1);
+    mbar_init(smem_u32(&bars[3 * S + 1]), 1);
+    mbar_init(smem_u32(&bars[3 * S + 2]), 2 * EPI_WARPS);
+    mbar_init(smem_u32(&bars[3 * S + 3]), 2 * EPI_WARPS);
+    for (int i = 0; i < SB; ++i) mbar_init(smem_u32(&bars[3 * S + 4 + i]), 1);
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 0) {
+    tmem_alloc_2sm(smem_u32(tmem_slot), TMEM_COLS);
+    tmem_relinquish_2sm();
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_wait();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---- TMA producer (both CTAs): A rows, and the raw quantised B rows
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = pair; tile < n_tiles && ok; tile += npairs) {
+        const int m0 = (tile % tiles_m) * 2 * HALF_ROWS + (int)rank * HALF_ROWS;
+        const int n0 = (tile / tiles_m) * BN + (int)rank * HALF_ROWS;
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const int s = it % S;
+          const uint32_t ph = (it / S) & 1u;
+          if (!mbar_wait(smem_u32(&bars[S + s]), ph ^ 1u, args.err, DEV_ERR_TIMEOUT_EMPTY)) {
+            ok = false;
+            break;
+          }
+          const uint32_t full_leader = mapa_shared(smem_u32(&bars[s]), 0);
+          if (leader) mbar_arrive_expect_tx(smem_u32(&bars[s]), 2 * A2_BYTES);
+          tma_load_2d_2sm(smem_u32(sA + s * A2_BYTES), &tmA, full_leader, kb * BK, m0);
+          const uint32_t rf = smem_u32(&bars[2 * S + s]);
+          uint8_t* raw = sR + s * QL::RAW;
+          mbar_arrive_expect_tx(rf, QL::RAW);
+          tma_load_2d(smem_u32(raw), &tmQ, rf, QT == QT_Q8_0 ? kb * 64 : kb * 32, n0);
+          tma_load_2d(smem_u32(raw + QL::RAW_Q), &tmS0, rf, n0, 2 * kb);
+          if (QT == QT_Q4_K) tma_load_2d(smem_u32(raw + QL::RAW_Q + 2 * HALF_ROWS * 4), &tmS1, rf, n0, 2 * kb);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ---- MMA issuer (leader CTA only)
+      constexpr uint32_t idesc = idesc_f16(2 * HALF_ROWS, BN, is_bf16<H>::value ? 1 : 0);
+      uint32_t it = 0;
+      int local = 0;
+      bool ok = true;
+      for (int tile = pair; tile < n_tiles && ok; tile += npairs, ++local) {
+        const int buf = local & 1;
+        const uint32_t use = (uint32_t)(local >> 1);
+        if (!mbar_wait(smem_u32(&bars[3 * S + 2 + buf]), (use & 1u) ^ 1u, args.err, DEV_ERR_TIMEOUT_ACCUM))
+          break;
+        tc_fence_after();
+        const uint32_t acc = tmem + (uint32_t)(buf * BN);
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const int s = it % S;
+          const uint32_t ph = (it / S) & 1u;
+          if (!mbar_wait(smem_u32(&bars[s]), ph, args.err, DEV_ERR_TIMEOUT_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const int sb = it % SB;
+          const uint64_t da = smem_desc_sw128(smem_u32(sA + s * A2_BYTES));
+          const uint64_t db = smem_desc_sw128(smem_u32(sB + sb * B2_BYTES));
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            umma_f16_2sm(acc, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          umma_commit_2sm_mc(smem_u32(&bars[S + s]), 0x3);           // A stage (both CTAs)
+          umma_commit_2sm_mc(smem_u32(&bars[3 * S + 4 + sb]), 0x3);  // converted B slot (both CTAs)
+        }
+        if (ok) umma_commit_2sm_mc(smem_u32(&bars[3 * S + buf]), 0x3);
+      }
+    }
+  } else if (warp < 2 + EPI_WARPS) {
+    // ---- epilogue warps 2..9 (both CTAs): this CTA's 128 rows of the tile
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const uint32_t acce_leader0 = mapa_shared(smem_u32(&bars[3 * S + 2]), 0);
+    const uint32_t acce_leader1 = mapa_shared(smem_u32(&bars[3 * S + 3]), 0);
+    int local = 0;
+    for (int tile = pair; tile < n_tiles; tile += npairs, ++local) {
+      const int buf = local & 1;
+      const uint32_t use = (uint32_t)(local >> 1);
+      const bool have = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars[3 * S + buf]), use & 1u, args.err,
+                                                          DEV_ERR_TIMEOUT_ACCUM) ? 1 : 0) != 0;
+      if (!have) break;
+      tc_fence_after();
+      const int m0 = (tile % tiles_m) * 2 * HALF_ROWS + (int)rank * HALF_ROWS;
+      const int n0 = (tile / tiles_m) * BN;
+      const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
+      epilogue_tile<H, EPI>(args, trow, m0 + q * 32, n0, half, sE + (warp - 2) * EPI_STAGE_BYTES);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote_cta(buf ? acce_leader1 : acce_leader0);
+    }
+  } else {
+    // ---- converter warps (both CTAs): raw quantised B rows -> 16-bit MMA tile
+    const int r = (warp - 2 - EPI_WARPS) * 32 + lane;  // B row within this CTA's half
+    uint32_t it = 0;
+    for (int tile = pair; tile < n_tiles; tile += npairs) {
+      bool ok = true;
+      for (int kb = 0; kb < KB; ++kb, ++it) {
+        const int s = it % S, sb = it % SB;
+        const uint32_t ph = (it / S) & 1u, phb = (it / SB) & 1u;
+        ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars[2 * S + s]), ph, args.err,
+                                               DEV_ERR_TIMEOUT_FULL) ? 1 : 0) != 0 &&
+             __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars[3 * S + 4 + sb]), phb ^ 1u, args.err,
+                                               DEV_ERR_TIMEOUT_EMPTY) ? 1 : 0) != 0;
+        if (!ok) break;
+        dequant_row<H, QT>(sR + s * QL::RAW, sB + sb * B2_BYTES, r);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          mbar_arrive_remote_cta(mapa_shared(smem_u32(&bars[s]), 0));  // B half ready (leader's stage)
+          mbar_arrive(smem_u32(&bars[S + s]));                      // raw stage consumed (local)
+        }
+      }
+      if (!ok) break;
     }
   }
 
@@ -517,6 +786,101 @@ static cudaError_t launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const 
   const int n_tiles = (a.N / BN) * ((a.M + BM - 1) / BM);
   const int grid = n_tiles < n_sm[dev & 63] ? n_tiles : n_sm[dev & 63];
   return launch_pdl(kern, dim3(grid), dim3(THREADS), SMEM_BYTES, st, ta, tb, a);
+}
+
+// Generic 2-D tensor map (u8 or f32 elements) for the quantised operands.
+static bool make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int esize, uint64_t inner,
+                         uint64_t outer, uint64_t stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                         CUtensorMapSwizzle sw) {
+  if (!get_encode_fn()) return false;
+  cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)outer};
+  cuuint64_t strides[1] = {(cuuint64_t)stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t es[2] = {1, 1};
+  (void)esize;
+  return g_encode(map, dt, 2, const_cast<void*>(base), dims, strides, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <typename H, int EPI, int QT>
+static cudaError_t launch_q(const CUtensorMap& ta, const CUtensorMap& tq, const CUtensorMap& t0,
+                            const CUtensorMap& t1, const GemmArgs& a, cudaStream_t st) {
+  auto kern = k_gemm_tc2q<H, EPI, QT>;
+  constexpr int smem = QLayout<QT>::SMEM;
+  static bool attr_set[64] = {};
+  static int max_pairs[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2, 1, 1);
+    cfg.blockDim = dim3(QTHREADS, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cudaLaunchAttribute at;
+    at.id = cudaLaunchAttributeClusterDimension;
+    at.val.clusterDim.x = 2; at.val.clusterDim.y = 1; at.val.clusterDim.z = 1;
+    cfg.attrs = &at;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      int sms = 0;
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      n = sms / 2;
+    }
+    max_pairs[dev & 63] = n;
+    attr_set[dev & 63] = true;
+  }
+  const int n_tiles = (a.N / BN) * ((a.M + 2 * HALF_ROWS - 1) / (2 * HALF_ROWS));
+  const int pairs = n_tiles < max_pairs[dev & 63] ? n_tiles : max_pairs[dev & 63];
+  return launch_pdl(kern, dim3(2 * pairs), dim3(QTHREADS), smem, st, ta, tq, t0, t1, a);
+}
+
+cudaError_t gemm_launch_q(const void* A, int lda, const QuantB& B, bool bf16, const GemmArgs& args,
+                          cudaStream_t st) {
+  if (args.M <= 0) return cudaSuccess;
+  if (B.type != QT_Q8_0 && B.type != QT_Q4_K) return cudaErrorInvalidValue;
+  if (args.N % BN != 0 || args.K % BK != 0 || args.K <= 0 || (lda % 8) != 0 || !B.q || !B.s0 ||
+      (B.type == QT_Q4_K && !B.s1) || (reinterpret_cast<uintptr_t>(A) & 15) ||
+      (reinterpret_cast<uintptr_t>(B.q) & 15) || (reinterpret_cast<uintptr_t>(B.s0) & 15) ||
+      (reinterpret_cast<uintptr_t>(B.s1) & 15) || (reinterpret_cast<uintptr_t>(args.bias) & 15) ||
+      (reinterpret_cast<uintptr_t>(args.out) & 15) || (args.ldo % 8) != 0)
+    return cudaErrorInvalidValue;
+  CUtensorMap ta, tq, t0, t1;
+  if (!make_tmap_kmajor(&ta, A, args.M, args.K, lda, HALF_ROWS, bf16)) return cudaErrorInvalidValue;
+  const uint64_t N = (uint64_t)args.N, K = (uint64_t)args.K;
+  if (B.type == QT_Q8_0) {
+    if (!make_tmap_2d(&tq, B.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K, N, K, 64, HALF_ROWS, CU_TENSOR_MAP_SWIZZLE_64B))
+      return cudaErrorInvalidValue;
+  } else {
+    if (!make_tmap_2d(&tq, B.q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, K / 2, N, K / 2, 32, HALF_ROWS,
+                      CU_TENSOR_MAP_SWIZZLE_32B))
+      return cudaErrorInvalidValue;
+  }
+  if (!make_tmap_2d(&t0, B.s0, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, N, K / 32, N * 4, HALF_ROWS, 2,
+                    CU_TENSOR_MAP_SWIZZLE_NONE))
+    return cudaErrorInvalidValue;
+  t1 = t0;
+  if (B.type == QT_Q4_K &&
+      !make_tmap_2d(&t1, B.s1, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, N, K / 32, N * 4, HALF_ROWS, 2,
+                    CU_TENSOR_MAP_SWIZZLE_NONE))
+    return cudaErrorInvalidValue;
+  const bool q8 = B.type == QT_Q8_0;
+  switch (args.epi) {
+#define PKC_GEMMQ_CASE(E)                                                                                     \
+  case E:                                                                                                     \
+    if (q8) return bf16 ? launch_q<__nv_bfloat16, E, QT_Q8_0>(ta, tq, t0, t1, args, st)                       \
+                    : launch_q<__half, E, QT_Q8_0>(ta, tq, t0, t1, args, st);                                 \
+    return bf16 ? launch_q<__nv_bfloat16, E, QT_Q4_K>(ta, tq, t0, t1, args, st)                               \
+                : launch_q<__half, E, QT_Q4_K>(ta, tq, t0, t1, args, st);
+    PKC_GEMMQ_CASE(EPI_STORE_H)
+    PKC_GEMMQ_CASE(EPI_RESID_F32)
+#undef PKC_GEMMQ_CASE
+    default:
+      return cudaErrorInvalidValue;
+  }
 }
 
 // PKC_GEMM_1SM=1 forces the 1-SM kernel (for A/B comparisons)

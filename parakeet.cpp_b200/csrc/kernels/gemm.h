@@ -41,6 +41,23 @@ bool make_tmap_kmajor(CUtensorMap* map, const void* base, int rows, int K, int l
 cudaError_t gemm_launch(const void* A, int lda, const void* B, int ldb, bool bf16,
                         const GemmArgs& args, cudaStream_t st);
 
+// Weights kept in their GGUF block-quantised form (repacked for TMA) and
+// dequantised inside the GEMM, between the TMA stage and the MMA:
+//   Q8_0: q int8 [N][K] (row stride K bytes), s0 = block scale d, f32 [K/32][N]
+//   Q4_K: q nibbles u8 [N][K/2] (byte j of a row: value 2j in the low nibble,
+//         2j+1 in the high one), s0 = d*sc and s1 = dmin*m of each 32-value
+//         sub-block, f32 [K/32][N]; value = s0*q - s1
+enum QuantType : int { QT_NONE = 0, QT_Q8_0 = 1, QT_Q4_K = 2 };
+struct QuantB {
+  int type;
+  const void* q;
+  const float* s0;
+  const float* s1;
+};
+// D[M,N] = A[M,K] * dequant(B)[N,K]^T; K % 64 == 0, N % 256 == 0.
+cudaError_t gemm_launch_q(const void* A, int lda, const QuantB& B, bool bf16, const GemmArgs& args,
+                          cudaStream_t st);
+
 int gemm_tile_m();
 bool gemm_2sm_enabled();
 int gemm_tile_n();

@@ -21,6 +21,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstdlib>
 #include <cstring>
 #include <functional>
 #include <thread>
@@ -117,6 +118,108 @@ bool read_h(const GgufFile& g, const std::string& name, int64_t N, int64_t K, bo
   return true;
 }
 
+// A block-quantised [N][K] weight repacked for the in-kernel dequantising GEMM
+// (layout in kernels/gemm.h, QuantB), still on the host.
+struct QHost {
+  int type = 0;                // QT_Q8_0 = 1, QT_Q4_K = 2
+  int64_t N = 0, K = 0;
+  std::vector<uint8_t> q;      // Q8_0: int8 [N][K]; Q4_K: nibbles [N][K/2]
+  std::vector<float> s0, s1;   // [K/32][N]
+};
+
+// Tensor `name` [N][K] as a QHost if the GGUF stores it as Q8_0 or Q4_K in
+// K-major rows (type stays 0 otherwise). Per-32-value factors are the ones of
+// the reference dequantisation (ggml_to_f32): Q8_0 d; Q4_K d*sc and dmin*m.
+bool read_quant(const GgufFile& g, const std::string& name, int64_t N, int64_t K, QHost& out,
+                std::string& err) {
+  out = QHost{};
+  const GgufTensor* t = g.tensor(name);
+  if (!t) { err = "missing tensor " + name; return false; }
+  if (t->nelem() != N * K || t->ne[0] != K) return true;
+  if (t->type != GT_Q8_0 && t->type != GT_Q4_K) return true;
+  if (K % 256 || N % 256) return true;
+  const size_t rb = ggml_row_bytes(t->type, K);
+  out.N = N;
+  out.K = K;
+  const int64_t nb = K / 32;
+  out.s0.assign((size_t)nb * N, 0.f);
+  if (t->type == GT_Q8_0) {
+    out.type = 1;
+    out.q.resize((size_t)N * K);
+    parallel_rows(N, [&](int64_t a, int64_t b) {
+      for (int64_t r = a; r < b; ++r) {
+        const uint8_t* row = t->data + rb * r;
+        for (int64_t j = 0; j < nb; ++j) {
+          const uint8_t* blk = row + j * 34;
+          uint16_t dh;
+          std::memcpy(&dh, blk, 2);
+          out.s0[(size_t)j * N + r] = f16_to_f32(dh);
+          std::memcpy(out.q.data() + (size_t)r * K + j * 32, blk + 2, 32);
+        }
+      }
+    });
+  } else {
+    out.type = 2;
+    out.q.resize((size_t)N * K / 2);
+    out.s1.assign((size_t)nb * N, 0.f);
+    parallel_rows(N, [&](int64_t a, int64_t b) {
+      for (int64_t r = a; r < b; ++r) {
+        const uint8_t* row = t->data + rb * r;
+        uint8_t* qr = out.q.data() + (size_t)r * (K / 2);
+        for (int64_t sb = 0; sb < K / 256; ++sb) {
+          const uint8_t* blk = row + sb * 144;
+          uint16_t dh, mh;
+          std::memcpy(&dh, blk, 2);
+          std::memcpy(&mh, blk + 2, 2);
+          const float dd = f16_to_f32(dh), dmin = f16_to_f32(mh);
+          const uint8_t* sc = blk + 4;
+          const uint8_t* qs = blk + 16;
+          uint8_t sv[8], mv[8];
+          for (int j = 0; j < 4; ++j) {
+            sv[j] = sc[j] & 63;
+            mv[j] = sc[j + 4] & 63;
+            sv[j + 4] = (uint8_t)((sc[j + 8] & 0x0F) | ((sc[j] >> 6) << 4));
+            mv[j + 4] = (uint8_t)((sc[j + 8] >> 4) | ((sc[j + 4] >> 6) << 4));
+          }
+          for (int j = 0; j < 8; ++j) {
+            const int64_t blk32 = sb * 8 + j;
+            out.s0[(size_t)blk32 * N + r] = dd * sv[j];
+            out.s1[(size_t)blk32 * N + r] = dmin * mv[j];
+          }
+          // value v of the super-block: nibble (v / 32) & 1 of byte 32 * (v / 64) + v % 32
+          for (int v = 0; v < 256; v += 2) {
+            const int q0 = (qs[32 * (v / 64) + v % 32] >> (4 * ((v / 32) & 1))) & 15;
+            const int q1 = (qs[32 * ((v + 1) / 64) + (v + 1) % 32] >> (4 * (((v + 1) / 32) & 1))) & 15;
+            qr[sb * 128 + v / 2] = (uint8_t)(q0 | (q1 << 4));
+          }
+        }
+      }
+    });
+  }
+  return true;
+}
+
+// Rows of b appended to a (same type and K).
+bool q_concat(QHost& a, const QHost& b) {
+  if (a.type == 0) { a = b; return true; }
+  if (a.type != b.type || a.K != b.K) return false;
+  const int64_t nb = a.K / 32, N = a.N + b.N;
+  a.q.insert(a.q.end(), b.q.begin(), b.q.end());
+  auto merge = [&](std::vector<float>& x, const std::vector<float>& y) {
+    if (x.empty()) return;
+    std::vector<float> m((size_t)nb * N);
+    for (int64_t j = 0; j < nb; ++j) {
+      std::memcpy(m.data() + (size_t)j * N, x.data() + (size_t)j * a.N, (size_t)a.N * 4);
+      std::memcpy(m.data() + (size_t)j * N + a.N, y.data() + (size_t)j * b.N, (size_t)b.N * 4);
+    }
+    x.swap(m);
+  };
+  merge(a.s0, b.s0);
+  merge(a.s1, b.s1);
+  a.N = N;
+  return true;
+}
+
 }  // namespace
 
 std::string read_config(const GgufFile& g, Config& c) {
@@ -184,6 +287,33 @@ std::string upload_weights(const GgufFile& g, const Config& c, DeviceWeights& w)
 
   auto put_f = [&](const std::vector<float>& v) { return as_off<float>(st.add(v.data(), v.size() * 4)); };
   auto put_h = [&](const std::vector<uint16_t>& v) { return as_off<void>(st.add(v.data(), v.size() * 2)); };
+  // PKC_DEQUANT_AT_LOAD=1: dequantise Q8_0 / Q4_K weights on the host (the
+  // earlier path, for A/B comparisons); default: keep them block-quantised
+  const char* dal = getenv("PKC_DEQUANT_AT_LOAD");
+  const bool keep_quant = !(dal && dal[0] == '1');
+  auto put_q = [&](const QHost& qh) {
+    QWeight qw;
+    qw.type = qh.type;
+    qw.q = as_off<void>(st.add(qh.q.data(), qh.q.size()));
+    qw.s0 = as_off<float>(st.add(qh.s0.data(), qh.s0.size() * 4));
+    if (!qh.s1.empty()) qw.s1 = as_off<float>(st.add(qh.s1.data(), qh.s1.size() * 4));
+    return qw;
+  };
+  // a linear weight: block-quantised form when available (qw set, returns
+  // null), else the 16-bit form
+  auto put_linear = [&](const std::string& name, int64_t N, int64_t Kd, QWeight& qw) -> void* {
+    qw = QWeight{};
+    if (keep_quant) {
+      QHost qh;
+      if (!read_quant(g, name, N, Kd, qh, err)) return nullptr;
+      if (qh.type) {
+        qw = put_q(qh);
+        return nullptr;
+      }
+    }
+    if (!read_h(g, name, N, Kd, bf, h, err)) return nullptr;
+    return put_h(h);
+  };
   auto opt_vec = [&](const std::string& name, int64_t n) -> float* {
     if (!g.tensor(name)) return nullptr;
     std::vector<float> v;
@@ -279,6 +409,8 @@ std::string upload_weights(const GgufFile& g, const Config& c, DeviceWeights& w)
   w.layers.assign(c.n_layers, LayerWeights{});
   std::vector<uint16_t> pos_all;
   pos_all.reserve((size_t)c.n_layers * d * d);
+  QHost pos_q;                // every layer's linear_pos, block-quantised alike
+  bool pos_quant = keep_quant;
   for (int li = 0; li < c.n_layers; ++li) {
     LayerWeights& L = w.layers[li];
     const std::string p = "encoder.layers." + std::to_string(li) + ".";
@@ -296,15 +428,15 @@ std::string upload_weights(const GgufFile& g, const Config& c, DeviceWeights& w)
       *ln.bb = vec(std::string(ln.nm) + ".bias", d);
       if (!*ln.gg || !*ln.bb) return err;
     }
-    struct { const char* nm; void** w1; void** w2; float** b1; float** b2; } ffs[] = {
-        {"feed_forward1", &L.ff1_w1, &L.ff1_w2, &L.ff1_b1, &L.ff1_b2},
-        {"feed_forward2", &L.ff2_w1, &L.ff2_w2, &L.ff2_b1, &L.ff2_b2}};
+    struct { const char* nm; void** w1; void** w2; float** b1; float** b2; QWeight* q1; QWeight* q2; } ffs[] = {
+        {"feed_forward1", &L.ff1_w1, &L.ff1_w2, &L.ff1_b1, &L.ff1_b2, &L.ff1_q1, &L.ff1_q2},
+        {"feed_forward2", &L.ff2_w1, &L.ff2_w2, &L.ff2_b1, &L.ff2_b2, &L.ff2_q1, &L.ff2_q2}};
     for (auto& ff : ffs) {
       const std::string n = p + ff.nm;
-      if (!read_h(g, n + ".linear1.weight", FF, d, bf, h, err)) return err;
-      *ff.w1 = put_h(h);
-      if (!read_h(g, n + ".linear2.weight", d, FF, bf, h, err)) return err;
-      *ff.w2 = put_h(h);
+      *ff.w1 = put_linear(n + ".linear1.weight", FF, d, *ff.q1);
+      if (!err.empty()) return err;
+      *ff.w2 = put_linear(n + ".linear2.weight", d, FF, *ff.q2);
+      if (!err.empty()) return err;
       *ff.b1 = opt_vec(n + ".linear1.bias", FF);
       *ff.b2 = opt_vec(n + ".linear2.bias", d);
       if (!err.empty()) return err;
@@ -315,23 +447,40 @@ std::string upload_weights(const GgufFile& g, const Config& c, DeviceWeights& w)
       const char* nms[3] = {"linear_q", "linear_k", "linear_v"};
       std::vector<float> bq((size_t)3 * d, 0.f);
       bool any_b = false;
+      // q, k and v block-quantised alike: one quantised [3d, d] weight
+      QHost qcat;
+      bool all_q = keep_quant;
+      for (int i = 0; i < 3 && all_q; ++i) {
+        QHost qi;
+        if (!read_quant(g, a + nms[i] + ".weight", d, d, qi, err)) return err;
+        all_q = qi.type != 0 && q_concat(qcat, qi);
+      }
+      L.qkv_q = QWeight{};
+      if (all_q) L.qkv_q = put_q(qcat);
       for (int i = 0; i < 3; ++i) {
+        if (all_q) break;
         if (!read_h(g, a + nms[i] + ".weight", d, d, bf, h, err)) return err;
         std::memcpy(qkv.data() + (size_t)i * d * d, h.data(), (size_t)d * d * 2);
+      }
+      for (int i = 0; i < 3; ++i)
         if (g.tensor(a + nms[i] + ".bias")) {
           if (!read_vec(g, a + nms[i] + ".bias", d, f, err)) return err;
           std::memcpy(bq.data() + (size_t)i * d, f.data(), (size_t)d * 4);
           any_b = true;
         }
-      }
-      L.qkv_w = put_h(qkv);
+      L.qkv_w = all_q ? nullptr : put_h(qkv);
       L.qkv_b = any_b ? put_f(bq) : nullptr;
     }
-    if (!read_h(g, a + "linear_pos.weight", d, d, bf, h, err)) return err;
-    pos_all.insert(pos_all.end(), h.begin(), h.end());
+    {
+      QHost qp;
+      if (pos_quant && !read_quant(g, a + "linear_pos.weight", d, d, qp, err)) return err;
+      pos_quant = pos_quant && qp.type != 0 && q_concat(pos_q, qp);
+      if (!read_h(g, a + "linear_pos.weight", d, d, bf, h, err)) return err;
+      pos_all.insert(pos_all.end(), h.begin(), h.end());
+    }
     L.pos_w = nullptr;
-    if (!read_h(g, a + "linear_out.weight", d, d, bf, h, err)) return err;
-    L.out_w = put_h(h);
+    L.out_w = put_linear(a + "linear_out.weight", d, d, L.out_q);
+    if (!err.empty()) return err;
     L.out_b = opt_vec(a + "linear_out.bias", d);
     if (!err.empty()) return err;
     L.pos_u = vec("self_attn.pos_bias_u", d);
@@ -379,7 +528,13 @@ std::string upload_weights(const GgufFile& g, const Config& c, DeviceWeights& w)
     }
   }
 
-  w.pos_all_w = put_h(pos_all);
+  w.pos_all_q = QWeight{};
+  if (pos_quant && pos_q.type) {
+    w.pos_all_q = put_q(pos_q);
+    w.pos_all_w = nullptr;
+  } else {
+    w.pos_all_w = put_h(pos_all);
+  }
   pos_all.clear();
   pos_all.shrink_to_fit();
 
@@ -400,6 +555,11 @@ std::string upload_weights(const GgufFile& g, const Config& c, DeviceWeights& w)
   reloc(w.dw1_w, base); reloc(w.dw1_b, base); reloc(w.dw2_w, base); reloc(w.dw2_b, base);
   reloc(w.pw1_w, base); reloc(w.pw2_w, base); reloc(w.pw1_b, base); reloc(w.pw2_b, base);
   reloc(w.out_w, base); reloc(w.out_b, base); reloc(w.pos_all_w, base);
+  auto reloc_q = [&](QWeight& qw) {
+    if (!qw.type) return;
+    reloc(qw.q, base); reloc(qw.s0, base); reloc(qw.s1, base);
+  };
+  reloc_q(w.pos_all_q);
   for (LayerWeights& L : w.layers) {
     float** fp[] = {&L.ln_ff1_g, &L.ln_ff1_b, &L.ln_att_g, &L.ln_att_b, &L.ln_conv_g, &L.ln_conv_b,
                     &L.ln_ff2_g, &L.ln_ff2_b, &L.ln_out_g, &L.ln_out_b, &L.ff1_b1, &L.ff1_b2,
@@ -409,6 +569,7 @@ std::string upload_weights(const GgufFile& g, const Config& c, DeviceWeights& w)
     void** vp[] = {&L.ff1_w1, &L.ff1_w2, &L.ff2_w1, &L.ff2_w2, &L.qkv_w, &L.pos_w, &L.out_w,
                    &L.pw1_w, &L.pw2_w};
     for (void** q : vp) reloc(*q, base);
+    for (QWeight* q : {&L.ff1_q1, &L.ff1_q2, &L.ff2_q1, &L.ff2_q2, &L.qkv_q, &L.out_q}) reloc_q(*q);
   }
   return "";
 }

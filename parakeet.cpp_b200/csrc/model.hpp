@@ -35,6 +35,15 @@ struct Config {
 // else the reason the model cannot run on this library.
 std::string read_config(const GgufFile& g, Config& c);
 
+// A linear weight [N][K] kept in its GGUF block format, repacked for TMA
+// (layout in kernels/gemm.h, QuantB). type 0 = absent.
+struct QWeight {
+  int type = 0;
+  void* q = nullptr;
+  float* s0 = nullptr;
+  float* s1 = nullptr;
+};
+
 struct LayerWeights {
   float *ln_ff1_g, *ln_ff1_b, *ln_att_g, *ln_att_b, *ln_conv_g, *ln_conv_b;
   float *ln_ff2_g, *ln_ff2_b, *ln_out_g, *ln_out_b;
@@ -53,6 +62,9 @@ struct LayerWeights {
   float *bn_scale, *bn_shift;                        // [d]
   void* pw2_w;                                       // [d, d]
   float* pw2_b;
+  // block-quantised forms (QT_Q8_0 / QT_Q4_K, dequantised inside the GEMM);
+  // when set, the matching 16-bit weight above is null
+  QWeight ff1_q1, ff1_q2, ff2_q1, ff2_q2, qkv_q, out_q;
 };
 
 struct DeviceWeights {
@@ -74,6 +86,7 @@ struct DeviceWeights {
   void* out_w;                    // bf16 [d, F3*C] (columns f*C + c)
   float* out_b;
   void* pos_all_w = nullptr;      // [L*d, d]: every layer's linear_pos, one GEMM per batch
+  QWeight pos_all_q;              // its block-quantised form, when every layer's linear_pos is
   std::vector<LayerWeights> layers;
 };
 

@@ -142,3 +142,26 @@ def test_bad_arguments(opened):
     with pytest.raises(pkc.PkcError) as e:
         m.encode_batch(mel, [50])
     assert e.value.status == 1
+
+
+@pytest.mark.parametrize("kind", ["q8_0", "q4_k"])
+def test_in_kernel_dequant_equals_load_time_dequant(models, kind, monkeypatch):
+    """Q8_0 / Q4_K weights dequantised inside the GEMM (the default) give the
+    same encoder output, bit for bit, as weights dequantised once on the host
+    at load (PKC_DEQUANT_AT_LOAD=1): same per-value arithmetic (d*q, or
+    (d*sc)*q - dmin*m in f32 rounded once) and the same MMA order."""
+    import pkc
+    pcm = clips([SR * 3 + 11, SR + 400, 5000], seed=7)
+    m = pkc.Model(models[kind])
+    try:
+        inkernel = m.encode_pcm_batch(pcm)
+    finally:
+        m.close()
+    monkeypatch.setenv("PKC_DEQUANT_AT_LOAD", "1")
+    m = pkc.Model(models[kind])
+    try:
+        atload = m.encode_pcm_batch(pcm)
+    finally:
+        m.close()
+    for a, b in zip(inkernel, atload):
+        np.testing.assert_array_equal(a, b)
