@@ -159,6 +159,29 @@ pkc_status pkc_gemm(const void* A, int lda, const void* Bw, int ldb, int M, int 
                     int dtype, int epi, int act, float alpha, const float* bias, void* out,
                     int ldo, void* stream);
 
+/* x[M,N] += alpha * (A[M,K] * B[N,K]^T + bias) in f32 (the residual update of
+   the encoder's FFN-down, attention-out and pointwise-conv-2 GEMMs), and, if
+   stats is not null, the per-row statistics of the updated x in 128-column
+   chunks: stats[(m * (N/128) + c) * 2 + {0,1}] = (mean, sum of squared
+   deviations) of x[m, 128c .. 128c+127]. No counterpart in the reference (its
+   graph keeps ggml_add and ggml_norm as separate nodes, src/encoder.cpp). */
+pkc_status pkc_gemm_resid_stats(const void* A, int lda, const void* Bw, int ldb, int M, int N, int K,
+                                int dtype, float alpha, const float* bias, float* x, int ldx,
+                                float* stats, void* stream);
+
+/* out = xhat * Bw[N,K]^T + bias with a fused epilogue, xhat = (x - mean) *
+   rstd per row (ggml_norm: population variance over K, eps 1e-5) computed
+   while the A operand is staged. With Bw = W diag(gamma) and bias = W beta + b
+   this is LayerNorm(x; gamma, beta) * W^T + b, the pre-norm + linear of the
+   reference's MHSA / conv / FFN blocks (src/encoder.cpp: ggml_norm ->
+   ggml_mul -> ggml_add -> ggml_mul_mat); the encoder folds gamma / beta that
+   way when it loads the weights. x f32 [M, ldx]; stats as written by
+   pkc_gemm_resid_stats for the same x (N there = K here); K a multiple of
+   128. epi 0 (store) or 3 (GLU); act as in pkc_gemm. */
+pkc_status pkc_gemm_ln(const float* x, int ldx, const float* stats, const void* Bw, int ldb, int M,
+                       int N, int K, int dtype, int epi, int act, const float* bias, void* out, int ldo,
+                       void* stream);
+
 /* Relative-position attention of one layer for B utterances packed along
    rows (item b owns rows [off_b, off_b + len[b])). qkv [M, 3d] and ptab
    [2*centre-1, d] in the compute type (dtype 0 f16, 1 bf16), bias_u/v [d] f32,

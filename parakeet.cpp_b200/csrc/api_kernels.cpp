@@ -62,6 +62,57 @@ extern "C" pkc_status pkc_gemm(const void* A, int lda, const void* Bw, int ldb, 
   return PKC_OK;
 }
 
+// launch, then read and clear the device error word
+static pkc_status finish_kernel_call(cudaError_t e, int* err, cudaStream_t st, const char* what) {
+  if (e != cudaSuccess) return pkc::set_thread_error(PKC_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+  int h_err = 0;
+  if (cudaMemcpyAsync(&h_err, err, sizeof(int), cudaMemcpyDeviceToHost, st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess)
+    return pkc::set_thread_error(PKC_ERR_CUDA, std::string(what) + ": synchronize failed");
+  if (h_err != 0) {
+    cudaMemsetAsync(err, 0, sizeof(int), st);
+    cudaStreamSynchronize(st);
+    return pkc::set_thread_error(PKC_ERR_KERNEL, std::string(what) + ": kernel error word " + std::to_string(h_err));
+  }
+  return PKC_OK;
+}
+
+extern "C" pkc_status pkc_gemm_resid_stats(const void* A, int lda, const void* Bw, int ldb, int M, int N,
+                                           int K, int dtype, float alpha, const float* bias, float* x,
+                                           int ldx, float* stats, void* stream) {
+  if (!A || !Bw || !x || M < 0 || N <= 0 || K <= 0 || (dtype != 0 && dtype != 1) || N % 128 != 0)
+    return pkc::set_thread_error(PKC_ERR_ARG, "pkc_gemm_resid_stats: bad arguments");
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int* err = dev_err_word(dev);
+  if (!err) return pkc::set_thread_error(PKC_ERR_CUDA, "pkc_gemm_resid_stats: error word allocation failed");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  pkc::GemmArgs a{};
+  a.M = M; a.N = N; a.K = K;
+  a.epi = pkc::EPI_RESID_F32; a.act = pkc::ACT_NONE; a.alpha = alpha; a.bias = bias;
+  a.out = x; a.ldo = ldx; a.err = err; a.stats = stats;
+  return finish_kernel_call(pkc::gemm_launch(A, lda, Bw, ldb, dtype == 1, a, st), err, st, "pkc_gemm_resid_stats");
+}
+
+extern "C" pkc_status pkc_gemm_ln(const float* x, int ldx, const float* stats, const void* Bw, int ldb, int M,
+                                  int N, int K, int dtype, int epi, int act, const float* bias, void* out, int ldo,
+                                  void* stream) {
+  if (!x || !stats || !Bw || !out || M < 0 || N <= 0 || K <= 0 ||
+      (dtype != 0 && dtype != 1) || (epi != pkc::EPI_STORE_H && epi != pkc::EPI_GLU_H))
+    return pkc::set_thread_error(PKC_ERR_ARG, "pkc_gemm_ln: bad arguments");
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int* err = dev_err_word(dev);
+  if (!err) return pkc::set_thread_error(PKC_ERR_CUDA, "pkc_gemm_ln: error word allocation failed");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  pkc::GemmArgs a{};
+  a.M = M; a.N = N; a.K = K;
+  a.epi = epi; a.act = act; a.alpha = 1.f; a.bias = bias;
+  a.out = out; a.ldo = ldo; a.err = err;
+  const pkc::LnA la{x, ldx, stats};
+  return finish_kernel_call(pkc::gemm_launch_ln(la, Bw, ldb, dtype == 1, a, st), err, st, "pkc_gemm_ln");
+}
+
 extern "C" int pkc_abi_version(void) { return PKC_ABI_VERSION; }
 
 extern "C" pkc_status pkc_relpos_attention(const void* qkv, const void* ptab, int centre,

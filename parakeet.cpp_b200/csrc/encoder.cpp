@@ -109,7 +109,15 @@ std::string DeviceRunner::init(const GgufFile& g) {
   // conv.0 map in memory (A/B comparisons); the default is the fused kernel
   const char* su = getenv("PKC_SUB_UNFUSED");
   sub_unfused_ = (su && su[0] == '1') || (cfg_.F1 != 64 && cfg_.F1 != 40);
-  return upload_weights(g, cfg_, w_);
+  // PKC_LN_FUSED=1: the QKV / pointwise-1 / FFN2-up GEMMs normalise their A
+  // operand themselves (k_gemm_tc2ln). Off by default: the f32 rows it stages
+  // through shared memory add ~80 KB of shared-memory traffic per CTA and
+  // k-block to a mainloop that the plain GEMM already runs at the
+  // shared-memory port's rate, so it is slower than the separate LayerNorm
+  // kernel at the encoder's shapes.
+  const char* lf = getenv("PKC_LN_FUSED");
+  ln_unfused_ = !(lf && lf[0] == '1') || cfg_.d_model % 128 != 0;
+  return upload_weights(g, cfg_, w_, !ln_unfused_);
 }
 
 bool DeviceRunner::ensure_ws(size_t bytes) {
@@ -208,10 +216,10 @@ std::vector<KernelStatAcc> DeviceRunner::profile_read() {
 pkc_status DeviceRunner::gemm(const void* A, int lda, const void* B, int ldb, bool bf16, int M,
                               int N, int K, int epi, int act, float alpha, const float* bias,
                               void* out, int ldo, cudaStream_t st, const char* name,
-                              std::string& err, const QWeight* qw) {
+                              std::string& err, const QWeight* qw, float* stats) {
   GemmArgs a{};
   a.M = M; a.N = N; a.K = K; a.epi = epi; a.act = act; a.alpha = alpha; a.bias = bias;
-  a.out = out; a.ldo = ldo; a.err = err_word_;
+  a.out = out; a.ldo = ldo; a.err = err_word_; a.stats = stats;
   prof_begin(st);
   cudaError_t e;
   if (qw && qw->type) {
@@ -227,6 +235,25 @@ pkc_status DeviceRunner::gemm(const void* A, int lda, const void* B, int ldb, bo
            2.0 * ((double)M * K + (double)N * K) + (double)M * ncols * osz * (epi == EPI_RESID_F32 ? 2 : 1));
   if (e != cudaSuccess) {
     err = std::string("GEMM ") + name + " launch failed: " + cudaGetErrorString(e);
+    return PKC_ERR_CUDA;
+  }
+  return PKC_OK;
+}
+
+pkc_status DeviceRunner::gemm_ln(const float* x, const float* stats, const void* B, bool bf16, int M, int N, int K, int epi, int act,
+                                 const float* bias, void* out, int ldo, cudaStream_t st, const char* name,
+                                 std::string& err) {
+  GemmArgs a{};
+  a.M = M; a.N = N; a.K = K; a.epi = epi; a.act = act; a.alpha = 1.f; a.bias = bias;
+  a.out = out; a.ldo = ldo; a.err = err_word_;
+  const LnA la{x, K, stats};
+  prof_begin(st);
+  const cudaError_t e = gemm_launch_ln(la, B, K, bf16, a, st);
+  const int ncols = epi == EPI_GLU_H ? N / 2 : N;
+  prof_end(st, name, 2.0 * M * N * K,
+           4.0 * M * K + (double)M * (K / 128) * 8 + 2.0 * N * K + 2.0 * M * ncols);
+  if (e != cudaSuccess) {
+    err = std::string("GEMM ") + name + " (LayerNorm fused) launch failed: " + cudaGetErrorString(e);
     return PKC_ERR_CUDA;
   }
   return PKC_OK;
@@ -284,6 +311,7 @@ pkc_status DeviceRunner::prepare(const Plan& p, cudaStream_t st, std::string& er
   const size_t o_pe = take((size_t)np * d * hs);
   const size_t o_pt = take((size_t)np * d * c.n_layers * hs);
   const size_t o_out = take((size_t)p.M * d * 4);
+  const size_t o_st = take(ln_unfused_ ? 0 : (size_t)p.M * (d / 128) * 8);
   if (!ensure_ws(sz)) {
     err = "workspace allocation of " + std::to_string(sz) + " bytes failed";
     return PKC_ERR_OOM;
@@ -301,6 +329,7 @@ pkc_status DeviceRunner::prepare(const Plan& p, cudaStream_t st, std::string& er
   b_.hbuf = base + o_h; b_.ffh = base + o_ff; b_.qkv = base + o_qkv; b_.ctx = base + o_ctx;
   b_.pe = base + o_pe; b_.ptab = base + o_pt;
   b_.out = reinterpret_cast<float*>(base + o_out);
+  b_.stats = ln_unfused_ ? nullptr : reinterpret_cast<float*>(base + o_st);
 
   // item tables -> pinned staging -> device (one copy)
   if (h_tables_cap_ < n_tab) {
@@ -418,33 +447,54 @@ pkc_status DeviceRunner::run_encoder(const Plan& p, cudaStream_t st, std::string
       prof_end(st, "layernorm", 0.0, (double)M * d * (4 + hs));
     }
     PKC_ST(gemm(b_.hbuf, d, L.ff1_w1, d, bf, M, FF, d, EPI_STORE_H, ACT_SILU, 1.f, L.ff1_b1, b_.ffh, FF, st, "gemm_ffn", err, &L.ff1_q1));
-    PKC_ST(gemm(b_.ffh, FF, L.ff1_w2, FF, bf, M, d, FF, EPI_RESID_F32, ACT_NONE, 0.5f, L.ff1_b2, b_.x, d, st, "gemm_ffn", err, &L.ff1_q2));
+    // LayerNorm inside the consuming GEMM when its weight is dense: the GEMM
+    // that updates x before it also writes x's per-128-column row statistics
+    const bool lnq = L.qkv_ln, lnc = L.pw1_ln, lnf = L.ff2_ln;
+    PKC_ST(gemm(b_.ffh, FF, L.ff1_w2, FF, bf, M, d, FF, EPI_RESID_F32, ACT_NONE, 0.5f, L.ff1_b2, b_.x, d, st, "gemm_ffn", err, &L.ff1_q2,
+                lnq ? b_.stats : nullptr));
     // MHSA
-    prof_begin(st);
-    PKC_CK(layernorm_launch(b_.x, M, d, L.ln_att_g, L.ln_att_b, b_.hbuf, bf, nullptr, nullptr, false, st), "ln");
-    prof_end(st, "layernorm", 0.0, (double)M * d * (4 + hs));
-    PKC_ST(gemm(b_.hbuf, d, L.qkv_w, d, bf, M, 3 * d, d, EPI_STORE_H, ACT_NONE, 1.f, L.qkv_b, b_.qkv, 3 * d, st, "gemm_qkv", err, &L.qkv_q));
+    if (lnq) {
+      PKC_ST(gemm_ln(b_.x, b_.stats, L.qkv_w, bf, M, 3 * d, d, EPI_STORE_H, ACT_NONE, L.qkv_b,
+                     b_.qkv, 3 * d, st, "gemm_qkv", err));
+    } else {
+      prof_begin(st);
+      PKC_CK(layernorm_launch(b_.x, M, d, L.ln_att_g, L.ln_att_b, b_.hbuf, bf, nullptr, nullptr, false, st), "ln");
+      prof_end(st, "layernorm", 0.0, (double)M * d * (4 + hs));
+      PKC_ST(gemm(b_.hbuf, d, L.qkv_w, d, bf, M, 3 * d, d, EPI_STORE_H, ACT_NONE, 1.f, L.qkv_b, b_.qkv, 3 * d, st, "gemm_qkv", err, &L.qkv_q));
+    }
     AttnArgs aa{b_.qkv, static_cast<const uint8_t*>(b_.ptab) + (size_t)li * d * 2, np, p.centre, Ld,
                 L.pos_u, L.pos_v, t_tiles, ntiles, t_v_off, t_v, b_.ctx, d, H, M, err_word_};
     prof_begin(st);
     PKC_CK(attention_launch(aa, bf, st), "attention");
     prof_end(st, "attention", attn_flops, (double)M * (3 * d + d) * hs + (double)np * d * hs);
-    PKC_ST(gemm(b_.ctx, d, L.out_w, d, bf, M, d, d, EPI_RESID_F32, ACT_NONE, 1.f, L.out_b, b_.x, d, st, "gemm_out", err, &L.out_q));
+    PKC_ST(gemm(b_.ctx, d, L.out_w, d, bf, M, d, d, EPI_RESID_F32, ACT_NONE, 1.f, L.out_b, b_.x, d, st, "gemm_out", err, &L.out_q,
+                lnc ? b_.stats : nullptr));
     // conv module
-    prof_begin(st);
-    PKC_CK(layernorm_launch(b_.x, M, d, L.ln_conv_g, L.ln_conv_b, b_.hbuf, bf, nullptr, nullptr, false, st), "ln");
-    prof_end(st, "layernorm", 0.0, (double)M * d * (4 + hs));
-    PKC_ST(gemm(b_.hbuf, d, L.pw1_w, d, bf, M, 2 * d, d, EPI_GLU_H, ACT_NONE, 1.f, L.pw1_b, b_.ctx, d, st, "gemm_pw1_glu", err));
+    if (lnc) {
+      PKC_ST(gemm_ln(b_.x, b_.stats, L.pw1_w, bf, M, 2 * d, d, EPI_GLU_H, ACT_NONE, L.pw1_b,
+                     b_.ctx, d, st, "gemm_pw1_glu", err));
+    } else {
+      prof_begin(st);
+      PKC_CK(layernorm_launch(b_.x, M, d, L.ln_conv_g, L.ln_conv_b, b_.hbuf, bf, nullptr, nullptr, false, st), "ln");
+      prof_end(st, "layernorm", 0.0, (double)M * d * (4 + hs));
+      PKC_ST(gemm(b_.hbuf, d, L.pw1_w, d, bf, M, 2 * d, d, EPI_GLU_H, ACT_NONE, 1.f, L.pw1_b, b_.ctx, d, st, "gemm_pw1_glu", err));
+    }
     prof_begin(st);
     PKC_CK(dwconv_bn_silu_launch(b_.ctx, b_.hbuf, d, K, L.dw_w, L.dw_b, L.bn_scale, L.bn_shift, t_v_off,
                                  t_v, p.B, p.max_v, bf, st), "dwconv");
     prof_end(st, "dwconv", 2.0 * M * d * K, (double)M * d * hs * 2);
-    PKC_ST(gemm(b_.hbuf, d, L.pw2_w, d, bf, M, d, d, EPI_RESID_F32, ACT_NONE, 1.f, L.pw2_b, b_.x, d, st, "gemm_pw2", err));
+    PKC_ST(gemm(b_.hbuf, d, L.pw2_w, d, bf, M, d, d, EPI_RESID_F32, ACT_NONE, 1.f, L.pw2_b, b_.x, d, st, "gemm_pw2", err, nullptr,
+                lnf ? b_.stats : nullptr));
     // FFN2
-    prof_begin(st);
-    PKC_CK(layernorm_launch(b_.x, M, d, L.ln_ff2_g, L.ln_ff2_b, b_.hbuf, bf, nullptr, nullptr, false, st), "ln");
-    prof_end(st, "layernorm", 0.0, (double)M * d * (4 + hs));
-    PKC_ST(gemm(b_.hbuf, d, L.ff2_w1, d, bf, M, FF, d, EPI_STORE_H, ACT_SILU, 1.f, L.ff2_b1, b_.ffh, FF, st, "gemm_ffn", err, &L.ff2_q1));
+    if (lnf) {
+      PKC_ST(gemm_ln(b_.x, b_.stats, L.ff2_w1, bf, M, FF, d, EPI_STORE_H, ACT_SILU, L.ff2_b1,
+                     b_.ffh, FF, st, "gemm_ffn", err));
+    } else {
+      prof_begin(st);
+      PKC_CK(layernorm_launch(b_.x, M, d, L.ln_ff2_g, L.ln_ff2_b, b_.hbuf, bf, nullptr, nullptr, false, st), "ln");
+      prof_end(st, "layernorm", 0.0, (double)M * d * (4 + hs));
+      PKC_ST(gemm(b_.hbuf, d, L.ff2_w1, d, bf, M, FF, d, EPI_STORE_H, ACT_SILU, 1.f, L.ff2_b1, b_.ffh, FF, st, "gemm_ffn", err, &L.ff2_q1));
+    }
     PKC_ST(gemm(b_.ffh, FF, L.ff2_w2, FF, bf, M, d, FF, EPI_RESID_F32, ACT_NONE, 0.5f, L.ff2_b2, b_.x, d, st, "gemm_ffn", err, &L.ff2_q2));
     // norm_out (+ next layer's norm_feed_forward1 in the same pass)
     const bool last = li + 1 == c.n_layers;

@@ -72,7 +72,14 @@ class DeviceRunner {
   void prof_end(cudaStream_t st, const char* name, double flops, double bytes);
   pkc_status gemm(const void* A, int lda, const void* B, int ldb, bool bf16, int M, int N, int K,
                   int epi, int act, float alpha, const float* bias, void* out, int ldo,
-                  cudaStream_t st, const char* name, std::string& err, const QWeight* qw = nullptr);
+                  cudaStream_t st, const char* name, std::string& err, const QWeight* qw = nullptr,
+                  float* stats = nullptr);
+  // D = xhat * B^T + bias, xhat = (x - mean) * rstd per row computed while
+  // the A operand is staged (B and bias carry the LayerNorm's gamma / beta);
+  // stats are x's per-128-column (mean, M2) partials
+  pkc_status gemm_ln(const float* x, const float* stats, const void* B, bool bf16,
+                     int M, int N, int K, int epi, int act, const float* bias, void* out, int ldo, cudaStream_t st,
+                     const char* name, std::string& err);
 
   Config cfg_;
   int device_;
@@ -82,6 +89,7 @@ class DeviceRunner {
   size_t ws_bytes_ = 0;
   int* err_word_ = nullptr;
   bool sub_unfused_ = false;
+  bool ln_unfused_ = false;
   int* h_tables_ = nullptr;  // pinned staging for the item tables
   size_t h_tables_cap_ = 0;
   // carved workspace pointers for the current plan
@@ -90,7 +98,7 @@ class DeviceRunner {
     float* melbatch = nullptr; void* s1 = nullptr; void* s2a = nullptr; void* s2b = nullptr;
     void* s3a = nullptr; void* s3b = nullptr; float* x = nullptr; void* hbuf = nullptr;
     void* ffh = nullptr; void* qkv = nullptr; void* pe = nullptr; void* ptab = nullptr;
-    void* ctx = nullptr; float* out = nullptr; int* tables = nullptr;
+    void* ctx = nullptr; float* out = nullptr; int* tables = nullptr; float* stats = nullptr;
   } b_;
   // device table pointers for the current plan
   int *t_pcm_off, *t_S, *t_mel_off, *t_Tm, *t_mval, *t_v1_off, *t_v1, *t_v2_off, *t_v2, *t_v_off,

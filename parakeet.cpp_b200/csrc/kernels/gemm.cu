@@ -54,6 +54,9 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t tro
   const int j1 = PAIRED ? j0 + BN / 128 : j0 + BN / 64;
   const int oc0 = PAIRED ? n0 / 2 : n0;  // output column of chunk 0
   float4 cur[8], nxt[8];
+  // EPI_RESID_F32 with stats: lane (rr, cc) merges row 4 * cc + rr's chunk
+  // statistics over this half's 128 columns (Chan's update, equal counts)
+  float run_mean = 0.f, run_m2 = 0.f;
   auto row_ok = [&](int k) { return row0 + 4 * k + rr < args.M; };
   auto resid = [&](int j, int k) {
     return reinterpret_cast<float4*>(reinterpret_cast<float*>(args.out) + (size_t)(row0 + 4 * k + rr) * args.ldo +
@@ -118,16 +121,44 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t tro
       asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
                    : "=f"(w.x), "=f"(w.y), "=f"(w.z), "=f"(w.w)
                    : "r"(sst + rl * 128 + ((cc ^ (rl & 7)) << 4)));
-      if (!row_ok(k)) continue;
+      const bool okr = row_ok(k);
       const size_t ro = (size_t)(row0 + rl) * args.ldo + oc;
       if constexpr (EPI == EPI_RESID_F32) {
-        float4 o = cur[k];
+        float4 o = okr ? cur[k] : make_float4(0.f, 0.f, 0.f, 0.f);
         o.x += args.alpha * (w.x + b4.x);
         o.y += args.alpha * (w.y + b4.y);
         o.z += args.alpha * (w.z + b4.z);
         o.w += args.alpha * (w.w + b4.w);
-        *reinterpret_cast<float4*>(reinterpret_cast<float*>(args.out) + ro) = o;
-      } else if constexpr (EPI == EPI_STORE_F32) {
+        if (okr) *reinterpret_cast<float4*>(reinterpret_cast<float*>(args.out) + ro) = o;
+        if (args.stats) {
+          // this chunk's 32 values of the row sit in the 8 lanes with the same rr
+          float sum = (o.x + o.y) + (o.z + o.w);
+          sum += __shfl_xor_sync(0xffffffffu, sum, 1);
+          sum += __shfl_xor_sync(0xffffffffu, sum, 2);
+          sum += __shfl_xor_sync(0xffffffffu, sum, 4);
+          const float mc = sum * (1.0f / 32.0f);
+          const float d0 = o.x - mc, d1 = o.y - mc, d2 = o.z - mc, d3 = o.w - mc;
+          float q = (d0 * d0 + d1 * d1) + (d2 * d2 + d3 * d3);
+          q += __shfl_xor_sync(0xffffffffu, q, 1);
+          q += __shfl_xor_sync(0xffffffffu, q, 2);
+          q += __shfl_xor_sync(0xffffffffu, q, 4);
+          if (cc == k) {
+            const int jj = j - j0;
+            if (jj == 0) {
+              run_mean = mc;
+              run_m2 = q;
+            } else {
+              const float dl = mc - run_mean;
+              const float inv = 1.0f / (float)(jj + 1);
+              run_mean += dl * inv;
+              run_m2 += q + dl * dl * (32.0f * (float)jj * inv);
+            }
+          }
+        }
+        continue;
+      }
+      if (!okr) continue;
+      if constexpr (EPI == EPI_STORE_F32) {
         *reinterpret_cast<float4*>(reinterpret_cast<float*>(args.out) + ro) =
             make_float4(args.alpha * (w.x + b4.x), args.alpha * (w.y + b4.y), args.alpha * (w.z + b4.z),
                         args.alpha * (w.w + b4.w));
@@ -151,6 +182,12 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t tro
 #pragma unroll
       for (int k = 0; k < 8; ++k) cur[k] = nxt[k];
     }
+  }
+  if constexpr (EPI == EPI_RESID_F32) {
+    const int rl = 4 * cc + rr;
+    if (args.stats && row0 + rl < args.M)
+      *reinterpret_cast<float2*>(args.stats + ((size_t)(row0 + rl) * (args.N / 128) + (oc0 + 32 * j0) / 128) * 2) =
+          make_float2(run_mean, run_m2);
   }
 }
 
@@ -703,6 +740,266 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
   if (warp == 0) tmem_dealloc_2sm(tmem, TMEM_COLS);
 }
 
+// ============================================================================
+// 2-SM variant with the LayerNorm fused into the A operand: D = xhat * B^T,
+// xhat = (X - mean) * rstd per row. X (the f32 residual stream) is
+// TMA-loaded into a raw ring of [128 rows x 32 columns] boxes; four converter
+// warps per CTA compute xhat -- mean and rstd of each row merged from the
+// per-128-column (mean, M2) partials that the GEMM which produced X wrote
+// (EPI_RESID_F32 with stats) -- and write the 16-bit, 128-byte-swizzled A
+// tile, one row per converter thread; B comes by TMA as in k_gemm_tc2. The
+// LayerNorm's gamma and beta are folded into B and the bias when the weights
+// are loaded. No normalised copy of X goes to memory.
+// Raw boxes are released by the converters as soon as they are in registers;
+// the B stage and the converted A slot of k-block `it` share index
+// it % LSTAGES and are released together by the MMA's commit.
+// Cost: per CTA and k-block the raw f32 rows add 32 KB of TMA writes, 32 KB of
+// converter reads and 16 KB of converter writes to shared memory, on top of
+// the 64 KB (TMA in, tensor-core reads) that the plain kernel already moves at
+// about the port's rate; measured at M=3277, N=3072, K=1024 it runs one
+// k-block per ~1.7k cycles against ~0.55k for k_gemm_tc2, with the MMA waiting
+// on the converters. It is therefore opt-in in the encoder.
+constexpr int LSTAGES = 4;                        // B stages = converted A slots
+constexpr int LRSTAGES = 4;                       // raw X boxes (two per k-block)
+constexpr int LRAW = HALF_ROWS * 32 * 4;          // one [128 x 32] f32 box
+constexpr int LSMEM = LRSTAGES * LRAW + LSTAGES * (B2_BYTES + A2_BYTES) + EPI_WARPS * EPI_STAGE_BYTES + 768 + 1024;
+
+struct LnParams {
+  const float* stats;   // [M][K/128][2]
+};
+
+template <typename H, int EPI>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
+    k_gemm_tc2ln(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmB, LnParams lp,
+                 GemmArgs args) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem =
+      reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sR = smem;                                 // raw X boxes
+  uint8_t* sB = sR + LRSTAGES * LRAW;                 // B stages
+  uint8_t* sA = sB + LSTAGES * B2_BYTES;              // converted A slots
+  uint8_t* sE = sA + LSTAGES * A2_BYTES;              // epilogue staging
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sE + EPI_WARPS * EPI_STAGE_BYTES);
+  // bars: [0,S) full (leader: B bytes of both CTAs + both CTAs' converters),
+  //       [S,2S) empty (MMA commit: B stage and A slot), [2S,2S+R) raw full,
+  //       [2S+R,2S+2R) raw empty (this CTA's converters),
+  //       ACC+{0,1} accumulator full, ACC+{2,3} accumulator empty
+  constexpr int S = LSTAGES;
+  constexpr int R = LRSTAGES;
+  constexpr int ACC = 2 * S + 2 * R;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + ACC + 4);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1;
+  const int npairs = gridDim.x >> 1;
+  const int KB = args.K / BK;
+  const int tiles_m = (args.M + 2 * HALF_ROWS - 1) / (2 * HALF_ROWS);
+  const int n_tiles = tiles_m * (args.N / BN);
+
+  if (threadIdx.x == 0) {
+    prefetch_tmap(&tmX);
+    prefetch_tmap(&tmB);
+    for (int i = 0; i < S; ++i) {
+      mbar_init(smem_u32(&bars[i]), 1 + 2 * CVT_WARPS);
+      mbar_init(smem_u32(&bars[S + i]), 1);
+    }
+    for (int i = 0; i < R; ++i) {
+      mbar_init(smem_u32(&bars[2 * S + i]), 1);
+      mbar_init(smem_u32(&bars[2 * S + R + i]), CVT_WARPS);
+    }
+    mbar_init(smem_u32(&bars[ACC + 0]), 1);
+    mbar_init(smem_u32(&bars[ACC + 1]), 1);
+    mbar_init(smem_u32(&bars[ACC + 2]), 2 * EPI_WARPS);
+    mbar_init(smem_u32(&bars[ACC + 3]), 2 * EPI_WARPS);
+    fence_barrier_init();
+    fence_proxy_async_smem();
+  }
+  if (warp == 0) {
+    tmem_alloc_2sm(smem_u32(tmem_slot), TMEM_COLS);
+    tmem_relinquish_2sm();
+  }
+  tc_fence_before();
+  cluster_sync();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  pdl_wait();
+
+  if (warp == 0) {
+    if (lane == 0) {
+      // ---- TMA producer (both CTAs): this CTA's B half and raw X rows
+      uint32_t it = 0;
+      bool ok = true;
+      for (int tile = pair; tile < n_tiles && ok; tile += npairs) {
+        const int m0 = (tile % tiles_m) * 2 * HALF_ROWS + (int)rank * HALF_ROWS;
+        const int n0 = (tile / tiles_m) * BN + (int)rank * HALF_ROWS;
+        for (int kb = 0; kb < KB && ok; ++kb, ++it) {
+          const int s = it % S;
+          if (!mbar_wait(smem_u32(&bars[S + s]), ((it / S) & 1u) ^ 1u, args.err, DEV_ERR_TIMEOUT_EMPTY)) {
+            ok = false;
+            break;
+          }
+          const uint32_t full_leader = mapa_shared(smem_u32(&bars[s]), 0);
+          if (leader) mbar_arrive_expect_tx(smem_u32(&bars[s]), 2 * B2_BYTES);
+          tma_load_2d_2sm(smem_u32(sB + s * B2_BYTES), &tmB, full_leader, kb * BK, n0);
+          for (int h = 0; h < 2; ++h) {
+            const uint32_t q = 2 * it + (uint32_t)h;
+            const int r = q % R;
+            if (!mbar_wait(smem_u32(&bars[2 * S + R + r]), ((q / R) & 1u) ^ 1u, args.err, DEV_ERR_TIMEOUT_EMPTY)) {
+              ok = false;
+              break;
+            }
+            const uint32_t rf = smem_u32(&bars[2 * S + r]);
+            mbar_arrive_expect_tx(rf, LRAW);
+            tma_load_2d(smem_u32(sR + r * LRAW), &tmX, rf, kb * BK + 32 * h, m0);
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && leader) {
+      // ---- MMA issuer (leader CTA only)
+      constexpr uint32_t idesc = idesc_f16(2 * HALF_ROWS, BN, is_bf16<H>::value ? 1 : 0);
+      uint32_t it = 0;
+      int local = 0;
+      bool ok = true;
+      for (int tile = pair; tile < n_tiles && ok; tile += npairs, ++local) {
+        const int buf = local & 1;
+        const uint32_t use = (uint32_t)(local >> 1);
+        if (!mbar_wait(smem_u32(&bars[ACC + 2 + buf]), (use & 1u) ^ 1u, args.err, DEV_ERR_TIMEOUT_ACCUM))
+          break;
+        tc_fence_after();
+        const uint32_t acc = tmem + (uint32_t)(buf * BN);
+        for (int kb = 0; kb < KB; ++kb, ++it) {
+          const int s = it % S;
+          if (!mbar_wait(smem_u32(&bars[s]), (it / S) & 1u, args.err, DEV_ERR_TIMEOUT_FULL)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t da = smem_desc_sw128(smem_u32(sA + s * A2_BYTES));
+          const uint64_t db = smem_desc_sw128(smem_u32(sB + s * B2_BYTES));
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            umma_f16_2sm(acc, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc, (kb > 0 || k > 0) ? 1u : 0u);
+          umma_commit_2sm_mc(smem_u32(&bars[S + s]), 0x3);  // B stage + A slot free (both CTAs)
+        }
+        if (ok) umma_commit_2sm_mc(smem_u32(&bars[ACC + buf]), 0x3);
+      }
+    }
+  } else if (warp < 2 + EPI_WARPS) {
+    // ---- epilogue warps 2..9 (both CTAs): this CTA's 128 rows of the tile
+    const int q = warp & 3;
+    const int half = (warp - 2) >> 2;
+    const uint32_t acce_leader0 = mapa_shared(smem_u32(&bars[ACC + 2]), 0);
+    const uint32_t acce_leader1 = mapa_shared(smem_u32(&bars[ACC + 3]), 0);
+    int local = 0;
+    for (int tile = pair; tile < n_tiles; tile += npairs, ++local) {
+      const int buf = local & 1;
+      const uint32_t use = (uint32_t)(local >> 1);
+      const bool have = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars[ACC + buf]), use & 1u, args.err,
+                                                          DEV_ERR_TIMEOUT_ACCUM) ? 1 : 0) != 0;
+      if (!have) break;
+      tc_fence_after();
+      const int m0 = (tile % tiles_m) * 2 * HALF_ROWS + (int)rank * HALF_ROWS;
+      const int n0 = (tile / tiles_m) * BN;
+      const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
+      epilogue_tile<H, EPI>(args, trow, m0 + q * 32, n0, half, sE + (warp - 2) * EPI_STAGE_BYTES);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_remote_cta(buf ? acce_leader1 : acce_leader0);
+    }
+  } else {
+    // ---- converter warps (both CTAs): raw X row -> xhat, 16-bit A row
+    const int r = (warp - 2 - EPI_WARPS) * 32 + lane;  // A row within this CTA's 128
+    const int nchunk = args.K / 128;
+    uint32_t it = 0;
+    bool ok = true;
+    for (int tile = pair; tile < n_tiles && ok; tile += npairs) {
+      // mean / rstd of this row (ggml_norm: population variance, eps 1e-5),
+      // merged from its equal-size 128-column partials
+      const int grow = (tile % tiles_m) * 2 * HALF_ROWS + (int)rank * HALF_ROWS + r;
+      float mean = 0.f, rstd = 0.f;
+      if (grow < args.M) {
+        const float2* st2 = reinterpret_cast<const float2*>(lp.stats) + (size_t)grow * nchunk;
+        float m2 = 0.f;
+        for (int c0 = 0; c0 < nchunk; c0 += 8) {
+          float2 v[8];
+#pragma unroll
+          for (int u = 0; u < 8; ++u) v[u] = c0 + u < nchunk ? __ldg(st2 + c0 + u) : make_float2(0.f, 0.f);
+#pragma unroll
+          for (int u = 0; u < 8; ++u) {
+            const int c = c0 + u;
+            if (c == 0) {
+              mean = v[u].x;
+              m2 = v[u].y;
+            } else if (c < nchunk) {
+              const float dl = v[u].x - mean;
+              const float inv = 1.0f / (float)(c + 1);
+              mean += dl * inv;
+              m2 += v[u].y + dl * dl * (128.0f * (float)c * inv);
+            }
+          }
+        }
+        rstd = 1.0f / sqrtf(m2 / (float)args.K + 1e-5f);
+      }
+      const float nmr = -mean * rstd;  // xhat = fma(x, rstd, nmr)
+      // the next tile's row statistics into L1 while this tile streams
+      {
+        const int nrow = ((tile + npairs) % tiles_m) * 2 * HALF_ROWS + (int)rank * HALF_ROWS + r;
+        if (tile + npairs < n_tiles && nrow < args.M) {
+          const char* p = reinterpret_cast<const char*>(lp.stats + (size_t)nrow * nchunk * 2);
+          for (int o = 0; o < nchunk * 8; o += 128) asm volatile("prefetch.global.L1 [%0];" ::"l"(p + o));
+        }
+      }
+      for (int kb = 0; kb < KB; ++kb, ++it) {
+        const int s = it % S;
+        ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars[S + s]), ((it / S) & 1u) ^ 1u, args.err,
+                                               DEV_ERR_TIMEOUT_EMPTY) ? 1 : 0) != 0;
+        if (!ok) break;
+        uint8_t* dst = sA + s * A2_BYTES + r * 128;
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const uint32_t qb = 2 * it + (uint32_t)h;
+          const int rb = qb % R;
+          ok = __all_sync(0xffffffffu, mbar_wait(smem_u32(&bars[2 * S + rb]), (qb / R) & 1u, args.err,
+                                                 DEV_ERR_TIMEOUT_FULL) ? 1 : 0) != 0;
+          if (!ok) break;
+          // row r of the box: 16-byte chunk c (columns 4c..4c+3) at (c ^ (r & 7))
+          const uint8_t* raw = sR + rb * LRAW + r * 128;
+          float4 x[8];
+#pragma unroll
+          for (int c = 0; c < 8; ++c) x[c] = *reinterpret_cast<const float4*>(raw + ((c ^ (r & 7)) << 4));
+          __syncwarp();
+          if (lane == 0) mbar_arrive(smem_u32(&bars[2 * S + R + rb]));  // box consumed
+#pragma unroll
+          for (int c2 = 0; c2 < 4; ++c2) {
+            const float4 a = x[2 * c2], b = x[2 * c2 + 1];
+            // 16-byte chunk (4h + c2) of the 128-byte A row (8 halves)
+            *reinterpret_cast<uint4*>(dst + (((4 * h + c2) ^ (r & 7)) << 4)) =
+                make_uint4(pack2<H>(fmaf(a.x, rstd, nmr), fmaf(a.y, rstd, nmr)),
+                           pack2<H>(fmaf(a.z, rstd, nmr), fmaf(a.w, rstd, nmr)),
+                           pack2<H>(fmaf(b.x, rstd, nmr), fmaf(b.y, rstd, nmr)),
+                           pack2<H>(fmaf(b.z, rstd, nmr), fmaf(b.w, rstd, nmr)));
+          }
+        }
+        if (!ok) break;
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_remote_cta(mapa_shared(smem_u32(&bars[s]), 0));  // A half ready
+      }
+    }
+  }
+
+  pdl_trigger();
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no CTA leaves while its peer may still signal its barriers
+  if (warp == 0) tmem_dealloc_2sm(tmem, TMEM_COLS);
+}
+
 }  // namespace
 
 // ------------------------------------------------------------------ host side
@@ -878,6 +1175,67 @@ cudaError_t gemm_launch_q(const void* A, int lda, const QuantB& B, bool bf16, co
     PKC_GEMMQ_CASE(EPI_STORE_H)
     PKC_GEMMQ_CASE(EPI_RESID_F32)
 #undef PKC_GEMMQ_CASE
+    default:
+      return cudaErrorInvalidValue;
+  }
+}
+
+template <typename H, int EPI>
+static cudaError_t launch_ln(const CUtensorMap& tx, const CUtensorMap& tb, const LnParams& lp, const GemmArgs& a,
+                             cudaStream_t st) {
+  auto kern = k_gemm_tc2ln<H, EPI>;
+  static bool attr_set[64] = {};
+  static int max_pairs[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, LSMEM);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2, 1, 1);
+    cfg.blockDim = dim3(QTHREADS, 1, 1);
+    cfg.dynamicSmemBytes = LSMEM;
+    cudaLaunchAttribute at;
+    at.id = cudaLaunchAttributeClusterDimension;
+    at.val.clusterDim.x = 2; at.val.clusterDim.y = 1; at.val.clusterDim.z = 1;
+    cfg.attrs = &at;
+    cfg.numAttrs = 1;
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      int sms = 0;
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      n = sms / 2;
+    }
+    max_pairs[dev & 63] = n;
+    attr_set[dev & 63] = true;
+  }
+  const int n_tiles = (a.N / BN) * ((a.M + 2 * HALF_ROWS - 1) / (2 * HALF_ROWS));
+  const int pairs = n_tiles < max_pairs[dev & 63] ? n_tiles : max_pairs[dev & 63];
+  return launch_pdl(kern, dim3(2 * pairs), dim3(QTHREADS), LSMEM, st, tx, tb, lp, a);
+}
+
+cudaError_t gemm_launch_ln(const LnA& A, const void* B, int ldb, bool bf16, const GemmArgs& args,
+                           cudaStream_t st) {
+  if (args.M <= 0) return cudaSuccess;
+  if (args.N % BN != 0 || args.K % 128 != 0 || args.K <= 0 || (A.ldx % 4) != 0 || (ldb % 8) != 0 || !A.x ||
+      !A.stats || (reinterpret_cast<uintptr_t>(A.x) & 15) || (reinterpret_cast<uintptr_t>(A.stats) & 7) || (reinterpret_cast<uintptr_t>(B) & 15) ||
+      (reinterpret_cast<uintptr_t>(args.bias) & 15) || (reinterpret_cast<uintptr_t>(args.out) & 15) ||
+      (args.ldo % 8) != 0)
+    return cudaErrorInvalidValue;
+  CUtensorMap tx, tb;
+  if (!make_tmap_2d(&tx, A.x, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, (uint64_t)args.K, (uint64_t)args.M,
+                    (uint64_t)A.ldx * 4, 32, HALF_ROWS, CU_TENSOR_MAP_SWIZZLE_128B))
+    return cudaErrorInvalidValue;
+  if (!make_tmap_kmajor(&tb, B, args.N, args.K, ldb, HALF_ROWS, bf16)) return cudaErrorInvalidValue;
+  const LnParams lp{A.stats};
+  switch (args.epi) {
+#define PKC_GEMMLN_CASE(E)                                                                                   \
+  case E:                                                                                                    \
+    return bf16 ? launch_ln<__nv_bfloat16, E>(tx, tb, lp, args, st) : launch_ln<__half, E>(tx, tb, lp, args, st);
+    PKC_GEMMLN_CASE(EPI_STORE_H)
+    PKC_GEMMLN_CASE(EPI_GLU_H)
+#undef PKC_GEMMLN_CASE
     default:
       return cudaErrorInvalidValue;
   }

@@ -23,6 +23,11 @@ struct GemmArgs {
   void* out;          // output base (h or f32 per epilogue)
   int ldo;            // output row stride in elements
   int* err;           // device error word
+  // EPI_RESID_F32 only, may be null: per-row statistics of the updated rows,
+  // (mean, M2 = sum of squared deviations) of every 128-column chunk, f32
+  // [M][N/128][2] -- what a LayerNorm of those rows needs, merged by the
+  // consumer (gemm_launch_ln)
+  float* stats;
 };
 
 typedef CUresult (*PFN_encodeTiled_t)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
@@ -57,6 +62,19 @@ struct QuantB {
 // D[M,N] = A[M,K] * dequant(B)[N,K]^T; K % 64 == 0, N % 256 == 0.
 cudaError_t gemm_launch_q(const void* A, int lda, const QuantB& B, bool bf16, const GemmArgs& args,
                           cudaStream_t st);
+
+// D[M,N] = xhat[M,K] * B[N,K]^T with xhat = (X - mean) * rstd per row
+// (ggml_norm: population variance, eps 1e-5), computed while A is staged for
+// the MMA: X f32 [M, K] (row stride ldx), stats from the EPI_RESID_F32 GEMM
+// that produced X. The LayerNorm's gamma / beta are expected folded into B
+// (columns scaled by gamma) and the bias (+ B * beta). Dense B only.
+struct LnA {
+  const float* x;
+  int ldx;
+  const float* stats;  // [M][K/128][2]
+};
+cudaError_t gemm_launch_ln(const LnA& A, const void* B, int ldb, bool bf16, const GemmArgs& args,
+                           cudaStream_t st);
 
 int gemm_tile_m();
 bool gemm_2sm_enabled();

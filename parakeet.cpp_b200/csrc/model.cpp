@@ -277,7 +277,24 @@ std::string read_config(const GgufFile& g, Config& c) {
   return "";
 }
 
-std::string upload_weights(const GgufFile& g, const Config& c, DeviceWeights& w) {
+// LayerNorm affine folded into the following linear layer:
+//   (xhat * gamma + beta) W^T + b = xhat (W diag(gamma))^T + (W beta + b)
+// W [N, K] f32 in place; bias [N] (created if the layer had none).
+static void fold_layernorm(std::vector<float>& W, int64_t N, int64_t K, const std::vector<float>& gamma,
+                           const std::vector<float>& beta, std::vector<float>& bias) {
+  if (bias.empty()) bias.assign((size_t)N, 0.f);
+  for (int64_t n = 0; n < N; ++n) {
+    float* row = W.data() + (size_t)n * K;
+    double acc = bias[(size_t)n];
+    for (int64_t k = 0; k < K; ++k) {
+      acc += (double)row[k] * (double)beta[(size_t)k];
+      row[k] *= gamma[(size_t)k];
+    }
+    bias[(size_t)n] = (float)acc;
+  }
+}
+
+std::string upload_weights(const GgufFile& g, const Config& c, DeviceWeights& w, bool fold_ln) {
   std::string err;
   Staging st;
   const int d = c.d_model, FF = c.ff_dim, C = c.sub_channels, K = c.conv_kernel, H = c.n_heads;
@@ -423,15 +440,18 @@ std::string upload_weights(const GgufFile& g, const Config& c, DeviceWeights& w)
         {"norm_feed_forward1", &L.ln_ff1_g, &L.ln_ff1_b}, {"norm_self_att", &L.ln_att_g, &L.ln_att_b},
         {"norm_conv", &L.ln_conv_g, &L.ln_conv_b}, {"norm_feed_forward2", &L.ln_ff2_g, &L.ln_ff2_b},
         {"norm_out", &L.ln_out_g, &L.ln_out_b}};
-    for (auto& ln : lns) {
-      *ln.gg = vec(std::string(ln.nm) + ".weight", d);
-      *ln.bb = vec(std::string(ln.nm) + ".bias", d);
-      if (!*ln.gg || !*ln.bb) return err;
+    std::vector<float> lng[5], lnb[5];  // host copies (gamma / beta of each norm)
+    for (int i = 0; i < 5; ++i) {
+      const std::string nm = p + lns[i].nm;
+      if (!read_vec(g, nm + ".weight", d, lng[i], err) || !read_vec(g, nm + ".bias", d, lnb[i], err)) return err;
+      *lns[i].gg = put_f(lng[i]);
+      *lns[i].bb = put_f(lnb[i]);
     }
     struct { const char* nm; void** w1; void** w2; float** b1; float** b2; QWeight* q1; QWeight* q2; } ffs[] = {
         {"feed_forward1", &L.ff1_w1, &L.ff1_w2, &L.ff1_b1, &L.ff1_b2, &L.ff1_q1, &L.ff1_q2},
         {"feed_forward2", &L.ff2_w1, &L.ff2_w2, &L.ff2_b1, &L.ff2_b2, &L.ff2_q1, &L.ff2_q2}};
-    for (auto& ff : ffs) {
+    for (int fi = 0; fi < 2; ++fi) {
+      auto& ff = ffs[fi];
       const std::string n = p + ff.nm;
       *ff.w1 = put_linear(n + ".linear1.weight", FF, d, *ff.q1);
       if (!err.empty()) return err;
@@ -440,6 +460,16 @@ std::string upload_weights(const GgufFile& g, const Config& c, DeviceWeights& w)
       *ff.b1 = opt_vec(n + ".linear1.bias", FF);
       *ff.b2 = opt_vec(n + ".linear2.bias", d);
       if (!err.empty()) return err;
+      if (fi == 1 && fold_ln && !ff.q1->type) {
+        // FFN2's linear1 takes norm_feed_forward2 folded in
+        std::vector<float> b1;
+        if (g.tensor(n + ".linear1.bias") && !read_vec(g, n + ".linear1.bias", FF, b1, err)) return err;
+        if (!read_f32(g, n + ".linear1.weight", FF, d, f, err)) return err;
+        fold_layernorm(f, FF, d, lng[3], lnb[3], b1);
+        *ff.w1 = put_h(to_h(f, bf));
+        *ff.b1 = put_f(b1);
+        L.ff2_ln = true;
+      }
     }
     const std::string a = p + "self_attn.";
     {
@@ -457,17 +487,30 @@ std::string upload_weights(const GgufFile& g, const Config& c, DeviceWeights& w)
       }
       L.qkv_q = QWeight{};
       if (all_q) L.qkv_q = put_q(qcat);
-      for (int i = 0; i < 3; ++i) {
-        if (all_q) break;
-        if (!read_h(g, a + nms[i] + ".weight", d, d, bf, h, err)) return err;
-        std::memcpy(qkv.data() + (size_t)i * d * d, h.data(), (size_t)d * d * 2);
-      }
       for (int i = 0; i < 3; ++i)
         if (g.tensor(a + nms[i] + ".bias")) {
           if (!read_vec(g, a + nms[i] + ".bias", d, f, err)) return err;
           std::memcpy(bq.data() + (size_t)i * d, f.data(), (size_t)d * 4);
           any_b = true;
         }
+      if (!all_q && fold_ln) {
+        // norm_self_att folded into the [3d, d] weight and its bias
+        std::vector<float> wq((size_t)3 * d * d);
+        for (int i = 0; i < 3; ++i) {
+          if (!read_f32(g, a + nms[i] + ".weight", d, d, f, err)) return err;
+          std::memcpy(wq.data() + (size_t)i * d * d, f.data(), (size_t)d * d * 4);
+        }
+        fold_layernorm(wq, 3 * d, d, lng[1], lnb[1], bq);
+        qkv = to_h(wq, bf);
+        any_b = true;
+        L.qkv_ln = true;
+      } else {
+        for (int i = 0; i < 3; ++i) {
+          if (all_q) break;
+          if (!read_h(g, a + nms[i] + ".weight", d, d, bf, h, err)) return err;
+          std::memcpy(qkv.data() + (size_t)i * d * d, h.data(), (size_t)d * d * 2);
+        }
+      }
       L.qkv_w = all_q ? nullptr : put_h(qkv);
       L.qkv_b = any_b ? put_f(bq) : nullptr;
     }
@@ -500,8 +543,13 @@ std::string upload_weights(const GgufFile& g, const Config& c, DeviceWeights& w)
         std::memcpy(paired.data() + (size_t)n * d, f.data() + (size_t)src * d, (size_t)d * 4);
         if (has_b) pb[n] = f2[src];
       }
+      if (fold_ln) {
+        // norm_conv folded into pointwise_conv1 (rows already GLU-paired)
+        fold_layernorm(paired, 2 * d, d, lng[2], lnb[2], pb);
+        L.pw1_ln = true;
+      }
       L.pw1_w = put_h(to_h(paired, bf));
-      L.pw1_b = has_b ? put_f(pb) : nullptr;
+      L.pw1_b = (has_b || fold_ln) ? put_f(pb) : nullptr;
       if (!read_f32(g, p + "conv.depthwise_conv.weight", d, K, f, err)) return err;
       std::vector<float> tap((size_t)K * d);
       for (int ch = 0; ch < d; ++ch)

@@ -65,6 +65,9 @@ struct LayerWeights {
   // block-quantised forms (QT_Q8_0 / QT_Q4_K, dequantised inside the GEMM);
   // when set, the matching 16-bit weight above is null
   QWeight ff1_q1, ff1_q2, ff2_q1, ff2_q2, qkv_q, out_q;
+  // the preceding LayerNorm's gamma folded into the weight's columns and
+  // W * beta into its bias (the GEMM then normalises its A operand itself)
+  bool qkv_ln = false, pw1_ln = false, ff2_ln = false;
 };
 
 struct DeviceWeights {
@@ -92,7 +95,9 @@ struct DeviceWeights {
 
 // Upload every encoder weight of `g` to the current CUDA device.
 // Returns an empty string on success, else an error message.
-std::string upload_weights(const GgufFile& g, const Config& c, DeviceWeights& w);
+// fold_ln: fold the pre-norm LayerNorms' gamma / beta into the dense QKV,
+// pointwise-conv-1 and FFN2-up weights / biases (for the LayerNorm-fused GEMM)
+std::string upload_weights(const GgufFile& g, const Config& c, DeviceWeights& w, bool fold_ln);
 void free_weights(DeviceWeights& w);
 
 }  // namespace pkc

@@ -98,6 +98,10 @@ def _declare(L):
         ("pkc_model_stream", c_void_p, c_void_p, c_int),
         ("pkc_profile_read", c_int, c_void_p, POINTER(KernelStat), c_int),
         ("pkc_shard_plan", c_int, POINTER(c_int), c_int, c_int, c_int, POINTER(c_int)),
+        ("pkc_gemm_resid_stats", c_int, c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int, c_int,
+         c_float, c_void_p, c_void_p, c_int, c_void_p, c_void_p),
+        ("pkc_gemm_ln", c_int, c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
+         c_int, c_int, c_void_p, c_void_p, c_int, c_void_p),
         ("pkc_relpos_attention", c_int, c_void_p, c_void_p, c_int, c_void_p, c_void_p, POINTER(c_int),
          c_int, c_int, c_int, c_int, c_void_p, c_void_p),
         ("pkc_relpos_attention_noalloc", c_int, c_void_p, c_void_p, c_int, c_void_p, c_void_p,
@@ -125,6 +129,26 @@ def gemm(A, B, M, N, K, *, bf16, epi, act=ACT_NONE, alpha=1.0, bias=None, out, l
     _check(lib().pkc_gemm(c_void_p(A), lda or K, c_void_p(B), ldb or K, M, N, K, 1 if bf16 else 0,
                           epi, act, alpha, c_void_p(bias) if bias else None, c_void_p(out), ldo,
                           c_void_p(stream) if stream else None))
+
+
+def gemm_resid_stats(A, B, M, N, K, *, bf16, alpha=1.0, bias=None, x, ldx=None, stats=None,
+                     lda=None, ldb=None, stream=0):
+    """x[M,N] += alpha * (A * B^T + bias) in f32, plus x's per-128-column row
+    statistics (mean, M2) into stats [M, N/128, 2] when given (device pointers)."""
+    _check(lib().pkc_gemm_resid_stats(c_void_p(A), lda or K, c_void_p(B), ldb or K, M, N, K,
+                                      1 if bf16 else 0, alpha, c_void_p(bias) if bias else None,
+                                      c_void_p(x), ldx or N, c_void_p(stats) if stats else None,
+                                      c_void_p(stream) if stream else None))
+
+
+def gemm_ln(x, stats, B, M, N, K, *, bf16, epi=EPI_STORE_H, act=ACT_NONE, bias=None, out, ldo, ldx=None,
+            ldb=None, stream=0):
+    """out = xhat * B^T + bias, xhat = (x - mean) * rstd per row computed
+    while the GEMM stages its A operand; a LayerNorm's gamma / beta go into B
+    (B = W diag(gamma)) and the bias (W beta + b). Device pointers as ints."""
+    _check(lib().pkc_gemm_ln(c_void_p(x), ldx or K, c_void_p(stats), c_void_p(B), ldb or K, M, N, K,
+                             1 if bf16 else 0, epi, act, c_void_p(bias) if bias else None, c_void_p(out), ldo,
+                             c_void_p(stream) if stream else None))
 
 
 def relpos_attention(qkv, ptab, centre, bias_u, bias_v, lens, d, n_heads, *, bf16, ctx, stream=0):

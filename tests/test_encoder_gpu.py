@@ -165,3 +165,31 @@ def test_in_kernel_dequant_equals_load_time_dequant(models, kind, monkeypatch):
         m.close()
     for a, b in zip(inkernel, atload):
         np.testing.assert_array_equal(a, b)
+
+
+@pytest.mark.parametrize("kind", ["f16", "bf16", "q8_0"])
+def test_fused_layernorm_matches_separate_layernorm(models, oracles, kind, monkeypatch):
+    """The pre-norm LayerNorms applied inside the QKV / pointwise-1 / FFN2-up
+    GEMMs (PKC_LN_FUSED=1: gamma / beta folded into the weights at load, row
+    statistics from the residual GEMM's epilogue) and as separate kernels (the
+    default) both stay within the oracle bound and agree well inside it. With
+    q8_0 weights only pointwise-1 (dense) takes the fused form."""
+    import pkc
+    pcm = clips([SR * 2 + 123, 7000, SR + 1], seed=21)
+    m = pkc.Model(models[kind])
+    try:
+        sep = m.encode_pcm_batch(pcm)
+    finally:
+        m.close()
+    monkeypatch.setenv("PKC_LN_FUSED", "1")
+    m = pkc.Model(models[kind])
+    try:
+        fused = m.encode_pcm_batch(pcm)
+    finally:
+        m.close()
+    import oracle
+    ref = oracle.encode_pcm_batch(oracles(kind), pcm)
+    for a, b, r in zip(fused, sep, ref.outs):
+        assert rel_err(a, r.T) < 2e-2
+        assert rel_err(b, r.T) < 2e-2
+        assert rel_err(a, b) < 1e-2

@@ -126,3 +126,97 @@ def test_one_sm_and_two_sm_kernels_agree(cuda):
     torch.cuda.synchronize()
     err = (out - (ref + bias)).abs().max().item() / ref.abs().max().item()
     assert err < 1e-4, err
+
+
+def _chunk_stats(x):
+    """per-row (mean, sum of squared deviations) of each 128-column chunk"""
+    import torch
+    M, N = x.shape
+    c = x.view(M, N // 128, 128)
+    mean = c.mean(dim=2)
+    m2 = ((c - mean[..., None]) ** 2).sum(dim=2)
+    return torch.stack([mean, m2], dim=-1)
+
+
+@pytest.mark.parametrize("M,N,K", [(333, 1024, 2048), (1, 512, 256), (4099, 1024, 4096), (129, 256, 128)])
+def test_resid_stats(cuda, M, N, K):
+    """The residual GEMM's epilogue also writes the updated rows' statistics
+    per 128-column chunk (the input of the LayerNorm fused into the next GEMM)."""
+    import torch
+    import pkc
+    A, B, bias, ref = _setup(M, N, K, torch.float16, seed=11)
+    base = torch.randn(M, N, device=cuda) + 3.0
+    x = base.clone()
+    stats = torch.full((M, N // 128, 2), float("nan"), device=cuda)
+    pkc.gemm_resid_stats(A.data_ptr(), B.data_ptr(), M, N, K, bf16=False, alpha=0.5, bias=bias.data_ptr(),
+                         x=x.data_ptr(), stats=stats.data_ptr())
+    torch.cuda.synchronize()
+    want = base + 0.5 * (ref + bias)
+    assert (x - want).abs().max().item() / want.abs().max().item() < 1e-4
+    ws = _chunk_stats(x)
+    assert torch.isfinite(stats).all()
+    assert (stats[..., 0] - ws[..., 0]).abs().max().item() < 1e-5 * max(1.0, ws[..., 0].abs().max().item())
+    assert (stats[..., 1] - ws[..., 1]).abs().max().item() < 1e-4 * ws[..., 1].abs().max().item()
+
+
+@pytest.mark.parametrize("bf16", [False, True])
+@pytest.mark.parametrize("M,N,K,epi,act", [(300, 768, 256, "store", "none"), (4099, 3072, 1024, "store", "none"),
+                                           (1, 256, 256, "store", "none"), (257, 2048, 512, "glu", "none"),
+                                           (1000, 4096, 1024, "store", "silu"), (700, 1024, 512, "glu", "none")])
+def test_gemm_layernorm_fused(cuda, bf16, M, N, K, epi, act):
+    """LayerNorm(x; gamma, beta) * W^T + b with the normalisation done while
+    the A operand is staged and gamma / beta folded into W and b (as the
+    encoder loads them), against torch fp32 (LayerNorm with population
+    variance, eps 1e-5, then the GEMM with W). Statistics come from the
+    residual GEMM's epilogue, as in the encoder. The bound covers the f16 /
+    bf16 roundings of xhat and of W diag(gamma)."""
+    import torch
+    import pkc
+    dt = torch.bfloat16 if bf16 else torch.float16
+    g = torch.Generator(device="cpu").manual_seed(M + N + K)
+    x0 = (torch.randn(M, K, generator=g) * 2.0 + 0.7).cuda()
+    gamma = (1.0 + 0.3 * torch.randn(K, generator=g)).cuda()
+    beta = (0.2 * torch.randn(K, generator=g)).cuda()
+    Bw = (torch.randn(N, K, generator=g) * 0.05).to(dt).cuda()
+    bias = (torch.randn(N, generator=g) * 0.1).cuda()
+    # x = x0 + 0 * (0 * 0^T) through the residual GEMM, which writes x's statistics
+    Az = torch.zeros(M, 128, dtype=dt, device=cuda)
+    Bz = torch.zeros(K, 128, dtype=dt, device=cuda)
+    x = x0.clone()
+    stats = torch.empty(M, K // 128, 2, device=cuda)
+    pkc.gemm_resid_stats(Az.data_ptr(), Bz.data_ptr(), M, K, 128, bf16=bf16, x=x.data_ptr(),
+                         stats=stats.data_ptr())
+    ncols = N // 2 if epi == "glu" else N
+    out = torch.zeros(M, ncols, dtype=dt, device=cuda)
+    Wf = (Bw.float() * gamma[None, :]).to(dt)
+    bf_ = (bias.double() + Bw.double() @ beta.double()).float()
+    pkc.gemm_ln(x.data_ptr(), stats.data_ptr(), Wf.data_ptr(), M, N, K,
+                bf16=bf16, epi=pkc.EPI_GLU_H if epi == "glu" else pkc.EPI_STORE_H,
+                act=pkc.ACT_SILU if act == "silu" else pkc.ACT_NONE, bias=bf_.data_ptr(), out=out.data_ptr(),
+                ldo=ncols)
+    torch.cuda.synchronize()
+    y = torch.nn.functional.layer_norm(x0, (K,), gamma, beta, eps=1e-5)
+    z = y @ Bw.float().t() + bias
+    if epi == "glu":
+        zt = z.view(M, N // 256, 2, 128)
+        a, gg = zt[:, :, 0, :].reshape(M, N // 2), zt[:, :, 1, :].reshape(M, N // 2)
+        want = a * torch.sigmoid(gg)
+    elif act == "silu":
+        want = torch.nn.functional.silu(z)
+    else:
+        want = z
+    tol = 2e-2 if bf16 else 4e-3
+    err = (out.float() - want).abs().max().item() / want.abs().max().item()
+    assert err < tol, err
+
+
+def test_gemm_layernorm_rejects_bad_shapes(cuda):
+    import torch
+    import pkc
+    x = torch.zeros(64, 96, device=cuda)
+    st = torch.zeros(64, 1, 2, device=cuda)
+    Bw = torch.zeros(256, 96, dtype=torch.float16, device=cuda)
+    out = torch.zeros(64, 256, dtype=torch.float16, device=cuda)
+    with pytest.raises(pkc.PkcError):   # K = 96 is not a multiple of 128
+        pkc.gemm_ln(x.data_ptr(), st.data_ptr(), Bw.data_ptr(), 64, 256, 96, bf16=False, out=out.data_ptr(),
+                    ldo=256)
