@@ -226,8 +226,10 @@ def run_ours(args, rank, world, local_rank):
     pinned = [torch.from_numpy(p).pin_memory() for p in pcm]
     host_pcm = [t.numpy() for t in pinned]
     host_out_bytes = out_floats * 4
+    # page-locked output buffer, reused every step (as the PCM input is)
+    host_out = torch.empty(model.out_floats(n), dtype=torch.float32).pin_memory().numpy()
     for _ in range(max(1, args.warmup)):
-        model.encode_pcm_batch(host_pcm, layout=pkc.LAYOUT_TIME_MAJOR)
+        model.encode_pcm_batch(host_pcm, layout=pkc.LAYOUT_TIME_MAJOR, out=host_out)
     lib_stream = torch.cuda.ExternalStream(model.stream(), device=dev)
     e_start = torch.cuda.Event(enable_timing=True)
     e_end = torch.cuda.Event(enable_timing=True)
@@ -237,7 +239,7 @@ def run_ours(args, rank, world, local_rank):
     t0 = time.perf_counter()
     e_start.record(lib_stream)
     for _ in range(args.steps):
-        model.encode_pcm_batch(host_pcm, layout=pkc.LAYOUT_TIME_MAJOR)
+        model.encode_pcm_batch(host_pcm, layout=pkc.LAYOUT_TIME_MAJOR, out=host_out)
     e_end.record(lib_stream)
     torch.cuda.synchronize(dev)
     e2e_wall = time.perf_counter() - t0
@@ -282,7 +284,7 @@ def run_ours(args, rank, world, local_rank):
                    "l2": "256 MiB written between timed steps (L2 flush); per-step working set > 1 GB"},
         "e2e": {"value": round(audio_total * args.steps / (e2e_max / 1e3), 1), "unit": UNIT,
                 "h2d_bytes_per_step": int(sum(n) * 4), "d2h_bytes_per_step": int(host_out_bytes),
-                "api": "pkc_encode_pcm_batch (host buffers, pinned PCM)",
+                "api": "pkc_encode_pcm_batch (host buffers: pinned PCM in, pinned output buffer reused per step)",
                 "wall_value": round(audio_total * args.steps / (wall_max / 1e3), 1)},
         "gpu_launches": int(round(launches_per_step * args.steps)),
         "roofline": {"bound": "tensor", "kernel": "k_gemm_tc (tcgen05 GEMM, all encoder projections)",

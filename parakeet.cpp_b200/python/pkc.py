@@ -235,17 +235,33 @@ class Model:
                                       out.ctypes.data, out.size, vt, ctypes.byref(dm)), self._h)
         return _split(out, list(vt), d, layout)
 
-    def encode_pcm_batch(self, pcms, layout=LAYOUT_CHANNELS_FIRST):
+    def encode_pcm_batch(self, pcms, layout=LAYOUT_CHANNELS_FIRST, out=None):
+        """Encode B clips of 16 kHz mono PCM (host arrays). Returns one array
+        per clip ([d, T'] channels-first or [T', d] time-major). `out`: an
+        optional contiguous float32 host array of at least
+        out_floats(lengths) elements to write into (the returned arrays are
+        views of it); pass page-locked memory (e.g. a pinned torch tensor's
+        .numpy()) and the download runs at full copy speed with no allocation
+        per call."""
         B = len(pcms)
         pcms = [np.ascontiguousarray(p, dtype=np.float32) for p in pcms]
         ptrs = (c_void_p * B)(*[p.ctypes.data for p in pcms])
         ns = _ints([len(p) for p in pcms])
         n = lib().pkc_encode_out_floats(self._h, ns, B)
-        out = np.zeros(n, dtype=np.float32)
+        if out is None:
+            out = np.empty(n, dtype=np.float32)
+        else:
+            if out.dtype != np.float32 or not out.flags["C_CONTIGUOUS"] or out.size < n:
+                raise ValueError(f"out must be a contiguous float32 array of at least {n} elements")
+            out = out.reshape(-1)[:n]
         vt = (c_int * B)()
         _check(lib().pkc_encode_pcm_batch(self._h, ptrs, ns, B, layout, out.ctypes.data, out.size,
                                           vt), self._h)
         return _split(out, list(vt), self.info.d_model, layout)
+
+    def out_floats(self, n_samples):
+        """Floats the encoder output of clips with these sample counts takes."""
+        return int(lib().pkc_encode_out_floats(self._h, _ints(n_samples), len(n_samples)))
 
     def encode_pcm_device(self, d_pcm, n_samples, d_out, stream=0, slot=0, sync=False):
         _check(lib().pkc_encode_pcm_device(self._h, slot, c_void_p(d_pcm), _ints(n_samples),
