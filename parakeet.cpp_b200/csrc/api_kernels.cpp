@@ -30,6 +30,33 @@ int* dev_err_word(int dev) {
   return words[dev];
 }
 
+// Stream-K workspace for one kernel-level GEMM call, on the call's stream
+// (these entry points synchronise before returning, so it is freed there).
+struct SplitKScratch {
+  float* ws = nullptr;
+  int* flags = nullptr;
+  cudaStream_t st = nullptr;
+  bool attach(pkc::GemmArgs& a, int dev, cudaStream_t stream) {
+    st = stream;
+    int sms = 0;
+    if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return false;
+    const int pairs = sms / 2;
+    if (cudaMallocAsync(reinterpret_cast<void**>(&ws), pkc::gemm_sk_ws_bytes(pairs), st) != cudaSuccess ||
+        cudaMallocAsync(reinterpret_cast<void**>(&flags), pkc::gemm_sk_flag_count(pairs) * sizeof(int), st) !=
+            cudaSuccess ||
+        cudaMemsetAsync(flags, 0, pkc::gemm_sk_flag_count(pairs) * sizeof(int), st) != cudaSuccess)
+      return false;
+    a.sk_ws = ws;
+    a.sk_flags = flags;
+    a.sk_pairs = pairs;
+    return true;
+  }
+  ~SplitKScratch() {
+    if (ws) cudaFreeAsync(ws, st);
+    if (flags) cudaFreeAsync(flags, st);
+  }
+};
+
 }  // namespace
 
 extern "C" pkc_status pkc_gemm(const void* A, int lda, const void* Bw, int ldb, int M, int N,
@@ -46,6 +73,8 @@ extern "C" pkc_status pkc_gemm(const void* A, int lda, const void* Bw, int ldb, 
   a.M = M; a.N = N; a.K = K;
   a.epi = epi; a.act = act; a.alpha = alpha; a.bias = bias;
   a.out = out; a.ldo = ldo; a.err = err;
+  SplitKScratch sks;
+  if (!sks.attach(a, dev, st)) return pkc::set_thread_error(PKC_ERR_OOM, "pkc_gemm: workspace allocation failed");
   cudaError_t e = pkc::gemm_launch(A, lda, Bw, ldb, dtype == 1, a, st);
   if (e != cudaSuccess)
     return pkc::set_thread_error(PKC_ERR_CUDA, std::string("pkc_gemm: ") + cudaGetErrorString(e));
@@ -91,6 +120,9 @@ extern "C" pkc_status pkc_gemm_resid_stats(const void* A, int lda, const void* B
   a.M = M; a.N = N; a.K = K;
   a.epi = pkc::EPI_RESID_F32; a.act = pkc::ACT_NONE; a.alpha = alpha; a.bias = bias;
   a.out = x; a.ldo = ldx; a.err = err; a.stats = stats;
+  SplitKScratch sks;
+  if (!sks.attach(a, dev, st))
+    return pkc::set_thread_error(PKC_ERR_OOM, "pkc_gemm_resid_stats: workspace allocation failed");
   return finish_kernel_call(pkc::gemm_launch(A, lda, Bw, ldb, dtype == 1, a, st), err, st, "pkc_gemm_resid_stats");
 }
 

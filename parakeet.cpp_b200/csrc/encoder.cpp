@@ -89,6 +89,8 @@ DeviceRunner::~DeviceRunner() {
   for (cudaEvent_t e : ev_pool_) cudaEventDestroy(e);
   if (ws_) cudaFree(ws_);
   if (err_word_) cudaFree(err_word_);
+  if (sk_ws_) cudaFree(sk_ws_);
+  if (sk_flags_) cudaFree(sk_flags_);
   if (h_tables_) cudaFreeHost(h_tables_);
   free_weights(w_);
   if (stream_) cudaStreamDestroy(stream_);
@@ -102,6 +104,11 @@ std::string DeviceRunner::init(const GgufFile& g) {
   if (cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking) != cudaSuccess) return "stream creation failed";
   if (cudaMalloc(&err_word_, sizeof(int)) != cudaSuccess) return "cudaMalloc failed";
   cudaMemset(err_word_, 0, sizeof(int));
+  sk_pairs_ = prop.multiProcessorCount / 2;
+  if (cudaMalloc(&sk_ws_, gemm_sk_ws_bytes(sk_pairs_)) != cudaSuccess ||
+      cudaMalloc(&sk_flags_, gemm_sk_flag_count(sk_pairs_) * sizeof(int)) != cudaSuccess)
+    return "cudaMalloc of the GEMM stream-K workspace failed";
+  cudaMemset(sk_flags_, 0, gemm_sk_flag_count(sk_pairs_) * sizeof(int));
   power_ld_ = cfg_.n_fft / 2 + 8;
   const char* ng = getenv("PKC_NO_GRAPH");
   use_graphs_ = !(ng && ng[0] == '1');
@@ -220,6 +227,7 @@ pkc_status DeviceRunner::gemm(const void* A, int lda, const void* B, int ldb, bo
   GemmArgs a{};
   a.M = M; a.N = N; a.K = K; a.epi = epi; a.act = act; a.alpha = alpha; a.bias = bias;
   a.out = out; a.ldo = ldo; a.err = err_word_; a.stats = stats;
+  a.sk_ws = sk_ws_; a.sk_flags = sk_flags_; a.sk_pairs = sk_pairs_;
   prof_begin(st);
   cudaError_t e;
   if (qw && qw->type) {
@@ -513,6 +521,8 @@ pkc_status DeviceRunner::finish(cudaStream_t st, std::string& err) {
   PKC_CK(cudaStreamSynchronize(st), "stream synchronize");
   if (h_err != 0) {
     cudaMemsetAsync(err_word_, 0, sizeof(int), st);
+    // a launch that gave up may have left stream-K flags raised
+    if (sk_flags_) cudaMemsetAsync(sk_flags_, 0, gemm_sk_flag_count(sk_pairs_) * sizeof(int), st);
     cudaStreamSynchronize(st);
     err = "kernel reported error " + std::to_string(h_err) + " (bounded wait timed out)";
     return PKC_ERR_KERNEL;

@@ -88,6 +88,10 @@ class DeviceRunner {
   void* ws_ = nullptr;
   size_t ws_bytes_ = 0;
   int* err_word_ = nullptr;
+  // stream-K workspace of the 2-SM GEMM (flags zero between launches)
+  float* sk_ws_ = nullptr;
+  int* sk_flags_ = nullptr;
+  int sk_pairs_ = 0;
   bool sub_unfused_ = false;
   bool ln_unfused_ = false;
   int* h_tables_ = nullptr;  // pinned staging for the item tables

@@ -18,6 +18,7 @@ enum DevErr : int {
   DEV_ERR_TIMEOUT_EMPTY = 102,  // producer waited too long for a free stage
   DEV_ERR_TIMEOUT_ACCUM = 103,  // epilogue waited too long for the accumulator
   DEV_ERR_TIMEOUT_ATTN = 104,   // attention pipeline wait ran out
+  DEV_ERR_TIMEOUT_SPLITK = 105, // a split tile's finisher waited too long for a partial sum
   DEV_ERR_BAD_SHAPE = 110,
 };
 
@@ -103,6 +104,27 @@ static __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity
 // records `code` in *err) if that does not happen within kWaitLimitNs.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err, int code) {
   return mbar_test_wait(bar, parity) || mbar_wait_slow(bar, parity, err, code);
+}
+
+// Flag in global memory set by another CTA of the same grid (st_release_gpu
+// after its data). Spins until *f != 0; false (and `code` in *err) after
+// kWaitLimitNs.
+static __device__ __noinline__ bool wait_flag_gpu(const int* f, int* err, int code) {
+  const unsigned long long t0 = globaltimer_ns();
+  for (uint32_t it = 0;; ++it) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+    if (v != 0) return true;
+    if ((it & 63u) == 63u && globaltimer_ns() - t0 > kWaitLimitNs) {
+      report_error(err, code);
+      return false;
+    }
+    __nanosleep(100);
+  }
+}
+
+__device__ __forceinline__ void st_release_gpu(int* f, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(f), "r"(v) : "memory");
 }
 
 // One lane of the (converged) warp: the issuing lane of warp-wide roles whose

@@ -338,7 +338,133 @@ constexpr int A2_BYTES = HALF_ROWS * BK * 2;
 constexpr int B2_BYTES = HALF_ROWS * BK * 2;
 constexpr int SMEM2_BYTES = STAGES2 * (A2_BYTES + B2_BYTES) + 8 * 4096 + 512 + 1024;
 
-template <typename H, int EPI>
+// ---- work schedule of the 2-SM kernel
+// Whole tiles: pair p takes tiles p, p + P, p + 2P, ... (P = CTA pairs).
+// Stream-K (args.sk_ws set): the W = tiles x KB k-blocks, in tile-major order,
+// are cut into P contiguous ranges [p W / P, (p + 1) W / P); a range is a
+// sequence of segments (tile, kb0, kb1). A segment with kb0 > 0 is a partial
+// sum: its epilogue spills the f32 accumulator to the pair's workspace slot
+// and raises a flag. The segment holding a split tile's k-block 0 (the last
+// segment of a range) finishes the tile: it adds the partials of the pairs
+// that follow, in pair order (so the result does not depend on timing), then
+// runs the fused epilogue. Partial segments come first in their ranges, so
+// finishers seldom wait. A range holds at most one partial segment, hence one
+// workspace slot per pair. Stream-K needs W >= P (no empty range); the kernel
+// falls back to whole tiles otherwise.
+struct SegIter {
+  long long u, b;
+  int tile_dp, step, KB, n_tiles;
+  bool sk;
+  __device__ __forceinline__ SegIter(bool sk_, int pair, int npairs, int KB_, int n_tiles_)
+      : tile_dp(pair), step(npairs), KB(KB_), n_tiles(n_tiles_), sk(sk_) {
+    const long long W = (long long)n_tiles_ * KB_;
+    u = sk_ ? (long long)pair * W / npairs : 0;
+    b = sk_ ? (long long)(pair + 1) * W / npairs : 0;
+  }
+  __device__ __forceinline__ bool next(int& tile, int& kb0, int& kb1) {
+    if (sk) {
+      if (u >= b) return false;
+      tile = (int)(u / KB);
+      kb0 = (int)(u - (long long)tile * KB);
+      const long long left = b - u;
+      kb1 = left < (long long)(KB - kb0) ? kb0 + (int)left : KB;
+      u += kb1 - kb0;
+      return true;
+    }
+    if (tile_dp >= n_tiles) return false;
+    tile = tile_dp;
+    kb0 = 0;
+    kb1 = KB;
+    tile_dp += step;
+    return true;
+  }
+};
+
+constexpr int SK_SLOT_FLOATS = 32 * 128;  // one epilogue warp: 32 rows x 128 accumulator columns
+
+// Accumulator column of 32-column chunk c (0..3) of the epilogue warp with
+// column half `half`: exactly the columns epilogue_tile reads in that warp
+// (value and gate chunks for the paired epilogues), so a warp's fix-up never
+// depends on another warp.
+template <int EPI>
+__device__ __forceinline__ int sk_col(int half, int c) {
+  constexpr bool PAIRED = EPI == EPI_GLU_H || EPI == EPI_POWER_F32;
+  return PAIRED ? (c >> 1) * (BN / 2) + half * (BN / 4) + (c & 1) * 32 : half * (BN / 2) + c * 32;
+}
+
+// Partial sum of one epilogue warp (TMEM lanes of `trow`, its 128
+// accumulator columns) to its workspace slot, lane-interleaved so each store
+// instruction writes 512 contiguous bytes; then the slot's flag.
+template <int EPI>
+__device__ __forceinline__ void sk_spill(const GemmArgs& args, uint32_t trow, int half, int slot) {
+  const int lane = threadIdx.x & 31;
+  float* dst = args.sk_ws + (size_t)slot * SK_SLOT_FLOATS;
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    uint32_t r[32];
+    tmem_ld32(trow + (uint32_t)sk_col<EPI>(half, c), r);
+    tmem_ld_wait();
+#pragma unroll
+    for (int e = 0; e < 8; ++e)
+      __stcg(reinterpret_cast<float4*>(dst + ((c * 8 + e) * 32 + lane) * 4),
+             make_float4(__uint_as_float(r[4 * e]), __uint_as_float(r[4 * e + 1]), __uint_as_float(r[4 * e + 2]),
+                         __uint_as_float(r[4 * e + 3])));
+  }
+  __threadfence();
+  __syncwarp();
+  if (lane == 0) st_release_gpu(args.sk_flags + slot, 1);
+}
+
+// Finisher of split tile `tile` (pair `pair` holds its k-block 0): add the
+// partial sums of the pairs after it whose (non-empty) ranges start inside
+// the tile, in pair order, into this warp's accumulator columns, back in
+// TMEM; clears their flags for the next launch. `slot` = this warp's own
+// slot; the same warp of pair q uses slot + (q - pair) * 2 * EPI_WARPS.
+template <int EPI>
+__device__ __forceinline__ void sk_fixup(const GemmArgs& args, uint32_t trow, int half, int slot, int pair,
+                                         int npairs, long long W, long long tile_end) {
+  const int lane = threadIdx.x & 31;
+  // contributors: pairs pair+1 .. pair+n (W >= npairs: no range is empty)
+  int n = 0;
+  while (pair + n + 1 < npairs && (long long)(pair + n + 1) * W / npairs < tile_end) ++n;
+  bool ok = true;
+  if (lane == 0)
+    for (int i = 1; i <= n && ok; ++i)
+      ok = wait_flag_gpu(args.sk_flags + slot + i * 2 * EPI_WARPS, args.err, DEV_ERR_TIMEOUT_SPLITK);
+  __syncwarp();
+  // every lane acquires the flags itself before reading the partials
+  for (int i = 1; i <= n; ++i) {
+    int v;
+    asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(args.sk_flags + slot + i * 2 * EPI_WARPS)
+                 : "memory");
+    (void)v;
+  }
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    uint32_t r[32];
+    tmem_ld32(trow + (uint32_t)sk_col<EPI>(half, c), r);
+    tmem_ld_wait();
+#pragma unroll 1
+    for (int i = 1; i <= n; ++i) {
+      const float* src = args.sk_ws + (size_t)(slot + i * 2 * EPI_WARPS) * SK_SLOT_FLOATS;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(src + ((c * 8 + e) * 32 + lane) * 4));
+        r[4 * e] = __float_as_uint(__uint_as_float(r[4 * e]) + v.x);
+        r[4 * e + 1] = __float_as_uint(__uint_as_float(r[4 * e + 1]) + v.y);
+        r[4 * e + 2] = __float_as_uint(__uint_as_float(r[4 * e + 2]) + v.z);
+        r[4 * e + 3] = __float_as_uint(__uint_as_float(r[4 * e + 3]) + v.w);
+      }
+    }
+    tmem_st32(trow + (uint32_t)sk_col<EPI>(half, c), r);
+  }
+  tmem_st_wait();
+  __syncwarp();
+  if (lane == 0)
+    for (int i = 1; i <= n; ++i) args.sk_flags[slot + i * 2 * EPI_WARPS] = 0;
+}
+
+template <typename H, int EPI, bool SK>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                GemmArgs args) {
@@ -361,6 +487,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   const int KB = args.K / BK;
   const int tiles_m = (args.M + 2 * HALF_ROWS - 1) / (2 * HALF_ROWS);
   const int n_tiles = tiles_m * (args.N / BN);
+  // the stream-K instantiation (SK) falls back to whole tiles if W < P
+  const bool sk = SK && (long long)n_tiles * KB >= npairs;
 
   if (threadIdx.x == 0) {
     prefetch_tmap(&tmA);
@@ -388,10 +516,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       // ---- TMA producer (both CTAs)
       uint32_t it = 0;
       bool ok = true;
-      for (int tile = pair; tile < n_tiles && ok; tile += npairs) {
+      SegIter sg(sk, pair, npairs, KB, n_tiles);
+      int tile, kb0, kb1;
+      while (ok && sg.next(tile, kb0, kb1)) {
         const int m0 = (tile % tiles_m) * 2 * HALF_ROWS + (int)rank * HALF_ROWS;
         const int n0 = (tile / tiles_m) * BN + (int)rank * HALF_ROWS;
-        for (int kb = 0; kb < KB; ++kb, ++it) {
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES2;
           const uint32_t ph = (it / STAGES2) & 1u;
           if (!mbar_wait(smem_u32(&bars[STAGES2 + s]), ph ^ 1u, args.err, DEV_ERR_TIMEOUT_EMPTY)) {
@@ -412,7 +542,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       uint32_t it = 0;
       int local = 0;
       bool ok = true;
-      for (int tile = pair; tile < n_tiles && ok; tile += npairs, ++local) {
+      SegIter sg(sk, pair, npairs, KB, n_tiles);
+      int tile, kb0, kb1;
+      for (; ok && sg.next(tile, kb0, kb1); ++local) {
         const int buf = local & 1;
         const uint32_t use = (uint32_t)(local >> 1);
         if (!mbar_wait(smem_u32(&bars[2 * STAGES2 + 2 + buf]), (use & 1u) ^ 1u, args.err,
@@ -420,7 +552,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           break;
         tc_fence_after();
         const uint32_t acc = tmem + (uint32_t)(buf * BN);
-        for (int kb = 0; kb < KB; ++kb, ++it) {
+        for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES2;
           const uint32_t ph = (it / STAGES2) & 1u;
           if (!mbar_wait(smem_u32(&bars[s]), ph, args.err, DEV_ERR_TIMEOUT_FULL)) {
@@ -433,7 +565,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k)
             umma_f16_2sm(acc, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc,
-                         (kb > 0 || k > 0) ? 1u : 0u);
+                         (kb > kb0 || k > 0) ? 1u : 0u);
           umma_commit_2sm_mc(smem_u32(&bars[STAGES2 + s]), 0x3);  // frees the stage in both CTAs
         }
         if (ok) umma_commit_2sm_mc(smem_u32(&bars[2 * STAGES2 + buf]), 0x3);  // accumulators ready
@@ -446,7 +578,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     const uint32_t acce_leader0 = mapa_shared(smem_u32(&bars[2 * STAGES2 + 2]), 0);
     const uint32_t acce_leader1 = mapa_shared(smem_u32(&bars[2 * STAGES2 + 3]), 0);
     int local = 0;
-    for (int tile = pair; tile < n_tiles; tile += npairs, ++local) {
+    SegIter sg(sk, pair, npairs, KB, n_tiles);
+    int tile, kb0, kb1;
+    // this warp's stream-K slot (pair, CTA rank, epilogue warp)
+    const int slot = (pair * 2 + (int)rank) * EPI_WARPS + (warp - 2);
+    for (; sg.next(tile, kb0, kb1); ++local) {
       const int buf = local & 1;
       const uint32_t use = (uint32_t)(local >> 1);
       const bool have =
@@ -457,7 +593,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       const int m0 = (tile % tiles_m) * 2 * HALF_ROWS + (int)rank * HALF_ROWS;
       const int n0 = (tile / tiles_m) * BN;
       const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
-      epilogue_tile<H, EPI>(args, trow, m0 + q * 32, n0, half, sE + (warp - 2) * EPI_STAGE_BYTES);
+      if (SK && kb0 > 0) {
+        sk_spill<EPI>(args, trow, half, slot);  // partial sum of a split tile
+      } else {
+        // finisher of a split tile: the pairs after this one whose ranges
+        // start inside the tile hold its remaining k-blocks
+        if (SK && kb1 < KB)
+          sk_fixup<EPI>(args, trow, half, slot, pair, npairs, (long long)n_tiles * KB, (long long)(tile + 1) * KB);
+        epilogue_tile<H, EPI>(args, trow, m0 + q * 32, n0, half, sE + (warp - 2) * EPI_STAGE_BYTES);
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive_remote_cta(buf ? acce_leader1 : acce_leader0);
@@ -1034,13 +1178,16 @@ bool make_tmap_kmajor(CUtensorMap* map, const void* base, int rows, int K, int l
 template <typename H, int EPI>
 static cudaError_t launch_t2(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
                              cudaStream_t st) {
-  auto kern = k_gemm_tc2<H, EPI>;
+  auto kern = k_gemm_tc2<H, EPI, false>;
+  auto kern_sk = k_gemm_tc2<H, EPI, true>;
   static bool attr_set[64] = {};
   static int max_pairs[64] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (!attr_set[dev & 63]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(kern_sk, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2, 1, 1);
@@ -1062,7 +1209,16 @@ static cudaError_t launch_t2(const CUtensorMap& ta, const CUtensorMap& tb, const
     attr_set[dev & 63] = true;
   }
   const int n_tiles = (a.N / BN) * ((a.M + 2 * HALF_ROWS - 1) / (2 * HALF_ROWS));
-  const int pairs = n_tiles < max_pairs[dev & 63] ? n_tiles : max_pairs[dev & 63];
+  const int mp = max_pairs[dev & 63];
+  int pairs = n_tiles < mp ? n_tiles : mp;
+  if (a.sk_ws && a.sk_flags && mp <= a.sk_pairs && gemm_splitk_enabled()) {
+    // stream-K when whole tiles would leave more than 15 % of the last
+    // wave's pairs idle, and every pair still gets >= 4 k-blocks
+    const int KB = a.K / BK;
+    const int waves = (n_tiles + mp - 1) / mp;
+    if ((double)n_tiles < 0.85 * (double)waves * mp && (long long)n_tiles * KB >= 4LL * mp)
+      return launch_pdl(kern_sk, dim3(2 * mp), dim3(THREADS), SMEM2_BYTES, st, ta, tb, a);
+  }
   return launch_pdl(kern, dim3(2 * pairs), dim3(THREADS), SMEM2_BYTES, st, ta, tb, a);
 }
 
@@ -1239,6 +1395,24 @@ cudaError_t gemm_launch_ln(const LnA& A, const void* B, int ldb, bool bf16, cons
     default:
       return cudaErrorInvalidValue;
   }
+}
+
+size_t gemm_sk_ws_bytes(int pairs) { return (size_t)pairs * 2 * EPI_WARPS * SK_SLOT_FLOATS * sizeof(float); }
+int gemm_sk_flag_count(int pairs) { return pairs * 2 * EPI_WARPS; }
+
+// PKC_GEMM_SPLITK=1: let the 2-SM kernel run the stream-K schedule. Off by
+// default: at the encoder's shapes the f32 partial sums that every pair
+// spills and the finishers read back (~19 MB through L2 at the same moment,
+// ~3.5 us each way, measured by per-pair timestamps at M = 3282, N = 1024,
+// K = 1024) cost more than the k-blocks the balanced ranges save, and
+// whole tiles keep each row's result independent of the batch.
+bool gemm_splitk_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("PKC_GEMM_SPLITK");
+    v = (e && e[0] == '1') ? 1 : 0;
+  }
+  return v == 1;
 }
 
 // PKC_GEMM_1SM=1 forces the 1-SM kernel (for A/B comparisons)

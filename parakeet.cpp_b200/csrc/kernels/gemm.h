@@ -28,7 +28,19 @@ struct GemmArgs {
   // [M][N/128][2] -- what a LayerNorm of those rows needs, merged by the
   // consumer (gemm_launch_ln)
   float* stats;
+  // Stream-K workspace (may be null: whole tiles only). With it, the 2-SM
+  // kernel may split tiles along K across CTA pairs when whole tiles would
+  // leave part of the last wave idle: sk_ws >= gemm_sk_ws_bytes(sk_pairs)
+  // bytes, sk_flags >= gemm_sk_flag_count(sk_pairs) ints, zero when the
+  // launch starts (the kernel leaves them zero). One workspace per stream.
+  float* sk_ws;
+  int* sk_flags;
+  int sk_pairs;       // CTA pairs the workspace has room for
 };
+
+// Stream-K workspace sizes for `pairs` CTA pairs (a device's SMs / 2).
+size_t gemm_sk_ws_bytes(int pairs);
+int gemm_sk_flag_count(int pairs);
 
 typedef CUresult (*PFN_encodeTiled_t)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                       const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
@@ -78,6 +90,8 @@ cudaError_t gemm_launch_ln(const LnA& A, const void* B, int ldb, bool bf16, cons
 
 int gemm_tile_m();
 bool gemm_2sm_enabled();
+// true when PKC_GEMM_SPLITK=1 (stream-K schedule allowed; whole tiles otherwise)
+bool gemm_splitk_enabled();
 int gemm_tile_n();
 int gemm_tile_k();
 

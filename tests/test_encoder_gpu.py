@@ -95,9 +95,15 @@ def test_encoder_matches_oracle(opened, oracles, kind):
 
 
 def test_batched_equals_standalone(opened):
+    """A clip's output does not depend on its batch mates, bit for bit (every
+    kernel computes a row the same way whatever the batch), and the same
+    batch twice gives the same bits."""
     m = opened("f16")
     pcm = clips([SR * 4 + 17, SR * 2 + 999, 3000], seed=2)
     together = m.encode_pcm_batch(pcm)
+    again = m.encode_pcm_batch(pcm)
+    for a, b in zip(together, again):
+        np.testing.assert_array_equal(a, b)
     for i, p in enumerate(pcm):
         alone = m.encode_pcm_batch([p])[0]
         np.testing.assert_array_equal(together[i], alone)

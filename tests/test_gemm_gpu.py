@@ -220,3 +220,51 @@ def test_gemm_layernorm_rejects_bad_shapes(cuda):
     with pytest.raises(pkc.PkcError):   # K = 96 is not a multiple of 128
         pkc.gemm_ln(x.data_ptr(), st.data_ptr(), Bw.data_ptr(), 64, 256, 96, bf16=False, out=out.data_ptr(),
                     ldo=256)
+
+
+_SPLITK_CHILD = r"""
+import sys, numpy as np, torch
+sys.path.insert(0, sys.argv[1])
+import pkc
+M, N, K, epi = (int(v) for v in sys.argv[2:6])
+g = torch.Generator().manual_seed(M * 7 + N + K)
+A = (torch.randn(M, K, generator=g) * 0.5).half().cuda()
+B = (torch.randn(N, K, generator=g) * 0.05).half().cuda()
+bias = (torch.randn(N, generator=g) * 0.1).cuda()
+ncols = N // 2 if epi == pkc.EPI_GLU_H else N
+f32 = epi in (pkc.EPI_RESID_F32, pkc.EPI_STORE_F32)
+out = (torch.randn(M, ncols, generator=g).cuda() if f32 else torch.zeros(M, ncols, dtype=torch.half, device="cuda"))
+pkc.gemm(A.data_ptr(), B.data_ptr(), M, N, K, bf16=False, epi=epi, alpha=0.5 if f32 else 1.0,
+         bias=bias.data_ptr(), out=out.data_ptr(), ldo=ncols)
+torch.cuda.synchronize()
+np.save(sys.argv[6], out.float().cpu().numpy())
+"""
+
+
+@pytest.mark.parametrize("M,N,K,epi", [(3282, 1024, 1024, "resid"), (3282, 3072, 1024, "store"),
+                                       (3282, 2048, 1024, "glu"), (3282, 1024, 4096, "resid"),
+                                       (600, 1024, 2048, "f32")])
+def test_stream_k_matches_whole_tiles(cuda, tmp_path, M, N, K, epi):
+    """With PKC_GEMM_SPLITK=1, shapes whose whole-tile schedule leaves part of
+    the last wave idle run stream-K (tiles split along K across CTA pairs,
+    partial sums added by the finishing pair in pair order). Against the
+    whole-tile kernel (the default; a child process each) the results differ
+    only by f32 summation order; the same call twice is bitwise identical."""
+    import os
+    import subprocess
+    import sys
+    import numpy as np
+    import pkc
+    e = {"resid": pkc.EPI_RESID_F32, "store": pkc.EPI_STORE_H, "glu": pkc.EPI_GLU_H, "f32": pkc.EPI_STORE_F32}[epi]
+    pydir = os.path.dirname(pkc.__file__)
+    outs = {}
+    for tag, env in (("sk", {"PKC_GEMM_SPLITK": "1"}), ("sk2", {"PKC_GEMM_SPLITK": "1"}), ("whole", {})):
+        f = str(tmp_path / f"{tag}.npy")
+        base = {k: v for k, v in os.environ.items() if k != "PKC_GEMM_SPLITK"}
+        subprocess.run([sys.executable, "-c", _SPLITK_CHILD, pydir, str(M), str(N), str(K), str(e), f],
+                       check=True, env={**base, **env}, timeout=300)
+        outs[tag] = np.load(f)
+    np.testing.assert_array_equal(outs["sk"], outs["sk2"])
+    scale = np.abs(outs["whole"]).max()
+    tol = 1e-5 if epi in ("resid", "f32") else 1e-3   # f16 outputs: a last-bit flip at most
+    assert np.abs(outs["sk"] - outs["whole"]).max() <= tol * scale
