@@ -71,11 +71,44 @@ void make_plan(const Config& c, const std::vector<int>& n_samples, const std::ve
   std::vector<int> order(B);
   for (int b = 0; b < B; ++b) order[b] = b;
   std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return p.v[a] > p.v[b]; });
-  for (int b : order)
-    for (int q0 = 0; q0 < p.v[b]; q0 += qt) {
-      p.attn_tiles.push_back(b);
-      p.attn_tiles.push_back(q0);
+  // two-part split: a per-utterance cost of frames x (1 + T / 3.5 d) (the
+  // projections per frame, plus attention growing with the length), halves
+  // as equal as a contiguous split allows. Only for batches whose halves
+  // still fill the GPU: measured at M = 3282 (C2) two parts were 8 % slower
+  // (each part's GEMMs fall under one efficient wave), at M ~ 13k (C3) 4 %
+  // faster. PKC_STREAMS=1: never split; PKC_STREAMS=2: split any batch of
+  // two or more utterances.
+  p.split_b = 0;
+  const char* sm = getenv("PKC_STREAMS");
+  const int mode = sm ? std::atoi(sm) : 0;
+  if (B >= 2 && mode != 1 && (mode == 2 || p.M >= 6144)) {
+    std::vector<double> cost(B);
+    double total = 0.0;
+    for (int b = 0; b < B; ++b) {
+      cost[b] = p.v[b] * (1.0 + p.v[b] / (3.5 * c.d_model));
+      total += cost[b];
     }
+    double pre = 0.0, best = 1e300;
+    for (int s = 1; s < B; ++s) {
+      pre += cost[s - 1];
+      const double gap = std::fabs(2.0 * pre - total);
+      if (gap < best) {
+        best = gap;
+        p.split_b = s;
+      }
+    }
+  }
+  for (int part = 0; part < 2; ++part) {
+    for (int b : order) {
+      const bool in1 = p.split_b > 0 && b >= p.split_b;
+      if ((part == 1) != in1) continue;
+      for (int q0 = 0; q0 < p.v[b]; q0 += qt) {
+        p.attn_tiles.push_back(b);
+        p.attn_tiles.push_back(q0);
+      }
+    }
+    if (part == 0) p.ntiles0 = (int)p.attn_tiles.size() / 2;
+  }
 }
 
 namespace {
@@ -91,6 +124,12 @@ DeviceRunner::~DeviceRunner() {
   if (err_word_) cudaFree(err_word_);
   if (sk_ws_) cudaFree(sk_ws_);
   if (sk_flags_) cudaFree(sk_flags_);
+  if (stream2_) {
+    cudaStreamSynchronize(stream2_);
+    cudaStreamDestroy(stream2_);
+  }
+  if (ev_fork_) cudaEventDestroy(ev_fork_);
+  if (ev_join_) cudaEventDestroy(ev_join_);
   if (h_tables_) cudaFreeHost(h_tables_);
   free_weights(w_);
   if (stream_) cudaStreamDestroy(stream_);
@@ -105,10 +144,14 @@ std::string DeviceRunner::init(const GgufFile& g) {
   if (cudaMalloc(&err_word_, sizeof(int)) != cudaSuccess) return "cudaMalloc failed";
   cudaMemset(err_word_, 0, sizeof(int));
   sk_pairs_ = prop.multiProcessorCount / 2;
-  if (cudaMalloc(&sk_ws_, gemm_sk_ws_bytes(sk_pairs_)) != cudaSuccess ||
-      cudaMalloc(&sk_flags_, gemm_sk_flag_count(sk_pairs_) * sizeof(int)) != cudaSuccess)
+  if (cudaMalloc(&sk_ws_, 2 * gemm_sk_ws_bytes(sk_pairs_)) != cudaSuccess ||
+      cudaMalloc(&sk_flags_, 2 * gemm_sk_flag_count(sk_pairs_) * sizeof(int)) != cudaSuccess)
     return "cudaMalloc of the GEMM stream-K workspace failed";
-  cudaMemset(sk_flags_, 0, gemm_sk_flag_count(sk_pairs_) * sizeof(int));
+  cudaMemset(sk_flags_, 0, 2 * gemm_sk_flag_count(sk_pairs_) * sizeof(int));
+  if (cudaStreamCreateWithFlags(&stream2_, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaEventCreateWithFlags(&ev_fork_, cudaEventDisableTiming) != cudaSuccess ||
+      cudaEventCreateWithFlags(&ev_join_, cudaEventDisableTiming) != cudaSuccess)
+    return "second stream / event creation failed";
   power_ld_ = cfg_.n_fft / 2 + 8;
   const char* ng = getenv("PKC_NO_GRAPH");
   use_graphs_ = !(ng && ng[0] == '1');
@@ -227,7 +270,10 @@ pkc_status DeviceRunner::gemm(const void* A, int lda, const void* B, int ldb, bo
   GemmArgs a{};
   a.M = M; a.N = N; a.K = K; a.epi = epi; a.act = act; a.alpha = alpha; a.bias = bias;
   a.out = out; a.ldo = ldo; a.err = err_word_; a.stats = stats;
-  a.sk_ws = sk_ws_; a.sk_flags = sk_flags_; a.sk_pairs = sk_pairs_;
+  // the part being issued owns one half of the stream-K workspace
+  a.sk_ws = sk_ws_ + (size_t)sk_part_ * (gemm_sk_ws_bytes(sk_pairs_) / sizeof(float));
+  a.sk_flags = sk_flags_ + (size_t)sk_part_ * gemm_sk_flag_count(sk_pairs_);
+  a.sk_pairs = sk_pairs_;
   prof_begin(st);
   cudaError_t e;
   if (qw && qw->type) {
@@ -389,7 +435,7 @@ pkc_status DeviceRunner::run_frontend(const Plan& p, cudaStream_t st, std::strin
 
 pkc_status DeviceRunner::run_encoder(const Plan& p, cudaStream_t st, std::string& err) {
   const Config& c = cfg_;
-  const int d = c.d_model, FF = c.ff_dim, C = c.sub_channels, H = c.n_heads, K = c.conv_kernel;
+  const int d = c.d_model, C = c.sub_channels;
   const bool bf = c.bf16;
   const int M = p.M;
   const double hs = 2.0;
@@ -440,78 +486,128 @@ pkc_status DeviceRunner::run_encoder(const Plan& p, cudaStream_t st, std::string
               st, "gemm_pos", err, &w_.pos_all_q));
 
 
+  // ---- conformer layers: one part, or two independent parts on two streams
   const int ntiles = (int)p.attn_tiles.size() / 2;
-  double attn_flops = 0.0;
-  for (int b = 0; b < p.B; ++b) {
-    const double T = p.v[b];
-    attn_flops += 2.0 * T * T * d * 2 + 2.0 * T * (2 * T - 1) * d;
+  auto attn_flops_of = [&](int b0, int b1) {
+    double f = 0.0;
+    for (int b = b0; b < b1; ++b) {
+      const double T = p.v[b];
+      f += 2.0 * T * T * d * 2 + 2.0 * T * (2 * T - 1) * d;
+    }
+    return f;
+  };
+  auto max_v_of = [&](int b0, int b1) {
+    int m = 0;
+    for (int b = b0; b < b1; ++b) m = std::max(m, p.v[b]);
+    return m;
+  };
+  const bool two = p.split_b > 0 && !prof_on_;
+  if (!two) {
+    const Part all{0, 0, M, 0, p.B, p.max_v, t_tiles, ntiles, attn_flops_of(0, p.B)};
+    for (int li = 0; li < c.n_layers; ++li) PKC_ST(run_layer(p, li, all, st, err));
+    return PKC_OK;
   }
+  const int sb = p.split_b;
+  const Part p0{0, 0, p.v_off[sb], 0, sb, max_v_of(0, sb), t_tiles, p.ntiles0, attn_flops_of(0, sb)};
+  const Part p1{1, p.v_off[sb], M - p.v_off[sb], sb, p.B - sb, max_v_of(sb, p.B), t_tiles + 2 * p.ntiles0,
+                ntiles - p.ntiles0, attn_flops_of(sb, p.B)};
+  // fork: the second stream starts after everything issued so far on st
+  PKC_CK(cudaEventRecord(ev_fork_, st), "fork event");
+  PKC_CK(cudaStreamWaitEvent(stream2_, ev_fork_, 0), "fork wait");
   for (int li = 0; li < c.n_layers; ++li) {
-    const LayerWeights& L = w_.layers[li];
-    // FFN1: r = x + 0.5 * FFN(LN(x))
-    if (li == 0) {
-      prof_begin(st);
-      PKC_CK(layernorm_launch(b_.x, M, d, L.ln_ff1_g, L.ln_ff1_b, b_.hbuf, bf, nullptr, nullptr, false, st), "ln");
-      prof_end(st, "layernorm", 0.0, (double)M * d * (4 + hs));
-    }
-    PKC_ST(gemm(b_.hbuf, d, L.ff1_w1, d, bf, M, FF, d, EPI_STORE_H, ACT_SILU, 1.f, L.ff1_b1, b_.ffh, FF, st, "gemm_ffn", err, &L.ff1_q1));
-    // LayerNorm inside the consuming GEMM when its weight is dense: the GEMM
-    // that updates x before it also writes x's per-128-column row statistics
-    const bool lnq = L.qkv_ln, lnc = L.pw1_ln, lnf = L.ff2_ln;
-    PKC_ST(gemm(b_.ffh, FF, L.ff1_w2, FF, bf, M, d, FF, EPI_RESID_F32, ACT_NONE, 0.5f, L.ff1_b2, b_.x, d, st, "gemm_ffn", err, &L.ff1_q2,
-                lnq ? b_.stats : nullptr));
-    // MHSA
-    if (lnq) {
-      PKC_ST(gemm_ln(b_.x, b_.stats, L.qkv_w, bf, M, 3 * d, d, EPI_STORE_H, ACT_NONE, L.qkv_b,
-                     b_.qkv, 3 * d, st, "gemm_qkv", err));
-    } else {
-      prof_begin(st);
-      PKC_CK(layernorm_launch(b_.x, M, d, L.ln_att_g, L.ln_att_b, b_.hbuf, bf, nullptr, nullptr, false, st), "ln");
-      prof_end(st, "layernorm", 0.0, (double)M * d * (4 + hs));
-      PKC_ST(gemm(b_.hbuf, d, L.qkv_w, d, bf, M, 3 * d, d, EPI_STORE_H, ACT_NONE, 1.f, L.qkv_b, b_.qkv, 3 * d, st, "gemm_qkv", err, &L.qkv_q));
-    }
-    AttnArgs aa{b_.qkv, static_cast<const uint8_t*>(b_.ptab) + (size_t)li * d * 2, np, p.centre, Ld,
-                L.pos_u, L.pos_v, t_tiles, ntiles, t_v_off, t_v, b_.ctx, d, H, M, err_word_};
-    prof_begin(st);
-    PKC_CK(attention_launch(aa, bf, st), "attention");
-    prof_end(st, "attention", attn_flops, (double)M * (3 * d + d) * hs + (double)np * d * hs);
-    PKC_ST(gemm(b_.ctx, d, L.out_w, d, bf, M, d, d, EPI_RESID_F32, ACT_NONE, 1.f, L.out_b, b_.x, d, st, "gemm_out", err, &L.out_q,
-                lnc ? b_.stats : nullptr));
-    // conv module
-    if (lnc) {
-      PKC_ST(gemm_ln(b_.x, b_.stats, L.pw1_w, bf, M, 2 * d, d, EPI_GLU_H, ACT_NONE, L.pw1_b,
-                     b_.ctx, d, st, "gemm_pw1_glu", err));
-    } else {
-      prof_begin(st);
-      PKC_CK(layernorm_launch(b_.x, M, d, L.ln_conv_g, L.ln_conv_b, b_.hbuf, bf, nullptr, nullptr, false, st), "ln");
-      prof_end(st, "layernorm", 0.0, (double)M * d * (4 + hs));
-      PKC_ST(gemm(b_.hbuf, d, L.pw1_w, d, bf, M, 2 * d, d, EPI_GLU_H, ACT_NONE, 1.f, L.pw1_b, b_.ctx, d, st, "gemm_pw1_glu", err));
-    }
-    prof_begin(st);
-    PKC_CK(dwconv_bn_silu_launch(b_.ctx, b_.hbuf, d, K, L.dw_w, L.dw_b, L.bn_scale, L.bn_shift, t_v_off,
-                                 t_v, p.B, p.max_v, bf, st), "dwconv");
-    prof_end(st, "dwconv", 2.0 * M * d * K, (double)M * d * hs * 2);
-    PKC_ST(gemm(b_.hbuf, d, L.pw2_w, d, bf, M, d, d, EPI_RESID_F32, ACT_NONE, 1.f, L.pw2_b, b_.x, d, st, "gemm_pw2", err, nullptr,
-                lnf ? b_.stats : nullptr));
-    // FFN2
-    if (lnf) {
-      PKC_ST(gemm_ln(b_.x, b_.stats, L.ff2_w1, bf, M, FF, d, EPI_STORE_H, ACT_SILU, L.ff2_b1,
-                     b_.ffh, FF, st, "gemm_ffn", err));
-    } else {
-      prof_begin(st);
-      PKC_CK(layernorm_launch(b_.x, M, d, L.ln_ff2_g, L.ln_ff2_b, b_.hbuf, bf, nullptr, nullptr, false, st), "ln");
-      prof_end(st, "layernorm", 0.0, (double)M * d * (4 + hs));
-      PKC_ST(gemm(b_.hbuf, d, L.ff2_w1, d, bf, M, FF, d, EPI_STORE_H, ACT_SILU, 1.f, L.ff2_b1, b_.ffh, FF, st, "gemm_ffn", err, &L.ff2_q1));
-    }
-    PKC_ST(gemm(b_.ffh, FF, L.ff2_w2, FF, bf, M, d, FF, EPI_RESID_F32, ACT_NONE, 0.5f, L.ff2_b2, b_.x, d, st, "gemm_ffn", err, &L.ff2_q2));
-    // norm_out (+ next layer's norm_feed_forward1 in the same pass)
-    const bool last = li + 1 == c.n_layers;
-    const LayerWeights* N = last ? nullptr : &w_.layers[li + 1];
-    prof_begin(st);
-    PKC_CK(layernorm_launch(b_.x, M, d, L.ln_out_g, L.ln_out_b, last ? nullptr : b_.hbuf, bf,
-                            last ? nullptr : N->ln_ff1_g, last ? nullptr : N->ln_ff1_b, true, st), "ln");
-    prof_end(st, "layernorm", 0.0, (double)M * d * (8 + (last ? 0 : hs)));
+    PKC_ST(run_layer(p, li, p0, st, err));
+    PKC_ST(run_layer(p, li, p1, stream2_, err));
   }
+  // join: st continues once the second part is done
+  PKC_CK(cudaEventRecord(ev_join_, stream2_), "join event");
+  PKC_CK(cudaStreamWaitEvent(st, ev_join_, 0), "join wait");
+  return PKC_OK;
+}
+
+pkc_status DeviceRunner::run_layer(const Plan& p, int li, const Part& q, cudaStream_t st, std::string& err) {
+  const Config& c = cfg_;
+  const int d = c.d_model, FF = c.ff_dim, H = c.n_heads, K = c.conv_kernel;
+  const bool bf = c.bf16;
+  const int M = q.M;
+  const double hs = 2.0;
+  const int np = 2 * p.centre - 1;
+  const int Ld = c.n_layers * d;
+  sk_part_ = q.idx;
+  // this part's rows of every row-major activation
+  const size_t r0 = (size_t)q.row0;
+  float* x = b_.x + r0 * d;
+  void* hbuf = static_cast<uint8_t*>(b_.hbuf) + r0 * d * 2;
+  void* ffh = static_cast<uint8_t*>(b_.ffh) + r0 * FF * 2;
+  void* qkv = static_cast<uint8_t*>(b_.qkv) + r0 * 3 * d * 2;
+  void* ctx = static_cast<uint8_t*>(b_.ctx) + r0 * d * 2;
+  float* stats = b_.stats ? b_.stats + r0 * (d / 128) * 2 : nullptr;
+  const int* v_off = t_v_off + q.b0;  // global row offsets of this part's utterances
+  const int* v_len = t_v + q.b0;
+
+  const LayerWeights& L = w_.layers[li];
+  // FFN1: r = x + 0.5 * FFN(LN(x))
+  if (li == 0) {
+    prof_begin(st);
+    PKC_CK(layernorm_launch(x, M, d, L.ln_ff1_g, L.ln_ff1_b, hbuf, bf, nullptr, nullptr, false, st), "ln");
+    prof_end(st, "layernorm", 0.0, (double)M * d * (4 + hs));
+  }
+  PKC_ST(gemm(hbuf, d, L.ff1_w1, d, bf, M, FF, d, EPI_STORE_H, ACT_SILU, 1.f, L.ff1_b1, ffh, FF, st, "gemm_ffn", err, &L.ff1_q1));
+  // LayerNorm inside the consuming GEMM when its weight carries the folded
+  // LayerNorm: the GEMM that updates x before it also writes x's
+  // per-128-column row statistics
+  const bool lnq = L.qkv_ln, lnc = L.pw1_ln, lnf = L.ff2_ln;
+  PKC_ST(gemm(ffh, FF, L.ff1_w2, FF, bf, M, d, FF, EPI_RESID_F32, ACT_NONE, 0.5f, L.ff1_b2, x, d, st, "gemm_ffn", err, &L.ff1_q2,
+              lnq ? stats : nullptr));
+  // MHSA
+  if (lnq) {
+    PKC_ST(gemm_ln(x, stats, L.qkv_w, bf, M, 3 * d, d, EPI_STORE_H, ACT_NONE, L.qkv_b, qkv, 3 * d, st, "gemm_qkv", err));
+  } else {
+    prof_begin(st);
+    PKC_CK(layernorm_launch(x, M, d, L.ln_att_g, L.ln_att_b, hbuf, bf, nullptr, nullptr, false, st), "ln");
+    prof_end(st, "layernorm", 0.0, (double)M * d * (4 + hs));
+    PKC_ST(gemm(hbuf, d, L.qkv_w, d, bf, M, 3 * d, d, EPI_STORE_H, ACT_NONE, 1.f, L.qkv_b, qkv, 3 * d, st, "gemm_qkv", err, &L.qkv_q));
+  }
+  // attention addresses the whole qkv / ctx buffers by global row offsets
+  AttnArgs aa{b_.qkv, static_cast<const uint8_t*>(b_.ptab) + (size_t)li * d * 2, np, p.centre, Ld,
+              L.pos_u, L.pos_v, q.tiles, q.ntiles, t_v_off, t_v, b_.ctx, d, H, p.M, err_word_};
+  prof_begin(st);
+  PKC_CK(attention_launch(aa, bf, st), "attention");
+  prof_end(st, "attention", q.attn_flops, (double)M * (3 * d + d) * hs + (double)np * d * hs);
+  PKC_ST(gemm(ctx, d, L.out_w, d, bf, M, d, d, EPI_RESID_F32, ACT_NONE, 1.f, L.out_b, x, d, st, "gemm_out", err, &L.out_q,
+              lnc ? stats : nullptr));
+  // conv module
+  if (lnc) {
+    PKC_ST(gemm_ln(x, stats, L.pw1_w, bf, M, 2 * d, d, EPI_GLU_H, ACT_NONE, L.pw1_b, ctx, d, st, "gemm_pw1_glu", err));
+  } else {
+    prof_begin(st);
+    PKC_CK(layernorm_launch(x, M, d, L.ln_conv_g, L.ln_conv_b, hbuf, bf, nullptr, nullptr, false, st), "ln");
+    prof_end(st, "layernorm", 0.0, (double)M * d * (4 + hs));
+    PKC_ST(gemm(hbuf, d, L.pw1_w, d, bf, M, 2 * d, d, EPI_GLU_H, ACT_NONE, 1.f, L.pw1_b, ctx, d, st, "gemm_pw1_glu", err));
+  }
+  // the depthwise kernel addresses rows by global offsets too
+  prof_begin(st);
+  PKC_CK(dwconv_bn_silu_launch(b_.ctx, b_.hbuf, d, K, L.dw_w, L.dw_b, L.bn_scale, L.bn_shift, v_off, v_len, q.nb,
+                               q.max_v, bf, st), "dwconv");
+  prof_end(st, "dwconv", 2.0 * M * d * K, (double)M * d * hs * 2);
+  PKC_ST(gemm(hbuf, d, L.pw2_w, d, bf, M, d, d, EPI_RESID_F32, ACT_NONE, 1.f, L.pw2_b, x, d, st, "gemm_pw2", err, nullptr,
+              lnf ? stats : nullptr));
+  // FFN2
+  if (lnf) {
+    PKC_ST(gemm_ln(x, stats, L.ff2_w1, bf, M, FF, d, EPI_STORE_H, ACT_SILU, L.ff2_b1, ffh, FF, st, "gemm_ffn", err));
+  } else {
+    prof_begin(st);
+    PKC_CK(layernorm_launch(x, M, d, L.ln_ff2_g, L.ln_ff2_b, hbuf, bf, nullptr, nullptr, false, st), "ln");
+    prof_end(st, "layernorm", 0.0, (double)M * d * (4 + hs));
+    PKC_ST(gemm(hbuf, d, L.ff2_w1, d, bf, M, FF, d, EPI_STORE_H, ACT_SILU, 1.f, L.ff2_b1, ffh, FF, st, "gemm_ffn", err, &L.ff2_q1));
+  }
+  PKC_ST(gemm(ffh, FF, L.ff2_w2, FF, bf, M, d, FF, EPI_RESID_F32, ACT_NONE, 0.5f, L.ff2_b2, x, d, st, "gemm_ffn", err, &L.ff2_q2));
+  // norm_out (+ next layer's norm_feed_forward1 in the same pass)
+  const bool last = li + 1 == c.n_layers;
+  const LayerWeights* N = last ? nullptr : &w_.layers[li + 1];
+  prof_begin(st);
+  PKC_CK(layernorm_launch(x, M, d, L.ln_out_g, L.ln_out_b, last ? nullptr : hbuf, bf,
+                          last ? nullptr : N->ln_ff1_g, last ? nullptr : N->ln_ff1_b, true, st), "ln");
+  prof_end(st, "layernorm", 0.0, (double)M * d * (8 + (last ? 0 : hs)));
   return PKC_OK;
 }
 
@@ -522,7 +618,7 @@ pkc_status DeviceRunner::finish(cudaStream_t st, std::string& err) {
   if (h_err != 0) {
     cudaMemsetAsync(err_word_, 0, sizeof(int), st);
     // a launch that gave up may have left stream-K flags raised
-    if (sk_flags_) cudaMemsetAsync(sk_flags_, 0, gemm_sk_flag_count(sk_pairs_) * sizeof(int), st);
+    if (sk_flags_) cudaMemsetAsync(sk_flags_, 0, 2 * gemm_sk_flag_count(sk_pairs_) * sizeof(int), st);
     cudaStreamSynchronize(st);
     err = "kernel reported error " + std::to_string(h_err) + " (bounded wait timed out)";
     return PKC_ERR_KERNEL;

@@ -23,7 +23,14 @@ struct Plan {
   int total_frames = 0, M1 = 0, M2 = 0, M = 0;
   int max_Tm = 0, max_v1 = 0, max_v2 = 0, max_v = 0;
   int centre = 0;                     // positional table centre = max v
-  std::vector<int> attn_tiles;        // (item, q0) pairs
+  std::vector<int> attn_tiles;        // (item, q0) pairs: part 0's tiles, then part 1's
+  // The conformer layers run as two independent parts on two streams when
+  // split_b > 0: utterances [0, split_b) (rows [0, v_off[split_b])) and the
+  // rest, so one part's kernel tails and latency-bound kernels overlap the
+  // other part's work. Every kernel treats rows / utterances independently,
+  // so the result is the same bits as one part.
+  int split_b = 0;
+  int ntiles0 = 0;                    // attention tiles of part 0
 };
 
 // n_samples given: PCM path. mel_T given instead (n_samples empty): mel path
@@ -66,6 +73,16 @@ class DeviceRunner {
   pkc_status prepare(const Plan& p, cudaStream_t st, std::string& err);
   pkc_status run_frontend(const Plan& p, cudaStream_t st, std::string& err);
   pkc_status run_encoder(const Plan& p, cudaStream_t st, std::string& err);
+  // a contiguous range of utterances / rows the layers are issued for
+  struct Part {
+    int idx;                  // 0 or 1 (selects the stream-K workspace half)
+    int row0, M;              // rows [row0, row0 + M)
+    int b0, nb, max_v;        // utterances [b0, b0 + nb)
+    const int* tiles;         // attention tiles (item, q0) of these utterances
+    int ntiles;
+    double attn_flops;
+  };
+  pkc_status run_layer(const Plan& p, int li, const Part& q, cudaStream_t st, std::string& err);
   pkc_status finish(cudaStream_t st, std::string& err);
   bool ensure_ws(size_t bytes);
   void prof_begin(cudaStream_t st);
@@ -89,9 +106,13 @@ class DeviceRunner {
   size_t ws_bytes_ = 0;
   int* err_word_ = nullptr;
   // stream-K workspace of the 2-SM GEMM (flags zero between launches)
-  float* sk_ws_ = nullptr;
+  float* sk_ws_ = nullptr;      // two halves, one per layer part
   int* sk_flags_ = nullptr;
   int sk_pairs_ = 0;
+  int sk_part_ = 0;             // part whose GEMMs are being issued
+  // second stream of the two-part layer schedule, and its fork / join events
+  cudaStream_t stream2_ = nullptr;
+  cudaEvent_t ev_fork_ = nullptr, ev_join_ = nullptr;
   bool sub_unfused_ = false;
   bool ln_unfused_ = false;
   int* h_tables_ = nullptr;  // pinned staging for the item tables

@@ -199,3 +199,32 @@ def test_fused_layernorm_matches_separate_layernorm(models, oracles, kind, monke
         assert rel_err(a, r.T) < 2e-2
         assert rel_err(b, r.T) < 2e-2
         assert rel_err(a, b) < 1e-2
+
+
+@pytest.mark.parametrize("kind", ["f16", "q8_0"])
+def test_two_part_layer_schedule_is_bitwise_single_stream(models, oracles, kind, monkeypatch):
+    """Large batches run their conformer layers as two utterance-contiguous
+    parts on two streams inside the CUDA graph (forced here with
+    PKC_STREAMS=2); every kernel computes a row / utterance the same way in
+    either schedule, so the output equals the one-stream schedule
+    (PKC_STREAMS=1) bit for bit, and stays within the oracle bound."""
+    import oracle
+    import pkc
+    pcm = clips([SR * 15 + 1000 * i for i in range(8)], seed=31)
+    monkeypatch.setenv("PKC_STREAMS", "2")
+    m = pkc.Model(models[kind])
+    try:
+        two = m.encode_pcm_batch(pcm)
+    finally:
+        m.close()
+    monkeypatch.setenv("PKC_STREAMS", "1")
+    m = pkc.Model(models[kind])
+    try:
+        one = m.encode_pcm_batch(pcm)
+    finally:
+        m.close()
+    for a, b in zip(two, one):
+        np.testing.assert_array_equal(a, b)
+    ref = oracle.encode_pcm_batch(oracles(kind), pcm[:2])
+    for a, r in zip(two[:2], ref.outs):
+        assert rel_err(a, r.T) < 2e-2
