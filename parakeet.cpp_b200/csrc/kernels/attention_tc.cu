@@ -167,7 +167,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   pdl_wait();
   pdl_trigger();
 
-  const int tile = blockIdx.x, head = blockIdx.y;
+  // heads vary fastest in launch order, so every head of the longest tile
+  // (the tile list is sorted longest utterance first) is issued first
+  const int head = blockIdx.x, tile = blockIdx.y;
   const int item = p.tiles[2 * tile], q0 = p.tiles[2 * tile + 1];
   const int off = p.item_off[item], T = p.item_len[item];
   const int nT = (T + KN - 1) / KN;
@@ -576,7 +578,7 @@ cudaError_t launch_tc(const AttnArgs& a, cudaStream_t st) {
     return cudaErrorInvalidValue;
   TcParams p{a.tiles, a.item_off, a.item_len, a.bias_u, a.bias_v, a.ctx, a.d, a.centre,
              1.4426950408889634f / sqrtf((float)DK), a.err};
-  return launch_pdl(kern, dim3(a.n_tiles, a.n_heads), dim3(THREADS), smem, st, tq, tp, p);
+  return launch_pdl(kern, dim3(a.n_heads, a.n_tiles), dim3(THREADS), smem, st, tq, tp, p);
 }
 
 }  // namespace
@@ -589,6 +591,7 @@ cudaError_t attention_tc_launch(const AttnArgs& a, bool bf16, cudaStream_t st) {
       (reinterpret_cast<uintptr_t>(a.qkv) & 15) || (reinterpret_cast<uintptr_t>(a.ptab) & 15) ||
       (reinterpret_cast<uintptr_t>(a.bias_u) & 15) || (reinterpret_cast<uintptr_t>(a.bias_v) & 15))
     return cudaErrorInvalidValue;
+  if (a.n_tiles > 65535) return cudaErrorInvalidValue;  // grid y
   const int dk = a.d / a.n_heads;
   if (dk == 128) return bf16 ? launch_tc<__nv_bfloat16, 128>(a, st) : launch_tc<__half, 128>(a, st);
   if (dk == 64) return bf16 ? launch_tc<__nv_bfloat16, 64>(a, st) : launch_tc<__half, 64>(a, st);
