@@ -117,9 +117,24 @@ __global__ void k_pos_table(H* out, int centre, int d) {
 // amplification (DW_FRAMES + K - 1) / DW_FRAMES -- keeps the K taps in
 // registers, and writes DW_FRAMES rows. grid (ceil(max_len / DW_FRAMES), B,
 // ceil(d / DW_CH)).
+// Depthwise Conv1d over each utterance's frames + bias -> BatchNorm -> SiLU.
+// A thread owns 2 channels (one 4-byte load per row: a warp reads 128
+// contiguous bytes) and DW_FRAMES output frames; it loads the
+// DW_FRAMES + K - 1 input rows once, converts each to f32 once, and
+// accumulates the K taps in f32. 256 threads cover 512 channels.
 constexpr int DW_FRAMES = 16;
-constexpr int DW_THREADS = 64;
-constexpr int DW_CH = DW_THREADS * 8;
+constexpr int DW_THREADS = 256;
+constexpr int DW_CH = DW_THREADS * 2;
+
+template <typename H> struct H2;
+template <> struct H2<__half> {
+  static __device__ __forceinline__ float2 to_f2(uint32_t v) { return __half22float2(*reinterpret_cast<const __half2*>(&v)); }
+};
+template <> struct H2<__nv_bfloat16> {
+  static __device__ __forceinline__ float2 to_f2(uint32_t v) {
+    return __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&v));
+  }
+};
 
 template <typename H, int K>
 __global__ void __launch_bounds__(DW_THREADS)
@@ -132,59 +147,44 @@ __global__ void __launch_bounds__(DW_THREADS)
   const int b = blockIdx.y;
   const int T = item_len[b];
   const int t0 = blockIdx.x * DW_FRAMES;
-  const int c0 = blockIdx.z * DW_CH + threadIdx.x * 8;
+  const int c0 = blockIdx.z * DW_CH + threadIdx.x * 2;
   if (t0 >= T || c0 >= d) return;
   constexpr int pad = (K - 1) / 2;
   constexpr int NR = DW_FRAMES + K - 1;
   const H* x = in + (size_t)item_off[b] * d + c0;
   H* y = out + (size_t)item_off[b] * d + c0;
-  uint4 rows[NR];
+  uint32_t raw[NR];
 #pragma unroll
   for (int r = 0; r < NR; ++r) {
     const int ti = t0 - pad + r;
-    rows[r] = (ti >= 0 && ti < T) ? __ldg(reinterpret_cast<const uint4*>(x + (size_t)ti * d)) : make_uint4(0, 0, 0, 0);
+    raw[r] = (ti >= 0 && ti < T) ? __ldg(reinterpret_cast<const uint32_t*>(x + (size_t)ti * d)) : 0u;
   }
-  float wk[K][8];
+  float2 wk[K];
 #pragma unroll
-  for (int k = 0; k < K; ++k) {
-    const float4 wa = __ldg(reinterpret_cast<const float4*>(w + (size_t)k * d + c0));
-    const float4 wb = __ldg(reinterpret_cast<const float4*>(w + (size_t)k * d + c0 + 4));
-    wk[k][0] = wa.x; wk[k][1] = wa.y; wk[k][2] = wa.z; wk[k][3] = wa.w;
-    wk[k][4] = wb.x; wk[k][5] = wb.y; wk[k][6] = wb.z; wk[k][7] = wb.w;
-  }
-  const float4 s0 = __ldg(reinterpret_cast<const float4*>(scale + c0)), s1 = __ldg(reinterpret_cast<const float4*>(scale + c0 + 4));
-  const float4 h0 = __ldg(reinterpret_cast<const float4*>(shift + c0)), h1 = __ldg(reinterpret_cast<const float4*>(shift + c0 + 4));
-  float sc[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-  float sh[8] = {h0.x, h0.y, h0.z, h0.w, h1.x, h1.y, h1.z, h1.w};
+  for (int k = 0; k < K; ++k) wk[k] = __ldg(reinterpret_cast<const float2*>(w + (size_t)k * d + c0));
+  const float2 sc = __ldg(reinterpret_cast<const float2*>(scale + c0));
+  float2 sh = __ldg(reinterpret_cast<const float2*>(shift + c0));
   if (bias) {
     // (acc + bias) * scale + shift = acc * scale + (bias * scale + shift)
-    const float4 b0 = __ldg(reinterpret_cast<const float4*>(bias + c0)), b1 = __ldg(reinterpret_cast<const float4*>(bias + c0 + 4));
-    const float bi[8] = {b0.x, b0.y, b0.z, b0.w, b1.x, b1.y, b1.z, b1.w};
-#pragma unroll
-    for (int c = 0; c < 8; ++c) sh[c] = fmaf(bi[c], sc[c], sh[c]);
+    const float2 bi = __ldg(reinterpret_cast<const float2*>(bias + c0));
+    sh.x = fmaf(bi.x, sc.x, sh.x);
+    sh.y = fmaf(bi.y, sc.y, sh.y);
   }
+  float2 xf[NR];
+#pragma unroll
+  for (int r = 0; r < NR; ++r) xf[r] = H2<H>::to_f2(raw[r]);
   const int nf = min(DW_FRAMES, T - t0);
 #pragma unroll
   for (int f = 0; f < DW_FRAMES; ++f) {
     if (f >= nf) break;
-    float acc[8];
-#pragma unroll
-    for (int c = 0; c < 8; ++c) acc[c] = 0.f;
+    float a0 = 0.f, a1 = 0.f;
 #pragma unroll
     for (int k = 0; k < K; ++k) {
-      const H* hv = reinterpret_cast<const H*>(&rows[f + k]);
-#pragma unroll
-      for (int c = 0; c < 8; ++c) acc[c] = fmaf(wk[k][c], from_h(hv[c]), acc[c]);
+      a0 = fmaf(wk[k].x, xf[f + k].x, a0);
+      a1 = fmaf(wk[k].y, xf[f + k].y, a1);
     }
-    float r[8];
-#pragma unroll
-    for (int c = 0; c < 8; ++c) r[c] = siluf_(fmaf(acc[c], sc[c], sh[c]));
-    uint4 o;
-    o.x = pack2<H>(r[0], r[1]);
-    o.y = pack2<H>(r[2], r[3]);
-    o.z = pack2<H>(r[4], r[5]);
-    o.w = pack2<H>(r[6], r[7]);
-    *reinterpret_cast<uint4*>(y + (size_t)(t0 + f) * d) = o;
+    *reinterpret_cast<uint32_t*>(y + (size_t)(t0 + f) * d) =
+        pack2<H>(siluf_(fmaf(a0, sc.x, sh.x)), siluf_(fmaf(a1, sc.y, sh.y)));
   }
 }
 
