@@ -245,6 +245,34 @@ def run_ours(args, rank, world, local_rank):
     e2e_wall = time.perf_counter() - t0
     e2e_ms = e_start.elapsed_time(e_end)
 
+    # ---- CTC transcription (models with a CTC head: the hybrid C1 / C4 and
+    # CTC models): PCM -> tokens through pkc_ctc_greedy_pcm_batch, host
+    # buffers, the head's kernels profiled beside it
+    ctc = None
+    if model.ctc_classes() > 0:
+        for _ in range(max(1, args.warmup)):
+            model.ctc_greedy_pcm_batch(host_pcm)
+        c_start = torch.cuda.Event(enable_timing=True)
+        c_end = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(dev)
+        c_start.record(lib_stream)
+        for _ in range(args.steps):
+            model.ctc_greedy_pcm_batch(host_pcm)
+        c_end.record(lib_stream)
+        torch.cuda.synchronize(dev)
+        ctc_ms = c_start.elapsed_time(c_end) / args.steps
+        model.profile_enable(True)
+        model.ctc_greedy_pcm_batch(host_pcm)
+        torch.cuda.synchronize(dev)
+        cst = [s for s in model.profile_read() if s["name"].startswith(("ctc_", "gemm_ctc"))]
+        model.profile_enable(False)
+        ctc = {"metric": "CTC transcription RTFx (PCM -> tokens: encoder + CTC head on the GPU, greedy fold on the host)",
+               "value": round(audio_s / (ctc_ms / 1e3), 1), "unit": UNIT, "ms_per_step": round(ctc_ms, 3),
+               "classes": model.ctc_classes(), "api": "pkc_ctc_greedy_pcm_batch (host buffers)",
+               "head_kernels": [{"name": s["name"], "ms": round(s["total_ms"], 4),
+                                 **({"tflops": round(s["flops"] / (s["total_ms"] / 1e3) / 1e12, 1)} if s["flops"] > 0 else
+                                    {"gbs": round(s["bytes"] / (s["total_ms"] / 1e3) / 1e9, 1)})} for s in cst]}
+
     ms_max, e2e_max, audio_total, wall_max = combine_ranks(ms, e2e_ms, audio_s, e2e_wall * 1e3, world, dev)
     model.close()
     if rank != 0:
@@ -295,6 +323,8 @@ def run_ours(args, rank, world, local_rank):
         "kernels": kernels,
         "clocks": clk.summary(),
     }
+    if ctc is not None:
+        line["ctc"] = ctc
     if not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args, path, pcm)
     return line

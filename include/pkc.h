@@ -26,6 +26,7 @@
 #define PKC_H
 
 #include <stddef.h>
+#include <stdint.h>
 
 #ifdef __cplusplus
 extern "C" {
@@ -114,6 +115,43 @@ pkc_status pkc_encode_batch(pkc_model* m, const float* mel, int B, int n_mels, i
    With several devices the clips are sharded across them by length. */
 pkc_status pkc_encode_pcm_batch(pkc_model* m, const float* const* pcm, const int* n_samples,
                                 int B, int layout, float* out, size_t out_cap, int* valid_Tout);
+
+/* One decoded token, laid out as the reference's TokenInfo
+   (src/decode_types.hpp:27-32): vocabulary id, frame (the token's
+   start_offset in encoder frames), confidence (NeMo's max_prob, min over the
+   token's argmax run) and span (1, as ctc_greedy emits it). */
+typedef struct pkc_token {
+  int32_t id;
+  int32_t frame;
+  float conf;
+  int32_t span;
+} pkc_token;
+
+/* Classes of the model's CTC head (vocab + 1, the blank included), 0 if the
+   GGUF has no CTC head (ctc_decoder.decoder_layers.0.* of hybrid models or
+   decoder.decoder_layers.0.* of CTC models, src/ctc_decoder.cpp:17-28). */
+int pkc_ctc_classes(const pkc_model* m);
+
+/* CTC transcription of B clips of PCM: mel front end + encoder + CTC head on
+   the GPU (the linear d -> V+1 and log_softmax of CTCDecoder::forward,
+   src/ctc_decoder.cpp:35-116, with the per-frame argmax and maximum
+   log-probability), then the greedy fold of ctc_greedy (src/search.cpp:21-90)
+   on the host. tokens_out receives the clips' tokens back to back,
+   n_tokens[b] clip b's count (a clip yields at most its encoder frame count,
+   so tokens_cap = the sum of those always suffices). logprobs_out may be NULL;
+   else it receives the log-probabilities [sum T'_b, V+1] time-major, clips
+   back to back (logprobs_cap floats). */
+pkc_status pkc_ctc_greedy_pcm_batch(pkc_model* m, const float* const* pcm, const int* n_samples, int B,
+                                    pkc_token* tokens_out, size_t tokens_cap, int* n_tokens,
+                                    float* logprobs_out, size_t logprobs_cap);
+
+/* The greedy fold alone (host arithmetic, no device): T frames of per-frame
+   argmax class and maximum log-probability -> tokens, following ctc_greedy
+   (src/search.cpp:21-90) over n_classes classes with the given blank id.
+   Returns the token count, or -1 if it exceeds cap (cap >= T always
+   suffices) or the arguments are invalid. */
+int pkc_ctc_fold(const int32_t* argmax, const float* max_logprob, int T, int n_classes, int blank_id,
+                 pkc_token* out, int cap);
 
 /* Floats needed by pkc_encode_pcm_batch's `out` for these clip lengths. */
 size_t pkc_encode_out_floats(const pkc_model* m, const int* n_samples, int B);

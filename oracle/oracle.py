@@ -13,6 +13,8 @@ What it restates (paths inside parakeet.cpp, the reference):
   * build_conv_module (batched)                      src/conformer.cpp:38-164
   * ConformerLayer::build_graph_batched              src/conformer.cpp:285-353
   * Encoder::forward_batch                           src/encoder.cpp:97-167
+  * CTCDecoder::forward (CTC head)                   src/ctc_decoder.cpp:35-116
+  * ctc_greedy (greedy fold, token frame / conf)     src/search.cpp:8-90
 The batched graph is restated literally: every item is zero-padded to the
 batch's T_max and every mask the reference builds (per-stage subsampling time
 masks, output-frame mask, attention key mask and padded-query zeroing, conv
@@ -436,3 +438,49 @@ def encode_pcm_batch(w: Weights, pcms, n_layers: int | None = None, gpu_graph_me
     """Model::transcribe_16k_batch steps 1-2 (src/model.cpp:164-181)."""
     mel, Ts = mel_batch(w, pcms, gpu_graph=gpu_graph_mel)
     return encoder_forward_batch(w, mel, Ts, n_layers=n_layers)
+
+
+# ------------------------------------------------------------------ CTC head
+
+def ctc_head_weights(w: Weights):
+    """The CTC head's weight [V+1, d] and bias [V+1] (hybrid name first, then
+    the standalone CTC model's, as src/ctc_decoder.cpp:17-28), or None."""
+    for pre in ("ctc_decoder.decoder_layers.0.", "decoder.decoder_layers.0."):
+        if pre + "weight" in w.t and pre + "bias" in w.t:
+            W = w.t[pre + "weight"].astype(np.float64)
+            return W.reshape(W.shape[0], -1), w.t[pre + "bias"].astype(np.float64)
+    return None
+
+
+def ctc_log_probs(w: Weights, x: np.ndarray) -> np.ndarray:
+    """CTCDecoder::forward (src/ctc_decoder.cpp:35-116): log_softmax(x W^T + b)
+    over the V+1 classes. x [T, d] time-major -> [T, V+1], float64."""
+    W, b = ctc_head_weights(w)
+    y = x.astype(np.float64) @ W.T + b
+    m = y.max(axis=1, keepdims=True)
+    return y - m - np.log(np.exp(y - m).sum(axis=1, keepdims=True))
+
+
+def ctc_greedy(logp: np.ndarray, blank_id: int):
+    """ctc_greedy (src/search.cpp:21-90): per-frame argmax (first maximum),
+    fold_consecutive emission, token frame = previous token's emit frame (the
+    first token's: max(0, t-1)), confidence = min over the token's argmax run of
+    (N exp(max logp) - 1) / (N - 1), span 1. Returns [(id, frame, conf, span)]."""
+    T, N = logp.shape
+    out = []
+    previous, prev_peak, have_prev, run_min = blank_id, 0, False, 1.0
+    for t in range(T):
+        p = int(np.argmax(logp[t]))
+        c = (N * math.exp(float(logp[t, p])) - 1.0) / (N - 1.0)
+        emit = (p != previous or previous == blank_id) and p != blank_id
+        if emit:
+            if out:
+                out[-1][2] = run_min
+            out.append([p, prev_peak if have_prev else max(0, t - 1), 0.0, 1])
+            run_min, prev_peak, have_prev = c, t, True
+        elif p == previous and p != blank_id:
+            run_min = min(run_min, c)
+        previous = p
+    if out:
+        out[-1][2] = run_min
+    return [tuple(o) for o in out]

@@ -2,6 +2,7 @@
 // multi-GPU sharding and profiling. No exception crosses this boundary.
 #include <algorithm>
 #include <cstring>
+#include <cmath>
 #include <memory>
 #include <mutex>
 #include <numeric>
@@ -124,6 +125,120 @@ int pkc_mel_frames(const pkc_model* m, int n_samples) {
 int pkc_encoder_frames(const pkc_model* m, int mel_frames) {
   if (!m || mel_frames <= 0) return 0;
   return pkc::encoder_frames_for(mel_frames);
+}
+
+int pkc_ctc_classes(const pkc_model* m) {
+  if (!m || m->runners.empty()) return 0;
+  return m->runners[0]->ctc_classes();
+}
+
+int pkc_ctc_fold(const int32_t* argmax, const float* max_logprob, int T, int n_classes, int blank_id,
+                 pkc_token* out, int cap) {
+  if (T < 0 || n_classes <= 1 || (T > 0 && (!argmax || !max_logprob)) || (cap > 0 && !out)) return -1;
+  // NeMo's rescaled max_prob confidence of one frame: (N p_max - 1) / (N - 1)
+  const float N = (float)n_classes;
+  auto conf = [&](float lp) { return (N * std::exp(lp) - 1.0f) / (N - 1.0f); };
+  // fold_consecutive: emit p when it differs from the previous frame's class
+  // (or that was blank) and is not blank; a token's frame is the previous
+  // token's emit frame (the first token's: its own minus one, floored at 0);
+  // its confidence the minimum over its argmax run
+  int n = 0;
+  int32_t previous = blank_id;
+  int prev_peak = 0;
+  bool have_prev = false;
+  float run_min = 1.0f;
+  for (int t = 0; t < T; ++t) {
+    const int32_t p = argmax[t];
+    const bool emit = (p != previous || previous == blank_id) && p != blank_id;
+    if (emit) {
+      if (n >= cap) return -1;
+      if (n > 0) out[n - 1].conf = run_min;
+      out[n] = pkc_token{p, have_prev ? (int32_t)prev_peak : (int32_t)(t > 0 ? t - 1 : 0), 0.0f, 1};
+      ++n;
+      run_min = conf(max_logprob[t]);
+      prev_peak = t;
+      have_prev = true;
+    } else if (p == previous && p != blank_id) {
+      run_min = std::min(run_min, conf(max_logprob[t]));
+    }
+    previous = p;
+  }
+  if (n > 0) out[n - 1].conf = run_min;
+  return n;
+}
+
+pkc_status pkc_ctc_greedy_pcm_batch(pkc_model* m, const float* const* pcm, const int* n_samples, int B,
+                                    pkc_token* tokens_out, size_t tokens_cap, int* n_tokens,
+                                    float* logprobs_out, size_t logprobs_cap) {
+  if (!m) return pkc::set_thread_error(PKC_ERR_ARG, "pkc_ctc_greedy_pcm_batch: model is NULL");
+  std::lock_guard<std::mutex> lk(m->mu);
+  if (!pcm || !n_samples || B <= 0 || !n_tokens || (tokens_cap > 0 && !tokens_out))
+    return fail(m, PKC_ERR_ARG, "pkc_ctc_greedy_pcm_batch: bad arguments");
+  const int V1 = m->runners[0]->ctc_classes();
+  if (!V1) return fail(m, PKC_ERR_UNSUPPORTED, "pkc_ctc_greedy_pcm_batch: the model has no CTC head");
+  try {
+    std::vector<size_t> off(B + 1, 0);  // frame offsets
+    for (int b = 0; b < B; ++b) {
+      if (n_samples[b] <= 0 || !pcm[b]) return fail(m, PKC_ERR_ARG, "pkc_ctc_greedy_pcm_batch: empty clip " + std::to_string(b));
+      off[b + 1] = off[b] + (size_t)pkc::encoder_frames_for(pkc::mel_frames_for(m->cfg, n_samples[b]));
+    }
+    const size_t M = off[B];
+    if (logprobs_out && logprobs_cap < M * (size_t)V1)
+      return fail(m, PKC_ERR_ARG, "pkc_ctc_greedy_pcm_batch: logprobs_out too small");
+    std::vector<int32_t> am(M);
+    std::vector<float> ml(M);
+    const int nd = (int)m->runners.size();
+    std::vector<double> cost(B);
+    for (int b = 0; b < B; ++b) cost[b] = clip_cost((int)(off[b + 1] - off[b]));
+    std::vector<int> assign(B, 0);
+    if (nd > 1) lpt_assign(cost, nd, assign);
+    std::vector<std::vector<int>> items(nd);
+    for (int b = 0; b < B; ++b) items[assign[b]].push_back(b);
+    std::vector<pkc_status> st(nd, PKC_OK);
+    std::vector<std::string> errs(nd);
+    auto run = [&](int k) {
+      try {
+        std::vector<const float*> p;
+        std::vector<int> n;
+        size_t tot = 0;
+        for (int b : items[k]) { p.push_back(pcm[b]); n.push_back(n_samples[b]); tot += off[b + 1] - off[b]; }
+        std::vector<int32_t> a(tot);
+        std::vector<float> l(tot), lp(logprobs_out ? tot * V1 : 0);
+        st[k] = m->runners[k]->ctc_pcm_host(p, n, a.data(), l.data(), logprobs_out ? lp.data() : nullptr, errs[k]);
+        if (st[k] != PKC_OK) return;
+        size_t pos = 0;  // scatter this device's clips back into batch order
+        for (int b : items[k]) {
+          const size_t t = off[b + 1] - off[b];
+          std::memcpy(am.data() + off[b], a.data() + pos, t * 4);
+          std::memcpy(ml.data() + off[b], l.data() + pos, t * 4);
+          if (logprobs_out) std::memcpy(logprobs_out + off[b] * V1, lp.data() + pos * V1, t * V1 * 4);
+          pos += t;
+        }
+      } catch (const std::exception& e) {
+        st[k] = PKC_ERR_INTERNAL;
+        errs[k] = e.what();
+      }
+    };
+    std::vector<std::thread> th;
+    for (int k = 0; k < nd; ++k)
+      if (!items[k].empty()) th.emplace_back(run, k);
+    for (auto& t : th) t.join();
+    for (int k = 0; k < nd; ++k)
+      if (st[k] != PKC_OK) return fail(m, st[k], "device " + std::to_string(m->runners[k]->device()) + ": " + errs[k]);
+    size_t used = 0;
+    for (int b = 0; b < B; ++b) {
+      const int T = (int)(off[b + 1] - off[b]);
+      const int cap = (int)std::min<size_t>(tokens_cap - used, (size_t)0x7fffffff);
+      const int n = pkc_ctc_fold(am.data() + off[b], ml.data() + off[b], T, V1, m->cfg.blank_id,
+                                 tokens_out ? tokens_out + used : nullptr, cap);
+      if (n < 0) return fail(m, PKC_ERR_ARG, "pkc_ctc_greedy_pcm_batch: tokens_out too small");
+      n_tokens[b] = n;
+      used += (size_t)n;
+    }
+    return PKC_OK;
+  } catch (const std::exception& e) {
+    return fail(m, PKC_ERR_INTERNAL, e.what());
+  }
 }
 
 size_t pkc_encode_out_floats(const pkc_model* m, const int* n_samples, int B) {

@@ -124,6 +124,7 @@ DeviceRunner::~DeviceRunner() {
   if (err_word_) cudaFree(err_word_);
   if (sk_ws_) cudaFree(sk_ws_);
   if (sk_flags_) cudaFree(sk_flags_);
+  if (ctc_ws_) cudaFree(ctc_ws_);
   if (stream2_) {
     cudaStreamSynchronize(stream2_);
     cudaStreamDestroy(stream2_);
@@ -726,6 +727,68 @@ pkc_status DeviceRunner::encode_pcm_host(const std::vector<const float*>& pcm,
   const int d = cfg_.d_model;
   const float* src = cf ? b_.out : b_.x;
   PKC_CK(cudaMemcpyAsync(host_out, src, (size_t)p.M * d * 4, cudaMemcpyDeviceToHost, st), "output download");
+  return finish(st, err);
+}
+
+pkc_status DeviceRunner::ctc_pcm_host(const std::vector<const float*>& pcm, const std::vector<int>& n,
+                                      int* argmax_out, float* maxlp_out, float* logprobs_out, std::string& err) {
+  if (!w_.ctc_v1) {
+    err = "the model has no CTC head";
+    return PKC_ERR_UNSUPPORTED;
+  }
+  cudaSetDevice(device_);
+  Plan p;
+  make_plan(cfg_, n, {}, p);
+  cudaStream_t st = stream_;
+  PKC_ST(prepare(p, st, err));
+  for (int b = 0; b < p.B; ++b)
+    if (n[b] > 0)
+      PKC_CK(cudaMemcpyAsync(b_.pcm + p.pcm_off[b], pcm[b], (size_t)n[b] * 4, cudaMemcpyHostToDevice, st), "pcm upload");
+  PKC_ST(run_graphed(p, st, false, err));  // x: time-major [M, d]
+  const int M = p.M, d = cfg_.d_model, V1 = w_.ctc_v1, Vp = w_.ctc_vpad;
+  const size_t o_a = 0, o_l = al((size_t)M * 3 * d * 2), o_am = o_l + al((size_t)M * Vp * 4),
+               o_ml = o_am + al((size_t)M * 4), o_lp = o_ml + al((size_t)M * 4);
+  const size_t bytes = o_lp + (logprobs_out ? al((size_t)M * V1 * 4) : 0);
+  if (bytes > ctc_ws_bytes_) {
+    cudaStreamSynchronize(st);
+    if (ctc_ws_) cudaFree(ctc_ws_);
+    ctc_ws_ = nullptr;
+    ctc_ws_bytes_ = 0;
+    PKC_CK(cudaMalloc(&ctc_ws_, bytes + bytes / 8), "CTC scratch allocation");
+    ctc_ws_bytes_ = bytes + bytes / 8;
+  }
+  uint8_t* scratch = static_cast<uint8_t*>(ctc_ws_);
+  float* logits = reinterpret_cast<float*>(scratch + o_l);
+  int* am = reinterpret_cast<int*>(scratch + o_am);
+  float* ml = reinterpret_cast<float*>(scratch + o_ml);
+  float* lp = logprobs_out ? reinterpret_cast<float*>(scratch + o_lp) : nullptr;
+  sk_part_ = 0;
+  pkc_status s = PKC_OK;
+  do {
+    prof_begin(st);
+    cudaError_t e = ctc_split3_launch(b_.x, M, d, scratch + o_a, st);
+    prof_end(st, "ctc_split", 0.0, (double)M * d * (4 + 6));
+    if (e != cudaSuccess) { err = std::string("ctc split: ") + cudaGetErrorString(e); s = PKC_ERR_CUDA; break; }
+    // f16 split operands whatever the model's compute type
+    s = gemm(scratch + o_a, 3 * d, w_.ctc_w, 3 * d, false, M, Vp, 3 * d, EPI_STORE_F32, ACT_NONE, 1.f, w_.ctc_b,
+             logits, Vp, st, "gemm_ctc", err);
+    if (s != PKC_OK) break;
+    prof_begin(st);
+    e = ctc_rows_launch(logits, M, Vp, V1, am, ml, lp, st);
+    prof_end(st, "ctc_rows", 0.0, (double)M * V1 * 4 * (lp ? 3 : 2) + (double)M * 8);
+    if (e != cudaSuccess) { err = std::string("ctc rows: ") + cudaGetErrorString(e); s = PKC_ERR_CUDA; break; }
+    if ((e = cudaMemcpyAsync(argmax_out, am, (size_t)M * 4, cudaMemcpyDeviceToHost, st)) != cudaSuccess ||
+        (e = cudaMemcpyAsync(maxlp_out, ml, (size_t)M * 4, cudaMemcpyDeviceToHost, st)) != cudaSuccess ||
+        (lp && (e = cudaMemcpyAsync(logprobs_out, lp, (size_t)M * V1 * 4, cudaMemcpyDeviceToHost, st)) != cudaSuccess)) {
+      err = std::string("CTC download: ") + cudaGetErrorString(e);
+      s = PKC_ERR_CUDA;
+      break;
+    }
+  } while (false);
+  if (s != PKC_OK) {
+    cudaStreamSynchronize(st);
+    return s;
+  }
   return finish(st, err);
 }
 

@@ -66,6 +66,14 @@ class DeviceRunner {
   pkc_status mel_host(const std::vector<const float*>& pcm, const std::vector<int>& n, int T_max,
                       float* host_out, std::string& err);
 
+  // CTC head (src/ctc_decoder.cpp:35 + the per-frame part of src/search.cpp:21):
+  // encoder, then per frame the argmax class and the maximum log-probability
+  // ([sum T'_b] each, clips back to back) and, if logprobs_out != null, the
+  // log-probabilities [sum T'_b, V+1]
+  pkc_status ctc_pcm_host(const std::vector<const float*>& pcm, const std::vector<int>& n, int* argmax_out,
+                          float* maxlp_out, float* logprobs_out, std::string& err);
+  int ctc_classes() const { return w_.ctc_v1; }
+
   void profile_enable(bool on);
   std::vector<KernelStatAcc> profile_read();
 
@@ -110,6 +118,9 @@ class DeviceRunner {
   int* sk_flags_ = nullptr;
   int sk_pairs_ = 0;
   int sk_part_ = 0;             // part whose GEMMs are being issued
+  // CTC head scratch (split operand, logits, per-frame results), grown on demand
+  void* ctc_ws_ = nullptr;
+  size_t ctc_ws_bytes_ = 0;
   // second stream of the two-part layer schedule, and its fork / join events
   cudaStream_t stream2_ = nullptr;
   cudaEvent_t ev_fork_ = nullptr, ev_join_ = nullptr;

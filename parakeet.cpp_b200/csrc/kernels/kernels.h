@@ -122,6 +122,15 @@ cudaError_t dwconv_bn_silu_launch(const void* in, void* out, int d, int K, const
                                   const int* item_off, const int* item_len, int B, int max_len,
                                   bool bf16, cudaStream_t st);
 
+// CTC head (ctc.cu): x f32 [M, d] -> [x_hi | x_hi | x_lo] f16 [M, 3d] (the A
+// operand of the ~22-bit split GEMM against [W_hi | W_lo | W_hi])
+cudaError_t ctc_split3_launch(const float* x, int M, int d, void* out, cudaStream_t st);
+// per frame of logits [M, ld] (V1 real classes): argmax (first maximum),
+// maximum log-probability (= -log-sum-exp of the shifted row) and, if
+// logprobs != null, the log-probabilities [M, V1]
+cudaError_t ctc_rows_launch(const float* logits, int M, int ld, int V1, int* argmax, float* maxlp, float* logprobs,
+                            cudaStream_t st);
+
 // packed time-major [M, d] -> per item channels-first [d, v_b], items concatenated
 cudaError_t to_channels_first_launch(const float* x, float* out, int d, const int* item_off,
                                      const int* item_len, int B, int max_len, cudaStream_t st);

@@ -586,6 +586,38 @@ std::string upload_weights(const GgufFile& g, const Config& c, DeviceWeights& w,
   pos_all.clear();
   pos_all.shrink_to_fit();
 
+  // ---------------- CTC head (src/ctc_decoder.cpp:17-28: hybrid name first)
+  {
+    std::string pre;
+    for (const char* cand : {"ctc_decoder.decoder_layers.0.", "decoder.decoder_layers.0."})
+      if (g.tensor(std::string(cand) + "weight") && g.tensor(std::string(cand) + "bias")) {
+        pre = cand;
+        break;
+      }
+    if (!pre.empty()) {
+      const int V1 = c.vocab_size + 1, Vp = (V1 + 255) / 256 * 256;
+      if (!read_f32(g, pre + "weight", V1, d, f, err)) return err;
+      if (!read_vec(g, pre + "bias", V1, f2, err)) return err;
+      std::vector<uint16_t> ws((size_t)Vp * 3 * d, 0);
+      for (int v = 0; v < V1; ++v)
+        for (int k = 0; k < d; ++k) {
+          const float x = f[(size_t)v * d + k];
+          const uint16_t hi = f32_to_f16(x);
+          const uint16_t lo = f32_to_f16(x - f16_to_f32(hi));
+          uint16_t* row = ws.data() + (size_t)v * 3 * d;
+          row[k] = hi;
+          row[d + k] = lo;
+          row[2 * d + k] = hi;
+        }
+      std::vector<float> bp((size_t)Vp, 0.f);
+      std::copy(f2.begin(), f2.end(), bp.begin());
+      w.ctc_w = put_h(ws);
+      w.ctc_b = put_f(bp);
+      w.ctc_v1 = V1;
+      w.ctc_vpad = Vp;
+    }
+  }
+
   // ---------------- upload
   void* dev = nullptr;
   if (cudaMalloc(&dev, st.buf.size()) != cudaSuccess)
@@ -603,6 +635,7 @@ std::string upload_weights(const GgufFile& g, const Config& c, DeviceWeights& w,
   reloc(w.dw1_w, base); reloc(w.dw1_b, base); reloc(w.dw2_w, base); reloc(w.dw2_b, base);
   reloc(w.pw1_w, base); reloc(w.pw2_w, base); reloc(w.pw1_b, base); reloc(w.pw2_b, base);
   reloc(w.out_w, base); reloc(w.out_b, base); reloc(w.pos_all_w, base);
+  if (w.ctc_v1) { reloc(w.ctc_w, base); reloc(w.ctc_b, base); }
   auto reloc_q = [&](QWeight& qw) {
     if (!qw.type) return;
     reloc(qw.q, base); reloc(qw.s0, base); reloc(qw.s1, base);

@@ -91,6 +91,13 @@ struct DeviceWeights {
   void* pos_all_w = nullptr;      // [L*d, d]: every layer's linear_pos, one GEMM per batch
   QWeight pos_all_q;              // its block-quantised form, when every layer's linear_pos is
   std::vector<LayerWeights> layers;
+  // CTC head (ctc_decoder.decoder_layers.0 of hybrid models, decoder.* of CTC
+  // models), when present: the f32 weight split for the ~22-bit GEMM as f16
+  // rows [W_hi | W_lo | W_hi] of length 3d, padded with zero rows to ctc_vpad
+  void* ctc_w = nullptr;          // f16 [ctc_vpad, 3d]
+  float* ctc_b = nullptr;         // [ctc_vpad]
+  int ctc_v1 = 0;                 // vocab + 1 (0: no CTC head)
+  int ctc_vpad = 0;               // ctc_v1 rounded up to 256
 };
 
 // Upload every encoder weight of `g` to the current CUDA device.

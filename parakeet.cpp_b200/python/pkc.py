@@ -50,6 +50,11 @@ class ModelInfo(ctypes.Structure):
     ]
 
 
+class Token(ctypes.Structure):
+    """pkc_token: the reference's TokenInfo (src/decode_types.hpp:27)."""
+    _fields_ = [("id", ctypes.c_int32), ("frame", ctypes.c_int32), ("conf", c_float), ("span", ctypes.c_int32)]
+
+
 class KernelStat(ctypes.Structure):
     _fields_ = [("name", c_char * 32), ("launches", c_longlong), ("total_ms", c_double),
                 ("flops", c_double), ("bytes", c_double)]
@@ -98,6 +103,10 @@ def _declare(L):
         ("pkc_model_stream", c_void_p, c_void_p, c_int),
         ("pkc_profile_read", c_int, c_void_p, POINTER(KernelStat), c_int),
         ("pkc_shard_plan", c_int, POINTER(c_int), c_int, c_int, c_int, POINTER(c_int)),
+        ("pkc_ctc_classes", c_int, c_void_p),
+        ("pkc_ctc_greedy_pcm_batch", c_int, c_void_p, POINTER(c_void_p), POINTER(c_int), c_int, POINTER(Token),
+         c_size_t, POINTER(c_int), c_void_p, c_size_t),
+        ("pkc_ctc_fold", c_int, c_void_p, c_void_p, c_int, c_int, c_int, POINTER(Token), c_int),
         ("pkc_gemm_resid_stats", c_int, c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int, c_int,
          c_float, c_void_p, c_void_p, c_int, c_void_p, c_void_p),
         ("pkc_gemm_ln", c_int, c_void_p, c_int, c_void_p, c_void_p, c_int, c_int, c_int, c_int, c_int,
@@ -129,6 +138,19 @@ def gemm(A, B, M, N, K, *, bf16, epi, act=ACT_NONE, alpha=1.0, bias=None, out, l
     _check(lib().pkc_gemm(c_void_p(A), lda or K, c_void_p(B), ldb or K, M, N, K, 1 if bf16 else 0,
                           epi, act, alpha, c_void_p(bias) if bias else None, c_void_p(out), ldo,
                           c_void_p(stream) if stream else None))
+
+
+def ctc_fold(argmax, max_logprob, n_classes, blank_id):
+    """The greedy CTC fold (host arithmetic): per-frame argmax classes and
+    maximum log-probabilities -> list of (id, frame, conf, span)."""
+    a = np.ascontiguousarray(argmax, dtype=np.int32)
+    lp = np.ascontiguousarray(max_logprob, dtype=np.float32)
+    T = len(a)
+    out = (Token * max(T, 1))()
+    n = lib().pkc_ctc_fold(a.ctypes.data, lp.ctypes.data, T, n_classes, blank_id, out, max(T, 1))
+    if n < 0:
+        raise PkcError(1, "pkc_ctc_fold: bad arguments")
+    return [(t.id, t.frame, t.conf, t.span) for t in out[:n]]
 
 
 def gemm_resid_stats(A, B, M, N, K, *, bf16, alpha=1.0, bias=None, x, ldx=None, stats=None,
@@ -258,6 +280,38 @@ class Model:
         _check(lib().pkc_encode_pcm_batch(self._h, ptrs, ns, B, layout, out.ctypes.data, out.size,
                                           vt), self._h)
         return _split(out, list(vt), self.info.d_model, layout)
+
+    def ctc_classes(self):
+        """Classes of the CTC head (vocab + 1), 0 without one."""
+        return int(lib().pkc_ctc_classes(self._h))
+
+    def ctc_greedy_pcm_batch(self, pcms, logprobs=False):
+        """CTC transcription: per clip a list of (id, frame, conf, span); with
+        logprobs=True also per clip the [T', V+1] log-probabilities."""
+        B = len(pcms)
+        pcms = [np.ascontiguousarray(p, dtype=np.float32) for p in pcms]
+        ptrs = (c_void_p * B)(*[p.ctypes.data for p in pcms])
+        ns = _ints([len(p) for p in pcms])
+        frames = [self.encoder_frames(self.mel_frames(len(p))) for p in pcms]
+        cap = max(1, sum(frames))
+        toks = (Token * cap)()
+        nt = (c_int * B)()
+        V1 = self.ctc_classes()
+        lp = np.empty((sum(frames), V1), dtype=np.float32) if logprobs else None
+        _check(lib().pkc_ctc_greedy_pcm_batch(self._h, ptrs, ns, B, toks, cap, nt,
+                                              lp.ctypes.data if logprobs else None,
+                                              lp.size if logprobs else 0), self._h)
+        out, pos = [], 0
+        for b in range(B):
+            out.append([(t.id, t.frame, t.conf, t.span) for t in toks[pos:pos + nt[b]]])
+            pos += nt[b]
+        if not logprobs:
+            return out
+        lps, f0 = [], 0
+        for T in frames:
+            lps.append(lp[f0:f0 + T])
+            f0 += T
+        return out, lps
 
     def out_floats(self, n_samples):
         """Floats the encoder output of clips with these sample counts takes."""

@@ -228,3 +228,65 @@ def test_two_part_layer_schedule_is_bitwise_single_stream(models, oracles, kind,
     ref = oracle.encode_pcm_batch(oracles(kind), pcm[:2])
     for a, r in zip(two[:2], ref.outs):
         assert rel_err(a, r.T) < 2e-2
+
+
+def test_ctc_head_matches_oracle_on_the_same_encoder_output(models, oracles):
+    """CTC head (hybrid model): the GPU's split-f16 GEMM (~22-bit products) +
+    log-softmax + argmax, fed the GPU's own encoder output, against the f64
+    restatement of CTCDecoder::forward on that same output: log-probabilities
+    within 1e-3, and the greedy tokens (ids, frames) identical to the oracle's
+    ctc_greedy wherever no frame's top two classes are within 1e-3."""
+    import oracle
+    import pkc
+    w = oracles("f32_bias")
+    m = pkc.Model(models["f32_bias"])
+    try:
+        assert m.ctc_classes() == int(w.kv["parakeet.vocab_size"]) + 1
+        pcm = clips([SR * 3 + 321, SR + 77, 9000], seed=41)
+        toks, lps = m.ctc_greedy_pcm_batch(pcm, logprobs=True)
+        xs = m.encode_pcm_batch(pcm, layout=pkc.LAYOUT_TIME_MAJOR)
+    finally:
+        m.close()
+    blank = int(w.kv["parakeet.blank_id"])
+    for tk, lp, x in zip(toks, lps, xs):
+        ref = oracle.ctc_log_probs(w, x)
+        assert np.abs(lp - ref).max() < 1e-3
+        top2 = np.sort(ref, axis=1)[:, -2:]
+        if (top2[:, 1] - top2[:, 0]).min() > 1e-3:
+            want = oracle.ctc_greedy(ref, blank)
+            assert [(t[0], t[1]) for t in tk] == [(t[0], t[1]) for t in want]
+            for t, u in zip(tk, want):
+                assert abs(t[2] - u[2]) < 1e-3
+
+
+def test_ctc_end_to_end_matches_oracle(models, oracles):
+    """PCM -> tokens through mel, encoder and CTC head against the oracle's
+    encoder + head: log-probabilities within the encoder's bound, and the
+    tokens equal the fold of the GPU's own per-frame results."""
+    import oracle
+    import pkc
+    w = oracles("f32_bias")
+    m = pkc.Model(models["f32_bias"])
+    try:
+        pcm = clips([SR * 2 + 5, 4000], seed=43)
+        toks, lps = m.ctc_greedy_pcm_batch(pcm, logprobs=True)
+    finally:
+        m.close()
+    ref = oracle.encode_pcm_batch(w, pcm)
+    blank = int(w.kv["parakeet.blank_id"])
+    for tk, lp, r in zip(toks, lps, ref.outs):
+        want = oracle.ctc_log_probs(w, r)
+        assert lp.shape == want.shape
+        assert np.abs(lp - want).max() < 2e-2 * np.abs(want).max()
+        am = lp.argmax(axis=1)
+        folded = pkc.ctc_fold(am, lp.max(axis=1), lp.shape[1], blank)
+        assert [(t[0], t[1]) for t in tk] == [(t[0], t[1]) for t in folded]
+
+
+def test_ctc_without_head_is_unsupported(opened):
+    import pkc
+    m = opened("f16")   # TDT-only synthetic model: no CTC head
+    assert m.ctc_classes() == 0
+    with pytest.raises(pkc.PkcError) as e:
+        m.ctc_greedy_pcm_batch(clips([SR], seed=1))
+    assert e.value.status == 4   # PKC_ERR_UNSUPPORTED
