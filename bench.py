@@ -245,6 +245,34 @@ def run_ours(args, rank, world, local_rank):
     e2e_wall = time.perf_counter() - t0
     e2e_ms = e_start.elapsed_time(e_end)
 
+    # ---- greedy transducer transcription (TDT / RNN-T models): PCM -> tokens
+    # through pkc_transducer_greedy_pcm_batch, everything on the GPU
+    trd = None
+    if model.transducer_kind() > 0:
+        for _ in range(max(1, args.warmup)):
+            model.transducer_greedy_pcm_batch(host_pcm)
+        t_start = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        torch.cuda.synchronize(dev)
+        t_start.record(lib_stream)
+        for _ in range(args.steps):
+            toks = model.transducer_greedy_pcm_batch(host_pcm)
+        t_end.record(lib_stream)
+        torch.cuda.synchronize(dev)
+        trd_ms = t_start.elapsed_time(t_end) / args.steps
+        model.profile_enable(True)
+        model.transducer_greedy_pcm_batch(host_pcm)
+        torch.cuda.synchronize(dev)
+        tst = {s["name"]: s["total_ms"] for s in model.profile_read()}
+        model.profile_enable(False)
+        trd = {"metric": "greedy " + ("TDT" if model.transducer_kind() == 2 else "RNN-T") +
+                         " transcription RTFx (PCM -> tokens, encoder and decode on the GPU)",
+               "value": round(audio_s / (trd_ms / 1e3), 1), "unit": UNIT, "ms_per_step": round(trd_ms, 3),
+               "decode_ms": round(tst.get("transducer_decode", 0.0), 3),
+               "joint_enc_gemm_ms": round(tst.get("gemm_joint_enc", 0.0), 4),
+               "tokens_per_step": sum(len(t) for t in toks),
+               "api": "pkc_transducer_greedy_pcm_batch (host buffers)"}
+
     # ---- CTC transcription (models with a CTC head: the hybrid C1 / C4 and
     # CTC models): PCM -> tokens through pkc_ctc_greedy_pcm_batch, host
     # buffers, the head's kernels profiled beside it
@@ -325,6 +353,8 @@ def run_ours(args, rank, world, local_rank):
     }
     if ctc is not None:
         line["ctc"] = ctc
+    if trd is not None:
+        line["transducer"] = trd
     if not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline(args, path, pcm)
     return line

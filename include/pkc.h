@@ -153,6 +153,21 @@ pkc_status pkc_ctc_greedy_pcm_batch(pkc_model* m, const float* const* pcm, const
 int pkc_ctc_fold(const int32_t* argmax, const float* max_logprob, int T, int n_classes, int blank_id,
                  pkc_token* out, int cap);
 
+/* Kind of the model's transducer decoder: 0 none, 1 RNN-T, 2 TDT (durations
+   in parakeet.tdt.durations). */
+int pkc_transducer_kind(const pkc_model* m);
+
+/* Greedy transducer transcription of B clips of PCM, all on the GPU: mel front
+   end + encoder, the joint's encoder projection, then the greedy loop of
+   tdt_greedy (src/tdt.cpp:8-126) or rnnt_greedy (src/rnnt.cpp:110-122) --
+   prediction LSTM, joint, argmax, max_symbols -- for all clips in lockstep.
+   Tokens as the reference's TokenInfo: frame = encoder frame of the emission,
+   conf = max_prob over the token classes, span = the TDT duration (1 for
+   RNN-T). tokens_out receives the clips' tokens back to back, n_tokens[b]
+   clip b's count (at most T'_b * max_symbols). */
+pkc_status pkc_transducer_greedy_pcm_batch(pkc_model* m, const float* const* pcm, const int* n_samples, int B,
+                                           pkc_token* tokens_out, size_t tokens_cap, int* n_tokens);
+
 /* Floats needed by pkc_encode_pcm_batch's `out` for these clip lengths. */
 size_t pkc_encode_out_floats(const pkc_model* m, const int* n_samples, int B);
 

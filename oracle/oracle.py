@@ -15,6 +15,8 @@ What it restates (paths inside parakeet.cpp, the reference):
   * Encoder::forward_batch                           src/encoder.cpp:97-167
   * CTCDecoder::forward (CTC head)                   src/ctc_decoder.cpp:35-116
   * ctc_greedy (greedy fold, token frame / conf)     src/search.cpp:8-90
+  * PredictionNet::step, Joint::step_logits          src/prediction.cpp, src/joint.hpp
+  * tdt_greedy, rnnt_decode_frames / rnnt_greedy     src/tdt.cpp:8-126, src/rnnt.cpp:17-122
 The batched graph is restated literally: every item is zero-padded to the
 batch's T_max and every mask the reference builds (per-stage subsampling time
 masks, output-frame mask, attention key mask and padded-query zeroing, conv
@@ -484,3 +486,122 @@ def ctc_greedy(logp: np.ndarray, blank_id: int):
     if out:
         out[-1][2] = run_min
     return [tuple(o) for o in out]
+
+
+# ------------------------------------------------------------ transducer decode
+
+class Transducer:
+    """Prediction network + joint of a transducer model, float64."""
+
+    def __init__(self, w: Weights):
+        kv = w.kv
+        self.H = int(kv["parakeet.decoder.pred_hidden"])
+        self.L = max(1, int(kv.get("parakeet.decoder.pred_rnn_layers", 1)))
+        self.J = int(kv["parakeet.joint.joint_hidden"])
+        self.V1 = int(kv["parakeet.vocab_size"]) + 1
+        self.blank = int(kv["parakeet.blank_id"])
+        self.max_symbols = int(kv.get("parakeet.decoding.max_symbols", 10))
+        du = kv.get("parakeet.tdt.durations")
+        self.durations = [int(x) for x in du] if du is not None else []
+        f = lambda n: w.t[n].astype(np.float64)
+        self.embed = f("decoder.prediction.embed.weight").reshape(self.V1, self.H)
+        p = "decoder.prediction.dec_rnn.lstm."
+        self.lstm = [(f(p + f"weight_ih_l{l}").reshape(4 * self.H, self.H), f(p + f"weight_hh_l{l}").reshape(4 * self.H, self.H),
+                      f(p + f"bias_ih_l{l}"), f(p + f"bias_hh_l{l}")) for l in range(self.L)]
+        self.w_enc, self.b_enc = f("joint.enc.weight").reshape(self.J, -1), f("joint.enc.bias")
+        self.w_pred, self.b_pred = f("joint.pred.weight").reshape(self.J, self.H), f("joint.pred.bias")
+        self.w_out, self.b_out = f("joint.joint_net.2.weight").reshape(-1, self.J), f("joint.joint_net.2.bias")
+
+    def zero_state(self):
+        return [np.zeros(self.H) for _ in range(self.L)], [np.zeros(self.H) for _ in range(self.L)]
+
+    def step(self, token, is_sos, state):
+        """PredictionNet::step: embedding (zero SOS input), stacked LSTM, gate
+        order i f g o; returns (g = top h', new state)."""
+        hs, cs = state
+        x = np.zeros(self.H) if is_sos else self.embed[token]
+        nh, nc = [], []
+        for l, (wi, wh, bi, bh) in enumerate(self.lstm):
+            z = wi @ x + bi + wh @ hs[l] + bh
+            H = self.H
+            i, fg, g, o = sigmoid(z[:H]), sigmoid(z[H:2 * H]), np.tanh(z[2 * H:3 * H]), sigmoid(z[3 * H:])
+            c = fg * cs[l] + i * g
+            h = o * np.tanh(c)
+            nh.append(h)
+            nc.append(c)
+            x = h
+        return x, (nh, nc)
+
+    def logits(self, enc_proj_t, g):
+        """Joint::step_logits: W_out ReLU(enc_proj[t] + W_pred g + b_pred) + b_out."""
+        f = np.maximum(enc_proj_t + self.w_pred @ g + self.b_pred, 0.0)
+        return self.w_out @ f + self.b_out
+
+
+def _argmax_gap(v):
+    """first argmax and the gap to the runner-up (inf for one element)"""
+    k = int(np.argmax(v))
+    if len(v) < 2:
+        return k, math.inf
+    s = np.sort(v)
+    return k, float(s[-1] - s[-2])
+
+
+def _max_prob_conf(a, k):
+    """decode_max_prob_conf (src/decode_common.hpp): (N p_k - 1) / (N - 1)"""
+    m = a.max()
+    p = math.exp(a[k] - m) / float(np.exp(a - m).sum())
+    N = float(len(a))
+    return (N * p - 1.0) / (N - 1.0)
+
+
+def transducer_greedy(tr: Transducer, enc: np.ndarray):
+    """tdt_greedy (durations present) or rnnt_greedy on one utterance's
+    encoder output enc [T, d]. Returns ([(id, frame, conf, span)], the smallest
+    top-two gap over every argmax taken)."""
+    enc_proj = enc.astype(np.float64) @ tr.w_enc.T + tr.b_enc
+    T = enc.shape[0]
+    out, gap = [], math.inf
+    state = tr.zero_state()
+    last, have = -1, False
+    g = nstate = None
+    g_valid = False
+    t = 0
+    if tr.durations:
+        ND = len(tr.durations)
+        while t < T:
+            sym, need, skip = 0, True, 0
+            while need and sym < tr.max_symbols:
+                if not g_valid:
+                    g, nstate = tr.step(last if have else tr.blank, not have, state)
+                    g_valid = True
+                lg = tr.logits(enc_proj[t], g)
+                k, g1 = _argmax_gap(lg[:tr.V1])
+                dk, g2 = _argmax_gap(lg[tr.V1:tr.V1 + ND])
+                gap = min(gap, g1, g2)
+                skip = tr.durations[dk]
+                if k != tr.blank:
+                    out.append((k, t, _max_prob_conf(lg[:tr.V1], k), skip))
+                    last, have, state, g_valid = k, True, nstate, False
+                sym += 1
+                t += skip
+                need = skip == 0
+            if sym == tr.max_symbols:
+                t += 1
+    else:
+        while t < T:
+            emitted = 0
+            while emitted < tr.max_symbols:
+                if not g_valid:
+                    g, nstate = tr.step(last if have else tr.blank, not have, state)
+                    g_valid = True
+                lg = tr.logits(enc_proj[t], g)
+                k, g1 = _argmax_gap(lg)
+                gap = min(gap, g1)
+                if k == tr.blank:
+                    break
+                out.append((k, t, _max_prob_conf(lg, k), 1))
+                last, have, state, g_valid = k, True, nstate, False
+                emitted += 1
+            t += 1
+    return out, gap

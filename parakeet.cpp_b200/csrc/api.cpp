@@ -241,6 +241,80 @@ pkc_status pkc_ctc_greedy_pcm_batch(pkc_model* m, const float* const* pcm, const
   }
 }
 
+int pkc_transducer_kind(const pkc_model* m) {
+  if (!m || m->runners.empty()) return 0;
+  return m->runners[0]->transducer_kind();
+}
+
+pkc_status pkc_transducer_greedy_pcm_batch(pkc_model* m, const float* const* pcm, const int* n_samples, int B,
+                                           pkc_token* tokens_out, size_t tokens_cap, int* n_tokens) {
+  if (!m) return pkc::set_thread_error(PKC_ERR_ARG, "pkc_transducer_greedy_pcm_batch: model is NULL");
+  std::lock_guard<std::mutex> lk(m->mu);
+  if (!pcm || !n_samples || B <= 0 || !n_tokens || (tokens_cap > 0 && !tokens_out))
+    return fail(m, PKC_ERR_ARG, "pkc_transducer_greedy_pcm_batch: bad arguments");
+  if (!m->runners[0]->transducer_kind())
+    return fail(m, PKC_ERR_UNSUPPORTED, "pkc_transducer_greedy_pcm_batch: the model has no transducer decoder");
+  try {
+    const int MS = std::max(1, m->runners[0]->max_symbols());
+    std::vector<int> T(B);
+    for (int b = 0; b < B; ++b) {
+      if (n_samples[b] <= 0 || !pcm[b])
+        return fail(m, PKC_ERR_ARG, "pkc_transducer_greedy_pcm_batch: empty clip " + std::to_string(b));
+      T[b] = pkc::encoder_frames_for(pkc::mel_frames_for(m->cfg, n_samples[b]));
+    }
+    const int nd = (int)m->runners.size();
+    std::vector<double> cost(B);
+    for (int b = 0; b < B; ++b) cost[b] = clip_cost(T[b]);
+    std::vector<int> assign(B, 0);
+    if (nd > 1) lpt_assign(cost, nd, assign);
+    std::vector<std::vector<int>> items(nd);
+    for (int b = 0; b < B; ++b) items[assign[b]].push_back(b);
+    // per clip: its token rows as the device wrote them
+    std::vector<std::vector<int>> rows(B);
+    std::vector<int> cnt(B, 0);
+    std::vector<pkc_status> st(nd, PKC_OK);
+    std::vector<std::string> errs(nd);
+    auto run = [&](int k) {
+      try {
+        std::vector<const float*> p;
+        std::vector<int> n;
+        size_t frames = 0;
+        for (int b : items[k]) { p.push_back(pcm[b]); n.push_back(n_samples[b]); frames += (size_t)T[b]; }
+        std::vector<int> tok(frames * MS * 4), nt(items[k].size());
+        st[k] = m->runners[k]->transducer_pcm_host(p, n, tok.data(), nt.data(), errs[k]);
+        if (st[k] != PKC_OK) return;
+        size_t pos = 0;  // token rows of this device's clips, in its order
+        for (size_t i = 0; i < items[k].size(); ++i) {
+          const int b = items[k][i];
+          cnt[b] = nt[i];
+          rows[b].assign(tok.begin() + pos * 4, tok.begin() + (pos + (size_t)nt[i]) * 4);
+          pos += (size_t)T[b] * MS;
+        }
+      } catch (const std::exception& e) {
+        st[k] = PKC_ERR_INTERNAL;
+        errs[k] = e.what();
+      }
+    };
+    std::vector<std::thread> th;
+    for (int k = 0; k < nd; ++k)
+      if (!items[k].empty()) th.emplace_back(run, k);
+    for (auto& t : th) t.join();
+    for (int k = 0; k < nd; ++k)
+      if (st[k] != PKC_OK) return fail(m, st[k], "device " + std::to_string(m->runners[k]->device()) + ": " + errs[k]);
+    size_t used = 0;
+    for (int b = 0; b < B; ++b) {
+      if (used + (size_t)cnt[b] > tokens_cap)
+        return fail(m, PKC_ERR_ARG, "pkc_transducer_greedy_pcm_batch: tokens_out too small");
+      if (cnt[b]) std::memcpy(tokens_out + used, rows[b].data(), (size_t)cnt[b] * sizeof(pkc_token));
+      n_tokens[b] = cnt[b];
+      used += (size_t)cnt[b];
+    }
+    return PKC_OK;
+  } catch (const std::exception& e) {
+    return fail(m, PKC_ERR_INTERNAL, e.what());
+  }
+}
+
 size_t pkc_encode_out_floats(const pkc_model* m, const int* n_samples, int B) {
   if (!m || !n_samples || B <= 0) return 0;
   size_t n = 0;

@@ -73,6 +73,16 @@ class DeviceRunner {
   pkc_status ctc_pcm_host(const std::vector<const float*>& pcm, const std::vector<int>& n, int* argmax_out,
                           float* maxlp_out, float* logprobs_out, std::string& err);
   int ctc_classes() const { return w_.ctc_v1; }
+  // Greedy transducer decode (tdt_greedy, src/tdt.cpp:8; rnnt_greedy,
+  // src/rnnt.cpp:110) on the GPU: encoder, encoder projection of the joint,
+  // then the lockstep decode kernel. tokens: per clip up to T'_b * max_symbols
+  // rows of int [4] (id, frame, conf bits, span) at row offset tok_off[b]
+  // (prefix sums of T'_b * max_symbols); n_tok[b] the count.
+  pkc_status transducer_pcm_host(const std::vector<const float*>& pcm, const std::vector<int>& n, int* tokens,
+                                 int* n_tok, std::string& err);
+  // 0: no transducer decoder; 1: RNN-T; 2: TDT
+  int transducer_kind() const { return w_.dec_ok ? (cfg_.durations.empty() ? 1 : 2) : 0; }
+  int max_symbols() const { return cfg_.max_symbols; }
 
   void profile_enable(bool on);
   std::vector<KernelStatAcc> profile_read();
@@ -118,9 +128,11 @@ class DeviceRunner {
   int* sk_flags_ = nullptr;
   int sk_pairs_ = 0;
   int sk_part_ = 0;             // part whose GEMMs are being issued
-  // CTC head scratch (split operand, logits, per-frame results), grown on demand
+  // scratch of the decoder heads (CTC: split operand, logits, per-frame
+  // results; transducer: encoder projection, state), grown on demand
   void* ctc_ws_ = nullptr;
   size_t ctc_ws_bytes_ = 0;
+  pkc_status ensure_aux(size_t bytes, cudaStream_t st, std::string& err);
   // second stream of the two-part layer schedule, and its fork / join events
   cudaStream_t stream2_ = nullptr;
   cudaEvent_t ev_fork_ = nullptr, ev_join_ = nullptr;

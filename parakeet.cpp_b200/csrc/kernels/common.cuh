@@ -19,6 +19,7 @@ enum DevErr : int {
   DEV_ERR_TIMEOUT_ACCUM = 103,  // epilogue waited too long for the accumulator
   DEV_ERR_TIMEOUT_ATTN = 104,   // attention pipeline wait ran out
   DEV_ERR_TIMEOUT_SPLITK = 105, // a split tile's finisher waited too long for a partial sum
+  DEV_ERR_TIMEOUT_DECODE = 106, // the transducer decode's grid barrier waited too long
   DEV_ERR_BAD_SHAPE = 110,
 };
 

@@ -131,6 +131,51 @@ cudaError_t ctc_split3_launch(const float* x, int M, int d, void* out, cudaStrea
 cudaError_t ctc_rows_launch(const float* logits, int M, int ld, int V1, int* argmax, float* maxlp, float* logprobs,
                             cudaStream_t st);
 
+// Greedy transducer (TDT when D > 0, else RNNT) decode of B utterances in
+// lockstep (transducer.cu). Device pointers; state arrays are per utterance
+// and must be initialised by the caller (t = sym = 0, cur = 0, have_token = 0,
+// pending = 1, done = (item_len == 0), ntok = 0; n_pending = the number of
+// pending utterances; the barrier words zero). B <= 4096.
+struct TransducerArgs {
+  int B, H, L, J, V1, D, blank, max_symbols, max_iters;
+  // weights (f32)
+  const float* embed;      // [V1, H]
+  const float* w_ih;       // [L][4H, H]
+  const float* w_hh;       // [L][4H, H]
+  const float* b_lstm;     // [L][4H] (b_ih + b_hh)
+  const float* w_pred;     // [J, H]
+  const float* b_pred;     // [J]
+  const float* w_out;      // [V1 + D, J]
+  const float* b_out;      // [V1 + D]
+  const int* durations;    // [D]
+  const float* zeros;      // [H] zeros (the SOS input)
+  // encoder projection, frames of all utterances: [M, ld_enc] (first J columns)
+  const float* enc_proj;
+  int ld_enc;
+  const int* item_off;     // [B] first frame row
+  const int* item_len;     // [B] frames
+  // state
+  float* h;                // [2][L][B][H] (committed buffer cur[b], step output 1 - cur[b])
+  float* c;                // [2][L][B][H]
+  float* pred_proj;        // [B, J]
+  int *t, *sym, *cur, *have_token, *last_token, *pending, *done, *ntok;
+  int* n_pending;
+  int* n_done;
+  void* partials;          // transducer_partial_bytes(grid, B)
+  // output tokens: utterance b at rows [tok_off[b], tok_off[b] + tok_cap[b]) of
+  // int [*, 4] = (id, frame, conf as float bits, span)
+  int* tokens;
+  const int* tok_off;
+  const int* tok_cap;
+  unsigned int* bar_count;
+  unsigned int* bar_gen;
+  int* err;
+};
+size_t transducer_smem_bytes(int H, int J, int B);
+size_t transducer_partial_bytes(int grid, int B);
+int transducer_grid();
+cudaError_t transducer_greedy_launch(const TransducerArgs& a, int grid, cudaStream_t st);
+
 // packed time-major [M, d] -> per item channels-first [d, v_b], items concatenated
 cudaError_t to_channels_first_launch(const float* x, float* out, int d, const int* item_off,
                                      const int* item_len, int B, int max_len, cudaStream_t st);

@@ -248,6 +248,13 @@ std::string read_config(const GgufFile& g, Config& c) {
   c.log_zero_guard = g.f32("parakeet.preprocessor.log_zero_guard", 0.f);
   c.vocab_size = (int)g.u32("parakeet.vocab_size");
   c.blank_id = (int)g.u32("parakeet.blank_id");
+  c.pred_hidden = (int)g.u32("parakeet.decoder.pred_hidden", 0);
+  c.pred_layers = (int)g.u32("parakeet.decoder.pred_rnn_layers", 1);
+  if (c.pred_layers <= 0) c.pred_layers = 1;  // src/prediction.cpp: default one layer
+  c.joint_hidden = (int)g.u32("parakeet.joint.joint_hidden", 0);
+  c.max_symbols = (int)g.u32("parakeet.decoding.max_symbols", 10);
+  c.durations.clear();
+  for (int64_t x : g.int_array("parakeet.tdt.durations")) c.durations.push_back((int)x);
   if (c.d_model <= 0 || c.vocab_size <= 0) return "GGUF lacks parakeet.encoder.d_model / vocab_size";
   if (c.n_layers <= 0 || c.n_heads <= 0 || c.d_model % c.n_heads) return "bad encoder geometry";
   const int dk = c.d_model / c.n_heads;
@@ -618,6 +625,61 @@ std::string upload_weights(const GgufFile& g, const Config& c, DeviceWeights& w,
     }
   }
 
+  // ---------------- transducer decoder (prediction LSTM + joint), f32
+  if (c.pred_hidden > 0 && c.joint_hidden > 0 && g.tensor("decoder.prediction.embed.weight") &&
+      g.tensor("joint.joint_net.2.weight")) {
+    const int Hp = c.pred_hidden, J = c.joint_hidden, L = c.pred_layers, V1 = c.vocab_size + 1;
+    const int D = (int)c.durations.size();
+    std::vector<float> emb, wi, wh, bb, t1, t2;
+    if (!read_f32(g, "decoder.prediction.embed.weight", V1, Hp, emb, err)) return err;
+    for (int l = 0; l < L; ++l) {
+      const std::string s = "decoder.prediction.dec_rnn.lstm.";
+      const std::string ls = "_l" + std::to_string(l);
+      if (!read_f32(g, s + "weight_ih" + ls, 4 * Hp, Hp, t1, err)) return err;
+      wi.insert(wi.end(), t1.begin(), t1.end());
+      if (!read_f32(g, s + "weight_hh" + ls, 4 * Hp, Hp, t1, err)) return err;
+      wh.insert(wh.end(), t1.begin(), t1.end());
+      if (!read_vec(g, s + "bias_ih" + ls, 4 * Hp, t1, err) || !read_vec(g, s + "bias_hh" + ls, 4 * Hp, t2, err))
+        return err;
+      for (int i = 0; i < 4 * Hp; ++i) bb.push_back(t1[i] + t2[i]);
+    }
+    w.dec_embed = put_f(emb);
+    w.dec_w_ih = put_f(wi);
+    w.dec_w_hh = put_f(wh);
+    w.dec_b = put_f(bb);
+    if (!read_f32(g, "joint.pred.weight", J, Hp, t1, err) || !read_vec(g, "joint.pred.bias", J, t2, err)) return err;
+    w.dec_w_pred = put_f(t1);
+    w.dec_b_pred = put_f(t2);
+    if (!read_f32(g, "joint.joint_net.2.weight", V1 + D, J, t1, err) ||
+        !read_vec(g, "joint.joint_net.2.bias", V1 + D, t2, err))
+      return err;
+    w.dec_w_out = put_f(t1);
+    w.dec_b_out = put_f(t2);
+    std::vector<int> du(c.durations.begin(), c.durations.end());
+    if (du.empty()) du.push_back(0);
+    w.dec_durations = as_off<int>(st.add(du.data(), du.size() * 4));
+    w.dec_zeros = put_f(std::vector<float>((size_t)Hp, 0.f));
+    // encoder projection: split f16 rows [W_hi | W_lo | W_hi], padded to 256
+    if (!read_f32(g, "joint.enc.weight", J, d, t1, err) || !read_vec(g, "joint.enc.bias", J, t2, err)) return err;
+    const int Jp = (J + 255) / 256 * 256;
+    std::vector<uint16_t> ws((size_t)Jp * 3 * d, 0);
+    for (int j = 0; j < J; ++j)
+      for (int k = 0; k < d; ++k) {
+        const float x = t1[(size_t)j * d + k];
+        const uint16_t hi = f32_to_f16(x), lo = f32_to_f16(x - f16_to_f32(hi));
+        uint16_t* row = ws.data() + (size_t)j * 3 * d;
+        row[k] = hi;
+        row[d + k] = lo;
+        row[2 * d + k] = hi;
+      }
+    std::vector<float> be((size_t)Jp, 0.f);
+    std::copy(t2.begin(), t2.end(), be.begin());
+    w.dec_w_enc = put_h(ws);
+    w.dec_b_enc = put_f(be);
+    w.dec_jpad = Jp;
+    w.dec_ok = true;
+  }
+
   // ---------------- upload
   void* dev = nullptr;
   if (cudaMalloc(&dev, st.buf.size()) != cudaSuccess)
@@ -636,6 +698,11 @@ std::string upload_weights(const GgufFile& g, const Config& c, DeviceWeights& w,
   reloc(w.pw1_w, base); reloc(w.pw2_w, base); reloc(w.pw1_b, base); reloc(w.pw2_b, base);
   reloc(w.out_w, base); reloc(w.out_b, base); reloc(w.pos_all_w, base);
   if (w.ctc_v1) { reloc(w.ctc_w, base); reloc(w.ctc_b, base); }
+  if (w.dec_ok) {
+    reloc(w.dec_embed, base); reloc(w.dec_w_ih, base); reloc(w.dec_w_hh, base); reloc(w.dec_b, base);
+    reloc(w.dec_w_pred, base); reloc(w.dec_b_pred, base); reloc(w.dec_w_out, base); reloc(w.dec_b_out, base);
+    reloc(w.dec_durations, base); reloc(w.dec_zeros, base); reloc(w.dec_w_enc, base); reloc(w.dec_b_enc, base);
+  }
   auto reloc_q = [&](QWeight& qw) {
     if (!qw.type) return;
     reloc(qw.q, base); reloc(qw.s0, base); reloc(qw.s1, base);

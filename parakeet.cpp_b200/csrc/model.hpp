@@ -25,6 +25,9 @@ struct Config {
   float preemph = 0.f, mag_power = 2.f, log_zero_guard = 0.f;
   std::string normalize = "per_feature";
   int vocab_size = 0, blank_id = 0;
+  // transducer decoder (0 when absent): prediction LSTM, joint, TDT durations
+  int pred_hidden = 0, pred_layers = 0, joint_hidden = 0, max_symbols = 0;
+  std::vector<int> durations;  // empty: RNN-T
   // derived
   int F1 = 0, F2 = 0, F3 = 0;
   uint32_t weight_type = 0;  // GGUF type of the encoder linear weights
@@ -98,6 +101,23 @@ struct DeviceWeights {
   float* ctc_b = nullptr;         // [ctc_vpad]
   int ctc_v1 = 0;                 // vocab + 1 (0: no CTC head)
   int ctc_vpad = 0;               // ctc_v1 rounded up to 256
+  // transducer decoder (f32, as in GGUF), when present (dec_ok)
+  bool dec_ok = false;
+  float* dec_embed = nullptr;     // [V1, H]
+  float* dec_w_ih = nullptr;      // [L][4H, H]
+  float* dec_w_hh = nullptr;      // [L][4H, H]
+  float* dec_b = nullptr;         // [L][4H] (b_ih + b_hh)
+  float* dec_w_pred = nullptr;    // [J, H]
+  float* dec_b_pred = nullptr;    // [J]
+  float* dec_w_out = nullptr;     // [V1 + D, J]
+  float* dec_b_out = nullptr;     // [V1 + D]
+  int* dec_durations = nullptr;   // [D]
+  float* dec_zeros = nullptr;     // [H]
+  // joint encoder projection as a split-f16 GEMM operand [W_hi | W_lo | W_hi],
+  // rows padded to dec_jpad (a multiple of 256), and its bias
+  void* dec_w_enc = nullptr;      // f16 [dec_jpad, 3d]
+  float* dec_b_enc = nullptr;     // [dec_jpad]
+  int dec_jpad = 0;
 };
 
 // Upload every encoder weight of `g` to the current CUDA device.

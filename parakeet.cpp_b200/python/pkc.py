@@ -104,6 +104,9 @@ def _declare(L):
         ("pkc_profile_read", c_int, c_void_p, POINTER(KernelStat), c_int),
         ("pkc_shard_plan", c_int, POINTER(c_int), c_int, c_int, c_int, POINTER(c_int)),
         ("pkc_ctc_classes", c_int, c_void_p),
+        ("pkc_transducer_kind", c_int, c_void_p),
+        ("pkc_transducer_greedy_pcm_batch", c_int, c_void_p, POINTER(c_void_p), POINTER(c_int), c_int,
+         POINTER(Token), c_size_t, POINTER(c_int)),
         ("pkc_ctc_greedy_pcm_batch", c_int, c_void_p, POINTER(c_void_p), POINTER(c_int), c_int, POINTER(Token),
          c_size_t, POINTER(c_int), c_void_p, c_size_t),
         ("pkc_ctc_fold", c_int, c_void_p, c_void_p, c_int, c_int, c_int, POINTER(Token), c_int),
@@ -312,6 +315,28 @@ class Model:
             lps.append(lp[f0:f0 + T])
             f0 += T
         return out, lps
+
+    def transducer_kind(self):
+        """0: no transducer decoder, 1: RNN-T, 2: TDT."""
+        return int(lib().pkc_transducer_kind(self._h))
+
+    def transducer_greedy_pcm_batch(self, pcms, max_symbols=10):
+        """Greedy RNN-T / TDT transcription on the GPU: per clip a list of
+        (id, frame, conf, span)."""
+        B = len(pcms)
+        pcms = [np.ascontiguousarray(p, dtype=np.float32) for p in pcms]
+        ptrs = (c_void_p * B)(*[p.ctypes.data for p in pcms])
+        ns = _ints([len(p) for p in pcms])
+        frames = [self.encoder_frames(self.mel_frames(len(p))) for p in pcms]
+        cap = max(1, sum(frames) * max_symbols)
+        toks = (Token * cap)()
+        nt = (c_int * B)()
+        _check(lib().pkc_transducer_greedy_pcm_batch(self._h, ptrs, ns, B, toks, cap, nt), self._h)
+        out, pos = [], 0
+        for b in range(B):
+            out.append([(t.id, t.frame, t.conf, t.span) for t in toks[pos:pos + nt[b]]])
+            pos += nt[b]
+        return out
 
     def out_floats(self, n_samples):
         """Floats the encoder output of clips with these sample counts takes."""

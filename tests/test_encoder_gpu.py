@@ -290,3 +290,44 @@ def test_ctc_without_head_is_unsupported(opened):
     with pytest.raises(pkc.PkcError) as e:
         m.ctc_greedy_pcm_batch(clips([SR], seed=1))
     assert e.value.status == 4   # PKC_ERR_UNSUPPORTED
+
+
+@pytest.mark.parametrize("kind", ["f16", "q8_0"])
+def test_transducer_greedy_matches_oracle(models, oracles, kind):
+    """Greedy transducer decode on the GPU (f16 model: TDT with durations
+    0..4; q8_0 model: RNN-T), fed the GPU's own encoder output, against the f64
+    restatement of tdt_greedy / rnnt_greedy (prediction LSTM, joint, argmax,
+    max_symbols, duration skips): token ids, frames and spans identical and
+    confidences within 1e-4, on clips whose decisions never come within 1e-5
+    of a tie (the synthetic weights make the joint logits nearly flat)."""
+    import oracle
+    import pkc
+    w = oracles(kind)
+    tr = oracle.Transducer(w)
+    m = pkc.Model(models[kind])
+    try:
+        assert m.transducer_kind() == (2 if tr.durations else 1)
+        pcm = clips([SR * 2 + 111, SR + 5, 7000, SR * 3], seed=51)
+        toks = m.transducer_greedy_pcm_batch(pcm)
+        xs = m.encode_pcm_batch(pcm, layout=pkc.LAYOUT_TIME_MAJOR)
+    finally:
+        m.close()
+    compared = 0
+    for tk, x in zip(toks, xs):
+        want, gap = oracle.transducer_greedy(tr, x)
+        if gap < 1e-5:
+            continue
+        compared += 1
+        assert [(t[0], t[1], t[3]) for t in tk] == [(t[0], t[1], t[3]) for t in want]
+        for t, u in zip(tk, want):
+            assert abs(t[2] - u[2]) < 1e-4
+    assert compared >= 2
+
+
+def test_transducer_absent_is_unsupported(models):
+    import pkc
+    m = pkc.Model(models["f32_bias"])   # hybrid model: has a transducer too
+    try:
+        assert m.transducer_kind() == 2
+    finally:
+        m.close()
