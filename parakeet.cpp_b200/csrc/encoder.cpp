@@ -621,7 +621,11 @@ pkc_status DeviceRunner::finish(cudaStream_t st, std::string& err) {
     // a launch that gave up may have left stream-K flags raised
     if (sk_flags_) cudaMemsetAsync(sk_flags_, 0, 2 * gemm_sk_flag_count(sk_pairs_) * sizeof(int), st);
     cudaStreamSynchronize(st);
-    err = "kernel reported error " + std::to_string(h_err) + " (bounded wait timed out)";
+    // codes of the device error word (DevErr in kernels/common.cuh)
+    const char* what = h_err == 110   ? "bad shape or capacity"
+                       : h_err == 111 ? "non-finite decoder logits"
+                                      : "bounded wait timed out";
+    err = "kernel reported error " + std::to_string(h_err) + " (" + what + ")";
     return PKC_ERR_KERNEL;
   }
   return PKC_OK;
@@ -760,16 +764,24 @@ pkc_status DeviceRunner::transducer_pcm_host(const std::vector<const float*>& pc
   const int M = p.M, B = p.B, d = c.d_model, H = c.pred_hidden, L = c.pred_layers, J = c.joint_hidden;
   const int Jp = w_.dec_jpad, MS = std::max(1, c.max_symbols);
   const int grid = transducer_grid();
+  // utterances decoded together (every CTA holds their state in shared memory)
+  const int V1 = c.vocab_size + 1, VP = V1 + (int)c.durations.size();
+  int BG = std::min(B, transducer_max_batch(H, J, L, VP, grid));
+  if (const char* e = std::getenv("PKC_DECODE_GROUP")) BG = std::min(BG, std::max(1, std::atoi(e)));
+  if (BG < 1) {
+    err = "decoder hidden sizes too large for the decode kernel";
+    return PKC_ERR_UNSUPPORTED;
+  }
   // token rows: utterance b at rows [v_off[b] * MS, v_off[b+1] * MS)
   size_t sz = 0;
   auto take = [&](size_t bytes) { const size_t o = sz; sz += al(bytes); return o; };
   const size_t o_a = take((size_t)M * 3 * d * 2), o_ep = take((size_t)M * Jp * 4);
-  const size_t o_h = take((size_t)2 * L * B * H * 4), o_c = take((size_t)2 * L * B * H * 4);
-  const size_t o_pp = take((size_t)B * J * 4), o_part = take(transducer_partial_bytes(grid, B));
+  const size_t o_h = take((size_t)2 * L * BG * H * 4), o_c = take((size_t)2 * L * BG * H * 4);
+  const size_t o_pp = take((size_t)BG * J * 4), o_part = take(transducer_partial_bytes(grid, BG));
   const size_t o_st = take((size_t)B * 12 * 4 + 64), o_tok = take((size_t)M * MS * 16);
   PKC_ST(ensure_aux(sz, st, err));
   uint8_t* ws = static_cast<uint8_t*>(ctc_ws_);
-  // per-utterance state (8 ints each), table (off, len, tok_off, tok_cap), counters
+  // per-utterance state (8 ints each), table (off, len, tok_off, tok_cap), barrier word
   std::vector<int> hs((size_t)B * 12 + 16, 0);
   int* s_t = hs.data();
   int* s_pending = s_t + 5 * B;
@@ -778,55 +790,55 @@ pkc_status DeviceRunner::transducer_pcm_host(const std::vector<const float*>& pc
   int* s_len = s_t + 9 * B;
   int* s_tok_off = s_t + 10 * B;
   int* s_tok_cap = s_t + 11 * B;
-  int ndone = 0;
   for (int b = 0; b < B; ++b) {
     s_pending[b] = p.v[b] > 0 ? 1 : 0;
     s_done[b] = p.v[b] > 0 ? 0 : 1;
-    ndone += s_done[b];
     s_off[b] = p.v_off[b];
     s_len[b] = p.v[b];
     s_tok_off[b] = p.v_off[b] * MS;
     s_tok_cap[b] = p.v[b] * MS;
   }
-  int* ctr = s_t + 12 * B;  // n_pending, n_done, bar_count, bar_gen
-  ctr[0] = B - ndone;
-  ctr[1] = ndone;
   int* d_st = reinterpret_cast<int*>(ws + o_st);
   PKC_CK(cudaMemcpyAsync(d_st, hs.data(), hs.size() * 4, cudaMemcpyHostToDevice, st), "decoder state upload");
-  PKC_CK(cudaMemsetAsync(ws + o_h, 0, (size_t)2 * L * B * H * 4, st), "decoder state reset");
-  PKC_CK(cudaMemsetAsync(ws + o_c, 0, (size_t)2 * L * B * H * 4, st), "decoder state reset");
   sk_part_ = 0;
   // encoder projection of the joint, every frame: [x_hi|x_hi|x_lo] . [W_hi|W_lo|W_hi]^T + b
   PKC_CK(ctc_split3_launch(b_.x, M, d, ws + o_a, st), "decoder split");
   PKC_ST(gemm(ws + o_a, 3 * d, w_.dec_w_enc, 3 * d, false, M, Jp, 3 * d, EPI_STORE_F32, ACT_NONE, 1.f, w_.dec_b_enc,
               ws + o_ep, Jp, st, "gemm_joint_enc", err));
-  TransducerArgs a{};
-  a.B = B; a.H = H; a.L = L; a.J = J; a.V1 = c.vocab_size + 1; a.D = (int)c.durations.size();
-  a.blank = c.blank_id; a.max_symbols = MS;
-  int maxv = 0;
-  for (int b = 0; b < B; ++b) maxv = std::max(maxv, p.v[b]);
-  a.max_iters = maxv * (MS + 1) + 4;
-  a.embed = w_.dec_embed; a.w_ih = w_.dec_w_ih; a.w_hh = w_.dec_w_hh; a.b_lstm = w_.dec_b;
-  a.w_pred = w_.dec_w_pred; a.b_pred = w_.dec_b_pred; a.w_out = w_.dec_w_out; a.b_out = w_.dec_b_out;
-  a.durations = w_.dec_durations; a.zeros = w_.dec_zeros;
-  a.enc_proj = reinterpret_cast<const float*>(ws + o_ep); a.ld_enc = Jp;
-  a.item_off = s_off - hs.data() + d_st; a.item_len = s_len - hs.data() + d_st;
-  a.h = reinterpret_cast<float*>(ws + o_h); a.c = reinterpret_cast<float*>(ws + o_c);
-  a.pred_proj = reinterpret_cast<float*>(ws + o_pp);
-  a.t = d_st; a.sym = d_st + B; a.cur = d_st + 2 * B; a.have_token = d_st + 3 * B; a.last_token = d_st + 4 * B;
-  a.pending = d_st + 5 * B; a.done = d_st + 6 * B; a.ntok = d_st + 7 * B;
-  a.n_pending = d_st + 12 * B; a.n_done = d_st + 12 * B + 1;
-  a.bar_count = reinterpret_cast<unsigned int*>(d_st + 12 * B + 2);
-  a.bar_gen = reinterpret_cast<unsigned int*>(d_st + 12 * B + 3);
-  a.partials = ws + o_part;
-  a.tokens = reinterpret_cast<int*>(ws + o_tok);
-  a.tok_off = d_st + 10 * B; a.tok_cap = d_st + 11 * B;
-  a.err = err_word_;
-  prof_begin(st);
-  PKC_CK(transducer_greedy_launch(a, grid, st), "transducer decode launch");
-  prof_end(st, "transducer_decode", 0.0, 0.0);
-  PKC_CK(cudaMemcpyAsync(n_tok, a.ntok, (size_t)B * 4, cudaMemcpyDeviceToHost, st), "token count download");
-  PKC_CK(cudaMemcpyAsync(tokens, a.tokens, (size_t)M * MS * 16, cudaMemcpyDeviceToHost, st), "token download");
+  int* d_ntok = d_st + 7 * B;
+  for (int b0 = 0; b0 < B; b0 += BG) {
+    const int nb = std::min(BG, B - b0);
+    PKC_CK(cudaMemsetAsync(ws + o_h, 0, (size_t)2 * L * nb * H * 4, st), "decoder state reset");
+    PKC_CK(cudaMemsetAsync(ws + o_c, 0, (size_t)2 * L * nb * H * 4, st), "decoder state reset");
+    PKC_CK(cudaMemsetAsync(ws + o_part, 0, transducer_key_bytes(nb), st), "decoder key reset");
+    PKC_CK(cudaMemsetAsync(d_st + 12 * B, 0, 4, st), "decoder barrier reset");
+    TransducerArgs a{};
+    a.B = nb; a.H = H; a.L = L; a.J = J; a.V1 = V1; a.D = (int)c.durations.size();
+    a.blank = c.blank_id; a.max_symbols = MS;
+    int maxv = 0;
+    for (int b = b0; b < b0 + nb; ++b) maxv = std::max(maxv, p.v[b]);
+    a.max_iters = maxv * (MS + 1) + 4;
+    a.embed = w_.dec_embed; a.w_ih = w_.dec_w_ih; a.w_hh = w_.dec_w_hh; a.b_lstm = w_.dec_b;
+    a.w_pred = w_.dec_w_pred; a.b_pred = w_.dec_b_pred; a.w_out = w_.dec_w_out; a.b_out = w_.dec_b_out;
+    a.durations = w_.dec_durations; a.zeros = w_.dec_zeros;
+    a.enc_proj = reinterpret_cast<const float*>(ws + o_ep); a.ld_enc = Jp;
+    a.item_off = d_st + 8 * B + b0; a.item_len = d_st + 9 * B + b0;
+    a.h = reinterpret_cast<float*>(ws + o_h); a.c = reinterpret_cast<float*>(ws + o_c);
+    a.pred_proj = reinterpret_cast<float*>(ws + o_pp);
+    a.t = d_st + b0; a.sym = d_st + B + b0; a.cur = d_st + 2 * B + b0; a.have_token = d_st + 3 * B + b0;
+    a.last_token = d_st + 4 * B + b0; a.pending = d_st + 5 * B + b0; a.done = d_st + 6 * B + b0;
+    a.ntok = d_ntok + b0;
+    a.bar_count = reinterpret_cast<unsigned int*>(d_st + 12 * B);
+    a.keys = reinterpret_cast<unsigned long long*>(ws + o_part);
+    a.tokens = reinterpret_cast<int*>(ws + o_tok);
+    a.tok_off = d_st + 10 * B + b0; a.tok_cap = d_st + 11 * B + b0;
+    a.err = err_word_;
+    prof_begin(st);
+    PKC_CK(transducer_greedy_launch(a, grid, st), "transducer decode launch");
+    prof_end(st, "transducer_decode", 0.0, 0.0);
+  }
+  PKC_CK(cudaMemcpyAsync(n_tok, d_ntok, (size_t)B * 4, cudaMemcpyDeviceToHost, st), "token count download");
+  PKC_CK(cudaMemcpyAsync(tokens, ws + o_tok, (size_t)M * MS * 16, cudaMemcpyDeviceToHost, st), "token download");
   return finish(st, err);
 }
 

@@ -21,6 +21,7 @@ enum DevErr : int {
   DEV_ERR_TIMEOUT_SPLITK = 105, // a split tile's finisher waited too long for a partial sum
   DEV_ERR_TIMEOUT_DECODE = 106, // the transducer decode's grid barrier waited too long
   DEV_ERR_BAD_SHAPE = 110,
+  DEV_ERR_NONFINITE = 111,      // a decode step found no finite maximum (NaN logits)
 };
 
 // Upper bound of any single mbarrier wait (nanoseconds of %globaltimer).

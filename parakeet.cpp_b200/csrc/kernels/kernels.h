@@ -134,8 +134,11 @@ cudaError_t ctc_rows_launch(const float* logits, int M, int ld, int V1, int* arg
 // Greedy transducer (TDT when D > 0, else RNNT) decode of B utterances in
 // lockstep (transducer.cu). Device pointers; state arrays are per utterance
 // and must be initialised by the caller (t = sym = 0, cur = 0, have_token = 0,
-// pending = 1, done = (item_len == 0), ntok = 0; n_pending = the number of
-// pending utterances; the barrier words zero). B <= 4096.
+// pending = 1, done = (item_len == 0), ntok = 0; h = c = 0; bar_count zero and
+// the first transducer_key_bytes(B) bytes of partials zero).
+// B <= transducer_max_batch(...): every CTA keeps the per-utterance state in
+// shared memory, so larger batches are decoded in groups. Weight rows, embed,
+// zeros, enc_proj rows, h and pred_proj must be 16-byte aligned (bulk copies).
 struct TransducerArgs {
   int B, H, L, J, V1, D, blank, max_symbols, max_iters;
   // weights (f32)
@@ -159,19 +162,22 @@ struct TransducerArgs {
   float* c;                // [2][L][B][H]
   float* pred_proj;        // [B, J]
   int *t, *sym, *cur, *have_token, *last_token, *pending, *done, *ntok;
-  int* n_pending;
-  int* n_done;
-  void* partials;          // transducer_partial_bytes(grid, B)
+  // transducer_partial_bytes(grid, B): argmax keys [2][3][B] u64, then the
+  // per-CTA confidence partials [2][grid][B] float2
+  unsigned long long* keys;
   // output tokens: utterance b at rows [tok_off[b], tok_off[b] + tok_cap[b]) of
   // int [*, 4] = (id, frame, conf as float bits, span)
   int* tokens;
   const int* tok_off;
   const int* tok_cap;
   unsigned int* bar_count;
-  unsigned int* bar_gen;
   int* err;
+  int held;                // set by the launcher (LSTM layers resident in shared memory)
 };
-size_t transducer_smem_bytes(int H, int J, int B);
+size_t transducer_smem_bytes(int H, int J, int L, int VP, int grid, int B);
+size_t transducer_smem_limit();
+int transducer_max_batch(int H, int J, int L, int VP, int grid);
+size_t transducer_key_bytes(int B);
 size_t transducer_partial_bytes(int grid, int B);
 int transducer_grid();
 cudaError_t transducer_greedy_launch(const TransducerArgs& a, int grid, cudaStream_t st);

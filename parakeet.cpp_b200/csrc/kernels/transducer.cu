@@ -8,19 +8,32 @@
 // every frame is one split-f16 GEMM before this kernel (as the reference's
 // precompute_enc_proj).
 //
-// One persistent grid (cooperative launch: every CTA resident), one joint
-// evaluation per utterance per iteration:
-//   P  (only when some utterance needs its prediction output recomputed)
-//      LSTM layer by layer, then the pred projection; each CTA owns a slice of
-//      hidden units (all four gate rows of a unit, so the cell update is local)
-//      and of projection rows, for every pending utterance
-//   J  joint: each CTA owns a slice of the V+1(+D) output rows; per utterance a
-//      partial (max, first argmax, sum of exp) of the token part and (max,
-//      first argmax) of the duration part
-//   D  CTA 0 merges the partials, applies the reference's per-utterance state
-//      machine, appends tokens, marks utterances that need a new prediction
-// Phases are separated by a grid barrier whose wait is bounded (kWaitLimitNs):
-// on a timeout the kernel records DEV_ERR_TIMEOUT_DECODE and every CTA leaves.
+// One persistent grid (cooperative launch: every CTA resident). Iteration =
+// one joint evaluation per live utterance:
+//   P  (only when some utterance emitted, so its prediction output is stale)
+//      LSTM layer by layer, then the pred projection
+//   J  joint: each CTA evaluates its slice of the V+1(+D) output rows and
+//      folds its best token and best duration into one packed 64-bit key per
+//      utterance with atomicMax (ordered value bits above the inverted row
+//      index, so the largest value and on ties the lowest index wins -- the
+//      reference's first-maximum argmax), plus a (max, sum of exp) partial of
+//      the token part for the confidence
+//   D  every CTA reads the two keys of each utterance and applies the
+//      reference's state machine to its own shared-memory copy of the state
+//      (all CTAs decide identically); CTA 0 appends the tokens
+// Each CTA owns a contiguous slice of hidden units (all four gate rows of a
+// unit, so the cell update is local), of pred rows and of joint rows. Those
+// weight rows are copied into its shared memory once, by bulk copies, and stay
+// there for the whole decode (the LSTM rows of all layers when they fit, else
+// one layer at a time, the next layer's copy overlapping the grid barrier).
+// Per phase the CTA bulk-copies the input vectors of 16 utterances into shared
+// memory and its 8 warps split K of the 8-row x 16-utterance dot products.
+// Confidences (max_prob, ((V+1) p_max - 1) / V) of the tokens emitted in one
+// iteration are merged from the per-CTA partials during the next one, by the
+// CTA the utterance maps to.
+// Phases are separated by a grid barrier (monotonic arrival counter) whose
+// wait, like every mbarrier wait, is bounded (kWaitLimitNs): on a timeout the
+// kernel records DEV_ERR_TIMEOUT_DECODE and every CTA leaves.
 // All arithmetic is f32 on f32 weights (the decoder weights are f32 in GGUF).
 #include <algorithm>
 
@@ -33,40 +46,117 @@ namespace {
 
 constexpr int TD_THREADS = 256;
 constexpr int TD_WARPS = TD_THREADS / 32;
-constexpr int TD_CHUNK = 8;  // utterances whose vectors sit in shared memory at once
-constexpr int TD_KV = 8;     // float4 per lane of one weight row: rows up to 8 * 128 = 1024 wide
-constexpr int TD_STG = 4;    // staged elements per thread and vector: vectors up to 4 * 256 = 1024 long
+constexpr int TD_CB = 16;  // utterances per staged chunk (one per lane of a half-warp)
+constexpr int TD_RG = 8;   // weight rows per dot-product pass (two LSTM units x four gates)
+constexpr int TD_MAX_DUR = 32;
+constexpr int TD_STATE_INTS = 13;  // per-utterance ints in each CTA's shared memory
+constexpr size_t TD_SMEM_LIMIT = 227 * 1024 - 1024;  // dynamic part (the static part is < 1 KB)
 
-struct Partial {
-  float tmax, tsum, dmax;
-  int targ, darg;
+// Shared-memory layout of one CTA (offsets in floats from the dynamic base).
+struct TdLayout {
+  int ldk;         // sX row stride: max(2H, 2J) + 4
+  int nu, nj, nv;  // most hidden units / pred rows / joint rows any CTA owns
+  int held;        // LSTM layers resident at once (L, or 1 when all do not fit)
+  int o_x, o_wl, o_wp, o_wj, o_bl, o_bp, o_bj, o_r, o_z, o_c, o_st;
+  size_t bytes;
 };
 
-__device__ __forceinline__ bool grid_sync(unsigned int* bar_count, unsigned int* bar_gen, int* err, int* smem_ok) {
+__host__ __device__ inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
+
+__host__ __device__ inline TdLayout td_layout(int H, int J, int L, int VP, int G, int B, int held) {
+  TdLayout t;
+  t.ldk = (2 * H > 2 * J ? 2 * H : 2 * J) + 4;
+  t.nu = ceil_div(H, G);
+  t.nj = ceil_div(J, G);
+  t.nv = ceil_div(VP, G);
+  t.held = held;
+  int o = 0;
+  auto take = [&](int n) {
+    const int r = o;
+    o += (n + 3) & ~3;
+    return r;
+  };
+  t.o_x = take(TD_CB * t.ldk);
+  t.o_wl = take(held * 4 * t.nu * 2 * H);
+  t.o_wp = take(t.nj * H);
+  t.o_wj = take(t.nv * J);
+  t.o_bl = take(L * 4 * t.nu);
+  t.o_bp = take(t.nj);
+  t.o_bj = take(t.nv);
+  t.o_r = take(TD_WARPS * TD_RG * TD_CB);
+  t.o_z = take(TD_RG * TD_CB);
+  t.o_c = take(t.nu * TD_CB);
+  t.o_st = take(TD_STATE_INTS * B);
+  t.bytes = (size_t)o * sizeof(float);
+  return t;
+}
+
+// The layout the launch uses: every LSTM layer resident when they all fit.
+inline TdLayout td_layout_for(int H, int J, int L, int VP, int G, int B) {
+  TdLayout t = td_layout(H, J, L, VP, G, B, L);
+  if (t.bytes > TD_SMEM_LIMIT && L > 1) t = td_layout(H, J, L, VP, G, B, 1);
+  return t;
+}
+
+// ---------------------------------------------------------------- bulk copies
+__device__ __forceinline__ void mbar_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.expect_tx.relaxed.cta.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(bytes) : "memory");
+}
+
+// Global -> this CTA's shared memory, completing `bytes` on the mbarrier.
+// Both addresses 16-byte aligned, bytes a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst),
+               "l"(src), "r"(bytes), "r"(bar)
+               : "memory");
+}
+
+// Generic-proxy writes to global memory before async-proxy reads of them.
+__device__ __forceinline__ void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+
+// One copy per calling lane (src null: none), then one arrival: the calling
+// warp must be converged.
+__device__ __forceinline__ void warp_copy(uint32_t bar, uint32_t dst, const void* src, uint32_t bytes) {
+  if (src) {
+    mbar_expect_tx(bar, bytes);
+    bulk_g2s(dst, src, bytes, bar);
+  }
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(bar);
+}
+
+// Every thread waits for the phase; false in every thread if any timed out
+// (the phase then stays outstanding).
+__device__ __forceinline__ bool cta_wait(uint32_t bar, uint32_t& parity, bool& outstanding, int* err) {
+  const bool ok = __syncthreads_and(mbar_wait(bar, parity, err, DEV_ERR_TIMEOUT_DECODE)) != 0;
+  if (ok) {
+    parity ^= 1u;
+    outstanding = false;
+  }
+  return ok;
+}
+
+// ---------------------------------------------------------------- grid barrier
+// Barrier k of the launch completes when the arrival counter (zeroed by the
+// host before the launch) reaches k * gridDim.x.
+__device__ __forceinline__ bool grid_sync(unsigned int* count, unsigned int& target, int* err, int* smem_ok) {
+  target += gridDim.x;
   __syncthreads();
   if (threadIdx.x == 0) {
     bool ok = true;
-    unsigned int g;
-    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(g) : "l"(bar_gen) : "memory");
     __threadfence();
-    const unsigned int arrived = atomicAdd(bar_count, 1u) + 1u;
-    if (arrived == gridDim.x) {
-      *bar_count = 0u;
-      __threadfence();
-      asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(bar_gen), "r"(g + 1u) : "memory");
-    } else {
-      const unsigned long long t0 = globaltimer_ns();
-      for (uint32_t it = 0;; ++it) {
-        unsigned int cur;
-        asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(cur) : "l"(bar_gen) : "memory");
-        if (cur != g) break;
-        if ((it & 255u) == 255u && globaltimer_ns() - t0 > kWaitLimitNs) {
-          report_error(err, DEV_ERR_TIMEOUT_DECODE);
-          ok = false;
-          break;
-        }
-        if (it > 4096u) __nanosleep(128);  // spin first: phases are a few microseconds
+    asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(count) : "memory");
+    const unsigned long long t0 = globaltimer_ns();
+    for (uint32_t it = 0;; ++it) {
+      unsigned int cur;
+      asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(cur) : "l"(count) : "memory");
+      if ((int)(cur - target) >= 0) break;
+      if ((it & 255u) == 255u && globaltimer_ns() - t0 > kWaitLimitNs) {
+        report_error(err, DEV_ERR_TIMEOUT_DECODE);
+        ok = false;
+        break;
       }
+      if (it > 4096u) __nanosleep(128);  // spin first: phases are a few microseconds
     }
     __threadfence();
     *smem_ok = ok ? 1 : 0;
@@ -77,72 +167,106 @@ __device__ __forceinline__ bool grid_sync(unsigned int* bar_count, unsigned int*
 
 __device__ __forceinline__ float sigm(float x) { return 1.0f / (1.0f + __expf(-x)); }
 
-// Weight-row slice of this lane, loaded as one block of independent loads
-// (volatile, so the compiler cannot sink them one by one next to their uses
-// under register pressure: each would then cost a full L2 round trip).
-__device__ __forceinline__ void load_row(float4 (&w)[8], const float* row, int n) {
-  const int lane = threadIdx.x & 31;
+// Order-preserving map of a float onto 32 unsigned bits; NaN ranks below
+// every number.
+__device__ __forceinline__ uint32_t ord_bits(float x) {
+  if (x != x) return 0u;
+  const uint32_t u = __float_as_uint(x);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+__device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
+  return ((unsigned long long)ord_bits(v) << 32) | (unsigned long long)(~(uint32_t)idx);
+}
+
+// sZ[r][i] = sum_k W[min(r, nr - 1)][k] * X[i][k] for r < TD_RG, i < TD_CB.
+// W rows at stride ldw, X rows at stride ldx (both in shared memory). All
+// threads call it; it ends with sZ visible to the CTA.
+__device__ __forceinline__ void cta_gemv(const float* W, int ldw, int nr, const float* X, int ldx, int K, float* sR,
+                                         float* sZ) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ks = ((K + TD_WARPS - 1) / TD_WARPS + 3) & ~3;  // k slice per warp, multiple of 4
+  const int kb = warp * ks, ke = min(K, kb + ks);
+  const int i = lane & (TD_CB - 1), rb = (lane >> 4) * 4;
+  const float* w[4];
 #pragma unroll
-  for (int u = 0; u < 8; ++u) {
-    const int k = lane * 4 + 128 * u;
-    if (k < n) {
-      asm volatile("ld.global.nc.v4.f32 {%0,%1,%2,%3}, [%4];"
-                   : "=f"(w[u].x), "=f"(w[u].y), "=f"(w[u].z), "=f"(w[u].w)
-                   : "l"(row + k));
-    } else {
-      w[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int rr = 0; rr < 4; ++rr) w[rr] = W + min(rb + rr, nr - 1) * ldw;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  const float* xr = X + i * ldx;
+#pragma unroll 4
+  for (int k = kb; k < ke; k += 4) {
+    const float4 x = *reinterpret_cast<const float4*>(xr + k);
+#pragma unroll
+    for (int rr = 0; rr < 4; ++rr) {
+      const float4 v = *reinterpret_cast<const float4*>(w[rr] + k);
+      acc[rr] = fmaf(v.x, x.x, fmaf(v.y, x.y, fmaf(v.z, x.z, fmaf(v.w, x.w, acc[rr]))));
     }
   }
-}
-
-// dot of a weight row (n floats, n % 4 == 0, 16-byte aligned) with a vector
-__device__ __forceinline__ float warp_dot(const float* __restrict__ w, const float* __restrict__ x, int n) {
-  const int lane = threadIdx.x & 31;
-  float s = 0.f;
-  for (int k = lane * 4; k < n; k += 128) {
-    const float4 a = __ldg(reinterpret_cast<const float4*>(w + k));
-    const float4 b = *reinterpret_cast<const float4*>(x + k);
-    s = fmaf(a.x, b.x, s);
-    s = fmaf(a.y, b.y, s);
-    s = fmaf(a.z, b.z, s);
-    s = fmaf(a.w, b.w, s);
-  }
 #pragma unroll
-  for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-  return s;
-}
-
-// Merge partial q into p (max with first index on ties; sum of exp rescaled).
-__device__ __forceinline__ void merge_partial(Partial& p, const Partial& q) {
-  if (q.tmax > p.tmax || (q.tmax == p.tmax && q.targ < p.targ)) {
-    p.tsum = (p.tmax == -INFINITY ? 0.f : p.tsum * __expf(p.tmax - q.tmax)) + q.tsum;
-    p.tmax = q.tmax;
-    p.targ = q.targ;
-  } else if (q.tmax != -INFINITY) {
-    p.tsum += q.tsum * __expf(q.tmax - p.tmax);
+  for (int rr = 0; rr < 4; ++rr) sR[(warp * TD_RG + rb + rr) * TD_CB + i] = acc[rr];
+  __syncthreads();
+  if (threadIdx.x < TD_RG * TD_CB) {
+    float s = 0.f;
+#pragma unroll
+    for (int w2 = 0; w2 < TD_WARPS; ++w2) s += sR[w2 * TD_RG * TD_CB + threadIdx.x];
+    sZ[threadIdx.x] = s;
   }
-  if (q.dmax > p.dmax || (q.dmax == p.dmax && q.darg < p.darg)) {
-    p.dmax = q.dmax;
-    p.darg = q.darg;
-  }
+  __syncthreads();
 }
 
 __global__ void __launch_bounds__(TD_THREADS, 1) k_transducer_greedy(TransducerArgs a) {
-  extern __shared__ float sh[];  // [TD_CHUNK][J] joint hidden vectors, then the utterance state
-  __shared__ int s_ok, s_pending, s_done;
+  extern __shared__ __align__(16) float sm[];
+  __shared__ __align__(8) unsigned long long s_bar[2];  // 0: weights, 1: inputs
+  __shared__ int s_ok, s_np, s_nd;
+  __shared__ int s_dur[TD_MAX_DUR];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = gridDim.x, cta = blockIdx.x;
   const int H = a.H, J = a.J, L = a.L, V1 = a.V1, VP = a.V1 + a.D, B = a.B;
-  // Every CTA keeps its own copy of the per-utterance state and makes the
-  // (deterministic) decisions itself, so no barrier follows the decisions;
-  // CTA 0 alone writes the tokens.
-  int* st_t = reinterpret_cast<int*>(sh + TD_CHUNK * max(2 * H, J));
+  const TdLayout lay = td_layout(H, J, L, VP, G, B, a.held);
+  const int ldk = lay.ldk;
+  float* sX = sm + lay.o_x;
+  float* sWl = sm + lay.o_wl;
+  float* sWp = sm + lay.o_wp;
+  float* sWj = sm + lay.o_wj;
+  float* sBl = sm + lay.o_bl;
+  float* sBp = sm + lay.o_bp;
+  float* sBj = sm + lay.o_bj;
+  float* sR = sm + lay.o_r;
+  float* sZ = sm + lay.o_z;
+  float* sC = sm + lay.o_c;
+  // per-utterance state (this CTA's copy) and constants
+  int* st_t = reinterpret_cast<int*>(sm + lay.o_st);
   int* st_sym = st_t + B;
   int* st_cur = st_sym + B;
   int* st_have = st_cur + B;
   int* st_last = st_have + B;
   int* st_pend = st_last + B;
   int* st_done = st_pend + B;
+  int* st_ntok = st_done + B;
+  int* st_off = st_ntok + B;
+  int* st_len = st_off + B;
+  int* st_toff = st_len + B;
+  int* st_tcap = st_toff + B;
+  int* st_emit = st_tcap + B;  // stored a token in the last iteration
+  const uint32_t bar_w = smem_u32(&s_bar[0]), bar_x = smem_u32(&s_bar[1]);
+  uint32_t par_w = 0, par_x = 0;
+  bool w_out = false, x_out = false;  // a phase of bar_w / bar_x with copies not yet waited for
+  unsigned int bar_target = 0;
+  unsigned long long* tok_key = a.keys;          // [3][B]
+  unsigned long long* dur_key = a.keys + 3 * B;  // [3][B]
+  float2* parts_all = reinterpret_cast<float2*>(a.keys + 6 * B);  // [2][G][B] (max, sum of exp)
+
+  // this CTA's rows: hidden units [u0, u1), pred rows [j0, j1), joint rows [v0, v1)
+  const int u0 = (int)((long long)H * cta / G), u1 = (int)((long long)H * (cta + 1) / G);
+  const int j0 = (int)((long long)J * cta / G), j1 = (int)((long long)J * (cta + 1) / G);
+  const int v0 = (int)((long long)VP * cta / G), v1 = (int)((long long)VP * (cta + 1) / G);
+  const int nu = u1 - u0, nj = j1 - j0, nv = v1 - v0;
+  const size_t wl_slot = (size_t)4 * lay.nu * 2 * H;  // floats per resident LSTM layer
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar_w, 1);
+    mbar_init(bar_x, 1);
+    fence_barrier_init();
+  }
   for (int b = threadIdx.x; b < B; b += TD_THREADS) {
     st_t[b] = a.t[b];
     st_sym[b] = a.sym[b];
@@ -151,381 +275,379 @@ __global__ void __launch_bounds__(TD_THREADS, 1) k_transducer_greedy(TransducerA
     st_last[b] = a.last_token[b];
     st_pend[b] = a.pending[b];
     st_done[b] = a.done[b];
+    st_ntok[b] = a.ntok[b];
+    st_off[b] = a.item_off[b];
+    st_len[b] = a.item_len[b];
+    st_toff[b] = a.tok_off[b];
+    st_tcap[b] = a.tok_cap[b];
+    st_emit[b] = 0;
   }
-  if (threadIdx.x == 0) s_pending = *a.n_pending;
+  for (int i = threadIdx.x; i < a.D; i += TD_THREADS) s_dur[i] = a.durations[i];
+  for (int i = threadIdx.x; i < L * 4 * nu; i += TD_THREADS) {  // [l][unit][gate]
+    const int l = i / (4 * nu), r = i % (4 * nu);
+    sBl[(l * lay.nu + (r >> 2)) * 4 + (r & 3)] = a.b_lstm[(size_t)l * 4 * H + (r & 3) * H + u0 + (r >> 2)];
+  }
+  for (int i = threadIdx.x; i < nj; i += TD_THREADS) sBp[i] = a.b_pred[j0 + i];
+  for (int i = threadIdx.x; i < nv; i += TD_THREADS) sBj[i] = a.b_out[v0 + i];
   __syncthreads();
 
-  for (int iter = 0;; ++iter) {
-    Partial* parts = reinterpret_cast<Partial*>(a.partials) + (size_t)(iter & 1) * G * B;
-    // ---- P: prediction network for utterances whose output is stale. The
-    // chunk's input / hidden vectors are staged in shared memory by one
-    // coalesced pass; a warp owns one hidden unit, holds each of its gate rows
-    // in registers (one round trip per row pair) and applies it to the chunk.
-    if (s_pending > 0) {
+  // copies of LSTM layer l's rows into resident slot s (row 4 u + q = gate q of
+  // unit u0 + u: [W_ih row | W_hh row]); lanes of warp 0 split them
+  auto copy_lstm = [&](int l, int s) {
+    const float* wi = a.w_ih + (size_t)l * 4 * H * H;
+    const float* wh = a.w_hh + (size_t)l * 4 * H * H;
+    float* dst = sWl + (size_t)s * wl_slot;
+    for (int c = lane; c < 8 * nu; c += 32) {
+      const int r = c >> 1, half = c & 1;
+      const size_t row = (size_t)((r & 3) * H + u0 + (r >> 2)) * H;
+      bulk_g2s(smem_u32(dst + (size_t)r * 2 * H + half * H), (half ? wh : wi) + row, (uint32_t)(H * 4), bar_w);
+    }
+  };
+
+  // resident weights: LSTM layers [0, held), pred rows, joint rows
+  if (warp == 0) {
+    if (lane == 0) mbar_expect_tx(bar_w, (uint32_t)((8 * nu * H * a.held + nj * H + nv * J) * 4));
+    __syncwarp();
+    for (int l = 0; l < a.held; ++l) copy_lstm(l, l);
+    for (int r = lane; r < nj; r += 32)
+      bulk_g2s(smem_u32(sWp + (size_t)r * H), a.w_pred + (size_t)(j0 + r) * H, (uint32_t)(H * 4), bar_w);
+    for (int r = lane; r < nv; r += 32)
+      bulk_g2s(smem_u32(sWj + (size_t)r * J), a.w_out + (size_t)(v0 + r) * J, (uint32_t)(J * 4), bar_w);
+    __syncwarp();
+    if (lane == 0) mbar_arrive(bar_w);
+  }
+  w_out = true;
+  // before leaving: give copies still in flight their (bounded) time to land
+  auto drain = [&]() {
+    if (w_out) mbar_wait(bar_w, par_w, nullptr, 0);
+    if (x_out) mbar_wait(bar_x, par_x, nullptr, 0);
+    __syncthreads();
+  };
+  const bool stream_lstm = a.held < L;  // one resident layer: the next one is copied during the barrier
+  if (!stream_lstm && !cta_wait(bar_w, par_w, w_out, a.err)) return drain();
+
+  auto chunk_has = [&](int c0, const int* flags, int want) {
+    bool any = false;
+    for (int i = 0; i < TD_CB && c0 + i < B; ++i) any |= flags[c0 + i] == want;
+    return any;
+  };
+  // confidence of the token utterance b stored in the last iteration, from
+  // that iteration's per-CTA partials (one warp)
+  auto merge_conf = [&](const float2* parts, int b) {
+    float m = -INFINITY, s = 0.f;
+    for (int c = lane; c < G; c += 32) {
+      const float2 q = __ldcg(parts + (size_t)c * B + b);
+      if (q.x > m) {
+        s = (m == -INFINITY ? 0.f : s * __expf(m - q.x)) + q.y;
+        m = q.x;
+      } else if (q.x != -INFINITY) {
+        s += q.y * __expf(q.x - m);
+      }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float om = __shfl_xor_sync(0xffffffffu, m, o), os = __shfl_xor_sync(0xffffffffu, s, o);
+      const float nm = fmaxf(m, om);
+      s = (m == -INFINITY ? 0.f : s * __expf(m - nm)) + (om == -INFINITY ? 0.f : os * __expf(om - nm));
+      m = nm;
+    }
+    if (lane == 0) {
+      // max_prob confidence over the token part: (N p_max - 1) / (N - 1), p_max = 1 / s
+      const float conf = ((float)V1 * (1.0f / s) - 1.0f) / ((float)V1 - 1.0f);
+      a.tokens[((size_t)st_toff[b] + st_ntok[b] - 1) * 4 + 2] = __float_as_int(conf);
+    }
+  };
+  auto merge_confs = [&](int it) {
+    const float2* pp = parts_all + (size_t)(it & 1) * G * B;
+    for (int b = cta; b < B; b += G)
+      if (st_emit[b]) merge_conf(pp, b);
+  };
+
+  int n_pending = 0;
+  for (int b = 0; b < B; ++b) n_pending += st_pend[b];
+  int iter = 0;
+  for (;; ++iter) {
+    // ---- P: prediction network (utterances whose output is stale)
+    if (n_pending > 0) {
       for (int l = 0; l < L; ++l) {
-        const float* wi = a.w_ih + (size_t)l * 4 * H * H;
-        const float* wh = a.w_hh + (size_t)l * 4 * H * H;
-        const float* bb = a.b_lstm + (size_t)l * 4 * H;
-        for (int b0 = 0; b0 < B; b0 += TD_CHUNK) {
-          bool any = false;
-          for (int bi = 0; bi < TD_CHUNK && b0 + bi < B; ++bi) any |= st_pend[b0 + bi] != 0;
-          if (!any) continue;  // uniform across the CTA
-          __syncthreads();
-          {
-            // every load of this thread first (global space, L2-coherent: the
-            // vectors were written by other CTAs in this launch), then the stores
-            float xv[TD_CHUNK][TD_STG], hv[TD_CHUNK][TD_STG];
-#pragma unroll
-            for (int bi = 0; bi < TD_CHUNK; ++bi) {
-              const int b = b0 + bi;
-              const bool act = b < B && st_pend[b];
-              const int cur = act ? st_cur[b] : 0;
-              const float* hp = a.h + (((size_t)cur * L + l) * B + (act ? b : 0)) * H;
-              const float* xp = !act ? nullptr
-                                : l > 0 ? a.h + (((size_t)(1 - cur) * L + (l - 1)) * B + b) * H
-                                : st_have[b] ? a.embed + (size_t)st_last[b] * H
-                                             : nullptr;  // SOS: zero input
-#pragma unroll
-              for (int r = 0; r < TD_STG; ++r) {
-                const int k = threadIdx.x + TD_THREADS * r;
-                xv[bi][r] = (xp && k < H) ? __ldcg(xp + k) : 0.f;
-                hv[bi][r] = (act && k < H) ? __ldcg(hp + k) : 0.f;
-              }
+        if (stream_lstm && !cta_wait(bar_w, par_w, w_out, a.err)) return drain();  // this layer's rows
+        const float* wl = sWl + (stream_lstm ? 0 : (size_t)l * wl_slot);
+        for (int c0 = 0; c0 < B; c0 += TD_CB) {
+          if (nu == 0 || !chunk_has(c0, st_pend, 1)) continue;  // uniform across the CTA
+          __syncthreads();  // earlier readers of sX / sC are done
+          if (warp == 0) {
+            // inputs [x | h] per pending utterance: x = embedding of the last
+            // token (zeros before the first one) for layer 0, the new output
+            // of the layer below otherwise; h = the committed state
+            fence_proxy_async_smem();
+            const int i = lane & (TD_CB - 1), b = c0 + i;
+            const float* src = nullptr;
+            if (b < B && st_pend[b]) {
+              const int cur = st_cur[b];
+              if (lane < TD_CB)
+                src = l > 0        ? a.h + (((size_t)(1 - cur) * L + (l - 1)) * B + b) * H
+                      : st_have[b] ? a.embed + (size_t)st_last[b] * H
+                                   : a.zeros;
+              else
+                src = a.h + (((size_t)cur * L + l) * B + b) * H;
             }
-#pragma unroll
-            for (int bi = 0; bi < TD_CHUNK; ++bi)
-#pragma unroll
-              for (int r = 0; r < TD_STG; ++r) {
-                const int k = threadIdx.x + TD_THREADS * r;
-                if (k < H) {
-                  sh[bi * 2 * H + k] = xv[bi][r];
-                  sh[bi * 2 * H + H + k] = hv[bi][r];
-                }
-              }
+            warp_copy(bar_x, smem_u32(sX + i * ldk + (lane < TD_CB ? 0 : H)), src, (uint32_t)(H * 4));
           }
-          __syncthreads();
-          for (int j = cta * TD_WARPS + warp; j < H; j += G * TD_WARPS) {
-            float acc[4][TD_CHUNK];
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-              float4 w1[TD_KV], w2[TD_KV];
-              load_row(w1, wi + (size_t)(q * H + j) * H, H);
-              load_row(w2, wh + (size_t)(q * H + j) * H, H);
-#pragma unroll
-              for (int bi = 0; bi < TD_CHUNK; ++bi) {
-                float s = 0.f;
-#pragma unroll
-                for (int u = 0; u < TD_KV; ++u) {
-                  const int k = lane * 4 + 128 * u;
-                  if (k < H) {
-                    const float4 x = *reinterpret_cast<const float4*>(sh + bi * 2 * H + k);
-                    const float4 h = *reinterpret_cast<const float4*>(sh + bi * 2 * H + H + k);
-                    s = fmaf(w1[u].x, x.x, s); s = fmaf(w1[u].y, x.y, s); s = fmaf(w1[u].z, x.z, s); s = fmaf(w1[u].w, x.w, s);
-                    s = fmaf(w2[u].x, h.x, s); s = fmaf(w2[u].y, h.y, s); s = fmaf(w2[u].z, h.z, s); s = fmaf(w2[u].w, h.w, s);
-                  }
-                }
-                acc[q][bi] = s;
-              }
-            }
-#pragma unroll
-            for (int q = 0; q < 4; ++q)
-#pragma unroll
-              for (int bi = 0; bi < TD_CHUNK; ++bi)
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) acc[q][bi] += __shfl_xor_sync(0xffffffffu, acc[q][bi], o);
-            if (lane < TD_CHUNK) {
-              // lane bi finishes utterance b0 + bi (values are warp-uniform)
-              float z[4];
-#pragma unroll
-              for (int q = 0; q < 4; ++q) {
-                float v = acc[q][0];
-#pragma unroll
-                for (int bi = 1; bi < TD_CHUNK; ++bi) v = lane == bi ? acc[q][bi] : v;
-                z[q] = v + bb[q * H + j];
-              }
-              const int b = b0 + lane;
-              if (b < B && st_pend[b]) {
+          x_out = true;
+          for (int e = threadIdx.x; e < nu * TD_CB; e += TD_THREADS) {  // committed cells [unit][item]
+            const int u = e / TD_CB, i = e % TD_CB, b = c0 + i;
+            sC[e] = (b < B && st_pend[b]) ? __ldcg(a.c + (((size_t)st_cur[b] * L + l) * B + b) * H + u0 + u) : 0.f;
+          }
+          if (!cta_wait(bar_x, par_x, x_out, a.err)) return drain();
+          for (int ug = 0; ug < nu; ug += 2) {
+            cta_gemv(wl + (size_t)ug * 4 * 2 * H, 2 * H, min(TD_RG, 4 * (nu - ug)), sX, ldk, 2 * H, sR, sZ);
+            if (threadIdx.x < 2 * TD_CB) {
+              const int uu = threadIdx.x / TD_CB, i = threadIdx.x % TD_CB, b = c0 + i, u = ug + uu;
+              if (u < nu && b < B && st_pend[b]) {
                 const int cur = st_cur[b];
-                const float cin = a.c[(((size_t)cur * L + l) * B + b) * H + j];
-                const float ig = sigm(z[0]), fg = sigm(z[1]), gg = tanhf(z[2]), og = sigm(z[3]);
-                const float cn = fmaf(fg, cin, ig * gg);
-                a.c[(((size_t)(1 - cur) * L + l) * B + b) * H + j] = cn;
-                a.h[(((size_t)(1 - cur) * L + l) * B + b) * H + j] = og * tanhf(cn);
+                const float* bl = sBl + (l * lay.nu + u) * 4;
+                const float zi = sZ[(uu * 4 + 0) * TD_CB + i] + bl[0];
+                const float zf = sZ[(uu * 4 + 1) * TD_CB + i] + bl[1];
+                const float zg = sZ[(uu * 4 + 2) * TD_CB + i] + bl[2];
+                const float zo = sZ[(uu * 4 + 3) * TD_CB + i] + bl[3];
+                const float cn = fmaf(sigm(zf), sC[u * TD_CB + i], sigm(zi) * tanhf(zg));
+                const size_t o = (((size_t)(1 - cur) * L + l) * B + b) * H + u0 + u;
+                a.c[o] = cn;
+                a.h[o] = sigm(zo) * tanhf(cn);
+                fence_proxy_async_global();  // read by the next phases' bulk copies
               }
             }
           }
         }
-        if (!grid_sync(a.bar_count, a.bar_gen, a.err, &s_ok)) return;
+        if (stream_lstm) {  // the slot is free: copy the next layer (of this step or the next)
+          __syncthreads();
+          if (warp == 0) {
+            fence_proxy_async_smem();
+            if (lane == 0) mbar_expect_tx(bar_w, (uint32_t)(8 * nu * H * 4));
+            __syncwarp();
+            copy_lstm((l + 1) % L, 0);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(bar_w);
+          }
+          w_out = true;
+        }
+        if (!grid_sync(a.bar_count, bar_target, a.err, &s_ok)) return drain();
       }
-      // pred projection of the new top-layer output: g vectors staged, a warp per row
-      for (int b0 = 0; b0 < B; b0 += TD_CHUNK) {
-        bool any = false;
-        for (int bi = 0; bi < TD_CHUNK && b0 + bi < B; ++bi) any |= st_pend[b0 + bi] != 0;
-        if (!any) continue;
+      // pred projection of the new top-layer output
+      for (int c0 = 0; c0 < B; c0 += TD_CB) {
+        if (nj == 0 || !chunk_has(c0, st_pend, 1)) continue;
         __syncthreads();
-        {
-          float gv[TD_CHUNK][TD_STG];
-#pragma unroll
-          for (int bi = 0; bi < TD_CHUNK; ++bi) {
-            const int b = b0 + bi;
-            const bool act = b < B && st_pend[b];
-            const float* gp = act ? a.h + (((size_t)(1 - st_cur[b]) * L + (L - 1)) * B + b) * H : nullptr;
-#pragma unroll
-            for (int r = 0; r < TD_STG; ++r) {
-              const int k = threadIdx.x + TD_THREADS * r;
-              gv[bi][r] = (act && k < H) ? __ldcg(gp + k) : 0.f;
+        if (warp == 0) {
+          fence_proxy_async_smem();
+          const int b = c0 + lane;
+          const float* src = (lane < TD_CB && b < B && st_pend[b])
+                                 ? a.h + (((size_t)(1 - st_cur[b]) * L + (L - 1)) * B + b) * H
+                                 : nullptr;
+          warp_copy(bar_x, smem_u32(sX + (lane & (TD_CB - 1)) * ldk), src, (uint32_t)(H * 4));
+        }
+        x_out = true;
+        if (!cta_wait(bar_x, par_x, x_out, a.err)) return drain();
+        for (int r0 = 0; r0 < nj; r0 += TD_RG) {
+          const int nr = min(TD_RG, nj - r0);
+          cta_gemv(sWp + (size_t)r0 * H, H, nr, sX, ldk, H, sR, sZ);
+          if (threadIdx.x < TD_RG * TD_CB) {
+            const int r = threadIdx.x / TD_CB, i = threadIdx.x % TD_CB, b = c0 + i;
+            if (r < nr && b < B && st_pend[b]) {
+              a.pred_proj[(size_t)b * J + j0 + r0 + r] = sZ[threadIdx.x] + sBp[r0 + r];
+              fence_proxy_async_global();
             }
           }
-#pragma unroll
-          for (int bi = 0; bi < TD_CHUNK; ++bi)
-#pragma unroll
-            for (int r = 0; r < TD_STG; ++r) {
-              const int k = threadIdx.x + TD_THREADS * r;
-              if (k < H) sh[bi * H + k] = gv[bi][r];
-            }
         }
-        __syncthreads();
-        for (int jj = cta * TD_WARPS + warp; jj < J; jj += G * TD_WARPS) {
-          float4 w[TD_KV];
-          load_row(w, a.w_pred + (size_t)jj * H, H);
-          float acc[TD_CHUNK];
-#pragma unroll
-          for (int bi = 0; bi < TD_CHUNK; ++bi) {
-            float s = 0.f;
-#pragma unroll
-            for (int u = 0; u < TD_KV; ++u) {
-              const int k = lane * 4 + 128 * u;
-              if (k < H) {
-                const float4 g = *reinterpret_cast<const float4*>(sh + bi * H + k);
-                s = fmaf(w[u].x, g.x, fmaf(w[u].y, g.y, fmaf(w[u].z, g.z, fmaf(w[u].w, g.w, s))));
+      }
+      if (!grid_sync(a.bar_count, bar_target, a.err, &s_ok)) return drain();
+    }
+
+    // ---- J: joint rows [v0, v1) of this CTA for every live utterance
+    const int kb = iter % 3;
+    float2* parts = parts_all + (size_t)(iter & 1) * G * B;
+    bool conf_done = iter == 0;
+    for (int c0 = 0; c0 < B; c0 += TD_CB) {
+      if (!chunk_has(c0, st_done, 0)) continue;
+      __syncthreads();
+      if (warp == 0) {  // [enc_proj row of the utterance's frame | pred_proj]
+        fence_proxy_async_smem();
+        const int i = lane & (TD_CB - 1), b = c0 + i;
+        const float* src = nullptr;
+        if (b < B && !st_done[b])
+          src = lane < TD_CB ? a.enc_proj + (size_t)(st_off[b] + st_t[b]) * a.ld_enc : a.pred_proj + (size_t)b * J;
+        warp_copy(bar_x, smem_u32(sX + i * ldk + (lane < TD_CB ? 0 : J)), src, (uint32_t)(J * 4));
+      }
+      x_out = true;
+      if (!conf_done && warp == 1) merge_confs(iter - 1);  // overlaps the copies
+      conf_done = true;
+      if (!cta_wait(bar_x, par_x, x_out, a.err)) return drain();
+      for (int e = threadIdx.x; e < TD_CB * (J / 4); e += TD_THREADS) {  // sX[i] = ReLU(enc + pred)
+        const int i = e / (J / 4), k = (e % (J / 4)) * 4;
+        float4* x = reinterpret_cast<float4*>(sX + i * ldk + k);
+        const float4 e4 = *x, p4 = *reinterpret_cast<const float4*>(sX + i * ldk + J + k);
+        *x = make_float4(fmaxf(e4.x + p4.x, 0.f), fmaxf(e4.y + p4.y, 0.f), fmaxf(e4.z + p4.z, 0.f),
+                         fmaxf(e4.w + p4.w, 0.f));
+      }
+      __syncthreads();
+      // thread i < TD_CB: running (token max, first arg, sum of exp) and (duration max, first arg)
+      float tmax = -INFINITY, tsum = 0.f, dmax = -INFINITY;
+      int targ = -1, darg = -1;
+      for (int r0 = 0; r0 < nv; r0 += TD_RG) {
+        const int nr = min(TD_RG, nv - r0);
+        cta_gemv(sWj + (size_t)r0 * J, J, nr, sX, ldk, J, sR, sZ);
+        if (threadIdx.x < TD_CB) {
+          for (int r = 0; r < nr; ++r) {  // rows in increasing order: the first maximum wins on ties
+            const int v = v0 + r0 + r;
+            const float lg = sZ[r * TD_CB + threadIdx.x] + sBj[r0 + r];
+            if (v < V1) {
+              if (targ < 0 || lg > tmax) {
+                tsum = (targ < 0 ? 0.f : tsum * __expf(tmax - lg)) + 1.f;
+                tmax = lg;
+                targ = v;
+              } else {
+                tsum += __expf(lg - tmax);
               }
+            } else if (darg < 0 || lg > dmax) {
+              dmax = lg;
+              darg = v - V1;
             }
-            acc[bi] = s;
-          }
-#pragma unroll
-          for (int bi = 0; bi < TD_CHUNK; ++bi)
-#pragma unroll
-            for (int o = 16; o > 0; o >>= 1) acc[bi] += __shfl_xor_sync(0xffffffffu, acc[bi], o);
-          if (lane < TD_CHUNK) {
-            float v = acc[0];
-#pragma unroll
-            for (int bi = 1; bi < TD_CHUNK; ++bi) v = lane == bi ? acc[bi] : v;
-            const int b = b0 + lane;
-            if (b < B && st_pend[b]) a.pred_proj[(size_t)b * J + jj] = v + a.b_pred[jj];
           }
         }
       }
-      if (!grid_sync(a.bar_count, a.bar_gen, a.err, &s_ok)) return;
+      if (threadIdx.x < TD_CB) {
+        const int b = c0 + threadIdx.x;
+        if (b < B && !st_done[b]) {
+          if (targ >= 0) atomicMax(tok_key + kb * B + b, argmax_key(tmax, targ));
+          if (darg >= 0) atomicMax(dur_key + kb * B + b, argmax_key(dmax, darg));
+          parts[(size_t)cta * B + b] = targ >= 0 ? make_float2(tmax, tsum) : make_float2(-INFINITY, 0.f);
+        }
+      }
     }
+    if (!conf_done && warp == 1) merge_confs(iter - 1);  // no live utterance left in any chunk
+    if (!grid_sync(a.bar_count, bar_target, a.err, &s_ok)) return drain();
 
-    // ---- J: joint output rows of this CTA for every active utterance; a warp
-    // reads each of its rows once and applies it to TD_CHUNK utterances
-    const int r0 = (int)((long long)VP * cta / G), r1 = (int)((long long)VP * (cta + 1) / G);
-    for (int b0 = 0; b0 < B; b0 += TD_CHUNK) {
-      const int nb = min(TD_CHUNK, B - b0);
-      bool any = false;
-      for (int bi = 0; bi < nb; ++bi) any |= !st_done[b0 + bi];
-      if (!any) continue;  // uniform across the CTA
-      __syncthreads();
-      {
-        float fv[TD_CHUNK][TD_STG];
-#pragma unroll
-        for (int bi = 0; bi < TD_CHUNK; ++bi) {
-          const int b = b0 + bi;
-          const bool act = bi < nb && !st_done[b];
-          const float* ep = act ? a.enc_proj + (size_t)(a.item_off[b] + st_t[b]) * a.ld_enc : nullptr;
-          const float* pp = act ? a.pred_proj + (size_t)b * J : nullptr;
-#pragma unroll
-          for (int r = 0; r < TD_STG; ++r) {
-            const int j = threadIdx.x + TD_THREADS * r;
-            fv[bi][r] = (act && j < J) ? fmaxf(__ldg(ep + j) + __ldcg(pp + j), 0.f) : 0.f;
-          }
-        }
-#pragma unroll
-        for (int bi = 0; bi < TD_CHUNK; ++bi)
-#pragma unroll
-          for (int r = 0; r < TD_STG; ++r) {
-            const int j = threadIdx.x + TD_THREADS * r;
-            if (j < J) sh[bi * J + j] = fv[bi][r];
-          }
-      }
-      __syncthreads();
-      float tmax[TD_CHUNK], tsum[TD_CHUNK], dmax[TD_CHUNK];
-      int targ[TD_CHUNK], darg[TD_CHUNK];
-#pragma unroll
-      for (int bi = 0; bi < TD_CHUNK; ++bi) {
-        tmax[bi] = -INFINITY; tsum[bi] = 0.f; dmax[bi] = -INFINITY;
-        targ[bi] = 0x7fffffff; darg[bi] = 0x7fffffff;
-      }
-      for (int v = r0 + warp; v < r1; v += TD_WARPS) {
-        float4 w[TD_KV];
-        load_row(w, a.w_out + (size_t)v * J, J);
-        float acc[TD_CHUNK];
-#pragma unroll
-        for (int bi = 0; bi < TD_CHUNK; ++bi) {
-          float s = 0.f;
-#pragma unroll
-          for (int u = 0; u < TD_KV; ++u) {
-            const int k = lane * 4 + 128 * u;
-            if (k < J) {
-              const float4 f = *reinterpret_cast<const float4*>(sh + bi * J + k);
-              s = fmaf(w[u].x, f.x, fmaf(w[u].y, f.y, fmaf(w[u].z, f.z, fmaf(w[u].w, f.w, s))));
-            }
-          }
-          acc[bi] = s;
-        }
-        const float bo = a.b_out[v];
-#pragma unroll
-        for (int bi = 0; bi < TD_CHUNK; ++bi) {
-#pragma unroll
-          for (int o = 16; o > 0; o >>= 1) acc[bi] += __shfl_xor_sync(0xffffffffu, acc[bi], o);
-          const float lg = acc[bi] + bo;
-          if (v < V1) {
-            if (lg > tmax[bi]) {
-              tsum[bi] = tsum[bi] * __expf(tmax[bi] - lg) + 1.f;
-              tmax[bi] = lg;
-              targ[bi] = v;
-            } else {
-              tsum[bi] += __expf(lg - tmax[bi]);
-            }
-          } else if (lg > dmax[bi]) {
-            dmax[bi] = lg;
-            darg[bi] = v - V1;
-          }
-        }
-      }
-      // merge the warps of this CTA per utterance (lane 0 of each holds the values)
-      __shared__ Partial wp[TD_WARPS][TD_CHUNK];
-      if (lane == 0)
-#pragma unroll
-        for (int bi = 0; bi < TD_CHUNK; ++bi) wp[warp][bi] = Partial{tmax[bi], tsum[bi], dmax[bi], targ[bi], darg[bi]};
-      __syncthreads();
-      if (threadIdx.x < nb) {
-        const int bi = threadIdx.x, b = b0 + bi;
-        if (!st_done[b]) {
-          Partial p = wp[0][bi];
-          for (int w = 1; w < TD_WARPS; ++w) merge_partial(p, wp[w][bi]);
-          parts[(size_t)cta * B + b] = p;
-        }
-      }
-      __syncthreads();
+    // ---- D: decisions, in every CTA (a thread per utterance)
+    if (threadIdx.x == 0) {
+      s_np = 0;
+      s_nd = 0;
     }
-    if (!grid_sync(a.bar_count, a.bar_gen, a.err, &s_ok)) return;
-
-    // ---- D: decisions, in every CTA (one warp per utterance)
-    for (int b = warp; b < B; b += TD_WARPS) {
-      if (st_done[b]) continue;
-      Partial p{-INFINITY, 0.f, -INFINITY, 0x7fffffff, 0x7fffffff};
-      for (int c0 = 0; c0 < G; c0 += 32 * 8) {
-        Partial q[8];
-#pragma unroll
-        for (int u = 0; u < 8; ++u) {  // all loads first
-          const int c = c0 + 32 * u + lane;
-          if (c < G) {
-            const float* pf = reinterpret_cast<const float*>(parts + (size_t)c * B + b);
-            q[u] = Partial{__ldcg(pf), __ldcg(pf + 1), __ldcg(pf + 2), __float_as_int(__ldcg(pf + 3)),
-                           __float_as_int(__ldcg(pf + 4))};
-          } else {
-            q[u] = Partial{-INFINITY, 0.f, -INFINITY, 0x7fffffff, 0x7fffffff};
-          }
-        }
-#pragma unroll
-        for (int u = 0; u < 8; ++u) merge_partial(p, q[u]);
-      }
-#pragma unroll
-      for (int o = 16; o > 0; o >>= 1) {
-        Partial q;
-        q.tmax = __shfl_xor_sync(0xffffffffu, p.tmax, o);
-        q.tsum = __shfl_xor_sync(0xffffffffu, p.tsum, o);
-        q.targ = __shfl_xor_sync(0xffffffffu, p.targ, o);
-        q.dmax = __shfl_xor_sync(0xffffffffu, p.dmax, o);
-        q.darg = __shfl_xor_sync(0xffffffffu, p.darg, o);
-        merge_partial(p, q);
-      }
-      if (lane == 0) {
-        const int k = p.targ;
-        int t = st_t[b];
-        const bool emit = k != a.blank;
-        const int skip = a.D > 0 ? a.durations[p.darg] : 1;
-        if (emit) {
-          if (cta == 0) {
-            // max_prob confidence over the token part: (N p_max - 1) / (N - 1)
-            const float conf = ((float)V1 * (1.0f / p.tsum) - 1.0f) / ((float)V1 - 1.0f);
-            const int n = a.ntok[b];
-            if (n < a.tok_cap[b]) {
-              int* tk = a.tokens + ((size_t)a.tok_off[b] + n) * 4;
-              tk[0] = k;
-              tk[1] = t;
-              tk[2] = __float_as_int(conf);
-              tk[3] = a.D > 0 ? skip : 1;
-              a.ntok[b] = n + 1;
-            } else {
-              report_error(a.err, DEV_ERR_BAD_SHAPE);
-            }
-          }
-          st_last[b] = k;
-          st_have[b] = 1;
-          st_cur[b] = 1 - st_cur[b];  // commit the step's (h', c')
-        }
-        int sym = st_sym[b] + 1;
-        if (a.D > 0) {
-          // tdt_greedy: symbols_added += 1; t += skip; stay while skip == 0
-          t += skip;
-          if (!(skip == 0 && sym < a.max_symbols)) {
-            if (sym == a.max_symbols) t += 1;
-            sym = 0;
-          }
-        } else if (!emit || sym >= a.max_symbols) {
-          // rnnt: blank -> next frame; max_symbols emissions -> next frame
-          t += 1;
-          sym = 0;
-        }
-        st_t[b] = t;
-        st_sym[b] = sym;
-        st_pend[b] = emit ? 1 : 0;  // a new committed state needs a new prediction
-        if (t >= a.item_len[b]) {
+    __syncthreads();
+    int np = 0, nd = 0;
+    for (int b = threadIdx.x; b < B; b += TD_THREADS) {
+      int emitted = 0;
+      if (!st_done[b]) {
+        const unsigned long long tk = __ldcg(tok_key + kb * B + b);
+        const unsigned long long dk = a.D > 0 ? __ldcg(dur_key + kb * B + b) : 0ull;
+        const int k = (int)~(uint32_t)tk, da = (int)~(uint32_t)dk;
+        if (tk == 0ull || k < 0 || k >= V1 || (a.D > 0 && (dk == 0ull || da < 0 || da >= a.D))) {
+          // no CTA produced a maximum: no token or duration to follow
+          if (cta == 0) report_error(a.err, DEV_ERR_NONFINITE);
           st_done[b] = 1;
           st_pend[b] = 0;
+        } else {
+          int t = st_t[b];
+          const bool emit = k != a.blank;
+          const int skip = a.D > 0 ? s_dur[da] : 1;
+          if (emit) {
+            const int n = st_ntok[b];
+            if (n < st_tcap[b]) {
+              if (cta == 0) {
+                int* tk4 = a.tokens + ((size_t)st_toff[b] + n) * 4;
+                tk4[0] = k;
+                tk4[1] = t;  // tk4[2], the confidence, is merged during the next iteration
+                tk4[3] = a.D > 0 ? skip : 1;
+                a.ntok[b] = n + 1;
+              }
+              st_ntok[b] = n + 1;
+              emitted = 1;
+            } else if (cta == 0) {
+              report_error(a.err, DEV_ERR_BAD_SHAPE);
+            }
+            st_last[b] = k;
+            st_have[b] = 1;
+            st_cur[b] = 1 - st_cur[b];  // commit the step's (h', c')
+          }
+          int sym = st_sym[b] + 1;
+          if (a.D > 0) {
+            // tdt_greedy: symbols_added += 1; t += skip; stay while skip == 0
+            t += skip;
+            if (!(skip == 0 && sym < a.max_symbols)) {
+              if (sym == a.max_symbols) t += 1;
+              sym = 0;
+            }
+          } else if (!emit || sym >= a.max_symbols) {
+            // rnnt: blank -> next frame; max_symbols emissions -> next frame
+            t += 1;
+            sym = 0;
+          }
+          st_t[b] = t;
+          st_sym[b] = sym;
+          st_pend[b] = emit ? 1 : 0;  // a new committed state needs a new prediction
+          if (t >= st_len[b]) {
+            st_done[b] = 1;
+            st_pend[b] = 0;
+          }
         }
       }
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      int np = 0, nd = 0;
-      for (int b = 0; b < B; ++b) {
-        np += st_pend[b];
-        nd += st_done[b];
+      st_emit[b] = emitted;
+      np += st_pend[b];
+      nd += st_done[b];
+      if (cta == 0) {  // keys of iteration iter + 2 (all CTAs last read them in iteration iter - 1)
+        tok_key[((iter + 2) % 3) * B + b] = 0ull;
+        dur_key[((iter + 2) % 3) * B + b] = 0ull;
       }
-      if (iter + 1 >= a.max_iters && nd < B) {
-        if (cta == 0) report_error(a.err, DEV_ERR_BAD_SHAPE);
-        nd = B;  // stop
-      }
-      s_pending = np;
-      s_done = nd;
     }
+    if (np) atomicAdd(&s_np, np);
+    if (nd) atomicAdd(&s_nd, nd);
     __syncthreads();
-    if (s_done >= B) return;
+    n_pending = s_np;
+    bool stop = s_nd >= B;
+    if (!stop && iter + 1 >= a.max_iters) {
+      if (cta == 0 && threadIdx.x == 0) report_error(a.err, DEV_ERR_BAD_SHAPE);
+      stop = true;
+    }
+    if (stop) break;
   }
+  // confidences of the final iteration's tokens (no later iteration overwrites them)
+  if (warp == 1) merge_confs(iter);
+  drain();  // a streamed layer copy may still be in flight
 }
 
 }  // namespace
 
-size_t transducer_smem_bytes(int H, int J, int B) {
-  return (size_t)TD_CHUNK * std::max(2 * H, J) * sizeof(float) + (size_t)7 * B * sizeof(int);
+size_t transducer_smem_bytes(int H, int J, int L, int VP, int grid, int B) {
+  return td_layout_for(H, J, L, VP, grid, B).bytes;
 }
-size_t transducer_partial_bytes(int grid, int B) { return (size_t)2 * grid * B * sizeof(Partial); }
+size_t transducer_smem_limit() { return TD_SMEM_LIMIT; }
+int transducer_max_batch(int H, int J, int L, int VP, int grid) {
+  const size_t fixed = transducer_smem_bytes(H, J, L, VP, grid, 0);
+  return fixed >= TD_SMEM_LIMIT ? 0 : (int)((TD_SMEM_LIMIT - fixed) / (TD_STATE_INTS * sizeof(int)));
+}
+size_t transducer_key_bytes(int B) { return (size_t)6 * B * sizeof(unsigned long long); }
+size_t transducer_partial_bytes(int grid, int B) {
+  return transducer_key_bytes(B) + (size_t)2 * grid * B * sizeof(float2);
+}
 
 cudaError_t transducer_greedy_launch(const TransducerArgs& a, int grid, cudaStream_t st) {
   if (a.B <= 0) return cudaSuccess;
-  if (a.H % 4 || a.J % 4 || a.H > TD_KV * 128 || a.J > TD_KV * 128 || a.L < 1 || grid < 1 || a.B > 4096)
+  const int VP = a.V1 + a.D;
+  if (a.H < 4 || a.J < 4 || a.H % 4 || a.J % 4 || a.L < 1 || grid < 1 || a.D < 0 || a.D > TD_MAX_DUR || a.V1 < 2)
     return cudaErrorInvalidValue;
-  const size_t smem = transducer_smem_bytes(a.H, a.J, a.B);
-  cudaError_t e = cudaFuncSetAttribute(k_transducer_greedy, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  // bulk copies: 16-byte aligned sources and destinations
+  auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
+  if (!al16(a.embed) || !al16(a.w_ih) || !al16(a.w_hh) || !al16(a.w_pred) || !al16(a.w_out) || !al16(a.zeros) ||
+      !al16(a.enc_proj) || a.ld_enc % 4 || !al16(a.h) || !al16(a.pred_proj) || !al16(a.keys))
+    return cudaErrorInvalidValue;
+  const TdLayout lay = td_layout_for(a.H, a.J, a.L, VP, grid, a.B);
+  if (lay.bytes > TD_SMEM_LIMIT) return cudaErrorInvalidValue;
+  cudaError_t e =
+      cudaFuncSetAttribute(k_transducer_greedy, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lay.bytes);
   if (e != cudaSuccess) return e;
   TransducerArgs ka = a;
+  ka.held = lay.held;
   void* params[] = {&ka};
   return cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(&k_transducer_greedy), dim3(grid),
-                                     dim3(TD_THREADS), params, smem, st);
+                                     dim3(TD_THREADS), params, lay.bytes, st);
 }
 
 // One CTA per SM: the cooperative launch guarantees they are all resident,
