@@ -820,7 +820,7 @@ pkc_status DeviceRunner::transducer_pcm_host(const std::vector<const float*>& pc
     a.max_iters = maxv * (MS + 1) + 4;
     a.embed = w_.dec_embed; a.w_ih = w_.dec_w_ih; a.w_hh = w_.dec_w_hh; a.b_lstm = w_.dec_b;
     a.w_pred = w_.dec_w_pred; a.b_pred = w_.dec_b_pred; a.w_out = w_.dec_w_out; a.b_out = w_.dec_b_out;
-    a.durations = w_.dec_durations; a.zeros = w_.dec_zeros;
+    a.durations = w_.dec_durations; a.zeros = w_.dec_zeros; a.gate0 = w_.dec_gate0;
     a.enc_proj = reinterpret_cast<const float*>(ws + o_ep); a.ld_enc = Jp;
     a.item_off = d_st + 8 * B + b0; a.item_len = d_st + 9 * B + b0;
     a.h = reinterpret_cast<float*>(ws + o_h); a.c = reinterpret_cast<float*>(ws + o_c);

@@ -151,7 +151,8 @@ struct TransducerArgs {
   const float* w_out;      // [V1 + D, J]
   const float* b_out;      // [V1 + D]
   const int* durations;    // [D]
-  const float* zeros;      // [H] zeros (the SOS input)
+  const float* zeros;      // [H] zeros
+  const float* gate0;      // [V1 + 1, 4H] layer-0 input gates (transducer_gate0_launch)
   // encoder projection, frames of all utterances: [M, ld_enc] (first J columns)
   const float* enc_proj;
   int ld_enc;
@@ -174,6 +175,11 @@ struct TransducerArgs {
   int* err;
   int held;                // set by the launcher (LSTM layers resident in shared memory)
 };
+// Layer-0 input gates of every token, computed once at load:
+// out[v] = W_ih0 embed[v] + b0 for v < V1 and out[V1] = b0 (the SOS step's zero
+// input). f32 throughout.
+cudaError_t transducer_gate0_launch(const float* embed, const float* w_ih0, const float* b0, int V1, int H,
+                                    float* out, cudaStream_t st);
 size_t transducer_smem_bytes(int H, int J, int L, int VP, int grid, int B);
 size_t transducer_smem_limit();
 int transducer_max_batch(int H, int J, int L, int VP, int grid);

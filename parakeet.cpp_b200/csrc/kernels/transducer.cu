@@ -21,6 +21,9 @@
 //   D  every CTA reads the two keys of each utterance and applies the
 //      reference's state machine to its own shared-memory copy of the state
 //      (all CTAs decide identically); CTA 0 appends the tokens
+// Layer 0's input part W_ih0 embed[token] + b0 is a table over the vocabulary
+// computed at load (transducer_gate0_launch), so layer 0 contracts only
+// W_hh0 h; deeper layers contract [W_ih | W_hh] [x | h].
 // Each CTA owns a contiguous slice of hidden units (all four gate rows of a
 // unit, so the cell update is local), of pred rows and of joint rows. Those
 // weight rows are copied into its shared memory once, by bulk copies, and stay
@@ -36,6 +39,7 @@
 // kernel records DEV_ERR_TIMEOUT_DECODE and every CTA leaves.
 // All arithmetic is f32 on f32 weights (the decoder weights are f32 in GGUF).
 #include <algorithm>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -57,7 +61,8 @@ struct TdLayout {
   int ldk;         // sX row stride: max(2H, 2J) + 4
   int nu, nj, nv;  // most hidden units / pred rows / joint rows any CTA owns
   int held;        // LSTM layers resident at once (L, or 1 when all do not fit)
-  int o_x, o_wl, o_wp, o_wj, o_bl, o_bp, o_bj, o_r, o_z, o_c, o_st;
+  int o_x, o_wl, o_wp, o_wj, o_bl, o_bp, o_bj, o_r, o_z, o_c, o_e, o_st;
+  int wl_l0, wl_l;  // floats of the layer-0 slot ([4 nu][H]) and of a deeper layer's ([4 nu][2H])
   size_t bytes;
 };
 
@@ -76,8 +81,11 @@ __host__ __device__ inline TdLayout td_layout(int H, int J, int L, int VP, int G
     o += (n + 3) & ~3;
     return r;
   };
+  t.wl_l0 = 4 * t.nu * H;
+  t.wl_l = 4 * t.nu * 2 * H;
   t.o_x = take(TD_CB * t.ldk);
-  t.o_wl = take(held * 4 * t.nu * 2 * H);
+  // held == L: layer 0, then layers 1.. in turn; held == 1: one slot of the larger size
+  t.o_wl = take(held == L ? t.wl_l0 + (L - 1) * t.wl_l : (L > 1 ? t.wl_l : t.wl_l0));
   t.o_wp = take(t.nj * H);
   t.o_wj = take(t.nv * J);
   t.o_bl = take(L * 4 * t.nu);
@@ -86,6 +94,7 @@ __host__ __device__ inline TdLayout td_layout(int H, int J, int L, int VP, int G
   t.o_r = take(TD_WARPS * TD_RG * TD_CB);
   t.o_z = take(TD_RG * TD_CB);
   t.o_c = take(t.nu * TD_CB);
+  t.o_e = take(t.nu * TD_CB * 4);
   t.o_st = take(TD_STATE_INTS * B);
   t.bytes = (size_t)o * sizeof(float);
   return t;
@@ -138,13 +147,14 @@ __device__ __forceinline__ bool cta_wait(uint32_t bar, uint32_t& parity, bool& o
 
 // ---------------------------------------------------------------- grid barrier
 // Barrier k of the launch completes when the arrival counter (zeroed by the
-// host before the launch) reaches k * gridDim.x.
+// host before the launch) reaches k * gridDim.x. The CTA's writes are ordered
+// before the release-add by the CTA barrier, and the acquire-load orders the
+// reads after it.
 __device__ __forceinline__ bool grid_sync(unsigned int* count, unsigned int& target, int* err, int* smem_ok) {
   target += gridDim.x;
   __syncthreads();
   if (threadIdx.x == 0) {
     bool ok = true;
-    __threadfence();
     asm volatile("red.release.gpu.global.add.u32 [%0], 1;" ::"l"(count) : "memory");
     const unsigned long long t0 = globaltimer_ns();
     for (uint32_t it = 0;; ++it) {
@@ -158,7 +168,6 @@ __device__ __forceinline__ bool grid_sync(unsigned int* count, unsigned int& tar
       }
       if (it > 4096u) __nanosleep(128);  // spin first: phases are a few microseconds
     }
-    __threadfence();
     *smem_ok = ok ? 1 : 0;
   }
   __syncthreads();
@@ -213,6 +222,31 @@ __device__ __forceinline__ void cta_gemv(const float* W, int ldw, int nr, const 
   __syncthreads();
 }
 
+// Confidence of one stored token from the per-CTA (max, sum of exp) partials
+// of its iteration (one warp): max_prob over the token part,
+// (N p_max - 1) / (N - 1) with N = V + 1 and p_max = 1 / (sum of exp(l - max)).
+__device__ __noinline__ void merge_conf(const float2* parts, int G, int B, int b, int V1, int* out) {
+  const int lane = threadIdx.x & 31;
+  float m = -INFINITY, s = 0.f;
+  for (int c = lane; c < G; c += 32) {
+    const float2 q = __ldcg(parts + (size_t)c * B + b);
+    if (q.x > m) {
+      s = (m == -INFINITY ? 0.f : s * __expf(m - q.x)) + q.y;
+      m = q.x;
+    } else if (q.x != -INFINITY) {
+      s += q.y * __expf(q.x - m);
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float om = __shfl_xor_sync(0xffffffffu, m, o), os = __shfl_xor_sync(0xffffffffu, s, o);
+    const float nm = fmaxf(m, om);
+    s = (m == -INFINITY ? 0.f : s * __expf(m - nm)) + (om == -INFINITY ? 0.f : os * __expf(om - nm));
+    m = nm;
+  }
+  if (lane == 0) *out = __float_as_int(((float)V1 * (1.0f / s) - 1.0f) / ((float)V1 - 1.0f));
+}
+
 __global__ void __launch_bounds__(TD_THREADS, 1) k_transducer_greedy(TransducerArgs a) {
   extern __shared__ __align__(16) float sm[];
   __shared__ __align__(8) unsigned long long s_bar[2];  // 0: weights, 1: inputs
@@ -233,6 +267,7 @@ __global__ void __launch_bounds__(TD_THREADS, 1) k_transducer_greedy(TransducerA
   float* sR = sm + lay.o_r;
   float* sZ = sm + lay.o_z;
   float* sC = sm + lay.o_c;
+  float* sE = sm + lay.o_e;  // layer-0 input gates of the chunk [unit][item][gate]
   // per-utterance state (this CTA's copy) and constants
   int* st_t = reinterpret_cast<int*>(sm + lay.o_st);
   int* st_sym = st_t + B;
@@ -260,7 +295,11 @@ __global__ void __launch_bounds__(TD_THREADS, 1) k_transducer_greedy(TransducerA
   const int j0 = (int)((long long)J * cta / G), j1 = (int)((long long)J * (cta + 1) / G);
   const int v0 = (int)((long long)VP * cta / G), v1 = (int)((long long)VP * (cta + 1) / G);
   const int nu = u1 - u0, nj = j1 - j0, nv = v1 - v0;
-  const size_t wl_slot = (size_t)4 * lay.nu * 2 * H;  // floats per resident LSTM layer
+  // resident LSTM rows of layer l: layer 0 as [4 nu][H] (W_hh), deeper layers [4 nu][2H] ([W_ih | W_hh])
+  auto wl_of = [&](int l) -> float* {
+    if (a.held < L) return sWl;
+    return sWl + (l == 0 ? 0 : (size_t)lay.wl_l0 + (size_t)(l - 1) * lay.wl_l);
+  };
 
   if (threadIdx.x == 0) {
     mbar_init(bar_w, 1);
@@ -283,7 +322,7 @@ __global__ void __launch_bounds__(TD_THREADS, 1) k_transducer_greedy(TransducerA
     st_emit[b] = 0;
   }
   for (int i = threadIdx.x; i < a.D; i += TD_THREADS) s_dur[i] = a.durations[i];
-  for (int i = threadIdx.x; i < L * 4 * nu; i += TD_THREADS) {  // [l][unit][gate]
+  for (int i = threadIdx.x; i < L * 4 * nu; i += TD_THREADS) {  // [l][unit][gate] (layer 0's is in gate0)
     const int l = i / (4 * nu), r = i % (4 * nu);
     sBl[(l * lay.nu + (r >> 2)) * 4 + (r & 3)] = a.b_lstm[(size_t)l * 4 * H + (r & 3) * H + u0 + (r >> 2)];
   }
@@ -291,24 +330,31 @@ __global__ void __launch_bounds__(TD_THREADS, 1) k_transducer_greedy(TransducerA
   for (int i = threadIdx.x; i < nv; i += TD_THREADS) sBj[i] = a.b_out[v0 + i];
   __syncthreads();
 
-  // copies of LSTM layer l's rows into resident slot s (row 4 u + q = gate q of
-  // unit u0 + u: [W_ih row | W_hh row]); lanes of warp 0 split them
-  auto copy_lstm = [&](int l, int s) {
+  // copies of LSTM layer l's rows (row 4 u + q = gate q of unit u0 + u): layer
+  // 0 the W_hh rows, deeper layers [W_ih row | W_hh row]; lanes of warp 0 split them
+  auto lstm_bytes = [&](int l) { return (uint32_t)((l == 0 ? 4 : 8) * nu * H * 4); };
+  auto copy_lstm = [&](int l) {
     const float* wi = a.w_ih + (size_t)l * 4 * H * H;
     const float* wh = a.w_hh + (size_t)l * 4 * H * H;
-    float* dst = sWl + (size_t)s * wl_slot;
-    for (int c = lane; c < 8 * nu; c += 32) {
-      const int r = c >> 1, half = c & 1;
+    float* dst = wl_of(l);
+    const int parts = l == 0 ? 1 : 2;
+    for (int c = lane; c < 4 * nu * parts; c += 32) {
+      const int r = c / parts, half = parts == 1 ? 1 : c % parts;
       const size_t row = (size_t)((r & 3) * H + u0 + (r >> 2)) * H;
-      bulk_g2s(smem_u32(dst + (size_t)r * 2 * H + half * H), (half ? wh : wi) + row, (uint32_t)(H * 4), bar_w);
+      bulk_g2s(smem_u32(dst + (size_t)r * parts * H + (parts == 1 ? 0 : half * H)), (half ? wh : wi) + row,
+               (uint32_t)(H * 4), bar_w);
     }
   };
 
   // resident weights: LSTM layers [0, held), pred rows, joint rows
   if (warp == 0) {
-    if (lane == 0) mbar_expect_tx(bar_w, (uint32_t)((8 * nu * H * a.held + nj * H + nv * J) * 4));
+    if (lane == 0) {
+      uint32_t bytes = (uint32_t)((nj * H + nv * J) * 4);
+      for (int l = 0; l < a.held; ++l) bytes += lstm_bytes(l);
+      mbar_expect_tx(bar_w, bytes);
+    }
     __syncwarp();
-    for (int l = 0; l < a.held; ++l) copy_lstm(l, l);
+    for (int l = 0; l < a.held; ++l) copy_lstm(l);
     for (int r = lane; r < nj; r += 32)
       bulk_g2s(smem_u32(sWp + (size_t)r * H), a.w_pred + (size_t)(j0 + r) * H, (uint32_t)(H * 4), bar_w);
     for (int r = lane; r < nv; r += 32)
@@ -331,36 +377,10 @@ __global__ void __launch_bounds__(TD_THREADS, 1) k_transducer_greedy(TransducerA
     for (int i = 0; i < TD_CB && c0 + i < B; ++i) any |= flags[c0 + i] == want;
     return any;
   };
-  // confidence of the token utterance b stored in the last iteration, from
-  // that iteration's per-CTA partials (one warp)
-  auto merge_conf = [&](const float2* parts, int b) {
-    float m = -INFINITY, s = 0.f;
-    for (int c = lane; c < G; c += 32) {
-      const float2 q = __ldcg(parts + (size_t)c * B + b);
-      if (q.x > m) {
-        s = (m == -INFINITY ? 0.f : s * __expf(m - q.x)) + q.y;
-        m = q.x;
-      } else if (q.x != -INFINITY) {
-        s += q.y * __expf(q.x - m);
-      }
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-      const float om = __shfl_xor_sync(0xffffffffu, m, o), os = __shfl_xor_sync(0xffffffffu, s, o);
-      const float nm = fmaxf(m, om);
-      s = (m == -INFINITY ? 0.f : s * __expf(m - nm)) + (om == -INFINITY ? 0.f : os * __expf(om - nm));
-      m = nm;
-    }
-    if (lane == 0) {
-      // max_prob confidence over the token part: (N p_max - 1) / (N - 1), p_max = 1 / s
-      const float conf = ((float)V1 * (1.0f / s) - 1.0f) / ((float)V1 - 1.0f);
-      a.tokens[((size_t)st_toff[b] + st_ntok[b] - 1) * 4 + 2] = __float_as_int(conf);
-    }
-  };
   auto merge_confs = [&](int it) {
     const float2* pp = parts_all + (size_t)(it & 1) * G * B;
     for (int b = cta; b < B; b += G)
-      if (st_emit[b]) merge_conf(pp, b);
+      if (st_emit[b]) merge_conf(pp, G, B, b, V1, a.tokens + ((size_t)st_toff[b] + st_ntok[b] - 1) * 4 + 2);
   };
 
   int n_pending = 0;
@@ -371,41 +391,44 @@ __global__ void __launch_bounds__(TD_THREADS, 1) k_transducer_greedy(TransducerA
     if (n_pending > 0) {
       for (int l = 0; l < L; ++l) {
         if (stream_lstm && !cta_wait(bar_w, par_w, w_out, a.err)) return drain();  // this layer's rows
-        const float* wl = sWl + (stream_lstm ? 0 : (size_t)l * wl_slot);
+        const float* wl = wl_of(l);
+        const int K = l == 0 ? H : 2 * H;  // layer 0: h only (its input part is in gate0)
         for (int c0 = 0; c0 < B; c0 += TD_CB) {
           if (nu == 0 || !chunk_has(c0, st_pend, 1)) continue;  // uniform across the CTA
           __syncthreads();  // earlier readers of sX / sC are done
           if (warp == 0) {
-            // inputs [x | h] per pending utterance: x = embedding of the last
-            // token (zeros before the first one) for layer 0, the new output
-            // of the layer below otherwise; h = the committed state
+            // inputs per pending utterance: layer 0 [h], deeper layers [x | h]
+            // with x the new output of the layer below; h = the committed state
             fence_proxy_async_smem();
+            fence_proxy_async_global();
             const int i = lane & (TD_CB - 1), b = c0 + i;
             const float* src = nullptr;
-            if (b < B && st_pend[b]) {
+            if (b < B && st_pend[b] && (l > 0 || lane >= TD_CB)) {
               const int cur = st_cur[b];
-              if (lane < TD_CB)
-                src = l > 0        ? a.h + (((size_t)(1 - cur) * L + (l - 1)) * B + b) * H
-                      : st_have[b] ? a.embed + (size_t)st_last[b] * H
-                                   : a.zeros;
-              else
-                src = a.h + (((size_t)cur * L + l) * B + b) * H;
+              src = lane < TD_CB ? a.h + (((size_t)(1 - cur) * L + (l - 1)) * B + b) * H
+                                 : a.h + (((size_t)cur * L + l) * B + b) * H;
             }
-            warp_copy(bar_x, smem_u32(sX + i * ldk + (lane < TD_CB ? 0 : H)), src, (uint32_t)(H * 4));
+            warp_copy(bar_x, smem_u32(sX + i * ldk + (lane < TD_CB || l == 0 ? 0 : H)), src, (uint32_t)(H * 4));
           }
           x_out = true;
           for (int e = threadIdx.x; e < nu * TD_CB; e += TD_THREADS) {  // committed cells [unit][item]
             const int u = e / TD_CB, i = e % TD_CB, b = c0 + i;
-            sC[e] = (b < B && st_pend[b]) ? __ldcg(a.c + (((size_t)st_cur[b] * L + l) * B + b) * H + u0 + u) : 0.f;
+            const bool act = b < B && st_pend[b];
+            sC[e] = act ? __ldcg(a.c + (((size_t)st_cur[b] * L + l) * B + b) * H + u0 + u) : 0.f;
+            if (l == 0) {  // input gates of the last token (row V1: the SOS step)
+              const float* g = a.gate0 + (size_t)(act && st_have[b] ? st_last[b] : V1) * 4 * H + u0 + u;
+#pragma unroll
+              for (int q = 0; q < 4; ++q) sE[e * 4 + q] = __ldg(g + (size_t)q * H);
+            }
           }
           if (!cta_wait(bar_x, par_x, x_out, a.err)) return drain();
           for (int ug = 0; ug < nu; ug += 2) {
-            cta_gemv(wl + (size_t)ug * 4 * 2 * H, 2 * H, min(TD_RG, 4 * (nu - ug)), sX, ldk, 2 * H, sR, sZ);
+            cta_gemv(wl + (size_t)ug * 4 * K, K, min(TD_RG, 4 * (nu - ug)), sX, ldk, K, sR, sZ);
             if (threadIdx.x < 2 * TD_CB) {
               const int uu = threadIdx.x / TD_CB, i = threadIdx.x % TD_CB, b = c0 + i, u = ug + uu;
               if (u < nu && b < B && st_pend[b]) {
                 const int cur = st_cur[b];
-                const float* bl = sBl + (l * lay.nu + u) * 4;
+                const float* bl = l == 0 ? sE + (u * TD_CB + i) * 4 : sBl + (l * lay.nu + u) * 4;
                 const float zi = sZ[(uu * 4 + 0) * TD_CB + i] + bl[0];
                 const float zf = sZ[(uu * 4 + 1) * TD_CB + i] + bl[1];
                 const float zg = sZ[(uu * 4 + 2) * TD_CB + i] + bl[2];
@@ -414,18 +437,18 @@ __global__ void __launch_bounds__(TD_THREADS, 1) k_transducer_greedy(TransducerA
                 const size_t o = (((size_t)(1 - cur) * L + l) * B + b) * H + u0 + u;
                 a.c[o] = cn;
                 a.h[o] = sigm(zo) * tanhf(cn);
-                fence_proxy_async_global();  // read by the next phases' bulk copies
               }
             }
           }
         }
+        if (threadIdx.x < 2 * TD_CB) fence_proxy_async_global();  // h is read by bulk copies next
         if (stream_lstm) {  // the slot is free: copy the next layer (of this step or the next)
           __syncthreads();
           if (warp == 0) {
             fence_proxy_async_smem();
-            if (lane == 0) mbar_expect_tx(bar_w, (uint32_t)(8 * nu * H * 4));
+            if (lane == 0) mbar_expect_tx(bar_w, lstm_bytes((l + 1) % L));
             __syncwarp();
-            copy_lstm((l + 1) % L, 0);
+            copy_lstm((l + 1) % L);
             __syncwarp();
             if (lane == 0) mbar_arrive(bar_w);
           }
@@ -439,6 +462,7 @@ __global__ void __launch_bounds__(TD_THREADS, 1) k_transducer_greedy(TransducerA
         __syncthreads();
         if (warp == 0) {
           fence_proxy_async_smem();
+          fence_proxy_async_global();
           const int b = c0 + lane;
           const float* src = (lane < TD_CB && b < B && st_pend[b])
                                  ? a.h + (((size_t)(1 - st_cur[b]) * L + (L - 1)) * B + b) * H
@@ -452,13 +476,11 @@ __global__ void __launch_bounds__(TD_THREADS, 1) k_transducer_greedy(TransducerA
           cta_gemv(sWp + (size_t)r0 * H, H, nr, sX, ldk, H, sR, sZ);
           if (threadIdx.x < TD_RG * TD_CB) {
             const int r = threadIdx.x / TD_CB, i = threadIdx.x % TD_CB, b = c0 + i;
-            if (r < nr && b < B && st_pend[b]) {
-              a.pred_proj[(size_t)b * J + j0 + r0 + r] = sZ[threadIdx.x] + sBp[r0 + r];
-              fence_proxy_async_global();
-            }
+            if (r < nr && b < B && st_pend[b]) a.pred_proj[(size_t)b * J + j0 + r0 + r] = sZ[threadIdx.x] + sBp[r0 + r];
           }
         }
       }
+      if (threadIdx.x < TD_RG * TD_CB) fence_proxy_async_global();  // pred_proj is read by bulk copies next
       if (!grid_sync(a.bar_count, bar_target, a.err, &s_ok)) return drain();
     }
 
@@ -471,6 +493,7 @@ __global__ void __launch_bounds__(TD_THREADS, 1) k_transducer_greedy(TransducerA
       __syncthreads();
       if (warp == 0) {  // [enc_proj row of the utterance's frame | pred_proj]
         fence_proxy_async_smem();
+        fence_proxy_async_global();
         const int i = lane & (TD_CB - 1), b = c0 + i;
         const float* src = nullptr;
         if (b < B && !st_done[b])
@@ -613,7 +636,59 @@ __global__ void __launch_bounds__(TD_THREADS, 1) k_transducer_greedy(TransducerA
   drain();  // a streamed layer copy may still be in flight
 }
 
+// out[v][r] = sum_k embed[v][k] w[r][k] + b[r] (v < V1), out[V1][r] = b[r]:
+// 64 x 64 output tiles, 16-deep k slabs in shared memory, 4 x 4 per thread.
+__global__ void __launch_bounds__(256) k_gate0(const float* __restrict__ embed, const float* __restrict__ w,
+                                               const float* __restrict__ b, int V1, int N, int K,
+                                               float* __restrict__ out) {
+  __shared__ float sa[16][64 + 4], sb[16][64 + 4];  // [k][row] of embed / w
+  const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+  const int r0 = blockIdx.x * 64, v0 = blockIdx.y * 64;
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < K; k0 += 16) {
+    for (int e = threadIdx.x; e < 64 * 16; e += 256) {
+      const int row = e / 16, k = e % 16;
+      const int v = v0 + row, r = r0 + row, kk = k0 + k;
+      sa[k][row] = (v < V1 && kk < K) ? embed[(size_t)v * K + kk] : 0.f;
+      sb[k][row] = (r < N && kk < K) ? w[(size_t)r * K + kk] : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+      float av[4], bv[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        av[j] = sa[k][ty * 4 + j];
+        bv[j] = sb[k][tx * 4 + j];
+      }
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int v = v0 + ty * 4 + i;
+    if (v > V1) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int r = r0 + tx * 4 + j;
+      if (r < N) out[(size_t)v * N + r] = (v < V1 ? acc[i][j] : 0.f) + b[r];
+    }
+  }
+}
+
 }  // namespace
+
+cudaError_t transducer_gate0_launch(const float* embed, const float* w_ih0, const float* b0, int V1, int H,
+                                    float* out, cudaStream_t st) {
+  if (V1 < 1 || H < 1) return cudaErrorInvalidValue;
+  const int N = 4 * H;
+  k_gate0<<<dim3((N + 63) / 64, (V1 + 1 + 63) / 64), 256, 0, st>>>(embed, w_ih0, b0, V1, N, H, out);
+  return cudaGetLastError();
+}
 
 size_t transducer_smem_bytes(int H, int J, int L, int VP, int grid, int B) {
   return td_layout_for(H, J, L, VP, grid, B).bytes;
@@ -635,10 +710,12 @@ cudaError_t transducer_greedy_launch(const TransducerArgs& a, int grid, cudaStre
     return cudaErrorInvalidValue;
   // bulk copies: 16-byte aligned sources and destinations
   auto al16 = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; };
-  if (!al16(a.embed) || !al16(a.w_ih) || !al16(a.w_hh) || !al16(a.w_pred) || !al16(a.w_out) || !al16(a.zeros) ||
+  if (!a.gate0 || !al16(a.w_ih) || !al16(a.w_hh) || !al16(a.w_pred) || !al16(a.w_out) ||
       !al16(a.enc_proj) || a.ld_enc % 4 || !al16(a.h) || !al16(a.pred_proj) || !al16(a.keys))
     return cudaErrorInvalidValue;
-  const TdLayout lay = td_layout_for(a.H, a.J, a.L, VP, grid, a.B);
+  TdLayout lay = td_layout_for(a.H, a.J, a.L, VP, grid, a.B);
+  if (const char* e = std::getenv("PKC_DECODE_STREAM"))  // one resident LSTM layer (the streamed path)
+    if (std::atoi(e) == 1 && a.L > 1) lay = td_layout(a.H, a.J, a.L, VP, grid, a.B, 1);
   if (lay.bytes > TD_SMEM_LIMIT) return cudaErrorInvalidValue;
   cudaError_t e =
       cudaFuncSetAttribute(k_transducer_greedy, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lay.bytes);

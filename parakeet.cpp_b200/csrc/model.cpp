@@ -27,6 +27,7 @@
 #include <thread>
 
 #include "half.hpp"
+#include "kernels/kernels.h"
 
 namespace pkc {
 
@@ -659,6 +660,7 @@ std::string upload_weights(const GgufFile& g, const Config& c, DeviceWeights& w,
     if (du.empty()) du.push_back(0);
     w.dec_durations = as_off<int>(st.add(du.data(), du.size() * 4));
     w.dec_zeros = put_f(std::vector<float>((size_t)Hp, 0.f));
+    w.dec_gate0 = as_off<float>(st.add(nullptr, (size_t)(V1 + 1) * 4 * Hp * 4));  // filled on the device
     // encoder projection: split f16 rows [W_hi | W_lo | W_hi], padded to 256
     if (!read_f32(g, "joint.enc.weight", J, d, t1, err) || !read_vec(g, "joint.enc.bias", J, t2, err)) return err;
     const int Jp = (J + 255) / 256 * 256;
@@ -702,6 +704,14 @@ std::string upload_weights(const GgufFile& g, const Config& c, DeviceWeights& w,
     reloc(w.dec_embed, base); reloc(w.dec_w_ih, base); reloc(w.dec_w_hh, base); reloc(w.dec_b, base);
     reloc(w.dec_w_pred, base); reloc(w.dec_b_pred, base); reloc(w.dec_w_out, base); reloc(w.dec_b_out, base);
     reloc(w.dec_durations, base); reloc(w.dec_zeros, base); reloc(w.dec_w_enc, base); reloc(w.dec_b_enc, base);
+    reloc(w.dec_gate0, base);
+    const int V1 = c.vocab_size + 1, Hp = c.pred_hidden;
+    if (transducer_gate0_launch(w.dec_embed, w.dec_w_ih, w.dec_b, V1, Hp, w.dec_gate0, nullptr) != cudaSuccess ||
+        cudaDeviceSynchronize() != cudaSuccess) {
+      cudaFree(dev);
+      w.arena = nullptr;
+      return "decoder gate table computation failed";
+    }
   }
   auto reloc_q = [&](QWeight& qw) {
     if (!qw.type) return;

@@ -113,6 +113,7 @@ struct DeviceWeights {
   float* dec_b_out = nullptr;     // [V1 + D]
   int* dec_durations = nullptr;   // [D]
   float* dec_zeros = nullptr;     // [H]
+  float* dec_gate0 = nullptr;     // [V1 + 1, 4H] layer-0 input gates W_ih0 embed[v] + b0 (row V1: SOS, b0 only)
   // joint encoder projection as a split-f16 GEMM operand [W_hi | W_lo | W_hi],
   // rows padded to dec_jpad (a multiple of 256), and its bias
   void* dec_w_enc = nullptr;      // f16 [dec_jpad, 3d]

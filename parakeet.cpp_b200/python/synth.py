@@ -41,6 +41,7 @@ class ModelCfg:
     vocab: int = 1024
     pred_hidden: int = 640
     joint_hidden: int = 640
+    pred_layers: int = 1
     durations: tuple = ()
     dtype: str = "f32"          # f32 | f16 | bf16 | q8_0 | q4_k
     biases: bool = False
@@ -51,7 +52,10 @@ class ModelCfg:
     seed: int = 1234
 
     def key(self) -> str:
-        h = hashlib.sha1(repr(sorted(asdict(self).items())).encode()).hexdigest()[:12]
+        items = asdict(self)
+        if items["pred_layers"] == 1:  # keeps the names of files made before the field existed
+            del items["pred_layers"]
+        h = hashlib.sha1(repr(sorted(items.items())).encode()).hexdigest()[:12]
         return f"{self.name}_{self.dtype}_{h}"
 
 
@@ -237,10 +241,11 @@ def model_tensors(cfg: ModelCfg):
     if cfg.arch != "ctc":
         Hp = cfg.pred_hidden
         yield "decoder.prediction.embed.weight", nrm(V1, Hp)
-        yield "decoder.prediction.dec_rnn.lstm.weight_ih_l0", nrm(4 * Hp, Hp)
-        yield "decoder.prediction.dec_rnn.lstm.weight_hh_l0", nrm(4 * Hp, Hp)
-        yield "decoder.prediction.dec_rnn.lstm.bias_ih_l0", nrm(4 * Hp)
-        yield "decoder.prediction.dec_rnn.lstm.bias_hh_l0", nrm(4 * Hp)
+        for l in range(cfg.pred_layers):
+            yield f"decoder.prediction.dec_rnn.lstm.weight_ih_l{l}", nrm(4 * Hp, Hp)
+            yield f"decoder.prediction.dec_rnn.lstm.weight_hh_l{l}", nrm(4 * Hp, Hp)
+            yield f"decoder.prediction.dec_rnn.lstm.bias_ih_l{l}", nrm(4 * Hp)
+            yield f"decoder.prediction.dec_rnn.lstm.bias_hh_l{l}", nrm(4 * Hp)
         J = cfg.joint_hidden
         yield "joint.enc.weight", nrm(J, d)
         yield "joint.enc.bias", nrm(J)
@@ -280,7 +285,7 @@ def write_gguf(cfg: ModelCfg, path: str) -> str:
     w.add_array("parakeet.tokenizer.pieces", [f"▁t{i}" for i in range(cfg.vocab)])
     if cfg.arch != "ctc":
         w.add_uint32("parakeet.decoder.pred_hidden", cfg.pred_hidden)
-        w.add_uint32("parakeet.decoder.pred_rnn_layers", 1)
+        w.add_uint32("parakeet.decoder.pred_rnn_layers", cfg.pred_layers)
         w.add_uint32("parakeet.joint.joint_hidden", cfg.joint_hidden)
         w.add_string("parakeet.joint.activation", "relu")
         w.add_uint32("parakeet.decoding.max_symbols", 10)

@@ -34,6 +34,8 @@ def models(tmp_path_factory):
         "q4_k": synth.small_cfg("c4_1.1b_q4k", n_mels=128, **small),
         "dk128": synth.small_cfg("c2_0.6b_f16", n_layers=2, d_model=512, n_heads=4, ff_dim=1024,
                                  vocab=64, pred_hidden=64, joint_hidden=64),
+        "tdt2": synth.small_cfg("c2_0.6b_f16", n_layers=2, d_model=256, n_heads=4, ff_dim=1024, n_mels=80,
+                                vocab=64, pred_hidden=128, joint_hidden=96, pred_layers=2),
     }
     return {k: synth.ensure_gguf(c, d) for k, c in cfgs.items()}
 
@@ -322,6 +324,40 @@ def test_transducer_greedy_matches_oracle(models, oracles, kind):
         for t, u in zip(tk, want):
             assert abs(t[2] - u[2]) < 1e-4
     assert compared >= 2
+
+
+@pytest.mark.parametrize("variant", ["resident", "streamed", "groups"])
+def test_transducer_two_layer_paths(models, oracles, monkeypatch, variant):
+    """Two-layer prediction LSTM (H = 128, J = 96) through the decode kernel's
+    three schedules: every layer resident in shared memory; one resident layer
+    with the next one streamed in during the grid barrier
+    (PKC_DECODE_STREAM=1); the batch decoded in groups of 2 utterances, one
+    launch each (PKC_DECODE_GROUP=2). Tokens identical to the f64 oracle."""
+    import oracle
+    import pkc
+    if variant == "streamed":
+        monkeypatch.setenv("PKC_DECODE_STREAM", "1")
+    if variant == "groups":
+        monkeypatch.setenv("PKC_DECODE_GROUP", "2")
+    tr = oracle.Transducer(oracles("tdt2"))
+    assert tr.L == 2
+    m = pkc.Model(models["tdt2"])
+    try:
+        pcm = clips([SR * 2 + 111, SR + 5, 7000, SR * 3, 3300, SR // 2 + 13], seed=57)
+        toks = m.transducer_greedy_pcm_batch(pcm)
+        xs = m.encode_pcm_batch(pcm, layout=pkc.LAYOUT_TIME_MAJOR)
+    finally:
+        m.close()
+    compared = 0
+    for tk, x in zip(toks, xs):
+        want, gap = oracle.transducer_greedy(tr, x)
+        if gap < 1e-5:
+            continue
+        compared += 1
+        assert [(t[0], t[1], t[3]) for t in tk] == [(t[0], t[1], t[3]) for t in want]
+        for t, u in zip(tk, want):
+            assert abs(t[2] - u[2]) < 1e-4
+    assert compared >= 3
 
 
 def test_transducer_absent_is_unsupported(models):
