@@ -173,7 +173,12 @@ def run_ours(args, rank, world, local_rank):
     n = [len(p) for p in pcm]
     audio_s = sum(n) / SR
 
+    t_open = time.perf_counter()
     model = pkc.Model(path, devices=(local_rank,))
+    load = {k: (round(v, 3) if isinstance(v, float) else v) for k, v in model.load_stats().items()}
+    load["open_s"] = round(time.perf_counter() - t_open, 3)
+    load["api"] = ("pkc_model_open: host re-pack once (or the PKC_PACK_CACHE pre-pack file), "
+                   "page-locked image, concurrent per-device upload")
     d = model.info.d_model
     out_floats = lib_out_floats = int(sum(model.encoder_frames(model.mel_frames(x)) for x in n) * d)
     flat = np.concatenate(pcm).astype(np.float32)
@@ -351,6 +356,7 @@ def run_ours(args, rank, world, local_rank):
         "kernels": kernels,
         "clocks": clk.summary(),
     }
+    line["load"] = load
     if ctc is not None:
         line["ctc"] = ctc
     if trd is not None:

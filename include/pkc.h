@@ -79,9 +79,25 @@ const char* pkc_last_error(const pkc_model* m);
 
 /* Load a parakeet GGUF and upload the encoder weights to each listed CUDA
    device (devices == NULL or n_devices == 0: device 0). Weights are re-packed
-   once at load into the kernels' layouts. */
+   once on the host into the kernels' layouts, page-locked, and copied to all
+   listed devices concurrently (one host thread per device).
+   Pre-pack cache: when the environment variable PKC_PACK_CACHE names a
+   directory, the packed image is read from there if a file for this GGUF
+   (path, size, modification time) and these packing options exists, else it
+   is written there after packing; a damaged or stale file is ignored. */
 pkc_status pkc_model_open(const char* gguf_path, const int* devices, int n_devices,
                           pkc_model** out);
+
+/* Timing of the last pkc_model_open of m: host seconds spent re-packing (or
+   reading the pre-pack cache), seconds of the slowest device's upload, and
+   whether the image came from the cache (1) or was packed (0). */
+pkc_status pkc_model_load_stats(const pkc_model* m, double* pack_seconds, double* upload_seconds,
+                                int* from_cache);
+
+/* Host only (no CUDA call): make sure the pre-pack cache directory holds the
+   packed image of gguf_path for the current packing options, packing it if
+   needed. Writes the cache file's path to path_out (path_cap bytes) if given. */
+pkc_status pkc_pack_cache_build(const char* gguf_path, const char* cache_dir, char* path_out, int path_cap);
 
 /* Release the model and all device memory it holds. Safe on NULL. */
 void pkc_model_close(pkc_model* m);

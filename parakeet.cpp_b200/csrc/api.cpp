@@ -1,6 +1,7 @@
 // The model-level C ABI (include/pkc.h): open/close, mel front end, encoder,
 // multi-GPU sharding and profiling. No exception crosses this boundary.
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <cmath>
 #include <memory>
@@ -19,6 +20,8 @@ struct pkc_model {
   std::vector<std::unique_ptr<pkc::DeviceRunner>> runners;
   std::mutex mu;
   std::string last_error;
+  double pack_s = 0, upload_s = 0;  // load: re-pack (or pack-cache read), slowest device's upload
+  int from_cache = 0;
 };
 
 namespace pkc {
@@ -74,18 +77,98 @@ pkc_status pkc_model_open(const char* gguf_path, const int* devices, int n_devic
     int count = 0;
     if (cudaGetDeviceCount(&count) != cudaSuccess || count == 0)
       return pkc::set_thread_error(PKC_ERR_CUDA, "no CUDA device available");
-    for (int dv : devs) {
+    for (int dv : devs)
       if (dv < 0 || dv >= count)
         return pkc::set_thread_error(PKC_ERR_ARG, "device index " + std::to_string(dv) + " out of range");
-      auto r = std::make_unique<pkc::DeviceRunner>(m->cfg, dv);
-      err = r->init(*g);
-      if (!err.empty()) {
-        const bool oom = err.find("cudaMalloc") != std::string::npos;
-        return pkc::set_thread_error(oom ? PKC_ERR_OOM : (err.find("tensor") != std::string::npos ? PKC_ERR_FORMAT : PKC_ERR_CUDA), err);
-      }
-      m->runners.push_back(std::move(r));
+    // one host image for every device: from the pre-pack cache when it holds
+    // this GGUF (PKC_PACK_CACHE=<dir>), else re-packed here (and stored there)
+    const bool fold = pkc::DeviceRunner::ln_fused(m->cfg);
+    pkc::PackedWeights pw;
+    const char* cache_dir = getenv("PKC_PACK_CACHE");
+    std::string cache_path;
+    uint64_t key = 0;
+    if (cache_dir && cache_dir[0]) {
+      key = pkc::pack_cache_key(gguf_path, m->cfg, fold);
+      cache_path = pkc::pack_cache_path(cache_dir, key);
+      if (!pkc::pack_cache_load(cache_path, key, m->cfg, pw).empty()) pw = pkc::PackedWeights{};
     }
+    if (!pw.from_cache) {
+      err = pkc::pack_weights(*g, m->cfg, fold, pw);
+      if (!err.empty())
+        return pkc::set_thread_error(err.find("tensor") != std::string::npos ? PKC_ERR_FORMAT : PKC_ERR_UNSUPPORTED, err);
+    }
+    const bool store = !pw.from_cache && !cache_path.empty();
+    m->pack_s = pw.pack_s;
+    m->from_cache = pw.from_cache ? 1 : 0;
+    // page-locked source: every device's copy runs at DMA rate, concurrently
+    const bool pinned = cudaHostRegister(pw.bytes.data(), pw.bytes.size(), cudaHostRegisterPortable) == cudaSuccess;
+    if (!pinned) cudaGetLastError();
+    std::vector<std::unique_ptr<pkc::DeviceRunner>> rs(devs.size());
+    std::vector<std::string> errs(devs.size());
+    {
+      std::vector<std::thread> th;
+      for (size_t k = 0; k < devs.size(); ++k)
+        th.emplace_back([&, k] {
+          try {
+            rs[k] = std::make_unique<pkc::DeviceRunner>(m->cfg, devs[k]);
+            errs[k] = rs[k]->init(pw);
+          } catch (const std::exception& e) {
+            errs[k] = std::string("device init: ") + e.what();
+          }
+        });
+      if (store) pkc::pack_cache_store(cache_path, key, pw);  // best effort, while the devices upload
+      for (auto& t : th) t.join();
+    }
+    if (pinned) cudaHostUnregister(pw.bytes.data());
+    for (size_t k = 0; k < devs.size(); ++k) {
+      if (!errs[k].empty()) {
+        const bool oom = errs[k].find("cudaMalloc") != std::string::npos;
+        return pkc::set_thread_error(oom ? PKC_ERR_OOM : PKC_ERR_CUDA, "device " + std::to_string(devs[k]) + ": " + errs[k]);
+      }
+      m->upload_s = std::max(m->upload_s, rs[k]->upload_seconds());
+    }
+    m->runners = std::move(rs);
     *out = m.release();
+    return PKC_OK;
+  } catch (const std::bad_alloc&) {
+    return pkc::set_thread_error(PKC_ERR_OOM, "host allocation failed");
+  } catch (const std::exception& e) {
+    return pkc::set_thread_error(PKC_ERR_INTERNAL, e.what());
+  }
+}
+
+pkc_status pkc_model_load_stats(const pkc_model* m, double* pack_seconds, double* upload_seconds, int* from_cache) {
+  if (!m) return pkc::set_thread_error(PKC_ERR_ARG, "pkc_model_load_stats: model is NULL");
+  if (pack_seconds) *pack_seconds = m->pack_s;
+  if (upload_seconds) *upload_seconds = m->upload_s;
+  if (from_cache) *from_cache = m->from_cache;
+  return PKC_OK;
+}
+
+pkc_status pkc_pack_cache_build(const char* gguf_path, const char* cache_dir, char* path_out, int path_cap) {
+  if (!gguf_path || !cache_dir) return pkc::set_thread_error(PKC_ERR_ARG, "pkc_pack_cache_build: NULL argument");
+  try {
+    pkc::GgufFile g;
+    std::string err;
+    if (!g.open(gguf_path, err))
+      return pkc::set_thread_error(err.rfind("cannot open", 0) == 0 ? PKC_ERR_IO : PKC_ERR_FORMAT, err);
+    pkc::Config cfg;
+    err = pkc::read_config(g, cfg);
+    if (!err.empty()) return pkc::set_thread_error(PKC_ERR_UNSUPPORTED, err);
+    const bool fold = pkc::DeviceRunner::ln_fused(cfg);
+    const uint64_t key = pkc::pack_cache_key(gguf_path, cfg, fold);
+    const std::string path = pkc::pack_cache_path(cache_dir, key);
+    pkc::PackedWeights pw;
+    if (!pkc::pack_cache_load(path, key, cfg, pw).empty()) {
+      err = pkc::pack_weights(g, cfg, fold, pw);
+      if (!err.empty()) return pkc::set_thread_error(PKC_ERR_FORMAT, err);
+      err = pkc::pack_cache_store(path, key, pw);
+      if (!err.empty()) return pkc::set_thread_error(PKC_ERR_IO, err);
+    }
+    if (path_out && path_cap > 0) {
+      if ((int)path.size() >= path_cap) return pkc::set_thread_error(PKC_ERR_ARG, "pkc_pack_cache_build: path_cap too small");
+      std::memcpy(path_out, path.c_str(), path.size() + 1);
+    }
     return PKC_OK;
   } catch (const std::bad_alloc&) {
     return pkc::set_thread_error(PKC_ERR_OOM, "host allocation failed");

@@ -12,6 +12,7 @@
 
 #include <algorithm>
 #include <cmath>
+#include <chrono>
 #include <cstdlib>
 #include <cstring>
 
@@ -136,7 +137,18 @@ DeviceRunner::~DeviceRunner() {
   if (stream_) cudaStreamDestroy(stream_);
 }
 
-std::string DeviceRunner::init(const GgufFile& g) {
+// PKC_LN_FUSED=1: the QKV / pointwise-1 / FFN2-up GEMMs normalise their A
+// operand themselves (k_gemm_tc2ln). Off by default: the f32 rows it stages
+// through shared memory add ~80 KB of shared-memory traffic per CTA and
+// k-block to a mainloop that the plain GEMM already runs at the
+// shared-memory port's rate, so it is slower than the separate LayerNorm
+// kernel at the encoder's shapes.
+bool DeviceRunner::ln_fused(const Config& c) {
+  const char* lf = getenv("PKC_LN_FUSED");
+  return lf && lf[0] == '1' && c.d_model % 128 == 0;
+}
+
+std::string DeviceRunner::init(const PackedWeights& pw) {
   if (cudaSetDevice(device_) != cudaSuccess) return "cannot select CUDA device " + std::to_string(device_);
   cudaDeviceProp prop;
   if (cudaGetDeviceProperties(&prop, device_) != cudaSuccess) return "cudaGetDeviceProperties failed";
@@ -160,15 +172,11 @@ std::string DeviceRunner::init(const GgufFile& g) {
   // conv.0 map in memory (A/B comparisons); the default is the fused kernel
   const char* su = getenv("PKC_SUB_UNFUSED");
   sub_unfused_ = (su && su[0] == '1') || (cfg_.F1 != 64 && cfg_.F1 != 40);
-  // PKC_LN_FUSED=1: the QKV / pointwise-1 / FFN2-up GEMMs normalise their A
-  // operand themselves (k_gemm_tc2ln). Off by default: the f32 rows it stages
-  // through shared memory add ~80 KB of shared-memory traffic per CTA and
-  // k-block to a mainloop that the plain GEMM already runs at the
-  // shared-memory port's rate, so it is slower than the separate LayerNorm
-  // kernel at the encoder's shapes.
-  const char* lf = getenv("PKC_LN_FUSED");
-  ln_unfused_ = !(lf && lf[0] == '1') || cfg_.d_model % 128 != 0;
-  return upload_weights(g, cfg_, w_, !ln_unfused_);
+  ln_unfused_ = !ln_fused(cfg_);  // must match the fold the weights were packed with
+  const auto t0 = std::chrono::steady_clock::now();
+  std::string err = upload_packed(pw, cfg_, w_, stream_);
+  upload_s_ = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+  return err;
 }
 
 bool DeviceRunner::ensure_ws(size_t bytes) {

@@ -50,7 +50,12 @@ class DeviceRunner {
  public:
   DeviceRunner(const Config& c, int device) : cfg_(c), device_(device) {}
   ~DeviceRunner();
-  std::string init(const GgufFile& g);
+  // Upload a packed weight image to this runner's device (and create its
+  // streams and workspaces).
+  std::string init(const PackedWeights& pw);
+  // Whether the weights are packed with the pre-norm LayerNorms folded in.
+  static bool ln_fused(const Config& c);
+  double upload_seconds() const { return upload_s_; }
   int device() const { return device_; }
   cudaStream_t stream() const { return stream_; }
 
@@ -138,6 +143,7 @@ class DeviceRunner {
   cudaEvent_t ev_fork_ = nullptr, ev_join_ = nullptr;
   bool sub_unfused_ = false;
   bool ln_unfused_ = false;
+  double upload_s_ = 0;
   int* h_tables_ = nullptr;  // pinned staging for the item tables
   size_t h_tables_cap_ = 0;
   // carved workspace pointers for the current plan

@@ -20,11 +20,18 @@
 #include "model.hpp"
 
 #include <algorithm>
+#include <chrono>
+#include <climits>
+#include <cstdio>
+#include <type_traits>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
 #include <functional>
 #include <thread>
+
+#include <sys/stat.h>
+#include <unistd.h>
 
 #include "half.hpp"
 #include "kernels/kernels.h"
@@ -52,6 +59,46 @@ template <typename T>
 void reloc(T*& p, uint8_t* base) {
   if (p) p = reinterpret_cast<T*>(base + (reinterpret_cast<uintptr_t>(p) - 1));
 }
+
+}  // namespace
+
+// Every field of the weight tables that the arena layout defines, in a fixed
+// order: the pointer fields (arena offsets + 1 before upload, device addresses
+// after) and the sizes and flags beside them. Relocation and the pack cache
+// both walk this one list.
+template <class F>
+void for_each_layer_field(LayerWeights& L, F&& f) {
+  f(L.ln_ff1_g); f(L.ln_ff1_b); f(L.ln_att_g); f(L.ln_att_b); f(L.ln_conv_g); f(L.ln_conv_b);
+  f(L.ln_ff2_g); f(L.ln_ff2_b); f(L.ln_out_g); f(L.ln_out_b);
+  f(L.ff1_w1); f(L.ff1_w2); f(L.ff2_w1); f(L.ff2_w2); f(L.ff1_b1); f(L.ff1_b2); f(L.ff2_b1); f(L.ff2_b2);
+  f(L.qkv_w); f(L.qkv_b); f(L.pos_w); f(L.out_w); f(L.out_b); f(L.pos_u); f(L.pos_v);
+  f(L.pw1_w); f(L.pw1_b); f(L.dw_w); f(L.dw_b); f(L.bn_scale); f(L.bn_shift); f(L.pw2_w); f(L.pw2_b);
+  for (QWeight* q : {&L.ff1_q1, &L.ff1_q2, &L.ff2_q1, &L.ff2_q2, &L.qkv_q, &L.out_q}) {
+    f(q->type); f(q->q); f(q->s0); f(q->s1);
+  }
+  f(L.qkv_ln); f(L.pw1_ln); f(L.ff2_ln);
+}
+
+template <class F>
+void for_each_top_field(DeviceWeights& w, F&& f) {
+  f(w.arena_bytes);
+  f(w.window); f(w.dft_basis); f(w.fb_start); f(w.fb_len); f(w.fb_off); f(w.fb_w);
+  f(w.c0_w); f(w.c0_b); f(w.dw1_w); f(w.dw1_b); f(w.dw2_w); f(w.dw2_b);
+  f(w.pw1_w); f(w.pw2_w); f(w.pw1_b); f(w.pw2_b); f(w.out_w); f(w.out_b);
+  f(w.pos_all_w); f(w.pos_all_q.type); f(w.pos_all_q.q); f(w.pos_all_q.s0); f(w.pos_all_q.s1);
+  f(w.ctc_w); f(w.ctc_b); f(w.ctc_v1); f(w.ctc_vpad);
+  f(w.dec_ok); f(w.dec_embed); f(w.dec_w_ih); f(w.dec_w_hh); f(w.dec_b); f(w.dec_w_pred); f(w.dec_b_pred);
+  f(w.dec_w_out); f(w.dec_b_out); f(w.dec_durations); f(w.dec_zeros); f(w.dec_gate0); f(w.dec_w_enc);
+  f(w.dec_b_enc); f(w.dec_jpad);
+}
+
+template <class F>
+void for_each_field(DeviceWeights& w, F&& f) {
+  for_each_top_field(w, f);
+  for (LayerWeights& L : w.layers) for_each_layer_field(L, f);
+}
+
+namespace {
 
 void parallel_rows(int64_t n, const std::function<void(int64_t, int64_t)>& fn) {
   const int nt = (int)std::min<int64_t>(std::max(1u, std::thread::hardware_concurrency()),
@@ -302,9 +349,12 @@ static void fold_layernorm(std::vector<float>& W, int64_t N, int64_t K, const st
   }
 }
 
-std::string upload_weights(const GgufFile& g, const Config& c, DeviceWeights& w, bool fold_ln) {
+std::string pack_weights(const GgufFile& g, const Config& c, bool fold_ln, PackedWeights& p) {
+  const auto t0 = std::chrono::steady_clock::now();
   std::string err;
   Staging st;
+  p = PackedWeights{};
+  DeviceWeights& w = p.tmpl;
   const int d = c.d_model, FF = c.ff_dim, C = c.sub_channels, K = c.conv_kernel, H = c.n_heads;
   const bool bf = c.bf16;
   std::vector<float> f, f2, f3, f4;
@@ -682,53 +732,188 @@ std::string upload_weights(const GgufFile& g, const Config& c, DeviceWeights& w,
     w.dec_ok = true;
   }
 
-  // ---------------- upload
+  w.arena_bytes = st.buf.size();
+  p.bytes = std::move(st.buf);
+  p.pack_s = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+  return "";
+}
+
+std::string upload_packed(const PackedWeights& p, const Config& c, DeviceWeights& w, cudaStream_t st) {
+  w = p.tmpl;
+  int dev_id = 0;
+  cudaGetDevice(&dev_id);
+  w.device = dev_id;
   void* dev = nullptr;
-  if (cudaMalloc(&dev, st.buf.size()) != cudaSuccess)
-    return "cudaMalloc of " + std::to_string(st.buf.size()) + " weight bytes failed";
-  if (cudaMemcpy(dev, st.buf.data(), st.buf.size(), cudaMemcpyHostToDevice) != cudaSuccess) {
+  if (cudaMalloc(&dev, p.bytes.size()) != cudaSuccess)
+    return "cudaMalloc of " + std::to_string(p.bytes.size()) + " weight bytes failed";
+  if (cudaMemcpyAsync(dev, p.bytes.data(), p.bytes.size(), cudaMemcpyHostToDevice, st) != cudaSuccess ||
+      cudaStreamSynchronize(st) != cudaSuccess) {
     cudaFree(dev);
     return "weight upload failed";
   }
   w.arena = dev;
-  w.arena_bytes = st.buf.size();
   uint8_t* base = static_cast<uint8_t*>(dev);
-  reloc(w.window, base); reloc(w.dft_basis, base);
-  reloc(w.fb_start, base); reloc(w.fb_len, base); reloc(w.fb_off, base); reloc(w.fb_w, base);
-  reloc(w.c0_w, base); reloc(w.c0_b, base);
-  reloc(w.dw1_w, base); reloc(w.dw1_b, base); reloc(w.dw2_w, base); reloc(w.dw2_b, base);
-  reloc(w.pw1_w, base); reloc(w.pw2_w, base); reloc(w.pw1_b, base); reloc(w.pw2_b, base);
-  reloc(w.out_w, base); reloc(w.out_b, base); reloc(w.pos_all_w, base);
-  if (w.ctc_v1) { reloc(w.ctc_w, base); reloc(w.ctc_b, base); }
+  for_each_field(w, [&](auto& f) {
+    using T = std::remove_reference_t<decltype(f)>;
+    if constexpr (std::is_pointer_v<T>) reloc(f, base);
+  });
   if (w.dec_ok) {
-    reloc(w.dec_embed, base); reloc(w.dec_w_ih, base); reloc(w.dec_w_hh, base); reloc(w.dec_b, base);
-    reloc(w.dec_w_pred, base); reloc(w.dec_b_pred, base); reloc(w.dec_w_out, base); reloc(w.dec_b_out, base);
-    reloc(w.dec_durations, base); reloc(w.dec_zeros, base); reloc(w.dec_w_enc, base); reloc(w.dec_b_enc, base);
-    reloc(w.dec_gate0, base);
     const int V1 = c.vocab_size + 1, Hp = c.pred_hidden;
-    if (transducer_gate0_launch(w.dec_embed, w.dec_w_ih, w.dec_b, V1, Hp, w.dec_gate0, nullptr) != cudaSuccess ||
-        cudaDeviceSynchronize() != cudaSuccess) {
+    if (transducer_gate0_launch(w.dec_embed, w.dec_w_ih, w.dec_b, V1, Hp, w.dec_gate0, st) != cudaSuccess ||
+        cudaStreamSynchronize(st) != cudaSuccess) {
       cudaFree(dev);
       w.arena = nullptr;
       return "decoder gate table computation failed";
     }
   }
-  auto reloc_q = [&](QWeight& qw) {
-    if (!qw.type) return;
-    reloc(qw.q, base); reloc(qw.s0, base); reloc(qw.s1, base);
-  };
-  reloc_q(w.pos_all_q);
-  for (LayerWeights& L : w.layers) {
-    float** fp[] = {&L.ln_ff1_g, &L.ln_ff1_b, &L.ln_att_g, &L.ln_att_b, &L.ln_conv_g, &L.ln_conv_b,
-                    &L.ln_ff2_g, &L.ln_ff2_b, &L.ln_out_g, &L.ln_out_b, &L.ff1_b1, &L.ff1_b2,
-                    &L.ff2_b1, &L.ff2_b2, &L.qkv_b, &L.out_b, &L.pos_u, &L.pos_v, &L.pw1_b,
-                    &L.dw_w, &L.dw_b, &L.bn_scale, &L.bn_shift, &L.pw2_b};
-    for (float** q : fp) reloc(*q, base);
-    void** vp[] = {&L.ff1_w1, &L.ff1_w2, &L.ff2_w1, &L.ff2_w2, &L.qkv_w, &L.pos_w, &L.out_w,
-                   &L.pw1_w, &L.pw2_w};
-    for (void** q : vp) reloc(*q, base);
-    for (QWeight* q : {&L.ff1_q1, &L.ff1_q2, &L.ff2_q1, &L.ff2_q2, &L.qkv_q, &L.out_q}) reloc_q(*q);
+  return "";
+}
+
+std::string upload_weights(const GgufFile& g, const Config& c, DeviceWeights& w, bool fold_ln) {
+  PackedWeights p;
+  std::string err = pack_weights(g, c, fold_ln, p);
+  if (!err.empty()) return err;
+  return upload_packed(p, c, w, nullptr);
+}
+
+// ---------------------------------------------------------------- pack cache
+namespace {
+
+constexpr char kPackMagic[8] = {'P', 'K', 'C', 'P', 'A', 'C', 'K', '1'};
+constexpr uint32_t kPackVersion = 1;  // bump when a packed layout or the field list changes
+
+struct PackHeader {
+  char magic[8];
+  uint32_t version, n_top, n_layer_fields, pad;
+  uint64_t key, n_layers, arena_bytes, data_offset;
+};
+
+uint64_t fnv1a(uint64_t h, const void* data, size_t n) {
+  const uint8_t* b = static_cast<const uint8_t*>(data);
+  for (size_t i = 0; i < n; ++i) {
+    h ^= b[i];
+    h *= 1099511628211ull;
   }
+  return h;
+}
+
+// Field values of the offset-encoded template as 64-bit words, in visit order.
+std::vector<uint64_t> field_words(DeviceWeights& w, size_t& n_top, size_t& n_layer) {
+  std::vector<uint64_t> out;
+  auto put = [&](auto& f) {
+    using T = std::remove_reference_t<decltype(f)>;
+    if constexpr (std::is_pointer_v<T>) out.push_back(reinterpret_cast<uintptr_t>(f));
+    else out.push_back(static_cast<uint64_t>(f));
+  };
+  for_each_top_field(w, put);
+  n_top = out.size();
+  n_layer = 0;
+  for (LayerWeights& L : w.layers) {
+    const size_t before = out.size();
+    for_each_layer_field(L, put);
+    n_layer = out.size() - before;
+  }
+  return out;
+}
+
+}  // namespace
+
+uint64_t pack_cache_key(const std::string& gguf_path, const Config& c, bool fold_ln) {
+  struct stat sb {};
+  char real[PATH_MAX];
+  const std::string rp = realpath(gguf_path.c_str(), real) ? std::string(real) : gguf_path;
+  uint64_t h = 1469598103934665603ull;
+  h = fnv1a(h, kPackMagic, sizeof(kPackMagic));
+  h = fnv1a(h, &kPackVersion, sizeof(kPackVersion));
+  h = fnv1a(h, rp.data(), rp.size());
+  if (stat(rp.c_str(), &sb) == 0) {
+    const uint64_t v[4] = {(uint64_t)sb.st_size, (uint64_t)sb.st_mtim.tv_sec, (uint64_t)sb.st_mtim.tv_nsec,
+                           (uint64_t)sb.st_ino};
+    h = fnv1a(h, v, sizeof(v));
+  }
+  const char* dal = getenv("PKC_DEQUANT_AT_LOAD");
+  const uint32_t opts[4] = {fold_ln ? 1u : 0u, (dal && dal[0] == '1') ? 1u : 0u, (uint32_t)c.n_layers,
+                            (uint32_t)sizeof(DeviceWeights)};
+  return fnv1a(h, opts, sizeof(opts));
+}
+
+std::string pack_cache_path(const std::string& dir, uint64_t key) {
+  char name[64];
+  snprintf(name, sizeof(name), "pkc_%016llx.pack", (unsigned long long)key);
+  return dir + "/" + name;
+}
+
+std::string pack_cache_store(const std::string& path, uint64_t key, const PackedWeights& p) {
+  DeviceWeights t = p.tmpl;
+  size_t n_top = 0, n_layer = 0;
+  const std::vector<uint64_t> words = field_words(t, n_top, n_layer);
+  PackHeader h{};
+  std::memcpy(h.magic, kPackMagic, sizeof(h.magic));
+  h.version = kPackVersion;
+  h.n_top = (uint32_t)n_top;
+  h.n_layer_fields = (uint32_t)n_layer;
+  h.key = key;
+  h.n_layers = t.layers.size();
+  h.arena_bytes = p.bytes.size();
+  h.data_offset = (sizeof(h) + words.size() * 8 + 4095) / 4096 * 4096;
+  const std::string tmp = path + ".tmp" + std::to_string(getpid());
+  FILE* f = fopen(tmp.c_str(), "wb");
+  if (!f) return "cannot create " + tmp;
+  bool ok = fwrite(&h, sizeof(h), 1, f) == 1 && fwrite(words.data(), 8, words.size(), f) == words.size();
+  const std::vector<uint8_t> pad(h.data_offset - sizeof(h) - words.size() * 8, 0);
+  ok = ok && (pad.empty() || fwrite(pad.data(), 1, pad.size(), f) == pad.size());
+  ok = ok && fwrite(p.bytes.data(), 1, p.bytes.size(), f) == p.bytes.size();
+  ok = (fclose(f) == 0) && ok;
+  if (!ok || rename(tmp.c_str(), path.c_str()) != 0) {
+    unlink(tmp.c_str());
+    return "cannot write " + path;
+  }
+  return "";
+}
+
+std::string pack_cache_load(const std::string& path, uint64_t key, const Config& c, PackedWeights& p) {
+  const auto t0 = std::chrono::steady_clock::now();
+  FILE* f = fopen(path.c_str(), "rb");
+  if (!f) return "no cache file " + path;
+  std::unique_ptr<FILE, int (*)(FILE*)> guard(f, fclose);
+  PackHeader h{};
+  if (fread(&h, sizeof(h), 1, f) != 1 || std::memcmp(h.magic, kPackMagic, sizeof(kPackMagic)) != 0 ||
+      h.version != kPackVersion)
+    return "not a pack cache file: " + path;
+  if (h.key != key) return "pack cache key mismatch: " + path;
+  DeviceWeights t{};
+  t.layers.assign((size_t)c.n_layers, LayerWeights{});
+  size_t n_top = 0, n_layer = 0;
+  field_words(t, n_top, n_layer);
+  if (h.n_layers != t.layers.size() || h.n_top != n_top || h.n_layer_fields != n_layer)
+    return "pack cache field layout mismatch: " + path;
+  std::vector<uint64_t> words(n_top + n_layer * t.layers.size());
+  if (fread(words.data(), 8, words.size(), f) != words.size()) return "truncated pack cache: " + path;
+  size_t k = 0;
+  auto get = [&](auto& fld) {
+    using T = std::remove_reference_t<decltype(fld)>;
+    if constexpr (std::is_pointer_v<T>) fld = reinterpret_cast<T>(static_cast<uintptr_t>(words[k++]));
+    else fld = static_cast<T>(words[k++]);
+  };
+  for_each_top_field(t, get);
+  for (LayerWeights& L : t.layers) for_each_layer_field(L, get);
+  if (t.arena_bytes != h.arena_bytes) return "pack cache size mismatch: " + path;
+  // every offset must land inside the arena
+  bool inside = true;
+  auto check = [&](auto& fld) {
+    using T = std::remove_reference_t<decltype(fld)>;
+    if constexpr (std::is_pointer_v<T>)
+      if (fld && reinterpret_cast<uintptr_t>(fld) - 1 >= h.arena_bytes) inside = false;
+  };
+  for_each_field(t, check);
+  if (!inside) return "pack cache offset out of range: " + path;
+  if (fseeko(f, (off_t)h.data_offset, SEEK_SET) != 0) return "truncated pack cache: " + path;
+  p = PackedWeights{};
+  p.bytes.resize(h.arena_bytes);
+  if (fread(p.bytes.data(), 1, p.bytes.size(), f) != p.bytes.size()) return "truncated pack cache: " + path;
+  p.tmpl = std::move(t);
+  p.from_cache = true;
+  p.pack_s = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
   return "";
 }
 

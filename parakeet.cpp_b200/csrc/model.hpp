@@ -121,6 +121,29 @@ struct DeviceWeights {
   int dec_jpad = 0;
 };
 
+// Host image of one device weight arena: every tensor re-packed into the layout
+// its kernel reads, and a DeviceWeights whose pointer fields hold arena offsets
+// (+1; 0 = absent) until upload_packed relocates them.
+struct PackedWeights {
+  std::vector<uint8_t> bytes;
+  DeviceWeights tmpl;
+  bool from_cache = false;
+  double pack_s = 0;  // host seconds to re-pack (or to read the pack cache)
+};
+
+// Re-pack every weight of `g` on the host (no CUDA call).
+std::string pack_weights(const GgufFile& g, const Config& c, bool fold_ln, PackedWeights& p);
+// Copy the image to the current device (p.bytes may be page-locked by the
+// caller), relocate the pointers and build the device-side derived tables.
+std::string upload_packed(const PackedWeights& p, const Config& c, DeviceWeights& w, cudaStream_t st);
+
+// Pre-pack cache: one file per (GGUF identity, packing options), holding the
+// field table and the arena image; a hit skips the re-pack.
+uint64_t pack_cache_key(const std::string& gguf_path, const Config& c, bool fold_ln);
+std::string pack_cache_path(const std::string& dir, uint64_t key);
+std::string pack_cache_store(const std::string& path, uint64_t key, const PackedWeights& p);
+std::string pack_cache_load(const std::string& path, uint64_t key, const Config& c, PackedWeights& p);
+
 // Upload every encoder weight of `g` to the current CUDA device.
 // Returns an empty string on success, else an error message.
 // fold_ln: fold the pre-norm LayerNorms' gamma / beta into the dense QKV,

@@ -87,6 +87,8 @@ def _declare(L):
     optional = [
         ("pkc_model_open", c_int, c_char_p, POINTER(c_int), c_int, POINTER(c_void_p)),
         ("pkc_model_close", None, c_void_p),
+        ("pkc_model_load_stats", c_int, c_void_p, POINTER(ctypes.c_double), POINTER(ctypes.c_double), POINTER(c_int)),
+        ("pkc_pack_cache_build", c_int, c_char_p, c_char_p, ctypes.c_char_p, c_int),
         ("pkc_model_info_get", c_int, c_void_p, POINTER(ModelInfo)),
         ("pkc_mel_frames", c_int, c_void_p, c_int),
         ("pkc_encoder_frames", c_int, c_void_p, c_int),
@@ -193,6 +195,14 @@ def relpos_attention_noalloc(qkv, ptab, centre, bias_u, bias_v, lens, d, n_heads
                                               c_void_p(stream) if stream else None))
 
 
+def pack_cache_build(gguf_path: str, cache_dir: str) -> str:
+    """pkc_pack_cache_build: the packed weight image of gguf_path in cache_dir
+    (made there if absent, host only); returns the cache file's path."""
+    buf = ctypes.create_string_buffer(4096)
+    _check(lib().pkc_pack_cache_build(gguf_path.encode(), cache_dir.encode(), buf, len(buf)))
+    return buf.value.decode()
+
+
 def shard_plan(n_samples, n_dev, hop=160):
     out = (c_int * len(n_samples))()
     _check(lib().pkc_shard_plan(_ints(n_samples), len(n_samples), n_dev, hop, out))
@@ -212,6 +222,12 @@ class Model:
         info = ModelInfo()
         _check(L.pkc_model_info_get(h, ctypes.byref(info)), h)
         self.info = info
+
+    def load_stats(self):
+        """pkc_model_load_stats: {"pack_s", "upload_s", "from_cache"} of this open."""
+        a, b, c = ctypes.c_double(), ctypes.c_double(), c_int()
+        _check(lib().pkc_model_load_stats(self._h, ctypes.byref(a), ctypes.byref(b), ctypes.byref(c)), self._h)
+        return {"pack_s": a.value, "upload_s": b.value, "from_cache": bool(c.value)}
 
     def close(self):
         if getattr(self, "_h", None):

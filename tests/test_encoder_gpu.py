@@ -8,6 +8,8 @@ normalised features (the reference's own GPU-vs-CPU mel test allows 0.05).
 Quantised weights (q8_0 / q4_k) are dequantised once to the compute type, so
 they carry one extra rounding of the weight and use the same bound.
 """
+import os
+
 import numpy as np
 import pytest
 
@@ -324,6 +326,29 @@ def test_transducer_greedy_matches_oracle(models, oracles, kind):
         for t, u in zip(tk, want):
             assert abs(t[2] - u[2]) < 1e-4
     assert compared >= 2
+
+
+def test_pack_cache_open_matches_packed_open(models, monkeypatch, tmp_path):
+    """Pre-pack cache through pkc_model_open (PKC_PACK_CACHE): the first open
+    packs and writes the cache, the second uploads from it; both give the same
+    encoder output bit for bit, and so does a two-runner open (devices 0, 0:
+    the host image uploaded concurrently to both, the batch sharded)."""
+    import pkc
+    monkeypatch.setenv("PKC_PACK_CACHE", str(tmp_path))
+    pcm = clips([SR * 2 + 7, SR + 333, 9000, SR * 3 + 1], seed=61)
+    outs, stats = [], []
+    for devices in [(0,), (0,), (0, 0)]:
+        m = pkc.Model(models["q8_0"], devices=devices)
+        try:
+            stats.append(m.load_stats())
+            outs.append(m.encode_pcm_batch(pcm))
+        finally:
+            m.close()
+    assert [s["from_cache"] for s in stats] == [False, True, True]
+    assert len([f for f in os.listdir(tmp_path) if f.endswith(".pack")]) == 1
+    for o in outs[1:]:
+        for a, b in zip(outs[0], o):
+            assert np.array_equal(a, b)
 
 
 @pytest.mark.parametrize("variant", ["resident", "streamed", "groups"])
