@@ -88,6 +88,55 @@ const char* pkc_last_error(const pkc_model* m);
 pkc_status pkc_model_open(const char* gguf_path, const int* devices, int n_devices,
                           pkc_model** out);
 
+/* ---- Cache-aware streaming encoder (StreamingEncoder, src/streaming_encoder.hpp:33-66).
+   For models with a parakeet.streaming.* schedule, chunked-limited attention,
+   causal subsampling and causal depthwise conv (e.g. the 120M EOU model). The
+   caller computes the log-mel of the audio and feeds it window by window: the
+   first window is chunk_size_first frames, later ones chunk_size new frames
+   preceded by pre_encode_cache_size frames of overlap. Each step returns the
+   chunk's valid encoder frames; the concatenation equals the offline
+   encoder's output except the final chunk's valid_out_len tail. */
+typedef struct pkc_stream pkc_stream;
+
+typedef struct pkc_stream_schedule {
+  int chunk_size_first;       /* mel frames of the first window */
+  int chunk_size;             /* new mel frames per later window (also the shift) */
+  int pre_encode_cache_size;  /* overlap frames prepended to later windows */
+  int valid_out_len;          /* encoder frames a mid-stream step returns */
+  int drop_extra_pre_encoded; /* subsampled frames dropped from later windows */
+  int attention_cache_size;   /* frames of left attention context kept per layer */
+} pkc_stream_schedule;
+
+/* chunk_size_first() / chunk_size() / pre_encode_cache_size() / valid_out_len()
+   of the reference; PKC_ERR_UNSUPPORTED for a model without a streaming schedule. */
+pkc_status pkc_stream_schedule_get(const pkc_model* m, pkc_stream_schedule* out);
+
+/* StreamingEncoder(ml) + reset(): a stream with zero caches on the model's
+   device_slot-th device (index into the devices passed to pkc_model_open).
+   PKC_ERR_UNSUPPORTED unless the model is a cache-aware streaming model. The
+   model must outlive the stream. Steps of different streams on one model run
+   one at a time. */
+pkc_status pkc_stream_begin(pkc_model* m, int device_slot, pkc_stream** out);
+
+/* reset(): zero the caches, step counter to 0 (a fresh stream). */
+pkc_status pkc_stream_reset(pkc_stream* s);
+
+/* step(mel_chunk_frames, n_mel_frames, is_last, n_valid_out): mel is
+   [n_mels][n_frames] f32 host memory, feature-major (mel[m * n_frames + t]),
+   the whole window including the overlap. out receives [n_valid_out][d_model]
+   time-major f32 (out_cap_floats >= valid frames * d_model, at most
+   (n_frames / 8 + 2) * d_model); mid-stream steps return valid_out_len
+   frames, the last (is_last != 0) all of the chunk's frames. A window too
+   short to produce a frame returns 0 frames and still advances the step. */
+pkc_status pkc_stream_step(pkc_stream* s, const float* mel, int n_frames, int is_last, float* out,
+                           size_t out_cap_floats, int* n_valid_out);
+
+/* step_num(): steps taken since begin / reset; -1 for NULL. */
+int pkc_stream_step_num(const pkc_stream* s);
+
+/* Release the stream's device caches. Safe on NULL. */
+void pkc_stream_free(pkc_stream* s);
+
 /* Timing of the last pkc_model_open of m: host seconds spent re-packing (or
    reading the pre-pack cache), seconds of the slowest device's upload, and
    whether the image came from the cache (1) or was packed (0). */

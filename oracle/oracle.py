@@ -17,6 +17,11 @@ What it restates (paths inside parakeet.cpp, the reference):
   * ctc_greedy (greedy fold, token frame / conf)     src/search.cpp:8-90
   * PredictionNet::step, Joint::step_logits          src/prediction.cpp, src/joint.hpp
   * tdt_greedy, rnnt_decode_frames / rnnt_greedy     src/tdt.cpp:8-126, src/rnnt.cpp:17-122
+  * causal models offline (B = 1): causal subsampling, chunked-limited
+    attention mask, causal depthwise conv, layer_norm conv norm
+      src/subsampling.cpp:25-46,260-388, src/relpos_attention.cpp:30-37,113-131,
+      src/conformer.cpp:38-164
+  * StreamingEncoder::step (cache-aware streaming)   src/streaming_encoder.cpp:98-460
 The batched graph is restated literally: every item is zero-padded to the
 batch's T_max and every mask the reference builds (per-stage subsampling time
 masks, output-frame mask, attention key mask and padded-query zeroing, conv
@@ -37,7 +42,10 @@ bin 8) and its GpuMel-vs-MelFrontend tolerance (tests/test_mel_gpu.cpp: < 0.05),
 (c) a literal pad/reshape/view restatement of rel_shift, and (d) the
 reference's batched == standalone padding-invariance property
 (tests/test_encoder_batch.cpp). The encoder graph beyond those anchors is
-"parity unpinned" against ggml's own kernels.
+"parity unpinned" against ggml's own kernels. The streaming restatement is
+pinned to the offline causal restatement by the reference's cache-aware
+equivalence (tests/test_streaming_encoder.cpp: the concatenated chunk outputs
+equal the offline encoder output except the final chunk's valid_out_len tail).
 """
 from __future__ import annotations
 
@@ -322,10 +330,22 @@ def rel_shift_literal(bd_raw: np.ndarray) -> np.ndarray:
     return np.ascontiguousarray(as_P_T[:, :T])                         # view [T, T] offset 0 + cont
 
 
+def chunked_visible(gq, gk, att_left: int, att_right: int):
+    """Chunked-limited attention (att_context_style "chunked_limited",
+    src/relpos_attention.cpp:113-131, src/streaming_encoder.cpp:231-260): with
+    chunk = att_right + 1, a key is visible iff 0 <= gq/chunk - gk/chunk <=
+    att_left/chunk (global query / key frame indices)."""
+    chunk = att_right + 1
+    left_chunks = att_left // chunk if chunk > 0 else 0
+    diff = np.asarray(gq)[:, None] // chunk - np.asarray(gk)[None, :] // chunk
+    return (diff >= 0) & (diff <= left_chunks)
+
+
 def relpos_attention(w: Weights, li: int, x: np.ndarray, pe: np.ndarray, valid: int,
-                     literal_shift: bool = False) -> np.ndarray:
+                     literal_shift: bool = False, chunked=None) -> np.ndarray:
     """RelPosAttention::build_graph_batched for one item (src/relpos_attention.cpp:162-306).
-    x [T, d] (the normalised attention input), pe [2T-1, d]."""
+    x [T, d] (the normalised attention input), pe [2T-1, d]; chunked = (att_left,
+    att_right) for chunked-limited models."""
     T, d = x.shape
     H = w.H
     dk = d // H
@@ -344,7 +364,10 @@ def relpos_attention(w: Weights, li: int, x: np.ndarray, pe: np.ndarray, valid: 
     else:
         bd = rel_shift_index(bd_raw)
     scale = 1.0 / math.sqrt(dk)
-    mask = np.where(np.arange(T) < valid, 0.0, -np.inf)[None, None, :]
+    vis = np.broadcast_to(np.arange(T)[None, :] < valid, (T, T))
+    if chunked is not None:
+        vis = vis & chunked_visible(np.arange(T), np.arange(T), *chunked)
+    mask = np.where(vis, 0.0, -np.inf)[None]
     s = (ac + bd) * scale + mask
     s = s - s.max(axis=-1, keepdims=True)
     e = np.exp(s)
@@ -365,8 +388,20 @@ def bn_fold(w: Weights, pre: str):
     return sc.astype(np.float64), sh.astype(np.float64)
 
 
-def conv_module(w: Weights, li: int, c: np.ndarray, valid: int) -> np.ndarray:
-    """build_conv_module for one item (src/conformer.cpp:38-164), batch_norm variant."""
+def conv_norm(w: Weights, pre: str, dw: np.ndarray, norm: str) -> np.ndarray:
+    """The norm between the depthwise conv and SiLU (src/conformer.cpp:128-154):
+    LayerNorm over channels (gamma / beta stored as conv.batch_norm.weight /
+    bias) or the host-folded BatchNorm."""
+    if norm == "layer_norm":
+        return layer_norm(dw, w.get(pre + "conv.batch_norm.weight"), w.get(pre + "conv.batch_norm.bias"))
+    sc, sh = bn_fold(w, pre)
+    return dw * sc + sh
+
+
+def conv_module(w: Weights, li: int, c: np.ndarray, valid: int, causal: bool = False,
+                norm: str = "batch_norm") -> np.ndarray:
+    """build_conv_module for one item (src/conformer.cpp:38-164); causal: the
+    depthwise input is padded K-1 on the left only (:102-108)."""
     T, d = c.shape
     pre = f"encoder.layers.{li}."
     g = lambda n: w.get(pre + n)
@@ -374,22 +409,22 @@ def conv_module(w: Weights, li: int, c: np.ndarray, valid: int) -> np.ndarray:
     glu = y[:, :d] * sigmoid(y[:, d:])
     glu[valid:] = 0.0
     K = w.K
-    pad = (K - 1) // 2
+    left = K - 1 if causal else (K - 1) // 2
     dww = g("conv.depthwise_conv.weight")[:, 0, :]             # [d, K]
-    gp = np.zeros((T + 2 * pad, d))
-    gp[pad:pad + T] = glu
+    gp = np.zeros((T + K - 1, d))
+    gp[left:left + T] = glu
     dw = np.zeros((T, d))
     for k in range(K):
         dw += gp[k:k + T] * dww[:, k][None, :]
     if g("conv.depthwise_conv.bias") is not None:
         dw += g("conv.depthwise_conv.bias")
-    sc, sh = bn_fold(w, pre)
-    nrm = silu(dw * sc + sh)
+    nrm = silu(conv_norm(w, pre, dw, norm))
     return linear(nrm, g("conv.pointwise_conv2.weight")[:, :, 0], g("conv.pointwise_conv2.bias"))
 
 
-def conformer_layer(w: Weights, li: int, x: np.ndarray, pe: np.ndarray, valid: int) -> np.ndarray:
-    """ConformerLayer::build_graph_batched for one item (src/conformer.cpp:285-353)."""
+def conformer_layer(w: Weights, li: int, x: np.ndarray, pe: np.ndarray, valid: int, sc=None) -> np.ndarray:
+    """ConformerLayer::build_graph_batched for one item (src/conformer.cpp:285-353);
+    sc (StreamCfg) switches on a causal model's attention mask, conv and conv norm."""
     pre = f"encoder.layers.{li}."
     g = lambda n: w.get(pre + n)
     ln = lambda t, nm: layer_norm(t, g(nm + ".weight"), g(nm + ".bias"))
@@ -399,8 +434,10 @@ def conformer_layer(w: Weights, li: int, x: np.ndarray, pe: np.ndarray, valid: i
         return linear(h, g(nm + ".linear2.weight"), g(nm + ".linear2.bias"))
 
     r = x + 0.5 * ff(ln(x, "norm_feed_forward1"), "feed_forward1")
-    r = r + relpos_attention(w, li, ln(r, "norm_self_att"), pe, valid)
-    r = r + conv_module(w, li, ln(r, "norm_conv"), valid)
+    chunked = (sc.att_left, sc.att_right) if sc is not None and sc.chunked else None
+    r = r + relpos_attention(w, li, ln(r, "norm_self_att"), pe, valid, chunked=chunked)
+    r = r + conv_module(w, li, ln(r, "norm_conv"), valid, causal=bool(sc and sc.conv_causal),
+                        norm=sc.conv_norm if sc is not None else "batch_norm")
     r = r + 0.5 * ff(ln(r, "norm_feed_forward2"), "feed_forward2")
     return ln(r, "norm_out")
 
@@ -443,6 +480,219 @@ def encode_pcm_batch(w: Weights, pcms, n_layers: int | None = None, gpu_graph_me
 
 
 # ------------------------------------------------------------------ CTC head
+
+# =========================================================== causal / cache-aware streaming models
+
+class StreamCfg:
+    """The causal-model and streaming-schedule keys of a GGUF
+    (src/model_loader.cpp:113-131, src/streaming_encoder.cpp:30-60)."""
+
+    def __init__(self, w: Weights):
+        kv = w.kv
+        self.style = str(kv.get("parakeet.encoder.att_context_style", "regular"))
+        self.att_left = int(kv.get("parakeet.encoder.att_context_left", -1))
+        self.att_right = int(kv.get("parakeet.encoder.att_context_right", -1))
+        self.chunked = self.style == "chunked_limited" and self.att_right >= 0
+        self.causal_sub = bool(kv.get("parakeet.encoder.causal_downsampling", False))
+        self.conv_causal = bool(kv.get("parakeet.encoder.conv_causal", False))
+        self.conv_norm = str(kv.get("parakeet.encoder.conv_norm_type", "batch_norm"))
+        arr = lambda k: [int(v) for v in kv.get(k, [])]
+        cs, pc = arr("parakeet.streaming.chunk_size"), arr("parakeet.streaming.pre_encode_cache_size")
+        self.chunk_first = cs[0] if len(cs) > 0 else 9
+        self.chunk_main = cs[1] if len(cs) > 1 else 16
+        self.pre_cache = pc[1] if len(pc) > 1 else 9
+        self.drop_extra = int(kv.get("parakeet.streaming.drop_extra_pre_encoded", 0))
+        self.cache_len = int(kv.get("parakeet.streaming.last_channel_cache_size", 0))
+        self.valid_out_len = int(kv.get("parakeet.streaming.valid_out_len", 0))
+        self.present = "parakeet.streaming.chunk_size" in kv
+
+
+def causal_valid_out_len(T: int, in_valid: int = -1) -> int:
+    """Subsampling::valid_out_len with causal paddings (all_paddings = 3)."""
+    v = in_valid if in_valid >= 0 else T - 1
+    for _ in range(3):
+        v = v // 2 + 1
+    return v
+
+
+def _conv3x3_s2_causal(x: np.ndarray, wk: np.ndarray) -> np.ndarray:
+    """NeMo CausalConv2D as the reference builds it (src/subsampling.cpp:283-295):
+    both spatial axes padded 2 before and 1 after, k=3, stride 2, no other pad."""
+    H, W = x.shape[-2:]
+    Ho, Wo = H // 2 + 1, W // 2 + 1
+    xp = np.zeros(x.shape[:-2] + (H + 3, W + 3), dtype=np.float64)
+    xp[..., 2:H + 2, 2:W + 2] = x
+    out = 0
+    for kh in range(3):
+        for kw in range(3):
+            sl = xp[..., kh:kh + 2 * Ho - 1:2, kw:kw + 2 * Wo - 1:2]
+            out = out + wk[..., kh, kw][..., None, None] * sl
+    return out
+
+
+def subsampling_causal(w: Weights, mel_tf: np.ndarray, in_valid: int = -1):
+    """Subsampling::build_graph, causal branch, one item (src/subsampling.cpp:260-388):
+    every stage's input time frames >= its valid length are zeroed before the
+    causal pad. mel_tf [T, F] -> (x [Tp, d], out_valid)."""
+    T, F = mel_tf.shape
+    v0 = in_valid if in_valid >= 0 else T - 1
+    v1 = v0 // 2 + 1
+    v2 = v1 // 2 + 1
+    mask_time = lambda t, v: t * (np.arange(t.shape[-2]) < v).astype(np.float64)[:, None]
+    g = lambda n: w.get("encoder.pre_encode." + n)
+    x = mask_time(mel_tf.astype(np.float64), v0)
+    y = _conv3x3_s2_causal(x[None], g("conv.0.weight")[:, 0])             # [C, T1, F1]
+    y = np.maximum(y + g("conv.0.bias")[:, None, None], 0.0)
+    for dw_i, pw_i, v in ((2, 3, v1), (5, 6, v2)):
+        y = mask_time(y, v)
+        y = _conv3x3_s2_causal(y, g(f"conv.{dw_i}.weight")[:, 0]) + g(f"conv.{dw_i}.bias")[:, None, None]
+        y = np.einsum("oc,chw->ohw", g(f"conv.{pw_i}.weight")[:, :, 0, 0], y) + g(f"conv.{pw_i}.bias")[:, None, None]
+        y = np.maximum(y, 0.0)
+    C, Tp, Fp = y.shape
+    flat = y.transpose(1, 0, 2).reshape(Tp, C * Fp)                       # idx c*F' + f
+    out_valid = min(causal_valid_out_len(T, in_valid), Tp)
+    flat[out_valid:] = 0.0
+    return flat @ g("out.weight").T + g("out.bias"), out_valid
+
+
+def encode_causal_offline(w: Weights, mel_ft: np.ndarray, n_layers: int | None = None) -> np.ndarray:
+    """The offline encoder on a causal (streaming-trained) model, one clip:
+    causal subsampling, chunked-limited attention, causal depthwise conv and its
+    conv norm (src/encoder.cpp + the causal branches above). mel [F, T] ->
+    [valid, d]."""
+    sc = StreamCfg(w)
+    x, vout = subsampling_causal(w, mel_ft.T, -1)
+    if w.xscaling:
+        x = x * math.sqrt(w.d)
+    pe = rel_pos_encoding(x.shape[0], w.d)
+    for li in range(w.L if n_layers is None else n_layers):
+        x = conformer_layer(w, li, x, pe, vout, sc)
+    return x[:vout]
+
+
+class StreamingEncoder:
+    """StreamingEncoder (src/streaming_encoder.cpp): per-layer attention cache
+    (the last cache_len normalised attention inputs), depthwise-conv cache (the
+    last K-1 GLU outputs) and the count of filled attention-cache frames."""
+
+    def __init__(self, w: Weights, n_layers: int | None = None):
+        self.w = w
+        self.sc = StreamCfg(w)
+        self.nl = w.L if n_layers is None else n_layers
+        self.reset()
+
+    def reset(self):
+        d, K = self.w.d, self.w.K
+        self.step_num = 0
+        self.clc = 0
+        self.ch = [np.zeros((self.sc.cache_len, d)) for _ in range(self.nl)]
+        self.tm = [np.zeros((K - 1, d)) for _ in range(self.nl)]
+
+    def _attention(self, li, attn_in, kv, pe, Tc):
+        w, sc = self.w, self.sc
+        d, H = w.d, w.H
+        dk = d // H
+        cache_len = sc.cache_len
+        Tk = cache_len + Tc
+        pre = f"encoder.layers.{li}.self_attn."
+        g = lambda n: w.get(pre + n)
+        q = linear(attn_in, g("linear_q.weight"), g("linear_q.bias")).reshape(Tc, H, dk).transpose(1, 0, 2)
+        k = linear(kv, g("linear_k.weight"), g("linear_k.bias")).reshape(Tk, H, dk).transpose(1, 0, 2)
+        v = linear(kv, g("linear_v.weight"), g("linear_v.bias")).reshape(Tk, H, dk).transpose(1, 0, 2)
+        P = 2 * Tk - 1
+        p = linear(pe.astype(np.float64), g("linear_pos.weight")).reshape(P, H, dk).transpose(1, 0, 2)
+        qu = q + g("pos_bias_u")[:, None, :]
+        qv = q + g("pos_bias_v")[:, None, :]
+        ac = qu @ k.transpose(0, 2, 1)                                     # [H, Tc, Tk]
+        bd_raw = qv @ p.transpose(0, 2, 1)                                 # [H, Tc, P]
+        i = np.arange(Tc)[:, None]
+        j = np.arange(Tk)[None, :]
+        bd = np.take_along_axis(bd_raw, np.broadcast_to(j + Tc - 1 - i, (H, Tc, Tk)), axis=-1)
+        gq = cache_len + np.arange(Tc)
+        vis = chunked_visible(gq, np.arange(Tk), sc.att_left, sc.att_right)
+        vis &= (np.arange(Tk) >= cache_len - self.clc)[None, :]           # empty-cache mask
+        s = (ac + bd) / math.sqrt(dk) + np.where(vis, 0.0, -np.inf)[None]
+        s = s - s.max(axis=-1, keepdims=True)
+        e = np.exp(s)
+        ctx = ((e / e.sum(axis=-1, keepdims=True)) @ v).transpose(1, 0, 2).reshape(Tc, d)
+        return linear(ctx, g("linear_out.weight"), g("linear_out.bias"))
+
+    def _layer(self, li, x, pe, Tc):
+        """build_stream_layer (src/streaming_encoder.cpp:98-338)."""
+        w, sc = self.w, self.sc
+        d, K = w.d, w.K
+        pre = f"encoder.layers.{li}."
+        g = lambda n: w.get(pre + n)
+        ln = lambda t, nm: layer_norm(t, g(nm + ".weight"), g(nm + ".bias"))
+
+        def ff(t, nm):
+            h = silu(linear(t, g(nm + ".linear1.weight"), g(nm + ".linear1.bias")))
+            return linear(h, g(nm + ".linear2.weight"), g(nm + ".linear2.bias"))
+
+        r = x + 0.5 * ff(ln(x, "norm_feed_forward1"), "feed_forward1")
+        attn_in = ln(r, "norm_self_att")
+        kv = np.concatenate([self.ch[li], attn_in], axis=0)
+        r = r + self._attention(li, attn_in, kv, pe, Tc)
+        next_ch = kv[-sc.cache_len:].copy() if sc.cache_len > 0 else kv[:0].copy()
+        c = ln(r, "norm_conv")
+        y = linear(c, g("conv.pointwise_conv1.weight")[:, :, 0], g("conv.pointwise_conv1.bias"))
+        glu = y[:, :d] * sigmoid(y[:, d:])
+        dw_in = np.concatenate([self.tm[li], glu], axis=0)               # [K-1+Tc, d]
+        next_tm = dw_in[-(K - 1):].copy()
+        dww = g("conv.depthwise_conv.weight")[:, 0, :]
+        dw = np.zeros((Tc, d))
+        for kk in range(K):
+            dw += dw_in[kk:kk + Tc] * dww[:, kk][None, :]
+        if g("conv.depthwise_conv.bias") is not None:
+            dw += g("conv.depthwise_conv.bias")
+        nrm = silu(conv_norm(w, pre, dw, sc.conv_norm))
+        r = r + linear(nrm, g("conv.pointwise_conv2.weight")[:, :, 0], g("conv.pointwise_conv2.bias"))
+        r = r + 0.5 * ff(ln(r, "norm_feed_forward2"), "feed_forward2")
+        return ln(r, "norm_out"), next_ch, next_tm
+
+    def step(self, mel_window_ft: np.ndarray, is_last: bool) -> np.ndarray:
+        """StreamingEncoder::step (src/streaming_encoder.cpp:340-460): mel
+        window [F, n] (already holding the pre-encode overlap) -> the chunk's
+        valid frames [valid, d]."""
+        w, sc = self.w, self.sc
+        n = mel_window_ft.shape[1]
+        x, _ = subsampling_causal(w, mel_window_ft.T, in_valid=n)
+        drop = sc.drop_extra if self.step_num != 0 else 0
+        Tc = x.shape[0] - drop
+        if Tc <= 0:
+            self.step_num += 1
+            return np.zeros((0, w.d))
+        x = x[drop:]
+        if w.xscaling:
+            x = x * math.sqrt(w.d)
+        pe = rel_pos_encoding(sc.cache_len + Tc, w.d)
+        nch, ntm = [], []
+        for li in range(self.nl):
+            x, a, b = self._layer(li, x, pe, Tc)
+            nch.append(a)
+            ntm.append(b)
+        self.ch, self.tm = nch, ntm
+        self.clc = min(sc.cache_len, self.clc + Tc)
+        self.step_num += 1
+        valid = Tc if is_last else min(sc.valid_out_len, Tc)
+        return x[:valid]
+
+
+def stream_schedule(sc: StreamCfg, T: int):
+    """The chunk windows (lo, hi, is_last) of a T-frame mel under the model's
+    schedule (CacheAwareStreamingAudioBuffer, tests/test_streaming_encoder.cpp:70-100)."""
+    out, idx, first = [], 0, True
+    while idx < T:
+        size = sc.chunk_first if first else sc.chunk_main
+        hi = min(idx + size, T)
+        if hi - idx <= 0:
+            break
+        lo = idx if first else max(0, idx - sc.pre_cache)
+        out.append((lo, hi, hi >= T))
+        idx += size
+        first = False
+    return out
+
 
 def ctc_head_weights(w: Weights):
     """The CTC head's weight [V+1, d] and bias [V+1] (hybrid name first, then

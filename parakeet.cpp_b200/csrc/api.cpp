@@ -24,6 +24,12 @@ struct pkc_model {
   int from_cache = 0;
 };
 
+struct pkc_stream {
+  pkc_model* m;
+  pkc::DeviceRunner* r;
+  pkc::DeviceRunner::StreamState* st;
+};
+
 namespace pkc {
 const char* model_error(const pkc_model* m) { return m->last_error.c_str(); }
 }  // namespace pkc
@@ -135,6 +141,73 @@ pkc_status pkc_model_open(const char* gguf_path, const int* devices, int n_devic
   } catch (const std::exception& e) {
     return pkc::set_thread_error(PKC_ERR_INTERNAL, e.what());
   }
+}
+
+pkc_status pkc_stream_schedule_get(const pkc_model* m, pkc_stream_schedule* o) {
+  if (!m || !o) return pkc::set_thread_error(PKC_ERR_ARG, "pkc_stream_schedule_get: NULL argument");
+  const pkc::Config& c = m->cfg;
+  if (!c.stream.present) return pkc::set_thread_error(PKC_ERR_UNSUPPORTED, "not a cache-aware streaming model");
+  o->chunk_size_first = c.stream.chunk_first;
+  o->chunk_size = c.stream.chunk_main;
+  o->pre_encode_cache_size = c.stream.pre_cache;
+  o->valid_out_len = c.stream.valid_out_len;
+  o->drop_extra_pre_encoded = c.stream.drop_extra;
+  o->attention_cache_size = c.stream.cache_len;
+  return PKC_OK;
+}
+
+pkc_status pkc_stream_begin(pkc_model* m, int device_slot, pkc_stream** out) {
+  if (!m || !out) return pkc::set_thread_error(PKC_ERR_ARG, "pkc_stream_begin: NULL argument");
+  *out = nullptr;
+  if (device_slot < 0 || device_slot >= (int)m->runners.size())
+    return fail(m, PKC_ERR_ARG, "pkc_stream_begin: device slot " + std::to_string(device_slot) + " out of range");
+  try {
+    std::lock_guard<std::mutex> lk(m->mu);
+    std::string err;
+    pkc::DeviceRunner* r = m->runners[device_slot].get();
+    pkc::DeviceRunner::StreamState* st = r->stream_create(err);
+    if (!st) return fail(m, err.find("cudaMalloc") != std::string::npos ? PKC_ERR_OOM : PKC_ERR_UNSUPPORTED, err);
+    *out = new pkc_stream{m, r, st};
+    return PKC_OK;
+  } catch (const std::bad_alloc&) {
+    return fail(m, PKC_ERR_OOM, "host allocation failed");
+  }
+}
+
+pkc_status pkc_stream_reset(pkc_stream* s) {
+  if (!s) return pkc::set_thread_error(PKC_ERR_ARG, "pkc_stream_reset: NULL stream");
+  std::lock_guard<std::mutex> lk(s->m->mu);
+  std::string err;
+  const pkc_status st = s->r->stream_reset(*s->st, err);
+  return st == PKC_OK ? PKC_OK : fail(s->m, st, err);
+}
+
+pkc_status pkc_stream_step(pkc_stream* s, const float* mel, int n_frames, int is_last, float* out,
+                           size_t out_cap_floats, int* n_valid_out) {
+  if (!s || !mel || !out || !n_valid_out) return pkc::set_thread_error(PKC_ERR_ARG, "pkc_stream_step: NULL argument");
+  *n_valid_out = 0;
+  if (n_frames <= 0) return fail(s->m, PKC_ERR_ARG, "pkc_stream_step: n_frames must be positive");
+  try {
+    std::lock_guard<std::mutex> lk(s->m->mu);
+    std::string err;
+    const pkc_status st = s->r->stream_step(*s->st, mel, n_frames, is_last != 0, out, out_cap_floats, n_valid_out, err);
+    return st == PKC_OK ? PKC_OK : fail(s->m, st, "pkc_stream_step: " + err);
+  } catch (const std::bad_alloc&) {
+    return fail(s->m, PKC_ERR_OOM, "host allocation failed");
+  }
+}
+
+int pkc_stream_step_num(const pkc_stream* s) { return s ? pkc::DeviceRunner::stream_step_num(*s->st) : -1; }
+
+void pkc_stream_free(pkc_stream* s) {
+  if (!s) return;
+  {
+    std::lock_guard<std::mutex> lk(s->m->mu);
+    cudaSetDevice(s->r->device());
+    cudaStreamSynchronize(s->r->stream());
+    pkc::DeviceRunner::stream_destroy(s->st);
+  }
+  delete s;
 }
 
 pkc_status pkc_model_load_stats(const pkc_model* m, double* pack_seconds, double* upload_seconds, int* from_cache) {

@@ -322,22 +322,12 @@ pkc_status DeviceRunner::gemm_ln(const float* x, const float* stats, const void*
   return PKC_OK;
 }
 
-#define PKC_CK(expr, what)                                                             \
-  do {                                                                                 \
-    cudaError_t e_ = (expr);                                                           \
-    if (e_ != cudaSuccess) {                                                           \
-      err = std::string(what) + ": " + cudaGetErrorString(e_);                         \
-      return PKC_ERR_CUDA;                                                             \
-    }                                                                                  \
-  } while (0)
-#define PKC_ST(expr)                 \
-  do {                               \
-    pkc_status s_ = (expr);          \
-    if (s_ != PKC_OK) return s_;     \
-  } while (0)
-
 pkc_status DeviceRunner::prepare(const Plan& p, cudaStream_t st, std::string& err) {
   const Config& c = cfg_;
+  if (c.causal()) {
+    err = "offline encoding of a causal (cache-aware streaming) model is not implemented; use pkc_stream_*";
+    return PKC_ERR_UNSUPPORTED;
+  }
   const int d = c.d_model, F = c.n_mels, C = c.sub_channels;
   const size_t hs = 2;
   const int B = p.B;

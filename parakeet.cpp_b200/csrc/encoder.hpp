@@ -92,6 +92,18 @@ class DeviceRunner {
   void profile_enable(bool on);
   std::vector<KernelStatAcc> profile_read();
 
+  // Cache-aware streaming encoder (StreamingEncoder, src/streaming_encoder.hpp:
+  // 33-66): per-stream caches and scratch on this runner's device (stream.cpp).
+  struct StreamState;
+  StreamState* stream_create(std::string& err);
+  static void stream_destroy(StreamState* s);
+  pkc_status stream_reset(StreamState& s, std::string& err);
+  // One chunk window: mel [n_mels][n_frames] host f32 (feature-major, the
+  // pre-encode overlap included); out [valid][d] host f32.
+  pkc_status stream_step(StreamState& s, const float* mel, int n_frames, bool is_last, float* out,
+                         size_t out_cap_floats, int* n_valid, std::string& err);
+  static int stream_step_num(const StreamState& s);
+
  private:
   pkc_status prepare(const Plan& p, cudaStream_t st, std::string& err);
   pkc_status run_frontend(const Plan& p, cudaStream_t st, std::string& err);
@@ -187,5 +199,20 @@ class DeviceRunner {
   cudaEvent_t prof_open_ = nullptr;
   bool prof_error_ = false;  // an event call failed while profiling (reported by profile_read)
 };
+
+// Error plumbing of the runner's methods (they return pkc_status and fill err).
+#define PKC_CK(expr, what)                                                             \
+  do {                                                                                 \
+    cudaError_t e_ = (expr);                                                           \
+    if (e_ != cudaSuccess) {                                                           \
+      err = std::string(what) + ": " + cudaGetErrorString(e_);                         \
+      return PKC_ERR_CUDA;                                                             \
+    }                                                                                  \
+  } while (0)
+#define PKC_ST(expr)                 \
+  do {                               \
+    pkc_status s_ = (expr);          \
+    if (s_ != PKC_OK) return s_;     \
+  } while (0)
 
 }  // namespace pkc

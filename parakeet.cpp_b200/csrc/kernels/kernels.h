@@ -188,6 +188,31 @@ size_t transducer_partial_bytes(int grid, int B);
 int transducer_grid();
 cudaError_t transducer_greedy_launch(const TransducerArgs& a, int grid, cudaStream_t st);
 
+// Cache-aware streaming encoder (stream.cu). Causal subsampling stages: mel
+// window [F][n] f32 (frames >= valid zero) -> [T1][F1][C] bf16, T1 = n/2 + 1,
+// F1 = F/2 + 1; depthwise stage [Ti][Fi][C] -> [Ti/2 + 1][Fi/2 + 1][C].
+cudaError_t causal_conv0_launch(const float* mel, int F, int n, int valid, const float* w, const float* b, int C,
+                                int T1, int F1, __nv_bfloat16* out, cudaStream_t st);
+cudaError_t causal_dw_launch(const __nv_bfloat16* in, int Ti, int Fi, int valid, const float* w, const float* b,
+                             int C, int To, int Fo, __nv_bfloat16* out, cudaStream_t st);
+struct StreamAttnArgs {
+  const void* qkv;       // [cache_len + Tc, 3d]: rows of [attention cache | chunk], q | k | v
+  const void* ptab;      // this layer's projected positions: row r = relative position cache_len + Tc - 1 - r
+  int ldp;               // row stride of ptab (elements)
+  const float* bias_u;   // [d]
+  const float* bias_v;
+  void* ctx;             // [Tc, d]
+  int d, n_heads, Tc, cache_len;
+  int filled;            // valid frames in the attention cache (its last `filled` rows)
+  int att_left, att_right;
+};
+cudaError_t stream_attention_launch(const StreamAttnArgs& a, bool bf16, cudaStream_t st);
+// in [K - 1 + Tc, d] (conv cache rows, then the chunk's GLU rows) -> out [Tc, d]:
+// depthwise conv + bias, then LayerNorm over d (g, b = gamma, beta) or the
+// folded BatchNorm (g, b = scale, shift), then SiLU
+cudaError_t stream_dwconv_launch(const void* in, void* out, int Tc, int d, int K, const float* w, const float* bias,
+                                 const float* g, const float* b, bool layer_norm, bool bf16, cudaStream_t st);
+
 // packed time-major [M, d] -> per item channels-first [d, v_b], items concatenated
 cudaError_t to_channels_first_launch(const float* x, float* out, int d, const int* item_off,
                                      const int* item_len, int B, int max_len, cudaStream_t st);

@@ -1,0 +1,256 @@
+// Cache-aware streaming encoder kernels (reference: StreamingEncoder,
+// src/streaming_encoder.cpp, and the causal branches of the subsampling and
+// conv module). One chunk is a few frames, so these kernels are sized for
+// latency, not for HBM bandwidth; the projections around them are the same
+// tcgen05 GEMMs the offline encoder uses.
+//
+//   k_causal_conv0   Conv2d(1 -> C, 3x3, stride 2) over the mel window, both
+//                    axes padded 2 before and 1 after (NeMo CausalConv2D,
+//                    src/subsampling.cpp:283-295), + bias + ReLU
+//   k_causal_dw      depthwise Conv2d(C, 3x3, stride 2), same padding, + bias
+//   k_stream_attn    rel-pos attention of the chunk's queries over the
+//                    [attention cache | chunk] keys with the chunked-limited and
+//                    empty-cache mask (src/streaming_encoder.cpp:170-284)
+//   k_stream_dwconv  causal depthwise Conv1d over [conv cache | GLU], + bias,
+//                    LayerNorm over channels or folded BatchNorm, SiLU
+//                    (src/streaming_encoder.cpp:286-338, src/conformer.cpp:102-154)
+#include "common.cuh"
+#include "kernels.h"
+
+namespace pkc {
+
+namespace {
+
+template <typename H>
+__device__ __forceinline__ float ld_h(const H* p) {
+  if constexpr (sizeof(H) == 2 && std::is_same<H, __half>::value) return __half2float(*p);
+  else return __bfloat162float(*p);
+}
+template <typename H>
+__device__ __forceinline__ H to_h(float v) {
+  if constexpr (std::is_same<H, __half>::value) return __float2half_rn(v);
+  else return __float2bfloat16_rn(v);
+}
+
+// mel [F][n] (feature-major window); frames >= valid are zero (the reference's
+// per-stage time mask). Output [T1][F1][C] bf16, channel fastest.
+__global__ void k_causal_conv0(const float* __restrict__ mel, int F, int n, int valid, const float* __restrict__ w,
+                               const float* __restrict__ b, int C, int T1, int F1, __nv_bfloat16* __restrict__ out) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)T1 * F1 * C) return;
+  const int c = (int)(i % C), f1 = (int)((i / C) % F1), t1 = (int)(i / ((long long)C * F1));
+  float acc = b[c];
+#pragma unroll
+  for (int kh = 0; kh < 3; ++kh) {
+    const int t = 2 * t1 + kh - 2;
+    if (t < 0 || t >= n || t >= valid) continue;
+#pragma unroll
+    for (int kw = 0; kw < 3; ++kw) {
+      const int f = 2 * f1 + kw - 2;
+      if (f < 0 || f >= F) continue;
+      acc = fmaf(w[c * 9 + kh * 3 + kw], mel[(size_t)f * n + t], acc);
+    }
+  }
+  out[i] = __float2bfloat16_rn(fmaxf(acc, 0.f));
+}
+
+// in [Ti][Fi][C], rows >= valid zero; w tap-major [9][C]. Out [To][Fo][C].
+__global__ void k_causal_dw(const __nv_bfloat16* __restrict__ in, int Ti, int Fi, int valid, const float* __restrict__ w,
+                            const float* __restrict__ b, int C, int To, int Fo, __nv_bfloat16* __restrict__ out) {
+  const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= (long long)To * Fo * C) return;
+  const int c = (int)(i % C), fo = (int)((i / C) % Fo), to = (int)(i / ((long long)C * Fo));
+  float acc = b[c];
+#pragma unroll
+  for (int kh = 0; kh < 3; ++kh) {
+    const int t = 2 * to + kh - 2;
+    if (t < 0 || t >= Ti || t >= valid) continue;
+#pragma unroll
+    for (int kw = 0; kw < 3; ++kw) {
+      const int f = 2 * fo + kw - 2;
+      if (f < 0 || f >= Fi) continue;
+      acc = fmaf(w[(kh * 3 + kw) * C + c], __bfloat162float(in[((size_t)t * Fi + f) * C + c]), acc);
+    }
+  }
+  out[i] = __float2bfloat16_rn(acc);
+}
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __syncthreads();  // red is reused
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float s = 0.f;
+  for (int w = 0; w < nw; ++w) s += red[w];
+  return s;
+}
+__device__ __forceinline__ float block_max(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  __syncthreads();
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float m = -INFINITY;
+  for (int w = 0; w < nw; ++w) m = fmaxf(m, red[w]);
+  return m;
+}
+
+constexpr int SA_THREADS = 128;
+constexpr int SA_MAX_KEYS = 4096;
+
+// One CTA per (head, query). qkv [Tk, 3d] (q | k | v), the chunk's queries
+// at rows cache_len .. Tk - 1; ptab rows 0 .. 2 Tk - 2 hold the projected
+// positions Tk - 1 ... -(Tk - 1) (row stride ldp); ctx [Tc, d].
+template <typename H>
+__global__ void __launch_bounds__(SA_THREADS) k_stream_attn(StreamAttnArgs a) {
+  __shared__ float qu[128], qv[128], red[SA_THREADS / 32];
+  __shared__ float prob[SA_MAX_KEYS];
+  const int head = blockIdx.x, i = blockIdx.y;
+  const int d = a.d, dk = d / a.n_heads, Tk = a.cache_len + a.Tc;
+  const H* qkv = static_cast<const H*>(a.qkv);
+  const H* ptab = static_cast<const H*>(a.ptab);
+  const int qrow = a.cache_len + i;
+  for (int e = threadIdx.x; e < dk; e += SA_THREADS) {
+    const float q = ld_h(qkv + (size_t)qrow * 3 * d + head * dk + e);
+    qu[e] = q + a.bias_u[head * dk + e];
+    qv[e] = q + a.bias_v[head * dk + e];
+  }
+  __syncthreads();
+  // chunked-limited: chunk = att_right + 1, visible iff 0 <= gq/chunk - gk/chunk <= att_left/chunk;
+  // the cache's first cache_len - filled columns are not filled yet
+  const int chunk = a.att_right + 1;
+  const int left_chunks = chunk > 0 ? a.att_left / chunk : 0;
+  const int gq = qrow, first_filled = a.cache_len - a.filled;
+  const float scale = rsqrtf((float)dk);
+  float mx = -INFINITY;
+  for (int j = threadIdx.x; j < Tk; j += SA_THREADS) {
+    const int diff = gq / chunk - j / chunk;
+    float s = -INFINITY;
+    if (j >= first_filled && diff >= 0 && diff <= left_chunks) {
+      const H* kr = qkv + (size_t)j * 3 * d + d + head * dk;
+      const H* pr = ptab + (size_t)(j + a.Tc - 1 - i) * a.ldp + head * dk;  // relative position gq - j
+      float ac = 0.f, bd = 0.f;
+      for (int e = 0; e < dk; ++e) {
+        ac = fmaf(qu[e], ld_h(kr + e), ac);
+        bd = fmaf(qv[e], ld_h(pr + e), bd);
+      }
+      s = (ac + bd) * scale;
+    }
+    prob[j] = s;
+    mx = fmaxf(mx, s);
+  }
+  mx = block_max(mx, red);
+  float sum = 0.f;
+  for (int j = threadIdx.x; j < Tk; j += SA_THREADS) {
+    const float p = prob[j] == -INFINITY ? 0.f : __expf(prob[j] - mx);
+    prob[j] = p;
+    sum += p;
+  }
+  sum = block_sum(sum, red);  // ends with a barrier: prob[] is complete
+  const float inv = 1.0f / sum;
+  for (int e = threadIdx.x; e < dk; e += SA_THREADS) {
+    float acc = 0.f;
+    for (int j = 0; j < Tk; ++j) acc = fmaf(prob[j], ld_h(qkv + (size_t)j * 3 * d + 2 * d + head * dk + e), acc);
+    static_cast<H*>(a.ctx)[(size_t)i * d + head * dk + e] = to_h<H>(acc * inv);
+  }
+}
+
+constexpr int SD_THREADS = 256;
+
+// One CTA per output frame t: in rows t .. t + K - 1 of [conv cache | GLU]
+// ([K - 1 + Tc, d]); out [Tc, d].
+template <typename H, int CPT>
+__global__ void __launch_bounds__(SD_THREADS) k_stream_dwconv(const H* __restrict__ in, H* __restrict__ out, int d,
+                                                              int K, const float* __restrict__ w,
+                                                              const float* __restrict__ bias,
+                                                              const float* __restrict__ g,
+                                                              const float* __restrict__ bt, int layer_norm) {
+  __shared__ float red[SD_THREADS / 32];
+  const int t = blockIdx.x;
+  float v[CPT];
+  float s = 0.f;
+#pragma unroll
+  for (int u = 0; u < CPT; ++u) {
+    const int c = threadIdx.x + u * SD_THREADS;
+    float acc = 0.f;
+    if (c < d) {
+      acc = bias ? bias[c] : 0.f;
+      for (int k = 0; k < K; ++k) acc = fmaf(w[k * d + c], ld_h(in + (size_t)(t + k) * d + c), acc);
+    }
+    v[u] = acc;
+    s += acc;
+  }
+  if (layer_norm) {  // ggml_norm over channels (population variance, eps 1e-5) * gamma + beta
+    const float mean = block_sum(s, red) / (float)d;
+    float q = 0.f;
+#pragma unroll
+    for (int u = 0; u < CPT; ++u)
+      if (threadIdx.x + u * SD_THREADS < d) q += (v[u] - mean) * (v[u] - mean);
+    const float rstd = rsqrtf(block_sum(q, red) / (float)d + 1e-5f);
+#pragma unroll
+    for (int u = 0; u < CPT; ++u) {
+      const int c = threadIdx.x + u * SD_THREADS;
+      if (c < d) v[u] = (v[u] - mean) * rstd * g[c] + bt[c];
+    }
+  } else {
+#pragma unroll
+    for (int u = 0; u < CPT; ++u) {
+      const int c = threadIdx.x + u * SD_THREADS;
+      if (c < d) v[u] = v[u] * g[c] + bt[c];
+    }
+  }
+#pragma unroll
+  for (int u = 0; u < CPT; ++u) {
+    const int c = threadIdx.x + u * SD_THREADS;
+    if (c < d) out[(size_t)t * d + c] = to_h<H>(v[u] / (1.0f + __expf(-v[u])));
+  }
+}
+
+}  // namespace
+
+cudaError_t causal_conv0_launch(const float* mel, int F, int n, int valid, const float* w, const float* b, int C,
+                                int T1, int F1, __nv_bfloat16* out, cudaStream_t st) {
+  const long long total = (long long)T1 * F1 * C;
+  if (total <= 0) return cudaSuccess;
+  k_causal_conv0<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(mel, F, n, valid, w, b, C, T1, F1, out);
+  return cudaGetLastError();
+}
+
+cudaError_t causal_dw_launch(const __nv_bfloat16* in, int Ti, int Fi, int valid, const float* w, const float* b,
+                             int C, int To, int Fo, __nv_bfloat16* out, cudaStream_t st) {
+  const long long total = (long long)To * Fo * C;
+  if (total <= 0) return cudaSuccess;
+  k_causal_dw<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(in, Ti, Fi, valid, w, b, C, To, Fo, out);
+  return cudaGetLastError();
+}
+
+cudaError_t stream_attention_launch(const StreamAttnArgs& a, bool bf16, cudaStream_t st) {
+  if (a.Tc <= 0) return cudaSuccess;
+  const int dk = a.n_heads > 0 ? a.d / a.n_heads : 0;
+  if (dk <= 0 || dk > 128 || a.cache_len + a.Tc > SA_MAX_KEYS || a.filled < 0 || a.filled > a.cache_len ||
+      a.att_right < 0)
+    return cudaErrorInvalidValue;
+  const dim3 grid(a.n_heads, a.Tc);
+  if (bf16) k_stream_attn<__nv_bfloat16><<<grid, SA_THREADS, 0, st>>>(a);
+  else k_stream_attn<__half><<<grid, SA_THREADS, 0, st>>>(a);
+  return cudaGetLastError();
+}
+
+cudaError_t stream_dwconv_launch(const void* in, void* out, int Tc, int d, int K, const float* w, const float* bias,
+                                 const float* g, const float* b, bool layer_norm, bool bf16, cudaStream_t st) {
+  if (Tc <= 0) return cudaSuccess;
+  if (d > 4 * SD_THREADS) return cudaErrorInvalidValue;
+  const int ln = layer_norm ? 1 : 0;
+  if (bf16)
+    k_stream_dwconv<__nv_bfloat16, 4><<<Tc, SD_THREADS, 0, st>>>(static_cast<const __nv_bfloat16*>(in),
+                                                                  static_cast<__nv_bfloat16*>(out), d, K, w, bias, g, b, ln);
+  else
+    k_stream_dwconv<__half, 4><<<Tc, SD_THREADS, 0, st>>>(static_cast<const __half*>(in), static_cast<__half*>(out), d,
+                                                           K, w, bias, g, b, ln);
+  return cudaGetLastError();
+}
+
+}  // namespace pkc

@@ -311,9 +311,29 @@ std::string read_config(const GgufFile& g, Config& c) {
   if (c.ff_dim % 256) return "ff_dim must be a multiple of 256";
   if (c.sub_channels != 256) return "subsampling_conv_channels must be 256";
   if (c.subsampling_factor != 8) return "only dw_striding 8x subsampling is implemented";
-  if (c.conv_norm_type != "batch_norm") return "conv_norm_type " + c.conv_norm_type + " (streaming) not supported";
-  if (c.att_context_style != "regular" || c.causal_downsampling || c.conv_causal)
-    return "cache-aware streaming models are out of scope";
+  if (c.conv_norm_type != "batch_norm" && c.conv_norm_type != "layer_norm")
+    return "conv_norm_type " + c.conv_norm_type + " not supported (batch_norm, layer_norm)";
+  c.conv_ln = c.conv_norm_type == "layer_norm";
+  if (c.att_context_style != "regular" && c.att_context_style != "chunked_limited")
+    return "att_context_style " + c.att_context_style + " not supported (regular, chunked_limited)";
+  c.att_left = g.i32("parakeet.encoder.att_context_left", -1);
+  c.att_right = g.i32("parakeet.encoder.att_context_right", -1);
+  c.chunked = c.att_context_style == "chunked_limited" && c.att_right >= 0;
+  {
+    const std::vector<int64_t> cs = g.int_array("parakeet.streaming.chunk_size");
+    const std::vector<int64_t> pc = g.int_array("parakeet.streaming.pre_encode_cache_size");
+    Config::Streaming& sc = c.stream;
+    sc.present = !cs.empty();
+    if (cs.size() > 0) sc.chunk_first = (int)cs[0];
+    if (cs.size() > 1) sc.chunk_main = (int)cs[1];
+    if (pc.size() > 1) sc.pre_cache = (int)pc[1];
+    sc.drop_extra = g.i32("parakeet.streaming.drop_extra_pre_encoded", 0);
+    sc.cache_len = g.i32("parakeet.streaming.last_channel_cache_size", 0);
+    sc.valid_out_len = g.i32("parakeet.streaming.valid_out_len", 0);
+    if (sc.present && (sc.chunk_first <= 0 || sc.chunk_main <= 0 || sc.pre_cache < 0 || sc.drop_extra < 0 ||
+                       sc.cache_len < 0 || sc.cache_len > 4096 || sc.valid_out_len < 0))
+      return "bad parakeet.streaming.* schedule";
+  }
   if (c.conv_kernel % 2 == 0 || c.conv_kernel < 3 || c.conv_kernel > 9)
     return "depthwise kernel must be odd, 3..9";
   if (c.n_fft != 512) return "n_fft must be 512";
@@ -321,9 +341,11 @@ std::string read_config(const GgufFile& g, Config& c) {
   if (c.mag_power != 2.f) return "mag_power must be 2";
   if (c.normalize != "per_feature") return "normalize must be per_feature";
   if (c.n_mels <= 0 || c.n_mels > 512) return "bad n_mels";
-  c.F1 = conv_len(c.n_mels);
-  c.F2 = conv_len(c.F1);
-  c.F3 = conv_len(c.F2);
+  // causal subsampling pads 2 before and 1 after (src/subsampling.cpp:25-46)
+  auto flen = [&](int n) { return c.causal_downsampling ? n / 2 + 1 : conv_len(n); };
+  c.F1 = flen(c.n_mels);
+  c.F2 = flen(c.F1);
+  c.F3 = flen(c.F2);
   if ((c.F3 * c.sub_channels) % 64) return "subsampling flatten width must be a multiple of 64";
   const GgufTensor* probe = g.tensor("encoder.layers.0.feed_forward1.linear1.weight");
   if (!probe) return "missing encoder.layers.0.feed_forward1.linear1.weight";
@@ -616,17 +638,23 @@ std::string pack_weights(const GgufFile& g, const Config& c, bool fold_ln, Packe
       L.dw_b = opt_vec(p + "conv.depthwise_conv.bias", d);
       if (!err.empty()) return err;
       if (!read_vec(g, p + "conv.batch_norm.weight", d, f, err) ||
-          !read_vec(g, p + "conv.batch_norm.bias", d, f2, err) ||
-          !read_vec(g, p + "conv.batch_norm.running_mean", d, f3, err) ||
-          !read_vec(g, p + "conv.batch_norm.running_var", d, f4, err))
+          !read_vec(g, p + "conv.batch_norm.bias", d, f2, err))
         return err;
-      std::vector<float> sc(d), sh(d);
-      for (int ch = 0; ch < d; ++ch) {
-        sc[ch] = f[ch] / std::sqrt(f4[ch] + 1e-5f);
-        sh[ch] = f2[ch] - f3[ch] * sc[ch];
+      if (c.conv_ln) {  // LayerNorm over channels: gamma / beta as they are
+        L.bn_scale = put_f(f);
+        L.bn_shift = put_f(f2);
+      } else {
+        if (!read_vec(g, p + "conv.batch_norm.running_mean", d, f3, err) ||
+            !read_vec(g, p + "conv.batch_norm.running_var", d, f4, err))
+          return err;
+        std::vector<float> sc(d), sh(d);
+        for (int ch = 0; ch < d; ++ch) {
+          sc[ch] = f[ch] / std::sqrt(f4[ch] + 1e-5f);
+          sh[ch] = f2[ch] - f3[ch] * sc[ch];
+        }
+        L.bn_scale = put_f(sc);
+        L.bn_shift = put_f(sh);
       }
-      L.bn_scale = put_f(sc);
-      L.bn_shift = put_f(sh);
       if (!read_f32(g, p + "conv.pointwise_conv2.weight", d, d, f, err)) return err;
       L.pw2_w = put_h(to_h(f, bf));
       L.pw2_b = opt_vec(p + "conv.pointwise_conv2.bias", d);

@@ -21,6 +21,19 @@ struct Config {
   bool xscaling = true;
   std::string att_context_style = "regular";
   bool causal_downsampling = false, conv_causal = false;
+  // cache-aware streaming (causal) models, src/model_loader.cpp:113-131
+  int att_left = -1, att_right = -1;
+  bool chunked = false;  // att_context_style chunked_limited with att_right >= 0
+  bool conv_ln = false;  // conv_norm_type layer_norm (gamma / beta under conv.batch_norm.*)
+  struct Streaming {
+    bool present = false;
+    int chunk_first = 9, chunk_main = 16;  // mel frames of the first / later chunk windows
+    int pre_cache = 9;                     // mel frames of overlap prepended to later windows
+    int drop_extra = 0;                    // subsampled frames dropped from later windows
+    int cache_len = 0;                     // attention cache (last_channel_cache_size)
+    int valid_out_len = 0;                 // frames a mid-stream chunk outputs
+  } stream;
+  bool causal() const { return causal_downsampling || conv_causal || chunked; }
   int sample_rate = 16000, n_mels = 0, n_fft = 0, win_length = 0, hop_length = 0;
   float preemph = 0.f, mag_power = 2.f, log_zero_guard = 0.f;
   std::string normalize = "per_feature";

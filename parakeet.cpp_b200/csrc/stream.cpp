@@ -1,0 +1,266 @@
+// Cache-aware streaming encoder on one device (reference: StreamingEncoder,
+// src/streaming_encoder.cpp:30-464).
+//
+// Per stream, on the device:
+//   attention cache  per layer [cache_len + Tc, d] compute-type rows: the last
+//                    cache_len normalised attention inputs, then this chunk's
+//                    (written there by the LayerNorm); the QKV GEMM reads all
+//                    cache_len + Tc rows, so K / V of the cache are projected
+//                    again each chunk exactly as the reference does
+//   conv cache       per layer [K - 1 + Tc, d]: the last K - 1 GLU outputs,
+//                    then this chunk's (written there by the GLU GEMM)
+// Both are double-buffered: the rows that become the next chunk's cache are
+// copied into the other buffer (NeMo update_cache / new_x[:, :, -LP:]), and
+// the buffers swap after the chunk.
+// Host state: the step number and the count of filled attention-cache rows
+// (cache_last_channel_len), which the attention mask reads.
+#include <algorithm>
+#include <cmath>
+
+#include "encoder.hpp"
+#include "kernels/gemm.h"
+#include "kernels/kernels.h"
+#include "status.hpp"
+
+namespace pkc {
+
+struct DeviceRunner::StreamState {
+  int step = 0;
+  int filled = 0;  // valid rows of the attention cache
+  int cur = 0;     // which cache buffer holds the live caches
+  int Tc_cap = 0, n_cap = 0;
+  int pos_Tc = -1;  // Tc the positional table was made for
+  void* kv[2] = {nullptr, nullptr};
+  void* cv[2] = {nullptr, nullptr};
+  void* scratch = nullptr;
+  size_t scratch_bytes = 0;
+  // scratch carve
+  float* mel = nullptr;
+  void *s1 = nullptr, *s2a = nullptr, *s2b = nullptr, *s3a = nullptr, *s3b = nullptr;
+  float* x = nullptr;
+  void *hbuf = nullptr, *ffh = nullptr, *qkv = nullptr, *ctx = nullptr, *pe = nullptr, *ptab = nullptr;
+};
+
+namespace {
+size_t al256(size_t x) { return (x + 255) / 256 * 256; }
+int half_up(int n) { return n / 2 + 1; }  // causal k=3, s=2 stage: pads 2 + 1
+}  // namespace
+
+DeviceRunner::StreamState* DeviceRunner::stream_create(std::string& err) {
+  const Config& c = cfg_;
+  if (!c.stream.present || !c.chunked || !c.causal_downsampling || !c.conv_causal) {
+    err = "not a cache-aware streaming model (needs parakeet.streaming.* keys, chunked_limited attention, "
+          "causal subsampling and causal conv)";
+    return nullptr;
+  }
+  for (const LayerWeights& L : w_.layers)
+    if (L.qkv_ln || L.pw1_ln || L.ff2_ln) {
+      err = "streaming needs the unfused LayerNorm weights (PKC_LN_FUSED unset)";
+      return nullptr;
+    }
+  auto* s = new StreamState();
+  std::string e;
+  if (stream_reset(*s, e) != PKC_OK) {
+    err = e;
+    stream_destroy(s);
+    return nullptr;
+  }
+  return s;
+}
+
+void DeviceRunner::stream_destroy(StreamState* s) {
+  if (!s) return;
+  for (int i = 0; i < 2; ++i) {
+    if (s->kv[i]) cudaFree(s->kv[i]);
+    if (s->cv[i]) cudaFree(s->cv[i]);
+  }
+  if (s->scratch) cudaFree(s->scratch);
+  delete s;
+}
+
+int DeviceRunner::stream_step_num(const StreamState& s) { return s.step; }
+
+pkc_status DeviceRunner::stream_reset(StreamState& s, std::string& err) {
+  cudaSetDevice(device_);
+  s.step = 0;
+  s.filled = 0;
+  s.cur = 0;
+  for (int i = 0; i < 2; ++i) {
+    if (s.kv[i]) PKC_CK(cudaMemsetAsync(s.kv[i], 0, (size_t)cfg_.n_layers * (cfg_.stream.cache_len + s.Tc_cap) * cfg_.d_model * 2, stream_), "stream cache reset");
+    if (s.cv[i]) PKC_CK(cudaMemsetAsync(s.cv[i], 0, (size_t)cfg_.n_layers * (cfg_.conv_kernel - 1 + s.Tc_cap) * cfg_.d_model * 2, stream_), "stream cache reset");
+  }
+  PKC_CK(cudaStreamSynchronize(stream_), "stream reset");
+  return PKC_OK;
+}
+
+pkc_status DeviceRunner::stream_step(StreamState& s, const float* mel, int n, bool is_last, float* out,
+                                     size_t out_cap, int* n_valid, std::string& err) {
+  const Config& c = cfg_;
+  cudaSetDevice(device_);
+  cudaStream_t st = stream_;
+  const int F = c.n_mels, C = c.sub_channels, d = c.d_model, FF = c.ff_dim, H = c.n_heads, K = c.conv_kernel;
+  const int Lc = c.n_layers, LP = K - 1, cache = c.stream.cache_len;
+  const bool bf = c.bf16;
+  *n_valid = 0;
+  if (n <= 0 || !mel) {
+    err = "empty mel window";
+    return PKC_ERR_ARG;
+  }
+  // subsampled lengths of the window (src/streaming_encoder.cpp:351-370)
+  const int T1 = half_up(n), T2 = half_up(T1), T3 = half_up(T2);
+  const int F1 = c.F1, F2 = c.F2, F3 = c.F3;
+  const int drop = s.step != 0 ? c.stream.drop_extra : 0;
+  const int Tc = T3 - drop;
+  if (Tc <= 0) {  // no output this step (a too-short tail window)
+    s.step += 1;
+    return PKC_OK;
+  }
+  const int valid = is_last ? Tc : std::min(c.stream.valid_out_len, Tc);
+  if (out_cap < (size_t)valid * d) {
+    err = "output buffer holds " + std::to_string(out_cap) + " floats, the chunk needs " + std::to_string((size_t)valid * d);
+    return PKC_ERR_ARG;
+  }
+  const int Tk = cache + Tc, P = 2 * Tk - 1;
+
+  // ---- capacity: caches keep their rows when they grow
+  if (Tc > s.Tc_cap) {
+    const int cap = std::max(Tc, 8);
+    for (int i = 0; i < 2; ++i) {
+      void *nk = nullptr, *nc = nullptr;
+      const size_t kb = (size_t)Lc * (cache + cap) * d * 2, cb = (size_t)Lc * (LP + cap) * d * 2;
+      PKC_CK(cudaMalloc(&nk, kb), "cudaMalloc of the streaming attention cache");
+      PKC_CK(cudaMalloc(&nc, cb), "cudaMalloc of the streaming conv cache");
+      PKC_CK(cudaMemsetAsync(nk, 0, kb, st), "stream cache init");
+      PKC_CK(cudaMemsetAsync(nc, 0, cb, st), "stream cache init");
+      if (s.kv[i]) {
+        PKC_CK(cudaMemcpy2DAsync(nk, (size_t)(cache + cap) * d * 2, s.kv[i], (size_t)(cache + s.Tc_cap) * d * 2,
+                                 (size_t)cache * d * 2, Lc, cudaMemcpyDeviceToDevice, st), "stream cache move");
+        PKC_CK(cudaMemcpy2DAsync(nc, (size_t)(LP + cap) * d * 2, s.cv[i], (size_t)(LP + s.Tc_cap) * d * 2,
+                                 (size_t)LP * d * 2, Lc, cudaMemcpyDeviceToDevice, st), "stream cache move");
+        PKC_CK(cudaStreamSynchronize(st), "stream cache move");
+        cudaFree(s.kv[i]);
+        cudaFree(s.cv[i]);
+      }
+      s.kv[i] = nk;
+      s.cv[i] = nc;
+    }
+    s.Tc_cap = cap;
+  }
+  const int cap = s.Tc_cap;
+  const int Tkc = std::max(cap, Tc) + cache, Pc = 2 * Tkc - 1;
+  {
+    size_t sz = 0;
+    auto take = [&](size_t b) { const size_t o = sz; sz += al256(b); return o; };
+    const size_t o_mel = take((size_t)F * n * 4), o_s1 = take((size_t)T1 * F1 * C * 2),
+                 o_s2a = take((size_t)T2 * F2 * C * 2), o_s2b = take((size_t)T2 * F2 * C * 2),
+                 o_s3a = take((size_t)T3 * F3 * C * 2), o_s3b = take((size_t)T3 * F3 * C * 2),
+                 o_x = take((size_t)T3 * d * 4), o_h = take((size_t)cap * d * 2), o_ff = take((size_t)cap * FF * 2),
+                 o_qkv = take((size_t)Tkc * 3 * d * 2), o_ctx = take((size_t)cap * d * 2), o_pe = take((size_t)Pc * d * 2),
+                 o_pt = take((size_t)Pc * Lc * d * 2);
+    if (sz > s.scratch_bytes) {
+      if (s.scratch) cudaFree(s.scratch);
+      s.scratch = nullptr;
+      s.scratch_bytes = 0;
+      PKC_CK(cudaMalloc(&s.scratch, sz), "cudaMalloc of the streaming scratch");
+      s.scratch_bytes = sz;
+      s.pos_Tc = -1;
+    }
+    uint8_t* b = static_cast<uint8_t*>(s.scratch);
+    s.mel = reinterpret_cast<float*>(b + o_mel);
+    s.s1 = b + o_s1; s.s2a = b + o_s2a; s.s2b = b + o_s2b; s.s3a = b + o_s3a; s.s3b = b + o_s3b;
+    s.x = reinterpret_cast<float*>(b + o_x);
+    s.hbuf = b + o_h; s.ffh = b + o_ff; s.qkv = b + o_qkv; s.ctx = b + o_ctx;
+    void* pe = b + o_pe;
+    void* pt = b + o_pt;
+    if (pe != s.pe || pt != s.ptab) s.pos_Tc = -1;
+    s.pe = pe;
+    s.ptab = pt;
+  }
+  sk_part_ = 0;
+  cudaGetLastError();
+
+  // ---- causal subsampling (the window is all real audio: no time mask bites)
+  PKC_CK(cudaMemcpyAsync(s.mel, mel, (size_t)F * n * 4, cudaMemcpyHostToDevice, st), "mel upload");
+  auto* s1 = static_cast<__nv_bfloat16*>(s.s1);
+  PKC_CK(causal_conv0_launch(s.mel, F, n, n, w_.c0_w, w_.c0_b, C, T1, F1, s1, st), "causal conv0");
+  PKC_CK(causal_dw_launch(s1, T1, F1, T1, w_.dw1_w, w_.dw1_b, C, T2, F2, static_cast<__nv_bfloat16*>(s.s2a), st),
+         "causal dw1");
+  PKC_ST(gemm(s.s2a, C, w_.pw1_w, C, true, T2 * F2, C, C, EPI_STORE_H, ACT_RELU, 1.f, w_.pw1_b, s.s2b, C, st,
+              "stream_sub_pw", err));
+  PKC_CK(causal_dw_launch(static_cast<const __nv_bfloat16*>(s.s2b), T2, F2, T2, w_.dw2_w, w_.dw2_b, C, T3, F3,
+                          static_cast<__nv_bfloat16*>(s.s3a), st), "causal dw2");
+  PKC_ST(gemm(s.s3a, C, w_.pw2_w, C, true, T3 * F3, C, C, EPI_STORE_H, ACT_RELU, 1.f, w_.pw2_b, s.s3b, C, st,
+              "stream_sub_pw", err));
+  const float xs = c.xscaling ? std::sqrt((float)d) : 1.f;
+  PKC_ST(gemm(s.s3b, F3 * C, w_.out_w, F3 * C, true, T3, d, F3 * C, EPI_STORE_F32, ACT_NONE, xs, w_.out_b, s.x, d,
+              st, "stream_sub_out", err));
+  float* x = s.x + (size_t)drop * d;  // drop_extra_pre_encoded leading frames
+
+  // ---- positional table over cache + chunk positions, every layer's linear_pos
+  const int Ld = Lc * d;
+  if (s.pos_Tc != Tc) {
+    PKC_CK(pos_table_launch(s.pe, Tk, d, bf, st), "pos_table");
+    PKC_ST(gemm(s.pe, d, w_.pos_all_w, d, bf, P, Ld, d, EPI_STORE_H, ACT_NONE, 1.f, nullptr, s.ptab, Ld, st,
+                "stream_pos", err, &w_.pos_all_q));
+    s.pos_Tc = Tc;
+  }
+
+  // ---- conformer layers with their caches (build_stream_layer, :98-338)
+  const size_t kv_rows = (size_t)cache + cap, cv_rows = (size_t)LP + cap;
+  for (int li = 0; li < Lc; ++li) {
+    const LayerWeights& L = w_.layers[li];
+    uint8_t* kvc = static_cast<uint8_t*>(s.kv[s.cur]) + (size_t)li * kv_rows * d * 2;
+    uint8_t* kvn = static_cast<uint8_t*>(s.kv[1 - s.cur]) + (size_t)li * kv_rows * d * 2;
+    uint8_t* cvc = static_cast<uint8_t*>(s.cv[s.cur]) + (size_t)li * cv_rows * d * 2;
+    uint8_t* cvn = static_cast<uint8_t*>(s.cv[1 - s.cur]) + (size_t)li * cv_rows * d * 2;
+    if (li == 0)
+      PKC_CK(layernorm_launch(x, Tc, d, L.ln_ff1_g, L.ln_ff1_b, s.hbuf, bf, nullptr, nullptr, false, st), "ln");
+    PKC_ST(gemm(s.hbuf, d, L.ff1_w1, d, bf, Tc, FF, d, EPI_STORE_H, ACT_SILU, 1.f, L.ff1_b1, s.ffh, FF, st,
+                "stream_ffn", err, &L.ff1_q1));
+    PKC_ST(gemm(s.ffh, FF, L.ff1_w2, FF, bf, Tc, d, FF, EPI_RESID_F32, ACT_NONE, 0.5f, L.ff1_b2, x, d, st,
+                "stream_ffn", err, &L.ff1_q2));
+    // attention input of this chunk, after the cache rows
+    PKC_CK(layernorm_launch(x, Tc, d, L.ln_att_g, L.ln_att_b, kvc + (size_t)cache * d * 2, bf, nullptr, nullptr,
+                            false, st), "ln");
+    PKC_ST(gemm(kvc, d, L.qkv_w, d, bf, Tk, 3 * d, d, EPI_STORE_H, ACT_NONE, 1.f, L.qkv_b, s.qkv, 3 * d, st,
+                "stream_qkv", err, &L.qkv_q));
+    StreamAttnArgs sa{s.qkv, static_cast<const uint8_t*>(s.ptab) + (size_t)li * d * 2, Ld, L.pos_u, L.pos_v,
+                      s.ctx, d, H, Tc, cache, s.filled, c.att_left, c.att_right};
+    PKC_CK(stream_attention_launch(sa, bf, st), "stream attention");
+    PKC_ST(gemm(s.ctx, d, L.out_w, d, bf, Tc, d, d, EPI_RESID_F32, ACT_NONE, 1.f, L.out_b, x, d, st, "stream_out",
+                err, &L.out_q));
+    // next attention cache: the last cache_len of [cache | chunk]
+    if (cache > 0)
+      PKC_CK(cudaMemcpyAsync(kvn, kvc + (size_t)Tc * d * 2, (size_t)cache * d * 2, cudaMemcpyDeviceToDevice, st),
+             "attention cache update");
+    // conv module: GLU rows after the conv cache, causal depthwise over both
+    PKC_CK(layernorm_launch(x, Tc, d, L.ln_conv_g, L.ln_conv_b, s.hbuf, bf, nullptr, nullptr, false, st), "ln");
+    PKC_ST(gemm(s.hbuf, d, L.pw1_w, d, bf, Tc, 2 * d, d, EPI_GLU_H, ACT_NONE, 1.f, L.pw1_b, cvc + (size_t)LP * d * 2,
+                d, st, "stream_pw1_glu", err));
+    if (LP > 0)
+      PKC_CK(cudaMemcpyAsync(cvn, cvc + (size_t)Tc * d * 2, (size_t)LP * d * 2, cudaMemcpyDeviceToDevice, st),
+             "conv cache update");
+    PKC_CK(stream_dwconv_launch(cvc, s.hbuf, Tc, d, K, L.dw_w, L.dw_b, L.bn_scale, L.bn_shift, c.conv_ln, bf, st),
+           "stream dwconv");
+    PKC_ST(gemm(s.hbuf, d, L.pw2_w, d, bf, Tc, d, d, EPI_RESID_F32, ACT_NONE, 1.f, L.pw2_b, x, d, st, "stream_pw2",
+                err));
+    PKC_CK(layernorm_launch(x, Tc, d, L.ln_ff2_g, L.ln_ff2_b, s.hbuf, bf, nullptr, nullptr, false, st), "ln");
+    PKC_ST(gemm(s.hbuf, d, L.ff2_w1, d, bf, Tc, FF, d, EPI_STORE_H, ACT_SILU, 1.f, L.ff2_b1, s.ffh, FF, st,
+                "stream_ffn", err, &L.ff2_q1));
+    PKC_ST(gemm(s.ffh, FF, L.ff2_w2, FF, bf, Tc, d, FF, EPI_RESID_F32, ACT_NONE, 0.5f, L.ff2_b2, x, d, st,
+                "stream_ffn", err, &L.ff2_q2));
+    const bool last = li + 1 == Lc;
+    const LayerWeights* N = last ? nullptr : &w_.layers[li + 1];
+    PKC_CK(layernorm_launch(x, Tc, d, L.ln_out_g, L.ln_out_b, last ? nullptr : s.hbuf, bf,
+                            last ? nullptr : N->ln_ff1_g, last ? nullptr : N->ln_ff1_b, true, st), "ln");
+  }
+  PKC_CK(cudaMemcpyAsync(out, x, (size_t)valid * d * 4, cudaMemcpyDeviceToHost, st), "stream output download");
+  PKC_ST(finish(st, err));
+  s.cur = 1 - s.cur;
+  s.filled = std::min(cache, s.filled + Tc);
+  s.step += 1;
+  *n_valid = valid;
+  return PKC_OK;
+}
+
+}  // namespace pkc

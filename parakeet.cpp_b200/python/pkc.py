@@ -50,6 +50,11 @@ class ModelInfo(ctypes.Structure):
     ]
 
 
+class StreamSchedule(ctypes.Structure):
+    _fields_ = [(n, c_int) for n in ("chunk_size_first", "chunk_size", "pre_encode_cache_size", "valid_out_len",
+                                     "drop_extra_pre_encoded", "attention_cache_size")]
+
+
 class Token(ctypes.Structure):
     """pkc_token: the reference's TokenInfo (src/decode_types.hpp:27)."""
     _fields_ = [("id", ctypes.c_int32), ("frame", ctypes.c_int32), ("conf", c_float), ("span", ctypes.c_int32)]
@@ -88,6 +93,12 @@ def _declare(L):
         ("pkc_model_open", c_int, c_char_p, POINTER(c_int), c_int, POINTER(c_void_p)),
         ("pkc_model_close", None, c_void_p),
         ("pkc_model_load_stats", c_int, c_void_p, POINTER(ctypes.c_double), POINTER(ctypes.c_double), POINTER(c_int)),
+        ("pkc_stream_schedule_get", c_int, c_void_p, POINTER(StreamSchedule)),
+        ("pkc_stream_begin", c_int, c_void_p, c_int, POINTER(c_void_p)),
+        ("pkc_stream_reset", c_int, c_void_p),
+        ("pkc_stream_step", c_int, c_void_p, c_void_p, c_int, c_int, c_void_p, c_size_t, POINTER(c_int)),
+        ("pkc_stream_step_num", c_int, c_void_p),
+        ("pkc_stream_free", None, c_void_p),
         ("pkc_pack_cache_build", c_int, c_char_p, c_char_p, ctypes.c_char_p, c_int),
         ("pkc_model_info_get", c_int, c_void_p, POINTER(ModelInfo)),
         ("pkc_mel_frames", c_int, c_void_p, c_int),
@@ -222,6 +233,12 @@ class Model:
         info = ModelInfo()
         _check(L.pkc_model_info_get(h, ctypes.byref(info)), h)
         self.info = info
+
+    def stream_schedule(self):
+        """pkc_stream_schedule_get as a dict."""
+        o = StreamSchedule()
+        _check(lib().pkc_stream_schedule_get(self._h, ctypes.byref(o)), self._h)
+        return {n: getattr(o, n) for n, _ in StreamSchedule._fields_}
 
     def load_stats(self):
         """pkc_model_load_stats: {"pack_s", "upload_s", "from_cache"} of this open."""
@@ -386,3 +403,45 @@ def _split(flat, vt, d, layout):
         outs.append(blk.reshape(d, t) if layout == LAYOUT_CHANNELS_FIRST else blk.reshape(t, d))
         off += t * d
     return outs
+
+
+class Stream:
+    """A cache-aware streaming encoder session (pkc_stream_*, the reference's
+    StreamingEncoder)."""
+
+    def __init__(self, model: "Model", device_slot: int = 0):
+        self.model = model
+        h = c_void_p()
+        _check(lib().pkc_stream_begin(model.handle, device_slot, ctypes.byref(h)), model.handle)
+        self._h = h
+        self.d = model.info.d_model
+
+    def step(self, mel_window, is_last: bool = False) -> np.ndarray:
+        """One window [n_mels, n] (feature-major, overlap included) -> the
+        chunk's valid frames [valid, d_model]."""
+        mel = np.ascontiguousarray(mel_window, dtype=np.float32)
+        n = mel.shape[1]
+        cap = (n // 8 + 2) * self.d
+        out = np.empty(cap, dtype=np.float32)
+        nv = c_int()
+        _check(lib().pkc_stream_step(self._h, mel.ctypes.data, n, 1 if is_last else 0, out.ctypes.data, cap,
+                                     ctypes.byref(nv)), self.model.handle)
+        return out[: nv.value * self.d].reshape(nv.value, self.d).copy()
+
+    def reset(self):
+        _check(lib().pkc_stream_reset(self._h), self.model.handle)
+
+    @property
+    def step_num(self) -> int:
+        return lib().pkc_stream_step_num(self._h)
+
+    def close(self):
+        if getattr(self, "_h", None):
+            lib().pkc_stream_free(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -42,6 +42,7 @@ class ModelCfg:
     pred_hidden: int = 640
     joint_hidden: int = 640
     pred_layers: int = 1
+    streaming: bool = False     # cache-aware streaming (causal) FastConformer
     durations: tuple = ()
     dtype: str = "f32"          # f32 | f16 | bf16 | q8_0 | q4_k
     biases: bool = False
@@ -55,6 +56,8 @@ class ModelCfg:
         items = asdict(self)
         if items["pred_layers"] == 1:  # keeps the names of files made before the field existed
             del items["pred_layers"]
+        if not items["streaming"]:
+            del items["streaming"]
         h = hashlib.sha1(repr(sorted(items.items())).encode()).hexdigest()[:12]
         return f"{self.name}_{self.dtype}_{h}"
 
@@ -70,6 +73,13 @@ CONFIGS = {
                             durations=(0, 1, 2, 3, 4), dtype="q4_k"),
     "c5_0.6b_bf16_long": ModelCfg("c5_0.6b_bf16_long", "tdt", 1024, 24, 8, 4096, 9, 128,
                                   vocab=8192, durations=(0, 1, 2, 3, 4), dtype="bf16"),
+}
+
+# The cache-aware streaming model class of the reference (parakeet_realtime_eou_120m:
+# 17 layers, d 512, causal subsampling, chunked-limited attention, layer_norm conv norm).
+STREAM_CONFIGS = {
+    "eou_120m_stream": ModelCfg("eou_120m_stream", "rnnt", 512, 17, 8, 2048, 9, 128, vocab=1026,
+                                dtype="f16", biases=True, streaming=True),
 }
 
 # Batch part of each configuration: (batch, min_s, max_s) with lengths U(min,max).
@@ -184,8 +194,8 @@ def model_tensors(cfg: ModelCfg):
     d, C, H = cfg.d_model, cfg.sub_channels, cfg.n_heads
     dk = d // H
     F3 = cfg.n_mels
-    for _ in range(3):
-        F3 = (F3 - 1) // 2 + 1
+    for _ in range(3):  # causal subsampling pads 2 + 1, offline 1 + 1
+        F3 = F3 // 2 + 1 if cfg.streaming else (F3 - 1) // 2 + 1
     nb = cfg.n_fft // 2 + 1
     yield "preprocessor.featurizer.fb", slaney_mel_fb(SR, cfg.n_fft, cfg.n_mels)[None]
     yield "preprocessor.featurizer.window", hann_symmetric(cfg.win_length)
@@ -226,10 +236,14 @@ def model_tensors(cfg: ModelCfg):
         yield p + "conv.depthwise_conv.weight", nrm(d, 1, cfg.conv_kernel)
         if cfg.biases:
             yield p + "conv.depthwise_conv.bias", nrm(d)
-        yield p + "conv.batch_norm.weight", ones(d)
-        yield p + "conv.batch_norm.bias", zeros(d)
-        yield p + "conv.batch_norm.running_mean", zeros(d)
-        yield p + "conv.batch_norm.running_var", ones(d)
+        if cfg.streaming:  # conv_norm_type layer_norm: gamma / beta under the batch_norm names
+            yield p + "conv.batch_norm.weight", ones(d) + nrm(d) * np.float32(10.0)
+            yield p + "conv.batch_norm.bias", nrm(d) * np.float32(10.0)
+        else:
+            yield p + "conv.batch_norm.weight", ones(d)
+            yield p + "conv.batch_norm.bias", zeros(d)
+            yield p + "conv.batch_norm.running_mean", zeros(d)
+            yield p + "conv.batch_norm.running_var", ones(d)
         yield p + "conv.pointwise_conv2.weight", nrm(d, d, 1)
         if cfg.biases:
             yield p + "conv.pointwise_conv2.bias", nrm(d)
@@ -266,7 +280,21 @@ def write_gguf(cfg: ModelCfg, path: str) -> str:
     w.add_uint32("parakeet.encoder.n_heads", cfg.n_heads)
     w.add_uint32("parakeet.encoder.ff_dim", cfg.ff_dim)
     w.add_uint32("parakeet.encoder.conv_kernel", cfg.conv_kernel)
-    w.add_string("parakeet.encoder.conv_norm_type", "batch_norm")
+    w.add_string("parakeet.encoder.conv_norm_type", "layer_norm" if cfg.streaming else "batch_norm")
+    if cfg.streaming:
+        # the cache-aware schedule of the 120M EOU streaming model (att_context_size [70, 1])
+        w.add_string("parakeet.encoder.att_context_style", "chunked_limited")
+        w.add_int32("parakeet.encoder.att_context_left", 70)
+        w.add_int32("parakeet.encoder.att_context_right", 1)
+        w.add_bool("parakeet.encoder.causal_downsampling", True)
+        w.add_bool("parakeet.encoder.conv_causal", True)
+        w.add_array("parakeet.streaming.chunk_size", [9, 16])
+        w.add_array("parakeet.streaming.shift_size", [9, 16])
+        w.add_array("parakeet.streaming.pre_encode_cache_size", [0, 9])
+        w.add_int32("parakeet.streaming.cache_drop_size", 0)
+        w.add_int32("parakeet.streaming.last_channel_cache_size", 70)
+        w.add_int32("parakeet.streaming.valid_out_len", 2)
+        w.add_int32("parakeet.streaming.drop_extra_pre_encoded", 2)
     w.add_uint32("parakeet.encoder.subsampling_factor", 8)
     w.add_uint32("parakeet.encoder.subsampling_conv_channels", cfg.sub_channels)
     w.add_bool("parakeet.encoder.xscaling", cfg.xscaling)
@@ -331,7 +359,7 @@ def ensure_gguf(cfg: ModelCfg, cache_dir: str | None = None) -> str:
 
 def small_cfg(base: str = "c2_0.6b_f16", **over) -> ModelCfg:
     """A reduced copy of a configuration for fast parity runs."""
-    c = CONFIGS[base]
+    c = CONFIGS[base] if base in CONFIGS else STREAM_CONFIGS[base]
     d = asdict(c)
     d.update(over)
     d["name"] = d.get("name", c.name) + "_small"

@@ -68,7 +68,7 @@ def test_open_bad_magic_is_format_error(tmp_path):
     assert st == 3
 
 
-def test_streaming_model_is_unsupported(tmp_path):
+def test_unknown_attention_style_is_unsupported(tmp_path):
     import gguf
     w = gguf.GGUFWriter(str(tmp_path / "s.gguf"), "parakeet")
     for k, v in (("parakeet.encoder.d_model", 256), ("parakeet.encoder.n_layers", 1),
@@ -78,11 +78,25 @@ def test_streaming_model_is_unsupported(tmp_path):
                  ("parakeet.preprocessor.n_fft", 512), ("parakeet.preprocessor.win_length", 400),
                  ("parakeet.preprocessor.hop_length", 160), ("parakeet.vocab_size", 16)):
         w.add_uint32(k, v)
-    w.add_string("parakeet.encoder.att_context_style", "chunked_limited")
+    w.add_string("parakeet.encoder.att_context_style", "chunked_limited_with_rc")
     w.add_tensor("encoder.layers.0.feed_forward1.linear1.weight", np.zeros((256, 256), np.float32))
     w.write_header_to_file(); w.write_kv_data_to_file(); w.write_tensors_to_file(); w.close()
     st, msg = _open_status(str(tmp_path / "s.gguf"))
-    assert st == 4 and "streaming" in msg
+    assert st == 4 and "att_context_style" in msg
+
+
+def test_streaming_model_config_is_accepted(tmp_path):
+    """A cache-aware streaming model (chunked-limited attention, causal
+    subsampling and conv, layer_norm conv norm, parakeet.streaming.* schedule)
+    passes config validation: without a GPU the open stops at device selection."""
+    import synth
+    import torch
+    if torch.cuda.is_available():
+        pytest.skip("covered by the GPU streaming tests")
+    cfg = synth.small_cfg("eou_120m_stream", n_layers=1, d_model=256, n_heads=4, ff_dim=256, n_mels=64,
+                          vocab=16, pred_hidden=16, joint_hidden=16)
+    st, msg = _open_status(synth.ensure_gguf(cfg, str(tmp_path)))
+    assert st == 5 and "CUDA" in msg
 
 
 def test_valid_model_reaches_device_selection(tiny_gguf):

@@ -150,3 +150,28 @@ def test_q4_k_quantiser_matches_gguf_dequant():
     step = (x.reshape(-1, 32).max(1) - np.minimum(x.reshape(-1, 32).min(1), 0)) / 15
     err = np.abs(back - x).reshape(-1, 32).max(1)
     assert np.all(err <= step * 0.75 + 1e-4)
+
+
+@pytest.mark.parametrize("T", [150, 1201])
+def test_streaming_oracle_equals_offline_causal(tmp_path, T):
+    """Cache-aware equivalence (tests/test_streaming_encoder.cpp of the
+    reference): the streaming restatement fed the model's chunk schedule gives
+    the offline causal encoder's output on every frame but the final chunk's
+    valid_out_len tail. 1201 mel frames (151 output frames) run the 70-frame
+    attention cache past full, so its roll and the chunked-limited left
+    context are exercised."""
+    import synth
+    import oracle
+    cfg = synth.small_cfg("eou_120m_stream", n_layers=2, d_model=128, n_heads=4, ff_dim=256, n_mels=64,
+                          sub_channels=32, vocab=16, pred_hidden=16, joint_hidden=16)
+    w = oracle.Weights(synth.ensure_gguf(cfg, str(tmp_path)))
+    sc = oracle.StreamCfg(w)
+    assert sc.chunked and sc.causal_sub and sc.conv_causal and sc.conv_norm == "layer_norm"
+    mel = np.random.default_rng(T).standard_normal((64, T))
+    off = oracle.encode_causal_offline(w, mel)
+    enc = oracle.StreamingEncoder(w)
+    st = np.concatenate([enc.step(mel[:, lo:hi], last) for lo, hi, last in oracle.stream_schedule(sc, T)])
+    assert st.shape == off.shape
+    m = len(st) - sc.valid_out_len
+    assert np.abs(st[:m] - off[:m]).max() <= 1e-12 * np.abs(off[:m]).max()
+    assert np.abs(st[m:] - off[m:]).max() > 1e-6   # the tail differs by design
