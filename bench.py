@@ -408,11 +408,176 @@ def cpu_baseline(args, path, pcm):
                       f"encoder = numpy float64 restatement, mel = parakeet.cpp MelFrontend (oracle/_ref)"}
 
 
+# ----------------------------------------------------------------- streaming
+
+def stream_windows(sch, T):
+    """The model's chunk schedule over T mel frames: (lo, hi, is_last)."""
+    out, idx, first = [], 0, True
+    while idx < T:
+        size = sch["chunk_size_first"] if first else sch["chunk_size"]
+        hi = min(idx + size, T)
+        lo = idx if first else max(0, idx - sch["pre_encode_cache_size"])
+        out.append((lo, hi, hi >= T))
+        idx += size
+        first = False
+    return out
+
+
+def stream_launches(cfg, n_windows, n_tc_changes):
+    """Kernels of one stream: per chunk 6 subsampling launches, 14 per layer
+    and the first layer's LayerNorm; the positional table and every layer's
+    linear_pos (2) when the chunk length changes."""
+    return n_windows * (6 + 14 * cfg.n_layers + 1) + 2 * n_tc_changes
+
+
+def run_stream(args, rank, world, local_rank):
+    """Cache-aware streaming encoder (pkc_stream_*): one stream of
+    args.stream_seconds of synthetic log-mel per GPU, fed window by window.
+    A step is the whole stream; value = audio seconds / device seconds."""
+    import numpy as np
+    import torch
+    import pkc
+    import synth
+    if world > 1:
+        raise SystemExit("the streaming bench runs on one GPU (one stream per process)")
+    cfg = synth.STREAM_CONFIGS[args.config]
+    path = synth.ensure_gguf(cfg)
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    model = pkc.Model(path, devices=(local_rank,))
+    sch = model.stream_schedule()
+    d = model.info.d_model
+    seconds = args.stream_seconds
+    T = int(round(seconds * SR / cfg.hop_length))
+    mel = np.random.default_rng(7).standard_normal((cfg.n_mels, T)).astype(np.float32)
+    wins = stream_windows(sch, T)
+    win_mel = [np.ascontiguousarray(mel[:, lo:hi]) for lo, hi, _ in wins]
+    s = pkc.Stream(model)
+    ext = torch.cuda.ExternalStream(model.stream(0), device=dev)
+
+    def one_stream(lat=None):
+        s.reset()
+        frames = 0
+        for (lo, hi, last), wm in zip(wins, win_mel):
+            t = time.perf_counter()
+            o = s.step(wm, last)
+            if lat is not None:
+                lat.append((time.perf_counter() - t) * 1e3)
+            frames += o.shape[0]
+        return frames
+
+    for _ in range(args.warmup):
+        frames = one_stream()
+    lat = []
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local_rank) as clk:
+        t0 = time.perf_counter()
+        ev0.record(ext)
+        for _ in range(args.steps):
+            one_stream(lat)
+        ev1.record(ext)
+        torch.cuda.synchronize(dev)
+        wall = time.perf_counter() - t0
+    dev_ms = ev0.elapsed_time(ev1)
+    s.close()
+    audio = seconds * args.steps
+    lat = sorted(lat)
+    pct = lambda q: round(lat[min(len(lat) - 1, int(q * len(lat)))], 3)
+    # roofline: one chunk reads every encoder weight once (f16: 2 bytes a parameter)
+    n_params = sum(int(np.prod(a.shape)) for n, a in synth.model_tensors(cfg) if n.startswith("encoder."))
+    wbytes = 2 * n_params
+    per_chunk_s = dev_ms / 1e3 / (args.steps * len(wins))
+    peaks, peak_src = load_peaks()
+    hbm = peaks.get("hbm_gbs")
+    achieved = wbytes / per_chunk_s / 1e9
+    n_tc = 2 if len(wins) > 1 else 1
+    line = {
+        "metric": "cache-aware streaming encoder RTFx (audio-s/s of one stream) and per-chunk latency",
+        "value": round(audio / (dev_ms / 1e3), 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(dev_ms / args.steps, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": cfg.dtype if cfg.dtype in ("f16", "bf16") else "f16",
+        "data": "synthetic log-mel (seeded N(0,1) features), random-init weights of the model class",
+        "config": {"workload": f"{args.config}: {cfg.n_layers}-layer d{d} causal FastConformer, one stream of "
+                               f"{seconds:g} s ({T} mel frames) in {len(wins)} windows "
+                               f"({sch['chunk_size_first']}, then {sch['pre_encode_cache_size']} + {sch['chunk_size']} mel frames)",
+                   "schedule": sch, "l2": "weights (2 bytes x {:.0f} M) exceed L2; no flush".format(n_params / 1e6)},
+        "chunk_latency_ms": {"p50": pct(0.5), "p90": pct(0.9), "p99": pct(0.99), "max": round(lat[-1], 3),
+                             "chunks": len(lat), "audio_ms_per_chunk": round(1e3 * sch["chunk_size"] * cfg.hop_length / SR, 1),
+                             "api": "pkc_stream_step (host mel window in, host frames out, synchronous)"},
+        "e2e": {"value": round(audio / wall, 1), "unit": UNIT,
+                "h2d_bytes_per_step": int(sum(w.nbytes for w in win_mel)),
+                "d2h_bytes_per_step": int(frames * d * 4), "api": "pkc_stream_step"},
+        "gpu_launches": int(stream_launches(cfg, len(wins), n_tc) * args.steps),
+        "roofline": {"bound": "hbm", "kernel": "one chunk through every layer (each weight read once)",
+                     "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+                     "frac": round(achieved / hbm, 3) if hbm else None, "traffic": None,
+                     "peak_source": f"{peak_src} hbm_gbs",
+                     "note": "latency-bound: a chunk is 2 frames, so its cost is launches and dependent "
+                             "small GEMMs, not bytes"},
+        "clocks": clk.summary(),
+    }
+    if not args.no_cpu_baseline:
+        import oracle
+        w = oracle.Weights(path)
+        enc = oracle.StreamingEncoder(w)
+        n_cpu = min(len(wins), 8)
+        t0 = time.perf_counter()
+        for (lo, hi, last), wm in list(zip(wins, win_mel))[:n_cpu]:
+            enc.step(wm, False)
+        dt = time.perf_counter() - t0
+        audio_cpu = n_cpu * sch["chunk_size"] * cfg.hop_length / SR
+        line["cpu_baseline"] = {"value": round(audio_cpu / dt, 3), "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+                                "sample": f"the first {n_cpu} windows of the stream through the numpy float64 "
+                                          "restatement of StreamingEncoder::step"}
+    model.close()
+    return line
+
+
+def run_reference_stream(args):
+    """Reference arm of the streaming configurations: the numpy float64
+    restatement of StreamingEncoder::step (ggml absent, so the reference's own
+    streaming graph cannot run here), a bounded prefix of the same stream."""
+    import numpy as np
+    import oracle
+    import synth
+    cfg = synth.STREAM_CONFIGS[args.config]
+    path = synth.ensure_gguf(cfg)
+    w = oracle.Weights(path)
+    sc = oracle.StreamCfg(w)
+    T = int(round(args.stream_seconds * SR / cfg.hop_length))
+    mel = np.random.default_rng(7).standard_normal((cfg.n_mels, T)).astype(np.float32)
+    wins = oracle.stream_schedule(sc, T)[:8]
+    audio = len(wins) * sc.chunk_main * cfg.hop_length / SR
+    enc = oracle.StreamingEncoder(w)
+    for _ in range(args.warmup):
+        enc.reset()
+        for lo, hi, last in wins:
+            enc.step(mel[:, lo:hi], False)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        enc.reset()
+        for lo, hi, last in wins:
+            enc.step(mel[:, lo:hi], False)
+    dt = time.perf_counter() - t0
+    v = audio * args.steps / dt
+    return {"metric": "cache-aware streaming encoder RTFx (audio-s/s of one stream) and per-chunk latency",
+            "value": round(v, 3), "unit": UNIT, "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(dt / args.steps * 1e3, 1), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f64", "impl": "reference", "data": "synthetic",
+            "config": {"workload": f"{args.config} (bounded CPU sample)", "sample": f"first {len(wins)} windows per step"},
+            "cpu_baseline": {"value": round(v, 3), "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
+                             "sample": f"first {len(wins)} windows of the stream per step; numpy float64 restatement"},
+            "e2e": {"value": round(v, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return None
     import oracle
     import synth
+    if args.config in synth.STREAM_CONFIGS:
+        return run_reference_stream(args)
     cfg = synth.CONFIGS[args.config]
     path = synth.ensure_gguf(cfg)
     pcm, winfo = workload(args.config, 0, args.batch)
@@ -448,6 +613,8 @@ def main():
     ap.add_argument("--config", default=DEFAULT_CONFIG)
     ap.add_argument("--batch", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--stream-seconds", type=float, default=20.0,
+                    help="audio per stream for the streaming configurations")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
     world = env_int("WORLD_SIZE", 1)
@@ -466,7 +633,11 @@ def main():
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
                                 device_id=torch.device("cuda", local_rank))
     try:
-        line = run_ours(args, rank, world, local_rank)
+        import synth
+        if args.config in synth.STREAM_CONFIGS:
+            line = run_stream(args, rank, world, local_rank)
+        else:
+            line = run_ours(args, rank, world, local_rank)
     finally:
         if world > 1:
             import torch.distributed as dist

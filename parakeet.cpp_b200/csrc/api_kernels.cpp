@@ -73,6 +73,7 @@ extern "C" pkc_status pkc_gemm(const void* A, int lda, const void* Bw, int ldb, 
   a.M = M; a.N = N; a.K = K;
   a.epi = epi; a.act = act; a.alpha = alpha; a.bias = bias;
   a.out = out; a.ldo = ldo; a.err = err;
+  a.skinny = 1;  // M <= 16: the skinny kernel
   SplitKScratch sks;
   if (!sks.attach(a, dev, st)) return pkc::set_thread_error(PKC_ERR_OOM, "pkc_gemm: workspace allocation failed");
   cudaError_t e = pkc::gemm_launch(A, lda, Bw, ldb, dtype == 1, a, st);

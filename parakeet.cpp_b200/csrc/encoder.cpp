@@ -279,6 +279,7 @@ pkc_status DeviceRunner::gemm(const void* A, int lda, const void* B, int ldb, bo
   GemmArgs a{};
   a.M = M; a.N = N; a.K = K; a.epi = epi; a.act = act; a.alpha = alpha; a.bias = bias;
   a.out = out; a.ldo = ldo; a.err = err_word_; a.stats = stats;
+  a.skinny = skinny_ok_ ? 1 : 0;
   // the part being issued owns one half of the stream-K workspace
   a.sk_ws = sk_ws_ + (size_t)sk_part_ * (gemm_sk_ws_bytes(sk_pairs_) / sizeof(float));
   a.sk_flags = sk_flags_ + (size_t)sk_part_ * gemm_sk_flag_count(sk_pairs_);

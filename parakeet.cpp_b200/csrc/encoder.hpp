@@ -119,6 +119,7 @@ class DeviceRunner {
   };
   pkc_status run_layer(const Plan& p, int li, const Part& q, cudaStream_t st, std::string& err);
   pkc_status finish(cudaStream_t st, std::string& err);
+  pkc_status stream_issue(StreamState& s, int n, int Tc, int drop, std::string& err);
   bool ensure_ws(size_t bytes);
   void prof_begin(cudaStream_t st);
   void prof_end(cudaStream_t st, const char* name, double flops, double bytes);
@@ -155,6 +156,7 @@ class DeviceRunner {
   cudaEvent_t ev_fork_ = nullptr, ev_join_ = nullptr;
   bool sub_unfused_ = false;
   bool ln_unfused_ = false;
+  bool skinny_ok_ = false;  // the streaming step issues M <= 16 GEMMs as skinny kernels
   double upload_s_ = 0;
   int* h_tables_ = nullptr;  // pinned staging for the item tables
   size_t h_tables_cap_ = 0;

@@ -1432,9 +1432,152 @@ int gemm_tile_n() { return BN; }
 int gemm_tile_k() { return BK; }
 int gemm_tile_m() { return BM; }
 
+// ---------------------------------------------------------------- skinny GEMM
+// M <= SKINNY_M rows (the streaming encoder's chunks, a few frames): a
+// 128-row tcgen05 tile would leave the tensor cores almost idle and walk K
+// through one CTA per 256 columns, so instead every SM streams a slice of the
+// weight once: one warp per weight row (per value/gate row pair for GLU),
+// 16-byte loads along K, the M rows of A staged in shared memory, f32
+// accumulation, a warp reduction and the same epilogues as the tcgen05 GEMM.
+constexpr int SKINNY_M = 16;
+constexpr int SKINNY_THREADS = 256;
+constexpr int SKINNY_WARPS = SKINNY_THREADS / 32;
+
+template <typename H>
+__device__ __forceinline__ void h8_to_f(const uint4& v, float (&f)[8]) {
+  const H* h = reinterpret_cast<const H*>(&v);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    if constexpr (std::is_same<H, __half>::value) f[i] = __half2float(h[i]);
+    else f[i] = __bfloat162float(h[i]);
+  }
+}
+
+template <typename H, int EPI>
+__global__ void __launch_bounds__(SKINNY_THREADS) k_gemm_skinny(const H* __restrict__ A, int lda,
+                                                                const H* __restrict__ B, int ldb, GemmArgs args) {
+  extern __shared__ uint4 sk_a[];  // A rows [M][K / 8] chunks of 8
+  constexpr bool PAIRED = EPI == EPI_GLU_H;
+  pdl_wait();
+  const int M = args.M, k8 = args.K / 8;
+  for (int e = threadIdx.x; e < M * k8; e += SKINNY_THREADS) {
+    const int m = e / k8, c = e - m * k8;
+    sk_a[e] = __ldg(reinterpret_cast<const uint4*>(A + (size_t)m * lda) + c);
+  }
+  __syncthreads();
+  pdl_trigger();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int units = PAIRED ? args.N / 2 : args.N;
+  for (int u = blockIdx.x * SKINNY_WARPS + warp; u < units; u += gridDim.x * SKINNY_WARPS) {
+    // GLU: value row blk * BN + c and its gate row BN / 2 later, output column u
+    const int na = PAIRED ? (u / (BN / 2)) * BN + u % (BN / 2) : u;
+    const int ng = na + BN / 2;
+    const uint4* wa = reinterpret_cast<const uint4*>(B + (size_t)na * ldb);
+    const uint4* wg = reinterpret_cast<const uint4*>(B + (size_t)(PAIRED ? ng : na) * ldb);
+    float acc[SKINNY_M], accg[SKINNY_M];
+#pragma unroll
+    for (int m = 0; m < SKINNY_M; ++m) acc[m] = accg[m] = 0.f;
+#pragma unroll 2
+    for (int c = lane; c < k8; c += 32) {
+      float fa[8], fg[8];
+      h8_to_f<H>(__ldg(wa + c), fa);
+      if constexpr (PAIRED) h8_to_f<H>(__ldg(wg + c), fg);
+#pragma unroll
+      for (int m = 0; m < SKINNY_M; ++m) {
+        if (m < M) {
+          float fx[8];
+          h8_to_f<H>(sk_a[m * k8 + c], fx);
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            acc[m] = fmaf(fa[i], fx[i], acc[m]);
+            if constexpr (PAIRED) accg[m] = fmaf(fg[i], fx[i], accg[m]);
+          }
+        }
+      }
+    }
+    // row m's sum ends in lane m
+    float mine = 0.f, mineg = 0.f;
+#pragma unroll
+    for (int m = 0; m < SKINNY_M; ++m) {
+      if (m < M) {
+        float v = acc[m], g = accg[m];
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          v += __shfl_xor_sync(0xffffffffu, v, o);
+          if constexpr (PAIRED) g += __shfl_xor_sync(0xffffffffu, g, o);
+        }
+        if (lane == m) {
+          mine = v;
+          mineg = g;
+        }
+      }
+    }
+    if (lane < M) {
+      const size_t ro = (size_t)lane * args.ldo + u;
+      const float b = args.bias ? args.bias[na] : 0.f;
+      if constexpr (EPI == EPI_RESID_F32) {
+        float* o = reinterpret_cast<float*>(args.out) + ro;
+        *o += args.alpha * (mine + b);
+      } else if constexpr (EPI == EPI_STORE_F32) {
+        reinterpret_cast<float*>(args.out)[ro] = args.alpha * (mine + b);
+      } else if constexpr (EPI == EPI_GLU_H) {
+        const float bg = args.bias ? args.bias[ng] : 0.f;
+        const float v = (mine + b) * sigmoidf_(mineg + bg);
+        reinterpret_cast<H*>(args.out)[ro] = std::is_same<H, __half>::value ? H(__float2half_rn(v)) : H(__float2bfloat16_rn(v));
+      } else {
+        float v = mine + b;
+        if (args.act == ACT_SILU) v = siluf_(v);
+        else if (args.act == ACT_RELU) v = fmaxf(v, 0.f);
+        reinterpret_cast<H*>(args.out)[ro] = std::is_same<H, __half>::value ? H(__float2half_rn(v)) : H(__float2bfloat16_rn(v));
+      }
+    }
+  }
+}
+
+bool gemm_skinny_enabled() {
+  static const bool on = [] {
+    const char* e = getenv("PKC_GEMM_SKINNY");
+    return !(e && e[0] == '0');
+  }();
+  return on;
+}
+
+template <typename H, int EPI>
+cudaError_t launch_skinny(const void* A, int lda, const void* B, int ldb, const GemmArgs& args, cudaStream_t st) {
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  const size_t smem = (size_t)args.M * args.K * sizeof(H);
+  const int units = EPI == EPI_GLU_H ? args.N / 2 : args.N;
+  const int grid = std::max(1, std::min((units + SKINNY_WARPS - 1) / SKINNY_WARPS, 2 * sms));
+  cudaError_t e = cudaFuncSetAttribute(k_gemm_skinny<H, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(k_gemm_skinny<H, EPI>, dim3(grid), dim3(SKINNY_THREADS), smem, st, static_cast<const H*>(A), lda,
+                    static_cast<const H*>(B), ldb, args);
+}
+
 cudaError_t gemm_launch(const void* A, int lda, const void* B, int ldb, bool bf16,
                         const GemmArgs& args, cudaStream_t st) {
   if (args.M <= 0) return cudaSuccess;
+  if (args.skinny && args.M <= SKINNY_M && !args.stats && args.N % BN == 0 && args.K % 8 == 0 && args.K <= 4096 && lda % 8 == 0 &&
+      ldb % 8 == 0 && !(reinterpret_cast<uintptr_t>(A) & 15) && !(reinterpret_cast<uintptr_t>(B) & 15) &&
+      args.epi != EPI_POWER_F32 && gemm_skinny_enabled()) {
+    switch (args.epi) {
+#define PKC_SKINNY_CASE(E) \
+  case E:                  \
+    return bf16 ? launch_skinny<__nv_bfloat16, E>(A, lda, B, ldb, args, st) : launch_skinny<__half, E>(A, lda, B, ldb, args, st);
+      PKC_SKINNY_CASE(EPI_STORE_H)
+      PKC_SKINNY_CASE(EPI_RESID_F32)
+      PKC_SKINNY_CASE(EPI_STORE_F32)
+      PKC_SKINNY_CASE(EPI_GLU_H)
+#undef PKC_SKINNY_CASE
+      default:
+        break;
+    }
+  }
   if (args.N % BN != 0 || args.K % BK != 0 || args.K <= 0 || (lda % 8) != 0 || (ldb % 8) != 0 ||
       (reinterpret_cast<uintptr_t>(A) & 15) || (reinterpret_cast<uintptr_t>(B) & 15) ||
       (reinterpret_cast<uintptr_t>(args.bias) & 15) || (reinterpret_cast<uintptr_t>(args.out) & 15) ||

@@ -36,6 +36,11 @@ struct GemmArgs {
   float* sk_ws;
   int* sk_flags;
   int sk_pairs;       // CTA pairs the workspace has room for
+  // nonzero: M <= 16 may run the CUDA-core skinny kernel (16-bit weights, no
+  // stats) instead of a 128-row tcgen05 tile. Its f32 sums run in another
+  // order, so callers whose output must not depend on the batch composition
+  // (the offline encoder) leave it 0.
+  int skinny;
 };
 
 // Stream-K workspace sizes for `pairs` CTA pairs (a device's SMs / 2).

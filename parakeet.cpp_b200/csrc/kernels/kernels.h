@@ -203,10 +203,12 @@ struct StreamAttnArgs {
   const float* bias_v;
   void* ctx;             // [Tc, d]
   int d, n_heads, Tc, cache_len;
-  int filled;            // valid frames in the attention cache (its last `filled` rows)
+  const int* filled;     // device: valid frames in the attention cache (its last `filled` rows)
   int att_left, att_right;
 };
 cudaError_t stream_attention_launch(const StreamAttnArgs& a, bool bf16, cudaStream_t st);
+// *filled = min(cache_len, *filled + Tc): the cache fill count after a chunk
+cudaError_t stream_advance_launch(int* filled, int Tc, int cache_len, cudaStream_t st);
 // in [K - 1 + Tc, d] (conv cache rows, then the chunk's GLU rows) -> out [Tc, d]:
 // depthwise conv + bias, then LayerNorm over d (g, b = gamma, beta) or the
 // folded BatchNorm (g, b = scale, shift), then SiLU

@@ -99,20 +99,53 @@ __device__ __forceinline__ float block_max(float v, float* red) {
 }
 
 constexpr int SA_THREADS = 128;
-constexpr int SA_MAX_KEYS = 4096;
 
 // One CTA per (head, query). qkv [Tk, 3d] (q | k | v), the chunk's queries
 // at rows cache_len .. Tk - 1; ptab rows 0 .. 2 Tk - 2 hold the projected
-// positions Tk - 1 ... -(Tk - 1) (row stride ldp); ctx [Tc, d].
+// positions Tk - 1 ... -(Tk - 1) (row stride ldp); ctx [Tc, d]. The head's
+// key, value and position rows the query reads are first staged in shared
+// memory with coalesced 16-byte loads (f32 there), so the dot products run
+// from shared memory instead of chains of dependent global loads.
 template <typename H>
 __global__ void __launch_bounds__(SA_THREADS) k_stream_attn(StreamAttnArgs a) {
+  extern __shared__ float sa_sm[];
   __shared__ float qu[128], qv[128], red[SA_THREADS / 32];
-  __shared__ float prob[SA_MAX_KEYS];
   const int head = blockIdx.x, i = blockIdx.y;
   const int d = a.d, dk = d / a.n_heads, Tk = a.cache_len + a.Tc;
+  const int ld = dk + 1;  // padded row stride: lanes of a key loop hit distinct banks
+  float* sK = sa_sm;                   // [Tk][ld]
+  float* sV = sK + (size_t)Tk * ld;    // [Tk][ld]
+  float* sP = sV + (size_t)Tk * ld;    // [Tk][ld]: position row of key j for this query
+  float* prob = sP + (size_t)Tk * ld;  // [Tk]
   const H* qkv = static_cast<const H*>(a.qkv);
   const H* ptab = static_cast<const H*>(a.ptab);
   const int qrow = a.cache_len + i;
+  // stage: 8 elements (16 bytes) per load, 4 loads in flight per thread
+  // before their stores (a load cannot pass an earlier store it may alias)
+  const int v8 = dk / 8, total = 3 * Tk * v8;
+  auto src_of = [&](int e) {
+    const int which = e / (Tk * v8), r = (e / v8) % Tk, c8 = (e % v8) * 8;
+    return which == 2 ? ptab + (size_t)(r + a.Tc - 1 - i) * a.ldp + head * dk + c8
+                      : qkv + (size_t)r * 3 * d + (which + 1) * d + head * dk + c8;
+  };
+  for (int e0 = threadIdx.x; e0 < total; e0 += 4 * SA_THREADS) {
+    uint4 raw[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int e = e0 + u * SA_THREADS;
+      raw[u] = e < total ? *reinterpret_cast<const uint4*>(src_of(e)) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int e = e0 + u * SA_THREADS;
+      if (e >= total) break;
+      const int which = e / (Tk * v8), r = (e / v8) % Tk, c8 = (e % v8) * 8;
+      const H* hv = reinterpret_cast<const H*>(&raw[u]);
+      float* dst = (which == 0 ? sK : which == 1 ? sV : sP) + (size_t)r * ld + c8;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) dst[q] = ld_h(hv + q);
+    }
+  }
   for (int e = threadIdx.x; e < dk; e += SA_THREADS) {
     const float q = ld_h(qkv + (size_t)qrow * 3 * d + head * dk + e);
     qu[e] = q + a.bias_u[head * dk + e];
@@ -123,24 +156,26 @@ __global__ void __launch_bounds__(SA_THREADS) k_stream_attn(StreamAttnArgs a) {
   // the cache's first cache_len - filled columns are not filled yet
   const int chunk = a.att_right + 1;
   const int left_chunks = chunk > 0 ? a.att_left / chunk : 0;
-  const int gq = qrow, first_filled = a.cache_len - a.filled;
+  const int filled = min(max(*a.filled, 0), a.cache_len);
+  const int gq = qrow, first_filled = a.cache_len - filled;
   const float scale = rsqrtf((float)dk);
   float mx = -INFINITY;
   for (int j = threadIdx.x; j < Tk; j += SA_THREADS) {
     const int diff = gq / chunk - j / chunk;
-    float s = -INFINITY;
+    float sc = -INFINITY;
     if (j >= first_filled && diff >= 0 && diff <= left_chunks) {
-      const H* kr = qkv + (size_t)j * 3 * d + d + head * dk;
-      const H* pr = ptab + (size_t)(j + a.Tc - 1 - i) * a.ldp + head * dk;  // relative position gq - j
+      const float* kr = sK + (size_t)j * ld;
+      const float* pr = sP + (size_t)j * ld;  // relative position gq - j
       float ac = 0.f, bd = 0.f;
+#pragma unroll 8
       for (int e = 0; e < dk; ++e) {
-        ac = fmaf(qu[e], ld_h(kr + e), ac);
-        bd = fmaf(qv[e], ld_h(pr + e), bd);
+        ac = fmaf(qu[e], kr[e], ac);
+        bd = fmaf(qv[e], pr[e], bd);
       }
-      s = (ac + bd) * scale;
+      sc = (ac + bd) * scale;
     }
-    prob[j] = s;
-    mx = fmaxf(mx, s);
+    prob[j] = sc;
+    mx = fmaxf(mx, sc);
   }
   mx = block_max(mx, red);
   float sum = 0.f;
@@ -153,10 +188,13 @@ __global__ void __launch_bounds__(SA_THREADS) k_stream_attn(StreamAttnArgs a) {
   const float inv = 1.0f / sum;
   for (int e = threadIdx.x; e < dk; e += SA_THREADS) {
     float acc = 0.f;
-    for (int j = 0; j < Tk; ++j) acc = fmaf(prob[j], ld_h(qkv + (size_t)j * 3 * d + 2 * d + head * dk + e), acc);
+#pragma unroll 4
+    for (int j = 0; j < Tk; ++j) acc = fmaf(prob[j], sV[(size_t)j * ld + e], acc);
     static_cast<H*>(a.ctx)[(size_t)i * d + head * dk + e] = to_h<H>(acc * inv);
   }
 }
+
+size_t stream_attn_smem(int Tk, int dk) { return ((size_t)3 * Tk * (dk + 1) + Tk) * sizeof(float); }
 
 constexpr int SD_THREADS = 256;
 
@@ -230,12 +268,32 @@ cudaError_t causal_dw_launch(const __nv_bfloat16* in, int Ti, int Fi, int valid,
 cudaError_t stream_attention_launch(const StreamAttnArgs& a, bool bf16, cudaStream_t st) {
   if (a.Tc <= 0) return cudaSuccess;
   const int dk = a.n_heads > 0 ? a.d / a.n_heads : 0;
-  if (dk <= 0 || dk > 128 || a.cache_len + a.Tc > SA_MAX_KEYS || a.filled < 0 || a.filled > a.cache_len ||
-      a.att_right < 0)
+  const int Tk = a.cache_len + a.Tc;
+  const size_t smem = stream_attn_smem(Tk, dk);
+  if (dk <= 0 || dk > 128 || dk % 8 || a.d % 8 || a.ldp % 8 || !a.filled || a.att_right < 0 || smem > 200 * 1024)
     return cudaErrorInvalidValue;
   const dim3 grid(a.n_heads, a.Tc);
-  if (bf16) k_stream_attn<__nv_bfloat16><<<grid, SA_THREADS, 0, st>>>(a);
-  else k_stream_attn<__half><<<grid, SA_THREADS, 0, st>>>(a);
+  cudaError_t e;
+  if (bf16) {
+    e = cudaFuncSetAttribute(k_stream_attn<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    k_stream_attn<__nv_bfloat16><<<grid, SA_THREADS, smem, st>>>(a);
+  } else {
+    e = cudaFuncSetAttribute(k_stream_attn<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    k_stream_attn<__half><<<grid, SA_THREADS, smem, st>>>(a);
+  }
+  return cudaGetLastError();
+}
+
+namespace {
+__global__ void k_stream_advance(int* filled, int Tc, int cache_len) {
+  if (threadIdx.x == 0 && blockIdx.x == 0) *filled = min(cache_len, *filled + Tc);
+}
+}  // namespace
+
+cudaError_t stream_advance_launch(int* filled, int Tc, int cache_len, cudaStream_t st) {
+  k_stream_advance<<<1, 32, 0, st>>>(filled, Tc, cache_len);
   return cudaGetLastError();
 }
 

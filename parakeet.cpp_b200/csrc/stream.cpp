@@ -16,6 +16,7 @@
 // (cache_last_channel_len), which the attention mask reads.
 #include <algorithm>
 #include <cmath>
+#include <cstring>
 
 #include "encoder.hpp"
 #include "kernels/gemm.h"
@@ -39,6 +40,22 @@ struct DeviceRunner::StreamState {
   void *s1 = nullptr, *s2a = nullptr, *s2b = nullptr, *s3a = nullptr, *s3b = nullptr;
   float* x = nullptr;
   void *hbuf = nullptr, *ffh = nullptr, *qkv = nullptr, *ctx = nullptr, *pe = nullptr, *ptab = nullptr;
+  int* d_filled = nullptr;  // the attention-cache fill count the kernels read
+  // page-locked staging of the window and the chunk's output (graph replays
+  // copy from / to fixed addresses)
+  float* h_mel = nullptr;
+  float* h_out = nullptr;
+  size_t h_mel_cap = 0, h_out_cap = 0;
+  // captured chunk graphs by (window frames, chunk frames, live cache buffer)
+  struct Graph {
+    int n, Tc, cur;
+    cudaGraphExec_t exec;
+  };
+  std::vector<Graph> graphs;
+  void drop_graphs() {
+    for (Graph& g : graphs) cudaGraphExecDestroy(g.exec);
+    graphs.clear();
+  }
 };
 
 namespace {
@@ -70,6 +87,10 @@ DeviceRunner::StreamState* DeviceRunner::stream_create(std::string& err) {
 
 void DeviceRunner::stream_destroy(StreamState* s) {
   if (!s) return;
+  s->drop_graphs();
+  if (s->d_filled) cudaFree(s->d_filled);
+  if (s->h_mel) cudaFreeHost(s->h_mel);
+  if (s->h_out) cudaFreeHost(s->h_out);
   for (int i = 0; i < 2; ++i) {
     if (s->kv[i]) cudaFree(s->kv[i]);
     if (s->cv[i]) cudaFree(s->cv[i]);
@@ -85,6 +106,8 @@ pkc_status DeviceRunner::stream_reset(StreamState& s, std::string& err) {
   s.step = 0;
   s.filled = 0;
   s.cur = 0;
+  if (!s.d_filled) PKC_CK(cudaMalloc(&s.d_filled, sizeof(int)), "cudaMalloc of the stream counter");
+  PKC_CK(cudaMemsetAsync(s.d_filled, 0, sizeof(int), stream_), "stream counter reset");
   for (int i = 0; i < 2; ++i) {
     if (s.kv[i]) PKC_CK(cudaMemsetAsync(s.kv[i], 0, (size_t)cfg_.n_layers * (cfg_.stream.cache_len + s.Tc_cap) * cfg_.d_model * 2, stream_), "stream cache reset");
     if (s.cv[i]) PKC_CK(cudaMemsetAsync(s.cv[i], 0, (size_t)cfg_.n_layers * (cfg_.conv_kernel - 1 + s.Tc_cap) * cfg_.d_model * 2, stream_), "stream cache reset");
@@ -98,7 +121,7 @@ pkc_status DeviceRunner::stream_step(StreamState& s, const float* mel, int n, bo
   const Config& c = cfg_;
   cudaSetDevice(device_);
   cudaStream_t st = stream_;
-  const int F = c.n_mels, C = c.sub_channels, d = c.d_model, FF = c.ff_dim, H = c.n_heads, K = c.conv_kernel;
+  const int F = c.n_mels, C = c.sub_channels, d = c.d_model, FF = c.ff_dim, K = c.conv_kernel;
   const int Lc = c.n_layers, LP = K - 1, cache = c.stream.cache_len;
   const bool bf = c.bf16;
   *n_valid = 0;
@@ -145,6 +168,7 @@ pkc_status DeviceRunner::stream_step(StreamState& s, const float* mel, int n, bo
       s.cv[i] = nc;
     }
     s.Tc_cap = cap;
+    s.drop_graphs();
   }
   const int cap = s.Tc_cap;
   const int Tkc = std::max(cap, Tc) + cache, Pc = 2 * Tkc - 1;
@@ -164,6 +188,7 @@ pkc_status DeviceRunner::stream_step(StreamState& s, const float* mel, int n, bo
       PKC_CK(cudaMalloc(&s.scratch, sz), "cudaMalloc of the streaming scratch");
       s.scratch_bytes = sz;
       s.pos_Tc = -1;
+      s.drop_graphs();
     }
     uint8_t* b = static_cast<uint8_t*>(s.scratch);
     s.mel = reinterpret_cast<float*>(b + o_mel);
@@ -172,15 +197,99 @@ pkc_status DeviceRunner::stream_step(StreamState& s, const float* mel, int n, bo
     s.hbuf = b + o_h; s.ffh = b + o_ff; s.qkv = b + o_qkv; s.ctx = b + o_ctx;
     void* pe = b + o_pe;
     void* pt = b + o_pt;
-    if (pe != s.pe || pt != s.ptab) s.pos_Tc = -1;
+    if (pe != s.pe || pt != s.ptab || s.mel != reinterpret_cast<float*>(b + o_mel)) {
+      s.pos_Tc = -1;
+      s.drop_graphs();
+    }
     s.pe = pe;
     s.ptab = pt;
+  }
+  if ((size_t)F * n > s.h_mel_cap || (size_t)T3 * d > s.h_out_cap) {
+    s.drop_graphs();
+    if (s.h_mel) cudaFreeHost(s.h_mel);
+    if (s.h_out) cudaFreeHost(s.h_out);
+    s.h_mel = s.h_out = nullptr;
+    s.h_mel_cap = s.h_out_cap = 0;
+    const size_t mc = std::max((size_t)F * n, (size_t)F * 64), oc = std::max((size_t)T3 * d, (size_t)16 * d);
+    PKC_CK(cudaMallocHost(&s.h_mel, mc * 4), "page-locked mel staging");
+    PKC_CK(cudaMallocHost(&s.h_out, oc * 4), "page-locked output staging");
+    s.h_mel_cap = mc;
+    s.h_out_cap = oc;
   }
   sk_part_ = 0;
   cudaGetLastError();
 
+  // positional table over cache + chunk positions and every layer's
+  // linear_pos: outside the graphs, only when the chunk length changes
+  const int Ld = Lc * d;
+  if (s.pos_Tc != Tc) {
+    PKC_CK(pos_table_launch(s.pe, Tk, d, bf, st), "pos_table");
+    PKC_ST(gemm(s.pe, d, w_.pos_all_w, d, bf, P, Ld, d, EPI_STORE_H, ACT_NONE, 1.f, nullptr, s.ptab, Ld, st,
+                "stream_pos", err, &w_.pos_all_q));
+    s.pos_Tc = Tc;
+  }
+  std::memcpy(s.h_mel, mel, (size_t)F * n * 4);
+  StreamState::Graph* hit = nullptr;
+  for (StreamState::Graph& g : s.graphs)
+    if (g.n == n && g.Tc == Tc && g.cur == s.cur) hit = &g;
+  if (use_graphs_ && !hit) {
+    cudaGraph_t graph = nullptr;
+    PKC_CK(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal), "graph capture begin");
+    const pkc_status ps = stream_issue(s, n, Tc, drop, err);
+    const cudaError_t ce = cudaStreamEndCapture(st, &graph);
+    if (ps != PKC_OK || ce != cudaSuccess) {
+      if (graph) cudaGraphDestroy(graph);
+      cudaGetLastError();
+      if (ps == PKC_OK) err = std::string("stream graph capture: ") + cudaGetErrorString(ce);
+      return ps != PKC_OK ? ps : PKC_ERR_CUDA;
+    }
+    cudaGraphExec_t exec = nullptr;
+    const cudaError_t ie = cudaGraphInstantiate(&exec, graph, 0);
+    cudaGraphDestroy(graph);
+    PKC_CK(ie, "stream graph instantiate");
+    if (s.graphs.size() >= 8) {
+      cudaStreamSynchronize(st);
+      cudaGraphExecDestroy(s.graphs.front().exec);
+      s.graphs.erase(s.graphs.begin());
+    }
+    s.graphs.push_back({n, Tc, s.cur, exec});
+    hit = &s.graphs.back();
+  }
+  if (hit) {
+    PKC_CK(cudaGraphLaunch(hit->exec, st), "stream graph launch");
+  } else {
+    PKC_ST(stream_issue(s, n, Tc, drop, err));
+  }
+  PKC_ST(finish(st, err));
+  std::memcpy(out, s.h_out, (size_t)valid * d * 4);
+  s.cur = 1 - s.cur;
+  s.filled = std::min(cache, s.filled + Tc);
+  s.step += 1;
+  *n_valid = valid;
+  return PKC_OK;
+}
+
+// One chunk's device work on the runner's stream, from the page-locked window
+// to the page-locked output (captured into a graph per shape).
+pkc_status DeviceRunner::stream_issue(StreamState& s, int n, int Tc, int drop, std::string& err) {
+  // chunk GEMMs have a few rows: the skinny kernel streams each weight once
+  // across every SM (the offline encoder keeps tcgen05 tiles for every M)
+  struct Skinny {
+    bool& f;
+    explicit Skinny(bool& x) : f(x) { f = true; }
+    ~Skinny() { f = false; }
+  } skinny(skinny_ok_);
+  const Config& c = cfg_;
+  cudaStream_t st = stream_;
+  const int F = c.n_mels, C = c.sub_channels, d = c.d_model, FF = c.ff_dim, H = c.n_heads, K = c.conv_kernel;
+  const int Lc = c.n_layers, LP = K - 1, cache = c.stream.cache_len, Ld = Lc * d;
+  const bool bf = c.bf16;
+  const int T1 = half_up(n), T2 = half_up(T1), T3 = half_up(T2);
+  const int F1 = c.F1, F2 = c.F2, F3 = c.F3;
+  const int Tk = cache + Tc, cap = s.Tc_cap;
+
   // ---- causal subsampling (the window is all real audio: no time mask bites)
-  PKC_CK(cudaMemcpyAsync(s.mel, mel, (size_t)F * n * 4, cudaMemcpyHostToDevice, st), "mel upload");
+  PKC_CK(cudaMemcpyAsync(s.mel, s.h_mel, (size_t)F * n * 4, cudaMemcpyHostToDevice, st), "mel upload");
   auto* s1 = static_cast<__nv_bfloat16*>(s.s1);
   PKC_CK(causal_conv0_launch(s.mel, F, n, n, w_.c0_w, w_.c0_b, C, T1, F1, s1, st), "causal conv0");
   PKC_CK(causal_dw_launch(s1, T1, F1, T1, w_.dw1_w, w_.dw1_b, C, T2, F2, static_cast<__nv_bfloat16*>(s.s2a), st),
@@ -195,15 +304,6 @@ pkc_status DeviceRunner::stream_step(StreamState& s, const float* mel, int n, bo
   PKC_ST(gemm(s.s3b, F3 * C, w_.out_w, F3 * C, true, T3, d, F3 * C, EPI_STORE_F32, ACT_NONE, xs, w_.out_b, s.x, d,
               st, "stream_sub_out", err));
   float* x = s.x + (size_t)drop * d;  // drop_extra_pre_encoded leading frames
-
-  // ---- positional table over cache + chunk positions, every layer's linear_pos
-  const int Ld = Lc * d;
-  if (s.pos_Tc != Tc) {
-    PKC_CK(pos_table_launch(s.pe, Tk, d, bf, st), "pos_table");
-    PKC_ST(gemm(s.pe, d, w_.pos_all_w, d, bf, P, Ld, d, EPI_STORE_H, ACT_NONE, 1.f, nullptr, s.ptab, Ld, st,
-                "stream_pos", err, &w_.pos_all_q));
-    s.pos_Tc = Tc;
-  }
 
   // ---- conformer layers with their caches (build_stream_layer, :98-338)
   const size_t kv_rows = (size_t)cache + cap, cv_rows = (size_t)LP + cap;
@@ -225,7 +325,7 @@ pkc_status DeviceRunner::stream_step(StreamState& s, const float* mel, int n, bo
     PKC_ST(gemm(kvc, d, L.qkv_w, d, bf, Tk, 3 * d, d, EPI_STORE_H, ACT_NONE, 1.f, L.qkv_b, s.qkv, 3 * d, st,
                 "stream_qkv", err, &L.qkv_q));
     StreamAttnArgs sa{s.qkv, static_cast<const uint8_t*>(s.ptab) + (size_t)li * d * 2, Ld, L.pos_u, L.pos_v,
-                      s.ctx, d, H, Tc, cache, s.filled, c.att_left, c.att_right};
+                      s.ctx, d, H, Tc, cache, s.d_filled, c.att_left, c.att_right};
     PKC_CK(stream_attention_launch(sa, bf, st), "stream attention");
     PKC_ST(gemm(s.ctx, d, L.out_w, d, bf, Tc, d, d, EPI_RESID_F32, ACT_NONE, 1.f, L.out_b, x, d, st, "stream_out",
                 err, &L.out_q));
@@ -254,12 +354,8 @@ pkc_status DeviceRunner::stream_step(StreamState& s, const float* mel, int n, bo
     PKC_CK(layernorm_launch(x, Tc, d, L.ln_out_g, L.ln_out_b, last ? nullptr : s.hbuf, bf,
                             last ? nullptr : N->ln_ff1_g, last ? nullptr : N->ln_ff1_b, true, st), "ln");
   }
-  PKC_CK(cudaMemcpyAsync(out, x, (size_t)valid * d * 4, cudaMemcpyDeviceToHost, st), "stream output download");
-  PKC_ST(finish(st, err));
-  s.cur = 1 - s.cur;
-  s.filled = std::min(cache, s.filled + Tc);
-  s.step += 1;
-  *n_valid = valid;
+  PKC_CK(stream_advance_launch(s.d_filled, Tc, cache, st), "stream advance");
+  PKC_CK(cudaMemcpyAsync(s.h_out, x, (size_t)Tc * d * 4, cudaMemcpyDeviceToHost, st), "stream output download");
   return PKC_OK;
 }
 

@@ -268,3 +268,45 @@ def test_stream_k_matches_whole_tiles(cuda, tmp_path, M, N, K, epi):
     scale = np.abs(outs["whole"]).max()
     tol = 1e-5 if epi in ("resid", "f32") else 1e-3   # f16 outputs: a last-bit flip at most
     assert np.abs(outs["sk"] - outs["whole"]).max() <= tol * scale
+
+
+@pytest.mark.parametrize("bf16", [False, True])
+@pytest.mark.parametrize("M", [1, 2, 5, 16])
+@pytest.mark.parametrize("epi", ["store_silu", "resid", "f32", "glu"])
+def test_skinny_epilogues(cuda, bf16, M, epi):
+    """M <= 16: the skinny CUDA-core GEMM (one warp per weight row, f32
+    accumulation) with every epilogue the streaming encoder uses, against
+    the fp32 reference; K = 2048 exercises several 16-byte chunks per lane."""
+    import torch
+    import pkc
+    N, K = 1024, 2048
+    dt = torch.bfloat16 if bf16 else torch.float16
+    A, B, bias, ref = _setup(M, N, K, dt, seed=20 + M)
+    x = ref + bias
+    tol = 1e-2 if bf16 else 3e-3
+    if epi == "store_silu":
+        out = torch.zeros(M, N, dtype=dt, device=cuda)
+        pkc.gemm(A.data_ptr(), B.data_ptr(), M, N, K, bf16=bf16, epi=pkc.EPI_STORE_H, act=pkc.ACT_SILU,
+                 bias=bias.data_ptr(), out=out.data_ptr(), ldo=N)
+        want, got = torch.nn.functional.silu(x), out.float()
+    elif epi == "resid":
+        base = torch.randn(M, N, device=cuda)
+        out = base.clone()
+        pkc.gemm(A.data_ptr(), B.data_ptr(), M, N, K, bf16=bf16, epi=pkc.EPI_RESID_F32, alpha=0.5,
+                 bias=bias.data_ptr(), out=out.data_ptr(), ldo=N)
+        want, got, tol = base + 0.5 * x, out, 1e-4
+    elif epi == "f32":
+        out = torch.zeros(M, N, device=cuda)
+        pkc.gemm(A.data_ptr(), B.data_ptr(), M, N, K, bf16=bf16, epi=pkc.EPI_STORE_F32, alpha=2.0,
+                 bias=bias.data_ptr(), out=out.data_ptr(), ldo=N)
+        want, got, tol = 2.0 * x, out, 1e-4
+    else:
+        xt = x.view(M, N // 256, 2, 128)
+        a, g = xt[:, :, 0, :].reshape(M, N // 2), xt[:, :, 1, :].reshape(M, N // 2)
+        out = torch.zeros(M, N // 2, dtype=dt, device=cuda)
+        pkc.gemm(A.data_ptr(), B.data_ptr(), M, N, K, bf16=bf16, epi=pkc.EPI_GLU_H, bias=bias.data_ptr(),
+                 out=out.data_ptr(), ldo=N // 2)
+        want, got = a * torch.sigmoid(g), out.float()
+    torch.cuda.synchronize()
+    err = (got - want).abs().max().item() / want.abs().max().item()
+    assert err < tol, err

@@ -132,3 +132,27 @@ def test_stream_needs_a_streaming_model(stream_models, tmp_path):
         assert e.value.status == 4
     finally:
         m.close()
+
+
+def test_stream_graph_replay_matches_eager(stream_models, monkeypatch):
+    """The chunk step replayed from captured CUDA graphs equals the eagerly
+    issued step (PKC_NO_GRAPH=1) bit for bit, across a cache roll."""
+    import oracle
+    import pkc
+    w = oracle.Weights(stream_models["f16"])
+    sc = oracle.StreamCfg(w)
+    mel = np.random.default_rng(9).standard_normal((64, 640)).astype(np.float32)
+    sched = oracle.stream_schedule(sc, 640)
+    res = []
+    for eager in (False, True):
+        if eager:
+            monkeypatch.setenv("PKC_NO_GRAPH", "1")
+        m = pkc.Model(stream_models["f16"])
+        try:
+            s = pkc.Stream(m)
+            res.append(run_stream(s, sched, mel))
+            s.close()
+        finally:
+            m.close()
+    for x, y in zip(*res):
+        assert np.array_equal(x, y)
