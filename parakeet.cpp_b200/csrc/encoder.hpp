@@ -120,6 +120,10 @@ class DeviceRunner {
   pkc_status run_layer(const Plan& p, int li, const Part& q, cudaStream_t st, std::string& err);
   pkc_status finish(cudaStream_t st, std::string& err);
   pkc_status stream_issue(StreamState& s, int n, int Tc, int drop, std::string& err);
+  // out = epi(LayerNorm(x rows) * g + b) . B^T on the skinny GEMM (M <= 16, 16-bit weights)
+  pkc_status gemm_skinny_ln(const float* x, int ldx, const float* g, const float* b, const void* B, bool bf16, int M,
+                            int N, int K, int epi, int act, float alpha, const float* bias, void* out, int ldo,
+                            cudaStream_t st, std::string& err);
   bool ensure_ws(size_t bytes);
   void prof_begin(cudaStream_t st);
   void prof_end(cudaStream_t st, const char* name, double flops, double bytes);

@@ -1460,9 +1460,49 @@ __global__ void __launch_bounds__(SKINNY_THREADS) k_gemm_skinny(const H* __restr
   constexpr bool PAIRED = EPI == EPI_GLU_H;
   pdl_wait();
   const int M = args.M, k8 = args.K / 8;
-  for (int e = threadIdx.x; e < M * k8; e += SKINNY_THREADS) {
-    const int m = e / k8, c = e - m * k8;
-    sk_a[e] = __ldg(reinterpret_cast<const uint4*>(A + (size_t)m * lda) + c);
+  if (args.ln_x) {
+    // LayerNorm of row m by warp m % 8: mean, then the mean square deviation
+    // (two passes, as ggml_norm), then the affine, rounded into the staging
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int m = warp; m < M; m += SKINNY_WARPS) {
+      const float* xr = args.ln_x + (size_t)m * args.ln_ldx;
+      float s = 0.f;
+      for (int k = lane * 4; k < args.K; k += 128) {
+        const float4 v = *reinterpret_cast<const float4*>(xr + k);
+        s += (v.x + v.y) + (v.z + v.w);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      const float mean = s / (float)args.K;
+      float q = 0.f;
+      for (int k = lane * 4; k < args.K; k += 128) {
+        const float4 v = *reinterpret_cast<const float4*>(xr + k);
+        const float a0 = v.x - mean, a1 = v.y - mean, a2 = v.z - mean, a3 = v.w - mean;
+        q += (a0 * a0 + a1 * a1) + (a2 * a2 + a3 * a3);
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+      const float rstd = rsqrtf(q / (float)args.K + 1e-5f);
+      for (int c = lane; c < k8; c += 32) {
+        const float4 v0 = *reinterpret_cast<const float4*>(xr + 8 * c);
+        const float4 v1 = *reinterpret_cast<const float4*>(xr + 8 * c + 4);
+        const float4 g0 = *reinterpret_cast<const float4*>(args.ln_g + 8 * c);
+        const float4 g1 = *reinterpret_cast<const float4*>(args.ln_g + 8 * c + 4);
+        const float4 b0 = *reinterpret_cast<const float4*>(args.ln_b + 8 * c);
+        const float4 b1 = *reinterpret_cast<const float4*>(args.ln_b + 8 * c + 4);
+        uint4 o;
+        o.x = pack2<H>((v0.x - mean) * rstd * g0.x + b0.x, (v0.y - mean) * rstd * g0.y + b0.y);
+        o.y = pack2<H>((v0.z - mean) * rstd * g0.z + b0.z, (v0.w - mean) * rstd * g0.w + b0.w);
+        o.z = pack2<H>((v1.x - mean) * rstd * g1.x + b1.x, (v1.y - mean) * rstd * g1.y + b1.y);
+        o.w = pack2<H>((v1.z - mean) * rstd * g1.z + b1.z, (v1.w - mean) * rstd * g1.w + b1.w);
+        sk_a[m * k8 + c] = o;
+      }
+    }
+  } else {
+    for (int e = threadIdx.x; e < M * k8; e += SKINNY_THREADS) {
+      const int m = e / k8, c = e - m * k8;
+      sk_a[e] = __ldg(reinterpret_cast<const uint4*>(A + (size_t)m * lda) + c);
+    }
   }
   __syncthreads();
   pdl_trigger();
@@ -1562,9 +1602,14 @@ cudaError_t launch_skinny(const void* A, int lda, const void* B, int ldb, const 
 cudaError_t gemm_launch(const void* A, int lda, const void* B, int ldb, bool bf16,
                         const GemmArgs& args, cudaStream_t st) {
   if (args.M <= 0) return cudaSuccess;
-  if (args.skinny && args.M <= SKINNY_M && !args.stats && args.N % BN == 0 && args.K % 8 == 0 && args.K <= 4096 && lda % 8 == 0 &&
-      ldb % 8 == 0 && !(reinterpret_cast<uintptr_t>(A) & 15) && !(reinterpret_cast<uintptr_t>(B) & 15) &&
-      args.epi != EPI_POWER_F32 && gemm_skinny_enabled()) {
+  auto al16 = [](const void* p) { return !(reinterpret_cast<uintptr_t>(p) & 15); };
+  const bool skinny = args.skinny && args.M <= SKINNY_M && !args.stats && args.N % BN == 0 && args.K % 8 == 0 &&
+                      args.K <= 4096 && lda % 8 == 0 && ldb % 8 == 0 && (args.ln_x || al16(A)) && al16(B) &&
+                      args.epi != EPI_POWER_F32 && gemm_skinny_enabled();
+  // the LayerNorm prologue exists on the skinny kernel only
+  if (args.ln_x && !(skinny && args.ln_ldx % 4 == 0 && al16(args.ln_x) && al16(args.ln_g) && al16(args.ln_b)))
+    return cudaErrorInvalidValue;
+  if (skinny) {
     switch (args.epi) {
 #define PKC_SKINNY_CASE(E) \
   case E:                  \

@@ -41,6 +41,13 @@ struct GemmArgs {
   // order, so callers whose output must not depend on the batch composition
   // (the offline encoder) leave it 0.
   int skinny;
+  // skinny kernel only: when ln_x is set, A is LayerNorm(ln_x rows) * ln_g +
+  // ln_b (ggml_norm, eps 1e-5) rounded to the operand type, computed while
+  // the rows are staged (ln_x f32 [M, K], row stride ln_ldx)
+  const float* ln_x;
+  int ln_ldx;
+  const float* ln_g;
+  const float* ln_b;
 };
 
 // Stream-K workspace sizes for `pairs` CTA pairs (a device's SMs / 2).

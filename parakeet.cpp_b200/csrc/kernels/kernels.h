@@ -196,7 +196,8 @@ cudaError_t causal_conv0_launch(const float* mel, int F, int n, int valid, const
 cudaError_t causal_dw_launch(const __nv_bfloat16* in, int Ti, int Fi, int valid, const float* w, const float* b,
                              int C, int To, int Fo, __nv_bfloat16* out, cudaStream_t st);
 struct StreamAttnArgs {
-  const void* qkv;       // [cache_len + Tc, 3d]: rows of [attention cache | chunk], q | k | v
+  const void* qkv;       // [Tc, 3d]: the chunk's q | k | v
+  const void* kv_cache;  // [cache_len, 2d]: projected k | v of the cached frames (oldest first)
   const void* ptab;      // this layer's projected positions: row r = relative position cache_len + Tc - 1 - r
   int ldp;               // row stride of ptab (elements)
   const float* bias_u;   // [d]

@@ -100,12 +100,13 @@ __device__ __forceinline__ float block_max(float v, float* red) {
 
 constexpr int SA_THREADS = 128;
 
-// One CTA per (head, query). qkv [Tk, 3d] (q | k | v), the chunk's queries
-// at rows cache_len .. Tk - 1; ptab rows 0 .. 2 Tk - 2 hold the projected
-// positions Tk - 1 ... -(Tk - 1) (row stride ldp); ctx [Tc, d]. The head's
-// key, value and position rows the query reads are first staged in shared
-// memory with coalesced 16-byte loads (f32 there), so the dot products run
-// from shared memory instead of chains of dependent global loads.
+// One CTA per (head, query). Keys / values j < cache_len come from the cache
+// of projected k | v rows, j >= cache_len from the chunk's qkv rows; ptab
+// rows 0 .. 2 Tk - 2 hold the projected positions Tk - 1 ... -(Tk - 1) (row
+// stride ldp); ctx [Tc, d]. The head's key, value and position rows the query
+// reads are first staged in shared memory with coalesced 16-byte loads (f32
+// there), so the dot products run from shared memory instead of chains of
+// dependent global loads.
 template <typename H>
 __global__ void __launch_bounds__(SA_THREADS) k_stream_attn(StreamAttnArgs a) {
   extern __shared__ float sa_sm[];
@@ -118,15 +119,17 @@ __global__ void __launch_bounds__(SA_THREADS) k_stream_attn(StreamAttnArgs a) {
   float* sP = sV + (size_t)Tk * ld;    // [Tk][ld]: position row of key j for this query
   float* prob = sP + (size_t)Tk * ld;  // [Tk]
   const H* qkv = static_cast<const H*>(a.qkv);
+  const H* kvc = static_cast<const H*>(a.kv_cache);
   const H* ptab = static_cast<const H*>(a.ptab);
-  const int qrow = a.cache_len + i;
+  const int qrow = a.cache_len + i;  // the query's frame among [cache | chunk]
   // stage: 8 elements (16 bytes) per load, 4 loads in flight per thread
   // before their stores (a load cannot pass an earlier store it may alias)
   const int v8 = dk / 8, total = 3 * Tk * v8;
   auto src_of = [&](int e) {
     const int which = e / (Tk * v8), r = (e / v8) % Tk, c8 = (e % v8) * 8;
-    return which == 2 ? ptab + (size_t)(r + a.Tc - 1 - i) * a.ldp + head * dk + c8
-                      : qkv + (size_t)r * 3 * d + (which + 1) * d + head * dk + c8;
+    if (which == 2) return ptab + (size_t)(r + a.Tc - 1 - i) * a.ldp + head * dk + c8;
+    return r < a.cache_len ? kvc + (size_t)r * 2 * d + which * d + head * dk + c8
+                           : qkv + (size_t)(r - a.cache_len) * 3 * d + (which + 1) * d + head * dk + c8;
   };
   for (int e0 = threadIdx.x; e0 < total; e0 += 4 * SA_THREADS) {
     uint4 raw[4];
@@ -147,7 +150,7 @@ __global__ void __launch_bounds__(SA_THREADS) k_stream_attn(StreamAttnArgs a) {
     }
   }
   for (int e = threadIdx.x; e < dk; e += SA_THREADS) {
-    const float q = ld_h(qkv + (size_t)qrow * 3 * d + head * dk + e);
+    const float q = ld_h(qkv + (size_t)i * 3 * d + head * dk + e);
     qu[e] = q + a.bias_u[head * dk + e];
     qv[e] = q + a.bias_v[head * dk + e];
   }

@@ -2,11 +2,12 @@
 // src/streaming_encoder.cpp:30-464).
 //
 // Per stream, on the device:
-//   attention cache  per layer [cache_len + Tc, d] compute-type rows: the last
-//                    cache_len normalised attention inputs, then this chunk's
-//                    (written there by the LayerNorm); the QKV GEMM reads all
-//                    cache_len + Tc rows, so K / V of the cache are projected
-//                    again each chunk exactly as the reference does
+//   attention cache  per layer [cache_len, 2d] compute-type rows: k | v of the
+//                    last cache_len frames. The reference keeps their
+//                    normalised attention inputs and projects them again each
+//                    chunk; the projection is per row and the same every time,
+//                    so the projected rows are kept instead and the QKV GEMM
+//                    sees only the chunk's rows
 //   conv cache       per layer [K - 1 + Tc, d]: the last K - 1 GLU outputs,
 //                    then this chunk's (written there by the GLU GEMM)
 // Both are double-buffered: the rows that become the next chunk's cache are
@@ -31,7 +32,7 @@ struct DeviceRunner::StreamState {
   int cur = 0;     // which cache buffer holds the live caches
   int Tc_cap = 0, n_cap = 0;
   int pos_Tc = -1;  // Tc the positional table was made for
-  void* kv[2] = {nullptr, nullptr};
+  void* kv[2] = {nullptr, nullptr};  // [L][cache_len][2d] each
   void* cv[2] = {nullptr, nullptr};
   void* scratch = nullptr;
   size_t scratch_bytes = 0;
@@ -62,6 +63,17 @@ namespace {
 size_t al256(size_t x) { return (x + 255) / 256 * 256; }
 int half_up(int n) { return n / 2 + 1; }  // causal k=3, s=2 stage: pads 2 + 1
 }  // namespace
+
+pkc_status DeviceRunner::gemm_skinny_ln(const float* x, int ldx, const float* g, const float* b, const void* B,
+                                        bool bf16, int M, int N, int K, int epi, int act, float alpha,
+                                        const float* bias, void* out, int ldo, cudaStream_t st, std::string& err) {
+  GemmArgs a{};
+  a.M = M; a.N = N; a.K = K; a.epi = epi; a.act = act; a.alpha = alpha; a.bias = bias;
+  a.out = out; a.ldo = ldo; a.err = err_word_; a.skinny = 1;
+  a.ln_x = x; a.ln_ldx = ldx; a.ln_g = g; a.ln_b = b;
+  PKC_CK(gemm_launch(nullptr, K, B, K, bf16, a, st), "LayerNorm + skinny GEMM");
+  return PKC_OK;
+}
 
 DeviceRunner::StreamState* DeviceRunner::stream_create(std::string& err) {
   const Config& c = cfg_;
@@ -109,7 +121,10 @@ pkc_status DeviceRunner::stream_reset(StreamState& s, std::string& err) {
   if (!s.d_filled) PKC_CK(cudaMalloc(&s.d_filled, sizeof(int)), "cudaMalloc of the stream counter");
   PKC_CK(cudaMemsetAsync(s.d_filled, 0, sizeof(int), stream_), "stream counter reset");
   for (int i = 0; i < 2; ++i) {
-    if (s.kv[i]) PKC_CK(cudaMemsetAsync(s.kv[i], 0, (size_t)cfg_.n_layers * (cfg_.stream.cache_len + s.Tc_cap) * cfg_.d_model * 2, stream_), "stream cache reset");
+    if (!s.kv[i] && cfg_.stream.cache_len > 0)
+      PKC_CK(cudaMalloc(&s.kv[i], (size_t)cfg_.n_layers * cfg_.stream.cache_len * 2 * cfg_.d_model * 2),
+             "cudaMalloc of the streaming attention cache");
+    if (s.kv[i]) PKC_CK(cudaMemsetAsync(s.kv[i], 0, (size_t)cfg_.n_layers * cfg_.stream.cache_len * 2 * cfg_.d_model * 2, stream_), "stream cache reset");
     if (s.cv[i]) PKC_CK(cudaMemsetAsync(s.cv[i], 0, (size_t)cfg_.n_layers * (cfg_.conv_kernel - 1 + s.Tc_cap) * cfg_.d_model * 2, stream_), "stream cache reset");
   }
   PKC_CK(cudaStreamSynchronize(stream_), "stream reset");
@@ -148,23 +163,17 @@ pkc_status DeviceRunner::stream_step(StreamState& s, const float* mel, int n, bo
   // ---- capacity: caches keep their rows when they grow
   if (Tc > s.Tc_cap) {
     const int cap = std::max(Tc, 8);
-    for (int i = 0; i < 2; ++i) {
-      void *nk = nullptr, *nc = nullptr;
-      const size_t kb = (size_t)Lc * (cache + cap) * d * 2, cb = (size_t)Lc * (LP + cap) * d * 2;
-      PKC_CK(cudaMalloc(&nk, kb), "cudaMalloc of the streaming attention cache");
+    for (int i = 0; i < 2; ++i) {  // the conv caches hold the chunk's GLU rows too: they grow with Tc
+      void* nc = nullptr;
+      const size_t cb = (size_t)Lc * (LP + cap) * d * 2;
       PKC_CK(cudaMalloc(&nc, cb), "cudaMalloc of the streaming conv cache");
-      PKC_CK(cudaMemsetAsync(nk, 0, kb, st), "stream cache init");
       PKC_CK(cudaMemsetAsync(nc, 0, cb, st), "stream cache init");
-      if (s.kv[i]) {
-        PKC_CK(cudaMemcpy2DAsync(nk, (size_t)(cache + cap) * d * 2, s.kv[i], (size_t)(cache + s.Tc_cap) * d * 2,
-                                 (size_t)cache * d * 2, Lc, cudaMemcpyDeviceToDevice, st), "stream cache move");
+      if (s.cv[i]) {
         PKC_CK(cudaMemcpy2DAsync(nc, (size_t)(LP + cap) * d * 2, s.cv[i], (size_t)(LP + s.Tc_cap) * d * 2,
                                  (size_t)LP * d * 2, Lc, cudaMemcpyDeviceToDevice, st), "stream cache move");
         PKC_CK(cudaStreamSynchronize(st), "stream cache move");
-        cudaFree(s.kv[i]);
         cudaFree(s.cv[i]);
       }
-      s.kv[i] = nk;
       s.cv[i] = nc;
     }
     s.Tc_cap = cap;
@@ -179,7 +188,7 @@ pkc_status DeviceRunner::stream_step(StreamState& s, const float* mel, int n, bo
                  o_s2a = take((size_t)T2 * F2 * C * 2), o_s2b = take((size_t)T2 * F2 * C * 2),
                  o_s3a = take((size_t)T3 * F3 * C * 2), o_s3b = take((size_t)T3 * F3 * C * 2),
                  o_x = take((size_t)T3 * d * 4), o_h = take((size_t)cap * d * 2), o_ff = take((size_t)cap * FF * 2),
-                 o_qkv = take((size_t)Tkc * 3 * d * 2), o_ctx = take((size_t)cap * d * 2), o_pe = take((size_t)Pc * d * 2),
+                 o_qkv = take((size_t)cap * 3 * d * 2), o_ctx = take((size_t)cap * d * 2), o_pe = take((size_t)Pc * d * 2),
                  o_pt = take((size_t)Pc * Lc * d * 2);
     if (sz > s.scratch_bytes) {
       if (s.scratch) cudaFree(s.scratch);
@@ -286,7 +295,7 @@ pkc_status DeviceRunner::stream_issue(StreamState& s, int n, int Tc, int drop, s
   const bool bf = c.bf16;
   const int T1 = half_up(n), T2 = half_up(T1), T3 = half_up(T2);
   const int F1 = c.F1, F2 = c.F2, F3 = c.F3;
-  const int Tk = cache + Tc, cap = s.Tc_cap;
+  const int cap = s.Tc_cap;
 
   // ---- causal subsampling (the window is all real audio: no time mask bites)
   PKC_CK(cudaMemcpyAsync(s.mel, s.h_mel, (size_t)F * n * 4, cudaMemcpyHostToDevice, st), "mel upload");
@@ -306,37 +315,47 @@ pkc_status DeviceRunner::stream_issue(StreamState& s, int n, int Tc, int drop, s
   float* x = s.x + (size_t)drop * d;  // drop_extra_pre_encoded leading frames
 
   // ---- conformer layers with their caches (build_stream_layer, :98-338)
-  const size_t kv_rows = (size_t)cache + cap, cv_rows = (size_t)LP + cap;
+  const size_t kv_rows = (size_t)cache, cv_rows = (size_t)LP + cap;
   for (int li = 0; li < Lc; ++li) {
     const LayerWeights& L = w_.layers[li];
-    uint8_t* kvc = static_cast<uint8_t*>(s.kv[s.cur]) + (size_t)li * kv_rows * d * 2;
-    uint8_t* kvn = static_cast<uint8_t*>(s.kv[1 - s.cur]) + (size_t)li * kv_rows * d * 2;
+    uint8_t* kvc = cache ? static_cast<uint8_t*>(s.kv[s.cur]) + (size_t)li * kv_rows * 2 * d * 2 : nullptr;
+    uint8_t* kvn = cache ? static_cast<uint8_t*>(s.kv[1 - s.cur]) + (size_t)li * kv_rows * 2 * d * 2 : nullptr;
     uint8_t* cvc = static_cast<uint8_t*>(s.cv[s.cur]) + (size_t)li * cv_rows * d * 2;
     uint8_t* cvn = static_cast<uint8_t*>(s.cv[1 - s.cur]) + (size_t)li * cv_rows * d * 2;
-    if (li == 0)
-      PKC_CK(layernorm_launch(x, Tc, d, L.ln_ff1_g, L.ln_ff1_b, s.hbuf, bf, nullptr, nullptr, false, st), "ln");
-    PKC_ST(gemm(s.hbuf, d, L.ff1_w1, d, bf, Tc, FF, d, EPI_STORE_H, ACT_SILU, 1.f, L.ff1_b1, s.ffh, FF, st,
-                "stream_ffn", err, &L.ff1_q1));
+    // x -> LayerNorm(g, b) -> GEMM: the norm inside the skinny GEMM's staging
+    // when it can run there (few rows, 16-bit weight), else its own kernel
+    auto ln_gemm = [&](const float* g, const float* b, const void* W, const QWeight* q, int N, int epi, int act,
+                       float alpha, const float* bias, void* out, int ldo, const char* name) -> pkc_status {
+      if (Tc <= 16 && !(q && q->type)) return gemm_skinny_ln(x, d, g, b, W, bf, Tc, N, d, epi, act, alpha, bias, out, ldo, st, err);
+      PKC_CK(layernorm_launch(x, Tc, d, g, b, s.hbuf, bf, nullptr, nullptr, false, st), "ln");
+      return gemm(s.hbuf, d, W, d, bf, Tc, N, d, epi, act, alpha, bias, out, ldo, st, name, err, q);
+    };
+    PKC_ST(ln_gemm(L.ln_ff1_g, L.ln_ff1_b, L.ff1_w1, &L.ff1_q1, FF, EPI_STORE_H, ACT_SILU, 1.f, L.ff1_b1, s.ffh, FF,
+                   "stream_ffn"));
     PKC_ST(gemm(s.ffh, FF, L.ff1_w2, FF, bf, Tc, d, FF, EPI_RESID_F32, ACT_NONE, 0.5f, L.ff1_b2, x, d, st,
                 "stream_ffn", err, &L.ff1_q2));
-    // attention input of this chunk, after the cache rows
-    PKC_CK(layernorm_launch(x, Tc, d, L.ln_att_g, L.ln_att_b, kvc + (size_t)cache * d * 2, bf, nullptr, nullptr,
-                            false, st), "ln");
-    PKC_ST(gemm(kvc, d, L.qkv_w, d, bf, Tk, 3 * d, d, EPI_STORE_H, ACT_NONE, 1.f, L.qkv_b, s.qkv, 3 * d, st,
-                "stream_qkv", err, &L.qkv_q));
-    StreamAttnArgs sa{s.qkv, static_cast<const uint8_t*>(s.ptab) + (size_t)li * d * 2, Ld, L.pos_u, L.pos_v,
+    // q | k | v of the chunk's frames; k | v of the cached frames are in kvc
+    PKC_ST(ln_gemm(L.ln_att_g, L.ln_att_b, L.qkv_w, &L.qkv_q, 3 * d, EPI_STORE_H, ACT_NONE, 1.f, L.qkv_b, s.qkv, 3 * d,
+                   "stream_qkv"));
+    StreamAttnArgs sa{s.qkv, kvc, static_cast<const uint8_t*>(s.ptab) + (size_t)li * d * 2, Ld, L.pos_u, L.pos_v,
                       s.ctx, d, H, Tc, cache, s.d_filled, c.att_left, c.att_right};
     PKC_CK(stream_attention_launch(sa, bf, st), "stream attention");
     PKC_ST(gemm(s.ctx, d, L.out_w, d, bf, Tc, d, d, EPI_RESID_F32, ACT_NONE, 1.f, L.out_b, x, d, st, "stream_out",
                 err, &L.out_q));
-    // next attention cache: the last cache_len of [cache | chunk]
-    if (cache > 0)
-      PKC_CK(cudaMemcpyAsync(kvn, kvc + (size_t)Tc * d * 2, (size_t)cache * d * 2, cudaMemcpyDeviceToDevice, st),
+    // next attention cache: the last cache_len k | v rows of [cache | chunk]
+    if (cache > 0) {
+      const int keep = std::max(0, cache - Tc), fresh = cache - keep;  // fresh <= Tc
+      if (keep > 0)
+        PKC_CK(cudaMemcpyAsync(kvn, kvc + (size_t)Tc * 2 * d * 2, (size_t)keep * 2 * d * 2, cudaMemcpyDeviceToDevice,
+                               st), "attention cache update");
+      PKC_CK(cudaMemcpy2DAsync(kvn + (size_t)keep * 2 * d * 2, (size_t)2 * d * 2,
+                               static_cast<const uint8_t*>(s.qkv) + ((size_t)(Tc - fresh) * 3 * d + d) * 2,
+                               (size_t)3 * d * 2, (size_t)2 * d * 2, fresh, cudaMemcpyDeviceToDevice, st),
              "attention cache update");
+    }
     // conv module: GLU rows after the conv cache, causal depthwise over both
-    PKC_CK(layernorm_launch(x, Tc, d, L.ln_conv_g, L.ln_conv_b, s.hbuf, bf, nullptr, nullptr, false, st), "ln");
-    PKC_ST(gemm(s.hbuf, d, L.pw1_w, d, bf, Tc, 2 * d, d, EPI_GLU_H, ACT_NONE, 1.f, L.pw1_b, cvc + (size_t)LP * d * 2,
-                d, st, "stream_pw1_glu", err));
+    PKC_ST(ln_gemm(L.ln_conv_g, L.ln_conv_b, L.pw1_w, nullptr, 2 * d, EPI_GLU_H, ACT_NONE, 1.f, L.pw1_b,
+                   cvc + (size_t)LP * d * 2, d, "stream_pw1_glu"));
     if (LP > 0)
       PKC_CK(cudaMemcpyAsync(cvn, cvc + (size_t)Tc * d * 2, (size_t)LP * d * 2, cudaMemcpyDeviceToDevice, st),
              "conv cache update");
@@ -344,15 +363,11 @@ pkc_status DeviceRunner::stream_issue(StreamState& s, int n, int Tc, int drop, s
            "stream dwconv");
     PKC_ST(gemm(s.hbuf, d, L.pw2_w, d, bf, Tc, d, d, EPI_RESID_F32, ACT_NONE, 1.f, L.pw2_b, x, d, st, "stream_pw2",
                 err));
-    PKC_CK(layernorm_launch(x, Tc, d, L.ln_ff2_g, L.ln_ff2_b, s.hbuf, bf, nullptr, nullptr, false, st), "ln");
-    PKC_ST(gemm(s.hbuf, d, L.ff2_w1, d, bf, Tc, FF, d, EPI_STORE_H, ACT_SILU, 1.f, L.ff2_b1, s.ffh, FF, st,
-                "stream_ffn", err, &L.ff2_q1));
+    PKC_ST(ln_gemm(L.ln_ff2_g, L.ln_ff2_b, L.ff2_w1, &L.ff2_q1, FF, EPI_STORE_H, ACT_SILU, 1.f, L.ff2_b1, s.ffh, FF,
+                   "stream_ffn"));
     PKC_ST(gemm(s.ffh, FF, L.ff2_w2, FF, bf, Tc, d, FF, EPI_RESID_F32, ACT_NONE, 0.5f, L.ff2_b2, x, d, st,
                 "stream_ffn", err, &L.ff2_q2));
-    const bool last = li + 1 == Lc;
-    const LayerWeights* N = last ? nullptr : &w_.layers[li + 1];
-    PKC_CK(layernorm_launch(x, Tc, d, L.ln_out_g, L.ln_out_b, last ? nullptr : s.hbuf, bf,
-                            last ? nullptr : N->ln_ff1_g, last ? nullptr : N->ln_ff1_b, true, st), "ln");
+    PKC_CK(layernorm_launch(x, Tc, d, L.ln_out_g, L.ln_out_b, nullptr, bf, nullptr, nullptr, true, st), "ln");
   }
   PKC_CK(stream_advance_launch(s.d_filled, Tc, cache, st), "stream advance");
   PKC_CK(cudaMemcpyAsync(s.h_out, x, (size_t)Tc * d * 4, cudaMemcpyDeviceToHost, st), "stream output download");
