@@ -426,10 +426,10 @@ def stream_windows(sch, T):
 def stream_launches(cfg, n_windows, n_tc_changes):
     """Kernels of one stream (16-bit weights): per chunk 6 subsampling
     launches, 11 per layer (the pre-norms run inside their skinny GEMMs; the
-    layer's output norm is its own kernel) and the cache-fill update; the
-    positional table and every layer's linear_pos (2) when the chunk length
-    changes."""
-    return n_windows * (6 + 11 * cfg.n_layers + 1) + 2 * n_tc_changes
+    layer's output norm is its own kernel), the cache roll and the cache-fill
+    update; the positional table and every layer's linear_pos (2) when the
+    chunk length changes."""
+    return n_windows * (6 + 11 * cfg.n_layers + 2) + 2 * n_tc_changes
 
 
 def run_stream(args, rank, world, local_rank):

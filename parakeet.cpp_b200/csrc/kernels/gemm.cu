@@ -1442,6 +1442,7 @@ int gemm_tile_m() { return BM; }
 constexpr int SKINNY_M = 16;
 constexpr int SKINNY_THREADS = 256;
 constexpr int SKINNY_WARPS = SKINNY_THREADS / 32;
+constexpr int SKINNY_PRE = 8;  // 16-byte weight chunks per lane fetched before the dependency wait (K <= 2048)
 
 template <typename H>
 __device__ __forceinline__ void h8_to_f(const uint4& v, float (&f)[8]) {
@@ -1458,8 +1459,26 @@ __global__ void __launch_bounds__(SKINNY_THREADS) k_gemm_skinny(const H* __restr
                                                                 const H* __restrict__ B, int ldb, GemmArgs args) {
   extern __shared__ uint4 sk_a[];  // A rows [M][K / 8] chunks of 8
   constexpr bool PAIRED = EPI == EPI_GLU_H;
-  pdl_wait();
   const int M = args.M, k8 = args.K / 8;
+  const int units = PAIRED ? args.N / 2 : args.N;
+  // the weight does not depend on the kernel before this one: the warp's first
+  // row (first SKINNY_PRE chunks per lane) is fetched before waiting for it
+  const int u_first = blockIdx.x * SKINNY_WARPS + (threadIdx.x >> 5);
+  uint4 pa[SKINNY_PRE], pg[SKINNY_PRE];
+  if (u_first < units) {
+    const int na = PAIRED ? (u_first / (BN / 2)) * BN + u_first % (BN / 2) : u_first;
+    const uint4* wa = reinterpret_cast<const uint4*>(B + (size_t)na * ldb);
+    const uint4* wg = reinterpret_cast<const uint4*>(B + (size_t)(na + BN / 2) * ldb);
+#pragma unroll
+    for (int j = 0; j < SKINNY_PRE; ++j) {
+      const int c = (threadIdx.x & 31) + 32 * j;
+      if (c < k8) {
+        pa[j] = __ldg(wa + c);
+        if constexpr (PAIRED) pg[j] = __ldg(wg + c);
+      }
+    }
+  }
+  pdl_wait();
   if (args.ln_x) {
     // LayerNorm of row m by warp m % 8: mean, then the mean square deviation
     // (two passes, as ggml_norm), then the affine, rounded into the staging
@@ -1506,22 +1525,24 @@ __global__ void __launch_bounds__(SKINNY_THREADS) k_gemm_skinny(const H* __restr
   }
   __syncthreads();
   pdl_trigger();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int units = PAIRED ? args.N / 2 : args.N;
-  for (int u = blockIdx.x * SKINNY_WARPS + warp; u < units; u += gridDim.x * SKINNY_WARPS) {
+  const int lane = threadIdx.x & 31;
+  for (int u = u_first; u < units; u += gridDim.x * SKINNY_WARPS) {
     // GLU: value row blk * BN + c and its gate row BN / 2 later, output column u
     const int na = PAIRED ? (u / (BN / 2)) * BN + u % (BN / 2) : u;
     const int ng = na + BN / 2;
     const uint4* wa = reinterpret_cast<const uint4*>(B + (size_t)na * ldb);
     const uint4* wg = reinterpret_cast<const uint4*>(B + (size_t)(PAIRED ? ng : na) * ldb);
+    // the residual this lane updates, in flight during the dot products
+    float resid = 0.f;
+    if constexpr (EPI == EPI_RESID_F32)
+      if (lane < M) resid = reinterpret_cast<const float*>(args.out)[(size_t)lane * args.ldo + u];
     float acc[SKINNY_M], accg[SKINNY_M];
 #pragma unroll
     for (int m = 0; m < SKINNY_M; ++m) acc[m] = accg[m] = 0.f;
-#pragma unroll 2
-    for (int c = lane; c < k8; c += 32) {
+    auto dot_chunk = [&](const uint4& wav, const uint4& wgv, int c) {
       float fa[8], fg[8];
-      h8_to_f<H>(__ldg(wa + c), fa);
-      if constexpr (PAIRED) h8_to_f<H>(__ldg(wg + c), fg);
+      h8_to_f<H>(wav, fa);
+      if constexpr (PAIRED) h8_to_f<H>(wgv, fg);
 #pragma unroll
       for (int m = 0; m < SKINNY_M; ++m) {
         if (m < M) {
@@ -1534,6 +1555,24 @@ __global__ void __launch_bounds__(SKINNY_THREADS) k_gemm_skinny(const H* __restr
           }
         }
       }
+    };
+    const bool first = u == u_first;
+#pragma unroll
+    for (int j = 0; j < SKINNY_PRE; ++j) {
+      const int c = lane + 32 * j;
+      if (c < k8) {
+        const uint4 va = first ? pa[j] : __ldg(wa + c);
+        uint4 vg = va;
+        if constexpr (PAIRED) vg = first ? pg[j] : __ldg(wg + c);
+        dot_chunk(va, vg, c);
+      }
+    }
+#pragma unroll 2
+    for (int c = lane + 32 * SKINNY_PRE; c < k8; c += 32) {
+      const uint4 va = __ldg(wa + c);
+      uint4 vg = va;
+      if constexpr (PAIRED) vg = __ldg(wg + c);
+      dot_chunk(va, vg, c);
     }
     // row m's sum ends in lane m
     float mine = 0.f, mineg = 0.f;
@@ -1556,8 +1595,7 @@ __global__ void __launch_bounds__(SKINNY_THREADS) k_gemm_skinny(const H* __restr
       const size_t ro = (size_t)lane * args.ldo + u;
       const float b = args.bias ? args.bias[na] : 0.f;
       if constexpr (EPI == EPI_RESID_F32) {
-        float* o = reinterpret_cast<float*>(args.out) + ro;
-        *o += args.alpha * (mine + b);
+        reinterpret_cast<float*>(args.out)[ro] = resid + args.alpha * (mine + b);
       } else if constexpr (EPI == EPI_STORE_F32) {
         reinterpret_cast<float*>(args.out)[ro] = args.alpha * (mine + b);
       } else if constexpr (EPI == EPI_GLU_H) {

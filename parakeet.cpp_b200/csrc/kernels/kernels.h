@@ -208,6 +208,20 @@ struct StreamAttnArgs {
   int att_left, att_right;
 };
 cudaError_t stream_attention_launch(const StreamAttnArgs& a, bool bf16, cudaStream_t st);
+// The next caches of every layer after a chunk (into the other buffer):
+// attention k | v = the last cache_len rows of [cache | the chunk's k | v],
+// conv = the last lp rows of [conv cache | the chunk's GLU rows]
+struct StreamRollArgs {
+  const void* kv_cur;    // [layers][cache_len][2d]
+  void* kv_next;
+  const void* qkv;       // [layers][qkv_layer_rows][3d], the chunk's rows first
+  int qkv_layer_rows;
+  const void* cv_cur;    // [layers][cv_layer_rows][d]: lp cache rows, then Tc GLU rows
+  void* cv_next;
+  int cv_layer_rows;
+  int layers, d, cache_len, Tc, lp;
+};
+cudaError_t stream_roll_launch(const StreamRollArgs& a, cudaStream_t st);
 // *filled = min(cache_len, *filled + Tc): the cache fill count after a chunk
 cudaError_t stream_advance_launch(int* filled, int Tc, int cache_len, cudaStream_t st);
 // in [K - 1 + Tc, d] (conv cache rows, then the chunk's GLU rows) -> out [Tc, d]:

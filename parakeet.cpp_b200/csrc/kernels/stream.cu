@@ -14,6 +14,8 @@
 //   k_stream_dwconv  causal depthwise Conv1d over [conv cache | GLU], + bias,
 //                    LayerNorm over channels or folded BatchNorm, SiLU
 //                    (src/streaming_encoder.cpp:286-338, src/conformer.cpp:102-154)
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
 
@@ -36,6 +38,8 @@ __device__ __forceinline__ H to_h(float v) {
 // per-stage time mask). Output [T1][F1][C] bf16, channel fastest.
 __global__ void k_causal_conv0(const float* __restrict__ mel, int F, int n, int valid, const float* __restrict__ w,
                                const float* __restrict__ b, int C, int T1, int F1, __nv_bfloat16* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (long long)T1 * F1 * C) return;
   const int c = (int)(i % C), f1 = (int)((i / C) % F1), t1 = (int)(i / ((long long)C * F1));
@@ -57,6 +61,8 @@ __global__ void k_causal_conv0(const float* __restrict__ mel, int F, int n, int 
 // in [Ti][Fi][C], rows >= valid zero; w tap-major [9][C]. Out [To][Fo][C].
 __global__ void k_causal_dw(const __nv_bfloat16* __restrict__ in, int Ti, int Fi, int valid, const float* __restrict__ w,
                             const float* __restrict__ b, int C, int To, int Fo, __nv_bfloat16* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (long long)To * Fo * C) return;
   const int c = (int)(i % C), fo = (int)((i / C) % Fo), to = (int)(i / ((long long)C * Fo));
@@ -111,6 +117,8 @@ template <typename H>
 __global__ void __launch_bounds__(SA_THREADS) k_stream_attn(StreamAttnArgs a) {
   extern __shared__ float sa_sm[];
   __shared__ float qu[128], qv[128], red[SA_THREADS / 32];
+  pdl_wait();
+  pdl_trigger();
   const int head = blockIdx.x, i = blockIdx.y;
   const int d = a.d, dk = d / a.n_heads, Tk = a.cache_len + a.Tc;
   const int ld = dk + 1;  // padded row stride: lanes of a key loop hit distinct banks
@@ -210,6 +218,8 @@ __global__ void __launch_bounds__(SD_THREADS) k_stream_dwconv(const H* __restric
                                                               const float* __restrict__ g,
                                                               const float* __restrict__ bt, int layer_norm) {
   __shared__ float red[SD_THREADS / 32];
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.x;
   float v[CPT];
   float s = 0.f;
@@ -256,16 +266,16 @@ cudaError_t causal_conv0_launch(const float* mel, int F, int n, int valid, const
                                 int T1, int F1, __nv_bfloat16* out, cudaStream_t st) {
   const long long total = (long long)T1 * F1 * C;
   if (total <= 0) return cudaSuccess;
-  k_causal_conv0<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(mel, F, n, valid, w, b, C, T1, F1, out);
-  return cudaGetLastError();
+  return launch_pdl(k_causal_conv0, dim3((unsigned)((total + 255) / 256)), dim3(256), 0, st, mel, F, n, valid, w, b, C,
+                    T1, F1, out);
 }
 
 cudaError_t causal_dw_launch(const __nv_bfloat16* in, int Ti, int Fi, int valid, const float* w, const float* b,
                              int C, int To, int Fo, __nv_bfloat16* out, cudaStream_t st) {
   const long long total = (long long)To * Fo * C;
   if (total <= 0) return cudaSuccess;
-  k_causal_dw<<<(unsigned)((total + 255) / 256), 256, 0, st>>>(in, Ti, Fi, valid, w, b, C, To, Fo, out);
-  return cudaGetLastError();
+  return launch_pdl(k_causal_dw, dim3((unsigned)((total + 255) / 256)), dim3(256), 0, st, in, Ti, Fi, valid, w, b, C,
+                    To, Fo, out);
 }
 
 cudaError_t stream_attention_launch(const StreamAttnArgs& a, bool bf16, cudaStream_t st) {
@@ -280,24 +290,58 @@ cudaError_t stream_attention_launch(const StreamAttnArgs& a, bool bf16, cudaStre
   if (bf16) {
     e = cudaFuncSetAttribute(k_stream_attn<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    k_stream_attn<__nv_bfloat16><<<grid, SA_THREADS, smem, st>>>(a);
-  } else {
-    e = cudaFuncSetAttribute(k_stream_attn<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-    if (e != cudaSuccess) return e;
-    k_stream_attn<__half><<<grid, SA_THREADS, smem, st>>>(a);
+    return launch_pdl(k_stream_attn<__nv_bfloat16>, grid, dim3(SA_THREADS), smem, st, a);
   }
-  return cudaGetLastError();
+  e = cudaFuncSetAttribute(k_stream_attn<__half>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  return launch_pdl(k_stream_attn<__half>, grid, dim3(SA_THREADS), smem, st, a);
 }
 
 namespace {
 __global__ void k_stream_advance(int* filled, int Tc, int cache_len) {
+  pdl_wait();
+  pdl_trigger();
   if (threadIdx.x == 0 && blockIdx.x == 0) *filled = min(cache_len, *filled + Tc);
+}
+
+// Every layer's next caches (grid.y = layer): attention k | v rows = the last
+// cache_len of [cache | chunk] (the chunk's rows at column d of its qkv rows),
+// conv rows = the last K - 1 of [conv cache | GLU rows]. 16-byte copies.
+__global__ void k_stream_roll(StreamRollArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  const int l = blockIdx.y;
+  const int d8 = a.d / 8;  // 16-byte chunks per d elements
+  const uint4* kvc = static_cast<const uint4*>(a.kv_cur) + (size_t)l * a.cache_len * 2 * d8;
+  uint4* kvn = static_cast<uint4*>(a.kv_next) + (size_t)l * a.cache_len * 2 * d8;
+  const uint4* q = static_cast<const uint4*>(a.qkv) + (size_t)l * a.qkv_layer_rows * 3 * d8;
+  const uint4* cvc = static_cast<const uint4*>(a.cv_cur) + (size_t)l * a.cv_layer_rows * d8;
+  uint4* cvn = static_cast<uint4*>(a.cv_next) + (size_t)l * a.cv_layer_rows * d8;
+  const int keep = max(0, a.cache_len - a.Tc), fresh = a.cache_len - keep;
+  const int n_kv = a.cache_len * 2 * d8, n_cv = a.lp * d8;
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < n_kv + n_cv; e += gridDim.x * blockDim.x) {
+    if (e < n_kv) {
+      const int r = e / (2 * d8), c = e % (2 * d8);
+      kvn[e] = r < keep ? kvc[(size_t)(r + a.Tc) * 2 * d8 + c]
+                        : q[(size_t)(a.Tc - fresh + (r - keep)) * 3 * d8 + d8 + c];
+    } else {
+      const int f = e - n_kv;  // conv cache row r = row Tc + r of [cache | GLU]
+      cvn[f] = cvc[(size_t)a.Tc * d8 + f];
+    }
+  }
 }
 }  // namespace
 
 cudaError_t stream_advance_launch(int* filled, int Tc, int cache_len, cudaStream_t st) {
-  k_stream_advance<<<1, 32, 0, st>>>(filled, Tc, cache_len);
-  return cudaGetLastError();
+  return launch_pdl(k_stream_advance, dim3(1), dim3(32), 0, st, filled, Tc, cache_len);
+}
+
+cudaError_t stream_roll_launch(const StreamRollArgs& a, cudaStream_t st) {
+  if (a.d % 8 || a.layers <= 0) return cudaErrorInvalidValue;
+  const long long n = (long long)a.cache_len * 2 * (a.d / 8) + (long long)a.lp * (a.d / 8);
+  if (n <= 0) return cudaSuccess;
+  const unsigned gx = (unsigned)std::min<long long>((n + 255) / 256, 64);
+  return launch_pdl(k_stream_roll, dim3(gx, a.layers), dim3(256), 0, st, a);
 }
 
 cudaError_t stream_dwconv_launch(const void* in, void* out, int Tc, int d, int K, const float* w, const float* bias,
@@ -306,12 +350,10 @@ cudaError_t stream_dwconv_launch(const void* in, void* out, int Tc, int d, int K
   if (d > 4 * SD_THREADS) return cudaErrorInvalidValue;
   const int ln = layer_norm ? 1 : 0;
   if (bf16)
-    k_stream_dwconv<__nv_bfloat16, 4><<<Tc, SD_THREADS, 0, st>>>(static_cast<const __nv_bfloat16*>(in),
-                                                                  static_cast<__nv_bfloat16*>(out), d, K, w, bias, g, b, ln);
-  else
-    k_stream_dwconv<__half, 4><<<Tc, SD_THREADS, 0, st>>>(static_cast<const __half*>(in), static_cast<__half*>(out), d,
-                                                           K, w, bias, g, b, ln);
-  return cudaGetLastError();
+    return launch_pdl(k_stream_dwconv<__nv_bfloat16, 4>, dim3(Tc), dim3(SD_THREADS), 0, st,
+                      static_cast<const __nv_bfloat16*>(in), static_cast<__nv_bfloat16*>(out), d, K, w, bias, g, b, ln);
+  return launch_pdl(k_stream_dwconv<__half, 4>, dim3(Tc), dim3(SD_THREADS), 0, st, static_cast<const __half*>(in),
+                    static_cast<__half*>(out), d, K, w, bias, g, b, ln);
 }
 
 }  // namespace pkc

@@ -188,7 +188,7 @@ pkc_status DeviceRunner::stream_step(StreamState& s, const float* mel, int n, bo
                  o_s2a = take((size_t)T2 * F2 * C * 2), o_s2b = take((size_t)T2 * F2 * C * 2),
                  o_s3a = take((size_t)T3 * F3 * C * 2), o_s3b = take((size_t)T3 * F3 * C * 2),
                  o_x = take((size_t)T3 * d * 4), o_h = take((size_t)cap * d * 2), o_ff = take((size_t)cap * FF * 2),
-                 o_qkv = take((size_t)cap * 3 * d * 2), o_ctx = take((size_t)cap * d * 2), o_pe = take((size_t)Pc * d * 2),
+                 o_qkv = take((size_t)Lc * cap * 3 * d * 2), o_ctx = take((size_t)cap * d * 2), o_pe = take((size_t)Pc * d * 2),
                  o_pt = take((size_t)Pc * Lc * d * 2);
     if (sz > s.scratch_bytes) {
       if (s.scratch) cudaFree(s.scratch);
@@ -319,9 +319,7 @@ pkc_status DeviceRunner::stream_issue(StreamState& s, int n, int Tc, int drop, s
   for (int li = 0; li < Lc; ++li) {
     const LayerWeights& L = w_.layers[li];
     uint8_t* kvc = cache ? static_cast<uint8_t*>(s.kv[s.cur]) + (size_t)li * kv_rows * 2 * d * 2 : nullptr;
-    uint8_t* kvn = cache ? static_cast<uint8_t*>(s.kv[1 - s.cur]) + (size_t)li * kv_rows * 2 * d * 2 : nullptr;
     uint8_t* cvc = static_cast<uint8_t*>(s.cv[s.cur]) + (size_t)li * cv_rows * d * 2;
-    uint8_t* cvn = static_cast<uint8_t*>(s.cv[1 - s.cur]) + (size_t)li * cv_rows * d * 2;
     // x -> LayerNorm(g, b) -> GEMM: the norm inside the skinny GEMM's staging
     // when it can run there (few rows, 16-bit weight), else its own kernel
     auto ln_gemm = [&](const float* g, const float* b, const void* W, const QWeight* q, int N, int epi, int act,
@@ -335,30 +333,18 @@ pkc_status DeviceRunner::stream_issue(StreamState& s, int n, int Tc, int drop, s
     PKC_ST(gemm(s.ffh, FF, L.ff1_w2, FF, bf, Tc, d, FF, EPI_RESID_F32, ACT_NONE, 0.5f, L.ff1_b2, x, d, st,
                 "stream_ffn", err, &L.ff1_q2));
     // q | k | v of the chunk's frames; k | v of the cached frames are in kvc
-    PKC_ST(ln_gemm(L.ln_att_g, L.ln_att_b, L.qkv_w, &L.qkv_q, 3 * d, EPI_STORE_H, ACT_NONE, 1.f, L.qkv_b, s.qkv, 3 * d,
+    // (each layer keeps its own qkv rows: the cache roll after the last layer reads them)
+    uint8_t* qkv = static_cast<uint8_t*>(s.qkv) + (size_t)li * cap * 3 * d * 2;
+    PKC_ST(ln_gemm(L.ln_att_g, L.ln_att_b, L.qkv_w, &L.qkv_q, 3 * d, EPI_STORE_H, ACT_NONE, 1.f, L.qkv_b, qkv, 3 * d,
                    "stream_qkv"));
-    StreamAttnArgs sa{s.qkv, kvc, static_cast<const uint8_t*>(s.ptab) + (size_t)li * d * 2, Ld, L.pos_u, L.pos_v,
+    StreamAttnArgs sa{qkv, kvc, static_cast<const uint8_t*>(s.ptab) + (size_t)li * d * 2, Ld, L.pos_u, L.pos_v,
                       s.ctx, d, H, Tc, cache, s.d_filled, c.att_left, c.att_right};
     PKC_CK(stream_attention_launch(sa, bf, st), "stream attention");
     PKC_ST(gemm(s.ctx, d, L.out_w, d, bf, Tc, d, d, EPI_RESID_F32, ACT_NONE, 1.f, L.out_b, x, d, st, "stream_out",
                 err, &L.out_q));
-    // next attention cache: the last cache_len k | v rows of [cache | chunk]
-    if (cache > 0) {
-      const int keep = std::max(0, cache - Tc), fresh = cache - keep;  // fresh <= Tc
-      if (keep > 0)
-        PKC_CK(cudaMemcpyAsync(kvn, kvc + (size_t)Tc * 2 * d * 2, (size_t)keep * 2 * d * 2, cudaMemcpyDeviceToDevice,
-                               st), "attention cache update");
-      PKC_CK(cudaMemcpy2DAsync(kvn + (size_t)keep * 2 * d * 2, (size_t)2 * d * 2,
-                               static_cast<const uint8_t*>(s.qkv) + ((size_t)(Tc - fresh) * 3 * d + d) * 2,
-                               (size_t)3 * d * 2, (size_t)2 * d * 2, fresh, cudaMemcpyDeviceToDevice, st),
-             "attention cache update");
-    }
     // conv module: GLU rows after the conv cache, causal depthwise over both
     PKC_ST(ln_gemm(L.ln_conv_g, L.ln_conv_b, L.pw1_w, nullptr, 2 * d, EPI_GLU_H, ACT_NONE, 1.f, L.pw1_b,
                    cvc + (size_t)LP * d * 2, d, "stream_pw1_glu"));
-    if (LP > 0)
-      PKC_CK(cudaMemcpyAsync(cvn, cvc + (size_t)Tc * d * 2, (size_t)LP * d * 2, cudaMemcpyDeviceToDevice, st),
-             "conv cache update");
     PKC_CK(stream_dwconv_launch(cvc, s.hbuf, Tc, d, K, L.dw_w, L.dw_b, L.bn_scale, L.bn_shift, c.conv_ln, bf, st),
            "stream dwconv");
     PKC_ST(gemm(s.hbuf, d, L.pw2_w, d, bf, Tc, d, d, EPI_RESID_F32, ACT_NONE, 1.f, L.pw2_b, x, d, st, "stream_pw2",
@@ -369,6 +355,10 @@ pkc_status DeviceRunner::stream_issue(StreamState& s, int n, int Tc, int drop, s
                 "stream_ffn", err, &L.ff2_q2));
     PKC_CK(layernorm_launch(x, Tc, d, L.ln_out_g, L.ln_out_b, nullptr, bf, nullptr, nullptr, true, st), "ln");
   }
+  // every layer's next caches, in one kernel after the last layer
+  StreamRollArgs ra{s.kv[s.cur], s.kv[1 - s.cur], s.qkv, cap, s.cv[s.cur], s.cv[1 - s.cur], (int)cv_rows, Lc, d, cache,
+                    Tc, LP};
+  PKC_CK(stream_roll_launch(ra, st), "stream cache roll");
   PKC_CK(stream_advance_launch(s.d_filled, Tc, cache, st), "stream advance");
   PKC_CK(cudaMemcpyAsync(s.h_out, x, (size_t)Tc * d * 4, cudaMemcpyDeviceToHost, st), "stream output download");
   return PKC_OK;
