@@ -519,6 +519,43 @@ def run_stream(args, rank, world, local_rank):
                              "small GEMMs, not bytes"},
         "clocks": clk.summary(),
     }
+    # serving form: args.stream_batch streams stepped together (pkc_stream_step_batch)
+    S = args.stream_batch
+    if S > 1:
+        streams = [pkc.Stream(model) for _ in range(S)]
+        mels_b = [np.random.default_rng(100 + i).standard_normal((cfg.n_mels, T)).astype(np.float32) for i in range(S)]
+        win_b = [[np.ascontiguousarray(mb[:, lo:hi]) for lo, hi, _ in wins] for mb in mels_b]
+
+        def batch_stream(lat=None):
+            for s in streams:
+                s.reset()
+            for k, (lo, hi, last) in enumerate(wins):
+                t = time.perf_counter()
+                pkc.stream_step_batch(streams, [wb[k] for wb in win_b], [last] * S)
+                if lat is not None:
+                    lat.append((time.perf_counter() - t) * 1e3)
+
+        for _ in range(args.warmup):
+            batch_stream()
+        blat = []
+        torch.cuda.synchronize(dev)
+        b0, b1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        b0.record(ext)
+        tb = time.perf_counter()
+        for _ in range(args.steps):
+            batch_stream(blat)
+        b1.record(ext)
+        torch.cuda.synchronize(dev)
+        bwall = time.perf_counter() - tb
+        bms = b0.elapsed_time(b1)
+        for s in streams:
+            s.close()
+        blat = sorted(blat)
+        bp = lambda q: round(blat[min(len(blat) - 1, int(q * len(blat)))], 3)
+        line["batched"] = {"streams": S, "value": round(S * audio / (bms / 1e3), 1), "unit": UNIT,
+                           "e2e_value": round(S * audio / bwall, 1),
+                           "chunk_latency_ms": {"p50": bp(0.5), "p99": bp(0.99), "max": round(blat[-1], 3)},
+                           "api": "pkc_stream_step_batch (all streams' windows in one chunk step)"}
     if not args.no_cpu_baseline:
         import oracle
         w = oracle.Weights(path)
@@ -617,6 +654,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--stream-seconds", type=float, default=20.0,
                     help="audio per stream for the streaming configurations")
+    ap.add_argument("--stream-batch", type=int, default=32,
+                    help="streams stepped together in the streaming configurations' batched measurement")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3) if args.impl == "ours" else args.warmup
     world = env_int("WORLD_SIZE", 1)

@@ -131,6 +131,17 @@ pkc_status pkc_stream_reset(pkc_stream* s);
 pkc_status pkc_stream_step(pkc_stream* s, const float* mel, int n_frames, int is_last, float* out,
                            size_t out_cap_floats, int* n_valid_out);
 
+/* Several streams of one model stepped together, one window each: their
+   frames are stacked so every weight is read once for all of them (the
+   serving form of step()). All streams belong to the same model and device
+   slot, every window is n_frames long, and the streams are all at their first
+   window or all past it. outs[i] receives stream i's valid frames
+   (n_valid_out[i] of them, out_cap_floats >= that * d_model); is_last[i] as in
+   pkc_stream_step. Up to 16 stacked frames the result equals stepping each
+   stream alone bit for bit. */
+pkc_status pkc_stream_step_batch(pkc_stream* const* streams, int n_streams, const float* const* mels, int n_frames,
+                                 const int* is_last, float* const* outs, size_t out_cap_floats, int* n_valid_out);
+
 /* step_num(): steps taken since begin / reset; -1 for NULL. */
 int pkc_stream_step_num(const pkc_stream* s);
 

@@ -197,6 +197,30 @@ pkc_status pkc_stream_step(pkc_stream* s, const float* mel, int n_frames, int is
   }
 }
 
+pkc_status pkc_stream_step_batch(pkc_stream* const* streams, int n_streams, const float* const* mels, int n_frames,
+                                 const int* is_last, float* const* outs, size_t out_cap_floats, int* n_valid_out) {
+  if (!streams || n_streams <= 0 || !mels || !is_last || !outs || !n_valid_out)
+    return pkc::set_thread_error(PKC_ERR_ARG, "pkc_stream_step_batch: NULL argument or no streams");
+  pkc_model* m = streams[0] ? streams[0]->m : nullptr;
+  if (!m) return pkc::set_thread_error(PKC_ERR_ARG, "pkc_stream_step_batch: NULL stream");
+  std::vector<pkc::DeviceRunner::StreamState*> ss((size_t)n_streams);
+  for (int i = 0; i < n_streams; ++i) {
+    if (!streams[i]) return fail(m, PKC_ERR_ARG, "pkc_stream_step_batch: NULL stream " + std::to_string(i));
+    if (streams[i]->m != m || streams[i]->r != streams[0]->r)
+      return fail(m, PKC_ERR_ARG, "pkc_stream_step_batch: the streams must belong to one model and device");
+    ss[(size_t)i] = streams[i]->st;
+  }
+  try {
+    std::lock_guard<std::mutex> lk(m->mu);
+    std::string err;
+    const pkc_status st = streams[0]->r->stream_step_batch(ss.data(), n_streams, mels, n_frames, is_last, outs,
+                                                           out_cap_floats, n_valid_out, err);
+    return st == PKC_OK ? PKC_OK : fail(m, st, "pkc_stream_step_batch: " + err);
+  } catch (const std::bad_alloc&) {
+    return fail(m, PKC_ERR_OOM, "host allocation failed");
+  }
+}
+
 int pkc_stream_step_num(const pkc_stream* s) { return s ? pkc::DeviceRunner::stream_step_num(*s->st) : -1; }
 
 void pkc_stream_free(pkc_stream* s) {

@@ -120,6 +120,7 @@ DeviceRunner::~DeviceRunner() {
   cudaSetDevice(device_);
   if (stream_) cudaStreamSynchronize(stream_);
   drop_graphs();
+  stream_scratch_free();
   for (cudaEvent_t e : ev_pool_) cudaEventDestroy(e);
   if (ws_) cudaFree(ws_);
   if (err_word_) cudaFree(err_word_);

@@ -102,6 +102,11 @@ class DeviceRunner {
   // pre-encode overlap included); out [valid][d] host f32.
   pkc_status stream_step(StreamState& s, const float* mel, int n_frames, bool is_last, float* out,
                          size_t out_cap_floats, int* n_valid, std::string& err);
+  // S streams of this runner stepped together, one window each (all
+  // n_frames long; all at their first window or all past it)
+  pkc_status stream_step_batch(StreamState* const* ss, int S, const float* const* mels, int n_frames,
+                               const int* is_last, float* const* outs, size_t out_cap_floats, int* n_valid,
+                               std::string& err);
   static int stream_step_num(const StreamState& s);
 
  private:
@@ -119,7 +124,10 @@ class DeviceRunner {
   };
   pkc_status run_layer(const Plan& p, int li, const Part& q, cudaStream_t st, std::string& err);
   pkc_status finish(cudaStream_t st, std::string& err);
-  pkc_status stream_issue(StreamState& s, int n, int Tc, int drop, std::string& err);
+  struct StreamScratch;
+  StreamScratch* sscr_ = nullptr;  // scratch, staging and graphs of the streaming chunk step
+  void stream_scratch_free();
+  pkc_status stream_issue(int S, int n, int Tc, int drop, std::string& err);
   // out = epi(LayerNorm(x rows) * g + b) . B^T on the skinny GEMM (M <= 16, 16-bit weights)
   pkc_status gemm_skinny_ln(const float* x, int ldx, const float* g, const float* b, const void* B, bool bf16, int M,
                             int N, int K, int epi, int act, float alpha, const float* bias, void* out, int ldo,

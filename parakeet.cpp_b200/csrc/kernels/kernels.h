@@ -188,47 +188,60 @@ size_t transducer_partial_bytes(int grid, int B);
 int transducer_grid();
 cudaError_t transducer_greedy_launch(const TransducerArgs& a, int grid, cudaStream_t st);
 
-// Cache-aware streaming encoder (stream.cu). Causal subsampling stages: mel
-// window [F][n] f32 (frames >= valid zero) -> [T1][F1][C] bf16, T1 = n/2 + 1,
-// F1 = F/2 + 1; depthwise stage [Ti][Fi][C] -> [Ti/2 + 1][Fi/2 + 1][C].
-cudaError_t causal_conv0_launch(const float* mel, int F, int n, int valid, const float* w, const float* b, int C,
-                                int T1, int F1, __nv_bfloat16* out, cudaStream_t st);
-cudaError_t causal_dw_launch(const __nv_bfloat16* in, int Ti, int Fi, int valid, const float* w, const float* b,
-                             int C, int To, int Fo, __nv_bfloat16* out, cudaStream_t st);
+// Cache-aware streaming encoder (stream.cu). S streams step together: their
+// windows / chunk frames are stacked along the rows, their caches are reached
+// through device tables of per-stream pointers.
+// Causal subsampling stages: mel windows [S][F][n] f32 -> [S][T1][F1][C] bf16,
+// T1 = n/2 + 1, F1 = F/2 + 1; depthwise stage [S][Ti][Fi][C] -> [S][Ti/2 + 1][Fi/2 + 1][C].
+cudaError_t causal_conv0_launch(const float* mel, int S, int F, int n, int valid, const float* w, const float* b,
+                                int C, int T1, int F1, __nv_bfloat16* out, cudaStream_t st);
+cudaError_t causal_dw_launch(const __nv_bfloat16* in, int S, int Ti, int Fi, int valid, const float* w,
+                             const float* b, int C, int To, int Fo, __nv_bfloat16* out, cudaStream_t st);
 struct StreamAttnArgs {
-  const void* qkv;       // [Tc, 3d]: the chunk's q | k | v
-  const void* kv_cache;  // [cache_len, 2d]: projected k | v of the cached frames (oldest first)
-  const void* ptab;      // this layer's projected positions: row r = relative position cache_len + Tc - 1 - r
-  int ldp;               // row stride of ptab (elements)
-  const float* bias_u;   // [d]
+  const void* qkv;              // [S * Tc, 3d]: the chunks' q | k | v, stream s at rows s * Tc
+  const void* const* kv_cache;  // [S]: stream s's k | v cache of every layer, [layers][cache_len][2d]
+  size_t kv_layer_off;          // elements from a cache base to this layer's block
+  const int* const* filled;     // [S]: stream s's count of valid cache rows (its last ones)
+  const void* ptab;             // this layer's projected positions: row r = relative position cache_len + Tc - 1 - r
+  int ldp;                      // row stride of ptab (elements)
+  const float* bias_u;          // [d]
   const float* bias_v;
-  void* ctx;             // [Tc, d]
-  int d, n_heads, Tc, cache_len;
-  const int* filled;     // device: valid frames in the attention cache (its last `filled` rows)
+  void* ctx;                    // [S * Tc, d]
+  int d, n_heads, Tc, cache_len, n_streams;
   int att_left, att_right;
 };
 cudaError_t stream_attention_launch(const StreamAttnArgs& a, bool bf16, cudaStream_t st);
-// The next caches of every layer after a chunk (into the other buffer):
-// attention k | v = the last cache_len rows of [cache | the chunk's k | v],
-// conv = the last lp rows of [conv cache | the chunk's GLU rows]
+// Causal depthwise conv over [conv cache (lp = K - 1 rows) | the chunk's GLU
+// rows] of every stream, + bias, LayerNorm over d (g, b = gamma, beta) or the
+// folded BatchNorm (g, b = scale, shift), SiLU -> out [S * Tc, d]
+struct StreamConvArgs {
+  const void* const* cv_cache;  // [S]: stream s's conv cache of every layer, [layers][lp][d]
+  size_t cv_layer_off;          // elements from a cache base to this layer's block
+  const void* glu;              // [S * Tc, d]
+  void* out;                    // [S * Tc, d]
+  const float* w;               // [K][d]
+  const float* bias;            // [d] or null
+  const float* g;
+  const float* b;
+  int d, K, Tc, n_streams, layer_norm;
+};
+cudaError_t stream_dwconv_launch(const StreamConvArgs& a, bool bf16, cudaStream_t st);
+// The next caches of every layer and stream after a chunk (into the other
+// buffers): attention k | v = the last cache_len rows of [cache | the chunk's
+// k | v], conv = the last lp rows of [conv cache | the chunk's GLU rows]
 struct StreamRollArgs {
-  const void* kv_cur;    // [layers][cache_len][2d]
-  void* kv_next;
-  const void* qkv;       // [layers][qkv_layer_rows][3d], the chunk's rows first
-  int qkv_layer_rows;
-  const void* cv_cur;    // [layers][cv_layer_rows][d]: lp cache rows, then Tc GLU rows
-  void* cv_next;
-  int cv_layer_rows;
-  int layers, d, cache_len, Tc, lp;
+  void* const* kv_cur;   // [S] -> [layers][cache_len][2d]
+  void* const* kv_next;
+  void* const* cv_cur;   // [S] -> [layers][lp][d]
+  void* const* cv_next;
+  const void* qkv;       // [layers][layer_rows][3d]: stream s's chunk rows at s * Tc
+  const void* glu;       // [layers][layer_rows][d]
+  int layer_rows;
+  int layers, d, cache_len, Tc, lp, n_streams;
 };
 cudaError_t stream_roll_launch(const StreamRollArgs& a, cudaStream_t st);
-// *filled = min(cache_len, *filled + Tc): the cache fill count after a chunk
-cudaError_t stream_advance_launch(int* filled, int Tc, int cache_len, cudaStream_t st);
-// in [K - 1 + Tc, d] (conv cache rows, then the chunk's GLU rows) -> out [Tc, d]:
-// depthwise conv + bias, then LayerNorm over d (g, b = gamma, beta) or the
-// folded BatchNorm (g, b = scale, shift), then SiLU
-cudaError_t stream_dwconv_launch(const void* in, void* out, int Tc, int d, int K, const float* w, const float* bias,
-                                 const float* g, const float* b, bool layer_norm, bool bf16, cudaStream_t st);
+// *filled[s] = min(cache_len, *filled[s] + Tc) for every stream
+cudaError_t stream_advance_launch(int* const* filled, int n_streams, int Tc, int cache_len, cudaStream_t st);
 
 // packed time-major [M, d] -> per item channels-first [d, v_b], items concatenated
 cudaError_t to_channels_first_launch(const float* x, float* out, int d, const int* item_off,

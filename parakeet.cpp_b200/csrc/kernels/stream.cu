@@ -1,19 +1,24 @@
 // Cache-aware streaming encoder kernels (reference: StreamingEncoder,
 // src/streaming_encoder.cpp, and the causal branches of the subsampling and
-// conv module). One chunk is a few frames, so these kernels are sized for
-// latency, not for HBM bandwidth; the projections around them are the same
-// tcgen05 GEMMs the offline encoder uses.
+// conv module). S streams step together: their windows and chunk frames are
+// stacked along the rows, and their caches are reached through device tables
+// of per-stream pointers. A chunk is a few frames per stream, so these kernels
+// are sized for latency; the projections around them are the library's GEMMs.
 //
-//   k_causal_conv0   Conv2d(1 -> C, 3x3, stride 2) over the mel window, both
+//   k_causal_conv0   Conv2d(1 -> C, 3x3, stride 2) over each mel window, both
 //                    axes padded 2 before and 1 after (NeMo CausalConv2D,
 //                    src/subsampling.cpp:283-295), + bias + ReLU
 //   k_causal_dw      depthwise Conv2d(C, 3x3, stride 2), same padding, + bias
-//   k_stream_attn    rel-pos attention of the chunk's queries over the
-//                    [attention cache | chunk] keys with the chunked-limited and
-//                    empty-cache mask (src/streaming_encoder.cpp:170-284)
-//   k_stream_dwconv  causal depthwise Conv1d over [conv cache | GLU], + bias,
-//                    LayerNorm over channels or folded BatchNorm, SiLU
+//   k_stream_attn    rel-pos attention of a stream's chunk queries over its
+//                    [attention cache | chunk] keys with the chunked-limited
+//                    and empty-cache mask (src/streaming_encoder.cpp:170-284)
+//   k_stream_dwconv  causal depthwise Conv1d over [conv cache | GLU rows],
+//                    + bias, LayerNorm over channels or folded BatchNorm, SiLU
 //                    (src/streaming_encoder.cpp:286-338, src/conformer.cpp:102-154)
+//   k_stream_roll    every layer's next attention and conv caches
+//   k_stream_advance the attention-cache fill counts
+// Every kernel is a programmatic dependent launch: it waits for its
+// predecessor before touching what that wrote.
 #include <algorithm>
 
 #include "common.cuh"
@@ -25,7 +30,7 @@ namespace {
 
 template <typename H>
 __device__ __forceinline__ float ld_h(const H* p) {
-  if constexpr (sizeof(H) == 2 && std::is_same<H, __half>::value) return __half2float(*p);
+  if constexpr (std::is_same<H, __half>::value) return __half2float(*p);
   else return __bfloat162float(*p);
 }
 template <typename H>
@@ -34,15 +39,20 @@ __device__ __forceinline__ H to_h(float v) {
   else return __float2bfloat16_rn(v);
 }
 
-// mel [F][n] (feature-major window); frames >= valid are zero (the reference's
-// per-stage time mask). Output [T1][F1][C] bf16, channel fastest.
-__global__ void k_causal_conv0(const float* __restrict__ mel, int F, int n, int valid, const float* __restrict__ w,
-                               const float* __restrict__ b, int C, int T1, int F1, __nv_bfloat16* __restrict__ out) {
+// mel [S][F][n] (feature-major windows); frames >= valid are zero (the
+// reference's per-stage time mask). Output [S][T1][F1][C] bf16.
+__global__ void k_causal_conv0(const float* __restrict__ mel, int S, int F, int n, int valid,
+                               const float* __restrict__ w, const float* __restrict__ b, int C, int T1, int F1,
+                               __nv_bfloat16* __restrict__ out) {
   pdl_wait();
   pdl_trigger();
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= (long long)T1 * F1 * C) return;
-  const int c = (int)(i % C), f1 = (int)((i / C) % F1), t1 = (int)(i / ((long long)C * F1));
+  const long long per = (long long)T1 * F1 * C;
+  if (i >= per * S) return;
+  const int s = (int)(i / per);
+  const long long r = i - s * per;
+  const int c = (int)(r % C), f1 = (int)((r / C) % F1), t1 = (int)(r / ((long long)C * F1));
+  const float* m = mel + (size_t)s * F * n;
   float acc = b[c];
 #pragma unroll
   for (int kh = 0; kh < 3; ++kh) {
@@ -52,20 +62,25 @@ __global__ void k_causal_conv0(const float* __restrict__ mel, int F, int n, int 
     for (int kw = 0; kw < 3; ++kw) {
       const int f = 2 * f1 + kw - 2;
       if (f < 0 || f >= F) continue;
-      acc = fmaf(w[c * 9 + kh * 3 + kw], mel[(size_t)f * n + t], acc);
+      acc = fmaf(w[c * 9 + kh * 3 + kw], m[(size_t)f * n + t], acc);
     }
   }
   out[i] = __float2bfloat16_rn(fmaxf(acc, 0.f));
 }
 
-// in [Ti][Fi][C], rows >= valid zero; w tap-major [9][C]. Out [To][Fo][C].
-__global__ void k_causal_dw(const __nv_bfloat16* __restrict__ in, int Ti, int Fi, int valid, const float* __restrict__ w,
-                            const float* __restrict__ b, int C, int To, int Fo, __nv_bfloat16* __restrict__ out) {
+// in [S][Ti][Fi][C], rows >= valid zero; w tap-major [9][C]. Out [S][To][Fo][C].
+__global__ void k_causal_dw(const __nv_bfloat16* __restrict__ in, int S, int Ti, int Fi, int valid,
+                            const float* __restrict__ w, const float* __restrict__ b, int C, int To, int Fo,
+                            __nv_bfloat16* __restrict__ out) {
   pdl_wait();
   pdl_trigger();
   const long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= (long long)To * Fo * C) return;
-  const int c = (int)(i % C), fo = (int)((i / C) % Fo), to = (int)(i / ((long long)C * Fo));
+  const long long per = (long long)To * Fo * C;
+  if (i >= per * S) return;
+  const int s = (int)(i / per);
+  const long long r = i - s * per;
+  const int c = (int)(r % C), fo = (int)((r / C) % Fo), to = (int)(r / ((long long)C * Fo));
+  const __nv_bfloat16* src = in + (size_t)s * Ti * Fi * C;
   float acc = b[c];
 #pragma unroll
   for (int kh = 0; kh < 3; ++kh) {
@@ -75,7 +90,7 @@ __global__ void k_causal_dw(const __nv_bfloat16* __restrict__ in, int Ti, int Fi
     for (int kw = 0; kw < 3; ++kw) {
       const int f = 2 * fo + kw - 2;
       if (f < 0 || f >= Fi) continue;
-      acc = fmaf(w[(kh * 3 + kw) * C + c], __bfloat162float(in[((size_t)t * Fi + f) * C + c]), acc);
+      acc = fmaf(w[(kh * 3 + kw) * C + c], __bfloat162float(src[((size_t)t * Fi + f) * C + c]), acc);
     }
   }
   out[i] = __float2bfloat16_rn(acc);
@@ -106,12 +121,12 @@ __device__ __forceinline__ float block_max(float v, float* red) {
 
 constexpr int SA_THREADS = 128;
 
-// One CTA per (head, query). Keys / values j < cache_len come from the cache
-// of projected k | v rows, j >= cache_len from the chunk's qkv rows; ptab
-// rows 0 .. 2 Tk - 2 hold the projected positions Tk - 1 ... -(Tk - 1) (row
-// stride ldp); ctx [Tc, d]. The head's key, value and position rows the query
-// reads are first staged in shared memory with coalesced 16-byte loads (f32
-// there), so the dot products run from shared memory instead of chains of
+// One CTA per (head, query, stream). Keys / values j < cache_len come from
+// the stream's cache of projected k | v rows, j >= cache_len from its chunk's
+// qkv rows; ptab rows 0 .. 2 Tk - 2 hold the projected positions Tk - 1 ...
+// -(Tk - 1) (row stride ldp). The head's key, value and position rows the
+// query reads are first staged in shared memory with coalesced 16-byte loads
+// (f32 there), so the dot products run from shared memory instead of chains of
 // dependent global loads.
 template <typename H>
 __global__ void __launch_bounds__(SA_THREADS) k_stream_attn(StreamAttnArgs a) {
@@ -119,15 +134,15 @@ __global__ void __launch_bounds__(SA_THREADS) k_stream_attn(StreamAttnArgs a) {
   __shared__ float qu[128], qv[128], red[SA_THREADS / 32];
   pdl_wait();
   pdl_trigger();
-  const int head = blockIdx.x, i = blockIdx.y;
+  const int head = blockIdx.x, i = blockIdx.y, s = blockIdx.z;
   const int d = a.d, dk = d / a.n_heads, Tk = a.cache_len + a.Tc;
   const int ld = dk + 1;  // padded row stride: lanes of a key loop hit distinct banks
   float* sK = sa_sm;                   // [Tk][ld]
   float* sV = sK + (size_t)Tk * ld;    // [Tk][ld]
   float* sP = sV + (size_t)Tk * ld;    // [Tk][ld]: position row of key j for this query
   float* prob = sP + (size_t)Tk * ld;  // [Tk]
-  const H* qkv = static_cast<const H*>(a.qkv);
-  const H* kvc = static_cast<const H*>(a.kv_cache);
+  const H* qkv = static_cast<const H*>(a.qkv) + (size_t)s * a.Tc * 3 * d;  // this stream's chunk rows
+  const H* kvc = a.cache_len ? static_cast<const H*>(a.kv_cache[s]) + a.kv_layer_off : nullptr;
   const H* ptab = static_cast<const H*>(a.ptab);
   const int qrow = a.cache_len + i;  // the query's frame among [cache | chunk]
   // stage: 8 elements (16 bytes) per load, 4 loads in flight per thread
@@ -167,7 +182,7 @@ __global__ void __launch_bounds__(SA_THREADS) k_stream_attn(StreamAttnArgs a) {
   // the cache's first cache_len - filled columns are not filled yet
   const int chunk = a.att_right + 1;
   const int left_chunks = chunk > 0 ? a.att_left / chunk : 0;
-  const int filled = min(max(*a.filled, 0), a.cache_len);
+  const int filled = min(max(*a.filled[s], 0), a.cache_len);
   const int gq = qrow, first_filled = a.cache_len - filled;
   const float scale = rsqrtf((float)dk);
   float mx = -INFINITY;
@@ -197,11 +212,12 @@ __global__ void __launch_bounds__(SA_THREADS) k_stream_attn(StreamAttnArgs a) {
   }
   sum = block_sum(sum, red);  // ends with a barrier: prob[] is complete
   const float inv = 1.0f / sum;
+  H* ctx = static_cast<H*>(a.ctx) + ((size_t)s * a.Tc + i) * d;
   for (int e = threadIdx.x; e < dk; e += SA_THREADS) {
     float acc = 0.f;
 #pragma unroll 4
     for (int j = 0; j < Tk; ++j) acc = fmaf(prob[j], sV[(size_t)j * ld + e], acc);
-    static_cast<H*>(a.ctx)[(size_t)i * d + head * dk + e] = to_h<H>(acc * inv);
+    ctx[head * dk + e] = to_h<H>(acc * inv);
   }
 }
 
@@ -209,33 +225,35 @@ size_t stream_attn_smem(int Tk, int dk) { return ((size_t)3 * Tk * (dk + 1) + Tk
 
 constexpr int SD_THREADS = 256;
 
-// One CTA per output frame t: in rows t .. t + K - 1 of [conv cache | GLU]
-// ([K - 1 + Tc, d]); out [Tc, d].
+// One CTA per (output frame t, stream): row r of [conv cache | GLU rows] is
+// cache row r (r < K - 1) or GLU row r - (K - 1) of the stream's chunk.
 template <typename H, int CPT>
-__global__ void __launch_bounds__(SD_THREADS) k_stream_dwconv(const H* __restrict__ in, H* __restrict__ out, int d,
-                                                              int K, const float* __restrict__ w,
-                                                              const float* __restrict__ bias,
-                                                              const float* __restrict__ g,
-                                                              const float* __restrict__ bt, int layer_norm) {
+__global__ void __launch_bounds__(SD_THREADS) k_stream_dwconv(StreamConvArgs a) {
   __shared__ float red[SD_THREADS / 32];
   pdl_wait();
   pdl_trigger();
-  const int t = blockIdx.x;
+  const int t = blockIdx.x, s = blockIdx.y, d = a.d, lp = a.K - 1;
+  const H* cache = lp ? static_cast<const H*>(a.cv_cache[s]) + a.cv_layer_off : nullptr;
+  const H* glu = static_cast<const H*>(a.glu) + (size_t)s * a.Tc * d;
   float v[CPT];
-  float s = 0.f;
+  float sm = 0.f;
 #pragma unroll
   for (int u = 0; u < CPT; ++u) {
     const int c = threadIdx.x + u * SD_THREADS;
     float acc = 0.f;
     if (c < d) {
-      acc = bias ? bias[c] : 0.f;
-      for (int k = 0; k < K; ++k) acc = fmaf(w[k * d + c], ld_h(in + (size_t)(t + k) * d + c), acc);
+      acc = a.bias ? a.bias[c] : 0.f;
+      for (int k = 0; k < a.K; ++k) {
+        const int r = t + k;
+        const H* row = r < lp ? cache + (size_t)r * d : glu + (size_t)(r - lp) * d;
+        acc = fmaf(a.w[k * d + c], ld_h(row + c), acc);
+      }
     }
     v[u] = acc;
-    s += acc;
+    sm += acc;
   }
-  if (layer_norm) {  // ggml_norm over channels (population variance, eps 1e-5) * gamma + beta
-    const float mean = block_sum(s, red) / (float)d;
+  if (a.layer_norm) {  // ggml_norm over channels (population variance, eps 1e-5) * gamma + beta
+    const float mean = block_sum(sm, red) / (float)d;
     float q = 0.f;
 #pragma unroll
     for (int u = 0; u < CPT; ++u)
@@ -244,48 +262,83 @@ __global__ void __launch_bounds__(SD_THREADS) k_stream_dwconv(const H* __restric
 #pragma unroll
     for (int u = 0; u < CPT; ++u) {
       const int c = threadIdx.x + u * SD_THREADS;
-      if (c < d) v[u] = (v[u] - mean) * rstd * g[c] + bt[c];
+      if (c < d) v[u] = (v[u] - mean) * rstd * a.g[c] + a.b[c];
     }
   } else {
 #pragma unroll
     for (int u = 0; u < CPT; ++u) {
       const int c = threadIdx.x + u * SD_THREADS;
-      if (c < d) v[u] = v[u] * g[c] + bt[c];
+      if (c < d) v[u] = v[u] * a.g[c] + a.b[c];
     }
   }
+  H* out = static_cast<H*>(a.out) + ((size_t)s * a.Tc + t) * d;
 #pragma unroll
   for (int u = 0; u < CPT; ++u) {
     const int c = threadIdx.x + u * SD_THREADS;
-    if (c < d) out[(size_t)t * d + c] = to_h<H>(v[u] / (1.0f + __expf(-v[u])));
+    if (c < d) out[c] = to_h<H>(v[u] / (1.0f + __expf(-v[u])));
+  }
+}
+
+__global__ void k_stream_advance(int* const* filled, int n_streams, int Tc, int cache_len) {
+  pdl_wait();
+  pdl_trigger();
+  for (int s = threadIdx.x; s < n_streams; s += blockDim.x) *filled[s] = min(cache_len, *filled[s] + Tc);
+}
+
+// grid (chunks, layers, streams). 16-byte copies.
+__global__ void k_stream_roll(StreamRollArgs a) {
+  pdl_wait();
+  pdl_trigger();
+  const int l = blockIdx.y, s = blockIdx.z;
+  const int d8 = a.d / 8;  // 16-byte chunks per d elements
+  const uint4* q = static_cast<const uint4*>(a.qkv) + ((size_t)l * a.layer_rows + (size_t)s * a.Tc) * 3 * d8;
+  const uint4* gl = static_cast<const uint4*>(a.glu) + ((size_t)l * a.layer_rows + (size_t)s * a.Tc) * d8;
+  const uint4* kvc = a.cache_len ? static_cast<const uint4*>(a.kv_cur[s]) + (size_t)l * a.cache_len * 2 * d8 : nullptr;
+  uint4* kvn = a.cache_len ? static_cast<uint4*>(a.kv_next[s]) + (size_t)l * a.cache_len * 2 * d8 : nullptr;
+  const uint4* cvc = a.lp ? static_cast<const uint4*>(a.cv_cur[s]) + (size_t)l * a.lp * d8 : nullptr;
+  uint4* cvn = a.lp ? static_cast<uint4*>(a.cv_next[s]) + (size_t)l * a.lp * d8 : nullptr;
+  const int keep = max(0, a.cache_len - a.Tc), fresh = a.cache_len - keep;
+  const int ckeep = max(0, a.lp - a.Tc), cfresh = a.lp - ckeep;
+  const int n_kv = a.cache_len * 2 * d8, n_cv = a.lp * d8;
+  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < n_kv + n_cv; e += gridDim.x * blockDim.x) {
+    if (e < n_kv) {
+      const int r = e / (2 * d8), c = e % (2 * d8);
+      kvn[e] = r < keep ? kvc[(size_t)(r + a.Tc) * 2 * d8 + c]
+                        : q[(size_t)(a.Tc - fresh + (r - keep)) * 3 * d8 + d8 + c];
+    } else {
+      const int f = e - n_kv, r = f / d8, c = f % d8;  // row r of the last lp of [cache | GLU]
+      cvn[f] = r < ckeep ? cvc[(size_t)(r + a.Tc) * d8 + c] : gl[(size_t)(a.Tc - cfresh + (r - ckeep)) * d8 + c];
+    }
   }
 }
 
 }  // namespace
 
-cudaError_t causal_conv0_launch(const float* mel, int F, int n, int valid, const float* w, const float* b, int C,
-                                int T1, int F1, __nv_bfloat16* out, cudaStream_t st) {
-  const long long total = (long long)T1 * F1 * C;
+cudaError_t causal_conv0_launch(const float* mel, int S, int F, int n, int valid, const float* w, const float* b,
+                                int C, int T1, int F1, __nv_bfloat16* out, cudaStream_t st) {
+  const long long total = (long long)S * T1 * F1 * C;
   if (total <= 0) return cudaSuccess;
-  return launch_pdl(k_causal_conv0, dim3((unsigned)((total + 255) / 256)), dim3(256), 0, st, mel, F, n, valid, w, b, C,
-                    T1, F1, out);
+  return launch_pdl(k_causal_conv0, dim3((unsigned)((total + 255) / 256)), dim3(256), 0, st, mel, S, F, n, valid, w, b,
+                    C, T1, F1, out);
 }
 
-cudaError_t causal_dw_launch(const __nv_bfloat16* in, int Ti, int Fi, int valid, const float* w, const float* b,
-                             int C, int To, int Fo, __nv_bfloat16* out, cudaStream_t st) {
-  const long long total = (long long)To * Fo * C;
+cudaError_t causal_dw_launch(const __nv_bfloat16* in, int S, int Ti, int Fi, int valid, const float* w,
+                             const float* b, int C, int To, int Fo, __nv_bfloat16* out, cudaStream_t st) {
+  const long long total = (long long)S * To * Fo * C;
   if (total <= 0) return cudaSuccess;
-  return launch_pdl(k_causal_dw, dim3((unsigned)((total + 255) / 256)), dim3(256), 0, st, in, Ti, Fi, valid, w, b, C,
-                    To, Fo, out);
+  return launch_pdl(k_causal_dw, dim3((unsigned)((total + 255) / 256)), dim3(256), 0, st, in, S, Ti, Fi, valid, w, b,
+                    C, To, Fo, out);
 }
 
 cudaError_t stream_attention_launch(const StreamAttnArgs& a, bool bf16, cudaStream_t st) {
-  if (a.Tc <= 0) return cudaSuccess;
+  if (a.Tc <= 0 || a.n_streams <= 0) return cudaSuccess;
   const int dk = a.n_heads > 0 ? a.d / a.n_heads : 0;
   const int Tk = a.cache_len + a.Tc;
   const size_t smem = stream_attn_smem(Tk, dk);
-  if (dk <= 0 || dk > 128 || dk % 8 || a.d % 8 || a.ldp % 8 || !a.filled || a.att_right < 0 || smem > 200 * 1024)
+  if (dk <= 0 || dk > 128 || dk % 8 || a.d % 8 || a.ldp % 8 || !a.filled || a.att_right < 0 || smem > 200 * 1024 ||
+      a.n_streams > 65535 || a.Tc > 65535)
     return cudaErrorInvalidValue;
-  const dim3 grid(a.n_heads, a.Tc);
+  const dim3 grid(a.n_heads, a.Tc, a.n_streams);
   cudaError_t e;
   if (bf16) {
     e = cudaFuncSetAttribute(k_stream_attn<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
@@ -297,63 +350,26 @@ cudaError_t stream_attention_launch(const StreamAttnArgs& a, bool bf16, cudaStre
   return launch_pdl(k_stream_attn<__half>, grid, dim3(SA_THREADS), smem, st, a);
 }
 
-namespace {
-__global__ void k_stream_advance(int* filled, int Tc, int cache_len) {
-  pdl_wait();
-  pdl_trigger();
-  if (threadIdx.x == 0 && blockIdx.x == 0) *filled = min(cache_len, *filled + Tc);
+cudaError_t stream_dwconv_launch(const StreamConvArgs& a, bool bf16, cudaStream_t st) {
+  if (a.Tc <= 0 || a.n_streams <= 0) return cudaSuccess;
+  if (a.d > 4 * SD_THREADS || a.K < 1 || a.n_streams > 65535) return cudaErrorInvalidValue;
+  const dim3 grid(a.Tc, a.n_streams);
+  if (bf16) return launch_pdl(k_stream_dwconv<__nv_bfloat16, 4>, grid, dim3(SD_THREADS), 0, st, a);
+  return launch_pdl(k_stream_dwconv<__half, 4>, grid, dim3(SD_THREADS), 0, st, a);
 }
 
-// Every layer's next caches (grid.y = layer): attention k | v rows = the last
-// cache_len of [cache | chunk] (the chunk's rows at column d of its qkv rows),
-// conv rows = the last K - 1 of [conv cache | GLU rows]. 16-byte copies.
-__global__ void k_stream_roll(StreamRollArgs a) {
-  pdl_wait();
-  pdl_trigger();
-  const int l = blockIdx.y;
-  const int d8 = a.d / 8;  // 16-byte chunks per d elements
-  const uint4* kvc = static_cast<const uint4*>(a.kv_cur) + (size_t)l * a.cache_len * 2 * d8;
-  uint4* kvn = static_cast<uint4*>(a.kv_next) + (size_t)l * a.cache_len * 2 * d8;
-  const uint4* q = static_cast<const uint4*>(a.qkv) + (size_t)l * a.qkv_layer_rows * 3 * d8;
-  const uint4* cvc = static_cast<const uint4*>(a.cv_cur) + (size_t)l * a.cv_layer_rows * d8;
-  uint4* cvn = static_cast<uint4*>(a.cv_next) + (size_t)l * a.cv_layer_rows * d8;
-  const int keep = max(0, a.cache_len - a.Tc), fresh = a.cache_len - keep;
-  const int n_kv = a.cache_len * 2 * d8, n_cv = a.lp * d8;
-  for (int e = blockIdx.x * blockDim.x + threadIdx.x; e < n_kv + n_cv; e += gridDim.x * blockDim.x) {
-    if (e < n_kv) {
-      const int r = e / (2 * d8), c = e % (2 * d8);
-      kvn[e] = r < keep ? kvc[(size_t)(r + a.Tc) * 2 * d8 + c]
-                        : q[(size_t)(a.Tc - fresh + (r - keep)) * 3 * d8 + d8 + c];
-    } else {
-      const int f = e - n_kv;  // conv cache row r = row Tc + r of [cache | GLU]
-      cvn[f] = cvc[(size_t)a.Tc * d8 + f];
-    }
-  }
-}
-}  // namespace
-
-cudaError_t stream_advance_launch(int* filled, int Tc, int cache_len, cudaStream_t st) {
-  return launch_pdl(k_stream_advance, dim3(1), dim3(32), 0, st, filled, Tc, cache_len);
+cudaError_t stream_advance_launch(int* const* filled, int n_streams, int Tc, int cache_len, cudaStream_t st) {
+  if (n_streams <= 0) return cudaSuccess;
+  return launch_pdl(k_stream_advance, dim3(1), dim3(256), 0, st, filled, n_streams, Tc, cache_len);
 }
 
 cudaError_t stream_roll_launch(const StreamRollArgs& a, cudaStream_t st) {
-  if (a.d % 8 || a.layers <= 0) return cudaErrorInvalidValue;
+  if (a.d % 8 || a.layers <= 0 || a.n_streams <= 0 || a.n_streams > 65535 || a.layers > 65535)
+    return cudaErrorInvalidValue;
   const long long n = (long long)a.cache_len * 2 * (a.d / 8) + (long long)a.lp * (a.d / 8);
   if (n <= 0) return cudaSuccess;
-  const unsigned gx = (unsigned)std::min<long long>((n + 255) / 256, 64);
-  return launch_pdl(k_stream_roll, dim3(gx, a.layers), dim3(256), 0, st, a);
-}
-
-cudaError_t stream_dwconv_launch(const void* in, void* out, int Tc, int d, int K, const float* w, const float* bias,
-                                 const float* g, const float* b, bool layer_norm, bool bf16, cudaStream_t st) {
-  if (Tc <= 0) return cudaSuccess;
-  if (d > 4 * SD_THREADS) return cudaErrorInvalidValue;
-  const int ln = layer_norm ? 1 : 0;
-  if (bf16)
-    return launch_pdl(k_stream_dwconv<__nv_bfloat16, 4>, dim3(Tc), dim3(SD_THREADS), 0, st,
-                      static_cast<const __nv_bfloat16*>(in), static_cast<__nv_bfloat16*>(out), d, K, w, bias, g, b, ln);
-  return launch_pdl(k_stream_dwconv<__half, 4>, dim3(Tc), dim3(SD_THREADS), 0, st, static_cast<const __half*>(in),
-                    static_cast<__half*>(out), d, K, w, bias, g, b, ln);
+  const unsigned gx = (unsigned)std::min<long long>((n + 255) / 256, 32);
+  return launch_pdl(k_stream_roll, dim3(gx, a.layers, a.n_streams), dim3(256), 0, st, a);
 }
 
 }  // namespace pkc

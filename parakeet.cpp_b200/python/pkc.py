@@ -98,6 +98,8 @@ def _declare(L):
         ("pkc_stream_reset", c_int, c_void_p),
         ("pkc_stream_step", c_int, c_void_p, c_void_p, c_int, c_int, c_void_p, c_size_t, POINTER(c_int)),
         ("pkc_stream_step_num", c_int, c_void_p),
+        ("pkc_stream_step_batch", c_int, POINTER(c_void_p), c_int, POINTER(c_void_p), c_int, POINTER(c_int),
+         POINTER(c_void_p), c_size_t, POINTER(c_int)),
         ("pkc_stream_free", None, c_void_p),
         ("pkc_pack_cache_build", c_int, c_char_p, c_char_p, ctypes.c_char_p, c_int),
         ("pkc_model_info_get", c_int, c_void_p, POINTER(ModelInfo)),
@@ -445,3 +447,21 @@ class Stream:
             self.close()
         except Exception:
             pass
+
+
+def stream_step_batch(streams, mel_windows, is_last):
+    """pkc_stream_step_batch: one window [n_mels, n] per stream (all the same
+    n) -> list of [valid_i, d_model] arrays."""
+    S = len(streams)
+    mels = [np.ascontiguousarray(m, dtype=np.float32) for m in mel_windows]
+    n = mels[0].shape[1]
+    d = streams[0].d
+    cap = (n // 8 + 2) * d
+    outs = [np.empty(cap, dtype=np.float32) for _ in range(S)]
+    hs = (c_void_p * S)(*[s._h.value for s in streams])
+    mp = (c_void_p * S)(*[m.ctypes.data for m in mels])
+    op = (c_void_p * S)(*[o.ctypes.data for o in outs])
+    last = (c_int * S)(*[1 if x else 0 for x in is_last])
+    nv = (c_int * S)()
+    _check(lib().pkc_stream_step_batch(hs, S, mp, n, last, op, cap, nv), streams[0].model.handle)
+    return [o[: nv[i] * d].reshape(nv[i], d).copy() for i, o in enumerate(outs)]

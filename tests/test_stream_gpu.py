@@ -156,3 +156,57 @@ def test_stream_graph_replay_matches_eager(stream_models, monkeypatch):
             m.close()
     for x, y in zip(*res):
         assert np.array_equal(x, y)
+
+
+def test_stream_batch_equals_streams_alone(stream_models):
+    """pkc_stream_step_batch: three streams with different audio stepped as
+    one batch (6 stacked frames, skinny GEMMs) equal each stream stepped alone
+    bit for bit, final chunk included; 12 streams (24 frames, tcgen05 GEMMs)
+    match the oracle's streaming restatement per stream and chunk."""
+    import oracle
+    import pkc
+    w = oracle.Weights(stream_models["f16"])
+    sc = oracle.StreamCfg(w)
+    T = 330
+    sched = oracle.stream_schedule(sc, T)
+    mels = [np.random.default_rng(100 + i).standard_normal((64, T)).astype(np.float32) for i in range(12)]
+    m = pkc.Model(stream_models["f16"])
+    try:
+        alone = []
+        for i in range(3):
+            s = pkc.Stream(m)
+            alone.append(run_stream(s, sched, mels[i]))
+            s.close()
+        for S in (3, 12):
+            streams = [pkc.Stream(m) for _ in range(S)]
+            got = [[] for _ in range(S)]
+            for lo, hi, last in sched:
+                outs = pkc.stream_step_batch(streams, [mels[i][:, lo:hi] for i in range(S)], [last] * S)
+                for i in range(S):
+                    got[i].append(outs[i])
+            assert all(s.step_num == len(sched) for s in streams)
+            for s in streams:
+                s.close()
+            if S == 3:
+                for i in range(3):
+                    for x, y in zip(alone[i], got[i]):
+                        assert np.array_equal(x, y)
+            else:
+                for i in (0, 5, 11):
+                    _, want = oracle_stream(w, mels[i])
+                    for g, x in zip(got[i], want):
+                        assert g.shape == x.shape
+                        if len(x):
+                            assert np.abs(g - x).max() <= TOL * np.abs(x).max()
+        # a batch mixing a stream at its first window with one past it is refused
+        a, b = pkc.Stream(m), pkc.Stream(m)
+        lo, hi, _ = sched[0]
+        a.step(mels[0][:, lo:hi])
+        lo, hi, _ = sched[1]
+        with pytest.raises(pkc.PkcError) as e:
+            pkc.stream_step_batch([a, b], [mels[0][:, lo:hi], mels[1][:, lo:hi]], [False, False])
+        assert e.value.status == 1
+        a.close()
+        b.close()
+    finally:
+        m.close()
