@@ -174,6 +174,7 @@ struct TransducerArgs {
   unsigned int* bar_count;
   int* err;
   int held;                // set by the launcher (LSTM layers resident in shared memory)
+  int jres;                // set by the launcher (joint rows resident, else streamed)
 };
 // Layer-0 input gates of every token, computed once at load:
 // out[v] = W_ih0 embed[v] + b0 for v < V1 and out[V1] = b0 (the SOS step's zero

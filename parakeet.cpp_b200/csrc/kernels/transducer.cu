@@ -61,6 +61,7 @@ struct TdLayout {
   int ldk;         // sX row stride: max(2H, 2J) + 4
   int nu, nj, nv;  // most hidden units / pred rows / joint rows any CTA owns
   int held;        // LSTM layers resident at once (L, or 1 when all do not fit)
+  int jres;        // joint rows resident (1), or streamed through a two-slot ring of TD_RG-row groups (0)
   int o_x, o_wl, o_wp, o_wj, o_bl, o_bp, o_bj, o_r, o_z, o_c, o_e, o_st;
   int wl_l0, wl_l;  // floats of the layer-0 slot ([4 nu][H]) and of a deeper layer's ([4 nu][2H])
   size_t bytes;
@@ -68,13 +69,14 @@ struct TdLayout {
 
 __host__ __device__ inline int ceil_div(int a, int b) { return (a + b - 1) / b; }
 
-__host__ __device__ inline TdLayout td_layout(int H, int J, int L, int VP, int G, int B, int held) {
+__host__ __device__ inline TdLayout td_layout(int H, int J, int L, int VP, int G, int B, int held, int jres) {
   TdLayout t;
   t.ldk = (2 * H > 2 * J ? 2 * H : 2 * J) + 4;
   t.nu = ceil_div(H, G);
   t.nj = ceil_div(J, G);
   t.nv = ceil_div(VP, G);
   t.held = held;
+  t.jres = jres;
   int o = 0;
   auto take = [&](int n) {
     const int r = o;
@@ -87,7 +89,7 @@ __host__ __device__ inline TdLayout td_layout(int H, int J, int L, int VP, int G
   // held == L: layer 0, then layers 1.. in turn; held == 1: one slot of the larger size
   t.o_wl = take(held == L ? t.wl_l0 + (L - 1) * t.wl_l : (L > 1 ? t.wl_l : t.wl_l0));
   t.o_wp = take(t.nj * H);
-  t.o_wj = take(t.nv * J);
+  t.o_wj = take(jres ? t.nv * J : 2 * TD_RG * J);
   t.o_bl = take(L * 4 * t.nu);
   t.o_bp = take(t.nj);
   t.o_bj = take(t.nv);
@@ -100,10 +102,14 @@ __host__ __device__ inline TdLayout td_layout(int H, int J, int L, int VP, int G
   return t;
 }
 
-// The layout the launch uses: every LSTM layer resident when they all fit.
+// The layout the launch uses: the first that fits of every LSTM layer
+// resident / one resident layer, each first with the joint rows resident,
+// then streamed (large vocabularies: 8 K classes are ~56 rows of J per CTA).
 inline TdLayout td_layout_for(int H, int J, int L, int VP, int G, int B) {
-  TdLayout t = td_layout(H, J, L, VP, G, B, L);
-  if (t.bytes > TD_SMEM_LIMIT && L > 1) t = td_layout(H, J, L, VP, G, B, 1);
+  TdLayout t = td_layout(H, J, L, VP, G, B, L, 1);
+  if (t.bytes > TD_SMEM_LIMIT && L > 1) t = td_layout(H, J, L, VP, G, B, 1, 1);
+  if (t.bytes > TD_SMEM_LIMIT) t = td_layout(H, J, L, VP, G, B, L, 0);
+  if (t.bytes > TD_SMEM_LIMIT && L > 1) t = td_layout(H, J, L, VP, G, B, 1, 0);
   return t;
 }
 
@@ -249,13 +255,13 @@ __device__ __noinline__ void merge_conf(const float2* parts, int G, int B, int b
 
 __global__ void __launch_bounds__(TD_THREADS, 1) k_transducer_greedy(TransducerArgs a) {
   extern __shared__ __align__(16) float sm[];
-  __shared__ __align__(8) unsigned long long s_bar[2];  // 0: weights, 1: inputs
+  __shared__ __align__(8) unsigned long long s_bar[4];  // 0: weights, 1: inputs, 2 / 3: joint ring slots
   __shared__ int s_ok, s_np, s_nd;
   __shared__ int s_dur[TD_MAX_DUR];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = gridDim.x, cta = blockIdx.x;
   const int H = a.H, J = a.J, L = a.L, V1 = a.V1, VP = a.V1 + a.D, B = a.B;
-  const TdLayout lay = td_layout(H, J, L, VP, G, B, a.held);
+  const TdLayout lay = td_layout(H, J, L, VP, G, B, a.held, a.jres);
   const int ldk = lay.ldk;
   float* sX = sm + lay.o_x;
   float* sWl = sm + lay.o_wl;
@@ -283,6 +289,9 @@ __global__ void __launch_bounds__(TD_THREADS, 1) k_transducer_greedy(TransducerA
   int* st_tcap = st_toff + B;
   int* st_emit = st_tcap + B;  // stored a token in the last iteration
   const uint32_t bar_w = smem_u32(&s_bar[0]), bar_x = smem_u32(&s_bar[1]);
+  const uint32_t bar_j[2] = {smem_u32(&s_bar[2]), smem_u32(&s_bar[3])};
+  uint32_t par_j[2] = {0, 0};
+  bool j_out[2] = {false, false};
   uint32_t par_w = 0, par_x = 0;
   bool w_out = false, x_out = false;  // a phase of bar_w / bar_x with copies not yet waited for
   unsigned int bar_target = 0;
@@ -304,6 +313,8 @@ __global__ void __launch_bounds__(TD_THREADS, 1) k_transducer_greedy(TransducerA
   if (threadIdx.x == 0) {
     mbar_init(bar_w, 1);
     mbar_init(bar_x, 1);
+    mbar_init(bar_j[0], 1);
+    mbar_init(bar_j[1], 1);
     fence_barrier_init();
   }
   for (int b = threadIdx.x; b < B; b += TD_THREADS) {
@@ -349,7 +360,7 @@ __global__ void __launch_bounds__(TD_THREADS, 1) k_transducer_greedy(TransducerA
   // resident weights: LSTM layers [0, held), pred rows, joint rows
   if (warp == 0) {
     if (lane == 0) {
-      uint32_t bytes = (uint32_t)((nj * H + nv * J) * 4);
+      uint32_t bytes = (uint32_t)((nj * H + (lay.jres ? nv : 0) * J) * 4);
       for (int l = 0; l < a.held; ++l) bytes += lstm_bytes(l);
       mbar_expect_tx(bar_w, bytes);
     }
@@ -357,7 +368,7 @@ __global__ void __launch_bounds__(TD_THREADS, 1) k_transducer_greedy(TransducerA
     for (int l = 0; l < a.held; ++l) copy_lstm(l);
     for (int r = lane; r < nj; r += 32)
       bulk_g2s(smem_u32(sWp + (size_t)r * H), a.w_pred + (size_t)(j0 + r) * H, (uint32_t)(H * 4), bar_w);
-    for (int r = lane; r < nv; r += 32)
+    for (int r = lane; r < (lay.jres ? nv : 0); r += 32)
       bulk_g2s(smem_u32(sWj + (size_t)r * J), a.w_out + (size_t)(v0 + r) * J, (uint32_t)(J * 4), bar_w);
     __syncwarp();
     if (lane == 0) mbar_arrive(bar_w);
@@ -367,7 +378,24 @@ __global__ void __launch_bounds__(TD_THREADS, 1) k_transducer_greedy(TransducerA
   auto drain = [&]() {
     if (w_out) mbar_wait(bar_w, par_w, nullptr, 0);
     if (x_out) mbar_wait(bar_x, par_x, nullptr, 0);
+    for (int q = 0; q < 2; ++q)
+      if (j_out[q]) mbar_wait(bar_j[q], par_j[q], nullptr, 0);
     __syncthreads();
+  };
+  // streamed joint rows: group g (rows v0 + 8g ..) into ring slot g & 1, one row per lane of warp 0
+  auto issue_joint = [&](int g) {
+    const int q = g & 1, r0 = g * TD_RG, nr = min(TD_RG, nv - r0);
+    if (warp == 0) {
+      fence_proxy_async_smem();
+      if (lane == 0) mbar_expect_tx(bar_j[q], (uint32_t)(nr * J * 4));
+      __syncwarp();
+      if (lane < nr)
+        bulk_g2s(smem_u32(sWj + (size_t)(q * TD_RG + lane) * J), a.w_out + (size_t)(v0 + r0 + lane) * J,
+                 (uint32_t)(J * 4), bar_j[q]);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_j[q]);
+    }
+    j_out[q] = true;
   };
   const bool stream_lstm = a.held < L;  // one resident layer: the next one is copied during the barrier
   if (!stream_lstm && !cta_wait(bar_w, par_w, w_out, a.err)) return drain();
@@ -501,6 +529,9 @@ __global__ void __launch_bounds__(TD_THREADS, 1) k_transducer_greedy(TransducerA
         warp_copy(bar_x, smem_u32(sX + i * ldk + (lane < TD_CB ? 0 : J)), src, (uint32_t)(J * 4));
       }
       x_out = true;
+      if (!lay.jres) {  // the first two row groups of the streamed joint weight
+        for (int g = 0; g < 2 && g * TD_RG < nv; ++g) issue_joint(g);
+      }
       if (!conf_done && warp == 1) merge_confs(iter - 1);  // overlaps the copies
       conf_done = true;
       if (!cta_wait(bar_x, par_x, x_out, a.err)) return drain();
@@ -515,9 +546,15 @@ __global__ void __launch_bounds__(TD_THREADS, 1) k_transducer_greedy(TransducerA
       // thread i < TD_CB: running (token max, first arg, sum of exp) and (duration max, first arg)
       float tmax = -INFINITY, tsum = 0.f, dmax = -INFINITY;
       int targ = -1, darg = -1;
-      for (int r0 = 0; r0 < nv; r0 += TD_RG) {
+      for (int r0 = 0, g = 0; r0 < nv; r0 += TD_RG, ++g) {
         const int nr = min(TD_RG, nv - r0);
-        cta_gemv(sWj + (size_t)r0 * J, J, nr, sX, ldk, J, sR, sZ);
+        const float* wj = sWj + (size_t)r0 * J;
+        if (!lay.jres) {
+          if (!cta_wait(bar_j[g & 1], par_j[g & 1], j_out[g & 1], a.err)) return drain();
+          wj = sWj + (size_t)(g & 1) * TD_RG * J;
+        }
+        cta_gemv(wj, J, nr, sX, ldk, J, sR, sZ);  // ends with a CTA barrier: the slot is free again
+        if (!lay.jres && r0 + 2 * TD_RG < nv) issue_joint(g + 2);
         if (threadIdx.x < TD_CB) {
           for (int r = 0; r < nr; ++r) {  // rows in increasing order: the first maximum wins on ties
             const int v = v0 + r0 + r;
@@ -715,13 +752,16 @@ cudaError_t transducer_greedy_launch(const TransducerArgs& a, int grid, cudaStre
     return cudaErrorInvalidValue;
   TdLayout lay = td_layout_for(a.H, a.J, a.L, VP, grid, a.B);
   if (const char* e = std::getenv("PKC_DECODE_STREAM"))  // one resident LSTM layer (the streamed path)
-    if (std::atoi(e) == 1 && a.L > 1) lay = td_layout(a.H, a.J, a.L, VP, grid, a.B, 1);
+    if (std::atoi(e) == 1 && a.L > 1) lay = td_layout(a.H, a.J, a.L, VP, grid, a.B, 1, lay.jres);
+  if (const char* e = std::getenv("PKC_DECODE_JOINT_STREAM"))  // joint rows streamed (the large-vocabulary path)
+    if (std::atoi(e) == 1) lay = td_layout(a.H, a.J, a.L, VP, grid, a.B, lay.held, 0);
   if (lay.bytes > TD_SMEM_LIMIT) return cudaErrorInvalidValue;
   cudaError_t e =
       cudaFuncSetAttribute(k_transducer_greedy, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)lay.bytes);
   if (e != cudaSuccess) return e;
   TransducerArgs ka = a;
   ka.held = lay.held;
+  ka.jres = lay.jres;
   void* params[] = {&ka};
   return cudaLaunchCooperativeKernel(reinterpret_cast<const void*>(&k_transducer_greedy), dim3(grid),
                                      dim3(TD_THREADS), params, lay.bytes, st);

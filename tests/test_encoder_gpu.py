@@ -38,6 +38,9 @@ def models(tmp_path_factory):
                                  vocab=64, pred_hidden=64, joint_hidden=64),
         "tdt2": synth.small_cfg("c2_0.6b_f16", n_layers=2, d_model=256, n_heads=4, ff_dim=1024, n_mels=80,
                                 vocab=64, pred_hidden=128, joint_hidden=96, pred_layers=2),
+        # C5's decoder geometry (8192 tokens, pred / joint 640) on a small encoder
+        "tdt_bigv": synth.small_cfg("c5_0.6b_bf16_long", n_layers=2, d_model=256, n_heads=4, ff_dim=1024,
+                                    n_mels=128),
     }
     return {k: synth.ensure_gguf(c, d) for k, c in cfgs.items()}
 
@@ -351,7 +354,7 @@ def test_pack_cache_open_matches_packed_open(models, monkeypatch, tmp_path):
             assert np.array_equal(a, b)
 
 
-@pytest.mark.parametrize("variant", ["resident", "streamed", "groups"])
+@pytest.mark.parametrize("variant", ["resident", "streamed", "groups", "joint_streamed"])
 def test_transducer_two_layer_paths(models, oracles, monkeypatch, variant):
     """Two-layer prediction LSTM (H = 128, J = 96) through the decode kernel's
     three schedules: every layer resident in shared memory; one resident layer
@@ -364,6 +367,8 @@ def test_transducer_two_layer_paths(models, oracles, monkeypatch, variant):
         monkeypatch.setenv("PKC_DECODE_STREAM", "1")
     if variant == "groups":
         monkeypatch.setenv("PKC_DECODE_GROUP", "2")
+    if variant == "joint_streamed":
+        monkeypatch.setenv("PKC_DECODE_JOINT_STREAM", "1")
     tr = oracle.Transducer(oracles("tdt2"))
     assert tr.L == 2
     m = pkc.Model(models["tdt2"])
@@ -383,6 +388,33 @@ def test_transducer_two_layer_paths(models, oracles, monkeypatch, variant):
         for t, u in zip(tk, want):
             assert abs(t[2] - u[2]) < 1e-4
     assert compared >= 3
+
+
+def test_transducer_large_vocabulary(models, oracles):
+    """8192 tokens + 5 durations with J = 640: a CTA's joint rows (56 x 640
+    f32) do not fit beside the resident LSTM / pred rows and the inputs, so
+    the decode streams them through its two-slot ring. Tokens identical to
+    the f64 oracle."""
+    import oracle
+    import pkc
+    tr = oracle.Transducer(oracles("tdt_bigv"))
+    m = pkc.Model(models["tdt_bigv"])
+    try:
+        pcm = clips([SR * 2 + 5, SR + 777, 9000], seed=71)
+        toks = m.transducer_greedy_pcm_batch(pcm)
+        xs = m.encode_pcm_batch(pcm, layout=pkc.LAYOUT_TIME_MAJOR)
+    finally:
+        m.close()
+    compared = 0
+    for tk, x in zip(toks, xs):
+        want, gap = oracle.transducer_greedy(tr, x)
+        if gap < 1e-5:
+            continue
+        compared += 1
+        assert [(t[0], t[1], t[3]) for t in tk] == [(t[0], t[1], t[3]) for t in want]
+        for t, u in zip(tk, want):
+            assert abs(t[2] - u[2]) < 1e-4
+    assert compared >= 2
 
 
 def test_transducer_absent_is_unsupported(models):
