@@ -45,7 +45,9 @@ struct DeviceRunner::StreamScratch {
   void* dev = nullptr;
   size_t bytes = 0;
   int S = -1, n = -1, Tc = -1;  // the shape the carve below was made for
-  float* mel = nullptr;
+  void** tabs = nullptr;  // device: kv_cur, kv_next, cv_cur, cv_next, filled, each [S]
+  float* mel = nullptr;   // right after the tables: one upload carries both
+  size_t in_bytes = 0;    // tables + windows
   void *s1 = nullptr, *s2a = nullptr, *s2b = nullptr, *s3a = nullptr, *s3b = nullptr;
   float* x3 = nullptr;  // subsampling output [S * T3, d]
   float* x = nullptr;   // the chunks' frames [S * Tc, d]
@@ -54,13 +56,11 @@ struct DeviceRunner::StreamScratch {
   void* glu = nullptr;  // [L][S * Tc][d]
   void* pe = nullptr;
   void* ptab = nullptr;
-  void** tabs = nullptr;  // device: kv_cur, kv_next, cv_cur, cv_next, filled, each [S]
   int pos_Tc = -1;        // Tc the positional table was made for
-  // page-locked staging
-  float* h_mel = nullptr;
+  // page-locked staging: the input mirrors the device's [tables | windows]
+  uint8_t* h_in = nullptr;
   float* h_out = nullptr;
-  void** h_tabs = nullptr;
-  size_t h_mel_cap = 0, h_out_cap = 0, h_tab_cap = 0;
+  size_t h_in_cap = 0, h_out_cap = 0;
   struct Graph {
     int S, n, Tc;
     cudaGraphExec_t exec;
@@ -94,9 +94,8 @@ void DeviceRunner::stream_scratch_free() {
   cudaSetDevice(device_);
   x->drop_graphs();
   if (x->dev) cudaFree(x->dev);
-  if (x->h_mel) cudaFreeHost(x->h_mel);
+  if (x->h_in) cudaFreeHost(x->h_in);
   if (x->h_out) cudaFreeHost(x->h_out);
-  if (x->h_tabs) cudaFreeHost(x->h_tabs);
   delete x;
   sscr_ = nullptr;
 }
@@ -228,14 +227,14 @@ pkc_status DeviceRunner::stream_step_batch(StreamState* const* ss, int S, const 
   {
     size_t sz = 0;
     auto take = [&](size_t b) { const size_t o = sz; sz += al256(b); return o; };
-    const size_t o_mel = take((size_t)S * F * n * 4), o_s1 = take((size_t)S * T1 * F1 * C * 2),
+    const size_t tab_b = al256((size_t)5 * S * sizeof(void*)), in_b = tab_b + (size_t)S * F * n * 4;
+    const size_t o_in = take(in_b), o_s1 = take((size_t)S * T1 * F1 * C * 2),
                  o_s2a = take((size_t)S * T2 * F2 * C * 2), o_s2b = take((size_t)S * T2 * F2 * C * 2),
                  o_s3a = take((size_t)S * T3 * F3 * C * 2), o_s3b = take((size_t)S * T3 * F3 * C * 2),
                  o_x3 = take((size_t)S * T3 * d * 4), o_x = take((size_t)M * d * 4), o_h = take((size_t)M * d * 2),
                  o_ff = take((size_t)M * FF * 2), o_ctx = take((size_t)M * d * 2),
                  o_qkv = take((size_t)Lc * M * 3 * d * 2), o_glu = take((size_t)Lc * M * d * 2),
-                 o_pe = take((size_t)P * d * 2), o_pt = take((size_t)P * Ld * 2),
-                 o_tab = take((size_t)5 * S * sizeof(void*));
+                 o_pe = take((size_t)P * d * 2), o_pt = take((size_t)P * Ld * 2);
     if (sz > x.bytes) {
       x.drop_graphs();
       if (x.dev) cudaFree(x.dev);
@@ -247,33 +246,31 @@ pkc_status DeviceRunner::stream_step_batch(StreamState* const* ss, int S, const 
     }
     if (x.S != S || x.n != n || x.Tc != Tc) {  // carve for this shape
       uint8_t* b = static_cast<uint8_t*>(x.dev);
-      x.mel = reinterpret_cast<float*>(b + o_mel);
+      x.tabs = reinterpret_cast<void**>(b + o_in);
+      x.mel = reinterpret_cast<float*>(b + o_in + tab_b);
+      x.in_bytes = in_b;
       x.s1 = b + o_s1; x.s2a = b + o_s2a; x.s2b = b + o_s2b; x.s3a = b + o_s3a; x.s3b = b + o_s3b;
       x.x3 = reinterpret_cast<float*>(b + o_x3);
       x.x = reinterpret_cast<float*>(b + o_x);
       x.hbuf = b + o_h; x.ffh = b + o_ff; x.ctx = b + o_ctx; x.qkv = b + o_qkv; x.glu = b + o_glu;
       x.pe = b + o_pe; x.ptab = b + o_pt;
-      x.tabs = reinterpret_cast<void**>(b + o_tab);
       x.S = S; x.n = n; x.Tc = Tc;
       x.pos_Tc = -1;
     }
   }
-  if ((size_t)S * F * n > x.h_mel_cap || (size_t)M * d > x.h_out_cap || (size_t)5 * S > x.h_tab_cap) {
+  if (x.in_bytes > x.h_in_cap || (size_t)M * d > x.h_out_cap) {
     x.drop_graphs();
-    if (x.h_mel) cudaFreeHost(x.h_mel);
+    if (x.h_in) cudaFreeHost(x.h_in);
     if (x.h_out) cudaFreeHost(x.h_out);
-    if (x.h_tabs) cudaFreeHost(x.h_tabs);
-    x.h_mel = x.h_out = nullptr;
-    x.h_tabs = nullptr;
-    x.h_mel_cap = x.h_out_cap = x.h_tab_cap = 0;
-    const size_t mc = std::max((size_t)S * F * n, (size_t)F * 64), oc = std::max((size_t)M * d, (size_t)16 * d),
-                 tc = std::max((size_t)5 * S, (size_t)40);
-    PKC_CK(cudaMallocHost(&x.h_mel, mc * 4), "page-locked mel staging");
+    x.h_in = nullptr;
+    x.h_out = nullptr;
+    x.h_in_cap = x.h_out_cap = 0;
+    const size_t ic = std::max(x.in_bytes, (size_t)256 + (size_t)F * 64 * 4),
+                 oc = std::max((size_t)M * d, (size_t)16 * d);
+    PKC_CK(cudaMallocHost(&x.h_in, ic), "page-locked input staging");
     PKC_CK(cudaMallocHost(&x.h_out, oc * 4), "page-locked output staging");
-    PKC_CK(cudaMallocHost(&x.h_tabs, tc * sizeof(void*)), "page-locked table staging");
-    x.h_mel_cap = mc;
+    x.h_in_cap = ic;
     x.h_out_cap = oc;
-    x.h_tab_cap = tc;
   }
   sk_part_ = 0;
   cudaGetLastError();
@@ -286,16 +283,20 @@ pkc_status DeviceRunner::stream_step_batch(StreamState* const* ss, int S, const 
                 "stream_pos", err, &w_.pos_all_q));
     x.pos_Tc = Tc;
   }
-  // staging: windows, then the per-stream tables (live and next cache buffers, fill counts)
-  for (int i = 0; i < S; ++i) std::memcpy(x.h_mel + (size_t)i * F * n, mels[i], (size_t)F * n * 4);
+  // staging, laid out as on the device: the per-stream tables (live and
+  // next cache buffers, fill counts), then the windows
+  void** h_tabs = reinterpret_cast<void**>(x.h_in);
+  float* h_mel = reinterpret_cast<float*>(x.h_in + (reinterpret_cast<uint8_t*>(x.mel) -
+                                                    reinterpret_cast<uint8_t*>(x.tabs)));
   for (int i = 0; i < S; ++i) {
     const StreamState& s = *ss[i];
-    x.h_tabs[0 * S + i] = s.kv[s.cur];
-    x.h_tabs[1 * S + i] = s.kv[1 - s.cur];
-    x.h_tabs[2 * S + i] = s.cv[s.cur];
-    x.h_tabs[3 * S + i] = s.cv[1 - s.cur];
-    x.h_tabs[4 * S + i] = s.d_filled;
+    h_tabs[0 * S + i] = s.kv[s.cur];
+    h_tabs[1 * S + i] = s.kv[1 - s.cur];
+    h_tabs[2 * S + i] = s.cv[s.cur];
+    h_tabs[3 * S + i] = s.cv[1 - s.cur];
+    h_tabs[4 * S + i] = s.d_filled;
   }
+  for (int i = 0; i < S; ++i) std::memcpy(h_mel + (size_t)i * F * n, mels[i], (size_t)F * n * 4);
   StreamScratch::Graph* hit = nullptr;
   for (StreamScratch::Graph& g : x.graphs)
     if (g.S == S && g.n == n && g.Tc == Tc) hit = &g;
@@ -365,9 +366,7 @@ pkc_status DeviceRunner::stream_issue(int S, int n, int Tc, int drop, std::strin
   void* const* cv_next = x.tabs + 3 * S;
   int* const* filled = reinterpret_cast<int* const*>(x.tabs + 4 * S);
 
-  PKC_CK(cudaMemcpyAsync(x.tabs, x.h_tabs, (size_t)5 * S * sizeof(void*), cudaMemcpyHostToDevice, st),
-         "stream table upload");
-  PKC_CK(cudaMemcpyAsync(x.mel, x.h_mel, (size_t)S * F * n * 4, cudaMemcpyHostToDevice, st), "mel upload");
+  PKC_CK(cudaMemcpyAsync(x.tabs, x.h_in, x.in_bytes, cudaMemcpyHostToDevice, st), "stream table and window upload");
   // ---- causal subsampling (each window is all real audio: no time mask bites)
   auto* s1 = static_cast<__nv_bfloat16*>(x.s1);
   PKC_CK(causal_conv0_launch(x.mel, S, F, n, n, w_.c0_w, w_.c0_b, C, T1, F1, s1, st), "causal conv0");
@@ -382,10 +381,14 @@ pkc_status DeviceRunner::stream_issue(int S, int n, int Tc, int drop, std::strin
   const float xs = c.xscaling ? std::sqrt((float)d) : 1.f;
   PKC_ST(gemm(x.s3b, F3 * C, w_.out_w, F3 * C, true, S * T3, d, F3 * C, EPI_STORE_F32, ACT_NONE, xs, w_.out_b, x.x3,
               d, st, "stream_sub_out", err));
-  // each stream's chunk frames (after its drop_extra_pre_encoded leading ones), stacked
-  PKC_CK(cudaMemcpy2DAsync(x.x, (size_t)Tc * d * 4, x.x3 + (size_t)drop * d, (size_t)T3 * d * 4, (size_t)Tc * d * 4, S,
-                           cudaMemcpyDeviceToDevice, st), "chunk frames");
-  float* xa = x.x;
+  // each stream's chunk frames (after its drop_extra_pre_encoded leading
+  // ones), stacked; one stream's, or undropped ones, are stacked already
+  float* xa = x.x3 + (size_t)drop * d;
+  if (S > 1 && drop > 0) {
+    PKC_CK(cudaMemcpy2DAsync(x.x, (size_t)Tc * d * 4, x.x3 + (size_t)drop * d, (size_t)T3 * d * 4,
+                             (size_t)Tc * d * 4, S, cudaMemcpyDeviceToDevice, st), "chunk frames");
+    xa = x.x;
+  }
 
   // ---- conformer layers with their caches (build_stream_layer, :98-338)
   for (int li = 0; li < Lc; ++li) {
