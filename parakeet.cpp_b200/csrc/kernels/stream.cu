@@ -20,6 +20,7 @@
 // Every kernel is a programmatic dependent launch: it waits for its
 // predecessor before touching what that wrote.
 #include <algorithm>
+#include <utility>
 
 #include "common.cuh"
 #include "kernels.h"
@@ -127,13 +128,15 @@ constexpr int SA_THREADS = 128;
 // -(Tk - 1) (row stride ldp). The head's key, value and position rows the
 // query reads are first staged in shared memory with coalesced 16-byte loads
 // (f32 there), so the dot products run from shared memory instead of chains of
-// dependent global loads.
+// dependent global loads. No kernel of a chunk step writes the live cache
+// (the roll writes the other buffer), the positional rows (made before the
+// step) or the fill count (updated by the step's last kernel), so those are
+// staged before the dependency wait, while the QKV GEMM before this kernel
+// still runs; only the chunk's own rows wait for it.
 template <typename H>
 __global__ void __launch_bounds__(SA_THREADS) k_stream_attn(StreamAttnArgs a) {
   extern __shared__ float sa_sm[];
   __shared__ float qu[128], qv[128], red[SA_THREADS / 32];
-  pdl_wait();
-  pdl_trigger();
   const int head = blockIdx.x, i = blockIdx.y, s = blockIdx.z;
   const int d = a.d, dk = d / a.n_heads, Tk = a.cache_len + a.Tc;
   const int ld = dk + 1;  // padded row stride: lanes of a key loop hit distinct banks
@@ -146,43 +149,63 @@ __global__ void __launch_bounds__(SA_THREADS) k_stream_attn(StreamAttnArgs a) {
   const H* ptab = static_cast<const H*>(a.ptab);
   const int qrow = a.cache_len + i;  // the query's frame among [cache | chunk]
   // stage: 8 elements (16 bytes) per load, 4 loads in flight per thread
-  // before their stores (a load cannot pass an earlier store it may alias)
-  const int v8 = dk / 8, total = 3 * Tk * v8;
-  auto src_of = [&](int e) {
-    const int which = e / (Tk * v8), r = (e / v8) % Tk, c8 = (e % v8) * 8;
-    if (which == 2) return ptab + (size_t)(r + a.Tc - 1 - i) * a.ldp + head * dk + c8;
-    return r < a.cache_len ? kvc + (size_t)r * 2 * d + which * d + head * dk + c8
-                           : qkv + (size_t)(r - a.cache_len) * 3 * d + (which + 1) * d + head * dk + c8;
+  // before their stores (a load cannot pass an earlier store it may alias);
+  // at(e) gives element group e's source and its f32 destination
+  const int v8 = dk / 8;
+  auto stage = [&](int total, auto at) {
+    for (int e0 = threadIdx.x; e0 < total; e0 += 4 * SA_THREADS) {
+      uint4 raw[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int e = e0 + u * SA_THREADS;
+        raw[u] = e < total ? *reinterpret_cast<const uint4*>(at(e).first) : make_uint4(0, 0, 0, 0);
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int e = e0 + u * SA_THREADS;
+        if (e >= total) break;
+        const H* hv = reinterpret_cast<const H*>(&raw[u]);
+        float* dst = at(e).second;
+#pragma unroll
+        for (int q = 0; q < 8; ++q) dst[q] = ld_h(hv + q);
+      }
+    }
   };
-  for (int e0 = threadIdx.x; e0 < total; e0 += 4 * SA_THREADS) {
-    uint4 raw[4];
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int e = e0 + u * SA_THREADS;
-      raw[u] = e < total ? *reinterpret_cast<const uint4*>(src_of(e)) : make_uint4(0, 0, 0, 0);
+  using Src = std::pair<const H*, float*>;
+  // before the wait: the cache's k | v rows, then the position row of every key
+  const int n_cache = 2 * a.cache_len * v8;
+  stage(n_cache + Tk * v8, [&](int e) -> Src {
+    if (e < n_cache) {
+      const int which = e / (a.cache_len * v8), r = (e / v8) % a.cache_len, c8 = (e % v8) * 8;
+      return {kvc + (size_t)r * 2 * d + which * d + head * dk + c8, (which ? sV : sK) + (size_t)r * ld + c8};
     }
-#pragma unroll
-    for (int u = 0; u < 4; ++u) {
-      const int e = e0 + u * SA_THREADS;
-      if (e >= total) break;
-      const int which = e / (Tk * v8), r = (e / v8) % Tk, c8 = (e % v8) * 8;
-      const H* hv = reinterpret_cast<const H*>(&raw[u]);
-      float* dst = (which == 0 ? sK : which == 1 ? sV : sP) + (size_t)r * ld + c8;
-#pragma unroll
-      for (int q = 0; q < 8; ++q) dst[q] = ld_h(hv + q);
-    }
+    const int f = e - n_cache, r = f / v8, c8 = (f % v8) * 8;
+    return {ptab + (size_t)(r + a.Tc - 1 - i) * a.ldp + head * dk + c8, sP + (size_t)r * ld + c8};
+  });
+  for (int e = threadIdx.x; e < dk; e += SA_THREADS) {
+    qu[e] = a.bias_u[head * dk + e];
+    qv[e] = a.bias_v[head * dk + e];
   }
+  const int filled_now = *a.filled[s];
+  pdl_wait();
+  pdl_trigger();
+  // after it: the chunk's k | v rows and the query, from this layer's QKV GEMM
+  stage(2 * a.Tc * v8, [&](int e) -> Src {
+    const int which = e / (a.Tc * v8), r = (e / v8) % a.Tc, c8 = (e % v8) * 8;
+    return {qkv + (size_t)r * 3 * d + (which + 1) * d + head * dk + c8,
+            (which ? sV : sK) + (size_t)(a.cache_len + r) * ld + c8};
+  });
   for (int e = threadIdx.x; e < dk; e += SA_THREADS) {
     const float q = ld_h(qkv + (size_t)i * 3 * d + head * dk + e);
-    qu[e] = q + a.bias_u[head * dk + e];
-    qv[e] = q + a.bias_v[head * dk + e];
+    qu[e] = q + qu[e];
+    qv[e] = q + qv[e];
   }
   __syncthreads();
   // chunked-limited: chunk = att_right + 1, visible iff 0 <= gq/chunk - gk/chunk <= att_left/chunk;
   // the cache's first cache_len - filled columns are not filled yet
   const int chunk = a.att_right + 1;
   const int left_chunks = chunk > 0 ? a.att_left / chunk : 0;
-  const int filled = min(max(*a.filled[s], 0), a.cache_len);
+  const int filled = min(max(filled_now, 0), a.cache_len);
   const int gq = qrow, first_filled = a.cache_len - filled;
   const float scale = rsqrtf((float)dk);
   float mx = -INFINITY;
@@ -226,29 +249,37 @@ size_t stream_attn_smem(int Tk, int dk) { return ((size_t)3 * Tk * (dk + 1) + Tk
 constexpr int SD_THREADS = 256;
 
 // One CTA per (output frame t, stream): row r of [conv cache | GLU rows] is
-// cache row r (r < K - 1) or GLU row r - (K - 1) of the stream's chunk.
+// cache row r (r < K - 1) or GLU row r - (K - 1) of the stream's chunk. The
+// live conv cache is not written during a chunk step, so its taps are summed
+// before the dependency wait and the GLU rows' taps after it (the same
+// ascending tap order as one loop).
 template <typename H, int CPT>
 __global__ void __launch_bounds__(SD_THREADS) k_stream_dwconv(StreamConvArgs a) {
   __shared__ float red[SD_THREADS / 32];
-  pdl_wait();
-  pdl_trigger();
   const int t = blockIdx.x, s = blockIdx.y, d = a.d, lp = a.K - 1;
   const H* cache = lp ? static_cast<const H*>(a.cv_cache[s]) + a.cv_layer_off : nullptr;
   const H* glu = static_cast<const H*>(a.glu) + (size_t)s * a.Tc * d;
+  const int k_glu = max(0, lp - t);  // taps k >= k_glu read GLU rows
   float v[CPT];
-  float sm = 0.f;
 #pragma unroll
   for (int u = 0; u < CPT; ++u) {
     const int c = threadIdx.x + u * SD_THREADS;
     float acc = 0.f;
     if (c < d) {
       acc = a.bias ? a.bias[c] : 0.f;
-      for (int k = 0; k < a.K; ++k) {
-        const int r = t + k;
-        const H* row = r < lp ? cache + (size_t)r * d : glu + (size_t)(r - lp) * d;
-        acc = fmaf(a.w[k * d + c], ld_h(row + c), acc);
-      }
+      for (int k = 0; k < min(k_glu, a.K); ++k) acc = fmaf(a.w[k * d + c], ld_h(cache + (size_t)(t + k) * d + c), acc);
     }
+    v[u] = acc;
+  }
+  pdl_wait();
+  pdl_trigger();
+  float sm = 0.f;
+#pragma unroll
+  for (int u = 0; u < CPT; ++u) {
+    const int c = threadIdx.x + u * SD_THREADS;
+    float acc = v[u];
+    if (c < d)
+      for (int k = k_glu; k < a.K; ++k) acc = fmaf(a.w[k * d + c], ld_h(glu + (size_t)(t + k - lp) * d + c), acc);
     v[u] = acc;
     sm += acc;
   }
