@@ -1465,6 +1465,7 @@ __global__ void __launch_bounds__(SKINNY_THREADS) k_gemm_skinny(const H* __restr
   // row (first SKINNY_PRE chunks per lane) is fetched before waiting for it
   const int u_first = blockIdx.x * SKINNY_WARPS + (threadIdx.x >> 5);
   uint4 pa[SKINNY_PRE], pg[SKINNY_PRE];
+  float pb = 0.f, pbg = 0.f;  // that row's bias (and gate bias)
   if (u_first < units) {
     const int na = PAIRED ? (u_first / (BN / 2)) * BN + u_first % (BN / 2) : u_first;
     const uint4* wa = reinterpret_cast<const uint4*>(B + (size_t)na * ldb);
@@ -1477,7 +1478,17 @@ __global__ void __launch_bounds__(SKINNY_THREADS) k_gemm_skinny(const H* __restr
         if constexpr (PAIRED) pg[j] = __ldg(wg + c);
       }
     }
+    if (args.bias) {
+      pb = __ldg(args.bias + na);
+      if constexpr (PAIRED) pbg = __ldg(args.bias + na + BN / 2);
+    }
   }
+  // the LayerNorm prologue's gamma / beta (128-byte lines) on their way to L1
+  if (args.ln_x)
+    for (int i = threadIdx.x; i < args.K / 32; i += SKINNY_THREADS) {
+      asm volatile("prefetch.global.L1 [%0];" ::"l"(args.ln_g + 32 * i));
+      asm volatile("prefetch.global.L1 [%0];" ::"l"(args.ln_b + 32 * i));
+    }
   pdl_wait();
   if (args.ln_x) {
     // LayerNorm of row m by warp m % 8: mean, then the mean square deviation
@@ -1593,13 +1604,13 @@ __global__ void __launch_bounds__(SKINNY_THREADS) k_gemm_skinny(const H* __restr
     }
     if (lane < M) {
       const size_t ro = (size_t)lane * args.ldo + u;
-      const float b = args.bias ? args.bias[na] : 0.f;
+      const float b = args.bias ? (first ? pb : args.bias[na]) : 0.f;
       if constexpr (EPI == EPI_RESID_F32) {
         reinterpret_cast<float*>(args.out)[ro] = resid + args.alpha * (mine + b);
       } else if constexpr (EPI == EPI_STORE_F32) {
         reinterpret_cast<float*>(args.out)[ro] = args.alpha * (mine + b);
       } else if constexpr (EPI == EPI_GLU_H) {
-        const float bg = args.bias ? args.bias[ng] : 0.f;
+        const float bg = args.bias ? (first ? pbg : args.bias[ng]) : 0.f;
         const float v = (mine + b) * sigmoidf_(mineg + bg);
         reinterpret_cast<H*>(args.out)[ro] = std::is_same<H, __half>::value ? H(__float2half_rn(v)) : H(__float2bfloat16_rn(v));
       } else {

@@ -21,26 +21,28 @@ __global__ void __launch_bounds__(256)
     k_layernorm(float* __restrict__ x, int M, const float* __restrict__ g, const float* __restrict__ b,
                 H* __restrict__ out_h, const float* __restrict__ g2, const float* __restrict__ b2,
                 int write_x) {
-  pdl_wait();
-  pdl_trigger();
   constexpr int D = NV * 128;
   const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
+  // gamma / beta are weights: loaded before the dependency wait, so their
+  // latency overlaps the kernel before this one instead of following the row
+  float4 g4[NV], b4[NV];
+  if (row < M) {
+#pragma unroll
+    for (int i = 0; i < NV; ++i) {
+      g4[i] = __ldg(reinterpret_cast<const float4*>(g + (i * 32 + lane) * 4));
+      b4[i] = __ldg(reinterpret_cast<const float4*>(b + (i * 32 + lane) * 4));
+    }
+  }
+  pdl_wait();
+  pdl_trigger();
   if (row >= M) return;
   float* xr = x + (size_t)row * D;
   float v[NV * 4];
-  // gamma / beta are issued together with the row so their latency overlaps
-  // the row load instead of following the reductions
-  float4 g4[NV], b4[NV];
 #pragma unroll
   for (int i = 0; i < NV; ++i) {
     const float4 q = *reinterpret_cast<const float4*>(xr + (i * 32 + lane) * 4);
     v[4 * i] = q.x; v[4 * i + 1] = q.y; v[4 * i + 2] = q.z; v[4 * i + 3] = q.w;
-  }
-#pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    g4[i] = __ldg(reinterpret_cast<const float4*>(g + (i * 32 + lane) * 4));
-    b4[i] = __ldg(reinterpret_cast<const float4*>(b + (i * 32 + lane) * 4));
   }
   auto norm = [&](const float* gg, const float* bb) {
     float s = 0.f;
