@@ -285,7 +285,10 @@ pkc_status pkc_shard_plan(const int* n_samples, int B, int n_dev, int hop, int* 
 /* D[M,N] = A[M,K] * B[N,K]^T with a fused epilogue on the tcgen05 GEMM.
    dtype 0 = f16, 1 = bf16 operands; epi/act as in the kernel header. M <= 16
    (K <= 4096, epi 0-3) runs the skinny CUDA-core kernel the streaming encoder
-   uses (PKC_GEMM_SKINNY=0: the tcgen05 tile for every M). */
+   uses (PKC_GEMM_SKINNY=0: the tcgen05 tile for every M). Bw and bias are
+   treated as weights: the kernel may start reading them before the kernel
+   launched before it on `stream` has finished (programmatic dependent
+   launch), so that kernel must not write them; A and out wait for it. */
 pkc_status pkc_gemm(const void* A, int lda, const void* Bw, int ldb, int M, int N, int K,
                     int dtype, int epi, int act, float alpha, const float* bias, void* out,
                     int ldo, void* stream);

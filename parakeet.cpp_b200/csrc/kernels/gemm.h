@@ -67,6 +67,9 @@ bool make_tmap_kmajor(CUtensorMap* map, const void* base, int rows, int K, int l
 // D[M,N] = A[M,K] * B[N,K]^T with the epilogue in args. A and B hold f16
 // (bf16 == false) or bf16 elements with row strides lda / ldb (elements).
 // Requires N % 256 == 0, K % 64 == 0, 16-byte aligned bases and strides.
+// B and args.bias are weights: the skinny kernel reads them before waiting
+// for the previous kernel in the stream (programmatic dependent launch),
+// which must not write them; A, the residual and the output wait for it.
 cudaError_t gemm_launch(const void* A, int lda, const void* B, int ldb, bool bf16,
                         const GemmArgs& args, cudaStream_t st);
 
