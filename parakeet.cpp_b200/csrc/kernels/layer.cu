@@ -144,12 +144,27 @@ __global__ void __launch_bounds__(DW_THREADS)
                      const float* __restrict__ w, const float* __restrict__ bias,
                      const float* __restrict__ scale, const float* __restrict__ shift,
                      const int* __restrict__ item_off, const int* __restrict__ item_len) {
+  const int t0 = blockIdx.x * DW_FRAMES;
+  const int c0 = blockIdx.z * DW_CH + threadIdx.x * 2;
+  // the taps and the folded BatchNorm are weights: loaded before the
+  // dependency wait, while the kernel before this one still runs
+  float2 wk[K], sc = make_float2(0.f, 0.f), sh = make_float2(0.f, 0.f);
+  if (c0 < d) {
+#pragma unroll
+    for (int k = 0; k < K; ++k) wk[k] = __ldg(reinterpret_cast<const float2*>(w + (size_t)k * d + c0));
+    sc = __ldg(reinterpret_cast<const float2*>(scale + c0));
+    sh = __ldg(reinterpret_cast<const float2*>(shift + c0));
+    if (bias) {
+      // (acc + bias) * scale + shift = acc * scale + (bias * scale + shift)
+      const float2 bi = __ldg(reinterpret_cast<const float2*>(bias + c0));
+      sh.x = fmaf(bi.x, sc.x, sh.x);
+      sh.y = fmaf(bi.y, sc.y, sh.y);
+    }
+  }
   pdl_wait();
   pdl_trigger();
   const int b = blockIdx.y;
   const int T = item_len[b];
-  const int t0 = blockIdx.x * DW_FRAMES;
-  const int c0 = blockIdx.z * DW_CH + threadIdx.x * 2;
   if (t0 >= T || c0 >= d) return;
   constexpr int pad = (K - 1) / 2;
   constexpr int NR = DW_FRAMES + K - 1;
@@ -160,17 +175,6 @@ __global__ void __launch_bounds__(DW_THREADS)
   for (int r = 0; r < NR; ++r) {
     const int ti = t0 - pad + r;
     raw[r] = (ti >= 0 && ti < T) ? __ldg(reinterpret_cast<const uint32_t*>(x + (size_t)ti * d)) : 0u;
-  }
-  float2 wk[K];
-#pragma unroll
-  for (int k = 0; k < K; ++k) wk[k] = __ldg(reinterpret_cast<const float2*>(w + (size_t)k * d + c0));
-  const float2 sc = __ldg(reinterpret_cast<const float2*>(scale + c0));
-  float2 sh = __ldg(reinterpret_cast<const float2*>(shift + c0));
-  if (bias) {
-    // (acc + bias) * scale + shift = acc * scale + (bias * scale + shift)
-    const float2 bi = __ldg(reinterpret_cast<const float2*>(bias + c0));
-    sh.x = fmaf(bi.x, sc.x, sh.x);
-    sh.y = fmaf(bi.y, sc.y, sh.y);
   }
   float2 xf[NR];
 #pragma unroll
