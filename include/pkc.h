@@ -332,7 +332,10 @@ pkc_status pkc_relpos_attention(const void* qkv, const void* ptab, int centre,
    device array that the library holds on each GPU until exit. Limits: at most
    1024 utterances and the query tiles of about 10000 x 64 frames per call;
    larger calls fail with PKC_ERR_ARG. The first call on a device looks up the
-   array's address. Calls that overlap on the GPU race on the shared array. */
+   array's address; make it before any stream capture begins. Calls that
+   overlapped on the GPU would race on the shared array, so the library runs
+   one call at a time per process and returns only after the call's work on
+   `stream` has finished. */
 pkc_status pkc_relpos_attention_noalloc(const void* qkv, const void* ptab, int centre,
                                         const float* bias_u, const float* bias_v, const int* lens,
                                         int B, int d, int n_heads, int dtype, void* ctx,

@@ -13,19 +13,22 @@
 // Properties of the shared table array:
 //   * It is allocated when the library is loaded, on every GPU that loads it,
 //     and stays until the process exits (kNoAllocTableInts * 4 bytes = 80 KiB).
-//   * Every call rewrites the part of it that the call uses, so no stale
-//     contents are read. Calls that overlap on the GPU (different streams or
-//     host threads at the same time) race on it and must be serialised by
-//     the caller.
+//   * Every call rewrites the part of it that the call uses (the device error
+//     word included, which starts each call at zero), so no stale contents
+//     are read. Calls that overlapped on the GPU would race on it, so the
+//     entry point holds one process-wide lock from its table upload until its
+//     stream has finished the call's work.
 //   * Its device address is looked up with cudaGetSymbolAddress once per
-//     device, with that device current, on the first call on that device.
-//     Host code never passes the symbol itself (in host code the name is
-//     only a host-side stand-in).
+//     device, with that device current, on the first call on that device;
+//     make that first call before any stream capture begins. Host code never
+//     passes the symbol itself (in host code the name is only a host-side
+//     stand-in).
+//   * The tables are built in a fixed file-scope host array of the same size
+//     (under the same lock), so a call allocates nothing on the host either.
 #include <cuda_runtime.h>
 
 #include <mutex>
 #include <string>
-#include <vector>
 
 #include "../../../include/pkc.h"
 #include "../status.hpp"
@@ -40,6 +43,9 @@ constexpr int kNoAllocMaxItems = 1024;
 static __device__ __align__(256) int g_noalloc_tables[kNoAllocTableInts];
 
 namespace {
+
+std::mutex g_noalloc_call_mu;             // one call at a time, until its GPU work is done
+int g_noalloc_host[kNoAllocTableInts];    // host image of the tables of the current call
 
 int* noalloc_table_ptr(int dev, std::string& err) {
   static std::mutex mu;
@@ -77,46 +83,47 @@ extern "C" pkc_status pkc_relpos_attention_noalloc(const void* qkv, const void* 
   if (B > kNoAllocMaxItems)
     return set_thread_error(PKC_ERR_ARG, "pkc_relpos_attention_noalloc: at most " +
                                              std::to_string(kNoAllocMaxItems) + " utterances per call");
-  std::vector<int> host;
-  host.reserve((size_t)2 * B + 1 + 64);
-  host.push_back(0);
-  for (int b = 0; b < B; ++b) {
+  for (int b = 0; b < B; ++b)
     if (lens[b] <= 0 || lens[b] > centre)
       return set_thread_error(PKC_ERR_ARG, "pkc_relpos_attention_noalloc: lens must be in [1, centre]");
-    host.push_back(host.back() + lens[b]);
-  }
-  host.insert(host.end(), lens, lens + B);
   const int qt = attn_query_tile();
   long long n_tiles = 0;
   for (int b = 0; b < B; ++b) n_tiles += (lens[b] + qt - 1) / qt;
-  if ((long long)host.size() + 2 * n_tiles + 1 > kNoAllocTableInts)
+  const int n_head = 2 * B + 1;  // offsets (B + 1), then lengths (B)
+  if (n_head + 2 * n_tiles + 1 > kNoAllocTableInts)
     return set_thread_error(PKC_ERR_ARG,
                             "pkc_relpos_attention_noalloc: " + std::to_string(n_tiles) +
                                 " query tiles exceed the fixed table (" +
-                                std::to_string((kNoAllocTableInts - 1 - (int)host.size()) / 2) + " max)");
-  const size_t tiles_at = host.size();
+                                std::to_string((kNoAllocTableInts - 1 - n_head) / 2) + " max)");
+  std::lock_guard<std::mutex> call_lock(g_noalloc_call_mu);
+  int* host = g_noalloc_host;
+  int n = 0;
+  host[n++] = 0;
+  for (int b = 0; b < B; ++b, ++n) host[n] = host[n - 1] + lens[b];
+  for (int b = 0; b < B; ++b) host[n++] = lens[b];
+  const int tiles_at = n;
   for (int b = 0; b < B; ++b)
     for (int q0 = 0; q0 < lens[b]; q0 += qt) {
-      host.push_back(b);
-      host.push_back(q0);
+      host[n++] = b;
+      host[n++] = q0;
     }
-  host.push_back(0);  // device error word
+  host[n++] = 0;  // device error word
   int dev = 0;
   cudaGetDevice(&dev);
   std::string err;
   int* tab = noalloc_table_ptr(dev, err);
   if (!tab) return set_thread_error(PKC_ERR_CUDA, "pkc_relpos_attention_noalloc: " + err);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
-  cudaError_t e = cudaMemcpyAsync(tab, host.data(), host.size() * sizeof(int), cudaMemcpyHostToDevice, st);
+  cudaError_t e = cudaMemcpyAsync(tab, host, (size_t)n * sizeof(int), cudaMemcpyHostToDevice, st);
   if (e == cudaSuccess) {
     AttnArgs a{qkv, ptab, 2 * centre - 1, centre, d, bias_u, bias_v, tab + tiles_at, (int)n_tiles,
-               tab, tab + B + 1, ctx, d, n_heads, host[B], tab + host.size() - 1};
+               tab, tab + B + 1, ctx, d, n_heads, host[B], tab + n - 1};
     e = attention_launch(a, dtype == 1, st);
   }
-  // the host table vector must outlive the copy
+  // the host tables are reused by the next call: finish this one's copy and kernel first
   if (e == cudaSuccess) e = cudaStreamSynchronize(st);
   int h_err = 0;
-  if (e == cudaSuccess) e = cudaMemcpy(&h_err, tab + host.size() - 1, sizeof(int), cudaMemcpyDeviceToHost);
+  if (e == cudaSuccess) e = cudaMemcpy(&h_err, tab + n - 1, sizeof(int), cudaMemcpyDeviceToHost);
   if (e != cudaSuccess)
     return set_thread_error(PKC_ERR_CUDA, std::string("pkc_relpos_attention_noalloc: ") + cudaGetErrorString(e));
   if (h_err != 0)
