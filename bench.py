@@ -58,18 +58,15 @@ def load_peaks():
 
 
 def profile_traffic(config):
-    """Per-launch DRAM traffic of the dominant kernel from the committed ncu
-    summary (a line `traffic_bytes_per_launch[<config>]: <int>`), else None."""
-    path = os.path.join(REPO, "profiles", "gemm_tcgen05_ncu.md")
+    """Per-launch DRAM traffic of the dominant kernel for this workload, from
+    the ncu figures committed in profiles/roofline_traffic.json, else None."""
+    path = os.path.join(REPO, "profiles", "roofline_traffic.json")
     try:
         with open(path) as f:
-            for line in f:
-                key = f"traffic_bytes_per_launch[{config}]:"
-                if line.strip().startswith(key):
-                    return float(line.split(":", 1)[1].strip())
-    except OSError:
-        pass
-    return None
+            ent = json.load(f).get(config)
+        return float(ent["bytes_per_launch"]) if ent else None
+    except (OSError, ValueError, KeyError, TypeError):
+        return None
 
 
 class ClockSampler:

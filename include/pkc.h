@@ -330,12 +330,15 @@ pkc_status pkc_relpos_attention(const void* qkv, const void* ptab, int centre,
    every byte), where a cudaMalloc is refused or stalls the whole device. No
    counterpart in the reference. Its small tables live in one fixed 80 KiB
    device array that the library holds on each GPU until exit. Limits: at most
-   1024 utterances and the query tiles of about 10000 x 64 frames per call;
-   larger calls fail with PKC_ERR_ARG. The first call on a device looks up the
-   array's address; make it before any stream capture begins. Calls that
-   overlapped on the GPU would race on the shared array, so the library runs
-   one call at a time per process and returns only after the call's work on
-   `stream` has finished. */
+   1024 utterances, and at most (20478 - 2B) / 2 query tiles of 128 frames
+   (about 10,000 tiles; B = utterances of the call); larger calls fail with
+   PKC_ERR_ARG. `stream` must belong to the current device (else PKC_ERR_ARG),
+   and a stream in capture mode is rejected with PKC_ERR_ARG. The first call
+   on a device looks up the array's address; make it before any stream
+   capture begins, and do not use this entry point on a device after
+   cudaDeviceReset. Calls that overlapped on the GPU would race on the shared
+   array, so the library runs one call at a time per process and returns only
+   after the call's work on `stream` has finished. */
 pkc_status pkc_relpos_attention_noalloc(const void* qkv, const void* ptab, int centre,
                                         const float* bias_u, const float* bias_v, const int* lens,
                                         int B, int d, int n_heads, int dtype, void* ctx,

@@ -312,6 +312,10 @@ int pkc_ctc_classes(const pkc_model* m) {
   return m->runners[0]->ctc_classes();
 }
 
+// The greedy fold of ctc_greedy (src/search.cpp:21-90): the state it keeps
+// (previous class, previous token's emit frame, the run's minimum confidence)
+// and its start-offset rule are the reference's, so the tokens, frames and
+// confidences match it exactly; only the per-frame argmax moved to the GPU.
 int pkc_ctc_fold(const int32_t* argmax, const float* max_logprob, int T, int n_classes, int blank_id,
                  pkc_token* out, int cap) {
   if (T < 0 || n_classes <= 1 || (T > 0 && (!argmax || !max_logprob)) || (cap > 0 && !out)) return -1;

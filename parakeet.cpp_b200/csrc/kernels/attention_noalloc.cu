@@ -20,13 +20,19 @@
 //     stream has finished the call's work.
 //   * Its device address is looked up with cudaGetSymbolAddress once per
 //     device, with that device current, on the first call on that device;
-//     make that first call before any stream capture begins. Host code never
-//     passes the symbol itself (in host code the name is only a host-side
-//     stand-in).
+//     make that first call before any stream capture begins. The address is
+//     kept for the life of the process, so the entry point must not be used
+//     on a device after cudaDeviceReset (or after the primary context was
+//     destroyed and re-created). Host code never passes the symbol itself (in
+//     host code the name is only a host-side stand-in).
 //   * The tables are built in a fixed file-scope host array of the same size
 //     (under the same lock), so a call allocates nothing on the host either.
+//   * Size limit: at most kNoAllocMaxItems utterances, and at most
+//     (kNoAllocTableInts - 2 - 2B) / 2 query tiles of attn_query_tile() frames
+//     (128), where B is the number of utterances of the call.
 #include <cuda_runtime.h>
 
+#include <map>
 #include <mutex>
 #include <string>
 
@@ -49,24 +55,18 @@ int g_noalloc_host[kNoAllocTableInts];    // host image of the tables of the cur
 
 int* noalloc_table_ptr(int dev, std::string& err) {
   static std::mutex mu;
-  static int* ptrs[64] = {};
-  static bool done[64] = {};
-  if (dev < 0 || dev >= 64) {
-    err = "device index out of range";
+  static std::map<int, int*> ptrs;
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = ptrs.find(dev);
+  if (it != ptrs.end()) return it->second;
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_tables);
+  if (e != cudaSuccess || !p) {
+    err = std::string("cudaGetSymbolAddress failed: ") + cudaGetErrorString(e);
     return nullptr;
   }
-  std::lock_guard<std::mutex> lk(mu);
-  if (!done[dev]) {
-    void* p = nullptr;
-    const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_tables);
-    if (e != cudaSuccess || !p) {
-      err = std::string("cudaGetSymbolAddress failed: ") + cudaGetErrorString(e);
-      return nullptr;
-    }
-    ptrs[dev] = static_cast<int*>(p);
-    done[dev] = true;
-  }
-  return ptrs[dev];
+  ptrs[dev] = static_cast<int*>(p);
+  return static_cast<int*>(p);
 }
 
 }  // namespace
@@ -92,9 +92,36 @@ extern "C" pkc_status pkc_relpos_attention_noalloc(const void* qkv, const void* 
   const int n_head = 2 * B + 1;  // offsets (B + 1), then lengths (B)
   if (n_head + 2 * n_tiles + 1 > kNoAllocTableInts)
     return set_thread_error(PKC_ERR_ARG,
-                            "pkc_relpos_attention_noalloc: " + std::to_string(n_tiles) +
-                                " query tiles exceed the fixed table (" +
-                                std::to_string((kNoAllocTableInts - 1 - n_head) / 2) + " max)");
+                            "pkc_relpos_attention_noalloc: " + std::to_string(n_tiles) + " query tiles of " +
+                                std::to_string(qt) + " frames exceed the fixed table (" +
+                                std::to_string((kNoAllocTableInts - 1 - n_head) / 2) + " max for " +
+                                std::to_string(B) + " utterances)");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  // the call waits for its stream and reads its error word back before it
+  // returns, which a stream in capture mode cannot do
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(st, &cap) != cudaSuccess) {
+    cudaGetLastError();
+    return set_thread_error(PKC_ERR_ARG, "pkc_relpos_attention_noalloc: invalid stream");
+  }
+  if (cap != cudaStreamCaptureStatusNone)
+    return set_thread_error(PKC_ERR_ARG,
+                            "pkc_relpos_attention_noalloc: stream is capturing; this entry point synchronises "
+                            "its stream and reads its error word back before returning");
+  // the table address is the current device's: the stream must belong to it
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (st) {
+    int sdev = -1;
+    if (cudaStreamGetDevice(st, &sdev) != cudaSuccess) {
+      cudaGetLastError();
+      return set_thread_error(PKC_ERR_ARG, "pkc_relpos_attention_noalloc: invalid stream");
+    }
+    if (sdev != dev)
+      return set_thread_error(PKC_ERR_ARG, "pkc_relpos_attention_noalloc: stream belongs to device " +
+                                               std::to_string(sdev) + " but device " + std::to_string(dev) +
+                                               " is current; make the stream's device current");
+  }
   std::lock_guard<std::mutex> call_lock(g_noalloc_call_mu);
   int* host = g_noalloc_host;
   int n = 0;
@@ -108,12 +135,9 @@ extern "C" pkc_status pkc_relpos_attention_noalloc(const void* qkv, const void* 
       host[n++] = q0;
     }
   host[n++] = 0;  // device error word
-  int dev = 0;
-  cudaGetDevice(&dev);
   std::string err;
   int* tab = noalloc_table_ptr(dev, err);
   if (!tab) return set_thread_error(PKC_ERR_CUDA, "pkc_relpos_attention_noalloc: " + err);
-  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   cudaError_t e = cudaMemcpyAsync(tab, host, (size_t)n * sizeof(int), cudaMemcpyHostToDevice, st);
   if (e == cudaSuccess) {
     AttnArgs a{qkv, ptab, 2 * centre - 1, centre, d, bias_u, bias_v, tab + tiles_at, (int)n_tiles,

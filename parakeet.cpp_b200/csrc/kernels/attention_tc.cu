@@ -48,6 +48,7 @@
 // Frames are packed per utterance (no padding); keys >= T are masked, query
 // rows >= T are computed but not stored -- the reference's masking.
 #include "common.cuh"
+#include "per_device.h"
 #include "gemm.h"
 #include "kernels.h"
 
@@ -563,14 +564,12 @@ template <typename H, int DK>
 cudaError_t launch_tc(const AttnArgs& a, cudaStream_t st) {
   auto kern = k_relpos_attn_tc<H, DK>;
   constexpr int smem = TcLayout<DK>::SMEM;
-  static bool attr_set[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!attr_set[dev & 63]) {
-    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
-    if (e != cudaSuccess) return e;
-    attr_set[dev & 63] = true;
-  }
+  static PerDevice once;
+  int unused = 0;
+  const cudaError_t ae = per_device(once, &unused, [&](int, int&) {
+    return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  });
+  if (ae != cudaSuccess) return ae;
   const bool bf = is_bf16<H>::value;
   CUtensorMap tq, tp;
   if (!make_tmap_kmajor(&tq, a.qkv, a.rows, 3 * a.d, 3 * a.d, 64, bf)) return cudaErrorInvalidValue;

@@ -15,6 +15,7 @@
 
 #include "common.cuh"
 #include "gemm.h"
+#include "per_device.h"
 
 namespace pkc {
 
@@ -1178,41 +1179,44 @@ bool make_tmap_kmajor(CUtensorMap* map, const void* base, int rows, int K, int l
   return r == CUDA_SUCCESS;
 }
 
+// CTA pairs of a 2-SM kernel that fit on the device at once (its shared
+// memory and thread count; the SM count / 2 if the occupancy query fails).
+template <typename K>
+static cudaError_t cluster_pairs(K kern, int smem, int threads, int dev, int& n) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2, 1, 1);
+  cfg.blockDim = dim3(threads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute at;
+  at.id = cudaLaunchAttributeClusterDimension;
+  at.val.clusterDim.x = 2; at.val.clusterDim.y = 1; at.val.clusterDim.z = 1;
+  cfg.attrs = &at;
+  cfg.numAttrs = 1;
+  n = 0;
+  if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
+    cudaGetLastError();
+    int sms = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    n = sms / 2;
+  }
+  return cudaSuccess;
+}
+
 template <typename H, int EPI>
 static cudaError_t launch_t2(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
                              cudaStream_t st) {
   auto kern = k_gemm_tc2<H, EPI, false>;
   auto kern_sk = k_gemm_tc2<H, EPI, true>;
-  static bool attr_set[64] = {};
-  static int max_pairs[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!attr_set[dev & 63]) {
+  static PerDevice once;
+  int mp = 0;
+  const cudaError_t ae = per_device(once, &mp, [&](int dev, int& n) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES);
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(kern_sk, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES);
     if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(kern_sk, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES);
-    if (e != cudaSuccess) return e;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(2, 1, 1);
-    cfg.blockDim = dim3(THREADS, 1, 1);
-    cfg.dynamicSmemBytes = SMEM2_BYTES;
-    cudaLaunchAttribute at;
-    at.id = cudaLaunchAttributeClusterDimension;
-    at.val.clusterDim.x = 2; at.val.clusterDim.y = 1; at.val.clusterDim.z = 1;
-    cfg.attrs = &at;
-    cfg.numAttrs = 1;
-    int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
-      cudaGetLastError();
-      int sms = 0;
-      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-      n = sms / 2;
-    }
-    max_pairs[dev & 63] = n;
-    attr_set[dev & 63] = true;
-  }
+    return cluster_pairs(kern, SMEM2_BYTES, THREADS, dev, n);
+  });
+  if (ae != cudaSuccess) return ae;
   const int n_tiles = (a.N / BN) * ((a.M + 2 * HALF_ROWS - 1) / (2 * HALF_ROWS));
-  const int mp = max_pairs[dev & 63];
   int pairs = n_tiles < mp ? n_tiles : mp;
   if (a.sk_ws && a.sk_flags && mp <= a.sk_pairs && gemm_splitk_enabled()) {
     // stream-K when whole tiles would leave more than 15 % of the last
@@ -1229,18 +1233,16 @@ template <typename H, int EPI>
 static cudaError_t launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
                             cudaStream_t st) {
   auto kern = k_gemm_tc<H, EPI>;
-  static bool attr_set[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!attr_set[dev & 63]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  static PerDevice once;
+  int n_sm = 0;
+  const cudaError_t ae = per_device(once, &n_sm, [&](int dev, int& n) {
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
     if (e != cudaSuccess) return e;
-    attr_set[dev & 63] = true;
-  }
-  static int n_sm[64] = {};
-  if (!n_sm[dev & 63]) cudaDeviceGetAttribute(&n_sm[dev & 63], cudaDevAttrMultiProcessorCount, dev);
+    return cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  });
+  if (ae != cudaSuccess) return ae;
   const int n_tiles = (a.N / BN) * ((a.M + BM - 1) / BM);
-  const int grid = n_tiles < n_sm[dev & 63] ? n_tiles : n_sm[dev & 63];
+  const int grid = n_tiles < n_sm ? n_tiles : n_sm;
   return launch_pdl(kern, dim3(grid), dim3(THREADS), SMEM_BYTES, st, ta, tb, a);
 }
 
@@ -1263,34 +1265,16 @@ static cudaError_t launch_q(const CUtensorMap& ta, const CUtensorMap& tq, const 
                             const CUtensorMap& t1, const GemmArgs& a, cudaStream_t st) {
   auto kern = k_gemm_tc2q<H, EPI, QT>;
   constexpr int smem = QLayout<QT>::SMEM;
-  static bool attr_set[64] = {};
-  static int max_pairs[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!attr_set[dev & 63]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  static PerDevice once;
+  int mp = 0;
+  const cudaError_t ae = per_device(once, &mp, [&](int dev, int& n) {
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return e;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(2, 1, 1);
-    cfg.blockDim = dim3(QTHREADS, 1, 1);
-    cfg.dynamicSmemBytes = smem;
-    cudaLaunchAttribute at;
-    at.id = cudaLaunchAttributeClusterDimension;
-    at.val.clusterDim.x = 2; at.val.clusterDim.y = 1; at.val.clusterDim.z = 1;
-    cfg.attrs = &at;
-    cfg.numAttrs = 1;
-    int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
-      cudaGetLastError();
-      int sms = 0;
-      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-      n = sms / 2;
-    }
-    max_pairs[dev & 63] = n;
-    attr_set[dev & 63] = true;
-  }
+    return cluster_pairs(kern, smem, QTHREADS, dev, n);
+  });
+  if (ae != cudaSuccess) return ae;
   const int n_tiles = (a.N / BN) * ((a.M + 2 * HALF_ROWS - 1) / (2 * HALF_ROWS));
-  const int pairs = n_tiles < max_pairs[dev & 63] ? n_tiles : max_pairs[dev & 63];
+  const int pairs = n_tiles < mp ? n_tiles : mp;
   return launch_pdl(kern, dim3(2 * pairs), dim3(QTHREADS), smem, st, ta, tq, t0, t1, a);
 }
 
@@ -1343,34 +1327,16 @@ template <typename H, int EPI>
 static cudaError_t launch_ln(const CUtensorMap& tx, const CUtensorMap& tb, const LnParams& lp, const GemmArgs& a,
                              cudaStream_t st) {
   auto kern = k_gemm_tc2ln<H, EPI>;
-  static bool attr_set[64] = {};
-  static int max_pairs[64] = {};
-  int dev = 0;
-  cudaGetDevice(&dev);
-  if (!attr_set[dev & 63]) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, LSMEM);
+  static PerDevice once;
+  int mp = 0;
+  const cudaError_t ae = per_device(once, &mp, [&](int dev, int& n) {
+    const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, LSMEM);
     if (e != cudaSuccess) return e;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(2, 1, 1);
-    cfg.blockDim = dim3(QTHREADS, 1, 1);
-    cfg.dynamicSmemBytes = LSMEM;
-    cudaLaunchAttribute at;
-    at.id = cudaLaunchAttributeClusterDimension;
-    at.val.clusterDim.x = 2; at.val.clusterDim.y = 1; at.val.clusterDim.z = 1;
-    cfg.attrs = &at;
-    cfg.numAttrs = 1;
-    int n = 0;
-    if (cudaOccupancyMaxActiveClusters(&n, kern, &cfg) != cudaSuccess || n <= 0) {
-      cudaGetLastError();
-      int sms = 0;
-      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-      n = sms / 2;
-    }
-    max_pairs[dev & 63] = n;
-    attr_set[dev & 63] = true;
-  }
+    return cluster_pairs(kern, LSMEM, QTHREADS, dev, n);
+  });
+  if (ae != cudaSuccess) return ae;
   const int n_tiles = (a.N / BN) * ((a.M + 2 * HALF_ROWS - 1) / (2 * HALF_ROWS));
-  const int pairs = n_tiles < max_pairs[dev & 63] ? n_tiles : max_pairs[dev & 63];
+  const int pairs = n_tiles < mp ? n_tiles : mp;
   return launch_pdl(kern, dim3(2 * pairs), dim3(QTHREADS), LSMEM, st, tx, tb, lp, a);
 }
 
@@ -1633,12 +1599,12 @@ bool gemm_skinny_enabled() {
 
 template <typename H, int EPI>
 cudaError_t launch_skinny(const void* A, int lda, const void* B, int ldb, const GemmArgs& args, cudaStream_t st) {
-  static int sms = 0;
-  if (!sms) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  }
+  static PerDevice once;
+  int sms = 0;
+  const cudaError_t ae = per_device(once, &sms, [](int dev, int& n) {
+    return cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+  });
+  if (ae != cudaSuccess) return ae;
   const size_t smem = (size_t)args.M * args.K * sizeof(H);
   const int units = EPI == EPI_GLU_H ? args.N / 2 : args.N;
   const int grid = std::max(1, std::min((units + SKINNY_WARPS - 1) / SKINNY_WARPS, 2 * sms));

@@ -106,14 +106,12 @@ struct AttnArgs {
   int rows;             // M: packed frames in qkv / ctx
   int* err;             // device error word (timeouts), may be null
 };
-// Dispatcher: the tcgen05 kernel unless PKC_ATTN_MMA_SYNC=1. The tile list in
-// AttnArgs must be built with attn_query_tile() rows per tile.
+// Dispatcher (the tcgen05 kernel). The tile list in AttnArgs must be built
+// with attn_query_tile() rows per tile.
 cudaError_t attention_launch(const AttnArgs& a, bool bf16, cudaStream_t st);
 int attn_query_tile();
 cudaError_t attention_tc_launch(const AttnArgs& a, bool bf16, cudaStream_t st);
 int attn_tc_query_tile();
-cudaError_t attention_mma_launch(const AttnArgs& a, bool bf16, cudaStream_t st);
-int attn_mma_query_tile();
 
 // Conv module middle: depthwise Conv1d(K, pad (K-1)/2) over each item's frames
 // (zeros outside) + bias -> BatchNorm (folded scale/shift) -> SiLU.

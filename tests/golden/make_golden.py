@@ -1,7 +1,7 @@
 """Regenerate tests/golden/ref_frontend.npz from parakeet.cpp's own code.
 
-Run in the build container (where /root/reference exists and oracle/_ref has
-been built by oracle/Makefile.ref): it calls the reference's compiled
+Run where the reference checkout exists (its root in PKC_REFERENCE_DIR, see
+oracle/Makefile.ref) and oracle/_ref has been built by oracle/Makefile.ref: it calls the reference's compiled
 MelFrontend::compute (src/mel.cpp), pk::rfft (src/fft.cpp) and
 pk::rel_pos_encoding (src/pos_enc.cpp) on seeded inputs and stores their
 outputs, so tests on machines without the reference checkout (the GPU box)
