@@ -316,6 +316,17 @@ pkc_status pkc_gemm_ln(const float* x, int ldx, const float* stats, const void* 
                        int N, int K, int dtype, int epi, int act, const float* bias, void* out, int ldo,
                        void* stream);
 
+/* The split-f16 GEMM of the f32-accurate path (f32 GGUF weights): A is
+   [M, 2Ks] f16 rows [A_hi | A_lo] and Bw [N, 2Ks] rows [B_hi | B_lo] with
+   hi = f16(v), lo = f16(v - hi) (row strides lda / ldb elements); the kernel
+   accumulates A_hi B_hi^T + A_hi B_lo^T + A_lo B_hi^T in f32 (~22 significant
+   bits per product) and applies epilogue epi / act as pkc_gemm. ofmt (epi 0
+   and 3 only): 0 f16, 1 f32, 2 split-f16 rows with the lo half at column +
+   split_ld. Replaces the F32 mul_mat of the reference's graphs
+   (src/conformer.cpp:319-324, src/relpos_attention.cpp:191-194,305). */
+pkc_status pkc_gemm_split(const void* A, int lda, const void* Bw, int ldb, int M, int N, int Ks, int epi, int act,
+                          float alpha, const float* bias, void* out, int ldo, int ofmt, int split_ld, void* stream);
+
 /* Relative-position attention of one layer for B utterances packed along
    rows (item b owns rows [off_b, off_b + len[b])). qkv [M, 3d] and ptab
    [2*centre-1, d] in the compute type (dtype 0 f16, 1 bf16), bias_u/v [d] f32,
@@ -323,6 +334,15 @@ pkc_status pkc_gemm_ln(const float* x, int ldx, const float* stats, const void* 
 pkc_status pkc_relpos_attention(const void* qkv, const void* ptab, int centre,
                                 const float* bias_u, const float* bias_v, const int* lens, int B,
                                 int d, int n_heads, int dtype, void* ctx, void* stream);
+
+/* The attention of the f32-accurate path: qkv f32 [M, 3d], ptab f32
+   [2*centre-1, d], everything in f32 (softmax with expf); ctx receives f16
+   rows [hi | lo] of width 2d (hi = f16(v), lo = f16(v - hi)), the split
+   operand of the output projection. Other arguments as pkc_relpos_attention
+   (src/relpos_attention.cpp:162-306). */
+pkc_status pkc_relpos_attention_f32(const float* qkv, const float* ptab, int centre, const float* bias_u,
+                                    const float* bias_v, const int* lens, int B, int d, int n_heads, void* ctx,
+                                    void* stream);
 
 /* The same attention as pkc_relpos_attention, for callers that may not
    allocate device memory: hosts whose own allocator owns all of HBM (a serving

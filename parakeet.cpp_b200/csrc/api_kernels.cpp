@@ -107,6 +107,25 @@ static pkc_status finish_kernel_call(cudaError_t e, int* err, cudaStream_t st, c
   return PKC_OK;
 }
 
+extern "C" pkc_status pkc_gemm_split(const void* A, int lda, const void* Bw, int ldb, int M, int N, int Ks, int epi,
+                                     int act, float alpha, const float* bias, void* out, int ldo, int ofmt,
+                                     int split_ld, void* stream) {
+  if (!A || !Bw || !out || M < 0 || N <= 0 || Ks <= 0 || epi < pkc::EPI_STORE_H || epi > pkc::EPI_GLU_H ||
+      ofmt < pkc::OUT_H || ofmt > pkc::OUT_SPLIT)
+    return pkc::set_thread_error(PKC_ERR_ARG, "pkc_gemm_split: bad arguments");
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int* err = dev_err_word(dev);
+  if (!err) return pkc::set_thread_error(PKC_ERR_CUDA, "pkc_gemm_split: error word allocation failed");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  pkc::GemmArgs a{};
+  a.M = M; a.N = N; a.K = 3 * Ks;
+  a.epi = epi; a.act = act; a.alpha = alpha; a.bias = bias;
+  a.out = out; a.ldo = ldo; a.err = err;
+  a.split_k = Ks; a.ofmt = ofmt; a.split_ld = split_ld;
+  return finish_kernel_call(pkc::gemm_launch(A, lda, Bw, ldb, false, a, st), err, st, "pkc_gemm_split");
+}
+
 extern "C" pkc_status pkc_gemm_resid_stats(const void* A, int lda, const void* Bw, int ldb, int M, int N,
                                            int K, int dtype, float alpha, const float* bias, float* x,
                                            int ldx, float* stats, void* stream) {
@@ -148,19 +167,20 @@ extern "C" pkc_status pkc_gemm_ln(const float* x, int ldx, const float* stats, c
 
 extern "C" int pkc_abi_version(void) { return PKC_ABI_VERSION; }
 
-extern "C" pkc_status pkc_relpos_attention(const void* qkv, const void* ptab, int centre,
-                                           const float* bias_u, const float* bias_v, const int* lens,
-                                           int B, int d, int n_heads, int dtype, void* ctx,
-                                           void* stream) {
-  if (!qkv || !ptab || !bias_u || !bias_v || !lens || B <= 0 || !ctx || n_heads <= 0 ||
-      (dtype != 0 && dtype != 1))
-    return pkc::set_thread_error(PKC_ERR_ARG, "pkc_relpos_attention: bad arguments");
+// Tables of one kernel-level attention call (offsets, lengths, tiles of `qt`
+// query rows, error word) in a temporary device buffer, then the launch.
+template <typename L>
+static pkc_status attention_call(const char* what, const void* qkv, const void* ptab, int centre,
+                                 const float* bias_u, const float* bias_v, const int* lens, int B, int d,
+                                 int n_heads, void* ctx, void* stream, int qt, L launch) {
+  if (!qkv || !ptab || !bias_u || !bias_v || !lens || B <= 0 || !ctx || n_heads <= 0)
+    return pkc::set_thread_error(PKC_ERR_ARG, std::string(what) + ": bad arguments");
   std::vector<int> off(B + 1, 0), len(lens, lens + B), tiles;
   for (int b = 0; b < B; ++b) {
     if (len[b] <= 0 || len[b] > centre)
-      return pkc::set_thread_error(PKC_ERR_ARG, "pkc_relpos_attention: lens must be in [1, centre]");
+      return pkc::set_thread_error(PKC_ERR_ARG, std::string(what) + ": lens must be in [1, centre]");
     off[b + 1] = off[b] + len[b];
-    for (int q0 = 0; q0 < len[b]; q0 += pkc::attn_query_tile()) {
+    for (int q0 = 0; q0 < len[b]; q0 += qt) {
       tiles.push_back(b);
       tiles.push_back(q0);
     }
@@ -173,20 +193,37 @@ extern "C" pkc_status pkc_relpos_attention(const void* qkv, const void* ptab, in
   host.push_back(0);  // device error word
   int* dtab = nullptr;
   if (cudaMalloc(&dtab, host.size() * sizeof(int)) != cudaSuccess)
-    return pkc::set_thread_error(PKC_ERR_OOM, "pkc_relpos_attention: table allocation failed");
+    return pkc::set_thread_error(PKC_ERR_OOM, std::string(what) + ": table allocation failed");
   cudaMemcpyAsync(dtab, host.data(), host.size() * sizeof(int), cudaMemcpyHostToDevice, st);
   int* derr = dtab + host.size() - 1;
   pkc::AttnArgs a{qkv, ptab, 2 * centre - 1, centre, d, bias_u, bias_v, dtab + 2 * B + 1,
                   (int)tiles.size() / 2, dtab, dtab + B + 1, ctx, d, n_heads, off[B], derr};
-  cudaError_t e = pkc::attention_launch(a, dtype == 1, st);
+  cudaError_t e = launch(a, st);
   cudaError_t e2 = cudaStreamSynchronize(st);
   int h_err = 0;
   if (e == cudaSuccess && e2 == cudaSuccess) e2 = cudaMemcpy(&h_err, derr, sizeof(int), cudaMemcpyDeviceToHost);
   cudaFree(dtab);
   if (e != cudaSuccess || e2 != cudaSuccess)
-    return pkc::set_thread_error(PKC_ERR_CUDA, std::string("pkc_relpos_attention: ") +
-                                                   cudaGetErrorString(e != cudaSuccess ? e : e2));
+    return pkc::set_thread_error(PKC_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e != cudaSuccess ? e : e2));
   if (h_err != 0)
-    return pkc::set_thread_error(PKC_ERR_KERNEL, "pkc_relpos_attention: kernel error word " + std::to_string(h_err));
+    return pkc::set_thread_error(PKC_ERR_KERNEL, std::string(what) + ": kernel error word " + std::to_string(h_err));
   return PKC_OK;
+}
+
+extern "C" pkc_status pkc_relpos_attention(const void* qkv, const void* ptab, int centre,
+                                           const float* bias_u, const float* bias_v, const int* lens,
+                                           int B, int d, int n_heads, int dtype, void* ctx,
+                                           void* stream) {
+  if (dtype != 0 && dtype != 1) return pkc::set_thread_error(PKC_ERR_ARG, "pkc_relpos_attention: bad dtype");
+  return attention_call("pkc_relpos_attention", qkv, ptab, centre, bias_u, bias_v, lens, B, d, n_heads, ctx, stream,
+                        pkc::attn_query_tile(),
+                        [&](const pkc::AttnArgs& a, cudaStream_t st) { return pkc::attention_launch(a, dtype == 1, st); });
+}
+
+extern "C" pkc_status pkc_relpos_attention_f32(const float* qkv, const float* ptab, int centre, const float* bias_u,
+                                               const float* bias_v, const int* lens, int B, int d, int n_heads,
+                                               void* ctx, void* stream) {
+  return attention_call("pkc_relpos_attention_f32", qkv, ptab, centre, bias_u, bias_v, lens, B, d, n_heads, ctx, stream,
+                        pkc::attn_f32_query_tile(),
+                        [](const pkc::AttnArgs& a, cudaStream_t st) { return pkc::attention_f32_launch(a, st); });
 }

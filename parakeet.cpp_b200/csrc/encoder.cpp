@@ -68,7 +68,7 @@ void make_plan(const Config& c, const std::vector<int>& n_samples, const std::ve
   p.centre = p.max_v;
   // attention query tiles, longest utterances first: a tile's cost grows with
   // its utterance's length, so the block scheduler gets the long ones early
-  const int qt = attn_query_tile();
+  const int qt = c.split ? attn_f32_query_tile() : attn_query_tile();
   std::vector<int> order(B);
   for (int b = 0; b < B; ++b) order[b] = b;
   std::stable_sort(order.begin(), order.end(), [&](int a, int b) { return p.v[a] > p.v[b]; });
@@ -146,7 +146,7 @@ DeviceRunner::~DeviceRunner() {
 // kernel at the encoder's shapes.
 bool DeviceRunner::ln_fused(const Config& c) {
   const char* lf = getenv("PKC_LN_FUSED");
-  return lf && lf[0] == '1' && c.d_model % 128 == 0;
+  return lf && lf[0] == '1' && c.d_model % 128 == 0 && !c.split;
 }
 
 std::string DeviceRunner::init(const PackedWeights& pw) {
@@ -305,6 +305,27 @@ pkc_status DeviceRunner::gemm(const void* A, int lda, const void* B, int ldb, bo
   return PKC_OK;
 }
 
+pkc_status DeviceRunner::gemm_split(const void* A, int lda, const void* B, int ldb, int M, int N, int Ks, int epi,
+                                    int act, float alpha, const float* bias, void* out, int ldo, int ofmt,
+                                    int split_ld, cudaStream_t st, const char* name, std::string& err) {
+  GemmArgs a{};
+  a.M = M; a.N = N; a.K = 3 * Ks; a.epi = epi; a.act = act; a.alpha = alpha; a.bias = bias;
+  a.out = out; a.ldo = ldo; a.err = err_word_;
+  a.split_k = Ks; a.ofmt = ofmt; a.split_ld = split_ld;
+  prof_begin(st);
+  const cudaError_t e = gemm_launch(A, lda, B, ldb, false, a, st);
+  const int ncols = epi == EPI_GLU_H ? N / 2 : N;
+  const double osz = (epi == EPI_RESID_F32 || epi == EPI_STORE_F32 || ofmt != OUT_H) ? 4.0 : 2.0;
+  // algorithmic work: one f32 contraction (2 M N Ks flops); bytes of the split operands
+  prof_end(st, name, 2.0 * M * N * Ks,
+           4.0 * ((double)M * Ks + (double)N * Ks) + (double)M * ncols * osz * (epi == EPI_RESID_F32 ? 2 : 1));
+  if (e != cudaSuccess) {
+    err = std::string("GEMM ") + name + " (split) launch failed: " + cudaGetErrorString(e);
+    return PKC_ERR_CUDA;
+  }
+  return PKC_OK;
+}
+
 pkc_status DeviceRunner::gemm_ln(const float* x, const float* stats, const void* B, bool bf16, int M, int N, int K, int epi, int act,
                                  const float* bias, void* out, int ldo, cudaStream_t st, const char* name,
                                  std::string& err) {
@@ -331,7 +352,9 @@ pkc_status DeviceRunner::prepare(const Plan& p, cudaStream_t st, std::string& er
     return PKC_ERR_UNSUPPORTED;
   }
   const int d = c.d_model, F = c.n_mels, C = c.sub_channels;
-  const size_t hs = 2;
+  // bytes per logical element of the 16-bit activations: split-f16 [hi | lo]
+  // rows (or f32) take 4 in the f32-accurate path
+  const size_t hs = c.split ? 4 : 2;
   const int B = p.B;
   // Same geometry as the previous batch on this stream: tables and carve are
   // still valid (lets a device-resident caller launch step after step without
@@ -353,11 +376,11 @@ pkc_status DeviceRunner::prepare(const Plan& p, cudaStream_t st, std::string& er
   const size_t o_pow = take((size_t)p.total_frames * power_ld_ * 4);
   const size_t o_log = take((size_t)p.total_frames * F * 4);
   const size_t o_mb = take((size_t)B * F * p.max_Tm * 4);
-  const size_t o_s1 = take(sub_unfused_ ? (size_t)p.M1 * c.F1 * C * 2 : 0);
-  const size_t o_s2a = take((size_t)p.M2 * c.F2 * C * 2);
-  const size_t o_s2b = take((size_t)p.M2 * c.F2 * C * 2);
-  const size_t o_s3a = take((size_t)p.M * c.F3 * C * 2);
-  const size_t o_s3b = take((size_t)p.M * c.F3 * C * 2);
+  const size_t o_s1 = take((sub_unfused_ || c.split) ? (size_t)p.M1 * c.F1 * C * hs : 0);
+  const size_t o_s2a = take((size_t)p.M2 * c.F2 * C * hs);
+  const size_t o_s2b = take((size_t)p.M2 * c.F2 * C * hs);
+  const size_t o_s3a = take((size_t)p.M * c.F3 * C * hs);
+  const size_t o_s3b = take((size_t)p.M * c.F3 * C * hs);
   const size_t o_x = take((size_t)p.M * d * 4);
   const size_t o_h = take((size_t)p.M * d * hs);
   const size_t o_ff = take((size_t)p.M * c.ff_dim * hs);
@@ -443,7 +466,9 @@ pkc_status DeviceRunner::run_encoder(const Plan& p, cudaStream_t st, std::string
   ItemTables t{p.B, t_pcm_off, t_S, t_mel_off, t_Tm, t_mval, t_v1_off, t_v1, t_v2_off, t_v2, t_v_off, t_v};
 
   // ---- subsampling (src/subsampling.cpp:48-240)
-  if (sub_unfused_) {
+  if (c.split) {
+    PKC_ST(run_subsampling_split(p, st, err));
+  } else if (sub_unfused_) {
     prof_begin(st);
     PKC_CK(sub_conv0_launch(b_.logmel, c.n_mels, w_.c0_w, w_.c0_b, C,
                             reinterpret_cast<__nv_bfloat16*>(b_.s1), c.F1, t, p.M1, st), "conv0");
@@ -462,29 +487,39 @@ pkc_status DeviceRunner::run_encoder(const Plan& p, cudaStream_t st, std::string
     prof_end(st, "sub_stage1", 2.0 * p.M1 * c.F1 * C * 9 + 2.0 * p.M2 * c.F2 * C * 9,
              (double)p.total_frames * c.n_mels * 4 + (double)p.M2 * c.F2 * C * 2);
   }
-  PKC_ST(gemm(b_.s2a, C, w_.pw1_w, C, true, p.M2 * c.F2, C, C, EPI_STORE_H, ACT_RELU, 1.f, w_.pw1_b,
-              b_.s2b, C, st, "gemm_sub_pw", err));
-  prof_begin(st);
-  PKC_CK(sub_dw_launch(reinterpret_cast<const __nv_bfloat16*>(b_.s2b), c.F2, t_v2_off, t_v2, w_.dw2_w,
-                       w_.dw2_b, C, reinterpret_cast<__nv_bfloat16*>(b_.s3a), c.F3, t_v_off, t_v, p.B,
-                       p.max_v, st), "dw2");
-  prof_end(st, "sub_dw", 2.0 * M * c.F3 * C * 9, ((double)p.M2 * c.F2 + (double)M * c.F3) * C * 2);
-  PKC_ST(gemm(b_.s3a, C, w_.pw2_w, C, true, M * c.F3, C, C, EPI_STORE_H, ACT_RELU, 1.f, w_.pw2_b,
-              b_.s3b, C, st, "gemm_sub_pw", err));
-  const float xs = c.xscaling ? std::sqrt((float)d) : 1.f;
-  PKC_ST(gemm(b_.s3b, c.F3 * C, w_.out_w, c.F3 * C, true, M, d, c.F3 * C, EPI_STORE_F32, ACT_NONE, xs,
-              w_.out_b, b_.x, d, st, "gemm_sub_out", err));
+  if (!c.split) {
+    PKC_ST(gemm(b_.s2a, C, w_.pw1_w, C, true, p.M2 * c.F2, C, C, EPI_STORE_H, ACT_RELU, 1.f, w_.pw1_b,
+                b_.s2b, C, st, "gemm_sub_pw", err));
+    prof_begin(st);
+    PKC_CK(sub_dw_launch(reinterpret_cast<const __nv_bfloat16*>(b_.s2b), c.F2, t_v2_off, t_v2, w_.dw2_w,
+                         w_.dw2_b, C, reinterpret_cast<__nv_bfloat16*>(b_.s3a), c.F3, t_v_off, t_v, p.B,
+                         p.max_v, st), "dw2");
+    prof_end(st, "sub_dw", 2.0 * M * c.F3 * C * 9, ((double)p.M2 * c.F2 + (double)M * c.F3) * C * 2);
+    PKC_ST(gemm(b_.s3a, C, w_.pw2_w, C, true, M * c.F3, C, C, EPI_STORE_H, ACT_RELU, 1.f, w_.pw2_b,
+                b_.s3b, C, st, "gemm_sub_pw", err));
+    const float xs = c.xscaling ? std::sqrt((float)d) : 1.f;
+    PKC_ST(gemm(b_.s3b, c.F3 * C, w_.out_w, c.F3 * C, true, M, d, c.F3 * C, EPI_STORE_F32, ACT_NONE, xs,
+                w_.out_b, b_.x, d, st, "gemm_sub_out", err));
+  }
 
   // ---- relative positional table (src/pos_enc.cpp:10-34), shared by the batch
   const int np = 2 * p.centre - 1;
-  prof_begin(st);
-  PKC_CK(pos_table_launch(b_.pe, p.centre, d, bf, st), "pos_table");
-  prof_end(st, "pos_table", 0.0, (double)np * d * hs);
-
-  // every layer's linear_pos (no bias) in one GEMM: ptab [np, L*d], layer l at column l*d
   const int Ld = c.n_layers * d;
-  PKC_ST(gemm(b_.pe, d, w_.pos_all_w, d, bf, np, Ld, d, EPI_STORE_H, ACT_NONE, 1.f, nullptr, b_.ptab, Ld,
-              st, "gemm_pos", err, &w_.pos_all_q));
+  if (c.split) {
+    prof_begin(st);
+    PKC_CK(pos_table_split_launch(reinterpret_cast<__half*>(b_.pe), p.centre, d, st), "pos_table");
+    prof_end(st, "pos_table", 0.0, (double)np * d * 4);
+    // every layer's linear_pos in one GEMM, f32 out: ptab [np, L*d]
+    PKC_ST(gemm_split(b_.pe, 2 * d, w_.pos_all_w, 2 * d, np, Ld, d, EPI_STORE_F32, ACT_NONE, 1.f, nullptr, b_.ptab,
+                      Ld, OUT_H, 0, st, "gemm_pos", err));
+  } else {
+    prof_begin(st);
+    PKC_CK(pos_table_launch(b_.pe, p.centre, d, bf, st), "pos_table");
+    prof_end(st, "pos_table", 0.0, (double)np * d * hs);
+    // every layer's linear_pos (no bias) in one GEMM: ptab [np, L*d], layer l at column l*d
+    PKC_ST(gemm(b_.pe, d, w_.pos_all_w, d, bf, np, Ld, d, EPI_STORE_H, ACT_NONE, 1.f, nullptr, b_.ptab, Ld,
+                st, "gemm_pos", err, &w_.pos_all_q));
+  }
 
 
   // ---- conformer layers: one part, or two independent parts on two streams
@@ -503,9 +538,12 @@ pkc_status DeviceRunner::run_encoder(const Plan& p, cudaStream_t st, std::string
     return m;
   };
   const bool two = p.split_b > 0 && !prof_on_;
+  auto layer = [&](int li, const Part& q, cudaStream_t s) {
+    return c.split ? run_layer_split(p, li, q, s, err) : run_layer(p, li, q, s, err);
+  };
   if (!two) {
     const Part all{0, 0, M, 0, p.B, p.max_v, t_tiles, ntiles, attn_flops_of(0, p.B)};
-    for (int li = 0; li < c.n_layers; ++li) PKC_ST(run_layer(p, li, all, st, err));
+    for (int li = 0; li < c.n_layers; ++li) PKC_ST(layer(li, all, st));
     return PKC_OK;
   }
   const int sb = p.split_b;
@@ -516,8 +554,8 @@ pkc_status DeviceRunner::run_encoder(const Plan& p, cudaStream_t st, std::string
   PKC_CK(cudaEventRecord(ev_fork_, st), "fork event");
   PKC_CK(cudaStreamWaitEvent(stream2_, ev_fork_, 0), "fork wait");
   for (int li = 0; li < c.n_layers; ++li) {
-    PKC_ST(run_layer(p, li, p0, st, err));
-    PKC_ST(run_layer(p, li, p1, stream2_, err));
+    PKC_ST(layer(li, p0, st));
+    PKC_ST(layer(li, p1, stream2_));
   }
   // join: st continues once the second part is done
   PKC_CK(cudaEventRecord(ev_join_, stream2_), "join event");
@@ -609,6 +647,110 @@ pkc_status DeviceRunner::run_layer(const Plan& p, int li, const Part& q, cudaStr
   PKC_CK(layernorm_launch(x, M, d, L.ln_out_g, L.ln_out_b, last ? nullptr : hbuf, bf,
                           last ? nullptr : N->ln_ff1_g, last ? nullptr : N->ln_ff1_b, true, st), "ln");
   prof_end(st, "layernorm", 0.0, (double)M * d * (8 + (last ? 0 : hs)));
+  return PKC_OK;
+}
+
+// Subsampling of the f32-accurate path: conv.0 and the depthwise convs in f32
+// on the CUDA cores, the pointwise convs and the output linear as split-f16
+// GEMMs (operands written as [hi | lo] rows by the kernel before each).
+pkc_status DeviceRunner::run_subsampling_split(const Plan& p, cudaStream_t st, std::string& err) {
+  const Config& c = cfg_;
+  const int d = c.d_model, C = c.sub_channels, M = p.M, KW = c.F3 * C;
+  ItemTables t{p.B, t_pcm_off, t_S, t_mel_off, t_Tm, t_mval, t_v1_off, t_v1, t_v2_off, t_v2, t_v_off, t_v};
+  float* s1 = reinterpret_cast<float*>(b_.s1);
+  __half* s2a = reinterpret_cast<__half*>(b_.s2a);
+  float* s2b = reinterpret_cast<float*>(b_.s2b);
+  __half* s3a = reinterpret_cast<__half*>(b_.s3a);
+  float* s3b = reinterpret_cast<float*>(b_.s3b);
+  prof_begin(st);
+  PKC_CK(sub_conv0_f32_launch(b_.logmel, c.n_mels, w_.c0_w, w_.c0_b, C, s1, c.F1, t, p.M1, st), "conv0");
+  prof_end(st, "sub_conv0", 2.0 * p.M1 * c.F1 * C * 9, (double)p.total_frames * c.n_mels * 4 + (double)p.M1 * c.F1 * C * 4);
+  prof_begin(st);
+  PKC_CK(sub_dw_f32split_launch(s1, c.F1, t_v1_off, t_v1, w_.dw1_w, w_.dw1_b, C, s2a, c.F2, t_v2_off, t_v2, p.B,
+                                p.max_v2, st), "dw1");
+  prof_end(st, "sub_dw", 2.0 * p.M2 * c.F2 * C * 9, ((double)p.M1 * c.F1 + (double)p.M2 * c.F2) * C * 4);
+  PKC_ST(gemm_split(s2a, 2 * C, w_.pw1_w, 2 * C, p.M2 * c.F2, C, C, EPI_STORE_H, ACT_RELU, 1.f, w_.pw1_b, s2b, C,
+                    OUT_F32, 0, st, "gemm_sub_pw", err));
+  prof_begin(st);
+  PKC_CK(sub_dw_f32split_launch(s2b, c.F2, t_v2_off, t_v2, w_.dw2_w, w_.dw2_b, C, s3a, c.F3, t_v_off, t_v, p.B,
+                                p.max_v, st), "dw2");
+  prof_end(st, "sub_dw", 2.0 * M * c.F3 * C * 9, ((double)p.M2 * c.F2 + (double)M * c.F3) * C * 4);
+  PKC_ST(gemm_split(s3a, 2 * C, w_.pw2_w, 2 * C, M * c.F3, C, C, EPI_STORE_H, ACT_RELU, 1.f, w_.pw2_b, s3b, C,
+                    OUT_F32, 0, st, "gemm_sub_pw", err));
+  // [M, F3 * C] f32 -> [hi | lo] rows (s3a is free again)
+  prof_begin(st);
+  PKC_CK(split_rows_launch(s3b, M, KW, KW, s3a, 2 * KW, st), "split");
+  prof_end(st, "split_rows", 0.0, (double)M * KW * 8);
+  const float xs = c.xscaling ? std::sqrt((float)d) : 1.f;
+  PKC_ST(gemm_split(s3a, 2 * KW, w_.out_w, 2 * KW, M, d, KW, EPI_STORE_F32, ACT_NONE, xs, w_.out_b, b_.x, d, OUT_H,
+                    0, st, "gemm_sub_out", err));
+  return PKC_OK;
+}
+
+// One conformer layer of the f32-accurate path (the same block as run_layer):
+// LayerNorms write split-f16 rows, the projections are split-f16 GEMMs with
+// f32 (or split) outputs, the attention and the depthwise conv run in f32.
+pkc_status DeviceRunner::run_layer_split(const Plan& p, int li, const Part& q, cudaStream_t st, std::string& err) {
+  const Config& c = cfg_;
+  const int d = c.d_model, FF = c.ff_dim, H = c.n_heads, K = c.conv_kernel;
+  const int M = q.M;
+  const int np = 2 * p.centre - 1;
+  const int Ld = c.n_layers * d;
+  const size_t r0 = (size_t)q.row0;
+  float* x = b_.x + r0 * d;
+  void* hbuf = static_cast<uint8_t*>(b_.hbuf) + r0 * d * 4;   // split [M, 2d]
+  void* ffh = static_cast<uint8_t*>(b_.ffh) + r0 * FF * 4;    // split [M, 2 FF]
+  void* qkv = static_cast<uint8_t*>(b_.qkv) + r0 * 3 * d * 4; // f32 [M, 3d]
+  void* ctx = static_cast<uint8_t*>(b_.ctx) + r0 * d * 4;     // split [M, 2d], or the GLU's f32 [M, d]
+  const int* v_off = t_v_off + q.b0;
+  const int* v_len = t_v + q.b0;
+  const LayerWeights& L = w_.layers[li];
+  auto ln = [&](const float* g, const float* b, const float* g2, const float* b2, bool write_x, void* out) {
+    prof_begin(st);
+    const cudaError_t e = layernorm_launch(x, M, d, g, b, out, false, g2, b2, write_x, st, true);
+    prof_end(st, "layernorm", 0.0, (double)M * d * (4 + 4 + (write_x ? 8 : 0)));
+    if (e != cudaSuccess) err = std::string("layernorm: ") + cudaGetErrorString(e);
+    return e == cudaSuccess ? PKC_OK : PKC_ERR_CUDA;
+  };
+  // FFN1: x += 0.5 * FFN(LN(x))
+  if (li == 0) PKC_ST(ln(L.ln_ff1_g, L.ln_ff1_b, nullptr, nullptr, false, hbuf));
+  PKC_ST(gemm_split(hbuf, 2 * d, L.ff1_w1, 2 * d, M, FF, d, EPI_STORE_H, ACT_SILU, 1.f, L.ff1_b1, ffh, 2 * FF,
+                    OUT_SPLIT, FF, st, "gemm_ffn", err));
+  PKC_ST(gemm_split(ffh, 2 * FF, L.ff1_w2, 2 * FF, M, d, FF, EPI_RESID_F32, ACT_NONE, 0.5f, L.ff1_b2, x, d, OUT_H, 0,
+                    st, "gemm_ffn", err));
+  // MHSA
+  PKC_ST(ln(L.ln_att_g, L.ln_att_b, nullptr, nullptr, false, hbuf));
+  PKC_ST(gemm_split(hbuf, 2 * d, L.qkv_w, 2 * d, M, 3 * d, d, EPI_STORE_F32, ACT_NONE, 1.f, L.qkv_b, qkv, 3 * d, OUT_H,
+                    0, st, "gemm_qkv", err));
+  AttnArgs aa{b_.qkv, reinterpret_cast<const float*>(b_.ptab) + (size_t)li * d, np, p.centre, Ld, L.pos_u, L.pos_v,
+              q.tiles, q.ntiles, t_v_off, t_v, b_.ctx, d, H, p.M, err_word_};
+  prof_begin(st);
+  PKC_CK(attention_f32_launch(aa, st), "attention (f32)");
+  prof_end(st, "attention", q.attn_flops, (double)M * (3 * d * 4 + d * 4) + (double)np * d * 4);
+  PKC_ST(gemm_split(ctx, 2 * d, L.out_w, 2 * d, M, d, d, EPI_RESID_F32, ACT_NONE, 1.f, L.out_b, x, d, OUT_H, 0, st,
+                    "gemm_out", err));
+  // conv module
+  PKC_ST(ln(L.ln_conv_g, L.ln_conv_b, nullptr, nullptr, false, hbuf));
+  PKC_ST(gemm_split(hbuf, 2 * d, L.pw1_w, 2 * d, M, 2 * d, d, EPI_GLU_H, ACT_NONE, 1.f, L.pw1_b, ctx, d, OUT_F32, 0,
+                    st, "gemm_pw1_glu", err));
+  prof_begin(st);
+  PKC_CK(dwconv_f32split_launch(reinterpret_cast<const float*>(b_.ctx), reinterpret_cast<__half*>(b_.hbuf), d, K,
+                                L.dw_w, L.dw_b, L.bn_scale, L.bn_shift, v_off, v_len, q.nb, q.max_v, st),
+         "dwconv (f32)");
+  prof_end(st, "dwconv", 2.0 * M * d * K, (double)M * d * 8);
+  PKC_ST(gemm_split(hbuf, 2 * d, L.pw2_w, 2 * d, M, d, d, EPI_RESID_F32, ACT_NONE, 1.f, L.pw2_b, x, d, OUT_H, 0, st,
+                    "gemm_pw2", err));
+  // FFN2
+  PKC_ST(ln(L.ln_ff2_g, L.ln_ff2_b, nullptr, nullptr, false, hbuf));
+  PKC_ST(gemm_split(hbuf, 2 * d, L.ff2_w1, 2 * d, M, FF, d, EPI_STORE_H, ACT_SILU, 1.f, L.ff2_b1, ffh, 2 * FF,
+                    OUT_SPLIT, FF, st, "gemm_ffn", err));
+  PKC_ST(gemm_split(ffh, 2 * FF, L.ff2_w2, 2 * FF, M, d, FF, EPI_RESID_F32, ACT_NONE, 0.5f, L.ff2_b2, x, d, OUT_H, 0,
+                    st, "gemm_ffn", err));
+  // norm_out (+ next layer's norm_feed_forward1 in the same pass)
+  const bool last = li + 1 == c.n_layers;
+  const LayerWeights* N = last ? nullptr : &w_.layers[li + 1];
+  PKC_ST(ln(L.ln_out_g, L.ln_out_b, last ? nullptr : N->ln_ff1_g, last ? nullptr : N->ln_ff1_b, true,
+            last ? nullptr : hbuf));
   return PKC_OK;
 }
 

@@ -123,6 +123,9 @@ class DeviceRunner {
     double attn_flops;
   };
   pkc_status run_layer(const Plan& p, int li, const Part& q, cudaStream_t st, std::string& err);
+  // the f32-accurate layer (Config::split): split-f16 GEMM operands, f32 attention
+  pkc_status run_layer_split(const Plan& p, int li, const Part& q, cudaStream_t st, std::string& err);
+  pkc_status run_subsampling_split(const Plan& p, cudaStream_t st, std::string& err);
   pkc_status finish(cudaStream_t st, std::string& err);
   struct StreamScratch;
   StreamScratch* sscr_ = nullptr;  // scratch, staging and graphs of the streaming chunk step
@@ -139,6 +142,11 @@ class DeviceRunner {
                   int epi, int act, float alpha, const float* bias, void* out, int ldo,
                   cudaStream_t st, const char* name, std::string& err, const QWeight* qw = nullptr,
                   float* stats = nullptr);
+  // split-f16 GEMM: A [M, 2 Ks] and B [N, 2 Ks] rows [hi | lo] (lda / ldb
+  // row strides), output as ofmt (OUT_SPLIT: lo half at column + split_ld)
+  pkc_status gemm_split(const void* A, int lda, const void* B, int ldb, int M, int N, int Ks, int epi, int act,
+                        float alpha, const float* bias, void* out, int ldo, int ofmt, int split_ld,
+                        cudaStream_t st, const char* name, std::string& err);
   // D = xhat * B^T + bias, xhat = (x - mean) * rstd per row computed while
   // the A operand is staged (B and bias carry the LayerNorm's gamma / beta);
   // stats are x's per-128-column (mean, M2) partials

@@ -34,6 +34,21 @@ constexpr uint32_t TMEM_COLS = 512;  // two 128 x 256 f32 accumulators
 
 constexpr int EPI_STAGE_BYTES = 32 * 32 * 4;  // per epilogue warp: 32 rows x 32 f32 columns
 
+// Operand columns of k-block kb: kb * BK for plain operands; in the split
+// mode (args.split_k = Ks) pass kb / (Ks / BK) reads (hi, hi), (hi, lo), (lo, hi)
+// of the [hi | lo] rows of A and B.
+__device__ __forceinline__ void kb_cols(const GemmArgs& a, int kb, int& ca, int& cb) {
+  if (!a.split_k) {
+    ca = cb = kb * BK;
+    return;
+  }
+  const int kbs = a.split_k / BK;
+  const int seg = kb / kbs;
+  const int kk = (kb - seg * kbs) * BK;
+  ca = kk + (seg == 2 ? a.split_k : 0);
+  cb = kk + (seg == 1 ? a.split_k : 0);
+}
+
 // Drain this warp's share of one accumulator tile (TMEM lanes row0..row0+31,
 // half `half` of the 32-column chunks) through the fused epilogue.
 // tcgen05.ld hands each thread one row, but a global access per thread-row
@@ -159,6 +174,32 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t tro
         continue;
       }
       if (!okr) continue;
+      if constexpr (EPI == EPI_STORE_H || EPI == EPI_GLU_H) {
+        if (args.ofmt != OUT_H) {
+          float x0 = w.x, x1 = w.y, x2 = w.z, x3 = w.w;
+          if constexpr (EPI == EPI_STORE_H) {
+            x0 += b4.x; x1 += b4.y; x2 += b4.z; x3 += b4.w;
+            if (args.act == ACT_SILU) {
+              x0 = siluf_(x0); x1 = siluf_(x1); x2 = siluf_(x2); x3 = siluf_(x3);
+            } else if (args.act == ACT_RELU) {
+              x0 = fmaxf(x0, 0.f); x1 = fmaxf(x1, 0.f); x2 = fmaxf(x2, 0.f); x3 = fmaxf(x3, 0.f);
+            }
+          }
+          if (args.ofmt == OUT_F32) {
+            *reinterpret_cast<float4*>(reinterpret_cast<float*>(args.out) + ro) = make_float4(x0, x1, x2, x3);
+          } else {
+            const __half h0 = __float2half_rn(x0), h1 = __float2half_rn(x1), h2 = __float2half_rn(x2),
+                         h3 = __float2half_rn(x3);
+            __half* o = reinterpret_cast<__half*>(args.out) + ro;
+            *reinterpret_cast<uint2*>(o) = make_uint2(pack2<__half>(__half2float(h0), __half2float(h1)),
+                                                      pack2<__half>(__half2float(h2), __half2float(h3)));
+            *reinterpret_cast<uint2*>(o + args.split_ld) =
+                make_uint2(pack2<__half>(x0 - __half2float(h0), x1 - __half2float(h1)),
+                           pack2<__half>(x2 - __half2float(h2), x3 - __half2float(h3)));
+          }
+          continue;
+        }
+      }
       if constexpr (EPI == EPI_STORE_F32) {
         *reinterpret_cast<float4*>(reinterpret_cast<float*>(args.out) + ro) =
             make_float4(args.alpha * (w.x + b4.x), args.alpha * (w.y + b4.y), args.alpha * (w.z + b4.z),
@@ -250,8 +291,10 @@ __global__ void __launch_bounds__(THREADS, 1)
           }
           const uint32_t fb = smem_u32(&bars[s]);
           mbar_arrive_expect_tx(fb, A_STAGE_BYTES + B_STAGE_BYTES);
-          tma_load_2d(smem_u32(sA + s * A_STAGE_BYTES), &tmA, fb, kb * BK, m0);
-          tma_load_2d(smem_u32(sB + s * B_STAGE_BYTES), &tmB, fb, kb * BK, n0);
+          int ca, cb;
+          kb_cols(args, kb, ca, cb);
+          tma_load_2d(smem_u32(sA + s * A_STAGE_BYTES), &tmA, fb, ca, m0);
+          tma_load_2d(smem_u32(sB + s * B_STAGE_BYTES), &tmB, fb, cb, n0);
         }
       }
     }
@@ -534,8 +577,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
           }
           const uint32_t full_leader = mapa_shared(smem_u32(&bars[s]), 0);
           if (leader) mbar_arrive_expect_tx(smem_u32(&bars[s]), 2 * (A2_BYTES + B2_BYTES));
-          tma_load_2d_2sm(smem_u32(sA + s * A2_BYTES), &tmA, full_leader, kb * BK, m0);
-          tma_load_2d_2sm(smem_u32(sB + s * B2_BYTES), &tmB, full_leader, kb * BK, n0);
+          int ca, cb;
+          kb_cols(args, kb, ca, cb);
+          tma_load_2d_2sm(smem_u32(sA + s * A2_BYTES), &tmA, full_leader, ca, m0);
+          tma_load_2d_2sm(smem_u32(sB + s * B2_BYTES), &tmB, full_leader, cb, n0);
         }
       }
     }
@@ -1282,6 +1327,7 @@ cudaError_t gemm_launch_q(const void* A, int lda, const QuantB& B, bool bf16, co
                           cudaStream_t st) {
   if (args.M <= 0) return cudaSuccess;
   if (B.type != QT_Q8_0 && B.type != QT_Q4_K) return cudaErrorInvalidValue;
+  if (args.split_k || args.ofmt != OUT_H) return cudaErrorInvalidValue;
   if (args.N % BN != 0 || args.K % BK != 0 || args.K <= 0 || (lda % 8) != 0 || !B.q || !B.s0 ||
       (B.type == QT_Q4_K && !B.s1) || (reinterpret_cast<uintptr_t>(A) & 15) ||
       (reinterpret_cast<uintptr_t>(B.q) & 15) || (reinterpret_cast<uintptr_t>(B.s0) & 15) ||
@@ -1343,6 +1389,7 @@ static cudaError_t launch_ln(const CUtensorMap& tx, const CUtensorMap& tb, const
 cudaError_t gemm_launch_ln(const LnA& A, const void* B, int ldb, bool bf16, const GemmArgs& args,
                            cudaStream_t st) {
   if (args.M <= 0) return cudaSuccess;
+  if (args.split_k || args.ofmt != OUT_H) return cudaErrorInvalidValue;
   if (args.N % BN != 0 || args.K % 128 != 0 || args.K <= 0 || (A.ldx % 4) != 0 || (ldb % 8) != 0 || !A.x ||
       !A.stats || (reinterpret_cast<uintptr_t>(A.x) & 15) || (reinterpret_cast<uintptr_t>(A.stats) & 7) || (reinterpret_cast<uintptr_t>(B) & 15) ||
       (reinterpret_cast<uintptr_t>(args.bias) & 15) || (reinterpret_cast<uintptr_t>(args.out) & 15) ||
@@ -1618,7 +1665,8 @@ cudaError_t gemm_launch(const void* A, int lda, const void* B, int ldb, bool bf1
                         const GemmArgs& args, cudaStream_t st) {
   if (args.M <= 0) return cudaSuccess;
   auto al16 = [](const void* p) { return !(reinterpret_cast<uintptr_t>(p) & 15); };
-  const bool skinny = args.skinny && args.M <= SKINNY_M && !args.stats && args.N % BN == 0 && args.K % 8 == 0 &&
+  const bool skinny = args.skinny && !args.split_k && args.ofmt == OUT_H && args.M <= SKINNY_M && !args.stats &&
+                      args.N % BN == 0 && args.K % 8 == 0 &&
                       args.K <= 4096 && lda % 8 == 0 && ldb % 8 == 0 && (args.ln_x || al16(A)) && al16(B) &&
                       args.epi != EPI_POWER_F32 && gemm_skinny_enabled();
   // the LayerNorm prologue exists on the skinny kernel only
@@ -1643,12 +1691,18 @@ cudaError_t gemm_launch(const void* A, int lda, const void* B, int ldb, bool bf1
       (reinterpret_cast<uintptr_t>(args.bias) & 15) || (reinterpret_cast<uintptr_t>(args.out) & 15) ||
       (args.ldo % 8) != 0)
     return cudaErrorInvalidValue;
+  // split-f16 operands: K = 3 Ks k-steps over [hi | lo] rows of width 2 Ks
+  if (args.split_k && (bf16 || args.split_k % BK != 0 || args.K != 3 * args.split_k || lda < 2 * args.split_k ||
+                       ldb < 2 * args.split_k))
+    return cudaErrorInvalidValue;
+  if (args.ofmt == OUT_SPLIT && (bf16 || args.split_ld <= 0 || args.split_ld % 4 != 0)) return cudaErrorInvalidValue;
+  const int kmap = args.split_k ? 2 * args.split_k : args.K;
   // 2-SM tiles once there are at least two 128-row blocks of A
   const bool two_sm = args.M > BM && gemm_2sm_enabled();
   const int box = two_sm ? HALF_ROWS : 0;
   CUtensorMap ta, tb;
-  if (!make_tmap_kmajor(&ta, A, args.M, args.K, lda, two_sm ? box : BM, bf16)) return cudaErrorInvalidValue;
-  if (!make_tmap_kmajor(&tb, B, args.N, args.K, ldb, two_sm ? box : BN, bf16)) return cudaErrorInvalidValue;
+  if (!make_tmap_kmajor(&ta, A, args.M, kmap, lda, two_sm ? box : BM, bf16)) return cudaErrorInvalidValue;
+  if (!make_tmap_kmajor(&tb, B, args.N, kmap, ldb, two_sm ? box : BN, bf16)) return cudaErrorInvalidValue;
   switch (args.epi) {
 #define PKC_GEMM_CASE(E)                                                                   \
   case E:                                                                                  \

@@ -13,6 +13,10 @@ enum EpiKind : int {
   EPI_POWER_F32 = 4,
 };
 enum ActKind : int { ACT_NONE = 0, ACT_SILU = 1, ACT_RELU = 2 };
+// Output form of EPI_STORE_H / EPI_GLU_H: the operand type (OUT_H), f32, or
+// the split-f16 pair of the f32-accurate mode (OUT_SPLIT: hi = f16(v) at the
+// column, lo = f16(v - hi) at the column + split_ld; f16 operands only).
+enum OutFmt : int { OUT_H = 0, OUT_F32 = 1, OUT_SPLIT = 2 };
 
 struct GemmArgs {
   int M, N, K;
@@ -48,6 +52,14 @@ struct GemmArgs {
   int ln_ldx;
   const float* ln_g;
   const float* ln_b;
+  // f32-accurate mode: split-f16 operands A [M, 2 Ks] = [A_hi | A_lo] and
+  // B [N, 2 Ks] = [B_hi | B_lo] (f16, K-major, row strides lda / ldb); the
+  // kernel accumulates A_hi B_hi^T + A_hi B_lo^T + A_lo B_hi^T, i.e. K =
+  // 3 Ks k-steps whose operand columns are remapped per pass (a product
+  // carries ~22 significant bits; A_lo B_lo is below f32 rounding). 0: plain.
+  int split_k;
+  int ofmt;       // OutFmt (EPI_STORE_H / EPI_GLU_H)
+  int split_ld;   // OUT_SPLIT: column offset of the lo half in the output rows
 };
 
 // Stream-K workspace sizes for `pairs` CTA pairs (a device's SMs / 2).

@@ -83,9 +83,10 @@ cudaError_t sub_dw_launch(const __nv_bfloat16* in, int F_in, const int* in_off, 
 // If g2 != nullptr: y = LN(x; g, b) is written back to x (f32) and
 // out_h = LN(y; g2, b2) (norm_out of one layer fused with the next layer's
 // norm_feed_forward1).
+// split (f32-accurate path): out_h is f16 [M, 2d], rows [hi | lo].
 cudaError_t layernorm_launch(float* x, int M, int d, const float* g, const float* b, void* out_h,
                              bool bf16, const float* g2, const float* b2, bool write_x,
-                             cudaStream_t st);
+                             cudaStream_t st, bool split = false);
 
 // Sinusoid table over relative positions centre-1 ... -(centre-1): [2*centre-1, d].
 cudaError_t pos_table_launch(void* out, int centre, int d, bool bf16, cudaStream_t st);
@@ -112,6 +113,28 @@ cudaError_t attention_launch(const AttnArgs& a, bool bf16, cudaStream_t st);
 int attn_query_tile();
 cudaError_t attention_tc_launch(const AttnArgs& a, bool bf16, cudaStream_t st);
 int attn_tc_query_tile();
+
+// ---- f32-accurate path (precise.cu): GEMM operands as f16 [hi | lo] rows
+// f32 [rows, K] (row stride ldx) -> f16 [rows, 2K] rows [hi | lo] (row stride ldo)
+cudaError_t split_rows_launch(const float* x, long long rows, int K, int ldx, __half* out, int ldo,
+                              cudaStream_t st);
+// sinusoid table [2*centre-1, 2d], rows [hi | lo]
+cudaError_t pos_table_split_launch(__half* out, int centre, int d, cudaStream_t st);
+// conv.0 + ReLU with f32 output [sum v1, F1, C]
+cudaError_t sub_conv0_f32_launch(const float* logmel, int F, const float* w, const float* b, int C, float* out,
+                                 int F1, const ItemTables& t, int total_v1, cudaStream_t st);
+// subsampling depthwise 3x3 s2 + bias: f32 [frames, F_in, C] -> f16 [frames * F_out, 2C] rows [hi | lo]
+cudaError_t sub_dw_f32split_launch(const float* in, int F_in, const int* in_off, const int* in_valid, const float* w,
+                                   const float* b, int C, __half* out, int F_out, const int* out_off,
+                                   const int* out_valid, int B, int max_out, cudaStream_t st);
+// conv module depthwise + BatchNorm + SiLU: f32 [M, d] -> f16 [M, 2d] rows [hi | lo]
+cudaError_t dwconv_f32split_launch(const float* in, __half* out, int d, int K, const float* w, const float* bias,
+                                   const float* scale, const float* shift, const int* item_off, const int* item_len,
+                                   int B, int max_len, cudaStream_t st);
+// rel-pos attention in f32: qkv f32 [M, 3d], ptab f32 (ptab_ld), ctx f16 [M, 2d]
+// rows [hi | lo]; tiles of attn_f32_query_tile() query rows
+cudaError_t attention_f32_launch(const AttnArgs& a, cudaStream_t st);
+int attn_f32_query_tile();
 
 // Conv module middle: depthwise Conv1d(K, pad (K-1)/2) over each item's frames
 // (zeros outside) + bias -> BatchNorm (folded scale/shift) -> SiLU.

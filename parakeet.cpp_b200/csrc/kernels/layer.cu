@@ -16,7 +16,9 @@ namespace pkc {
 namespace {
 
 // One warp per row; each lane holds d/32 values (NV float4 chunks).
-template <int NV, typename H>
+// SPLIT (f32-accurate path, H = f16): out_h rows are [hi | lo] of width 2d,
+// hi = f16(y), lo = f16(y - hi).
+template <int NV, typename H, bool SPLIT>
 __global__ void __launch_bounds__(256)
     k_layernorm(float* __restrict__ x, int M, const float* __restrict__ g, const float* __restrict__ b,
                 H* __restrict__ out_h, const float* __restrict__ g2, const float* __restrict__ b2,
@@ -84,13 +86,25 @@ __global__ void __launch_bounds__(256)
   }
   if (g2) norm(nullptr, nullptr);
   if (out_h) {
-    H* o = out_h + (size_t)row * D;
+    H* o = out_h + (size_t)row * D * (SPLIT ? 2 : 1);
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
-      uint2 w;
-      w.x = pack2<H>(v[4 * i], v[4 * i + 1]);
-      w.y = pack2<H>(v[4 * i + 2], v[4 * i + 3]);
-      *reinterpret_cast<uint2*>(o + (i * 32 + lane) * 4) = w;
+      if constexpr (SPLIT) {
+        float hi[4], lo[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          hi[e] = from_h(to_h<H>(v[4 * i + e]));
+          lo[e] = v[4 * i + e] - hi[e];
+        }
+        *reinterpret_cast<uint2*>(o + (i * 32 + lane) * 4) = make_uint2(pack2<H>(hi[0], hi[1]), pack2<H>(hi[2], hi[3]));
+        *reinterpret_cast<uint2*>(o + D + (i * 32 + lane) * 4) =
+            make_uint2(pack2<H>(lo[0], lo[1]), pack2<H>(lo[2], lo[3]));
+      } else {
+        uint2 w;
+        w.x = pack2<H>(v[4 * i], v[4 * i + 1]);
+        w.y = pack2<H>(v[4 * i + 2], v[4 * i + 3]);
+        *reinterpret_cast<uint2*>(o + (i * 32 + lane) * 4) = w;
+      }
     }
   }
 }
@@ -220,16 +234,19 @@ __global__ void k_to_chfirst(const float* __restrict__ x, float* __restrict__ ou
 
 cudaError_t layernorm_launch(float* x, int M, int d, const float* g, const float* b, void* out_h,
                              bool bf16, const float* g2, const float* b2, bool write_x,
-                             cudaStream_t st) {
+                             cudaStream_t st, bool split) {
   if (M <= 0) return cudaSuccess;
+  if (split && bf16) return cudaErrorInvalidValue;
   const dim3 grid((M + 7) / 8);
   const int wx = write_x ? 1 : 0;
   cudaError_t e = cudaSuccess;
 #define PKC_LN(NV)                                                                                   \
-  if (bf16)                                                                                          \
-    e = launch_pdl(k_layernorm<NV, __nv_bfloat16>, grid, dim3(256), 0, st, x, M, g, b, (__nv_bfloat16*)out_h, g2, b2, wx); \
+  if (split)                                                                                         \
+    e = launch_pdl(k_layernorm<NV, __half, true>, grid, dim3(256), 0, st, x, M, g, b, (__half*)out_h, g2, b2, wx); \
+  else if (bf16)                                                                                     \
+    e = launch_pdl(k_layernorm<NV, __nv_bfloat16, false>, grid, dim3(256), 0, st, x, M, g, b, (__nv_bfloat16*)out_h, g2, b2, wx); \
   else                                                                                               \
-    e = launch_pdl(k_layernorm<NV, __half>, grid, dim3(256), 0, st, x, M, g, b, (__half*)out_h, g2, b2, wx);
+    e = launch_pdl(k_layernorm<NV, __half, false>, grid, dim3(256), 0, st, x, M, g, b, (__half*)out_h, g2, b2, wx);
   switch (d) {
     case 256: PKC_LN(2) break;
     case 512: PKC_LN(4) break;

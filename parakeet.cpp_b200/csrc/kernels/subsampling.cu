@@ -23,9 +23,14 @@ namespace {
 // thread keeps its 9 taps in registers, the three input mel rows sit in shared
 // memory, and each step over f writes C consecutive bf16 (coalesced).
 // grid.x = sum of v1 over the batch (row -> utterance by binary search).
+__device__ __forceinline__ void store_act(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
+__device__ __forceinline__ void store_act(float* p, float v) { *p = v; }
+
+// O: bf16 (the f16 / bf16 compute path) or f32 (the f32-accurate path)
+template <typename O>
 __global__ void __launch_bounds__(256)
     k_conv0(const float* __restrict__ logmel, int F, const float* __restrict__ w,
-            const float* __restrict__ bias, int C, __nv_bfloat16* __restrict__ out, int F1,
+            const float* __restrict__ bias, int C, O* __restrict__ out, int F1,
             ItemTables t) {
   pdl_wait();
   pdl_trigger();
@@ -46,7 +51,7 @@ __global__ void __launch_bounds__(256)
     rows[i] = (fi >= 0 && fi < F && ti >= 0 && ti < valid) ? x[(size_t)ti * F + fi] : 0.f;
   }
   __syncthreads();
-  __nv_bfloat16* o = out + (size_t)row * F1 * C;
+  O* o = out + (size_t)row * F1 * C;
   for (int c = threadIdx.x; c < C; c += blockDim.x) {
     float wk[9];
 #pragma unroll
@@ -58,7 +63,7 @@ __global__ void __launch_bounds__(256)
       for (int kh = 0; kh < 3; ++kh)
 #pragma unroll
         for (int kw = 0; kw < 3; ++kw) s = fmaf(wk[kh * 3 + kw], rows[kh * (F + 2) + 2 * f + kw], s);
-      o[(size_t)f * C + c] = __float2bfloat16_rn(fmaxf(s, 0.f));
+      store_act(o + (size_t)f * C + c, fmaxf(s, 0.f));
     }
   }
 }
@@ -313,7 +318,14 @@ cudaError_t sub_conv0_launch(const float* logmel, int F, const float* w, const f
                              cudaStream_t st) {
   if (t.B <= 0 || total_v1 <= 0) return cudaSuccess;
   const size_t smem = (size_t)3 * (F + 2) * sizeof(float);
-  return launch_pdl(k_conv0, dim3(total_v1), dim3(256), smem, st, logmel, F, w, b, C, out, F1, t);
+  return launch_pdl(k_conv0<__nv_bfloat16>, dim3(total_v1), dim3(256), smem, st, logmel, F, w, b, C, out, F1, t);
+}
+
+cudaError_t sub_conv0_f32_launch(const float* logmel, int F, const float* w, const float* b, int C, float* out,
+                                 int F1, const ItemTables& t, int total_v1, cudaStream_t st) {
+  if (t.B <= 0 || total_v1 <= 0) return cudaSuccess;
+  const size_t smem = (size_t)3 * (F + 2) * sizeof(float);
+  return launch_pdl(k_conv0<float>, dim3(total_v1), dim3(256), smem, st, logmel, F, w, b, C, out, F1, t);
 }
 
 cudaError_t sub_dw_launch(const __nv_bfloat16* in, int F_in, const int* in_off, const int* in_valid,

@@ -150,6 +150,22 @@ std::vector<uint16_t> to_h(const std::vector<float>& v, bool bf16) {
   return h;
 }
 
+// f32 rows [N][K] -> f16 rows [N][2K] = [hi | lo] with hi = f16(w) and
+// lo = f16(w - hi): the split-f16 form of the f32-accurate path.
+std::vector<uint16_t> to_split(const std::vector<float>& v, int64_t N, int64_t K) {
+  std::vector<uint16_t> h((size_t)(N * 2 * K));
+  parallel_rows(N, [&](int64_t a, int64_t b) {
+    for (int64_t n = a; n < b; ++n)
+      for (int64_t k = 0; k < K; ++k) {
+        const float x = v[(size_t)(n * K + k)];
+        const uint16_t hi = f32_to_f16(x);
+        h[(size_t)(n * 2 * K + k)] = hi;
+        h[(size_t)(n * 2 * K + K + k)] = f32_to_f16(x - f16_to_f32(hi));
+      }
+  });
+  return h;
+}
+
 // Linear weight [N][K] in the target 16-bit type; bytes copied verbatim when
 // the GGUF already stores that type.
 bool read_h(const GgufFile& g, const std::string& name, int64_t N, int64_t K, bool bf16,
@@ -351,6 +367,11 @@ std::string read_config(const GgufFile& g, Config& c) {
   if (!probe) return "missing encoder.layers.0.feed_forward1.linear1.weight";
   c.weight_type = probe->type;
   c.bf16 = probe->type == GT_BF16;
+  // f32 weights run the f32-accurate split-f16 path, as the reference runs an
+  // f32 model in f32 (PKC_F32_AS_F16=1: f16 operands instead); the streaming
+  // encoder's kernels have no split form
+  const char* fa = getenv("PKC_F32_AS_F16");
+  c.split = probe->type == GT_F32 && !c.causal() && !(fa && fa[0] == '1');
   return "";
 }
 
@@ -379,6 +400,7 @@ std::string pack_weights(const GgufFile& g, const Config& c, bool fold_ln, Packe
   DeviceWeights& w = p.tmpl;
   const int d = c.d_model, FF = c.ff_dim, C = c.sub_channels, K = c.conv_kernel, H = c.n_heads;
   const bool bf = c.bf16;
+  const bool sp = c.split;
   std::vector<float> f, f2, f3, f4;
   std::vector<uint16_t> h;
 
@@ -407,6 +429,11 @@ std::string pack_weights(const GgufFile& g, const Config& c, bool fold_ln, Packe
         qw = put_q(qh);
         return nullptr;
       }
+    }
+    if (sp) {
+      std::vector<float> wf;
+      if (!read_f32(g, name, N, Kd, wf, err)) return nullptr;
+      return put_h(to_split(wf, N, Kd));
     }
     if (!read_h(g, name, N, Kd, bf, h, err)) return nullptr;
     return put_h(h);
@@ -484,7 +511,7 @@ std::string pack_weights(const GgufFile& g, const Config& c, bool fold_ln, Packe
       if (!read_vec(g, p + "conv." + std::to_string(dwi) + ".bias", C, f, err)) return err;
       float* dwb = put_f(f);
       if (!read_f32(g, p + "conv." + std::to_string(pwi) + ".weight", C, C, f, err)) return err;
-      void* pww = put_h(to_h(f, true));
+      void* pww = put_h(sp ? to_split(f, C, C) : to_h(f, true));
       if (!read_vec(g, p + "conv." + std::to_string(pwi) + ".bias", C, f, err)) return err;
       float* pwb = put_f(f);
       if (s == 0) { w.dw1_w = dww; w.dw1_b = dwb; w.pw1_w = pww; w.pw1_b = pwb; }
@@ -497,7 +524,7 @@ std::string pack_weights(const GgufFile& g, const Config& c, bool fold_ln, Packe
       for (int ch = 0; ch < C; ++ch)
         for (int ff = 0; ff < F3; ++ff)
           perm[(size_t)o * KW + ff * C + ch] = f[(size_t)o * KW + ch * F3 + ff];
-    w.out_w = put_h(to_h(perm, true));
+    w.out_w = put_h(sp ? to_split(perm, d, KW) : to_h(perm, true));
     if (!read_vec(g, p + "out.bias", d, f, err)) return err;
     w.out_b = put_f(f);
   }
@@ -584,6 +611,13 @@ std::string pack_weights(const GgufFile& g, const Config& c, bool fold_ln, Packe
         qkv = to_h(wq, bf);
         any_b = true;
         L.qkv_ln = true;
+      } else if (sp && !all_q) {
+        std::vector<float> wq((size_t)3 * d * d);
+        for (int i = 0; i < 3; ++i) {
+          if (!read_f32(g, a + nms[i] + ".weight", d, d, f, err)) return err;
+          std::memcpy(wq.data() + (size_t)i * d * d, f.data(), (size_t)d * d * 4);
+        }
+        qkv = to_split(wq, 3 * d, d);
       } else {
         for (int i = 0; i < 3; ++i) {
           if (all_q) break;
@@ -598,7 +632,12 @@ std::string pack_weights(const GgufFile& g, const Config& c, bool fold_ln, Packe
       QHost qp;
       if (pos_quant && !read_quant(g, a + "linear_pos.weight", d, d, qp, err)) return err;
       pos_quant = pos_quant && qp.type != 0 && q_concat(pos_q, qp);
-      if (!read_h(g, a + "linear_pos.weight", d, d, bf, h, err)) return err;
+      if (sp) {
+        if (!read_f32(g, a + "linear_pos.weight", d, d, f, err)) return err;
+        h = to_split(f, d, d);
+      } else if (!read_h(g, a + "linear_pos.weight", d, d, bf, h, err)) {
+        return err;
+      }
       pos_all.insert(pos_all.end(), h.begin(), h.end());
     }
     L.pos_w = nullptr;
@@ -628,7 +667,7 @@ std::string pack_weights(const GgufFile& g, const Config& c, bool fold_ln, Packe
         fold_layernorm(paired, 2 * d, d, lng[2], lnb[2], pb);
         L.pw1_ln = true;
       }
-      L.pw1_w = put_h(to_h(paired, bf));
+      L.pw1_w = put_h(sp ? to_split(paired, 2 * d, d) : to_h(paired, bf));
       L.pw1_b = (has_b || fold_ln) ? put_f(pb) : nullptr;
       if (!read_f32(g, p + "conv.depthwise_conv.weight", d, K, f, err)) return err;
       std::vector<float> tap((size_t)K * d);
@@ -656,7 +695,7 @@ std::string pack_weights(const GgufFile& g, const Config& c, bool fold_ln, Packe
         L.bn_shift = put_f(sh);
       }
       if (!read_f32(g, p + "conv.pointwise_conv2.weight", d, d, f, err)) return err;
-      L.pw2_w = put_h(to_h(f, bf));
+      L.pw2_w = put_h(sp ? to_split(f, d, d) : to_h(f, bf));
       L.pw2_b = opt_vec(p + "conv.pointwise_conv2.bias", d);
       if (!err.empty()) return err;
     }
@@ -860,8 +899,8 @@ uint64_t pack_cache_key(const std::string& gguf_path, const Config& c, bool fold
     h = fnv1a(h, v, sizeof(v));
   }
   const char* dal = getenv("PKC_DEQUANT_AT_LOAD");
-  const uint32_t opts[4] = {fold_ln ? 1u : 0u, (dal && dal[0] == '1') ? 1u : 0u, (uint32_t)c.n_layers,
-                            (uint32_t)sizeof(DeviceWeights)};
+  const uint32_t opts[5] = {fold_ln ? 1u : 0u, (dal && dal[0] == '1') ? 1u : 0u, (uint32_t)c.n_layers,
+                            (uint32_t)sizeof(DeviceWeights), c.split ? 1u : 0u};
   return fnv1a(h, opts, sizeof(opts));
 }
 

@@ -45,6 +45,9 @@ struct Config {
   int F1 = 0, F2 = 0, F3 = 0;
   uint32_t weight_type = 0;  // GGUF type of the encoder linear weights
   bool bf16 = false;         // tensor-core operand type of the conformer layers
+  // f32-accurate path (f32 GGUF weights, offline encoder): every linear
+  // weight and GEMM operand as split-f16 [hi | lo] rows, f32 between GEMMs
+  bool split = false;
 };
 
 // Read and validate the configuration. Returns an empty string on success,

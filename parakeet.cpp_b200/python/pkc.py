@@ -133,6 +133,10 @@ def _declare(L):
          c_int, c_int, c_int, c_int, c_void_p, c_void_p),
         ("pkc_relpos_attention_noalloc", c_int, c_void_p, c_void_p, c_int, c_void_p, c_void_p,
          POINTER(c_int), c_int, c_int, c_int, c_int, c_void_p, c_void_p),
+        ("pkc_gemm_split", c_int, c_void_p, c_int, c_void_p, c_int, c_int, c_int, c_int, c_int, c_int,
+         c_float, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p),
+        ("pkc_relpos_attention_f32", c_int, c_void_p, c_void_p, c_int, c_void_p, c_void_p, POINTER(c_int),
+         c_int, c_int, c_int, c_void_p, c_void_p),
     ]
     for name, res, *args in optional:
         if hasattr(L, name):
@@ -156,6 +160,25 @@ def gemm(A, B, M, N, K, *, bf16, epi, act=ACT_NONE, alpha=1.0, bias=None, out, l
     _check(lib().pkc_gemm(c_void_p(A), lda or K, c_void_p(B), ldb or K, M, N, K, 1 if bf16 else 0,
                           epi, act, alpha, c_void_p(bias) if bias else None, c_void_p(out), ldo,
                           c_void_p(stream) if stream else None))
+
+
+OUT_H, OUT_F32, OUT_SPLIT = 0, 1, 2
+
+
+def gemm_split(A, B, M, N, Ks, *, epi, act=ACT_NONE, alpha=1.0, bias=None, out, ldo, ofmt=OUT_H, split_ld=0,
+               lda=None, ldb=None, stream=0):
+    """Split-f16 GEMM of the f32-accurate path: A [M, 2Ks] and B [N, 2Ks] f16
+    rows [hi | lo] (device pointers as ints)."""
+    _check(lib().pkc_gemm_split(c_void_p(A), lda or 2 * Ks, c_void_p(B), ldb or 2 * Ks, M, N, Ks, epi, act, alpha,
+                                c_void_p(bias) if bias else None, c_void_p(out), ldo, ofmt, split_ld,
+                                c_void_p(stream) if stream else None))
+
+
+def relpos_attention_f32(qkv, ptab, centre, bias_u, bias_v, lens, d, n_heads, *, ctx, stream=0):
+    """f32 rel-pos attention (f32 qkv / ptab in, split-f16 [M, 2d] ctx out)."""
+    _check(lib().pkc_relpos_attention_f32(c_void_p(qkv), c_void_p(ptab), centre, c_void_p(bias_u), c_void_p(bias_v),
+                                          _ints(lens), len(lens), d, n_heads, c_void_p(ctx),
+                                          c_void_p(stream) if stream else None))
 
 
 def ctc_fold(argmax, max_logprob, n_classes, blank_id):

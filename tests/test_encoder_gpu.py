@@ -1,12 +1,14 @@
 """GPU parity: libpkc.so (through the C ABI) against the CPU oracle, which
 restates parakeet.cpp's batched encoder graph in float64.
 
-Tolerances (stated per the north star): encoder outputs within 2e-2 relative
-error (max |gpu - oracle| / max |oracle| over each utterance's output) for the
-f16 / bf16 compute path; the log-mel front end within 2e-3 absolute on
-normalised features (the reference's own GPU-vs-CPU mel test allows 0.05).
-Quantised weights (q8_0 / q4_k) are dequantised once to the compute type, so
-they carry one extra rounding of the weight and use the same bound.
+Tolerances (stated per the north star), per element with the reference's
+comparator form |gpu - oracle| <= atol + rtol |oracle| (tests/parity.py:
+atol = rtol * rms of the output): rtol 1e-3 for f32 weights (the
+f32-accurate split-f16 path), 2e-2 for the f16 / bf16 compute path; the
+log-mel front end within 2e-3 absolute on normalised features (the
+reference's own GPU-vs-CPU mel test allows 0.05). Quantised weights (q8_0 /
+q4_k) are dequantised to the compute type exactly as the oracle dequantises
+them, so they carry the f16 path's bound.
 """
 import os
 
@@ -22,6 +24,10 @@ def rel_err(got, ref):
     return float(np.abs(got - ref).max() / max(np.abs(ref).max(), 1e-30))
 
 
+# per-element bound of each model kind (f32 weights: the f32-accurate path)
+RTOL = {"f32_bias": 1e-3, "f32_xs": 1e-3}
+
+
 @pytest.fixture(scope="session")
 def models(tmp_path_factory):
     import synth
@@ -31,6 +37,9 @@ def models(tmp_path_factory):
     cfgs = {
         "f16": synth.small_cfg("c2_0.6b_f16", n_mels=80, **small),
         "f32_bias": synth.small_cfg("c1_110m", **small),
+        # the reference scales the subsampling output by sqrt(d_model) when
+        # parakeet.encoder.xscaling is set (src/encoder.cpp:59-61,123)
+        "f32_xs": synth.small_cfg("c1_110m", xscaling=True, **small),
         "bf16": synth.small_cfg("c5_0.6b_bf16_long", n_mels=128, **small),
         "q8_0": synth.small_cfg("c3_0.6b_q8", n_mels=80, **small),
         "q4_k": synth.small_cfg("c4_1.1b_q4k", n_mels=128, **small),
@@ -88,17 +97,18 @@ def test_mel_front_end_matches_oracle(opened, oracles):
     assert np.abs(got - ref_fft).max() < 2e-3
 
 
-@pytest.mark.parametrize("kind", ["f16", "f32_bias", "bf16", "q8_0", "q4_k", "dk128"])
+@pytest.mark.parametrize("kind", ["f16", "f32_bias", "f32_xs", "bf16", "q8_0", "q4_k", "dk128"])
 def test_encoder_matches_oracle(opened, oracles, kind):
     import oracle
+    from parity import max_rel_err
     m, w = opened(kind), oracles(kind)
     pcm = clips([SR * 3 + 500, SR * 1 + 1234, SR * 2], seed=1)
     outs = m.encode_pcm_batch(pcm)
     ref = oracle.encode_pcm_batch(w, pcm)
     assert [o.shape[1] for o in outs] == ref.valid
-    for got, r in zip(outs, ref.outs):
-        e = rel_err(got, r.T)
-        assert e < 2e-2, (kind, e)
+    errs = [max_rel_err(got, r.T) for got, r in zip(outs, ref.outs)]
+    print(f"encoder {kind}: per-element max rel err {[f'{e:.2e}' for e in errs]}")
+    assert max(errs) <= RTOL.get(kind, 2e-2), (kind, errs)
 
 
 def test_batched_equals_standalone(opened):
