@@ -56,6 +56,28 @@ import numpy as np
 
 LN_EPS = 1e-5
 BN_EPS = 1e-5
+
+# Arithmetic type of the encoder restatement: float64 for every parity use.
+# compute_dtype(np.float32) runs the same graph in float32 (weights are stored
+# float32, so every op then stays float32): only the timed CPU baseline of
+# bench.py uses it, to time the reference's f32 CPU path fairly.
+_DT = np.float64
+
+
+class compute_dtype:
+    """Context manager: run the encoder restatement in the given numpy type."""
+
+    def __init__(self, dt):
+        self.dt = dt
+
+    def __enter__(self):
+        global _DT
+        self.prev, _DT = _DT, self.dt
+        return self
+
+    def __exit__(self, *exc):
+        global _DT
+        _DT = self.prev
 NORM_EPS = 1e-5       # per-feature mel normalisation (src/mel.cpp:13)
 INF_VAL = 10000.0     # sinusoid base (src/pos_enc.cpp:8)
 
@@ -241,7 +263,7 @@ def _conv3x3_s2(x: np.ndarray, wk: np.ndarray) -> np.ndarray:
     leading dims; returns sum_{kh,kw} wk*x at stride 2 -> [..., H', W']."""
     H, W = x.shape[-2:]
     Ho, Wo = conv_out_len(H), conv_out_len(W)
-    xp = np.zeros(x.shape[:-2] + (H + 2, W + 2), dtype=np.float64)
+    xp = np.zeros(x.shape[:-2] + (H + 2, W + 2), dtype=_DT)
     xp[..., 1:H + 1, 1:W + 1] = x
     out = 0
     for kh in range(3):
@@ -256,14 +278,14 @@ def subsampling_batched(w: Weights, mel: np.ndarray, valid_in: list[int]):
     mel [B, F, T] -> (x [B, Tp, d], out_valid [B])."""
     B, F, T = mel.shape
     C = w.C
-    x = mel.astype(np.float64).transpose(0, 2, 1)             # [B, T, F] (H=T, W=F)
+    x = mel.astype(_DT).transpose(0, 2, 1)                    # [B, T, F] (H=T, W=F)
     vt0 = [v if v >= 0 else T - 1 for v in valid_in]
     vt1 = [cdiv_trunc(v - 1, 2) + 1 for v in vt0]
     vt2 = [cdiv_trunc(v - 1, 2) + 1 for v in vt1]
 
     def mask_time(t, vt):                                    # t [B, C?, H, W]
         H = t.shape[-2]
-        m = (np.arange(H)[None, :] < np.array(vt)[:, None]).astype(np.float64)
+        m = (np.arange(H)[None, :] < np.array(vt)[:, None]).astype(_DT)
         return t * m.reshape((t.shape[0],) + (1,) * (t.ndim - 3) + (H, 1))
 
     g = lambda n: w.get("encoder.pre_encode." + n)
@@ -280,7 +302,7 @@ def subsampling_batched(w: Weights, mel: np.ndarray, valid_in: list[int]):
     _, _, Tp, Fp = y.shape
     flat = y.transpose(0, 2, 1, 3).reshape(B, Tp, C * Fp)      # idx c*F' + f
     out_valid = [min(valid_out_len(T, v), Tp) for v in valid_in]
-    m = (np.arange(Tp)[None, :] < np.array(out_valid)[:, None]).astype(np.float64)
+    m = (np.arange(Tp)[None, :] < np.array(out_valid)[:, None]).astype(_DT)
     flat = flat * m[:, :, None]
     out = flat @ g("out.weight").T + g("out.bias")
     return out, out_valid
@@ -354,7 +376,7 @@ def relpos_attention(w: Weights, li: int, x: np.ndarray, pe: np.ndarray, valid: 
     q = linear(x, g("linear_q.weight"), g("linear_q.bias")).reshape(T, H, dk).transpose(1, 0, 2)
     k = linear(x, g("linear_k.weight"), g("linear_k.bias")).reshape(T, H, dk).transpose(1, 0, 2)
     v = linear(x, g("linear_v.weight"), g("linear_v.bias")).reshape(T, H, dk).transpose(1, 0, 2)
-    p = linear(pe.astype(np.float64), g("linear_pos.weight")).reshape(2 * T - 1, H, dk).transpose(1, 0, 2)
+    p = linear(pe.astype(_DT), g("linear_pos.weight")).reshape(2 * T - 1, H, dk).transpose(1, 0, 2)
     qu = q + g("pos_bias_u")[:, None, :]
     qv = q + g("pos_bias_v")[:, None, :]
     ac = qu @ k.transpose(0, 2, 1)                              # [H, Tq, Tk]
@@ -367,7 +389,7 @@ def relpos_attention(w: Weights, li: int, x: np.ndarray, pe: np.ndarray, valid: 
     vis = np.broadcast_to(np.arange(T)[None, :] < valid, (T, T))
     if chunked is not None:
         vis = vis & chunked_visible(np.arange(T), np.arange(T), *chunked)
-    mask = np.where(vis, 0.0, -np.inf)[None]
+    mask = np.where(vis, 0.0, -np.inf).astype(_DT)[None]
     s = (ac + bd) * scale + mask
     s = s - s.max(axis=-1, keepdims=True)
     e = np.exp(s)
@@ -385,7 +407,7 @@ def bn_fold(w: Weights, pre: str):
     var = w.get(pre + "conv.batch_norm.running_var").astype(np.float32)
     sc = (gmm / np.sqrt(var + np.float32(BN_EPS))).astype(np.float32)
     sh = (bb - m * sc).astype(np.float32)
-    return sc.astype(np.float64), sh.astype(np.float64)
+    return sc.astype(_DT), sh.astype(_DT)
 
 
 def conv_norm(w: Weights, pre: str, dw: np.ndarray, norm: str) -> np.ndarray:
@@ -411,9 +433,9 @@ def conv_module(w: Weights, li: int, c: np.ndarray, valid: int, causal: bool = F
     K = w.K
     left = K - 1 if causal else (K - 1) // 2
     dww = g("conv.depthwise_conv.weight")[:, 0, :]             # [d, K]
-    gp = np.zeros((T + K - 1, d))
+    gp = np.zeros((T + K - 1, d), dtype=_DT)
     gp[left:left + T] = glu
-    dw = np.zeros((T, d))
+    dw = np.zeros((T, d), dtype=_DT)
     for k in range(K):
         dw += gp[k:k + T] * dww[:, k][None, :]
     if g("conv.depthwise_conv.bias") is not None:
@@ -805,10 +827,12 @@ def _max_prob_conf(a, k):
     return (N * p - 1.0) / (N - 1.0)
 
 
-def transducer_greedy(tr: Transducer, enc: np.ndarray):
+def transducer_greedy(tr: Transducer, enc: np.ndarray, trace=None):
     """tdt_greedy (durations present) or rnnt_greedy on one utterance's
     encoder output enc [T, d]. Returns ([(id, frame, conf, span)], the smallest
-    top-two gap over every argmax taken)."""
+    top-two gap over every argmax taken). If trace is a list, every joint
+    decision appends (tokens emitted before it, its top-two gap (TDT: the
+    smaller of the token and duration gaps), frame t, prediction output g)."""
     enc_proj = enc.astype(np.float64) @ tr.w_enc.T + tr.b_enc
     T = enc.shape[0]
     out, gap = [], math.inf
@@ -829,6 +853,8 @@ def transducer_greedy(tr: Transducer, enc: np.ndarray):
                 k, g1 = _argmax_gap(lg[:tr.V1])
                 dk, g2 = _argmax_gap(lg[tr.V1:tr.V1 + ND])
                 gap = min(gap, g1, g2)
+                if trace is not None:
+                    trace.append((len(out), min(g1, g2), t, g))
                 skip = tr.durations[dk]
                 if k != tr.blank:
                     out.append((k, t, _max_prob_conf(lg[:tr.V1], k), skip))
@@ -848,6 +874,8 @@ def transducer_greedy(tr: Transducer, enc: np.ndarray):
                 lg = tr.logits(enc_proj[t], g)
                 k, g1 = _argmax_gap(lg)
                 gap = min(gap, g1)
+                if trace is not None:
+                    trace.append((len(out), g1, t, g))
                 if k == tr.blank:
                     break
                 out.append((k, t, _max_prob_conf(lg, k), 1))
