@@ -2,21 +2,25 @@
 
 One step = one batch of synthetic utterances through the hot path (log-mel
 front end, dw-striding subsampling, all conformer layers) of the workload's
-model. `value` is audio-seconds per second with the PCM already in HBM (the
-device-resident C-ABI entry); `e2e` is the same metric through the public
-host-buffer C-ABI call (pinned PCM in, encoder output back to host memory,
-copies inside the timed region).
+model. The default workload is the north star's: the 0.6B-class encoder with
+f16 weights on a GLOBAL batch of 64 clips of U(2, 35) s (BASELINE
+configuration 3's batch). `value` is audio-seconds per second with the PCM
+already in HBM (the device-resident C-ABI entry); `e2e` is the same metric
+through the public host-buffer C-ABI call (pinned PCM in, encoder output back
+to host memory, copies inside the timed region).
 
-Multi-GPU: one process per GPU (torchrun); every rank encodes its own batch of
-the workload (utterances sharded by whole clips, no collective on the data
-path) -> "scaling": "weak". Timing is CUDA events on the launching stream,
-max over ranks.
+Multi-GPU: one process per GPU (torchrun). The global batch is sharded by
+whole utterances with the library's own LPT planner (pkc_shard_plan): every
+rank encodes its share of the same 64 clips, so the total work is fixed as N
+grows -> "scaling": "strong". No collective on the data path; timing is CUDA
+events on the launching stream, max over ranks (NCCL all-reduce of the
+figures after the timed region).
 
 `--impl reference` times the reference's CPU path on the host cores instead:
 parakeet.cpp's ggml encoder cannot be built here (its ggml dependency is absent
 from the checkout), so the encoder runs as the CPU restatement in oracle/
-(numpy, float64, all BLAS threads) and the mel front end as parakeet.cpp's own
-MelFrontend compiled from its sources (oracle/_ref) when present.
+(numpy in float32, every BLAS thread) and the mel front end as parakeet.cpp's
+own MelFrontend compiled from its sources (oracle/_ref) when present.
 """
 from __future__ import annotations
 
@@ -36,6 +40,11 @@ for p in (os.path.join(REPO, "parakeet.cpp_b200", "python"), os.path.join(REPO, 
 METRIC = "batch RTFx (audio-s/s) at 1/2/4/8 B200; per-kernel % of HBM/tensor peak"
 UNIT = "audio-s/s"
 DEFAULT_CONFIG = "c2_0.6b_f16"
+# global batch of each workload (split across the ranks): the north star's
+# batch 64 for the 0.6B f16 / q8_0 models, the configuration's own otherwise
+GLOBAL_BATCH = {"c2_0.6b_f16": 64, "c3_0.6b_q8": 64}
+# the reference's default CPU thread count (src/ggml_graph.cpp:47)
+REF_DEFAULT_THREADS = 8
 SR = 16000
 L2_FLUSH_BYTES = 256 << 20
 
@@ -125,12 +134,23 @@ class ClockSampler:
                 "samples": len(sm)}
 
 
-def workload(config, rank, batch=None):
+def workload(config, batch=None):
+    """The global batch of a workload: every rank draws the same clips."""
     import synth
     b, lo, hi = synth.BATCHES[config]
-    b = batch or b
-    pcm = synth.synth_batch(config, seed=1000 + rank, batch=b)
+    b = batch or GLOBAL_BATCH.get(config, b)
+    pcm = synth.synth_batch(config, seed=1000, batch=b)
     return pcm, {"batch": b, "len_s": [lo, hi]}
+
+
+def my_share(pcm, world, rank):
+    """Indices of the clips this rank encodes: the library's LPT plan over
+    the ranks (pkc_shard_plan, cost T'(1 + T'/8192) per clip)."""
+    if world <= 1:
+        return list(range(len(pcm)))
+    import pkc
+    assign = pkc.shard_plan([len(p) for p in pcm], world)
+    return [i for i, a in enumerate(assign) if a == rank]
 
 
 def combine_ranks(ms, e2e_ms, audio_s, wall_ms, world, device):
@@ -150,8 +170,106 @@ def combine_ranks(ms, e2e_ms, audio_s, wall_ms, world, device):
 
 # ----------------------------------------------------------------------- ours
 
-def run_ours(args, rank, world, local_rank):
+def measure_encoder(model, pcm, dev, steps, warmup, world, profile=True):
+    """One rank's share of the workload: device-resident steps (CUDA events
+    per step, L2 flushed between steps outside the events), the per-kernel
+    profile pass, and e2e steps through the host-buffer API. Returns the
+    rank's figures (ms for `steps` steps)."""
     import numpy as np
+    import torch
+    import torch.distributed as dist
+    import pkc
+    n = [len(p) for p in pcm]
+    res = {"audio_s": sum(n) / SR, "clips": len(pcm), "ms": 0.0, "e2e_ms": 0.0, "e2e_wall_ms": 0.0,
+           "stats": [], "prof_steps": 0, "h2d": int(sum(n) * 4), "d2h": 0}
+    d = model.info.d_model
+    out_floats = int(sum(model.encoder_frames(model.mel_frames(x)) for x in n) * d) if n else 0
+    res["d2h"] = out_floats * 4
+    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
+    stream = torch.cuda.Stream(dev)
+    torch.cuda.set_stream(stream)
+    if n:
+        flat = np.concatenate(pcm).astype(np.float32)
+        d_pcm = torch.from_numpy(flat).to(dev)
+        d_out = torch.empty(out_floats, dtype=torch.float32, device=dev)
+
+        def step():
+            model.encode_pcm_device(d_pcm.data_ptr(), n, d_out.data_ptr(), stream=stream.cuda_stream)
+    else:
+        def step():
+            pass
+    for _ in range(warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    if n:
+        model.encode_pcm_device(d_pcm.data_ptr(), n, d_out.data_ptr(), stream=stream.cuda_stream, sync=True)
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(steps)]
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    for i in range(steps):
+        flush.zero_()
+        starts[i].record(stream)
+        step()
+        ends[i].record(stream)
+    torch.cuda.synchronize(dev)
+    if world > 1:
+        dist.barrier()
+    res["ms"] = sum(a.elapsed_time(b) for a, b in zip(starts, ends))
+    if n:
+        # the device path reports kernel errors through its error word on sync
+        model.encode_pcm_device(d_pcm.data_ptr(), n, d_out.data_ptr(), stream=stream.cuda_stream, sync=True)
+    if profile and n:
+        res["prof_steps"] = max(1, min(steps, 5))
+        model.profile_enable(True)
+        for _ in range(res["prof_steps"]):
+            step()
+        torch.cuda.synchronize(dev)
+        res["stats"] = model.profile_read()
+        model.profile_enable(False)
+    # e2e: public host-buffer API, pinned PCM in, output to a pinned host buffer
+    if n:
+        host_pcm = [torch.from_numpy(p).pin_memory().numpy() for p in pcm]
+        host_out = torch.empty(model.out_floats(n), dtype=torch.float32).pin_memory().numpy()
+        for _ in range(max(1, warmup)):
+            model.encode_pcm_batch(host_pcm, layout=pkc.LAYOUT_TIME_MAJOR, out=host_out)
+        lib_stream = torch.cuda.ExternalStream(model.stream(), device=dev)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    if n:
+        e0.record(lib_stream)
+        for _ in range(steps):
+            model.encode_pcm_batch(host_pcm, layout=pkc.LAYOUT_TIME_MAJOR, out=host_out)
+        e1.record(lib_stream)
+    torch.cuda.synchronize(dev)
+    res["e2e_wall_ms"] = (time.perf_counter() - t0) * 1e3
+    if n:
+        res["e2e_ms"] = e0.elapsed_time(e1)
+        res["host_pcm"] = host_pcm
+    return res
+
+
+def kernel_table(stats, prof_steps, peak, hbm):
+    kernels = []
+    tot_ms = sum(s["total_ms"] for s in stats) or 1.0
+    for s in sorted(stats, key=lambda s: -s["total_ms"]):
+        k = {"name": s["name"], "launches_per_step": s["launches"] / prof_steps,
+             "ms_per_step": round(s["total_ms"] / prof_steps, 4), "share": round(s["total_ms"] / tot_ms, 4)}
+        if s["flops"] > 0 and s["name"].startswith(("gemm", "attention")):
+            k["tflops"] = round(s["flops"] / (s["total_ms"] / 1e3) / 1e12, 1)
+            k["frac_tensor_peak"] = round(k["tflops"] / peak, 3)
+        elif s["bytes"] > 0:
+            k["gbs"] = round(s["bytes"] / (s["total_ms"] / 1e3) / 1e9, 1)
+            k["frac_hbm_peak"] = round(k["gbs"] / hbm, 3)
+        kernels.append(k)
+    return kernels
+
+
+def run_ours(args, rank, world, local_rank):
     import torch
     import torch.distributed as dist
     import pkc
@@ -166,9 +284,9 @@ def run_ours(args, rank, world, local_rank):
         dist.barrier()
     path = synth.ensure_gguf(cfg)
 
-    pcm, winfo = workload(args.config, rank, args.batch)
-    n = [len(p) for p in pcm]
-    audio_s = sum(n) / SR
+    pcm_all, winfo = workload(args.config, args.batch)
+    mine = my_share(pcm_all, world, rank)
+    pcm = [pcm_all[i] for i in mine]
 
     t_open = time.perf_counter()
     model = pkc.Model(path, devices=(local_rank,))
@@ -177,82 +295,19 @@ def run_ours(args, rank, world, local_rank):
     load["api"] = ("pkc_model_open: host re-pack once (or the PKC_PACK_CACHE pre-pack file), "
                    "page-locked image, concurrent per-device upload")
     d = model.info.d_model
-    out_floats = lib_out_floats = int(sum(model.encoder_frames(model.mel_frames(x)) for x in n) * d)
-    flat = np.concatenate(pcm).astype(np.float32)
-    d_pcm = torch.from_numpy(flat).to(dev)
-    d_out = torch.empty(out_floats, dtype=torch.float32, device=dev)
-    flush = torch.empty(L2_FLUSH_BYTES // 4, dtype=torch.float32, device=dev)
-    # one stream for everything timed: the library launches on it, the events
-    # are recorded on it, and the L2 flush runs on it between steps
-    stream = torch.cuda.Stream(dev)
-    torch.cuda.set_stream(stream)
 
-    def step():
-        model.encode_pcm_device(d_pcm.data_ptr(), n, d_out.data_ptr(), stream=stream.cuda_stream)
-
-    for _ in range(args.warmup):
-        step()
-    torch.cuda.synchronize(dev)
-    model.encode_pcm_device(d_pcm.data_ptr(), n, d_out.data_ptr(), stream=stream.cuda_stream, sync=True)
-
-    # ---- timed region: K steps, L2 flushed between steps (outside the step events)
-    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize(dev)
     with ClockSampler(local_rank) as clk:
-        for i in range(args.steps):
-            flush.zero_()
-            starts[i].record(stream)
-            step()
-            ends[i].record(stream)
-        torch.cuda.synchronize(dev)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize(dev)
-    ms = sum(s.elapsed_time(e) for s, e in zip(starts, ends))
-    # the device path reports kernel errors through its error word on sync
-    model.encode_pcm_device(d_pcm.data_ptr(), n, d_out.data_ptr(), stream=stream.cuda_stream, sync=True)
-
-    # ---- per-kernel classes (a separate profiled pass of the same steps)
-    model.profile_enable(True)
-    for _ in range(max(1, min(args.steps, 5))):
-        step()
-    torch.cuda.synchronize(dev)
-    stats = model.profile_read()
-    model.profile_enable(False)
-    prof_steps = max(1, min(args.steps, 5))
-
-    # ---- e2e: public host-buffer API, pinned PCM in, output to host
-    pinned = [torch.from_numpy(p).pin_memory() for p in pcm]
-    host_pcm = [t.numpy() for t in pinned]
-    host_out_bytes = out_floats * 4
-    # page-locked output buffer, reused every step (as the PCM input is)
-    host_out = torch.empty(model.out_floats(n), dtype=torch.float32).pin_memory().numpy()
-    for _ in range(max(1, args.warmup)):
-        model.encode_pcm_batch(host_pcm, layout=pkc.LAYOUT_TIME_MAJOR, out=host_out)
-    lib_stream = torch.cuda.ExternalStream(model.stream(), device=dev)
-    e_start = torch.cuda.Event(enable_timing=True)
-    e_end = torch.cuda.Event(enable_timing=True)
-    if world > 1:
-        dist.barrier()
-    torch.cuda.synchronize(dev)
-    t0 = time.perf_counter()
-    e_start.record(lib_stream)
-    for _ in range(args.steps):
-        model.encode_pcm_batch(host_pcm, layout=pkc.LAYOUT_TIME_MAJOR, out=host_out)
-    e_end.record(lib_stream)
-    torch.cuda.synchronize(dev)
-    e2e_wall = time.perf_counter() - t0
-    e2e_ms = e_start.elapsed_time(e_end)
+        r = measure_encoder(model, pcm, dev, args.steps, args.warmup, world)
+    stats, prof_steps = r["stats"], max(1, r["prof_steps"])
+    host_pcm = r.get("host_pcm", [])
 
     # ---- greedy transducer transcription (TDT / RNN-T models): PCM -> tokens
-    # through pkc_transducer_greedy_pcm_batch, everything on the GPU
+    # through pkc_transducer_greedy_pcm_batch, everything on the GPU (rank 0's share)
     trd = None
-    if model.transducer_kind() > 0:
+    if model.transducer_kind() > 0 and host_pcm and rank == 0:
         for _ in range(max(1, args.warmup)):
             model.transducer_greedy_pcm_batch(host_pcm)
+        lib_stream = torch.cuda.ExternalStream(model.stream(), device=dev)
         t_start = torch.cuda.Event(enable_timing=True)
         t_end = torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize(dev)
@@ -268,20 +323,20 @@ def run_ours(args, rank, world, local_rank):
         tst = {s["name"]: s["total_ms"] for s in model.profile_read()}
         model.profile_enable(False)
         trd = {"metric": "greedy " + ("TDT" if model.transducer_kind() == 2 else "RNN-T") +
-                         " transcription RTFx (PCM -> tokens, encoder and decode on the GPU)",
-               "value": round(audio_s / (trd_ms / 1e3), 1), "unit": UNIT, "ms_per_step": round(trd_ms, 3),
+                         " transcription RTFx (PCM -> tokens, encoder and decode on the GPU; rank 0's share)",
+               "value": round(r["audio_s"] / (trd_ms / 1e3), 1), "unit": UNIT, "ms_per_step": round(trd_ms, 3),
                "decode_ms": round(tst.get("transducer_decode", 0.0), 3),
                "joint_enc_gemm_ms": round(tst.get("gemm_joint_enc", 0.0), 4),
                "tokens_per_step": sum(len(t) for t in toks),
                "api": "pkc_transducer_greedy_pcm_batch (host buffers)"}
 
-    # ---- CTC transcription (models with a CTC head: the hybrid C1 / C4 and
-    # CTC models): PCM -> tokens through pkc_ctc_greedy_pcm_batch, host
-    # buffers, the head's kernels profiled beside it
+    # ---- CTC transcription (hybrid / CTC models): PCM -> tokens through
+    # pkc_ctc_greedy_pcm_batch, host buffers (rank 0's share)
     ctc = None
-    if model.ctc_classes() > 0:
+    if model.ctc_classes() > 0 and host_pcm and rank == 0:
         for _ in range(max(1, args.warmup)):
             model.ctc_greedy_pcm_batch(host_pcm)
+        lib_stream = torch.cuda.ExternalStream(model.stream(), device=dev)
         c_start = torch.cuda.Event(enable_timing=True)
         c_end = torch.cuda.Event(enable_timing=True)
         torch.cuda.synchronize(dev)
@@ -296,83 +351,205 @@ def run_ours(args, rank, world, local_rank):
         torch.cuda.synchronize(dev)
         cst = [s for s in model.profile_read() if s["name"].startswith(("ctc_", "gemm_ctc"))]
         model.profile_enable(False)
-        ctc = {"metric": "CTC transcription RTFx (PCM -> tokens: encoder + CTC head on the GPU, greedy fold on the host)",
-               "value": round(audio_s / (ctc_ms / 1e3), 1), "unit": UNIT, "ms_per_step": round(ctc_ms, 3),
+        ctc = {"metric": "CTC transcription RTFx (PCM -> tokens: encoder + CTC head on the GPU, greedy fold on "
+                         "the host; rank 0's share)",
+               "value": round(r["audio_s"] / (ctc_ms / 1e3), 1), "unit": UNIT, "ms_per_step": round(ctc_ms, 3),
                "classes": model.ctc_classes(), "api": "pkc_ctc_greedy_pcm_batch (host buffers)",
                "head_kernels": [{"name": s["name"], "ms": round(s["total_ms"], 4),
                                  **({"tflops": round(s["flops"] / (s["total_ms"] / 1e3) / 1e12, 1)} if s["flops"] > 0 else
                                     {"gbs": round(s["bytes"] / (s["total_ms"] / 1e3) / 1e9, 1)})} for s in cst]}
-
-    ms_max, e2e_max, audio_total, wall_max = combine_ranks(ms, e2e_ms, audio_s, e2e_wall * 1e3, world, dev)
     model.close()
+
+    ms_max, e2e_max, _, wall_max = combine_ranks(r["ms"], r["e2e_ms"], r["audio_s"], r["e2e_wall_ms"], world, dev)
+    audio_total = sum(len(p) for p in pcm_all) / SR
+
+    # ---- the q8_0 model of configuration 3 on the same global batch
+    c3 = None
+    if args.config == DEFAULT_CONFIG and not args.no_q8:
+        c3 = measure_other("c3_0.6b_q8", pcm_all, mine, dev, args, rank, world)
+
+    # ---- in-process multi-device path (pkc_model_open with all N devices,
+    # pkc_encode_pcm_batch sharding the global batch across them): rank 0
+    # alone, the other ranks waiting on a host-side barrier
+    multi = None
+    if world > 1 and not args.no_multi:
+        multi = measure_multi_device(path, pcm_all, world, rank, args)
+
     if rank != 0:
         return None
-
     value = audio_total * args.steps / (ms_max / 1e3)
     peaks, peak_src = load_peaks()
+    peak = peaks.get("bf16_tflops")
+    peak_sus = peaks.get("bf16_tflops_sustained")
+    hbm = peaks["hbm_gbs"]
+    kernels = kernel_table(stats, prof_steps, peak, hbm)
+    # roofline: the dominant kernel class (largest share of the profiled step)
     gemm = [s for s in stats if s["name"].startswith("gemm_")]
+    dom = max(gemm, key=lambda s: s["total_ms"]) if gemm else None
+    achieved = dom["flops"] / (dom["total_ms"] / 1e3) / 1e12 if dom else 0.0
     g_ms = sum(s["total_ms"] for s in gemm)
     g_fl = sum(s["flops"] for s in gemm)
-    g_n = sum(s["launches"] for s in gemm)
-    achieved = g_fl / (g_ms / 1e3) / 1e12 if g_ms > 0 else 0.0
-    peak = peaks.get("bf16_tflops_sustained", peaks.get("bf16_tflops"))
-    traffic = profile_traffic(args.config)
     launches_per_step = sum(s["launches"] for s in stats) / prof_steps
-    kernels = []
-    tot_ms = sum(s["total_ms"] for s in stats) or 1.0
-    for s in sorted(stats, key=lambda s: -s["total_ms"]):
-        k = {"name": s["name"], "launches_per_step": s["launches"] / prof_steps,
-             "ms_per_step": round(s["total_ms"] / prof_steps, 4), "share": round(s["total_ms"] / tot_ms, 4)}
-        if s["flops"] > 0 and s["name"].startswith(("gemm", "attention")):
-            k["tflops"] = round(s["flops"] / (s["total_ms"] / 1e3) / 1e12, 1)
-            k["frac_tensor_peak"] = round(k["tflops"] / peak, 3)
-        elif s["bytes"] > 0:
-            k["gbs"] = round(s["bytes"] / (s["total_ms"] / 1e3) / 1e9, 1)
-            k["frac_hbm_peak"] = round(k["gbs"] / peaks["hbm_gbs"], 3)
-        kernels.append(k)
+    step_flops = sum(s["flops"] for s in stats) / prof_steps
     line = {
         "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 3),
-        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f16" if not "bf16" in args.config else "bf16",
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
+        "dtype": "f16" if "bf16" not in args.config else "bf16",
         "data": "synthetic (seeded sines + noise; random-init weights, BASELINE.json init)",
-        "config": {"workload": f"{args.config}: {synth.CONFIGS[args.config].n_layers}-layer d{d} FastConformer encoder "
-                               f"({synth.CONFIGS[args.config].dtype} weights), PCM -> encoder output, "
-                               f"batch {winfo['batch']} clips of U({winfo['len_s'][0]},{winfo['len_s'][1]}) s per GPU",
-                   "audio_s_per_step_per_gpu": round(audio_s, 2), "parallelism": f"utterance-sharded dp{world}",
+        "config": {"workload": f"{args.config}: {cfg.n_layers}-layer d{d} FastConformer encoder "
+                               f"({cfg.dtype} weights), PCM -> encoder output, global batch {winfo['batch']} clips "
+                               f"of U({winfo['len_s'][0]},{winfo['len_s'][1]}) s sharded by utterance over "
+                               f"{world} GPU(s)",
+                   "global_batch": winfo["batch"], "audio_s_per_step": round(audio_total, 2),
+                   "clips_on_rank0": len(pcm), "parallelism": f"utterance-sharded dp{world} (LPT, pkc_shard_plan)",
                    "l2": "256 MiB written between timed steps (L2 flush); per-step working set > 1 GB"},
         "e2e": {"value": round(audio_total * args.steps / (e2e_max / 1e3), 1), "unit": UNIT,
-                "h2d_bytes_per_step": int(sum(n) * 4), "d2h_bytes_per_step": int(host_out_bytes),
+                "h2d_bytes_per_step": r["h2d"], "d2h_bytes_per_step": r["d2h"],
                 "api": "pkc_encode_pcm_batch (host buffers: pinned PCM in, pinned output buffer reused per step)",
-                "wall_value": round(audio_total * args.steps / (wall_max / 1e3), 1)},
+                "wall_value": round(audio_total * args.steps / (wall_max / 1e3), 1),
+                "note": "h2d / d2h bytes are rank 0's share"},
         "gpu_launches": int(round(launches_per_step * args.steps)),
-        "roofline": {"bound": "tensor", "kernel": "k_gemm_tc (tcgen05 GEMM, all encoder projections)",
+        "roofline": {"bound": "tensor", "kernel": f"{dom['name'] if dom else '-'} (tcgen05 GEMM class with the "
+                                                  "largest share of the step)",
                      "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
-                     "frac": round(achieved / peak, 3) if peak else None, "traffic": traffic,
-                     "launches_per_step": g_n / prof_steps,
-                     "peak_source": f"{peak_src} bf16_tflops_sustained (dense f16/bf16 tensor peak)"},
+                     "frac": round(achieved / peak, 3) if peak else None,
+                     "frac_of_sustained": round(achieved / peak_sus, 3) if peak_sus else None,
+                     "traffic": profile_traffic(args.config),
+                     "launches_per_step": (dom["launches"] / prof_steps) if dom else 0,
+                     "all_gemm_tflops": round(g_fl / (g_ms / 1e3) / 1e12, 1) if g_ms else None,
+                     "step_tflops": round(step_flops / (ms_max / args.steps / 1e3) / 1e12, 1) if world == 1 else None,
+                     "peak_source": f"{peak_src} bf16_tflops (burst dense f16/bf16 tensor peak); "
+                                    f"frac_of_sustained against bf16_tflops_sustained"},
         "kernels": kernels,
         "clocks": clk.summary(),
     }
     line["load"] = load
+    if c3 is not None:
+        line["c3_q8"] = c3
+    if multi is not None:
+        line["multi_device_in_process"] = multi
     if ctc is not None:
         line["ctc"] = ctc
     if trd is not None:
         line["transducer"] = trd
     if not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_baseline(args, path, pcm)
+        line["cpu_baseline"] = cpu_baseline(args, path, pcm_all)
     return line
+
+
+def measure_other(config, pcm_all, mine, dev, args, rank, world):
+    """Device-resident and e2e throughput of another model on the same global
+    batch and shard (the configuration-3 q8_0 weights)."""
+    import torch.distributed as dist
+    import pkc
+    import synth
+    if rank == 0 or world == 1:
+        synth.ensure_gguf(synth.CONFIGS[config])
+    if world > 1:
+        dist.barrier()
+    path = synth.ensure_gguf(synth.CONFIGS[config])
+    model = pkc.Model(path, devices=(dev.index,))
+    pcm = [pcm_all[i] for i in mine]
+    r = measure_encoder(model, pcm, dev, args.steps, args.warmup, world, profile=(rank == 0))
+    model.close()
+    ms_max, e2e_max, _, _ = combine_ranks(r["ms"], r["e2e_ms"], r["audio_s"], r["e2e_wall_ms"], world, dev)
+    audio_total = sum(len(p) for p in pcm_all) / SR
+    if rank != 0:
+        return None
+    peaks, _ = load_peaks()
+    cfg = synth.CONFIGS[config]
+    prof_steps = max(1, r["prof_steps"])
+    gemm = [s for s in r["stats"] if s["name"].startswith("gemm_")]
+    g_ms = sum(s["total_ms"] for s in gemm)
+    return {"workload": f"{config}: {cfg.n_layers}-layer d{cfg.d_model}, {cfg.dtype} weights dequantised inside "
+                        f"the GEMM, the same global batch and shard",
+            "value": round(audio_total * args.steps / (ms_max / 1e3), 1), "unit": UNIT,
+            "ms_per_step": round(ms_max / args.steps, 3),
+            "e2e": {"value": round(audio_total * args.steps / (e2e_max / 1e3), 1), "unit": UNIT,
+                    "api": "pkc_encode_pcm_batch (host buffers)"},
+            "all_gemm_tflops": round(sum(s["flops"] for s in gemm) / (g_ms / 1e3) / 1e12, 1) if g_ms else None,
+            "kernels": kernel_table(r["stats"], prof_steps, peaks.get("bf16_tflops"), peaks["hbm_gbs"])[:8]}
+
+
+def measure_multi_device(path, pcm_all, world, rank, args):
+    """Rank 0 opens the model on all `world` GPUs in one process and encodes
+    the global batch through pkc_encode_pcm_batch (LPT over the devices, one
+    host thread per device); the other ranks have closed their models and
+    wait on a gloo barrier (host-side, so their GPUs stay idle). Time: CUDA
+    events on every device's library stream, the max over devices."""
+    import torch
+    import torch.distributed as dist
+    import pkc
+    g = dist.new_group(backend="gloo")
+    out = None
+    if rank == 0:
+        model = pkc.Model(path, devices=tuple(range(world)))
+        try:
+            host_pcm = [torch.from_numpy(p).pin_memory().numpy() for p in pcm_all]
+            host_out = torch.empty(model.out_floats([len(p) for p in pcm_all]),
+                                   dtype=torch.float32).pin_memory().numpy()
+            for _ in range(max(1, args.warmup)):
+                model.encode_pcm_batch(host_pcm, layout=pkc.LAYOUT_TIME_MAJOR, out=host_out)
+            evs = []
+            for k in range(world):
+                s = torch.cuda.ExternalStream(model.stream(k), device=torch.device("cuda", k))
+                a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                evs.append((s, a, b))
+            for k in range(world):
+                torch.cuda.synchronize(k)
+            t0 = time.perf_counter()
+            for s, a, _ in evs:
+                a.record(s)
+            for _ in range(args.steps):
+                model.encode_pcm_batch(host_pcm, layout=pkc.LAYOUT_TIME_MAJOR, out=host_out)
+            for s, _, b in evs:
+                b.record(s)
+            for k in range(world):
+                torch.cuda.synchronize(k)
+            wall = time.perf_counter() - t0
+            ms = max(a.elapsed_time(b) for _, a, b in evs)
+        finally:
+            model.close()
+        audio = sum(len(p) for p in pcm_all) / SR
+        out = {"value": round(audio * args.steps / (ms / 1e3), 1), "unit": UNIT, "devices": world,
+               "ms_per_step": round(ms / args.steps, 3), "wall_value": round(audio * args.steps / wall, 1),
+               "api": "pkc_model_open(path, [0..N-1]) + pkc_encode_pcm_batch (host buffers, in-process LPT "
+                      "sharding, one host thread per device)",
+               "timing": "CUDA events on each device's library stream, max over devices"}
+    dist.barrier(group=g)
+    return out
 
 
 # ----------------------------------------------------------------------- CPU
 
-def cpu_sample(pcm_all, budget_s=2.0):
-    """A bounded slice of the workload: the shortest clip of the batch, cut to
-    at most budget_s seconds."""
-    c = min(pcm_all, key=len)
-    return [c[: int(budget_s * SR)]]
+def cpu_sample(pcm_all, k=4):
+    """A bounded sample of the workload that keeps its length mix: k clips of
+    the batch at evenly spaced length quantiles (for U(2, 35) s clips about
+    1/8, 3/8, 5/8 and 7/8 of the way through the sorted lengths)."""
+    order = sorted(range(len(pcm_all)), key=lambda i: len(pcm_all[i]))
+    n = len(order)
+    picks = sorted({order[min(n - 1, int((2 * q + 1) * n / (2 * k)))] for q in range(k)})
+    return [pcm_all[i] for i in picks]
+
+
+def cpu_threads():
+    """BLAS threads numpy uses (all host cores unless limited)."""
+    try:
+        import threadpoolctl
+        info = threadpoolctl.threadpool_info()
+        n = max((d.get("num_threads", 0) for d in info if d.get("user_api") == "blas"), default=0)
+        if n:
+            return n
+    except Exception:
+        pass
+    return os.cpu_count()
 
 
 def cpu_encode(w, clip):
+    """The reference's CPU path on one clip: parakeet.cpp's own MelFrontend
+    (compiled from its sources, oracle/_ref) when present, then the encoder
+    restatement in float32 with every BLAS thread."""
     import numpy as np
     import oracle
     import ref
@@ -383,26 +560,35 @@ def cpu_encode(w, clip):
                         fb=w.fb())
     else:
         feats = oracle.mel_frontend(w, clip)
-    return oracle.encoder_forward_batch(w, feats[None], [feats.shape[1]])
+    with oracle.compute_dtype(np.float32):
+        return oracle.encoder_forward_batch(w, feats[None], [feats.shape[1]])
 
 
-def cpu_baseline(args, path, pcm):
+def cpu_sample_desc(sample, reps):
+    secs = [round(len(c) / SR, 1) for c in sample]
+    return (f"{reps} pass(es) over {len(sample)} clips of the batch at its length quantiles ({secs} s); "
+            f"encoder = numpy float32 restatement of the reference's graph ({cpu_threads()} BLAS threads; the "
+            f"reference's ggml CPU default is {REF_DEFAULT_THREADS} threads), mel = parakeet.cpp MelFrontend "
+            f"(oracle/_ref); parakeet.cpp's ggml encoder itself is not buildable here (ggml absent)")
+
+
+def cpu_baseline(args, path, pcm_all):
     import oracle
     w = oracle.Weights(path)
-    sample = cpu_sample(pcm)
+    sample = cpu_sample(pcm_all)
     audio = sum(len(c) for c in sample) / SR
     cpu_encode(w, sample[0])  # warm
     t0 = time.perf_counter()
     reps = 0
     while True:
-        cpu_encode(w, sample[0])
+        for c in sample:
+            cpu_encode(w, c)
         reps += 1
         if time.perf_counter() - t0 > 10.0 or reps >= 3:
             break
     dt = (time.perf_counter() - t0) / reps
-    return {"value": round(audio / dt, 3), "unit": UNIT, "cores": os.cpu_count(), "kind": "port",
-            "sample": f"1 clip of {audio:.2f} s (shortest of the batch) through the full model; "
-                      f"encoder = numpy float64 restatement, mel = parakeet.cpp MelFrontend (oracle/_ref)"}
+    return {"value": round(audio / dt, 3), "unit": UNIT, "cores": cpu_threads(), "kind": "port",
+            "sample": cpu_sample_desc(sample, reps)}
 
 
 # ----------------------------------------------------------------- streaming
@@ -608,6 +794,9 @@ def run_reference_stream(args):
 
 
 def run_reference(args, rank, world):
+    """The reference arm: parakeet.cpp's CPU path on the host cores (rank 0
+    alone; other ranks exit without work). Each step encodes the next clip of
+    the length-quantile sample of the same global batch."""
     if rank != 0:
         return None
     import oracle
@@ -616,27 +805,29 @@ def run_reference(args, rank, world):
         return run_reference_stream(args)
     cfg = synth.CONFIGS[args.config]
     path = synth.ensure_gguf(cfg)
-    pcm, winfo = workload(args.config, 0, args.batch)
+    pcm_all, winfo = workload(args.config, args.batch)
     w = oracle.Weights(path)
-    sample = cpu_sample(pcm)
-    audio = sum(len(c) for c in sample) / SR
-    for _ in range(args.warmup):
-        cpu_encode(w, sample[0])
+    sample = cpu_sample(pcm_all)
+    for k in range(args.warmup):
+        cpu_encode(w, sample[k % len(sample)])
+    audio = 0.0
     t0 = time.perf_counter()
-    for _ in range(args.steps):
-        cpu_encode(w, sample[0])
+    for k in range(args.steps):
+        c = sample[k % len(sample)]
+        cpu_encode(w, c)
+        audio += len(c) / SR
     dt = time.perf_counter() - t0
-    v = audio * args.steps / dt
-    cores = os.cpu_count()
+    v = audio / dt
+    desc = cpu_sample_desc(sample, 1).replace("1 pass(es) over", f"{args.steps} steps cycling through")
     return {"metric": METRIC, "value": round(v, 3), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(dt / args.steps * 1e3, 1), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f64", "impl": "reference",
-            "data": "synthetic", "config": {"workload": f"{args.config} (bounded CPU sample)",
-                                             "sample": f"1 clip of {audio:.2f} s per step"},
-            "cpu_baseline": {"value": round(v, 3), "unit": UNIT, "cores": cores, "kind": "port",
-                             "sample": f"1 clip of {audio:.2f} s per step; parakeet.cpp's ggml encoder is not "
-                                       "buildable here (ggml absent), so the encoder is the numpy float64 "
-                                       "restatement and the mel front end parakeet.cpp's own MelFrontend"},
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "impl": "reference",
+            "data": "synthetic",
+            "config": {"workload": f"{args.config}: global batch {winfo['batch']} clips of "
+                                   f"U({winfo['len_s'][0]},{winfo['len_s'][1]}) s (bounded CPU sample: one clip per step)",
+                       "sample": desc},
+            "cpu_baseline": {"value": round(v, 3), "unit": UNIT, "cores": cpu_threads(), "kind": "port",
+                             "sample": desc},
             "e2e": {"value": round(v, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
 
 
@@ -649,6 +840,8 @@ def main():
     ap.add_argument("--config", default=DEFAULT_CONFIG)
     ap.add_argument("--batch", type=int, default=None)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-q8", action="store_true", help="skip the configuration-3 q8_0 measurement")
+    ap.add_argument("--no-multi", action="store_true", help="skip the in-process multi-device measurement")
     ap.add_argument("--stream-seconds", type=float, default=20.0,
                     help="audio per stream for the streaming configurations")
     ap.add_argument("--stream-batch", type=int, default=32,
