@@ -112,14 +112,14 @@ def _run_full(cfg_name, pcm, tol, decode):
         m.close()
     w = oracle.Weights(path)
     ref = oracle.encode_pcm_batch(w, pcm)
-    errs = [max_rel_err(x, r.T) for x, r in zip(xs, ref.outs)]
+    errs = [max_rel_err(x, r) for x, r in zip(xs, ref.outs)]  # both time-major [T', d]
     print(f"{cfg_name}: encoder per-element max rel err {[f'{e:.2e}' for e in errs]}")
     assert max(errs) <= tol, errs
     if toks is not None:
         tr = oracle.Transducer(w)
         for b, (x, r) in enumerate(zip(xs, ref.outs)):
             T = min(x.shape[0], decode["transducer"])
-            x_ref = r.T[:T]
+            x_ref = r[:T]
             # tokens of frames < T (greedy decoding is causal over frames)
             gtk = [t for t in toks[b] if t[1] < T]
             n_safe, n_all, tau, delta = _transducer_prefix(tr, x_ref, x[:T], gtk)
@@ -128,7 +128,7 @@ def _run_full(cfg_name, pcm, tol, decode):
     if ctc is not None:
         tks, lps = ctc
         for b, (lp, r) in enumerate(zip(lps, ref.outs)):
-            n_safe, n_all, tau, delta = _ctc_frames(lp, oracle.ctc_log_probs(w, r.T))
+            n_safe, n_all, tau, delta = _ctc_frames(lp, oracle.ctc_log_probs(w, r))
             print(f"{cfg_name} clip {b}: CTC argmax identical on {n_safe} of {n_all} frames "
                   f"(margin > tau {tau:.2e}; log-prob deviation {delta:.2e})")
     return errs
