@@ -188,7 +188,12 @@ pkc_status pkc_encode_batch(pkc_model* m, const float* mel, int B, int n_mels, i
                             int* valid_Tout, int* d_model_out);
 
 /* PCM -> encoder output in one call (mel front end + encoder), host buffers.
-   With several devices the clips are sharded across them by length. */
+   With several devices the clips are sharded across them by length (one host
+   thread per device, each copying its clips' outputs straight into `out`); a
+   device's failure returns that device's status and message. Failure
+   injection for tests: the environment variable PKC_FAULT_DEVICE_SLOT=k makes
+   the worker of device slot k fail on the host before it touches its device
+   (PKC_ERR_INTERNAL). */
 pkc_status pkc_encode_pcm_batch(pkc_model* m, const float* const* pcm, const int* n_samples,
                                 int B, int layout, float* out, size_t out_cap, int* valid_Tout);
 
@@ -334,6 +339,17 @@ pkc_status pkc_gemm_split(const void* A, int lda, const void* Bw, int ldb, int M
 pkc_status pkc_relpos_attention(const void* qkv, const void* ptab, int centre,
                                 const float* bias_u, const float* bias_v, const int* lens, int B,
                                 int d, int n_heads, int dtype, void* ctx, void* stream);
+
+/* Failure detection check: runs this library's bounded-wait helpers (every
+   mbarrier wait and cross-CTA flag wait of its kernels uses them) on a
+   condition that never comes true -- kind 0: an mbarrier no thread arrives
+   on, kind 1: a global flag no thread sets -- with a limit of limit_ms
+   (0 < limit_ms <= 2000; the kernels' own limit is 2000 ms). The wait runs
+   out, records its code in the device error word (*error_code, 108) and the
+   kernel returns: PKC_ERR_KERNEL, with the CUDA context still usable. No
+   counterpart in the reference (its failures are host status codes only,
+   src/parakeet_capi.cpp:207-294). */
+pkc_status pkc_bounded_wait_check(int kind, double limit_ms, int* error_code);
 
 /* The attention of the f32-accurate path: qkv f32 [M, 3d], ptab f32
    [2*centre-1, d], everything in f32 (softmax with expf); ctx receives f16

@@ -3,6 +3,7 @@
 #include <algorithm>
 #include <cstdlib>
 #include <cstring>
+#include <stdexcept>
 #include <cmath>
 #include <memory>
 #include <mutex>
@@ -44,6 +45,16 @@ pkc_status fail(pkc_model* m, pkc_status st, const std::string& msg) {
 // Encoder frames (T') of a clip, and the sharding cost T'(1 + T'/8192):
 // linear work per frame plus the attention's quadratic term.
 double clip_cost(int v) { return (double)v * (1.0 + (double)v / 8192.0); }
+
+// Host-side failure injection for the failure-detection tests: when the
+// environment variable PKC_FAULT_DEVICE_SLOT names device slot k, the
+// multi-device dispatcher's worker for slot k throws before it touches its
+// device (a failed worker, made on the host: no GPU is faulted). Read on
+// every call so a test can switch it on and off.
+bool fault_injected(int slot) {
+  const char* e = std::getenv("PKC_FAULT_DEVICE_SLOT");
+  return e && e[0] && std::atoi(e) == slot;
+}
 
 void lpt_assign(const std::vector<double>& cost, int n_dev, std::vector<int>& assign) {
   const int B = (int)cost.size();
@@ -604,7 +615,8 @@ pkc_status pkc_encode_pcm_batch(pkc_model* m, const float* const* pcm, const int
     lpt_assign(cost, nd, assign);
     std::vector<std::vector<int>> items(nd);
     for (int b = 0; b < B; ++b) items[assign[b]].push_back(b);
-    std::vector<std::vector<float>> bufs(nd);
+    // each device copies its clips' outputs straight to their places in
+    // `out` (one device-to-host copy per clip, no intermediate host buffer)
     std::vector<pkc_status> st(nd, PKC_OK);
     std::vector<std::string> errs(nd);
     std::vector<std::thread> th;
@@ -612,12 +624,16 @@ pkc_status pkc_encode_pcm_batch(pkc_model* m, const float* const* pcm, const int
       if (items[k].empty()) continue;
       th.emplace_back([&, k] {
         try {
+          if (fault_injected(k)) throw std::runtime_error("injected host fault (PKC_FAULT_DEVICE_SLOT)");
           std::vector<const float*> p;
           std::vector<int> n;
-          size_t tot = 0;
-          for (int b : items[k]) { p.push_back(pcm[b]); n.push_back(n_samples[b]); tot += off[b + 1] - off[b]; }
-          bufs[k].resize(tot);
-          st[k] = m->runners[k]->encode_pcm_host(p, n, layout, bufs[k].data(), errs[k]);
+          std::vector<float*> dst;
+          for (int b : items[k]) {
+            p.push_back(pcm[b]);
+            n.push_back(n_samples[b]);
+            dst.push_back(out + off[b]);
+          }
+          st[k] = m->runners[k]->encode_pcm_host_items(p, n, layout, dst, errs[k]);
         } catch (const std::exception& e) {
           st[k] = PKC_ERR_INTERNAL;
           errs[k] = e.what();
@@ -627,14 +643,6 @@ pkc_status pkc_encode_pcm_batch(pkc_model* m, const float* const* pcm, const int
     for (auto& t : th) t.join();
     for (int k = 0; k < nd; ++k)
       if (st[k] != PKC_OK) return fail(m, st[k], "device " + std::to_string(m->runners[k]->device()) + ": " + errs[k]);
-    for (int k = 0; k < nd; ++k) {
-      size_t pos = 0;
-      for (int b : items[k]) {
-        const size_t n = off[b + 1] - off[b];
-        std::memcpy(out + off[b], bufs[k].data() + pos, n * 4);
-        pos += n;
-      }
-    }
     return PKC_OK;
   } catch (const std::exception& e) {
     return fail(m, PKC_ERR_INTERNAL, e.what());

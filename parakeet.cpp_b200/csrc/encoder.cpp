@@ -876,6 +876,28 @@ pkc_status DeviceRunner::encode_pcm_host(const std::vector<const float*>& pcm,
   return finish(st, err);
 }
 
+pkc_status DeviceRunner::encode_pcm_host_items(const std::vector<const float*>& pcm, const std::vector<int>& n,
+                                               int layout, const std::vector<float*>& item_out, std::string& err) {
+  cudaSetDevice(device_);
+  Plan p;
+  make_plan(cfg_, n, {}, p);
+  cudaStream_t st = stream_;
+  PKC_ST(prepare(p, st, err));
+  for (int b = 0; b < p.B; ++b)
+    if (n[b] > 0)
+      PKC_CK(cudaMemcpyAsync(b_.pcm + p.pcm_off[b], pcm[b], (size_t)n[b] * 4, cudaMemcpyHostToDevice, st), "pcm upload");
+  const bool cf = layout == PKC_LAYOUT_CHANNELS_FIRST;
+  PKC_ST(run_graphed(p, st, cf, err));
+  const int d = cfg_.d_model;
+  const float* src = cf ? b_.out : b_.x;
+  // every clip's block is contiguous in either layout (rows v_off[b] ..)
+  for (int b = 0; b < p.B; ++b)
+    if (p.v[b] > 0)
+      PKC_CK(cudaMemcpyAsync(item_out[b], src + (size_t)p.v_off[b] * d, (size_t)p.v[b] * d * 4, cudaMemcpyDeviceToHost,
+                             st), "output download");
+  return finish(st, err);
+}
+
 pkc_status DeviceRunner::ensure_aux(size_t bytes, cudaStream_t st, std::string& err) {
   if (bytes <= ctc_ws_bytes_) return PKC_OK;
   cudaStreamSynchronize(st);

@@ -64,6 +64,11 @@ class DeviceRunner {
   // x_out (device, may be the workspace) - see encode_* helpers.
   pkc_status encode_pcm_host(const std::vector<const float*>& pcm, const std::vector<int>& n,
                              int layout, float* host_out, std::string& err);
+  // The same with one host destination per clip (the clip's frames copied
+  // there by their own device-to-host copy): the multi-device dispatcher's
+  // form, which writes each device's clips straight into the caller's buffer.
+  pkc_status encode_pcm_host_items(const std::vector<const float*>& pcm, const std::vector<int>& n, int layout,
+                                   const std::vector<float*>& item_out, std::string& err);
   pkc_status encode_pcm_device(const float* d_pcm, const std::vector<int>& n, float* d_out,
                                cudaStream_t st, bool sync, std::string& err);
   pkc_status encode_mel_host(const float* mel, int B, int n_mels, int T_max, const int* valid_T,

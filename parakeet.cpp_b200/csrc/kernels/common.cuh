@@ -20,6 +20,7 @@ enum DevErr : int {
   DEV_ERR_TIMEOUT_ATTN = 104,   // attention pipeline wait ran out
   DEV_ERR_TIMEOUT_SPLITK = 105, // a split tile's finisher waited too long for a partial sum
   DEV_ERR_TIMEOUT_DECODE = 106, // the transducer decode's grid barrier waited too long
+  DEV_ERR_TIMEOUT_CHECK = 108,  // the bounded-wait check kernel's wait ran out (as it is meant to)
   DEV_ERR_BAD_SHAPE = 110,
   DEV_ERR_NONFINITE = 111,      // a decode step found no finite maximum (NaN logits)
 };
@@ -91,11 +92,12 @@ __device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
 
 // Slow path of mbar_wait (kept out of line: the inlined loop made even an
 // already-completed wait cost several times the test itself).
-static __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, int* err, int code) {
+static __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity, int* err, int code,
+                                                   unsigned long long limit_ns = kWaitLimitNs) {
   const unsigned long long t0 = globaltimer_ns();
   for (uint32_t it = 1;; ++it) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 0u && globaltimer_ns() - t0 > kWaitLimitNs) {
+    if ((it & 255u) == 0u && globaltimer_ns() - t0 > limit_ns) {
       report_error(err, code);
       return false;
     }
@@ -103,21 +105,24 @@ static __device__ __noinline__ bool mbar_wait_slow(uint32_t bar, uint32_t parity
 }
 
 // Wait until the phase with the given parity has completed. Returns false (and
-// records `code` in *err) if that does not happen within kWaitLimitNs.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err, int code) {
-  return mbar_test_wait(bar, parity) || mbar_wait_slow(bar, parity, err, code);
+// records `code` in *err) if that does not happen within limit_ns (every
+// kernel's waits use kWaitLimitNs; the bounded-wait check passes a short one).
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int* err, int code,
+                                          unsigned long long limit_ns = kWaitLimitNs) {
+  return mbar_test_wait(bar, parity) || mbar_wait_slow(bar, parity, err, code, limit_ns);
 }
 
 // Flag in global memory set by another CTA of the same grid (st_release_gpu
 // after its data). Spins until *f != 0; false (and `code` in *err) after
 // kWaitLimitNs.
-static __device__ __noinline__ bool wait_flag_gpu(const int* f, int* err, int code) {
+static __device__ __noinline__ bool wait_flag_gpu(const int* f, int* err, int code,
+                                                  unsigned long long limit_ns = kWaitLimitNs) {
   const unsigned long long t0 = globaltimer_ns();
   for (uint32_t it = 0;; ++it) {
     int v;
     asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
     if (v != 0) return true;
-    if ((it & 63u) == 63u && globaltimer_ns() - t0 > kWaitLimitNs) {
+    if ((it & 63u) == 63u && globaltimer_ns() - t0 > limit_ns) {
       report_error(err, code);
       return false;
     }

@@ -26,6 +26,8 @@ STATUS_NAMES = {
     4: "PKC_ERR_UNSUPPORTED", 5: "PKC_ERR_CUDA", 6: "PKC_ERR_OOM", 7: "PKC_ERR_KERNEL",
     8: "PKC_ERR_INTERNAL",
 }
+(PKC_ERR_ARG, PKC_ERR_IO, PKC_ERR_FORMAT, PKC_ERR_UNSUPPORTED, PKC_ERR_CUDA, PKC_ERR_OOM, PKC_ERR_KERNEL,
+ PKC_ERR_INTERNAL) = range(1, 9)
 LAYOUT_CHANNELS_FIRST = 0
 LAYOUT_TIME_MAJOR = 1
 
@@ -137,6 +139,7 @@ def _declare(L):
          c_float, c_void_p, c_void_p, c_int, c_int, c_int, c_void_p),
         ("pkc_relpos_attention_f32", c_int, c_void_p, c_void_p, c_int, c_void_p, c_void_p, POINTER(c_int),
          c_int, c_int, c_int, c_void_p, c_void_p),
+        ("pkc_bounded_wait_check", c_int, c_int, ctypes.c_double, POINTER(c_int)),
     ]
     for name, res, *args in optional:
         if hasattr(L, name):
@@ -179,6 +182,14 @@ def relpos_attention_f32(qkv, ptab, centre, bias_u, bias_v, lens, d, n_heads, *,
     _check(lib().pkc_relpos_attention_f32(c_void_p(qkv), c_void_p(ptab), centre, c_void_p(bias_u), c_void_p(bias_v),
                                           _ints(lens), len(lens), d, n_heads, c_void_p(ctx),
                                           c_void_p(stream) if stream else None))
+
+
+def bounded_wait_check(kind, limit_ms):
+    """pkc_bounded_wait_check: (status, device error code) of a bounded wait
+    on a condition that never comes true (kind 0 mbarrier, 1 global flag)."""
+    code = c_int(0)
+    st = lib().pkc_bounded_wait_check(kind, float(limit_ms), ctypes.byref(code))
+    return st, code.value
 
 
 def ctc_fold(argmax, max_logprob, n_classes, blank_id):
