@@ -233,6 +233,21 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t tro
   }
 }
 
+// Tile index -> row block (tile_mb) and column block (tile_nb). The tiles a
+// wave runs at the same time should share the larger operand, so that it
+// crosses HBM once while the smaller one stays in L2: column blocks fastest
+// when A has more rows than B (the encoder's GEMMs at batch size: the N / 256
+// tiles of a row block run together and read its A rows once; row blocks
+// fastest would stream all of A once per column block, which for the
+// K = 4096 FFN-down at M = 14k frames measured 3.6x its algorithmic bytes),
+// row blocks fastest otherwise.
+__device__ __forceinline__ int tile_mb(int tile, int tiles_m, int tiles_n, bool nfast) {
+  return nfast ? tile / tiles_n : tile % tiles_m;
+}
+__device__ __forceinline__ int tile_nb(int tile, int tiles_m, int tiles_n, bool nfast) {
+  return nfast ? tile % tiles_n : tile / tiles_m;
+}
+
 template <typename H, int EPI>
 __global__ void __launch_bounds__(THREADS, 1)
     k_gemm_tc(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -251,7 +266,9 @@ __global__ void __launch_bounds__(THREADS, 1)
   const int lane = threadIdx.x & 31;
   const int KB = args.K / BK;
   const int tiles_m = (args.M + BM - 1) / BM;
-  const int n_tiles = tiles_m * (args.N / BN);
+  const int tiles_n = args.N / BN;
+  const int n_tiles = tiles_m * tiles_n;
+  const bool nfast = args.M > args.N;
 
   if (threadIdx.x == 0) {
     prefetch_tmap(&tmA);
@@ -280,8 +297,8 @@ __global__ void __launch_bounds__(THREADS, 1)
       uint32_t it = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < n_tiles && ok; tile += gridDim.x) {
-        const int m0 = (tile % tiles_m) * BM;
-        const int n0 = (tile / tiles_m) * BN;
+        const int m0 = tile_mb(tile, tiles_m, tiles_n, nfast) * BM;
+        const int n0 = tile_nb(tile, tiles_m, tiles_n, nfast) * BN;
         for (int kb = 0; kb < KB; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1u;
@@ -345,8 +362,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                                             DEV_ERR_TIMEOUT_ACCUM) ? 1 : 0) != 0;
       if (!have) break;
       tc_fence_after();
-      const int m0 = (tile % tiles_m) * BM;
-      const int n0 = (tile / tiles_m) * BN;
+      const int m0 = tile_mb(tile, tiles_m, tiles_n, nfast) * BM;
+      const int n0 = tile_nb(tile, tiles_m, tiles_n, nfast) * BN;
       const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
       epilogue_tile<H, EPI>(args, trow, m0 + q * 32, n0, half, sE + (warp - 2) * EPI_STAGE_BYTES);
       tc_fence_before();
@@ -533,7 +550,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   const int npairs = gridDim.x >> 1;
   const int KB = args.K / BK;
   const int tiles_m = (args.M + 2 * HALF_ROWS - 1) / (2 * HALF_ROWS);
-  const int n_tiles = tiles_m * (args.N / BN);
+  const int tiles_n = args.N / BN;
+  const int n_tiles = tiles_m * tiles_n;
+  const bool nfast = args.M > args.N;
   // the stream-K instantiation (SK) falls back to whole tiles if W < P
   const bool sk = SK && (long long)n_tiles * KB >= npairs;
 
@@ -566,8 +585,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       SegIter sg(sk, pair, npairs, KB, n_tiles);
       int tile, kb0, kb1;
       while (ok && sg.next(tile, kb0, kb1)) {
-        const int m0 = (tile % tiles_m) * 2 * HALF_ROWS + (int)rank * HALF_ROWS;
-        const int n0 = (tile / tiles_m) * BN + (int)rank * HALF_ROWS;
+        const int m0 = tile_mb(tile, tiles_m, tiles_n, nfast) * 2 * HALF_ROWS + (int)rank * HALF_ROWS;
+        const int n0 = tile_nb(tile, tiles_m, tiles_n, nfast) * BN + (int)rank * HALF_ROWS;
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES2;
           const uint32_t ph = (it / STAGES2) & 1u;
@@ -639,8 +658,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                                             DEV_ERR_TIMEOUT_ACCUM) ? 1 : 0) != 0;
       if (!have) break;
       tc_fence_after();
-      const int m0 = (tile % tiles_m) * 2 * HALF_ROWS + (int)rank * HALF_ROWS;
-      const int n0 = (tile / tiles_m) * BN;
+      const int m0 = tile_mb(tile, tiles_m, tiles_n, nfast) * 2 * HALF_ROWS + (int)rank * HALF_ROWS;
+      const int n0 = tile_nb(tile, tiles_m, tiles_n, nfast) * BN;
       const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
       if (SK && kb0 > 0) {
         sk_spill<EPI>(args, trow, half, slot);  // partial sum of a split tile
@@ -787,7 +806,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
   const int npairs = gridDim.x >> 1;
   const int KB = args.K / BK;
   const int tiles_m = (args.M + 2 * HALF_ROWS - 1) / (2 * HALF_ROWS);
-  const int n_tiles = tiles_m * (args.N / BN);
+  const int tiles_n = args.N / BN;
+  const int n_tiles = tiles_m * tiles_n;
+  const bool nfast = args.M > args.N;
 
   if (threadIdx.x == 0) {
     prefetch_tmap(&tmA);
@@ -823,8 +844,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
       uint32_t it = 0;
       bool ok = true;
       for (int tile = pair; tile < n_tiles && ok; tile += npairs) {
-        const int m0 = (tile % tiles_m) * 2 * HALF_ROWS + (int)rank * HALF_ROWS;
-        const int n0 = (tile / tiles_m) * BN + (int)rank * HALF_ROWS;
+        const int m0 = tile_mb(tile, tiles_m, tiles_n, nfast) * 2 * HALF_ROWS + (int)rank * HALF_ROWS;
+        const int n0 = tile_nb(tile, tiles_m, tiles_n, nfast) * BN + (int)rank * HALF_ROWS;
         for (int kb = 0; kb < KB; ++kb, ++it) {
           const int s = it % S;
           const uint32_t ph = (it / S) & 1u;
@@ -892,8 +913,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
                                                           DEV_ERR_TIMEOUT_ACCUM) ? 1 : 0) != 0;
       if (!have) break;
       tc_fence_after();
-      const int m0 = (tile % tiles_m) * 2 * HALF_ROWS + (int)rank * HALF_ROWS;
-      const int n0 = (tile / tiles_m) * BN;
+      const int m0 = tile_mb(tile, tiles_m, tiles_n, nfast) * 2 * HALF_ROWS + (int)rank * HALF_ROWS;
+      const int n0 = tile_nb(tile, tiles_m, tiles_n, nfast) * BN;
       const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
       epilogue_tile<H, EPI>(args, trow, m0 + q * 32, n0, half, sE + (warp - 2) * EPI_STAGE_BYTES);
       tc_fence_before();
@@ -990,7 +1011,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
   const int npairs = gridDim.x >> 1;
   const int KB = args.K / BK;
   const int tiles_m = (args.M + 2 * HALF_ROWS - 1) / (2 * HALF_ROWS);
-  const int n_tiles = tiles_m * (args.N / BN);
+  const int tiles_n = args.N / BN;
+  const int n_tiles = tiles_m * tiles_n;
+  const bool nfast = args.M > args.N;
 
   if (threadIdx.x == 0) {
     prefetch_tmap(&tmX);
@@ -1026,8 +1049,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
       uint32_t it = 0;
       bool ok = true;
       for (int tile = pair; tile < n_tiles && ok; tile += npairs) {
-        const int m0 = (tile % tiles_m) * 2 * HALF_ROWS + (int)rank * HALF_ROWS;
-        const int n0 = (tile / tiles_m) * BN + (int)rank * HALF_ROWS;
+        const int m0 = tile_mb(tile, tiles_m, tiles_n, nfast) * 2 * HALF_ROWS + (int)rank * HALF_ROWS;
+        const int n0 = tile_nb(tile, tiles_m, tiles_n, nfast) * BN + (int)rank * HALF_ROWS;
         for (int kb = 0; kb < KB && ok; ++kb, ++it) {
           const int s = it % S;
           if (!mbar_wait(smem_u32(&bars[S + s]), ((it / S) & 1u) ^ 1u, args.err, DEV_ERR_TIMEOUT_EMPTY)) {
@@ -1096,8 +1119,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
                                                           DEV_ERR_TIMEOUT_ACCUM) ? 1 : 0) != 0;
       if (!have) break;
       tc_fence_after();
-      const int m0 = (tile % tiles_m) * 2 * HALF_ROWS + (int)rank * HALF_ROWS;
-      const int n0 = (tile / tiles_m) * BN;
+      const int m0 = tile_mb(tile, tiles_m, tiles_n, nfast) * 2 * HALF_ROWS + (int)rank * HALF_ROWS;
+      const int n0 = tile_nb(tile, tiles_m, tiles_n, nfast) * BN;
       const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
       epilogue_tile<H, EPI>(args, trow, m0 + q * 32, n0, half, sE + (warp - 2) * EPI_STAGE_BYTES);
       tc_fence_before();
@@ -1113,7 +1136,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
     for (int tile = pair; tile < n_tiles && ok; tile += npairs) {
       // mean / rstd of this row (ggml_norm: population variance, eps 1e-5),
       // merged from its equal-size 128-column partials
-      const int grow = (tile % tiles_m) * 2 * HALF_ROWS + (int)rank * HALF_ROWS + r;
+      const int grow = tile_mb(tile, tiles_m, tiles_n, nfast) * 2 * HALF_ROWS + (int)rank * HALF_ROWS + r;
       float mean = 0.f, rstd = 0.f;
       if (grow < args.M) {
         const float2* st2 = reinterpret_cast<const float2*>(lp.stats) + (size_t)grow * nchunk;
@@ -1141,7 +1164,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(512, 1)
       const float nmr = -mean * rstd;  // xhat = fma(x, rstd, nmr)
       // the next tile's row statistics into L1 while this tile streams
       {
-        const int nrow = ((tile + npairs) % tiles_m) * 2 * HALF_ROWS + (int)rank * HALF_ROWS + r;
+        const int nrow = tile_mb(tile + npairs, tiles_m, tiles_n, nfast) * 2 * HALF_ROWS + (int)rank * HALF_ROWS + r;
         if (tile + npairs < n_tiles && nrow < args.M) {
           const char* p = reinterpret_cast<const char*>(lp.stats + (size_t)nrow * nchunk * 2);
           for (int o = 0; o < nchunk * 8; o += 128) asm volatile("prefetch.global.L1 [%0];" ::"l"(p + o));
