@@ -133,6 +133,13 @@ DeviceRunner::~DeviceRunner() {
   }
   if (ev_fork_) cudaEventDestroy(ev_fork_);
   if (ev_join_) cudaEventDestroy(ev_join_);
+  for (cudaStream_t s : {cs_in_, cs_out_})
+    if (s) {
+      cudaStreamSynchronize(s);
+      cudaStreamDestroy(s);
+    }
+  for (cudaEvent_t e : {ev_in_[0], ev_in_[1], ev_out_[0], ev_out_[1], ev_prior_})
+    if (e) cudaEventDestroy(e);
   if (h_tables_) cudaFreeHost(h_tables_);
   free_weights(w_);
   if (stream_) cudaStreamDestroy(stream_);
@@ -166,6 +173,11 @@ std::string DeviceRunner::init(const PackedWeights& pw) {
       cudaEventCreateWithFlags(&ev_fork_, cudaEventDisableTiming) != cudaSuccess ||
       cudaEventCreateWithFlags(&ev_join_, cudaEventDisableTiming) != cudaSuccess)
     return "second stream / event creation failed";
+  if (cudaStreamCreateWithFlags(&cs_in_, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&cs_out_, cudaStreamNonBlocking) != cudaSuccess)
+    return "copy stream creation failed";
+  for (cudaEvent_t* e : {&ev_in_[0], &ev_in_[1], &ev_out_[0], &ev_out_[1], &ev_prior_})
+    if (cudaEventCreateWithFlags(e, cudaEventDisableTiming) != cudaSuccess) return "copy event creation failed";
   power_ld_ = cfg_.n_fft / 2 + 8;
   const char* ng = getenv("PKC_NO_GRAPH");
   use_graphs_ = !(ng && ng[0] == '1');
@@ -436,72 +448,101 @@ pkc_status DeviceRunner::prepare(const Plan& p, cudaStream_t st, std::string& er
   return PKC_OK;
 }
 
-pkc_status DeviceRunner::run_frontend(const Plan& p, cudaStream_t st, std::string& err) {
+ItemTables DeviceRunner::tables_of(int b0, int b1) const {
+  return ItemTables{b1 - b0,         t_pcm_off + b0, t_S + b0,  t_mel_off + b0, t_Tm + b0, t_mval + b0,
+                    t_v1_off + b0,   t_v1 + b0,      t_v2_off + b0, t_v2 + b0,  t_v_off + b0, t_v + b0};
+}
+
+pkc_status DeviceRunner::run_frontend(const Plan& p, int b0, int b1, cudaStream_t st, std::string& err) {
   const Config& c = cfg_;
-  ItemTables t{p.B, t_pcm_off, t_S, t_mel_off, t_Tm, t_mval, t_v1_off, t_v1, t_v2_off, t_v2, t_v_off, t_v};
-  MelArgs ma{b_.pcm, w_.window, c.n_fft, c.hop_length, c.preemph, p.total_frames,
-             reinterpret_cast<__half*>(b_.dft_a), b_.power, power_ld_};
+  const ItemTables t = tables_of(b0, b1);
+  const int f0 = p.mel_off[b0], nf = p.mel_off[b1] - f0;
+  const double samples = (double)(p.pcm_off[b1] - p.pcm_off[b0]);
+  __half* dft_a = reinterpret_cast<__half*>(b_.dft_a);
+  MelArgs ma{b_.pcm, w_.window, c.n_fft, c.hop_length, c.preemph, nf, dft_a, b_.power, power_ld_, f0};
   prof_begin(st);
   PKC_CK(mel_frames_launch(ma, t, st), "mel_frames");
-  prof_end(st, "mel_frames", 0.0, (double)p.total_samples * 4 * 3.2 + (double)p.total_frames * 3 * c.n_fft * 2);
-  PKC_ST(gemm(b_.dft_a, 3 * c.n_fft, w_.dft_basis, 3 * c.n_fft, false, p.total_frames, c.n_fft,
-              3 * c.n_fft, EPI_POWER_F32, ACT_NONE, 1.f, nullptr, b_.power, power_ld_, st, "gemm_dft", err));
-  FbArgs fa{b_.power, power_ld_, w_.fb_start, w_.fb_len, w_.fb_off, w_.fb_w, c.n_mels,
-            c.log_zero_guard, p.total_frames, b_.logmel};
+  prof_end(st, "mel_frames", 0.0, samples * 4 * 3.2 + (double)nf * 3 * c.n_fft * 2);
+  PKC_ST(gemm(dft_a + (size_t)f0 * 3 * c.n_fft, 3 * c.n_fft, w_.dft_basis, 3 * c.n_fft, false, nf, c.n_fft,
+              3 * c.n_fft, EPI_POWER_F32, ACT_NONE, 1.f, nullptr, b_.power + (size_t)f0 * power_ld_, power_ld_, st,
+              "gemm_dft", err));
+  FbArgs fa{b_.power + (size_t)f0 * power_ld_, power_ld_, w_.fb_start, w_.fb_len, w_.fb_off, w_.fb_w, c.n_mels,
+            c.log_zero_guard, nf, b_.logmel + (size_t)f0 * c.n_mels};
   prof_begin(st);
   PKC_CK(mel_fb_log_launch(fa, st), "mel_fb_log");
-  prof_end(st, "mel_fb_log", 0.0, (double)p.total_frames * (power_ld_ + c.n_mels) * 4);
+  prof_end(st, "mel_fb_log", 0.0, (double)nf * (power_ld_ + c.n_mels) * 4);
   prof_begin(st);
   PKC_CK(mel_norm_launch(b_.logmel, c.n_mels, t, st), "mel_norm");
-  prof_end(st, "mel_norm", 0.0, (double)p.total_frames * c.n_mels * 4 * 3);
+  prof_end(st, "mel_norm", 0.0, (double)nf * c.n_mels * 4 * 3);
   return PKC_OK;
 }
 
-pkc_status DeviceRunner::run_encoder(const Plan& p, cudaStream_t st, std::string& err) {
+pkc_status DeviceRunner::run_subsampling(const Plan& p, int b0, int b1, cudaStream_t st, std::string& err) {
   const Config& c = cfg_;
   const int d = c.d_model, C = c.sub_channels;
-  const bool bf = c.bf16;
-  const int M = p.M;
-  const double hs = 2.0;
-  ItemTables t{p.B, t_pcm_off, t_S, t_mel_off, t_Tm, t_mval, t_v1_off, t_v1, t_v2_off, t_v2, t_v_off, t_v};
-
-  // ---- subsampling (src/subsampling.cpp:48-240)
   if (c.split) {
-    PKC_ST(run_subsampling_split(p, st, err));
-  } else if (sub_unfused_) {
+    if (b0 != 0 || b1 != p.B) {
+      err = "internal: the f32-accurate subsampling runs on whole batches";
+      return PKC_ERR_INTERNAL;
+    }
+    return run_subsampling_split(p, st, err);
+  }
+  const ItemTables t = tables_of(b0, b1);
+  int max_v2 = 0, max_v = 0;
+  for (int b = b0; b < b1; ++b) {
+    max_v2 = std::max(max_v2, p.v2[b]);
+    max_v = std::max(max_v, p.v[b]);
+  }
+  const int r1 = p.v1_off[b0], M1 = p.v1_off[b1] - r1;
+  const int r2 = p.v2_off[b0], M2 = p.v2_off[b1] - r2;
+  const int r3 = p.v_off[b0], M = p.v_off[b1] - r3;
+  const int nf = p.mel_off[b1] - p.mel_off[b0];
+  __nv_bfloat16* s2a = reinterpret_cast<__nv_bfloat16*>(b_.s2a);
+  __nv_bfloat16* s2b = reinterpret_cast<__nv_bfloat16*>(b_.s2b);
+  __nv_bfloat16* s3a = reinterpret_cast<__nv_bfloat16*>(b_.s3a);
+  __nv_bfloat16* s3b = reinterpret_cast<__nv_bfloat16*>(b_.s3b);
+  // ---- subsampling (src/subsampling.cpp:48-240)
+  if (sub_unfused_) {
+    if (b0 != 0 || b1 != p.B) {
+      err = "internal: the unfused subsampling runs on whole batches";
+      return PKC_ERR_INTERNAL;
+    }
     prof_begin(st);
     PKC_CK(sub_conv0_launch(b_.logmel, c.n_mels, w_.c0_w, w_.c0_b, C,
                             reinterpret_cast<__nv_bfloat16*>(b_.s1), c.F1, t, p.M1, st), "conv0");
     prof_end(st, "sub_conv0", 2.0 * p.M1 * c.F1 * C * 9, (double)p.total_frames * c.n_mels * 4 + (double)p.M1 * c.F1 * C * 2);
     prof_begin(st);
     PKC_CK(sub_dw_launch(reinterpret_cast<const __nv_bfloat16*>(b_.s1), c.F1, t_v1_off, t_v1, w_.dw1_w,
-                         w_.dw1_b, C, reinterpret_cast<__nv_bfloat16*>(b_.s2a), c.F2, t_v2_off, t_v2, p.B,
-                         p.max_v2, st), "dw1");
+                         w_.dw1_b, C, s2a, c.F2, t_v2_off, t_v2, p.B, p.max_v2, st), "dw1");
     prof_end(st, "sub_dw", 2.0 * p.M2 * c.F2 * C * 9, ((double)p.M1 * c.F1 + (double)p.M2 * c.F2) * C * 2);
   } else {
     // conv.0 + ReLU + first depthwise in one kernel; algorithmic bytes: mel
     // read once, stage-2 frames written once
     prof_begin(st);
-    PKC_CK(sub_stage1_launch(b_.logmel, c.n_mels, w_.c0_w, w_.c0_b, w_.dw1_w, w_.dw1_b, C,
-                             reinterpret_cast<__nv_bfloat16*>(b_.s2a), c.F1, t, p.max_v2, st), "stage1");
-    prof_end(st, "sub_stage1", 2.0 * p.M1 * c.F1 * C * 9 + 2.0 * p.M2 * c.F2 * C * 9,
-             (double)p.total_frames * c.n_mels * 4 + (double)p.M2 * c.F2 * C * 2);
+    PKC_CK(sub_stage1_launch(b_.logmel, c.n_mels, w_.c0_w, w_.c0_b, w_.dw1_w, w_.dw1_b, C, s2a, c.F1, t, max_v2, st),
+           "stage1");
+    prof_end(st, "sub_stage1", 2.0 * M1 * c.F1 * C * 9 + 2.0 * M2 * c.F2 * C * 9,
+             (double)nf * c.n_mels * 4 + (double)M2 * c.F2 * C * 2);
   }
-  if (!c.split) {
-    PKC_ST(gemm(b_.s2a, C, w_.pw1_w, C, true, p.M2 * c.F2, C, C, EPI_STORE_H, ACT_RELU, 1.f, w_.pw1_b,
-                b_.s2b, C, st, "gemm_sub_pw", err));
-    prof_begin(st);
-    PKC_CK(sub_dw_launch(reinterpret_cast<const __nv_bfloat16*>(b_.s2b), c.F2, t_v2_off, t_v2, w_.dw2_w,
-                         w_.dw2_b, C, reinterpret_cast<__nv_bfloat16*>(b_.s3a), c.F3, t_v_off, t_v, p.B,
-                         p.max_v, st), "dw2");
-    prof_end(st, "sub_dw", 2.0 * M * c.F3 * C * 9, ((double)p.M2 * c.F2 + (double)M * c.F3) * C * 2);
-    PKC_ST(gemm(b_.s3a, C, w_.pw2_w, C, true, M * c.F3, C, C, EPI_STORE_H, ACT_RELU, 1.f, w_.pw2_b,
-                b_.s3b, C, st, "gemm_sub_pw", err));
-    const float xs = c.xscaling ? std::sqrt((float)d) : 1.f;
-    PKC_ST(gemm(b_.s3b, c.F3 * C, w_.out_w, c.F3 * C, true, M, d, c.F3 * C, EPI_STORE_F32, ACT_NONE, xs,
-                w_.out_b, b_.x, d, st, "gemm_sub_out", err));
-  }
+  const size_t o2 = (size_t)r2 * c.F2 * C, o3 = (size_t)r3 * c.F3 * C;
+  PKC_ST(gemm(s2a + o2, C, w_.pw1_w, C, true, M2 * c.F2, C, C, EPI_STORE_H, ACT_RELU, 1.f, w_.pw1_b, s2b + o2, C, st,
+              "gemm_sub_pw", err));
+  prof_begin(st);
+  PKC_CK(sub_dw_launch(s2b, c.F2, t_v2_off + b0, t_v2 + b0, w_.dw2_w, w_.dw2_b, C, s3a, c.F3, t_v_off + b0, t_v + b0,
+                       b1 - b0, max_v, st), "dw2");
+  prof_end(st, "sub_dw", 2.0 * M * c.F3 * C * 9, ((double)M2 * c.F2 + (double)M * c.F3) * C * 2);
+  PKC_ST(gemm(s3a + o3, C, w_.pw2_w, C, true, M * c.F3, C, C, EPI_STORE_H, ACT_RELU, 1.f, w_.pw2_b, s3b + o3, C, st,
+              "gemm_sub_pw", err));
+  const float xs = c.xscaling ? std::sqrt((float)d) : 1.f;
+  PKC_ST(gemm(s3b + o3, c.F3 * C, w_.out_w, c.F3 * C, true, M, d, c.F3 * C, EPI_STORE_F32, ACT_NONE, xs, w_.out_b,
+              b_.x + (size_t)r3 * d, d, st, "gemm_sub_out", err));
+  return PKC_OK;
+}
 
+pkc_status DeviceRunner::run_pos(const Plan& p, cudaStream_t st, std::string& err) {
+  const Config& c = cfg_;
+  const int d = c.d_model;
+  const double hs = 2.0;
   // ---- relative positional table (src/pos_enc.cpp:10-34), shared by the batch
   const int np = 2 * p.centre - 1;
   const int Ld = c.n_layers * d;
@@ -514,42 +555,53 @@ pkc_status DeviceRunner::run_encoder(const Plan& p, cudaStream_t st, std::string
                       Ld, OUT_H, 0, st, "gemm_pos", err));
   } else {
     prof_begin(st);
-    PKC_CK(pos_table_launch(b_.pe, p.centre, d, bf, st), "pos_table");
+    PKC_CK(pos_table_launch(b_.pe, p.centre, d, c.bf16, st), "pos_table");
     prof_end(st, "pos_table", 0.0, (double)np * d * hs);
     // every layer's linear_pos (no bias) in one GEMM: ptab [np, L*d], layer l at column l*d
-    PKC_ST(gemm(b_.pe, d, w_.pos_all_w, d, bf, np, Ld, d, EPI_STORE_H, ACT_NONE, 1.f, nullptr, b_.ptab, Ld,
+    PKC_ST(gemm(b_.pe, d, w_.pos_all_w, d, c.bf16, np, Ld, d, EPI_STORE_H, ACT_NONE, 1.f, nullptr, b_.ptab, Ld,
                 st, "gemm_pos", err, &w_.pos_all_q));
   }
+  return PKC_OK;
+}
 
+namespace {
+double attn_flops_range(const Plan& p, int d, int b0, int b1) {
+  double f = 0.0;
+  for (int b = b0; b < b1; ++b) {
+    const double T = p.v[b];
+    f += 2.0 * T * T * d * 2 + 2.0 * T * (2 * T - 1) * d;
+  }
+  return f;
+}
+int max_v_range(const Plan& p, int b0, int b1) {
+  int m = 0;
+  for (int b = b0; b < b1; ++b) m = std::max(m, p.v[b]);
+  return m;
+}
+}  // namespace
+
+pkc_status DeviceRunner::run_encoder(const Plan& p, cudaStream_t st, std::string& err) {
+  const Config& c = cfg_;
+  const int M = p.M;
+  PKC_ST(run_subsampling(p, 0, p.B, st, err));
+  PKC_ST(run_pos(p, st, err));
 
   // ---- conformer layers: one part, or two independent parts on two streams
   const int ntiles = (int)p.attn_tiles.size() / 2;
-  auto attn_flops_of = [&](int b0, int b1) {
-    double f = 0.0;
-    for (int b = b0; b < b1; ++b) {
-      const double T = p.v[b];
-      f += 2.0 * T * T * d * 2 + 2.0 * T * (2 * T - 1) * d;
-    }
-    return f;
-  };
-  auto max_v_of = [&](int b0, int b1) {
-    int m = 0;
-    for (int b = b0; b < b1; ++b) m = std::max(m, p.v[b]);
-    return m;
-  };
   const bool two = p.split_b > 0 && !prof_on_;
   auto layer = [&](int li, const Part& q, cudaStream_t s) {
     return c.split ? run_layer_split(p, li, q, s, err) : run_layer(p, li, q, s, err);
   };
   if (!two) {
-    const Part all{0, 0, M, 0, p.B, p.max_v, t_tiles, ntiles, attn_flops_of(0, p.B)};
+    const Part all{0, 0, M, 0, p.B, p.max_v, t_tiles, ntiles, attn_flops_range(p, c.d_model, 0, p.B)};
     for (int li = 0; li < c.n_layers; ++li) PKC_ST(layer(li, all, st));
     return PKC_OK;
   }
   const int sb = p.split_b;
-  const Part p0{0, 0, p.v_off[sb], 0, sb, max_v_of(0, sb), t_tiles, p.ntiles0, attn_flops_of(0, sb)};
-  const Part p1{1, p.v_off[sb], M - p.v_off[sb], sb, p.B - sb, max_v_of(sb, p.B), t_tiles + 2 * p.ntiles0,
-                ntiles - p.ntiles0, attn_flops_of(sb, p.B)};
+  const Part p0{0, 0, p.v_off[sb], 0, sb, max_v_range(p, 0, sb), t_tiles, p.ntiles0,
+                attn_flops_range(p, c.d_model, 0, sb)};
+  const Part p1{1, p.v_off[sb], M - p.v_off[sb], sb, p.B - sb, max_v_range(p, sb, p.B), t_tiles + 2 * p.ntiles0,
+                ntiles - p.ntiles0, attn_flops_range(p, c.d_model, sb, p.B)};
   // fork: the second stream starts after everything issued so far on st
   PKC_CK(cudaEventRecord(ev_fork_, st), "fork event");
   PKC_CK(cudaStreamWaitEvent(stream2_, ev_fork_, 0), "fork wait");
@@ -558,6 +610,52 @@ pkc_status DeviceRunner::run_encoder(const Plan& p, cudaStream_t st, std::string
     PKC_ST(layer(li, p1, stream2_));
   }
   // join: st continues once the second part is done
+  PKC_CK(cudaEventRecord(ev_join_, stream2_), "join event");
+  PKC_CK(cudaStreamWaitEvent(st, ev_join_, 0), "join wait");
+  return PKC_OK;
+}
+
+bool DeviceRunner::split_front(const Plan& p) const {
+  return p.split_b > 0 && !prof_on_ && !cfg_.split && !sub_unfused_;
+}
+
+pkc_status DeviceRunner::run_two_part(const Plan& p, cudaStream_t st, bool transpose, std::string& err) {
+  const Config& c = cfg_;
+  const int d = c.d_model, M = p.M, sb = p.split_b;
+  const int ntiles = (int)p.attn_tiles.size() / 2;
+  // the positional table does not depend on the audio: it runs before the fork
+  PKC_ST(run_pos(p, st, err));
+  PKC_CK(cudaEventRecord(ev_fork_, st), "fork event");
+  PKC_CK(cudaStreamWaitEvent(stream2_, ev_fork_, 0), "fork wait");
+  cudaStream_t ss[2] = {st, stream2_};
+  const int bb[3] = {0, sb, p.B};
+  // inside a capture the copy events become external event nodes of the
+  // graph; launched eagerly they are plain waits and records
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  PKC_CK(cudaStreamIsCapturing(st, &cap), "capture status");
+  const bool ext = cap == cudaStreamCaptureStatusActive;
+  const Part parts[2] = {
+      {0, 0, p.v_off[sb], 0, sb, max_v_range(p, 0, sb), t_tiles, p.ntiles0, attn_flops_range(p, d, 0, sb)},
+      {1, p.v_off[sb], M - p.v_off[sb], sb, p.B - sb, max_v_range(p, sb, p.B), t_tiles + 2 * p.ntiles0,
+       ntiles - p.ntiles0, attn_flops_range(p, d, sb, p.B)}};
+  for (int k = 0; k < 2; ++k) {
+    if (io_) PKC_CK(cudaStreamWaitEvent(ss[k], ev_in_[k], ext ? cudaEventWaitExternal : 0), "input wait");
+    PKC_ST(run_frontend(p, bb[k], bb[k + 1], ss[k], err));
+    PKC_ST(run_subsampling(p, bb[k], bb[k + 1], ss[k], err));
+  }
+  for (int li = 0; li < c.n_layers; ++li)
+    for (int k = 0; k < 2; ++k) PKC_ST(run_layer(p, li, parts[k], ss[k], err));
+  for (int k = 0; k < 2; ++k) {
+    if (transpose) {
+      prof_begin(ss[k]);
+      PKC_CK(to_channels_first_launch(b_.x, b_.out, d, t_v_off + bb[k], t_v + bb[k], bb[k + 1] - bb[k],
+                                      parts[k].max_v, ss[k]), "transpose");
+      prof_end(ss[k], "to_channels_first", 0.0, (double)parts[k].M * d * 8);
+    }
+    if (io_)
+      PKC_CK(ext ? cudaEventRecordWithFlags(ev_out_[k], ss[k], cudaEventRecordExternal) : cudaEventRecord(ev_out_[k], ss[k]),
+             "output event");
+  }
   PKC_CK(cudaEventRecord(ev_join_, stream2_), "join event");
   PKC_CK(cudaStreamWaitEvent(st, ev_join_, 0), "join wait");
   return PKC_OK;
@@ -783,7 +881,8 @@ void DeviceRunner::drop_graphs() {
 
 pkc_status DeviceRunner::run_eager(const Plan& p, cudaStream_t st, bool transpose, std::string& err) {
   cudaGetLastError();  // launch checks below must not see an unrelated earlier error
-  PKC_ST(run_frontend(p, st, err));
+  if (split_front(p)) return run_two_part(p, st, transpose, err);
+  PKC_ST(run_frontend(p, 0, p.B, st, err));
   PKC_ST(run_encoder(p, st, err));
   if (transpose) {
     prof_begin(st);
@@ -797,7 +896,8 @@ pkc_status DeviceRunner::run_graphed(const Plan& p, cudaStream_t st, bool transp
   if (!use_graphs_) return run_eager(p, st, transpose, err);
   GraphEntry* hit = nullptr;
   for (GraphEntry& g : graphs_)
-    if (g.key == last_key_ && g.pcm == b_.pcm && g.x == b_.x && g.transpose == transpose && g.prof == prof_on_)
+    if (g.key == last_key_ && g.pcm == b_.pcm && g.x == b_.x && g.transpose == transpose && g.prof == prof_on_ &&
+        g.io == io_)
       hit = &g;
   if (!hit) {
     GraphEntry ge;
@@ -806,6 +906,7 @@ pkc_status DeviceRunner::run_graphed(const Plan& p, cudaStream_t st, bool transp
     ge.x = b_.x;
     ge.transpose = transpose;
     ge.prof = prof_on_;
+    ge.io = io_;
     std::vector<ProfRec> saved;
     saved.swap(prof_recs_);
     capture_events_ = &ge.events;
@@ -857,6 +958,76 @@ pkc_status DeviceRunner::run_graphed(const Plan& p, cudaStream_t st, bool transp
   return PKC_OK;
 }
 
+// Copies of the utterances [b0, b1) between host blocks (host(b), n(b) floats)
+// and the device rows dev + off(b) (consecutive utterances are consecutive on
+// the device), one cudaMemcpyAsync per run of utterances that are also
+// consecutive on the host.
+template <typename Host, typename Count, typename Off>
+static cudaError_t copy_runs(int b0, int b1, Host host, Count n, Off off, float* dev, cudaMemcpyKind kind,
+                             cudaStream_t st) {
+  int b = b0;
+  while (b < b1) {
+    if (n(b) <= 0) {
+      ++b;
+      continue;
+    }
+    float* h = host(b);
+    size_t len = (size_t)n(b);
+    int e = b + 1;
+    while (e < b1 && (n(e) <= 0 || host(e) == h + len)) len += (size_t)std::max(0, n(e++));
+    float* dv = dev + off(b);
+    const cudaError_t r = kind == cudaMemcpyHostToDevice ? cudaMemcpyAsync(dv, h, len * 4, kind, st)
+                                                         : cudaMemcpyAsync(h, dv, len * 4, kind, st);
+    if (r != cudaSuccess) return r;
+    b = e;
+  }
+  return cudaSuccess;
+}
+
+template <typename Dst>
+pkc_status DeviceRunner::encode_host_overlapped(const Plan& p, const std::vector<const float*>& pcm, bool cf, Dst dst,
+                                                std::string& err) {
+  const int d = cfg_.d_model;
+  const int bb[3] = {0, p.split_b, p.B};
+  cudaStream_t st = stream_;
+  // the uploads overwrite the PCM buffer: after everything already on st
+  PKC_CK(cudaEventRecord(ev_prior_, st), "upload ordering event");
+  PKC_CK(cudaStreamWaitEvent(cs_in_, ev_prior_, 0), "upload ordering wait");
+  for (int k = 0; k < 2; ++k) {
+    PKC_CK(copy_runs(
+               bb[k], bb[k + 1], [&](int b) { return const_cast<float*>(pcm[b]); }, [&](int b) { return p.S[b]; },
+               [&](int b) { return (size_t)p.pcm_off[b]; }, b_.pcm, cudaMemcpyHostToDevice, cs_in_),
+           "pcm upload");
+    PKC_CK(cudaEventRecord(ev_in_[k], cs_in_), "upload event");
+  }
+  io_ = true;
+  const pkc_status s = run_graphed(p, st, cf, err);
+  io_ = false;
+  if (s != PKC_OK) {
+    cudaStreamSynchronize(cs_in_);
+    cudaStreamSynchronize(st);
+    return s;
+  }
+  float* src = cf ? b_.out : b_.x;
+  cudaError_t ce = cudaSuccess;
+  for (int k = 0; k < 2 && ce == cudaSuccess; ++k) {
+    ce = cudaStreamWaitEvent(cs_out_, ev_out_[k], 0);
+    if (ce == cudaSuccess)
+      ce = copy_runs(
+          bb[k], bb[k + 1], dst, [&](int b) { return p.v[b] * d; }, [&](int b) { return (size_t)p.v_off[b] * d; },
+          src, cudaMemcpyDeviceToHost, cs_out_);
+  }
+  const pkc_status fs = finish(st, err);
+  const cudaError_t se = cudaStreamSynchronize(cs_out_);
+  cudaStreamSynchronize(cs_in_);
+  if (fs != PKC_OK) return fs;
+  if (ce != cudaSuccess || se != cudaSuccess) {
+    err = std::string("output download: ") + cudaGetErrorString(ce != cudaSuccess ? ce : se);
+    return PKC_ERR_CUDA;
+  }
+  return PKC_OK;
+}
+
 pkc_status DeviceRunner::encode_pcm_host(const std::vector<const float*>& pcm,
                                          const std::vector<int>& n, int layout, float* host_out,
                                          std::string& err) {
@@ -865,12 +1036,14 @@ pkc_status DeviceRunner::encode_pcm_host(const std::vector<const float*>& pcm,
   make_plan(cfg_, n, {}, p);
   cudaStream_t st = stream_;
   PKC_ST(prepare(p, st, err));
+  const bool cf = layout == PKC_LAYOUT_CHANNELS_FIRST;
+  const int d = cfg_.d_model;
+  if (split_front(p))
+    return encode_host_overlapped(p, pcm, cf, [&](int b) { return host_out + (size_t)p.v_off[b] * d; }, err);
   for (int b = 0; b < p.B; ++b)
     if (n[b] > 0)
       PKC_CK(cudaMemcpyAsync(b_.pcm + p.pcm_off[b], pcm[b], (size_t)n[b] * 4, cudaMemcpyHostToDevice, st), "pcm upload");
-  const bool cf = layout == PKC_LAYOUT_CHANNELS_FIRST;
   PKC_ST(run_graphed(p, st, cf, err));
-  const int d = cfg_.d_model;
   const float* src = cf ? b_.out : b_.x;
   PKC_CK(cudaMemcpyAsync(host_out, src, (size_t)p.M * d * 4, cudaMemcpyDeviceToHost, st), "output download");
   return finish(st, err);
@@ -883,10 +1056,11 @@ pkc_status DeviceRunner::encode_pcm_host_items(const std::vector<const float*>& 
   make_plan(cfg_, n, {}, p);
   cudaStream_t st = stream_;
   PKC_ST(prepare(p, st, err));
+  const bool cf = layout == PKC_LAYOUT_CHANNELS_FIRST;
+  if (split_front(p)) return encode_host_overlapped(p, pcm, cf, [&](int b) { return item_out[b]; }, err);
   for (int b = 0; b < p.B; ++b)
     if (n[b] > 0)
       PKC_CK(cudaMemcpyAsync(b_.pcm + p.pcm_off[b], pcm[b], (size_t)n[b] * 4, cudaMemcpyHostToDevice, st), "pcm upload");
-  const bool cf = layout == PKC_LAYOUT_CHANNELS_FIRST;
   PKC_ST(run_graphed(p, st, cf, err));
   const int d = cfg_.d_model;
   const float* src = cf ? b_.out : b_.x;
@@ -1122,8 +1296,8 @@ pkc_status DeviceRunner::mel_host(const std::vector<const float*>& pcm, const st
   for (int b = 0; b < p.B; ++b)
     if (n[b] > 0)
       PKC_CK(cudaMemcpyAsync(b_.pcm + p.pcm_off[b], pcm[b], (size_t)n[b] * 4, cudaMemcpyHostToDevice, st), "pcm upload");
-  PKC_ST(run_frontend(p, st, err));
-  ItemTables t{p.B, t_pcm_off, t_S, t_mel_off, t_Tm, t_mval, t_v1_off, t_v1, t_v2_off, t_v2, t_v_off, t_v};
+  PKC_ST(run_frontend(p, 0, p.B, st, err));
+  const ItemTables t = tables_of(0, p.B);
   PKC_CK(mel_to_batch_launch(b_.logmel, cfg_.n_mels, T_max, b_.melbatch, t, st), "mel batch");
   PKC_CK(cudaMemcpyAsync(host_out, b_.melbatch, (size_t)p.B * cfg_.n_mels * T_max * 4,
                          cudaMemcpyDeviceToHost, st), "mel download");

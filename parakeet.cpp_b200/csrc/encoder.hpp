@@ -11,6 +11,8 @@
 
 namespace pkc {
 
+struct ItemTables;  // kernels/kernels.h
+
 // Geometry of one batch on one device: every utterance keeps only its valid
 // frames at every stage (the reference pads to T_max and masks).
 struct Plan {
@@ -116,8 +118,30 @@ class DeviceRunner {
 
  private:
   pkc_status prepare(const Plan& p, cudaStream_t st, std::string& err);
-  pkc_status run_frontend(const Plan& p, cudaStream_t st, std::string& err);
+  // device tables of utterances [b0, b1): every table holds absolute offsets,
+  // so a range's tables are the batch's shifted to b0
+  ItemTables tables_of(int b0, int b1) const;
+  // mel front end / subsampling of utterances [b0, b1)
+  pkc_status run_frontend(const Plan& p, int b0, int b1, cudaStream_t st, std::string& err);
+  pkc_status run_subsampling(const Plan& p, int b0, int b1, cudaStream_t st, std::string& err);
+  pkc_status run_pos(const Plan& p, cudaStream_t st, std::string& err);
+  // subsampling, positional table and layers of the whole batch (one part, or
+  // the layers as two parts on two streams)
   pkc_status run_encoder(const Plan& p, cudaStream_t st, std::string& err);
+  // Two-part plans whose front end splits as well: positional table on st,
+  // then each half of the utterances runs front end -> subsampling -> layers
+  // (-> channels-first output) on its own stream. With io_, each half first
+  // waits for ev_in_[k] and records ev_out_[k] when its output is final
+  // (external event nodes when captured), so the host's upload of the second
+  // half and download of the first overlap the other half's kernels.
+  bool split_front(const Plan& p) const;
+  pkc_status run_two_part(const Plan& p, cudaStream_t st, bool transpose, std::string& err);
+  // host PCM in, host output out for a two-part plan: each half's uploads on
+  // cs_in_, the graph, each half's downloads on cs_out_ after its ev_out_
+  // (dst(b) = where utterance b's [v_b, d] block goes)
+  template <typename Dst>
+  pkc_status encode_host_overlapped(const Plan& p, const std::vector<const float*>& pcm, bool cf, Dst dst,
+                                    std::string& err);
   // a contiguous range of utterances / rows the layers are issued for
   struct Part {
     int idx;                  // 0 or 1 (selects the stream-K workspace half)
@@ -179,6 +203,12 @@ class DeviceRunner {
   // second stream of the two-part layer schedule, and its fork / join events
   cudaStream_t stream2_ = nullptr;
   cudaEvent_t ev_fork_ = nullptr, ev_join_ = nullptr;
+  // host input / output copies of two-part plans, and the events that tie
+  // each half's copies to its kernels
+  cudaStream_t cs_in_ = nullptr, cs_out_ = nullptr;
+  cudaEvent_t ev_in_[2] = {nullptr, nullptr}, ev_out_[2] = {nullptr, nullptr};
+  cudaEvent_t ev_prior_ = nullptr;  // st's earlier work, before the uploads may overwrite the PCM buffer
+  bool io_ = false;  // the launch sequence being issued waits for / records those events
   bool sub_unfused_ = false;
   bool ln_unfused_ = false;
   bool skinny_ok_ = false;  // the streaming step issues M <= 16 GEMMs as skinny kernels
@@ -208,7 +238,7 @@ class DeviceRunner {
     std::vector<int> key;
     const void* pcm = nullptr;
     const void* x = nullptr;
-    bool transpose = false, prof = false;
+    bool transpose = false, prof = false, io = false;
     cudaGraphExec_t exec = nullptr;
     std::vector<ProfRec> recs;
     std::vector<cudaEvent_t> events;

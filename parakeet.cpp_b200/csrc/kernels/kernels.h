@@ -34,10 +34,11 @@ struct MelArgs {
   const float* window;  // [n_fft], centre-padded
   int n_fft, hop;
   float preemph;
-  int total_frames;
-  __half* dft_a;        // [total_frames, 3*n_fft]
-  float* power;         // [total_frames, power_ld]
+  int total_frames;     // frames row0 .. row0 + total_frames - 1 (of the whole batch)
+  __half* dft_a;        // [rows of the batch, 3*n_fft]
+  float* power;         // [rows of the batch, power_ld]
   int power_ld;
+  int row0;             // first frame (a range of whole utterances; the tables give absolute offsets)
 };
 cudaError_t mel_frames_launch(const MelArgs& a, const ItemTables& t, cudaStream_t st);
 

@@ -33,8 +33,8 @@ __global__ void __launch_bounds__(FR_THREADS)
     k_mel_frames(MelArgs a, ItemTables t) {
   pdl_wait();
   pdl_trigger();
-  const int row = blockIdx.x;
-  if (row >= a.total_frames) return;
+  const int row = a.row0 + (int)blockIdx.x;
+  if (row >= a.row0 + a.total_frames) return;
   const int b = find_item(t.mel_off, t.B, row);
   const int fr = row - t.mel_off[b];
   const float* s = a.pcm + t.pcm_off[b];

@@ -37,4 +37,19 @@ cudaError_t per_device(PerDevice& pd, int* out, F&& init) {
   return cudaSuccess;
 }
 
+// Raise kernel `kern`'s dynamic shared memory allowance on the current device
+// to at least `bytes`; the largest allowance granted is kept per device.
+template <typename K>
+cudaError_t allow_smem(PerDevice& pd, K kern, int bytes) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  std::lock_guard<std::mutex> g(pd.mu);
+  auto it = pd.val.find(dev);
+  if (it != pd.val.end() && it->second >= bytes) return cudaSuccess;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess) pd.val[dev] = bytes;
+  return e;
+}
+
 }  // namespace pkc

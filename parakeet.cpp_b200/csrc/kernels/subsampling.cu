@@ -13,6 +13,7 @@
 // [frames*F, C] x [C, C] GEMMs.
 #include "common.cuh"
 #include "kernels.h"
+#include "per_device.h"
 
 namespace pkc {
 
@@ -293,16 +294,12 @@ cudaError_t sub_stage1_launch(const float* logmel, int F, const float* w0, const
   if (C % S1_CG != 0) return cudaErrorInvalidValue;
   const size_t smem = sub_stage1_smem(F, F1);
   const dim3 grid((max_v2 + S1_T2 - 1) / S1_T2, t.B, C / S1_CG);
-  int dev = 0;
-  cudaGetDevice(&dev);
+  // the largest dynamic shared memory this kernel has been allowed, per device
 #define PKC_S1(FF)                                                                                   \
   {                                                                                                  \
-    static size_t attr[64] = {};                                                                     \
-    if (attr[dev & 63] < smem) {                                                                     \
-      const cudaError_t e = cudaFuncSetAttribute(k_sub_stage1<FF>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem); \
-      if (e != cudaSuccess) return e;                                                                \
-      attr[dev & 63] = smem;                                                                         \
-    }                                                                                                \
+    static PerDevice attr;                                                                           \
+    const cudaError_t e = allow_smem(attr, k_sub_stage1<FF>, (int)smem);                             \
+    if (e != cudaSuccess) return e;                                                                  \
     return launch_pdl(k_sub_stage1<FF>, grid, dim3(S1_THREADS), smem, st, logmel, F, w0, b0, w1, b1, C, out, t); \
   }
   switch (F1) {

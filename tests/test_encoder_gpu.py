@@ -247,6 +247,53 @@ def test_two_part_layer_schedule_is_bitwise_single_stream(models, oracles, kind,
         assert rel_err(a, r.T) < 2e-2
 
 
+@pytest.mark.parametrize("kind", ["f16", "q8_0"])
+def test_two_part_host_copies_pair_with_their_half(models, kind, monkeypatch):
+    """Two-part plans split the mel front end and subsampling by utterance
+    half as well, and the host entry points overlap their copies with the
+    other half's kernels: each half's uploads go on a copy stream whose event
+    its first kernel waits for (an external event node of the CUDA graph), and
+    each half's downloads wait for an event its last kernel records. Checked
+    bit for bit against the one-stream schedule: two calls of one geometry
+    with different audio (the graph replays, and every call's copies must pair
+    with its own kernels), both output layouts, the device-resident entry (the
+    split front end without copies), eager launches (PKC_NO_GRAPH=1) and two
+    runners on one device (the per-clip output path of the multi-device
+    dispatcher)."""
+    import pkc
+    import torch
+    lens = [SR * 15 + 1000 * i for i in range(8)]
+    a, b = clips(lens, seed=41), clips(lens, seed=42)
+
+    def run(streams, devices=(0,), eager=False):
+        monkeypatch.setenv("PKC_STREAMS", streams)
+        if eager:
+            monkeypatch.setenv("PKC_NO_GRAPH", "1")
+        else:
+            monkeypatch.delenv("PKC_NO_GRAPH", raising=False)
+        m = pkc.Model(models[kind], devices=devices)
+        try:
+            r = {"a": m.encode_pcm_batch(a), "b": m.encode_pcm_batch(b),
+                 "a_tm": m.encode_pcm_batch(a, layout=pkc.LAYOUT_TIME_MAJOR), "a_again": m.encode_pcm_batch(a)}
+            if len(devices) == 1:
+                flat = torch.from_numpy(np.concatenate(a)).cuda()
+                out = torch.empty(m.out_floats(lens), device="cuda")
+                m.encode_pcm_device(flat.data_ptr(), lens, out.data_ptr(), sync=True)
+                r["device"] = [out.cpu().numpy()]
+        finally:
+            m.close()
+        return r
+
+    one = run("1")
+    assert not np.array_equal(one["a"][0], one["b"][0])
+    for variant in ({}, {"eager": True}, {"devices": (0, 0)}):
+        two = run("2", **variant)
+        for key, outs in two.items():
+            assert len(outs) == len(one[key])
+            for i, (x, y) in enumerate(zip(outs, one[key])):
+                np.testing.assert_array_equal(x, y, err_msg=f"{variant} {key} clip {i}")
+
+
 def test_ctc_head_matches_oracle_on_the_same_encoder_output(models, oracles):
     """CTC head (hybrid model): the GPU's split-f16 GEMM (~22-bit products) +
     log-softmax + argmax, fed the GPU's own encoder output, against the f64
