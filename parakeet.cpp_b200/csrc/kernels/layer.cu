@@ -8,102 +8,121 @@
 //                   -> SiLU, with zeros outside each utterance's frames (the
 //                   reference's pre-depthwise time mask, :63-79)
 //   k_to_chfirst    packed time-major -> per-utterance channels-first output
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
+#include "per_device.h"
 
 namespace pkc {
 
 namespace {
 
-// One warp per row; each lane holds d/32 values (NV float4 chunks).
+// One warp per row, each lane holding d/32 values (NV float4 chunks); the
+// grid is at most a few CTAs per SM and every warp walks rows with a stride,
+// loading its next row while it normalises the current one. gamma / beta of
+// both norms are staged once per CTA in shared memory (they are weights:
+// before the dependency wait) instead of 2 d floats of registers per lane,
+// which left room for two rows per SM sub-partition at d = 1024.
 // SPLIT (f32-accurate path, H = f16): out_h rows are [hi | lo] of width 2d,
 // hi = f16(y), lo = f16(y - hi).
+constexpr int LN_THREADS = 256;
+constexpr int LN_WARPS = LN_THREADS / 32;
+
 template <int NV, typename H, bool SPLIT>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(LN_THREADS)
     k_layernorm(float* __restrict__ x, int M, const float* __restrict__ g, const float* __restrict__ b,
                 H* __restrict__ out_h, const float* __restrict__ g2, const float* __restrict__ b2,
                 int write_x) {
   constexpr int D = NV * 128;
-  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  // gamma / beta are weights: loaded before the dependency wait, so their
-  // latency overlaps the kernel before this one instead of following the row
-  float4 g4[NV], b4[NV];
-  if (row < M) {
-#pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      g4[i] = __ldg(reinterpret_cast<const float4*>(g + (i * 32 + lane) * 4));
-      b4[i] = __ldg(reinterpret_cast<const float4*>(b + (i * 32 + lane) * 4));
+  __shared__ float4 s_g[2][D / 4], s_b[2][D / 4];
+  for (int i = threadIdx.x; i < D / 4; i += LN_THREADS) {
+    s_g[0][i] = __ldg(reinterpret_cast<const float4*>(g) + i);
+    s_b[0][i] = __ldg(reinterpret_cast<const float4*>(b) + i);
+    if (g2) {
+      s_g[1][i] = __ldg(reinterpret_cast<const float4*>(g2) + i);
+      s_b[1][i] = __ldg(reinterpret_cast<const float4*>(b2) + i);
     }
   }
+  __syncthreads();
   pdl_wait();
   pdl_trigger();
-  if (row >= M) return;
-  float* xr = x + (size_t)row * D;
-  float v[NV * 4];
+  const int lane = threadIdx.x & 31;
+  const int stride = gridDim.x * LN_WARPS;
+  int row = blockIdx.x * LN_WARPS + (threadIdx.x >> 5);
+  float4 nx[NV];
+  if (row < M) {
+    const float* xr = x + (size_t)row * D;
 #pragma unroll
-  for (int i = 0; i < NV; ++i) {
-    const float4 q = *reinterpret_cast<const float4*>(xr + (i * 32 + lane) * 4);
-    v[4 * i] = q.x; v[4 * i + 1] = q.y; v[4 * i + 2] = q.z; v[4 * i + 3] = q.w;
+    for (int i = 0; i < NV; ++i) nx[i] = *reinterpret_cast<const float4*>(xr + (i * 32 + lane) * 4);
   }
-  auto norm = [&](const float* gg, const float* bb) {
-    float s = 0.f;
-#pragma unroll
-    for (int i = 0; i < NV * 4; ++i) s += v[i];
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-    const float mean = s / (float)D;
-    float s2 = 0.f;
-#pragma unroll
-    for (int i = 0; i < NV * 4; ++i) {
-      v[i] -= mean;
-      s2 += v[i] * v[i];
-    }
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
-    const float scale = 1.0f / sqrtf(s2 / (float)D + 1e-5f);
+  for (; row < M; row += stride) {
+    float v[NV * 4];
 #pragma unroll
     for (int i = 0; i < NV; ++i) {
-      v[4 * i] = v[4 * i] * scale * g4[i].x + b4[i].x;
-      v[4 * i + 1] = v[4 * i + 1] * scale * g4[i].y + b4[i].y;
-      v[4 * i + 2] = v[4 * i + 2] * scale * g4[i].z + b4[i].z;
-      v[4 * i + 3] = v[4 * i + 3] * scale * g4[i].w + b4[i].w;
+      v[4 * i] = nx[i].x; v[4 * i + 1] = nx[i].y; v[4 * i + 2] = nx[i].z; v[4 * i + 3] = nx[i].w;
     }
-    if (gg) {  // the second norm's gamma / beta (loaded after the first norm used g4 / b4)
+    // the warp's next row in flight while this one is normalised
+    if (row + stride < M) {
+      const float* xn = x + (size_t)(row + stride) * D;
+#pragma unroll
+      for (int i = 0; i < NV; ++i) nx[i] = *reinterpret_cast<const float4*>(xn + (i * 32 + lane) * 4);
+    }
+    float* xr = x + (size_t)row * D;
+    auto norm = [&](int w) {
+      float s = 0.f;
+#pragma unroll
+      for (int i = 0; i < NV * 4; ++i) s += v[i];
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+      const float mean = s / (float)D;
+      float s2 = 0.f;
+#pragma unroll
+      for (int i = 0; i < NV * 4; ++i) {
+        v[i] -= mean;
+        s2 += v[i] * v[i];
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) s2 += __shfl_xor_sync(0xffffffffu, s2, o);
+      const float scale = 1.0f / sqrtf(s2 / (float)D + 1e-5f);
 #pragma unroll
       for (int i = 0; i < NV; ++i) {
-        g4[i] = __ldg(reinterpret_cast<const float4*>(gg + (i * 32 + lane) * 4));
-        b4[i] = __ldg(reinterpret_cast<const float4*>(bb + (i * 32 + lane) * 4));
+        const float4 g4 = s_g[w][i * 32 + lane], b4 = s_b[w][i * 32 + lane];
+        v[4 * i] = v[4 * i] * scale * g4.x + b4.x;
+        v[4 * i + 1] = v[4 * i + 1] * scale * g4.y + b4.y;
+        v[4 * i + 2] = v[4 * i + 2] * scale * g4.z + b4.z;
+        v[4 * i + 3] = v[4 * i + 3] * scale * g4.w + b4.w;
       }
+    };
+    norm(0);
+    if (write_x) {
+#pragma unroll
+      for (int i = 0; i < NV; ++i)
+        *reinterpret_cast<float4*>(xr + (i * 32 + lane) * 4) =
+            make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
     }
-  };
-  norm(g2, b2);
-  if (write_x) {
+    if (g2) norm(1);
+    if (out_h) {
+      H* o = out_h + (size_t)row * D * (SPLIT ? 2 : 1);
 #pragma unroll
-    for (int i = 0; i < NV; ++i)
-      *reinterpret_cast<float4*>(xr + (i * 32 + lane) * 4) =
-          make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
-  }
-  if (g2) norm(nullptr, nullptr);
-  if (out_h) {
-    H* o = out_h + (size_t)row * D * (SPLIT ? 2 : 1);
+      for (int i = 0; i < NV; ++i) {
+        if constexpr (SPLIT) {
+          float hi[4], lo[4];
 #pragma unroll
-    for (int i = 0; i < NV; ++i) {
-      if constexpr (SPLIT) {
-        float hi[4], lo[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          hi[e] = from_h(to_h<H>(v[4 * i + e]));
-          lo[e] = v[4 * i + e] - hi[e];
+          for (int e = 0; e < 4; ++e) {
+            hi[e] = from_h(to_h<H>(v[4 * i + e]));
+            lo[e] = v[4 * i + e] - hi[e];
+          }
+          *reinterpret_cast<uint2*>(o + (i * 32 + lane) * 4) =
+              make_uint2(pack2<H>(hi[0], hi[1]), pack2<H>(hi[2], hi[3]));
+          *reinterpret_cast<uint2*>(o + D + (i * 32 + lane) * 4) =
+              make_uint2(pack2<H>(lo[0], lo[1]), pack2<H>(lo[2], lo[3]));
+        } else {
+          uint2 w;
+          w.x = pack2<H>(v[4 * i], v[4 * i + 1]);
+          w.y = pack2<H>(v[4 * i + 2], v[4 * i + 3]);
+          *reinterpret_cast<uint2*>(o + (i * 32 + lane) * 4) = w;
         }
-        *reinterpret_cast<uint2*>(o + (i * 32 + lane) * 4) = make_uint2(pack2<H>(hi[0], hi[1]), pack2<H>(hi[2], hi[3]));
-        *reinterpret_cast<uint2*>(o + D + (i * 32 + lane) * 4) =
-            make_uint2(pack2<H>(lo[0], lo[1]), pack2<H>(lo[2], lo[3]));
-      } else {
-        uint2 w;
-        w.x = pack2<H>(v[4 * i], v[4 * i + 1]);
-        w.y = pack2<H>(v[4 * i + 2], v[4 * i + 3]);
-        *reinterpret_cast<uint2*>(o + (i * 32 + lane) * 4) = w;
       }
     }
   }
@@ -232,21 +251,42 @@ __global__ void k_to_chfirst(const float* __restrict__ x, float* __restrict__ ou
 
 }  // namespace
 
+namespace {
+// one launch of k_layernorm<NV, H, SPLIT>: rows stride over one wave (the
+// CTAs resident on all SMs at once, from the occupancy of this instantiation)
+template <int NV, typename H, bool SPLIT>
+cudaError_t ln_go(float* x, int M, const float* g, const float* b, H* out, const float* g2, const float* b2,
+                  int wx, cudaStream_t st) {
+  auto kern = k_layernorm<NV, H, SPLIT>;
+  static PerDevice wave;
+  int w = 0;
+  const cudaError_t we = per_device(wave, &w, [&](int dev, int& v) {
+    int n_sm = 0, per_sm = 0;
+    cudaError_t r = cudaDeviceGetAttribute(&n_sm, cudaDevAttrMultiProcessorCount, dev);
+    if (r == cudaSuccess) r = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, LN_THREADS, 0);
+    v = std::max(1, per_sm) * n_sm;
+    return r;
+  });
+  if (we != cudaSuccess) return we;
+  const int need = (M + LN_WARPS - 1) / LN_WARPS;
+  return launch_pdl(kern, dim3(std::min(need, w)), dim3(LN_THREADS), 0, st, x, M, g, b, out, g2, b2, wx);
+}
+}  // namespace
+
 cudaError_t layernorm_launch(float* x, int M, int d, const float* g, const float* b, void* out_h,
                              bool bf16, const float* g2, const float* b2, bool write_x,
                              cudaStream_t st, bool split) {
   if (M <= 0) return cudaSuccess;
   if (split && bf16) return cudaErrorInvalidValue;
-  const dim3 grid((M + 7) / 8);
   const int wx = write_x ? 1 : 0;
   cudaError_t e = cudaSuccess;
 #define PKC_LN(NV)                                                                                   \
   if (split)                                                                                         \
-    e = launch_pdl(k_layernorm<NV, __half, true>, grid, dim3(256), 0, st, x, M, g, b, (__half*)out_h, g2, b2, wx); \
+    e = ln_go<NV, __half, true>(x, M, g, b, (__half*)out_h, g2, b2, wx, st);                         \
   else if (bf16)                                                                                     \
-    e = launch_pdl(k_layernorm<NV, __nv_bfloat16, false>, grid, dim3(256), 0, st, x, M, g, b, (__nv_bfloat16*)out_h, g2, b2, wx); \
+    e = ln_go<NV, __nv_bfloat16, false>(x, M, g, b, (__nv_bfloat16*)out_h, g2, b2, wx, st);          \
   else                                                                                               \
-    e = launch_pdl(k_layernorm<NV, __half, false>, grid, dim3(256), 0, st, x, M, g, b, (__half*)out_h, g2, b2, wx);
+    e = ln_go<NV, __half, false>(x, M, g, b, (__half*)out_h, g2, b2, wx, st);
   switch (d) {
     case 256: PKC_LN(2) break;
     case 512: PKC_LN(4) break;
