@@ -177,11 +177,19 @@ __global__ void __launch_bounds__(S1_THREADS)
   uint8_t* s1 = smem_raw + (((size_t)S1_MROWS * FP * 4 + 127) / 128) * 128;      // [S1_ROWS*F1][S1_CG] bf16
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
 
-  // 1. mel rows
-  for (int i = tid; i < S1_MROWS * FP; i += S1_THREADS) {
-    const int r = i / FP, col = i % FP - 1;
-    const int tm = tm_0 + r;
-    melt[i] = (col >= 0 && col < F && tm >= 0 && tm < mvalid) ? mel[(size_t)tm * F + col] : 0.f;
+  // 1. mel rows: thread tid owns padded column tid (FP <= S1_THREADS, checked
+  //    at launch), its S1_MROWS loads in flight together
+  if (tid < FP) {
+    const int col = tid - 1;
+    const bool col_ok = col >= 0 && col < F;
+    float v[S1_MROWS];
+#pragma unroll
+    for (int r = 0; r < S1_MROWS; ++r) {
+      const int tm = tm_0 + r;
+      v[r] = (col_ok && tm >= 0 && tm < mvalid) ? mel[(size_t)tm * F + col] : 0.f;
+    }
+#pragma unroll
+    for (int r = 0; r < S1_MROWS; ++r) melt[r * FP + tid] = v[r];
   }
   __syncthreads();
 
@@ -202,18 +210,24 @@ __global__ void __launch_bounds__(S1_THREADS)
       bias[nt][0] = b0[cg0 + nt * 8 + 2 * t4];
       bias[nt][1] = b0[cg0 + nt * 8 + 2 * t4 + 1];
     }
-    auto tap = [&](int p, int k) -> float {
-      if (p >= NP || k >= 9) return 0.f;
-      const int r1 = p / F1, f1 = p % F1;
-      return melt[(2 * r1 + k / 3) * FP + 2 * f1 + k % 3];
-    };
+    // tap k of position p = (r1, f1) reads melt[(2 r1 + k / 3) FP + 2 f1 + k % 3]:
+    // a position's base plus a tap offset. This thread's taps are 2 t4,
+    // 2 t4 + 1 (always < 9) and 2 t4 + 8 (< 9 only for t4 = 0); 2 t4 + 9 is
+    // past the 9 taps (the zero K padding).
+    auto toff = [&](int k) { return (k / 3) * FP + k % 3; };
+    const int o0 = toff(2 * t4), o1 = toff(2 * t4 + 1), o2 = toff(8);
+    const bool has8 = t4 == 0;
+    auto base = [&](int p) { return 2 * (p / F1) * FP + 2 * (p % F1); };
     for (int mt = warp; mt < MT; mt += S1_THREADS / 32) {
       const int p0 = mt * 16 + g, p1 = p0 + 8;
+      const bool in0 = p0 < NP, in1 = p1 < NP;
+      const float* m0 = melt + base(p0);
+      const float* m1 = melt + base(p1);
       uint32_t a[4];
-      a[0] = pack2<__half>(tap(p0, 2 * t4), tap(p0, 2 * t4 + 1));
-      a[1] = pack2<__half>(tap(p1, 2 * t4), tap(p1, 2 * t4 + 1));
-      a[2] = pack2<__half>(tap(p0, 2 * t4 + 8), tap(p0, 2 * t4 + 9));
-      a[3] = pack2<__half>(tap(p1, 2 * t4 + 8), tap(p1, 2 * t4 + 9));
+      a[0] = pack2<__half>(in0 ? m0[o0] : 0.f, in0 ? m0[o1] : 0.f);
+      a[1] = pack2<__half>(in1 ? m1[o0] : 0.f, in1 ? m1[o1] : 0.f);
+      a[2] = pack2<__half>(in0 && has8 ? m0[o2] : 0.f, 0.f);
+      a[3] = pack2<__half>(in1 && has8 ? m1[o2] : 0.f, 0.f);
       // rows of this tile's positions outside [0, v1) are zero (stage-2 input mask)
       const bool live0 = p0 < NP && t1_0 + p0 / F1 >= 0 && t1_0 + p0 / F1 < v1b;
       const bool live1 = p1 < NP && t1_0 + p1 / F1 >= 0 && t1_0 + p1 / F1 < v1b;
@@ -291,7 +305,7 @@ cudaError_t sub_stage1_launch(const float* logmel, int F, const float* w0, const
                               const float* b1, int C, __nv_bfloat16* out, int F1, const ItemTables& t,
                               int max_v2, cudaStream_t st) {
   if (t.B <= 0 || max_v2 <= 0) return cudaSuccess;
-  if (C % S1_CG != 0) return cudaErrorInvalidValue;
+  if (C % S1_CG != 0 || F + 2 > S1_THREADS) return cudaErrorInvalidValue;
   const size_t smem = sub_stage1_smem(F, F1);
   const dim3 grid((max_v2 + S1_T2 - 1) / S1_T2, t.B, C / S1_CG);
   // the largest dynamic shared memory this kernel has been allowed, per device
