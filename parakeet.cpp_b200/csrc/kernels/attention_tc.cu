@@ -79,7 +79,8 @@ struct TcLayout {
   static constexpr int OFF_RING = OFF_QU + Q_BYTES;
   static constexpr int OFF_SKEW = OFF_RING + RING * T_BYTES;
   static constexpr int OFF_RED = OFF_SKEW + QM * SKEW_LD * 4;  // [2 parity][2 half][QM] floats
-  static constexpr int OFF_BAR = OFF_RED + 2 * 2 * QM * 4;
+  static constexpr int OFF_BIAS = OFF_RED + 2 * 2 * QM * 4;  // [u | v] of the head, 2 dk floats
+  static constexpr int OFF_BAR = OFF_BIAS + 2 * DK * 4;
   static constexpr int OFF_SLOT = OFF_BAR + N_BARS * 8;
   static constexpr int SMEM = OFF_SLOT + 16 + 1024;  // + alignment slack
 };
@@ -160,6 +161,15 @@ __global__ void __launch_bounds__(THREADS, 1)
   if (warp == 1) {
     tmem_alloc(smem_u32(tmem_slot), 512);
     tmem_relinquish();
+  }
+  // the head's pos_bias_u / pos_bias_v are weights: staged before the
+  // dependency wait, so the Q preparation reads them from shared memory
+  {
+    float4* sb = reinterpret_cast<float4*>(sm + L::OFF_BIAS);
+    const int hd = blockIdx.x;
+    for (int j = threadIdx.x; j < DK / 2; j += THREADS)
+      sb[j] = j < DK / 4 ? *reinterpret_cast<const float4*>(p.bias_u + hd * DK + 4 * j)
+                         : *reinterpret_cast<const float4*>(p.bias_v + hd * DK + 4 * (j - DK / 4));
   }
   tc_fence_before();
   __syncthreads();
@@ -314,10 +324,11 @@ __global__ void __launch_bounds__(THREADS, 1)
         uint8_t* src = sm + L::OFF_QU + kb * QM * 128 + i * 128 + ((c8 ^ (i & 7)) << 4);
         const uint4 raw = *reinterpret_cast<const uint4*>(src);
         const H* hv = reinterpret_cast<const H*>(&raw);
-        const float4 u0 = *reinterpret_cast<const float4*>(p.bias_u + head * DK + col);
-        const float4 u1 = *reinterpret_cast<const float4*>(p.bias_u + head * DK + col + 4);
-        const float4 v0 = *reinterpret_cast<const float4*>(p.bias_v + head * DK + col);
-        const float4 v1 = *reinterpret_cast<const float4*>(p.bias_v + head * DK + col + 4);
+        const float* sbu = reinterpret_cast<const float*>(sm + L::OFF_BIAS);
+        const float4 u0 = *reinterpret_cast<const float4*>(sbu + col);
+        const float4 u1 = *reinterpret_cast<const float4*>(sbu + col + 4);
+        const float4 v0 = *reinterpret_cast<const float4*>(sbu + DK + col);
+        const float4 v1 = *reinterpret_cast<const float4*>(sbu + DK + col + 4);
         const float bu[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
         const float bv[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
         uint32_t wu[4];
