@@ -127,6 +127,7 @@ DeviceRunner::~DeviceRunner() {
   if (sk_ws_) cudaFree(sk_ws_);
   if (sk_flags_) cudaFree(sk_flags_);
   if (ctc_ws_) cudaFree(ctc_ws_);
+  if (qkv_bu_) cudaFree(qkv_bu_);
   if (stream2_) {
     cudaStreamSynchronize(stream2_);
     cudaStreamDestroy(stream2_);
@@ -189,6 +190,24 @@ std::string DeviceRunner::init(const PackedWeights& pw) {
   const auto t0 = std::chrono::steady_clock::now();
   std::string err = upload_packed(pw, cfg_, w_, stream_);
   upload_s_ = std::chrono::duration<double>(std::chrono::steady_clock::now() - t0).count();
+  if (!err.empty()) return err;
+  if (!cfg_.split && !cfg_.causal()) {
+    // QKV bias + [pos_bias_u | 0 | 0] per layer, for the offline encoder
+    const int d = cfg_.d_model, nl = cfg_.n_layers;
+    std::vector<float> hb((size_t)nl * 3 * d, 0.f), hu((size_t)d);
+    for (int l = 0; l < nl; ++l) {
+      const LayerWeights& lw = w_.layers[l];
+      float* row = hb.data() + (size_t)l * 3 * d;
+      if (lw.qkv_b && cudaMemcpy(row, lw.qkv_b, (size_t)3 * d * 4, cudaMemcpyDeviceToHost) != cudaSuccess)
+        return "QKV bias download failed";
+      if (!lw.pos_u || cudaMemcpy(hu.data(), lw.pos_u, (size_t)d * 4, cudaMemcpyDeviceToHost) != cudaSuccess)
+        return "pos_bias_u download failed";
+      for (int k = 0; k < d; ++k) row[k] += hu[k];
+    }
+    if (cudaMalloc(&qkv_bu_, hb.size() * 4) != cudaSuccess ||
+        cudaMemcpy(qkv_bu_, hb.data(), hb.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess)
+      return "QKV + pos_bias_u upload failed";
+  }
   return err;
 }
 
@@ -696,17 +715,20 @@ pkc_status DeviceRunner::run_layer(const Plan& p, int li, const Part& q, cudaStr
   PKC_ST(gemm(ffh, FF, L.ff1_w2, FF, bf, M, d, FF, EPI_RESID_F32, ACT_NONE, 0.5f, L.ff1_b2, x, d, st, "gemm_ffn", err, &L.ff1_q2,
               lnq ? stats : nullptr));
   // MHSA
+  // q comes out of the GEMM as q + pos_bias_u when qkv_bu_ carries u
+  const float* qkv_bias = qkv_bu_ ? qkv_bu_ + (size_t)li * 3 * d : L.qkv_b;
   if (lnq) {
-    PKC_ST(gemm_ln(x, stats, L.qkv_w, bf, M, 3 * d, d, EPI_STORE_H, ACT_NONE, L.qkv_b, qkv, 3 * d, st, "gemm_qkv", err));
+    PKC_ST(gemm_ln(x, stats, L.qkv_w, bf, M, 3 * d, d, EPI_STORE_H, ACT_NONE, qkv_bias, qkv, 3 * d, st, "gemm_qkv", err));
   } else {
     prof_begin(st);
     PKC_CK(layernorm_launch(x, M, d, L.ln_att_g, L.ln_att_b, hbuf, bf, nullptr, nullptr, false, st), "ln");
     prof_end(st, "layernorm", 0.0, (double)M * d * (4 + hs));
-    PKC_ST(gemm(hbuf, d, L.qkv_w, d, bf, M, 3 * d, d, EPI_STORE_H, ACT_NONE, 1.f, L.qkv_b, qkv, 3 * d, st, "gemm_qkv", err, &L.qkv_q));
+    PKC_ST(gemm(hbuf, d, L.qkv_w, d, bf, M, 3 * d, d, EPI_STORE_H, ACT_NONE, 1.f, qkv_bias, qkv, 3 * d, st, "gemm_qkv", err, &L.qkv_q));
   }
   // attention addresses the whole qkv / ctx buffers by global row offsets
   AttnArgs aa{b_.qkv, static_cast<const uint8_t*>(b_.ptab) + (size_t)li * d * 2, np, p.centre, Ld,
-              L.pos_u, L.pos_v, q.tiles, q.ntiles, t_v_off, t_v, b_.ctx, d, H, p.M, err_word_};
+              L.pos_u, L.pos_v, q.tiles, q.ntiles, t_v_off, t_v, b_.ctx, d, H, p.M, err_word_,
+              qkv_bu_ ? 1 : 0};
   prof_begin(st);
   PKC_CK(attention_launch(aa, bf, st), "attention");
   prof_end(st, "attention", q.attn_flops, (double)M * (3 * d + d) * hs + (double)np * d * hs);

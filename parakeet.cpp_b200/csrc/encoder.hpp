@@ -209,6 +209,11 @@ class DeviceRunner {
   cudaEvent_t ev_in_[2] = {nullptr, nullptr}, ev_out_[2] = {nullptr, nullptr};
   cudaEvent_t ev_prior_ = nullptr;  // st's earlier work, before the uploads may overwrite the PCM buffer
   bool io_ = false;  // the launch sequence being issued waits for / records those events
+  // The offline encoder's QKV bias with pos_bias_u added to its q columns,
+  // [n_layers][3d] f32 (derived at load, not part of the packed weights):
+  // the attention then takes q + u as the GEMM wrote it. Null for the
+  // f32-accurate and causal models.
+  float* qkv_bu_ = nullptr;
   bool sub_unfused_ = false;
   bool ln_unfused_ = false;
   bool skinny_ok_ = false;  // the streaming step issues M <= 16 GEMMs as skinny kernels

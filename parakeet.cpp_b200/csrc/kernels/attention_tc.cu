@@ -97,6 +97,7 @@ struct TcParams {
   int d, centre;
   float scale_log2;
   int* err;
+  int qu_folded;        // q columns hold q + bias_u (AttnArgs::qu_folded)
 };
 
 // window column wc (0..191) of key tile t -> TMEM column of its chunk slot
@@ -164,12 +165,20 @@ __global__ void __launch_bounds__(THREADS, 1)
   }
   // the head's pos_bias_u / pos_bias_v are weights: staged before the
   // dependency wait, so the Q preparation reads them from shared memory
+  // ([u | v], or [0 | v - u] when q already carries u)
   {
     float4* sb = reinterpret_cast<float4*>(sm + L::OFF_BIAS);
     const int hd = blockIdx.x;
-    for (int j = threadIdx.x; j < DK / 2; j += THREADS)
-      sb[j] = j < DK / 4 ? *reinterpret_cast<const float4*>(p.bias_u + hd * DK + 4 * j)
-                         : *reinterpret_cast<const float4*>(p.bias_v + hd * DK + 4 * (j - DK / 4));
+    for (int j = threadIdx.x; j < DK / 2; j += THREADS) {
+      const int jj = j < DK / 4 ? j : j - DK / 4;
+      const float4 u = *reinterpret_cast<const float4*>(p.bias_u + hd * DK + 4 * jj);
+      if (j < DK / 4) {
+        sb[j] = p.qu_folded ? make_float4(0.f, 0.f, 0.f, 0.f) : u;
+      } else {
+        const float4 v = *reinterpret_cast<const float4*>(p.bias_v + hd * DK + 4 * jj);
+        sb[j] = p.qu_folded ? make_float4(v.x - u.x, v.y - u.y, v.z - u.z, v.w - u.w) : v;
+      }
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -235,7 +244,9 @@ __global__ void __launch_bounds__(THREADS, 1)
     constexpr int fmt = is_bf16<H>::value ? 1 : 0;
     constexpr uint32_t id_s = idesc_f16(QM, KN, fmt);
     constexpr uint32_t id_pv = idesc_f16(QM, DK, fmt) | (1u << 16);  // B (V) MN-major
-    bool ok = wwait(B_QREADY, 0);
+    // q + u in shared memory: the TMA tile itself when q carries u (S(0) can
+    // go once it has landed), else after the softmax warps rewrote it
+    bool ok = wwait(p.qu_folded ? B_QFULL : B_QREADY, 0);
     tc_fence_after();
     const uint64_t dqu = smem_desc_sw128(sbase + L::OFF_QU);
     // K-step kk (16 elements of dk): k-block kk/4, 32 bytes per step inside it
@@ -282,7 +293,14 @@ __global__ void __launch_bounds__(THREADS, 1)
       umma_commit_if(leader, bar(B_PVDONE + (u & 1)));
       return true;
     };
-    ok = ok && c_mma(0) && c_mma(1) && s_mma(0) && c_mma(2);
+    if (p.qu_folded) {
+      // q + v (tensor memory) is ready at QREADY
+      ok = ok && s_mma(0) && wwait(B_QREADY, 0);
+      tc_fence_after();
+      ok = ok && c_mma(0) && c_mma(1) && c_mma(2);
+    } else {
+      ok = ok && c_mma(0) && c_mma(1) && s_mma(0) && c_mma(2);
+    }
     if (ok) umma_commit_if(leader, bar(B_SFULL));
     // S(u+1) and chunk u+3 go to the tensor pipe as soon as the softmax has
     // read tile u, ahead of P(u-1) V(u-1): the softmax waits on S, while
@@ -338,7 +356,7 @@ __global__ void __launch_bounds__(THREADS, 1)
           wu[e] = pack2<H>(x0 + bu[2 * e], x1 + bu[2 * e + 1]);
           qv[4 * k + e] = pack2<H>(x0 + bv[2 * e], x1 + bv[2 * e + 1]);
         }
-        *reinterpret_cast<uint4*>(src) = make_uint4(wu[0], wu[1], wu[2], wu[3]);
+        if (!p.qu_folded) *reinterpret_cast<uint4*>(src) = make_uint4(wu[0], wu[1], wu[2], wu[3]);
       }
       if constexpr (DK == 128) {
         tmem_st32(trow + TM_QV + 32u * hh, qv);
@@ -587,7 +605,7 @@ cudaError_t launch_tc(const AttnArgs& a, cudaStream_t st) {
   if (!make_tmap_kmajor(&tp, a.ptab, a.ptab_rows, a.d, a.ptab_ld > 0 ? a.ptab_ld : a.d, 64, bf))
     return cudaErrorInvalidValue;
   TcParams p{a.tiles, a.item_off, a.item_len, a.bias_u, a.bias_v, a.ctx, a.d, a.centre,
-             1.4426950408889634f / sqrtf((float)DK), a.err};
+             1.4426950408889634f / sqrtf((float)DK), a.err, a.qu_folded ? 1 : 0};
   return launch_pdl(kern, dim3(a.n_heads, a.n_tiles), dim3(THREADS), smem, st, tq, tp, p);
 }
 

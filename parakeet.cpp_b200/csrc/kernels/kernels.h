@@ -107,6 +107,10 @@ struct AttnArgs {
   int d, n_heads;
   int rows;             // M: packed frames in qkv / ctx
   int* err;             // device error word (timeouts), may be null
+  // nonzero: the q columns of qkv already hold q + bias_u (the QKV GEMM's
+  // bias carried it), so the kernel uses them as they are and adds only
+  // bias_v - bias_u for the positional term
+  int qu_folded = 0;
 };
 // Dispatcher (the tcgen05 kernel). The tile list in AttnArgs must be built
 // with attn_query_tile() rows per tile.
