@@ -139,7 +139,9 @@ DeviceRunner::~DeviceRunner() {
       cudaStreamSynchronize(s);
       cudaStreamDestroy(s);
     }
-  for (cudaEvent_t e : {ev_in_[0], ev_in_[1], ev_out_[0], ev_out_[1], ev_prior_})
+  for (cudaEvent_t e : ev_in_)
+    if (e) cudaEventDestroy(e);
+  for (cudaEvent_t e : {ev_out_[0], ev_out_[1], ev_prior_})
     if (e) cudaEventDestroy(e);
   if (h_tables_) cudaFreeHost(h_tables_);
   free_weights(w_);
@@ -177,7 +179,9 @@ std::string DeviceRunner::init(const PackedWeights& pw) {
   if (cudaStreamCreateWithFlags(&cs_in_, cudaStreamNonBlocking) != cudaSuccess ||
       cudaStreamCreateWithFlags(&cs_out_, cudaStreamNonBlocking) != cudaSuccess)
     return "copy stream creation failed";
-  for (cudaEvent_t* e : {&ev_in_[0], &ev_in_[1], &ev_out_[0], &ev_out_[1], &ev_prior_})
+  for (cudaEvent_t& e : ev_in_)
+    if (cudaEventCreateWithFlags(&e, cudaEventDisableTiming) != cudaSuccess) return "copy event creation failed";
+  for (cudaEvent_t* e : {&ev_out_[0], &ev_out_[1], &ev_prior_})
     if (cudaEventCreateWithFlags(e, cudaEventDisableTiming) != cudaSuccess) return "copy event creation failed";
   power_ld_ = cfg_.n_fft / 2 + 8;
   const char* ng = getenv("PKC_NO_GRAPH");
@@ -638,6 +642,20 @@ bool DeviceRunner::split_front(const Plan& p) const {
   return p.split_b > 0 && !prof_on_ && !cfg_.split && !sub_unfused_;
 }
 
+void DeviceRunner::front_groups(const Plan& p, int (&gb)[kFrontGroups + 1]) const {
+  const int bb[3] = {0, p.split_b, p.B};
+  for (int k = 0; k < 2; ++k) {
+    // the split of [bb[k], bb[k+1]) nearest to half its samples
+    const double half = 0.5 * (p.pcm_off[bb[k]] + p.pcm_off[bb[k + 1]]);
+    int m = bb[k];
+    while (m + 1 < bb[k + 1] && p.pcm_off[m + 1] <= half) ++m;
+    if (m == bb[k] && bb[k + 1] - bb[k] > 1) m = bb[k] + 1;
+    gb[2 * k] = bb[k];
+    gb[2 * k + 1] = m;
+  }
+  gb[kFrontGroups] = p.B;
+}
+
 pkc_status DeviceRunner::run_two_part(const Plan& p, cudaStream_t st, bool transpose, std::string& err) {
   const Config& c = cfg_;
   const int d = c.d_model, M = p.M, sb = p.split_b;
@@ -657,10 +675,14 @@ pkc_status DeviceRunner::run_two_part(const Plan& p, cudaStream_t st, bool trans
       {0, 0, p.v_off[sb], 0, sb, max_v_range(p, 0, sb), t_tiles, p.ntiles0, attn_flops_range(p, d, 0, sb)},
       {1, p.v_off[sb], M - p.v_off[sb], sb, p.B - sb, max_v_range(p, sb, p.B), t_tiles + 2 * p.ntiles0,
        ntiles - p.ntiles0, attn_flops_range(p, d, sb, p.B)}};
-  for (int k = 0; k < 2; ++k) {
-    if (io_) PKC_CK(cudaStreamWaitEvent(ss[k], ev_in_[k], ext ? cudaEventWaitExternal : 0), "input wait");
-    PKC_ST(run_frontend(p, bb[k], bb[k + 1], ss[k], err));
-    PKC_ST(run_subsampling(p, bb[k], bb[k + 1], ss[k], err));
+  int gb[kFrontGroups + 1];
+  front_groups(p, gb);
+  for (int g = 0; g < kFrontGroups; ++g) {
+    cudaStream_t s = ss[g / 2];
+    if (io_) PKC_CK(cudaStreamWaitEvent(s, ev_in_[g], ext ? cudaEventWaitExternal : 0), "input wait");
+    if (gb[g] == gb[g + 1]) continue;
+    PKC_ST(run_frontend(p, gb[g], gb[g + 1], s, err));
+    PKC_ST(run_subsampling(p, gb[g], gb[g + 1], s, err));
   }
   for (int li = 0; li < c.n_layers; ++li)
     for (int k = 0; k < 2; ++k) PKC_ST(run_layer(p, li, parts[k], ss[k], err));
@@ -1015,12 +1037,14 @@ pkc_status DeviceRunner::encode_host_overlapped(const Plan& p, const std::vector
   // the uploads overwrite the PCM buffer: after everything already on st
   PKC_CK(cudaEventRecord(ev_prior_, st), "upload ordering event");
   PKC_CK(cudaStreamWaitEvent(cs_in_, ev_prior_, 0), "upload ordering wait");
-  for (int k = 0; k < 2; ++k) {
+  int gb[kFrontGroups + 1];
+  front_groups(p, gb);
+  for (int g = 0; g < kFrontGroups; ++g) {
     PKC_CK(copy_runs(
-               bb[k], bb[k + 1], [&](int b) { return const_cast<float*>(pcm[b]); }, [&](int b) { return p.S[b]; },
+               gb[g], gb[g + 1], [&](int b) { return const_cast<float*>(pcm[b]); }, [&](int b) { return p.S[b]; },
                [&](int b) { return (size_t)p.pcm_off[b]; }, b_.pcm, cudaMemcpyHostToDevice, cs_in_),
            "pcm upload");
-    PKC_CK(cudaEventRecord(ev_in_[k], cs_in_), "upload event");
+    PKC_CK(cudaEventRecord(ev_in_[g], cs_in_), "upload event");
   }
   io_ = true;
   const pkc_status s = run_graphed(p, st, cf, err);

@@ -130,10 +130,11 @@ class DeviceRunner {
   pkc_status run_encoder(const Plan& p, cudaStream_t st, std::string& err);
   // Two-part plans whose front end splits as well: positional table on st,
   // then each half of the utterances runs front end -> subsampling -> layers
-  // (-> channels-first output) on its own stream. With io_, each half first
-  // waits for ev_in_[k] and records ev_out_[k] when its output is final
-  // (external event nodes when captured), so the host's upload of the second
-  // half and download of the first overlap the other half's kernels.
+  // (-> channels-first output) on its own stream, the front end as two
+  // groups. With io_, each group first waits for its ev_in_ and each half
+  // records ev_out_[k] when its output is final (external event nodes when
+  // captured), so the host's uploads after the first group's, and the first
+  // half's download, overlap kernels.
   bool split_front(const Plan& p) const;
   pkc_status run_two_part(const Plan& p, cudaStream_t st, bool transpose, std::string& err);
   // host PCM in, host output out for a two-part plan: each half's uploads on
@@ -206,7 +207,12 @@ class DeviceRunner {
   // host input / output copies of two-part plans, and the events that tie
   // each half's copies to its kernels
   cudaStream_t cs_in_ = nullptr, cs_out_ = nullptr;
-  cudaEvent_t ev_in_[2] = {nullptr, nullptr}, ev_out_[2] = {nullptr, nullptr};
+  // front-end groups of a two-part plan: each half of the utterances in two
+  // groups [gb[g], gb[g + 1]) of about equal audio, group g uploaded before
+  // ev_in_[g] is recorded; only the first group's upload is not overlapped
+  static constexpr int kFrontGroups = 4;
+  void front_groups(const Plan& p, int (&gb)[kFrontGroups + 1]) const;
+  cudaEvent_t ev_in_[kFrontGroups] = {}, ev_out_[2] = {nullptr, nullptr};
   cudaEvent_t ev_prior_ = nullptr;  // st's earlier work, before the uploads may overwrite the PCM buffer
   bool io_ = false;  // the launch sequence being issued waits for / records those events
   // The offline encoder's QKV bias with pos_bias_u added to its q columns,
