@@ -266,6 +266,12 @@ pkc_status pkc_encode_pcm_device(pkc_model* m, int device_slot, const float* d_p
    own events. NULL for a bad slot. */
 void* pkc_model_stream(const pkc_model* m, int device_slot);
 
+/* Kernel launches of the CUDA graph that device slot `device_slot` launched
+   most recently (its kernel nodes, counted once when the graph was
+   instantiated); 0 before any graph launch, with PKC_NO_GRAPH=1, or for a bad
+   slot. A diagnostic with no counterpart in the reference. */
+int pkc_last_graph_kernels(const pkc_model* m, int device_slot);
+
 /* Per-kernel-class timing (CUDA events around every launch on the model's
    stream). enable != 0 turns it on and clears the accumulators. */
 pkc_status pkc_profile_enable(pkc_model* m, int enable);

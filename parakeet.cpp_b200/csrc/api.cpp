@@ -674,6 +674,11 @@ void* pkc_model_stream(const pkc_model* m, int device_slot) {
   return reinterpret_cast<void*>(m->runners[device_slot]->stream());
 }
 
+int pkc_last_graph_kernels(const pkc_model* m, int device_slot) {
+  if (!m || device_slot < 0 || device_slot >= (int)m->runners.size()) return 0;
+  return m->runners[device_slot]->last_graph_kernels();
+}
+
 pkc_status pkc_profile_enable(pkc_model* m, int enable) {
   if (!m) return pkc::set_thread_error(PKC_ERR_ARG, "pkc_profile_enable: model is NULL");
   std::lock_guard<std::mutex> lk(m->mu);

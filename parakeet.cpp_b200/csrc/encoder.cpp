@@ -968,6 +968,16 @@ pkc_status DeviceRunner::run_graphed(const Plan& p, cudaStream_t st, bool transp
       if (s == PKC_OK) err = std::string("graph capture: ") + cudaGetErrorString(ce);
       return s != PKC_OK ? s : PKC_ERR_CUDA;
     }
+    // kernel nodes of the captured sequence (the launch count of one replay)
+    size_t n_nodes = 0;
+    if (cudaGraphGetNodes(graph, nullptr, &n_nodes) == cudaSuccess && n_nodes > 0) {
+      std::vector<cudaGraphNode_t> nodes(n_nodes);
+      if (cudaGraphGetNodes(graph, nodes.data(), &n_nodes) == cudaSuccess)
+        for (size_t i = 0; i < n_nodes; ++i) {
+          cudaGraphNodeType ty;
+          if (cudaGraphNodeGetType(nodes[i], &ty) == cudaSuccess && ty == cudaGraphNodeTypeKernel) ++ge.kernels;
+        }
+    }
     const cudaError_t ie = cudaGraphInstantiate(&ge.exec, graph, 0);
     cudaGraphDestroy(graph);
     if (ie != cudaSuccess) {
@@ -986,6 +996,7 @@ pkc_status DeviceRunner::run_graphed(const Plan& p, cudaStream_t st, bool transp
     hit = &graphs_.back();
   }
   PKC_CK(cudaGraphLaunch(hit->exec, st), "graph launch");
+  last_kernels_ = hit->kernels;
   if (hit->prof) {
     // the graph's event nodes are re-recorded on every replay: read them now
     PKC_CK(cudaStreamSynchronize(st), "profile synchronize");

@@ -60,6 +60,7 @@ class DeviceRunner {
   double upload_seconds() const { return upload_s_; }
   int device() const { return device_; }
   cudaStream_t stream() const { return stream_; }
+  int last_graph_kernels() const { return last_kernels_; }
 
   // Runs the front end (if pcm) and the encoder. Inputs either in host memory
   // (copied in) or already on the device. Output: time-major [M, d] f32 in
@@ -250,11 +251,13 @@ class DeviceRunner {
     const void* pcm = nullptr;
     const void* x = nullptr;
     bool transpose = false, prof = false, io = false;
+    int kernels = 0;  // kernel nodes of the graph
     cudaGraphExec_t exec = nullptr;
     std::vector<ProfRec> recs;
     std::vector<cudaEvent_t> events;
   };
   std::vector<GraphEntry> graphs_;
+  int last_kernels_ = 0;  // kernel nodes of the graph launched last
   std::vector<cudaEvent_t>* capture_events_ = nullptr;
   bool use_graphs_ = true;
   pkc_status run_graphed(const Plan& p, cudaStream_t st, bool transpose, std::string& err);

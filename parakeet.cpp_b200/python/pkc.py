@@ -118,6 +118,7 @@ def _declare(L):
          c_void_p, c_void_p, c_int),
         ("pkc_profile_enable", c_int, c_void_p, c_int),
         ("pkc_model_stream", c_void_p, c_void_p, c_int),
+        ("pkc_last_graph_kernels", c_int, c_void_p, c_int),
         ("pkc_profile_read", c_int, c_void_p, POINTER(KernelStat), c_int),
         ("pkc_shard_plan", c_int, POINTER(c_int), c_int, c_int, c_int, POINTER(c_int)),
         ("pkc_ctc_classes", c_int, c_void_p),
@@ -416,6 +417,10 @@ class Model:
                                            len(n_samples), c_void_p(d_out),
                                            c_void_p(stream) if stream else None, 1 if sync else 0),
                self._h)
+
+    def last_graph_kernels(self, slot=0):
+        """Kernel launches of the CUDA graph this device slot launched last."""
+        return int(lib().pkc_last_graph_kernels(self._h, slot))
 
     def stream(self, slot=0):
         """cudaStream_t (as int) that the host-buffer entry points use."""

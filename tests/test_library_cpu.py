@@ -134,6 +134,7 @@ def test_null_model_calls_fail_cleanly():
     assert L.pkc_mel_frames(None, 16000) == 0
     assert L.pkc_encoder_frames(None, 100) == 0
     assert L.pkc_model_stream(None, 0) is None
+    assert L.pkc_last_graph_kernels(None, 0) == 0
     st = L.pkc_encode_pcm_batch(None, None, None, 0, 0, None, 0, None)
     assert st == 1
     assert b"NULL" in L.pkc_last_error(None)
