@@ -346,6 +346,18 @@ pkc_status pkc_relpos_attention(const void* qkv, const void* ptab, int centre,
                                 const float* bias_u, const float* bias_v, const int* lens, int B,
                                 int d, int n_heads, int dtype, void* ctx, void* stream);
 
+/* The conv module's depthwise stage for B utterances packed along rows (item
+   b owns rows [off_b, off_b + lens[b]), lens on the host, zero allowed):
+   out = SiLU((depthwise Conv1d(in; w, pad (K-1)/2, zeros outside the item) +
+   bias) * scale + shift), i.e. the BatchNorm folded to scale / shift. in /
+   out [sum lens, d] in the compute type (dtype 0 f16, 1 bf16), w [K][d],
+   bias (may be null), scale, shift [d] f32; K in {3, 5, 7, 9}, d % 8 == 0.
+   Device pointers. Replaces the depthwise conv + batch_norm + silu nodes of
+   src/conformer.cpp:112-154. */
+pkc_status pkc_conv_depthwise(const void* in, const int* lens, int B, int d, int K, const float* w,
+                              const float* bias, const float* scale, const float* shift, int dtype,
+                              void* out, void* stream);
+
 /* Failure detection check: runs this library's bounded-wait helpers (every
    mbarrier wait and cross-CTA flag wait of its kernels uses them) on a
    condition that never comes true -- kind 0: an mbarrier no thread arrives

@@ -4,6 +4,7 @@
 // directly (encoder.cpp).
 #include <cuda_runtime.h>
 
+#include <algorithm>
 #include <mutex>
 #include <string>
 
@@ -226,4 +227,33 @@ extern "C" pkc_status pkc_relpos_attention_f32(const float* qkv, const float* pt
   return attention_call("pkc_relpos_attention_f32", qkv, ptab, centre, bias_u, bias_v, lens, B, d, n_heads, ctx, stream,
                         pkc::attn_f32_query_tile(),
                         [](const pkc::AttnArgs& a, cudaStream_t st) { return pkc::attention_f32_launch(a, st); });
+}
+
+extern "C" pkc_status pkc_conv_depthwise(const void* in, const int* lens, int B, int d, int K, const float* w,
+                                         const float* bias, const float* scale, const float* shift, int dtype,
+                                         void* out, void* stream) {
+  if (!in || !lens || B <= 0 || !w || !scale || !shift || !out || (dtype != 0 && dtype != 1))
+    return pkc::set_thread_error(PKC_ERR_ARG, "pkc_conv_depthwise: bad arguments");
+  std::vector<int> host(2 * B + 1, 0);  // [off | len]
+  int max_len = 0;
+  for (int b = 0; b < B; ++b) {
+    if (lens[b] < 0) return pkc::set_thread_error(PKC_ERR_ARG, "pkc_conv_depthwise: negative length");
+    host[b + 1] = host[b] + lens[b];
+    host[B + 1 + b] = lens[b];
+    max_len = std::max(max_len, lens[b]);
+  }
+  if (host[B] == 0) return PKC_OK;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  int* dtab = nullptr;
+  if (cudaMalloc(&dtab, host.size() * sizeof(int)) != cudaSuccess)
+    return pkc::set_thread_error(PKC_ERR_OOM, "pkc_conv_depthwise: table allocation failed");
+  cudaMemcpyAsync(dtab, host.data(), host.size() * sizeof(int), cudaMemcpyHostToDevice, st);
+  cudaError_t e = pkc::dwconv_bn_silu_launch(in, out, d, K, w, bias, scale, shift, dtab, dtab + B + 1, B, max_len,
+                                             dtype == 1, st);
+  cudaError_t e2 = cudaStreamSynchronize(st);
+  cudaFree(dtab);
+  if (e != cudaSuccess || e2 != cudaSuccess)
+    return pkc::set_thread_error(PKC_ERR_CUDA, std::string("pkc_conv_depthwise: ") +
+                                                   cudaGetErrorString(e != cudaSuccess ? e : e2));
+  return PKC_OK;
 }

@@ -141,6 +141,8 @@ def _declare(L):
         ("pkc_relpos_attention_f32", c_int, c_void_p, c_void_p, c_int, c_void_p, c_void_p, POINTER(c_int),
          c_int, c_int, c_int, c_void_p, c_void_p),
         ("pkc_bounded_wait_check", c_int, c_int, ctypes.c_double, POINTER(c_int)),
+        ("pkc_conv_depthwise", c_int, c_void_p, POINTER(c_int), c_int, c_int, c_int, c_void_p, c_void_p,
+         c_void_p, c_void_p, c_int, c_void_p, c_void_p),
     ]
     for name, res, *args in optional:
         if hasattr(L, name):
@@ -231,6 +233,14 @@ def relpos_attention(qkv, ptab, centre, bias_u, bias_v, lens, d, n_heads, *, bf1
     _check(lib().pkc_relpos_attention(c_void_p(qkv), c_void_p(ptab), centre, c_void_p(bias_u),
                                       c_void_p(bias_v), _ints(lens), len(lens), d, n_heads,
                                       1 if bf16 else 0, c_void_p(ctx), c_void_p(stream) if stream else None))
+
+
+def conv_depthwise(x, lens, d, K, w, bias, scale, shift, *, bf16, out, stream=0):
+    """Conv module depthwise stage (depthwise Conv1d + bias, folded BatchNorm,
+    SiLU) on packed rows; device pointers as ints, bias may be 0."""
+    _check(lib().pkc_conv_depthwise(c_void_p(x), _ints(lens), len(lens), d, K, c_void_p(w),
+                                    c_void_p(bias) if bias else None, c_void_p(scale), c_void_p(shift),
+                                    1 if bf16 else 0, c_void_p(out), c_void_p(stream) if stream else None))
 
 
 def relpos_attention_noalloc(qkv, ptab, centre, bias_u, bias_v, lens, d, n_heads, *, bf16, ctx,

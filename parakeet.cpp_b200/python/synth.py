@@ -47,6 +47,10 @@ class ModelCfg:
     dtype: str = "f32"          # f32 | f16 | bf16 | q8_0 | q4_k
     biases: bool = False
     xscaling: bool = False
+    # LayerNorm affines of the conformer layers: gamma 1 + N(0, 0.1), beta
+    # N(0, 0.05) instead of the BASELINE init's (1, 0), so that the parity
+    # tests see a non-trivial LayerNorm scale and shift
+    ln_affine: bool = False
     n_fft: int = 512
     win_length: int = 400
     hop_length: int = 160
@@ -58,6 +62,8 @@ class ModelCfg:
             del items["pred_layers"]
         if not items["streaming"]:
             del items["streaming"]
+        if not items["ln_affine"]:
+            del items["ln_affine"]
         h = hashlib.sha1(repr(sorted(items.items())).encode()).hexdigest()[:12]
         return f"{self.name}_{self.dtype}_{h}"
 
@@ -214,8 +220,12 @@ def model_tensors(cfg: ModelCfg):
     for li in range(cfg.n_layers):
         p = f"encoder.layers.{li}."
         for ln in ("norm_feed_forward1", "norm_self_att", "norm_conv", "norm_feed_forward2", "norm_out"):
-            yield p + ln + ".weight", ones(d)
-            yield p + ln + ".bias", zeros(d)
+            if cfg.ln_affine:
+                yield p + ln + ".weight", ones(d) + nrm(d) * np.float32(5.0)
+                yield p + ln + ".bias", nrm(d) * np.float32(2.5)
+            else:
+                yield p + ln + ".weight", ones(d)
+                yield p + ln + ".bias", zeros(d)
         for ff in ("feed_forward1", "feed_forward2"):
             yield p + ff + ".linear1.weight", nrm(cfg.ff_dim, d)
             if cfg.biases:

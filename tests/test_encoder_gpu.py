@@ -25,7 +25,7 @@ def rel_err(got, ref):
 
 
 # per-element bound of each model kind (f32 weights: the f32-accurate path)
-RTOL = {"f32_bias": 1e-3, "f32_xs": 1e-3}
+RTOL = {"f32_bias": 1e-3, "f32_xs": 1e-3, "f32_ln": 1e-3}
 
 
 @pytest.fixture(scope="session")
@@ -41,6 +41,12 @@ def models(tmp_path_factory):
         # parakeet.encoder.xscaling is set (src/encoder.cpp:59-61,123)
         "f32_xs": synth.small_cfg("c1_110m", xscaling=True, **small),
         "bf16": synth.small_cfg("c5_0.6b_bf16_long", n_mels=128, **small),
+        # non-trivial LayerNorm gamma / beta (the BASELINE init has 1 / 0)
+        "f16_ln": synth.small_cfg("c2_0.6b_f16", n_mels=80, ln_affine=True, **small),
+        "bf16_ln": synth.small_cfg("c5_0.6b_bf16_long", n_mels=128, ln_affine=True, **small),
+        "q8_ln": synth.small_cfg("c3_0.6b_q8", n_mels=80, ln_affine=True, **small),
+        "q4_ln": synth.small_cfg("c4_1.1b_q4k", n_mels=128, ln_affine=True, **small),
+        "f32_ln": synth.small_cfg("c1_110m", ln_affine=True, **small),
         "q8_0": synth.small_cfg("c3_0.6b_q8", n_mels=80, **small),
         "q4_k": synth.small_cfg("c4_1.1b_q4k", n_mels=128, **small),
         "dk128": synth.small_cfg("c2_0.6b_f16", n_layers=2, d_model=512, n_heads=4, ff_dim=1024,
@@ -97,7 +103,8 @@ def test_mel_front_end_matches_oracle(opened, oracles):
     assert np.abs(got - ref_fft).max() < 2e-3
 
 
-@pytest.mark.parametrize("kind", ["f16", "f32_bias", "f32_xs", "bf16", "q8_0", "q4_k", "dk128"])
+@pytest.mark.parametrize("kind", ["f16", "f32_bias", "f32_xs", "bf16", "q8_0", "q4_k", "dk128", "f16_ln", "bf16_ln",
+                                  "q8_ln", "q4_ln", "f32_ln"])
 def test_encoder_matches_oracle(opened, oracles, kind):
     import oracle
     from parity import max_rel_err
