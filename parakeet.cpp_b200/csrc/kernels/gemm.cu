@@ -57,17 +57,19 @@ __device__ __forceinline__ void kb_cols(const GemmArgs& a, int kb, int& ca, int&
 // row r at (c ^ (r & 7)), conflict-free both ways -- and leaves with lanes
 // laid along the rows: each instruction then covers 4 rows x 128 bytes.
 // Every lane executes the TMEM loads (.sync.aligned); only rows < M store.
-template <typename H, int EPI>
+template <typename H, int EPI, int TBN = BN>
 __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t trow, int row0, int n0,
                                               int half, uint8_t* stage) {
   constexpr bool PAIRED = EPI == EPI_GLU_H || EPI == EPI_POWER_F32;
+  // the paired epilogues read value and gate columns of one 256-wide tile
+  static_assert(TBN == BN || !PAIRED, "paired epilogues need 256-column tiles");
   const int lane = threadIdx.x & 31;
   const int rr = lane >> 3, cc = lane & 7;  // coalesced layout: rows 4k + rr, 16-byte chunk cc
   const uint32_t sst = smem_u32(stage);
   // output chunk j: columns [32j, 32j + 32) of the output tile (PAIRED: value
   // columns 32j and gate columns BN/2 + 32j of the accumulator)
-  const int j0 = PAIRED ? half * (BN / 128) : half * (BN / 64);
-  const int j1 = PAIRED ? j0 + BN / 128 : j0 + BN / 64;
+  const int j0 = PAIRED ? half * (BN / 128) : half * (TBN / 64);
+  const int j1 = PAIRED ? j0 + BN / 128 : j0 + TBN / 64;
   const int oc0 = PAIRED ? n0 / 2 : n0;  // output column of chunk 0
   float4 cur[8], nxt[8];
   // EPI_RESID_F32 with stats: lane (rr, cc) merges row 4 * cc + rr's chunk
@@ -528,10 +530,16 @@ __device__ __forceinline__ void sk_fixup(const GemmArgs& args, uint32_t trow, in
     for (int i = 1; i <= n; ++i) args.sk_flags[slot + i * 2 * EPI_WARPS] = 0;
 }
 
-template <typename H, int EPI, bool SK>
+// TBN = 128: pair tiles of 256 x 128 (each CTA stages 64 rows of B) for
+// GEMMs whose 256-wide tiles would fill at most half of the SM pairs (the
+// encoder's N = 1024 GEMMs on a few utterances); whole tiles, no row
+// statistics, no paired epilogue.
+template <typename H, int EPI, bool SK, int TBN = BN>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
     k_gemm_tc2(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                GemmArgs args) {
+  static_assert(TBN == BN || (TBN == 128 && !SK), "128-column pair tiles are whole tiles only");
+  constexpr int TB2 = (TBN / 2) * BK * 2;  // this CTA's B rows per stage
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem =
       reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -550,7 +558,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   const int npairs = gridDim.x >> 1;
   const int KB = args.K / BK;
   const int tiles_m = (args.M + 2 * HALF_ROWS - 1) / (2 * HALF_ROWS);
-  const int tiles_n = args.N / BN;
+  const int tiles_n = args.N / TBN;
   const int n_tiles = tiles_m * tiles_n;
   const bool nfast = args.M > args.N;
   // the stream-K instantiation (SK) falls back to whole tiles if W < P
@@ -586,7 +594,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       int tile, kb0, kb1;
       while (ok && sg.next(tile, kb0, kb1)) {
         const int m0 = tile_mb(tile, tiles_m, tiles_n, nfast) * 2 * HALF_ROWS + (int)rank * HALF_ROWS;
-        const int n0 = tile_nb(tile, tiles_m, tiles_n, nfast) * BN + (int)rank * HALF_ROWS;
+        const int n0 = tile_nb(tile, tiles_m, tiles_n, nfast) * TBN + (int)rank * (TBN / 2);
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES2;
           const uint32_t ph = (it / STAGES2) & 1u;
@@ -595,7 +603,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
             break;
           }
           const uint32_t full_leader = mapa_shared(smem_u32(&bars[s]), 0);
-          if (leader) mbar_arrive_expect_tx(smem_u32(&bars[s]), 2 * (A2_BYTES + B2_BYTES));
+          if (leader) mbar_arrive_expect_tx(smem_u32(&bars[s]), 2 * (A2_BYTES + TB2));
           int ca, cb;
           kb_cols(args, kb, ca, cb);
           tma_load_2d_2sm(smem_u32(sA + s * A2_BYTES), &tmA, full_leader, ca, m0);
@@ -606,7 +614,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
   } else if (warp == 1) {
     if (lane == 0 && leader) {
       // ---- MMA issuer (leader CTA only)
-      constexpr uint32_t idesc = idesc_f16(2 * HALF_ROWS, BN, is_bf16<H>::value ? 1 : 0);
+      constexpr uint32_t idesc = idesc_f16(2 * HALF_ROWS, TBN, is_bf16<H>::value ? 1 : 0);
       uint32_t it = 0;
       int local = 0;
       bool ok = true;
@@ -619,7 +627,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
                        DEV_ERR_TIMEOUT_ACCUM))
           break;
         tc_fence_after();
-        const uint32_t acc = tmem + (uint32_t)(buf * BN);
+        const uint32_t acc = tmem + (uint32_t)(buf * TBN);
         for (int kb = kb0; kb < kb1; ++kb, ++it) {
           const int s = it % STAGES2;
           const uint32_t ph = (it / STAGES2) & 1u;
@@ -659,8 +667,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
       if (!have) break;
       tc_fence_after();
       const int m0 = tile_mb(tile, tiles_m, tiles_n, nfast) * 2 * HALF_ROWS + (int)rank * HALF_ROWS;
-      const int n0 = tile_nb(tile, tiles_m, tiles_n, nfast) * BN;
-      const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * BN);
+      const int n0 = tile_nb(tile, tiles_m, tiles_n, nfast) * TBN;
+      const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(buf * TBN);
       if (SK && kb0 > 0) {
         sk_spill<EPI>(args, trow, half, slot);  // partial sum of a split tile
       } else {
@@ -668,7 +676,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(THREADS, 1)
         // start inside the tile hold its remaining k-blocks
         if (SK && kb1 < KB)
           sk_fixup<EPI>(args, trow, half, slot, pair, npairs, (long long)n_tiles * KB, (long long)(tile + 1) * KB);
-        epilogue_tile<H, EPI>(args, trow, m0 + q * 32, n0, half, sE + (warp - 2) * EPI_STAGE_BYTES);
+        epilogue_tile<H, EPI, TBN>(args, trow, m0 + q * 32, n0, half, sE + (warp - 2) * EPI_STAGE_BYTES);
       }
       tc_fence_before();
       __syncwarp();
@@ -1297,6 +1305,34 @@ static cudaError_t launch_t2(const CUtensorMap& ta, const CUtensorMap& tb, const
   return launch_pdl(kern, dim3(2 * pairs), dim3(THREADS), SMEM2_BYTES, st, ta, tb, a);
 }
 
+// 256 x 128 pair tiles (k_gemm_tc2<.., TBN = 128>); tb's box is 64 rows.
+template <typename H, int EPI>
+static cudaError_t launch_t2n(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a, int n_tiles,
+                              cudaStream_t st) {
+  auto kern = k_gemm_tc2<H, EPI, false, 128>;
+  static PerDevice once;
+  int unused = 0;
+  const cudaError_t ae = per_device(once, &unused, [&](int, int&) {
+    return cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES);
+  });
+  if (ae != cudaSuccess) return ae;
+  return launch_pdl(kern, dim3(2 * n_tiles), dim3(THREADS), SMEM2_BYTES, st, ta, tb, a);
+}
+
+// SM pairs of the current device (cached per device)
+static int device_sm_pairs() {
+  static PerDevice pd;
+  int v = 0;
+  if (per_device(pd, &v, [](int dev, int& n) {
+        int sms = 0;
+        const cudaError_t e = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        n = sms / 2;
+        return e;
+      }) != cudaSuccess)
+    return 0;
+  return v;
+}
+
 template <typename H, int EPI>
 static cudaError_t launch_t(const CUtensorMap& ta, const CUtensorMap& tb, const GemmArgs& a,
                             cudaStream_t st) {
@@ -1455,6 +1491,16 @@ bool gemm_splitk_enabled() {
 }
 
 // PKC_GEMM_1SM=1 forces the 1-SM kernel (for A/B comparisons)
+// PKC_GEMM_NARROW=0: never the 256 x 128 pair tiles
+static bool gemm_narrow_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("PKC_GEMM_NARROW");
+    v = (e && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
+}
+
 bool gemm_2sm_enabled() {
   static int v = -1;
   if (v < 0) {
@@ -1723,9 +1769,36 @@ cudaError_t gemm_launch(const void* A, int lda, const void* B, int ldb, bool bf1
   // 2-SM tiles once there are at least two 128-row blocks of A
   const bool two_sm = args.M > BM && gemm_2sm_enabled();
   const int box = two_sm ? HALF_ROWS : 0;
+  // 256 x 128 pair tiles when the 256-wide ones would fill at most half of
+  // the SM pairs (twice the tiles at about 0.8 of the per-tile rate: their
+  // shared-memory traffic per MMA is higher), for the unpaired epilogues
+  // without row statistics. A row's sums run in the same order either way.
+  bool narrow = false;
+  int n_narrow = 0;
+  if (two_sm && gemm_narrow_enabled() && !gemm_splitk_enabled() && !args.stats && !args.split_k &&
+      args.N % 128 == 0 && (args.epi == EPI_STORE_H || args.epi == EPI_RESID_F32 || args.epi == EPI_STORE_F32)) {
+    const long long rows = (args.M + 2 * HALF_ROWS - 1) / (2 * HALF_ROWS);
+    const long long t256 = (long long)(args.N / BN) * rows;
+    const int pairs = device_sm_pairs();
+    narrow = pairs > 0 && 2 * t256 <= pairs;
+    n_narrow = (int)(rows * (args.N / 128));
+  }
   CUtensorMap ta, tb;
   if (!make_tmap_kmajor(&ta, A, args.M, kmap, lda, two_sm ? box : BM, bf16)) return cudaErrorInvalidValue;
-  if (!make_tmap_kmajor(&tb, B, args.N, kmap, ldb, two_sm ? box : BN, bf16)) return cudaErrorInvalidValue;
+  if (!make_tmap_kmajor(&tb, B, args.N, kmap, ldb, narrow ? 64 : two_sm ? box : BN, bf16)) return cudaErrorInvalidValue;
+  if (narrow) {
+    switch (args.epi) {
+#define PKC_GEMM_NARROW(E) \
+  case E:                  \
+    return bf16 ? launch_t2n<__nv_bfloat16, E>(ta, tb, args, n_narrow, st) : launch_t2n<__half, E>(ta, tb, args, n_narrow, st);
+      PKC_GEMM_NARROW(EPI_STORE_H)
+      PKC_GEMM_NARROW(EPI_RESID_F32)
+      PKC_GEMM_NARROW(EPI_STORE_F32)
+#undef PKC_GEMM_NARROW
+      default:
+        return cudaErrorInvalidValue;
+    }
+  }
   switch (args.epi) {
 #define PKC_GEMM_CASE(E)                                                                   \
   case E:                                                                                  \

@@ -310,3 +310,28 @@ def test_skinny_epilogues(cuda, bf16, M, epi):
     torch.cuda.synchronize()
     err = (got - want).abs().max().item() / want.abs().max().item()
     assert err < tol, err
+
+
+@pytest.mark.parametrize("epi", ["store_h", "resid_f32", "store_f32"])
+def test_narrow_tiles_match_wide_tiles_bitwise(cuda, epi):
+    """A GEMM whose 256-wide pair tiles would fill at most half of the SM pairs
+    runs 256 x 128 pair tiles; a row's sums run in the same order in both, so
+    the rows of a small-M call equal the same rows of a large-M call (wide
+    tiles) bit for bit -- a clip's encoder output does not depend on how
+    many clips share its batch."""
+    import torch
+    import pkc
+    N, K, Ms, Mb = 1024, 1024, 700, 20000
+    A, B, bias, _ = _setup(Mb, N, K, torch.float16, seed=5)
+    e = {"store_h": pkc.EPI_STORE_H, "resid_f32": pkc.EPI_RESID_F32, "store_f32": pkc.EPI_STORE_F32}[epi]
+    dt = torch.float16 if epi == "store_h" else torch.float32
+    g = torch.Generator(device="cpu").manual_seed(6)
+    x0 = torch.randn(Mb, N, generator=g).to(dt).to(cuda)
+    outs = []
+    for M in (Ms, Mb):
+        out = x0[:M].clone()
+        pkc.gemm(A.data_ptr(), B.data_ptr(), M, N, K, bf16=False, epi=e, alpha=0.5, bias=bias.data_ptr(),
+                 out=out.data_ptr(), ldo=N)
+        torch.cuda.synchronize()
+        outs.append(out)
+    assert torch.equal(outs[0], outs[1][:Ms])
