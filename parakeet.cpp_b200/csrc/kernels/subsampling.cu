@@ -143,6 +143,35 @@ constexpr int S1_ROWS = 2 * S1_T2 + 1;
 constexpr int S1_MROWS = 4 * S1_T2 + 3;
 constexpr int S1_THREADS = 256;
 
+// relu(a), relu(b) rounded to bf16 and packed (a in the low half), one instruction
+__device__ __forceinline__ uint32_t pack_relu_bf16(float a, float b) {
+  uint32_t d;
+  asm("cvt.rn.relu.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(b), "f"(a));
+  return d;
+}
+// two bf16 (low, high halves of u) as the two f32 lanes of a 64-bit register
+__device__ __forceinline__ uint64_t bf2_to_f2(uint32_t u) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "r"(u << 16), "r"(u & 0xffff0000u));
+  return d;
+}
+// d = a * b + c in each f32 lane (fma.rn, as fmaf)
+__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+  return d;
+}
+__device__ __forceinline__ uint32_t f2_to_bf2(uint64_t v) {
+  uint32_t lo, hi;
+  asm("mov.b64 {%0, %1}, %2;" : "=r"(lo), "=r"(hi) : "l"(v));
+  return pack2<__nv_bfloat16>(__uint_as_float(lo), __uint_as_float(hi));
+}
+
 __device__ __forceinline__ void mma16816_f16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
   asm volatile(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
@@ -233,15 +262,17 @@ __global__ void __launch_bounds__(S1_THREADS)
       const bool live1 = p1 < NP && t1_0 + p1 / F1 >= 0 && t1_0 + p1 / F1 < v1b;
 #pragma unroll
       for (int nt = 0; nt < NT; ++nt) {
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        // the bias is the accumulator's starting value (as in the CUDA-core
+        // conv.0, which starts its sum at the bias); ReLU in the bf16 rounding
+        float acc[4] = {bias[nt][0], bias[nt][1], bias[nt][0], bias[nt][1]};
         mma16816_f16(acc, a, bf[nt][0], bf[nt][1]);
         // (position, 8-channel chunk nt) at chunk slot nt ^ (f1 & 7) of the position's 128-byte row
         if (p0 < NP) {
-          const uint32_t v = live0 ? pack2<__nv_bfloat16>(fmaxf(acc[0] + bias[nt][0], 0.f), fmaxf(acc[1] + bias[nt][1], 0.f)) : 0u;
+          const uint32_t v = live0 ? pack_relu_bf16(acc[0], acc[1]) : 0u;
           *reinterpret_cast<uint32_t*>(s1 + (size_t)p0 * (S1_CG * 2) + ((nt ^ ((p0 % F1) & 7)) << 4) + 4 * t4) = v;
         }
         if (p1 < NP) {
-          const uint32_t v = live1 ? pack2<__nv_bfloat16>(fmaxf(acc[2] + bias[nt][0], 0.f), fmaxf(acc[3] + bias[nt][1], 0.f)) : 0u;
+          const uint32_t v = live1 ? pack_relu_bf16(acc[2], acc[3]) : 0u;
           *reinterpret_cast<uint32_t*>(s1 + (size_t)p1 * (S1_CG * 2) + ((nt ^ ((p1 % F1) & 7)) << 4) + 4 * t4) = v;
         }
       }
@@ -251,28 +282,28 @@ __global__ void __launch_bounds__(S1_THREADS)
 
   // 3. depthwise 3x3 s2 p1 + bias: thread = 8 channels (chunk ch) of positions
   //    (frame tt, f2) = pos, pos + 32, ...
+  // taps and bias as channel pairs: the sums run two channels per
+  // instruction (fma.rn.f32x2), each lane exactly as fmaf
   const int ch = tid & 7;
   const int c = cg0 + ch * 8;
-  float wk[9][8], bi[8];
+  uint64_t wk[9][4], bi[4];
 #pragma unroll
   for (int k = 0; k < 9; ++k) {
     const float4 wa = __ldg(reinterpret_cast<const float4*>(w1 + (size_t)k * C + c));
     const float4 wb = __ldg(reinterpret_cast<const float4*>(w1 + (size_t)k * C + c + 4));
-    wk[k][0] = wa.x; wk[k][1] = wa.y; wk[k][2] = wa.z; wk[k][3] = wa.w;
-    wk[k][4] = wb.x; wk[k][5] = wb.y; wk[k][6] = wb.z; wk[k][7] = wb.w;
+    wk[k][0] = f2_pack(wa.x, wa.y); wk[k][1] = f2_pack(wa.z, wa.w);
+    wk[k][2] = f2_pack(wb.x, wb.y); wk[k][3] = f2_pack(wb.z, wb.w);
   }
   {
     const float4 ba = __ldg(reinterpret_cast<const float4*>(b1 + c));
     const float4 bb = __ldg(reinterpret_cast<const float4*>(b1 + c + 4));
-    bi[0] = ba.x; bi[1] = ba.y; bi[2] = ba.z; bi[3] = ba.w; bi[4] = bb.x; bi[5] = bb.y; bi[6] = bb.z; bi[7] = bb.w;
+    bi[0] = f2_pack(ba.x, ba.y); bi[1] = f2_pack(ba.z, ba.w); bi[2] = f2_pack(bb.x, bb.y); bi[3] = f2_pack(bb.z, bb.w);
   }
   __nv_bfloat16* ob = out + (size_t)t.v2_off[b] * F2 * C;
   for (int pos = tid >> 3; pos < S1_T2 * F2; pos += S1_THREADS / 8) {
     const int tt = pos / F2, f2 = pos % F2;
     if (t2_0 + tt >= v2b) break;
-    float acc[8];
-#pragma unroll
-    for (int e = 0; e < 8; ++e) acc[e] = bi[e];
+    uint64_t acc[4] = {bi[0], bi[1], bi[2], bi[3]};
 #pragma unroll
     for (int kh = 0; kh < 3; ++kh) {
 #pragma unroll
@@ -281,16 +312,16 @@ __global__ void __launch_bounds__(S1_THREADS)
         if (f1 < 0 || f1 >= F1) continue;
         const int p = (2 * tt + kh) * F1 + f1;
         const uint4 raw = *reinterpret_cast<const uint4*>(s1 + (size_t)p * (S1_CG * 2) + ((ch ^ (f1 & 7)) << 4));
-        const __nv_bfloat16* hv = reinterpret_cast<const __nv_bfloat16*>(&raw);
+        const uint32_t rv[4] = {raw.x, raw.y, raw.z, raw.w};
 #pragma unroll
-        for (int e = 0; e < 8; ++e) acc[e] = fmaf(wk[kh * 3 + kw][e], __bfloat162float(hv[e]), acc[e]);
+        for (int e = 0; e < 4; ++e) acc[e] = ffma2(wk[kh * 3 + kw][e], bf2_to_f2(rv[e]), acc[e]);
       }
     }
     uint4 o;
-    o.x = pack2<__nv_bfloat16>(acc[0], acc[1]);
-    o.y = pack2<__nv_bfloat16>(acc[2], acc[3]);
-    o.z = pack2<__nv_bfloat16>(acc[4], acc[5]);
-    o.w = pack2<__nv_bfloat16>(acc[6], acc[7]);
+    o.x = f2_to_bf2(acc[0]);
+    o.y = f2_to_bf2(acc[1]);
+    o.z = f2_to_bf2(acc[2]);
+    o.w = f2_to_bf2(acc[3]);
     *reinterpret_cast<uint4*>(ob + ((size_t)(t2_0 + tt) * F2 + f2) * C + c) = o;
   }
 }
