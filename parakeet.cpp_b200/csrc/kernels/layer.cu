@@ -188,18 +188,24 @@ __global__ void __launch_bounds__(DW_THREADS)
     pdl_trigger();
     return;
   }
-  // the taps and the folded BatchNorm: before the dependency wait
-  float2 wk[K];
+  // the taps and the folded BatchNorm: before the dependency wait. The
+  // thread's two channels ride in the two lanes of the packed FMA
+  // (fma.rn.f32x2: each lane rounded as fmaf), half the FMA instructions.
+  uint64_t wk[K];
 #pragma unroll
-  for (int k = 0; k < K; ++k) wk[k] = __ldg(reinterpret_cast<const float2*>(w + (size_t)k * d + c0));
-  const float2 sc = __ldg(reinterpret_cast<const float2*>(scale + c0));
-  float2 sh = __ldg(reinterpret_cast<const float2*>(shift + c0));
+  for (int k = 0; k < K; ++k) {
+    const float2 v = __ldg(reinterpret_cast<const float2*>(w + (size_t)k * d + c0));
+    wk[k] = f2_pack(v.x, v.y);
+  }
+  const float2 scf = __ldg(reinterpret_cast<const float2*>(scale + c0));
+  float2 shf = __ldg(reinterpret_cast<const float2*>(shift + c0));
   if (bias) {
     // (acc + bias) * scale + shift = acc * scale + (bias * scale + shift)
     const float2 bi = __ldg(reinterpret_cast<const float2*>(bias + c0));
-    sh.x = fmaf(bi.x, sc.x, sh.x);
-    sh.y = fmaf(bi.y, sc.y, sh.y);
+    shf.x = fmaf(bi.x, scf.x, shf.x);
+    shf.y = fmaf(bi.y, scf.y, shf.y);
   }
+  const uint64_t sc = f2_pack(scf.x, scf.y), sh = f2_pack(shf.x, shf.y);
   pdl_wait();
   pdl_trigger();
   constexpr int pad = (K - 1) / 2;
@@ -210,13 +216,16 @@ __global__ void __launch_bounds__(DW_THREADS)
     return (ti >= 0 && ti < T) ? __ldg(reinterpret_cast<const uint32_t*>(x + (size_t)ti * d)) : 0u;
   };
   // window rows: frames t - pad .. t - pad + NR - 1 of the chunk starting at t
-  float2 xf[NR];
+  uint64_t xf[NR];
   {
     uint32_t raw[NR];
 #pragma unroll
     for (int r = 0; r < NR; ++r) raw[r] = row(t0 - pad + r);
 #pragma unroll
-    for (int r = 0; r < NR; ++r) xf[r] = H2<H>::to_f2(raw[r]);
+    for (int r = 0; r < NR; ++r) {
+      const float2 v = H2<H>::to_f2(raw[r]);
+      xf[r] = f2_pack(v.x, v.y);
+    }
   }
 #pragma unroll 1
   for (int c = 0; c < DW_CHUNKS; ++c) {
@@ -233,20 +242,20 @@ __global__ void __launch_bounds__(DW_THREADS)
 #pragma unroll
     for (int f = 0; f < DW_FRAMES; ++f) {
       if (f >= nf) break;
-      float a0 = 0.f, a1 = 0.f;
+      uint64_t a = 0ull;  // (+0, +0)
 #pragma unroll
-      for (int k = 0; k < K; ++k) {
-        a0 = fmaf(wk[k].x, xf[f + k].x, a0);
-        a1 = fmaf(wk[k].y, xf[f + k].y, a1);
-      }
-      *reinterpret_cast<uint32_t*>(y + (size_t)(tc + f) * d) =
-          pack2<H>(siluf_(fmaf(a0, sc.x, sh.x)), siluf_(fmaf(a1, sc.y, sh.y)));
+      for (int k = 0; k < K; ++k) a = ffma2(wk[k], xf[f + k], a);
+      const float2 v = f2_unpack(ffma2(a, sc, sh));
+      *reinterpret_cast<uint32_t*>(y + (size_t)(tc + f) * d) = pack2<H>(siluf_(v.x), siluf_(v.y));
     }
     if (more) {
 #pragma unroll
       for (int r = 0; r < K - 1; ++r) xf[r] = xf[r + DW_FRAMES];
 #pragma unroll
-      for (int r = 0; r < DW_FRAMES; ++r) xf[K - 1 + r] = H2<H>::to_f2(nraw[r]);
+      for (int r = 0; r < DW_FRAMES; ++r) {
+        const float2 v = H2<H>::to_f2(nraw[r]);
+        xf[K - 1 + r] = f2_pack(v.x, v.y);
+      }
     }
   }
 }

@@ -155,21 +155,9 @@ __device__ __forceinline__ uint64_t bf2_to_f2(uint32_t u) {
   asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "r"(u << 16), "r"(u & 0xffff0000u));
   return d;
 }
-// d = a * b + c in each f32 lane (fma.rn, as fmaf)
-__device__ __forceinline__ uint64_t ffma2(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t d;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
-  return d;
-}
-__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
-  uint64_t d;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
-  return d;
-}
 __device__ __forceinline__ uint32_t f2_to_bf2(uint64_t v) {
-  uint32_t lo, hi;
-  asm("mov.b64 {%0, %1}, %2;" : "=r"(lo), "=r"(hi) : "l"(v));
-  return pack2<__nv_bfloat16>(__uint_as_float(lo), __uint_as_float(hi));
+  const float2 f = f2_unpack(v);
+  return pack2<__nv_bfloat16>(f.x, f.y);
 }
 
 __device__ __forceinline__ void mma16816_f16(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
