@@ -561,25 +561,50 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bar(B_PVDONE + ((nT - 1) & 1)), ((uint32_t)(nT - 1) >> 1) & 1u,
                                                   p.err, DEV_ERR_TIMEOUT_ATTN)) != 0;
+    // Epilogue: O / l rounded to the operand type, staged through the (now
+    // idle) Q tile as [QM rows x DK] with 16-byte chunk c of row r at
+    // c ^ (r & 7) (conflict-free both ways), then stored by all 8 softmax
+    // warps with the lanes along the rows: each instruction writes whole
+    // rows instead of one 16-byte piece of 32 rows.
+    constexpr int CH = DK / 8;  // 16-byte chunks per row
+    uint8_t* stile = sm + L::OFF_QU;
     if (ok) {
       tc_fence_after();
       const float inv = 1.0f / lsum;
-      const bool store = q0 + i < T;
-      H* dst = reinterpret_cast<H*>(p.ctx) + (size_t)(off + q0 + i) * p.d + head * DK;
 #pragma unroll 1
       for (int c = hh * (DK / 64); c < (hh + 1) * (DK / 64); ++c) {
         uint32_t o[32];
         tmem_ld32(trow + TM_O + 32u * c, o);
         tmem_ld_wait();
-        if (store) {
-          uint4* d4 = reinterpret_cast<uint4*>(dst + 32 * c);
 #pragma unroll
-          for (int k = 0; k < 4; ++k)
-            d4[k] = make_uint4(pack2<H>(__uint_as_float(o[8 * k]) * inv, __uint_as_float(o[8 * k + 1]) * inv),
-                               pack2<H>(__uint_as_float(o[8 * k + 2]) * inv, __uint_as_float(o[8 * k + 3]) * inv),
-                               pack2<H>(__uint_as_float(o[8 * k + 4]) * inv, __uint_as_float(o[8 * k + 5]) * inv),
-                               pack2<H>(__uint_as_float(o[8 * k + 6]) * inv, __uint_as_float(o[8 * k + 7]) * inv));
+        for (int k = 0; k < 4; ++k) {
+          const int ch = 4 * c + k;  // chunk of this row
+          *reinterpret_cast<uint4*>(stile + i * (DK * 2) + ((ch ^ (i & 7)) << 4)) =
+              make_uint4(pack2<H>(__uint_as_float(o[8 * k]) * inv, __uint_as_float(o[8 * k + 1]) * inv),
+                         pack2<H>(__uint_as_float(o[8 * k + 2]) * inv, __uint_as_float(o[8 * k + 3]) * inv),
+                         pack2<H>(__uint_as_float(o[8 * k + 4]) * inv, __uint_as_float(o[8 * k + 5]) * inv),
+                         pack2<H>(__uint_as_float(o[8 * k + 6]) * inv, __uint_as_float(o[8 * k + 7]) * inv));
         }
+      }
+    }
+    // every softmax thread arrives here exactly once (no path leaves the
+    // branch early); the tile is stored only if all of them had it ready
+    uint32_t all_ok;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
+        "bar.red.and.pred q, 1, %2, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(all_ok)
+        : "r"(ok ? 1u : 0u), "r"(32 * SM_WARPS)
+        : "memory");
+    if (all_ok) {
+      const int t = threadIdx.x - 64;  // 0 .. 32 * SM_WARPS - 1
+      H* base = reinterpret_cast<H*>(p.ctx) + (size_t)(off + q0) * p.d + head * DK;
+#pragma unroll
+      for (int k = 0; k < QM * CH / (32 * SM_WARPS); ++k) {
+        const int idx = t + 32 * SM_WARPS * k;
+        const int r = idx / CH, c = idx % CH;
+        const uint4 v = *reinterpret_cast<const uint4*>(stile + r * (DK * 2) + ((c ^ (r & 7)) << 4));
+        if (q0 + r < T) *reinterpret_cast<uint4*>(base + (size_t)r * p.d + 8 * c) = v;
       }
     }
   }
