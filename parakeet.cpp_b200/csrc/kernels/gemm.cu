@@ -80,10 +80,17 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t tro
     return reinterpret_cast<float4*>(reinterpret_cast<float*>(args.out) + (size_t)(row0 + 4 * k + rr) * args.ldo +
                                      oc0 + 32 * j + 4 * cc);
   };
+  // EPI_RESID_F32 without statistics adds alpha (acc + bias) to the residual
+  // with a vector reduction in L2 (red.global.add.v4.f32: one update per
+  // element, so the sums are those of load + add + store) and loads nothing;
+  // with statistics the updated rows are needed here, so they are loaded
+  const bool rload = EPI == EPI_RESID_F32 && args.stats != nullptr;
   if constexpr (EPI == EPI_RESID_F32) {
+    if (rload) {
 #pragma unroll
-    for (int k = 0; k < 8; ++k)
-      if (row_ok(k)) cur[k] = *resid(j0, k);
+      for (int k = 0; k < 8; ++k)
+        if (row_ok(k)) cur[k] = *resid(j0, k);
+    }
   }
 #pragma unroll 1
   for (int j = j0; j < j1; ++j) {
@@ -112,7 +119,7 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t tro
       tmem_ld32(trow + 32 * j, r);
       if constexpr (EPI == EPI_RESID_F32) {
         // residual of the next chunk in flight during this one
-        if (j + 1 < j1) {
+        if (rload && j + 1 < j1) {
 #pragma unroll
           for (int k = 0; k < 8; ++k)
             if (row_ok(k)) nxt[k] = *resid(j + 1, k);
@@ -142,6 +149,16 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t tro
       const bool okr = row_ok(k);
       const size_t ro = (size_t)(row0 + rl) * args.ldo + oc;
       if constexpr (EPI == EPI_RESID_F32) {
+        if (!rload) {
+          if (okr) {
+            float* dst = reinterpret_cast<float*>(args.out) + ro;
+            asm volatile("red.global.add.v4.f32 [%0], {%1, %2, %3, %4};" ::"l"(dst),
+                         "f"(args.alpha * (w.x + b4.x)), "f"(args.alpha * (w.y + b4.y)),
+                         "f"(args.alpha * (w.z + b4.z)), "f"(args.alpha * (w.w + b4.w))
+                         : "memory");
+          }
+          continue;
+        }
         float4 o = okr ? cur[k] : make_float4(0.f, 0.f, 0.f, 0.f);
         o.x += args.alpha * (w.x + b4.x);
         o.y += args.alpha * (w.y + b4.y);
@@ -223,8 +240,10 @@ __device__ __forceinline__ void epilogue_tile(const GemmArgs& args, uint32_t tro
     }
     __syncwarp();  // the staging tile is reused by the next chunk
     if constexpr (EPI == EPI_RESID_F32) {
+      if (rload) {
 #pragma unroll
-      for (int k = 0; k < 8; ++k) cur[k] = nxt[k];
+        for (int k = 0; k < 8; ++k) cur[k] = nxt[k];
+      }
     }
   }
   if constexpr (EPI == EPI_RESID_F32) {
